@@ -1,0 +1,47 @@
+// Plain C++ launchers of the packmla kernels (no torch types): the .cu files compile without
+// torch headers; csrc/torch_ops.cpp validates tensors and calls these.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+void launch_native_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
+                         const int64_t* positions, const float* freqs, int64_t freq_rows, uint8_t* pool,
+                         int64_t pool_slots, int rows, int* err, cudaStream_t stream);
+void launch_packed_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
+                         uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int rows, int* err,
+                         cudaStream_t stream);
+
+struct DecodeParams {
+  const __nv_bfloat16* q;  // [B, H, 512]
+  int64_t q_stride_b, q_stride_h;
+  int B, H, num_groups, num_splits, rows_per_split;
+  // SWA (Native) rows
+  const uint8_t* swa_pool;
+  int64_t swa_pool_slots;
+  const int32_t* swa_slots;  // [B, swa_cap]
+  int swa_cap;
+  const int32_t* swa_len;    // [B]
+  // CSA rows
+  int csa_packed;
+  const uint8_t* csa_pool;   // native pages (csa_packed == 0)
+  const uint8_t* csa_values; // packed planes
+  const uint64_t* csa_bitmap;
+  const uint8_t* csa_scales;
+  int64_t csa_pool_rows;
+  const int32_t* csa_slots;  // [B, csa_cap]
+  const int32_t* csa_pos;    // [B, csa_cap] token position of the record (RoPE row)
+  int csa_cap;
+  const int32_t* csa_len;    // [B]
+  const float* freqs;        // [P, 32, 2]
+  int64_t freq_rows;
+  float scale_log2;          // softmax scale * log2(e)
+  float* part_o;             // [B, splits, H, 512]
+  float* part_ml;            // [B, splits, H, 2]
+  int* err;
+};
+
+void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,
+                              __nv_bfloat16* out, float* lse, cudaStream_t stream);
+
+void launch_umma_probe(const void* a, const void* b, int K, int N, int mode, float* d, int* err, cudaStream_t stream);

@@ -1,0 +1,162 @@
+// Torch-facing wrappers: argument validation, then the plain launchers of csrc/*.cu.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "launchers.h"
+
+namespace {
+constexpr int kD = 512;
+constexpr int kPage = 64;
+constexpr int kNativePageBytes = kPage * 584;
+
+void check_rows(const torch::Tensor& raw) {
+  TORCH_CHECK(raw.is_cuda() && raw.scalar_type() == torch::kFloat32, "raw must be CUDA float32");
+  TORCH_CHECK(raw.dim() == 2 && raw.size(1) == kD && raw.stride(1) == 1, "raw must be [R, 512] row-contiguous");
+  TORCH_CHECK(raw.stride(0) % 4 == 0 && (reinterpret_cast<uintptr_t>(raw.data_ptr()) % 16) == 0,
+              "raw rows must be 16-byte aligned");
+}
+void check_err(const torch::Tensor& err) {
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == torch::kInt32 && err.numel() >= 4, "err must be CUDA int32[4]");
+}
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+}  // namespace
+
+void native_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, torch::Tensor positions,
+                  torch::Tensor freqs, torch::Tensor pool, torch::Tensor err) {
+  check_rows(raw);
+  check_err(err);
+  TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == torch::kFloat32 && weight.numel() == kD && weight.is_contiguous());
+  TORCH_CHECK(slots.scalar_type() == torch::kInt64 && positions.scalar_type() == torch::kInt64);
+  TORCH_CHECK(slots.numel() == raw.size(0) && positions.numel() == raw.size(0));
+  TORCH_CHECK(slots.is_contiguous() && positions.is_contiguous());
+  TORCH_CHECK(freqs.scalar_type() == torch::kFloat32 && freqs.dim() == 3 && freqs.size(1) == 32 && freqs.size(2) == 2 &&
+              freqs.is_contiguous(), "freqs must be float32 [P, 32, 2]");
+  TORCH_CHECK(pool.scalar_type() == torch::kUInt8 && pool.is_contiguous() && pool.numel() % kNativePageBytes == 0,
+              "pool must be uint8 pages of 64 native records");
+  const c10::cuda::CUDAGuard g(raw.device());
+  launch_native_store(raw.data_ptr<float>(), raw.stride(0), weight.data_ptr<float>(), (float)eps,
+                      slots.data_ptr<int64_t>(), positions.data_ptr<int64_t>(), freqs.data_ptr<float>(), freqs.size(0),
+                      pool.data_ptr<uint8_t>(), pool.numel() / kNativePageBytes * kPage, raw.size(0),
+                      err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void packed_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, torch::Tensor values,
+                  torch::Tensor bitmap, torch::Tensor scales, torch::Tensor err) {
+  check_rows(raw);
+  check_err(err);
+  TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == torch::kFloat32 && weight.numel() == kD && weight.is_contiguous());
+  TORCH_CHECK(slots.scalar_type() == torch::kInt64 && slots.numel() == raw.size(0) && slots.is_contiguous());
+  TORCH_CHECK(values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.size(1) == 256 && values.is_contiguous());
+  TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.dim() == 2 && bitmap.size(1) == 8 && bitmap.is_contiguous());
+  TORCH_CHECK(scales.scalar_type() == torch::kUInt8 && scales.dim() == 2 && scales.size(1) == 8 && scales.is_contiguous());
+  TORCH_CHECK(bitmap.size(0) == values.size(0) && scales.size(0) == values.size(0));
+  const c10::cuda::CUDAGuard g(raw.device());
+  launch_packed_store(raw.data_ptr<float>(), raw.stride(0), weight.data_ptr<float>(), (float)eps,
+                      slots.data_ptr<int64_t>(), values.data_ptr<uint8_t>(),
+                      reinterpret_cast<uint64_t*>(bitmap.data_ptr<int64_t>()), scales.data_ptr<uint8_t>(),
+                      values.size(0), raw.size(0), err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor swa_slots, torch::Tensor swa_len,
+                       bool csa_packed, torch::Tensor csa_pool, torch::Tensor csa_values, torch::Tensor csa_bitmap,
+                       torch::Tensor csa_scales, torch::Tensor csa_slots, torch::Tensor csa_pos, torch::Tensor csa_len,
+                       torch::Tensor freqs, torch::Tensor sink, double scale, torch::Tensor q_pos, int64_t num_splits,
+                       torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse,
+                       torch::Tensor err) {
+  constexpr int kHG = 64, kTile = 128;
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
+  TORCH_CHECK(q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "q rows must be 16-byte aligned");
+  check_err(err);
+  const int B = q.size(0), H = q.size(1);
+  TORCH_CHECK(swa_slots.scalar_type() == torch::kInt32 && swa_slots.dim() == 2 && swa_slots.size(0) == B && swa_slots.is_contiguous());
+  TORCH_CHECK(csa_slots.scalar_type() == torch::kInt32 && csa_slots.dim() == 2 && csa_slots.size(0) == B && csa_slots.is_contiguous());
+  TORCH_CHECK(csa_pos.scalar_type() == torch::kInt32 && csa_pos.sizes() == csa_slots.sizes() && csa_pos.is_contiguous());
+  TORCH_CHECK(swa_len.scalar_type() == torch::kInt32 && swa_len.numel() == B && swa_len.is_contiguous());
+  TORCH_CHECK(csa_len.scalar_type() == torch::kInt32 && csa_len.numel() == B && csa_len.is_contiguous());
+  TORCH_CHECK(swa_pool.scalar_type() == torch::kUInt8 && swa_pool.numel() % kNativePageBytes == 0 && swa_pool.is_contiguous());
+  TORCH_CHECK(freqs.scalar_type() == torch::kFloat32 && freqs.dim() == 3 && freqs.size(1) == 32 && freqs.is_contiguous());
+  TORCH_CHECK(sink.scalar_type() == torch::kFloat32 && sink.numel() == H && sink.is_contiguous());
+  TORCH_CHECK(q_pos.scalar_type() == torch::kInt32 && q_pos.numel() == B && q_pos.is_contiguous());
+  TORCH_CHECK(num_splits >= 1);
+  TORCH_CHECK(part_o.scalar_type() == torch::kFloat32 && part_o.numel() >= (int64_t)B * num_splits * H * kD);
+  TORCH_CHECK(part_ml.scalar_type() == torch::kFloat32 && part_ml.numel() >= (int64_t)B * num_splits * H * 2);
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)B * H * kD);
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.numel() == (int64_t)B * H);
+  if (B == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  DecodeParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride_b = q.stride(0);
+  p.q_stride_h = q.stride(1);
+  p.B = B;
+  p.H = H;
+  p.num_groups = (H + kHG - 1) / kHG;
+  p.num_splits = (int)num_splits;
+  const int cap = swa_slots.size(1) + csa_slots.size(1);
+  p.rows_per_split = ((cap + num_splits - 1) / num_splits + kTile - 1) / kTile * kTile;
+  p.swa_pool = swa_pool.data_ptr<uint8_t>();
+  p.swa_pool_slots = swa_pool.numel() / kNativePageBytes * kPage;
+  p.swa_slots = swa_slots.data_ptr<int32_t>();
+  p.swa_cap = swa_slots.size(1);
+  p.swa_len = swa_len.data_ptr<int32_t>();
+  p.csa_packed = csa_packed ? 1 : 0;
+  if (csa_packed) {
+    TORCH_CHECK(csa_values.scalar_type() == torch::kUInt8 && csa_values.dim() == 2 && csa_values.size(1) == 256 && csa_values.is_contiguous());
+    TORCH_CHECK(csa_bitmap.scalar_type() == torch::kInt64 && csa_bitmap.size(0) == csa_values.size(0) && csa_bitmap.is_contiguous());
+    TORCH_CHECK(csa_scales.scalar_type() == torch::kUInt8 && csa_scales.size(0) == csa_values.size(0) && csa_scales.is_contiguous());
+    p.csa_values = csa_values.data_ptr<uint8_t>();
+    p.csa_bitmap = reinterpret_cast<const uint64_t*>(csa_bitmap.data_ptr<int64_t>());
+    p.csa_scales = csa_scales.data_ptr<uint8_t>();
+    p.csa_pool_rows = csa_values.size(0);
+  } else {
+    TORCH_CHECK(csa_pool.scalar_type() == torch::kUInt8 && csa_pool.numel() % kNativePageBytes == 0 && csa_pool.is_contiguous());
+    p.csa_pool = csa_pool.data_ptr<uint8_t>();
+    p.csa_pool_rows = csa_pool.numel() / kNativePageBytes * kPage;
+  }
+  p.csa_slots = csa_slots.data_ptr<int32_t>();
+  p.csa_pos = csa_pos.data_ptr<int32_t>();
+  p.csa_cap = csa_slots.size(1);
+  p.csa_len = csa_len.data_ptr<int32_t>();
+  p.freqs = freqs.data_ptr<float>();
+  p.freq_rows = freqs.size(0);
+  p.scale_log2 = (float)scale * 1.4426950408889634f;
+  p.part_o = part_o.data_ptr<float>();
+  p.part_ml = part_ml.data_ptr<float>();
+  p.err = err.data_ptr<int>();
+  launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
+                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::Tensor err) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.is_contiguous());
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == torch::kBFloat16 && b.is_contiguous());
+  check_err(err);
+  int K, N;
+  if (mode == 0) {
+    TORCH_CHECK(a.dim() == 2 && a.size(0) == 128 && b.dim() == 2 && b.size(1) == a.size(1));
+    K = a.size(1);
+    N = b.size(0);
+  } else {
+    TORCH_CHECK(a.dim() == 2 && a.size(1) == 128 && b.dim() == 2 && b.size(0) == a.size(0));
+    K = a.size(0);
+    N = b.size(1);
+  }
+  TORCH_CHECK(K % 16 == 0 && K <= 128 && (N == 16 || N == 32 || N == 64), "probe supports K<=128, N in {16,32,64}");
+  const c10::cuda::CUDAGuard g(a.device());
+  auto d = torch::zeros({128, N}, a.options().dtype(torch::kFloat32));
+  launch_umma_probe(a.data_ptr(), b.data_ptr(), K, N, (int)mode, d.data_ptr<float>(), err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return d;
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "packmla sm_100a kernels";
+  m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
+  m.def("packed_store", &packed_store, "FP32 rows -> Packed 328 B C4 records (planes)");
+  m.def("umma_probe", &umma_probe, "tcgen05 operand-layout self-test (one MMA)");
+  m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine");
+}

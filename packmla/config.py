@@ -1,0 +1,164 @@
+"""Typed configuration: model geometry and engine/server options.
+
+Model geometry of DeepSeek-V4-Flash-0731 as far as the reference records it:
+
+* 43 served layers with MoE; compression ratio per layer [0,0,4,128,4,128,...,4]
+  (server-info `_dsv4_c4_cache_compression_ratios`; MoE experts prepared for
+  model.layers.0..42 in benchmarks/lswb-replay/c27-packed256-n3-20261020/kernel/repeat1/server/serve_kernel.log);
+* 64 query heads over one 512-wide latent (448 NoPE + 64 RoPE), SWA window 128,
+  CSA top-k 512, page 256 tokens (server-info, training/data/dataset.py:32-42);
+* hidden 4096, fused q_a+kv_a output 1536 = 1024 (q LoRA) + 512 (latent), q_b
+  output 16 heads x 512 per TP4 rank, o_proj input 2048 per TP4 rank, shared
+  expert intermediate 2048 (DeepGEMM JIT shapes N=1536/8192/4096/1024 at K=4096/1024/2048/512
+  in the same log);
+* FP8 e4m3 dense weights, MXFP4 routed experts (`is_fp4_experts=True`, quant=fp8).
+
+Values the reference does not contain (routed-expert count, top-k, vocab, indexer
+width, grouped-output split) are documented assumptions sized so the weights
+total ~151 GB, matching the 4 x 38.6 GB the log reports at TP4.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import json
+from dataclasses import dataclass, field
+
+from .formats import abi
+
+
+def v4_flash_ratios(num_layers: int = 43) -> list[int]:
+    ratios = []
+    for i in range(num_layers):
+        if i < 2:
+            ratios.append(0)
+        else:
+            ratios.append(abi.C4_RATIO if i % 2 == 0 else abi.C128_RATIO)
+    return ratios
+
+
+@dataclass
+class ModelConfig:
+    name: str = "v4-flash"
+    vocab_size: int = 129280
+    hidden_size: int = 4096
+    num_layers: int = 43
+    num_heads: int = 64
+    latent_dim: int = abi.LATENT_DIM
+    rope_dim: int = abi.ROPE_DIM
+    q_lora_rank: int = 1024
+    o_groups: int = 8
+    o_lora_rank: int = 1024
+    window: int = abi.SWA_WINDOW
+    compress_ratios: list[int] = field(default_factory=v4_flash_ratios)
+    index_heads: int = 64
+    index_dim: int = 128
+    index_topk: int = 512
+    n_routed_experts: int = 256
+    n_shared_experts: int = 1
+    moe_topk: int = 8
+    moe_intermediate: int = 2048
+    routed_scaling: float = 1.0
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    max_position: int = 1 << 20
+    expert_format: str = "mxfp4"  # "mxfp4" | "bf16" (tiny CPU configs)
+    dense_format: str = "fp8"  # "fp8" | "bf16"
+
+    def __post_init__(self):
+        if len(self.compress_ratios) != self.num_layers:
+            raise ValueError("compress_ratios must have one entry per layer")
+        if self.num_heads % self.o_groups:
+            raise ValueError("num_heads must be a multiple of o_groups")
+        if self.latent_dim != abi.LATENT_DIM or self.rope_dim != abi.ROPE_DIM:
+            raise ValueError("the record ABI fixes latent 512 = 448 + 64")
+
+    @property
+    def heads_per_group(self) -> int:
+        return self.num_heads // self.o_groups
+
+    @property
+    def c4_layers(self) -> list[int]:
+        return [i for i, r in enumerate(self.compress_ratios) if r == abi.C4_RATIO]
+
+    @property
+    def c128_layers(self) -> list[int]:
+        return [i for i, r in enumerate(self.compress_ratios) if r == abi.C128_RATIO]
+
+    def to_json(self) -> str:
+        return json.dumps(dataclasses.asdict(self))
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "ModelConfig":
+        return cls(**d)
+
+    @classmethod
+    def tiny(cls, num_layers: int = 4, **kw) -> "ModelConfig":
+        """A small config with the same record ABI (latent 512) for CPU tests."""
+        ratios = [0] + [abi.C4_RATIO if i % 2 == 1 else abi.C128_RATIO for i in range(1, num_layers)]
+        base = dict(
+            name="tiny",
+            vocab_size=512,
+            hidden_size=256,
+            num_layers=num_layers,
+            num_heads=8,
+            q_lora_rank=128,
+            o_groups=2,
+            o_lora_rank=128,
+            compress_ratios=ratios,
+            index_heads=4,
+            index_dim=64,
+            index_topk=16,
+            n_routed_experts=8,
+            moe_topk=2,
+            moe_intermediate=128,
+            expert_format="bf16",
+            dense_format="bf16",
+            max_position=8192,
+        )
+        base.update(kw)
+        return cls(**base)
+
+
+KV_FORMATS = ("native", "direct")
+
+
+@dataclass
+class EngineConfig:
+    """Serving options; flag names mirror the reference server (scripts/local/run-server.sh:55-139)."""
+
+    kv_cache_format: str = "direct"  # native | direct
+    tp: int = 1
+    ep: int = 1
+    mem_fraction_static: float = 0.88
+    max_running_requests: int = 256
+    chunked_prefill_size: int = 8192
+    context_length: int = 1 << 20
+    cuda_graph_bs: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16, 24, 32, 40, 48, 64, 96, 128])
+    disable_cuda_graph: bool = False
+    enable_hierarchical_cache: bool = False
+    hicache_ratio: float = 2.0
+    keep_count: int = abi.PACKED_KEEP
+    swa_full_tokens_ratio: float = 0.1
+    random_seed: int = 0
+    device: str = "cuda"
+    fused_collectives: bool = True
+
+    def validate(self) -> None:
+        """Reject unsupported combinations before any pool allocation.
+
+        Mirrors the reference's startup checks: Direct serving supports 256 survivors
+        only, and HiCache requires the 256 layout (docs/agents/numerical-and-validation.md:13-16).
+        """
+        if self.kv_cache_format not in KV_FORMATS:
+            raise ValueError(f"--kv-cache-format must be one of {KV_FORMATS}")
+        if self.kv_cache_format == "direct" and self.keep_count != abi.PACKED_KEEP:
+            raise ValueError("direct serving supports keep_count 256 only")
+        if self.enable_hierarchical_cache and self.keep_count != abi.PACKED_KEEP:
+            raise ValueError("HiCache requires the 256-survivor layout")
+        if not 0.0 < self.mem_fraction_static <= 0.98:
+            raise ValueError("mem_fraction_static must be in (0, 0.98]")
+        if self.tp < 1 or self.ep < 1:
+            raise ValueError("tp and ep must be >= 1")
+        if self.hicache_ratio <= 0:
+            raise ValueError("hicache_ratio must be positive")

@@ -1,0 +1,52 @@
+"""Loader of the in-tree CUDA extension `packmla._C`.
+
+CUDA tensors always go through the extension; if it is missing the call fails
+loudly (no silent PyTorch fallback).  CPU tensors use the fp32 oracle instead.
+"""
+from __future__ import annotations
+
+import torch
+
+_EXT = None
+_ERR: dict[int, torch.Tensor] = {}
+
+
+def ext():
+    global _EXT
+    if _EXT is None:
+        try:
+            from packmla import _C  # noqa: WPS433
+        except ImportError as exc:  # pragma: no cover - exercised on GPU boxes only
+            raise RuntimeError(
+                "packmla CUDA extension is not built; run `python setup.py build_ext --inplace`"
+            ) from exc
+        _EXT = _C
+    return _EXT
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32[4] error word written by kernels instead of trapping."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ERR.get(idx)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _ERR[idx] = t
+    return t
+
+
+ERROR_NAMES = {1: "bounded wait timed out", 2: "index out of range", 3: "bad argument", 4: "peer timed out"}
+
+
+def check_errors(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronize and raise if any kernel on `device` reported an error."""
+    devs = [device] if device is not None else [torch.device("cuda", i) for i in list(_ERR)]
+    for d in devs:
+        w = error_word(d)
+        vals = w.tolist()
+        if reset:
+            w.zero_()
+        if vals[0] != 0:
+            raise RuntimeError(
+                f"packmla kernel error on {d}: {ERROR_NAMES.get(vals[0], vals[0])} "
+                f"(block {vals[1]}, detail {vals[2]}, count {vals[3]})"
+            )

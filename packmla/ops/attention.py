@@ -1,0 +1,132 @@
+"""Sparse MLA decode attention over Native SWA rows and Native/Packed C4 rows.
+
+CUDA: tcgen05 kernel + split combine (csrc/attention_decode.cu).
+CPU: fp32 oracle (packmla/oracle/attention.py) over rows decoded by the codec.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..formats import abi, codec
+from ..oracle import attention as oracle
+from ._ext import error_word, ext
+from .kv import native_pool_read
+
+NUM_SMS_B200 = 148
+KV_TILE = 128
+HEAD_GROUP = 64
+
+
+@dataclass
+class PackedPlanes:
+    values: torch.Tensor  # uint8 [rows, 256]
+    bitmap: torch.Tensor  # int64 [rows, 8]
+    scales: torch.Tensor  # uint8 [rows, 8]
+
+
+def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
+    groups = (heads + HEAD_GROUP - 1) // HEAD_GROUP
+    tiles = max(1, math.ceil(max_rows / KV_TILE))
+    want = max(1, math.ceil(num_sms / max(1, batch * groups)))
+    return max(1, min(tiles, want))
+
+
+class DecodeWorkspace:
+    """Split-KV partials with stable pointers (safe to capture in CUDA graphs)."""
+
+    def __init__(self, batch: int, heads: int, splits: int, device):
+        self.splits = splits
+        self.part_o = torch.empty(batch * splits * heads * abi.LATENT_DIM, dtype=torch.float32, device=device)
+        self.part_ml = torch.empty(batch * splits * heads * 2, dtype=torch.float32, device=device)
+
+
+def sparse_mla_decode(
+    q: torch.Tensor,
+    swa_pool: torch.Tensor,
+    swa_slots: torch.Tensor,
+    swa_len: torch.Tensor,
+    csa_slots: torch.Tensor,
+    csa_pos: torch.Tensor,
+    csa_len: torch.Tensor,
+    freqs: torch.Tensor,
+    sink: torch.Tensor,
+    scale: float,
+    q_pos: torch.Tensor,
+    csa_pool: torch.Tensor | None = None,
+    csa_planes: PackedPlanes | None = None,
+    num_splits: int | None = None,
+    workspace: DecodeWorkspace | None = None,
+    out: torch.Tensor | None = None,
+    lse: torch.Tensor | None = None,
+):
+    """q [B,H,512] bf16 (tail rotated by the query position) -> (out bf16 [B,H,512], lse fp32 [B,H]).
+
+    SWA rows: Native records at `swa_slots` [B, W] (first `swa_len[b]` used; -1 = masked).
+    C4 rows: `csa_slots` [B, K] physical records, `csa_pos` [B, K] token positions (RoPE rows
+    for Packed), first `csa_len[b]` used.  Exactly one of csa_pool (Native pages) /
+    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].
+    """
+    if (csa_pool is None) == (csa_planes is None):
+        raise ValueError("give exactly one of csa_pool (native) or csa_planes (packed)")
+    B, H, _ = q.shape
+    if not q.is_cuda:
+        return _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos,
+                           csa_pool, csa_planes)
+    if num_splits is None:
+        num_splits = workspace.splits if workspace is not None else choose_splits(
+            B, H, swa_slots.shape[1] + csa_slots.shape[1])
+    if workspace is None or workspace.splits != num_splits:
+        workspace = DecodeWorkspace(B, H, num_splits, q.device)
+    if out is None:
+        out = torch.empty(B, H, abi.LATENT_DIM, dtype=torch.bfloat16, device=q.device)
+    if lse is None:
+        lse = torch.empty(B, H, dtype=torch.float32, device=q.device)
+    packed = csa_planes is not None
+    dev = q.device
+    native_pool = csa_pool if not packed else torch.empty(0, dtype=torch.uint8, device=dev)
+    values = csa_planes.values if packed else torch.empty(0, 256, dtype=torch.uint8, device=dev)
+    bitmap = csa_planes.bitmap if packed else torch.empty(0, 8, dtype=torch.int64, device=dev)
+    scales = csa_planes.scales if packed else torch.empty(0, 8, dtype=torch.uint8, device=dev)
+    ext().sparse_mla_decode(
+        q, swa_pool, swa_slots, swa_len, packed, native_pool, values, bitmap, scales,
+        csa_slots, csa_pos, csa_len, freqs, sink, float(scale), q_pos, int(num_splits),
+        workspace.part_o, workspace.part_ml, out, lse, error_word(dev),
+    )
+    return out, lse
+
+
+def gather_rows_cpu(swa_pool, swa_slots_b, n_swa, csa_slots_b, csa_pos_b, n_csa, freqs, csa_pool, csa_planes):
+    """Decoded fp32 rows [N, 512] of one query (masked -1 entries dropped)."""
+    rows = []
+    s = swa_slots_b[:n_swa].long()
+    s = s[s >= 0]
+    if s.numel():
+        rows.append(codec.native_decode(native_pool_read(swa_pool, s).cpu()))
+    c = csa_slots_b[:n_csa].long()
+    p = csa_pos_b[:n_csa].long()
+    valid = c >= 0
+    c, p = c[valid], p[valid]
+    if c.numel():
+        if csa_planes is None:
+            rows.append(codec.native_decode(native_pool_read(csa_pool, c).cpu()))
+        else:
+            fr = torch.view_as_complex(freqs[p].float().contiguous()).cpu()
+            rows.append(codec.packed_read(csa_planes.values[c].cpu(), csa_planes.bitmap[c].cpu(),
+                                          csa_planes.scales[c].cpu(), fr))
+    if not rows:
+        return torch.zeros(0, abi.LATENT_DIM)
+    return torch.cat(rows)
+
+
+def _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos, csa_pool,
+                csa_planes):
+    B = q.shape[0]
+    kv = []
+    for b in range(B):
+        kv.append(gather_rows_cpu(swa_pool, swa_slots[b], int(swa_len[b]), csa_slots[b], csa_pos[b], int(csa_len[b]),
+                                  freqs, csa_pool, csa_planes))
+    qf = torch.view_as_complex(freqs[q_pos.long()].float().contiguous())
+    return oracle.sparse_mla_decode(q.float(), kv, sink.float(), scale, qf)

@@ -1,0 +1,84 @@
+"""KV store ops: FP32 compressor rows -> Native pages or Packed planes.
+
+CUDA tensors run the sm_100a store kernels (csrc/kv_store.cu); CPU tensors run the
+oracle codec (packmla/formats/codec.py).  Both write the same bytes.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..formats import abi, codec
+from ._ext import error_word, ext
+
+
+def freq_table_f32(freqs_complex: torch.Tensor) -> torch.Tensor:
+    """complex64 [P, 32] -> float32 [P, 32, 2] (cos, sin) contiguous."""
+    return torch.view_as_real(freqs_complex.to(torch.complex64)).contiguous()
+
+
+def native_store(
+    raw: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    slots: torch.Tensor,
+    positions: torch.Tensor,
+    freqs: torch.Tensor,
+    pool: torch.Tensor,
+) -> None:
+    """Write Native records for rows `raw` [R,512] at physical `slots` (-1 = skip).
+
+    `positions` are the RoPE table rows (token positions); `freqs` is float32 [P,32,2];
+    `pool` is uint8 pages of 64 records (data rows then scale rows).
+    """
+    if raw.is_cuda:
+        ext().native_store(raw, weight, float(eps), slots.to(torch.int64), positions.to(torch.int64), freqs, pool,
+                           error_word(raw.device))
+        return
+    keep = slots >= 0
+    if not bool(keep.any()):
+        return
+    fr = torch.view_as_complex(freqs[positions[keep].long()].contiguous())
+    rec = codec.native_encode(raw[keep].float(), weight.float(), eps, fr)
+    pages = pool.view(-1, abi.NATIVE_PAGE_BYTES)
+    for s, row in zip(slots[keep].tolist(), rec):
+        page, r = divmod(s, abi.RECORDS_PER_PAGE)
+        pages[page, r * abi.NATIVE_DATA_BYTES : (r + 1) * abi.NATIVE_DATA_BYTES] = row[: abi.NATIVE_DATA_BYTES]
+        off = abi.RECORDS_PER_PAGE * abi.NATIVE_DATA_BYTES + r * abi.NATIVE_SCALE_BYTES
+        pages[page, off : off + abi.NATIVE_SCALE_BYTES] = row[abi.NATIVE_DATA_BYTES :]
+
+
+def packed_store(
+    raw: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    slots: torch.Tensor,
+    values: torch.Tensor,
+    bitmap: torch.Tensor,
+    scales: torch.Tensor,
+) -> None:
+    """Select top-256 |raw|, masked RMSNorm, quantize and write the three planes at `slots`."""
+    if raw.is_cuda:
+        ext().packed_store(raw, weight, float(eps), slots.to(torch.int64), values, bitmap, scales,
+                           error_word(raw.device))
+        return
+    keep = slots >= 0
+    if not bool(keep.any()):
+        return
+    v, b, s = codec.packed_encode(raw[keep].float(), weight.float(), eps)
+    idx = slots[keep].long()
+    values[idx] = v
+    bitmap[idx] = b
+    scales[idx] = s
+
+
+def native_pool_read(pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
+    """Gather Native records [R, 584] (logical order) from a paged pool (CPU or CUDA)."""
+    pages = pool.view(-1, abi.NATIVE_PAGE_BYTES)
+    s = slots.long()
+    page, r = s // abi.RECORDS_PER_PAGE, s % abi.RECORDS_PER_PAGE
+    d_idx = r[:, None] * abi.NATIVE_DATA_BYTES + torch.arange(abi.NATIVE_DATA_BYTES, device=pool.device)[None]
+    s_idx = (abi.RECORDS_PER_PAGE * abi.NATIVE_DATA_BYTES + r[:, None] * abi.NATIVE_SCALE_BYTES
+             + torch.arange(abi.NATIVE_SCALE_BYTES, device=pool.device)[None])
+    data = pages[page[:, None], d_idx]
+    sc = pages[page[:, None], s_idx]
+    return torch.cat((data, sc), -1)
