@@ -45,3 +45,8 @@ void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const in
                               __nv_bfloat16* out, float* lse, cudaStream_t stream);
 
 void launch_umma_probe(const void* a, const void* b, int K, int N, int mode, float* d, int* err, cudaStream_t stream);
+
+void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const int32_t* topk_ids, const float* topk_w,
+                    int expert_base, int E, const uint8_t* w13, const uint8_t* s13, const uint8_t* w2,
+                    const uint8_t* s2, int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active,
+                    __nv_bfloat16* act, float* out, int num_sms, cudaStream_t stream);

@@ -153,10 +153,49 @@ torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::
   return d;
 }
 
+void moe_fp4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base, torch::Tensor w13,
+             torch::Tensor s13, torch::Tensor w2, torch::Tensor s2, torch::Tensor offsets, torch::Tensor slot_token,
+             torch::Tensor slot_weight, torch::Tensor active, torch::Tensor act, torch::Tensor out,
+             torch::Tensor err) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
+  check_err(err);
+  const int T = h.size(0), H = h.size(1);
+  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.dim() == 2 && topk_ids.size(0) == T && topk_ids.is_contiguous());
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.sizes() == topk_ids.sizes() && topk_w.is_contiguous());
+  const int k = topk_ids.size(1);
+  TORCH_CHECK(w13.scalar_type() == torch::kUInt8 && w13.dim() == 3 && w13.size(2) * 2 == H && w13.is_contiguous());
+  const int E = w13.size(0), I = w13.size(1) / 2;
+  TORCH_CHECK(s13.scalar_type() == torch::kUInt8 && s13.dim() == 3 && s13.size(0) == E && s13.size(1) == 2 * I &&
+              s13.size(2) * 32 == H && s13.is_contiguous());
+  TORCH_CHECK(w2.scalar_type() == torch::kUInt8 && w2.dim() == 3 && w2.size(0) == E && w2.size(1) == H &&
+              w2.size(2) * 2 == I && w2.is_contiguous());
+  TORCH_CHECK(s2.scalar_type() == torch::kUInt8 && s2.dim() == 3 && s2.size(0) == E && s2.size(1) == H &&
+              s2.size(2) * 32 == I && s2.is_contiguous());
+  TORCH_CHECK((H == 1024 || H == 2048 || H == 4096) && (I == 1024 || I == 2048 || I == 4096),
+              "moe_fp4 supports hidden and intermediate sizes 1024, 2048 or 4096");
+  TORCH_CHECK(E <= 4096, "too many local experts");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() >= E + 1);
+  TORCH_CHECK(active.scalar_type() == torch::kInt32 && active.numel() >= E + 1);
+  TORCH_CHECK(slot_token.scalar_type() == torch::kInt32 && slot_token.numel() >= (int64_t)T * k);
+  TORCH_CHECK(slot_weight.scalar_type() == torch::kFloat32 && slot_weight.numel() >= (int64_t)T * k);
+  TORCH_CHECK(act.scalar_type() == torch::kBFloat16 && act.is_contiguous() && act.numel() >= (int64_t)T * k * I);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == (int64_t)T * H);
+  const c10::cuda::CUDAGuard g(h.device());
+  static int num_sms = 0;
+  if (num_sms == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, h.device().index()));
+  launch_moe_fp4(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), T, H, I, k, topk_ids.data_ptr<int32_t>(),
+                 topk_w.data_ptr<float>(), (int)expert_base, E, w13.data_ptr<uint8_t>(), s13.data_ptr<uint8_t>(),
+                 w2.data_ptr<uint8_t>(), s2.data_ptr<uint8_t>(), offsets.data_ptr<int32_t>(),
+                 slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(), active.data_ptr<int32_t>(),
+                 reinterpret_cast<__nv_bfloat16*>(act.data_ptr()), out.data_ptr<float>(), num_sms, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
   m.def("packed_store", &packed_store, "FP32 rows -> Packed 328 B C4 records (planes)");
   m.def("umma_probe", &umma_probe, "tcgen05 operand-layout self-test (one MMA)");
+  m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
   m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine");
 }

@@ -1,0 +1,76 @@
+"""Device timing (CUDA events, max over ranks) and SM-clock sampling during timed regions."""
+from __future__ import annotations
+
+import csv
+import io
+import os
+import statistics
+import subprocess
+import tempfile
+
+import torch
+
+
+class ClockSampler:
+    """Runs `nvidia-smi ... -lms 200` for this GPU while active; summarises clocks and throttle reasons."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, out_path: str | None = None):
+        self.gpu = gpu_index
+        self.path = out_path or tempfile.mktemp(suffix=".csv")
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = list(csv.reader(io.StringIO(open(self.path).read())))
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def time_device(fn, steps: int, device) -> float:
+    """Milliseconds of `steps` calls of fn on the current stream (CUDA events, synced both sides)."""
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end)

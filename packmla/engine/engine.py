@@ -1,0 +1,320 @@
+"""Serving engine: requests, FCFS scheduler with chunked prefill, CUDA-graph decode runner.
+
+Public API (what the HTTP server and bench.py call):
+
+    eng = Engine.build(model_cfg, engine_cfg, device)            # random-init weights, KV pool
+    rid = eng.add_request(prompt_ids, SamplingParams(max_new_tokens=256))
+    while eng.has_work(): eng.step()                             # one prefill chunk or one decode step
+    eng.result(rid).output_ids
+
+Reference behaviour: SGLang scheduler + `decode_cuda_graph_runner.py` (R8, third_party/README.md:294-298):
+chunked prefill (8192), full decode CUDA graphs for padded batch sizes, FCFS admission bounded by
+the KV pool.  Multi-rank: every rank runs the same deterministic schedule in lockstep; logits are
+identical on all ranks after the all-reduces, so sampling needs no broadcast.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..kv.pool import KVPool, plan_capacity
+from ..models.v4flash import V4FlashModel
+from ..models.weights import init_weights
+from ..utils.metrics import Metrics
+
+
+@dataclass
+class SamplingParams:
+    max_new_tokens: int = 16
+    temperature: float = 0.0  # 0 = greedy
+    ignore_eos: bool = True
+    eos_token_id: int | None = None
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: list[int]
+    params: SamplingParams
+    output_ids: list[int] = field(default_factory=list)
+    slot: int = -1
+    prefilled: int = 0
+    finished: bool = False
+    t_arrival: float = 0.0
+    t_first_token: float | None = None
+    t_finish: float | None = None
+
+    @property
+    def context_len(self) -> int:
+        return self.prefilled + len(self.output_ids)
+
+
+class DecodeGraphRunner:
+    """Captures model.decode(+ sampling) per padded batch size; replays with copied inputs."""
+
+    def __init__(self, model: V4FlashModel, buckets: list[int], dummy_slot: int, enabled: bool):
+        self.model = model
+        self.device = model.device
+        self.buckets = sorted(buckets)
+        self.max_b = self.buckets[-1]
+        self.dummy_slot = dummy_slot
+        self.enabled = enabled and self.device.type == "cuda"
+        dev = self.device
+        self.tokens = torch.zeros(self.max_b, dtype=torch.int64, device=dev)
+        self.positions = torch.zeros(self.max_b, dtype=torch.int64, device=dev)
+        self.slots = torch.full((self.max_b,), dummy_slot, dtype=torch.int64, device=dev)
+        self.temps = torch.zeros(self.max_b, dtype=torch.float32, device=dev)
+        self.out_tokens = torch.zeros(self.max_b, dtype=torch.int64, device=dev)
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.pool_handle = None
+
+    def _forward(self, b: int) -> None:
+        logits = self.model.decode(self.tokens[:b], self.positions[:b], self.slots[:b])
+        self.out_tokens[:b] = sample(logits, self.temps[:b])
+
+    def bucket(self, b: int) -> int:
+        for s in self.buckets:
+            if s >= b:
+                return s
+        raise ValueError(f"batch {b} exceeds the largest graph bucket {self.max_b}")
+
+    def capture(self, sizes: list[int] | None = None) -> None:
+        if not self.enabled:
+            return
+        sizes = sizes or self.buckets
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for b in sorted(sizes, reverse=True):
+                self.slots[:b] = self.dummy_slot
+                self.positions[:b] = 0
+                self._forward(b)  # warm-up (allocations, lazy inits)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=self.pool_handle, stream=stream):
+                    self._forward(b)
+                if self.pool_handle is None:
+                    self.pool_handle = g.pool()
+                self.graphs[b] = g
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        self.model.pool.comp_state_reset(self.dummy_slot)
+
+    def run(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, temps: torch.Tensor) -> torch.Tensor:
+        """Inputs are (pinned) host or device tensors of length b; returns device token ids [b]."""
+        b = tokens.shape[0]
+        bp = self.bucket(b) if self.enabled else b
+        self.tokens[:b].copy_(tokens, non_blocking=True)
+        self.positions[:b].copy_(positions, non_blocking=True)
+        self.slots[:b].copy_(slots, non_blocking=True)
+        self.temps[:b].copy_(temps, non_blocking=True)
+        if bp > b:
+            self.slots[b:bp] = self.dummy_slot
+            self.positions[b:bp] = 0
+            self.tokens[b:bp] = 0
+        if self.enabled and bp in self.graphs:
+            self.graphs[bp].replay()
+        else:
+            self._forward(bp)
+        return self.out_tokens[:b]
+
+    def release(self) -> None:
+        self.graphs.clear()
+        self.pool_handle = None
+
+
+def sample(logits: torch.Tensor, temps: torch.Tensor) -> torch.Tensor:
+    """Greedy where temperature == 0, else Gumbel-max sampling (graph-capturable)."""
+    greedy = logits.argmax(-1)
+    u = torch.rand_like(logits).clamp_(min=1e-20)
+    g = -torch.log(-torch.log(u))
+    t = temps.clamp(min=1e-5)[:, None]
+    sampled = (logits / t + g).argmax(-1)
+    return torch.where(temps > 0, sampled, greedy)
+
+
+class Engine:
+    def __init__(self, model_cfg: ModelConfig, engine_cfg: EngineConfig, model: V4FlashModel, pool: KVPool,
+                 comm=None):
+        self.cfg = model_cfg
+        self.ecfg = engine_cfg
+        self.model = model
+        self.pool = pool
+        self.comm = comm
+        self.device = pool.device
+        self.metrics = Metrics()
+        self.dummy_slot = pool.max_requests - 1
+        pool._free_slots.remove(self.dummy_slot)
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.done: dict[int, Request] = {}
+        self._ids = itertools.count()
+        buckets = [b for b in engine_cfg.cuda_graph_bs if b <= pool.max_requests - 1] or [1]
+        self.runner = DecodeGraphRunner(model, buckets, self.dummy_slot, not engine_cfg.disable_cuda_graph)
+        pin = self.device.type == "cuda"
+        mb = self.runner.max_b
+        self._h_tokens = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
+        self._h_pos = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
+        self._h_slots = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
+        self._h_temps = torch.zeros(mb, dtype=torch.float32, pin_memory=pin)
+        self._h_out = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
+        self.h2d_bytes_last = 0
+        self.d2h_bytes_last = 0
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def build(cls, model_cfg: ModelConfig, engine_cfg: EngineConfig, device="cuda", rank: int = 0, world: int = 1,
+              comm=None, max_context: int = 1 << 15, max_requests: int | None = None, kv_bytes: int | None = None,
+              seed: int = 0, weights: dict | None = None) -> "Engine":
+        engine_cfg.validate()
+        dev = torch.device(device)
+        W = weights if weights is not None else init_weights(model_cfg, rank, world, dev, seed)
+        max_requests = max_requests or engine_cfg.max_running_requests
+        max_requests += 1  # + dummy slot for padded graph rows
+        if kv_bytes is None:
+            if dev.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(dev)
+                kv_bytes = int(free * engine_cfg.mem_fraction_static) - (2 << 30)
+            else:
+                kv_bytes = 64 << 20
+        cap = plan_capacity(model_cfg, engine_cfg, kv_bytes)
+        pages = max(cap.num_pages, 1)
+        pool = KVPool(model_cfg, engine_cfg, pages, max_requests, max_context, dev)
+        model = V4FlashModel(model_cfg, W, pool, comm)
+        eng = cls(model_cfg, engine_cfg, model, pool, comm)
+        eng.capacity = cap
+        return eng
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> int:
+        if not prompt:
+            raise ValueError("empty prompt")
+        req = Request(next(self._ids), list(prompt), params or SamplingParams(), t_arrival=time.perf_counter())
+        self.waiting.append(req)
+        self.metrics.inc("requests_received")
+        return req.rid
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def result(self, rid: int) -> Request:
+        return self.done[rid]
+
+    def abort(self, rid: int) -> bool:
+        for q in (self.waiting, self.running):
+            for r in list(q):
+                if r.rid == rid:
+                    q.remove(r)
+                    if r.slot >= 0:
+                        self.pool.release(r.slot)
+                    r.finished = True
+                    self.done[rid] = r
+                    return True
+        return False
+
+    # ------------------------------------------------------------------ scheduling
+    def _admit(self) -> Request | None:
+        if not self.waiting:
+            return None
+        req = self.waiting[0]
+        if req.slot < 0:
+            need = len(req.prompt) + req.params.max_new_tokens
+            if need > self.pool.max_context:
+                self.waiting.popleft()
+                raise ValueError(f"request {req.rid} needs {need} tokens > max_context {self.pool.max_context}")
+            if len(self.running) >= self.runner.max_b or not self.pool._free_slots:
+                return None
+            pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
+            if pages_needed > self.pool.pages.free:
+                return None
+            req.slot = self.pool.admit(need)
+        return req
+
+    def step(self) -> list[tuple[int, int]]:
+        """Run one prefill chunk (if a request is waiting and fits) or one decode step.
+
+        Returns the (rid, token) pairs produced by this step.
+        """
+        req = self._admit()
+        if req is not None:
+            return self._prefill_chunk(req)
+        if self.running:
+            return self._decode()
+        return []
+
+    def _prefill_chunk(self, req: Request) -> list[tuple[int, int]]:
+        chunk = self.ecfg.chunked_prefill_size
+        start = req.prefilled
+        toks = req.prompt[start:start + chunk]
+        t = torch.tensor(toks, dtype=torch.int64)
+        if self.device.type == "cuda":
+            t = t.pin_memory().to(self.device, non_blocking=True)
+        logits = self.model.prefill(t, start, req.slot)
+        req.prefilled += len(toks)
+        self.metrics.inc("prefill_tokens", len(toks))
+        if req.prefilled < len(req.prompt):
+            return []
+        self.waiting.popleft()
+        temp = torch.tensor([req.params.temperature], device=self.device)
+        tok = int(sample(logits[None], temp)[0])
+        self._emit(req, tok)
+        if not req.finished:
+            self.running.append(req)
+        return [(req.rid, tok)]
+
+    def _decode(self) -> list[tuple[int, int]]:
+        reqs = self.running
+        b = len(reqs)
+        for i, r in enumerate(reqs):
+            self._h_tokens[i] = r.output_ids[-1]
+            self._h_pos[i] = r.context_len - 1
+            self._h_slots[i] = r.slot
+            self._h_temps[i] = r.params.temperature
+        self.h2d_bytes_last = b * (8 + 8 + 8 + 4)
+        out = self.runner.run(self._h_tokens[:b], self._h_pos[:b], self._h_slots[:b], self._h_temps[:b])
+        self._h_out[:b].copy_(out, non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        self.d2h_bytes_last = b * 8
+        toks = self._h_out[:b].tolist()
+        produced = []
+        for r, tok in zip(list(reqs), toks):
+            self._emit(r, tok)
+            produced.append((r.rid, tok))
+        self.running = [r for r in reqs if not r.finished]
+        self.metrics.inc("decode_steps")
+        self.metrics.inc("decode_tokens", b)
+        return produced
+
+    def _emit(self, req: Request, tok: int) -> None:
+        if req.t_first_token is None:
+            req.t_first_token = time.perf_counter()
+        req.output_ids.append(tok)
+        eos = req.params.eos_token_id
+        if len(req.output_ids) >= req.params.max_new_tokens or (not req.params.ignore_eos and eos is not None
+                                                                 and tok == eos):
+            req.finished = True
+            req.t_finish = time.perf_counter()
+            self.pool.release(req.slot)
+            self.done[req.rid] = req
+            self.metrics.inc("requests_finished")
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | None = None) -> list[list[int]]:
+        rids = [self.add_request(p, params) for p in prompts]
+        while self.has_work():
+            self.step()
+        return [self.result(r).output_ids for r in rids]
+
+    def server_info(self) -> dict:
+        return {
+            "kv_cache_format": self.ecfg.kv_cache_format,
+            "max_total_num_tokens": self.capacity.max_total_tokens,
+            "bytes_per_full_token": self.capacity.bytes_per_full_token,
+            "num_pages": self.pool.num_pages,
+            "max_running_requests": self.pool.max_requests - 1,
+            "cuda_graph_bs": self.runner.buckets,
+            "tp": self.ecfg.tp,
+        }

@@ -1,0 +1,218 @@
+"""Paged KV memory for compressed-sparse MLA layers, with capacity accounting.
+
+Layout (per rank; the latent KV is shared by all heads, so TP ranks hold full copies):
+
+* page = 256 tokens = 64 C4 records.  A request owns a row of the page table; the same
+  page id addresses every C4 layer's pool (one allocation serves all layers).
+* C4 layers:   Native pages (584 B/record) in `native` mode, or Packed planes
+               (256 + 64 + 8 B/record) in `direct` mode; plus FP8 indexer keys
+               (index_dim B + 4 B fp32 scale per record).
+* C128 layers: Native pages; one C128 record per 128 tokens, 64 records per C128 page.
+* SWA:         per layer a ring of 128 Native records per request slot.
+* compressor state: online-softmax pooling state (max, sum, weighted sum) per layer per
+  request slot for the latent (512) and, on C4 layers, the indexer key.
+
+Capacity follows the reference's accounting (`DSV4 memory calculation: bytes_per_full_token`
+in the serve logs): bytes per full token = C4 record bytes / 4 over C4 layers + indexer key
+bytes / 4 + C128 record bytes / 128 + swa_full_tokens_ratio x SWA bytes over all layers.
+The Packed/Native ratio of `max_total_tokens` is the KV-capacity metric (reference: 1.2113x,
+docs/report.md:30).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..formats import abi
+
+
+@dataclass
+class CapacityReport:
+    kv_format: str
+    bytes_per_full_token: float
+    available_bytes: int
+    fixed_bytes: int
+    max_total_tokens: int
+    num_pages: int
+
+    def as_dict(self) -> dict:
+        return dict(self.__dict__)
+
+
+def c4_record_bytes(kv_format: str) -> int:
+    return abi.PACKED_RECORD_BYTES if kv_format == "direct" else abi.NATIVE_RECORD_BYTES
+
+
+def bytes_per_full_token(cfg: ModelConfig, kv_format: str, swa_ratio: float) -> float:
+    c4 = len(cfg.c4_layers) * (c4_record_bytes(kv_format) + cfg.index_dim + 4) / abi.C4_RATIO
+    c128 = len(cfg.c128_layers) * abi.NATIVE_RECORD_BYTES / abi.C128_RATIO
+    swa = swa_ratio * cfg.num_layers * abi.NATIVE_RECORD_BYTES
+    return c4 + c128 + swa
+
+
+def fixed_bytes(cfg: ModelConfig, max_requests: int) -> int:
+    """Per-request state independent of context length (compressor state)."""
+    comp = 0
+    for r in cfg.compress_ratios:
+        if r:
+            comp += 3 * abi.LATENT_DIM * 4
+            if r == abi.C4_RATIO:
+                comp += 3 * cfg.index_dim * 4
+    return max_requests * comp
+
+
+def plan_capacity(cfg: ModelConfig, ecfg: EngineConfig, available_bytes: int) -> CapacityReport:
+    """Token capacity for a KV budget; pages of 256 tokens."""
+    bpt = bytes_per_full_token(cfg, ecfg.kv_cache_format, ecfg.swa_full_tokens_ratio)
+    fixed = fixed_bytes(cfg, ecfg.max_running_requests)
+    usable = max(0, available_bytes - fixed)
+    tokens = int(usable // bpt)
+    pages = tokens // (abi.RECORDS_PER_PAGE * abi.C4_RATIO)
+    return CapacityReport(ecfg.kv_cache_format, bpt, available_bytes, fixed,
+                          pages * abi.RECORDS_PER_PAGE * abi.C4_RATIO, pages)
+
+
+class PageAllocator:
+    """Free-list page allocator (host side)."""
+
+    def __init__(self, num_pages: int):
+        self.num_pages = num_pages
+        self._free = list(range(num_pages - 1, -1, -1))
+
+    @property
+    def free(self) -> int:
+        return len(self._free)
+
+    def alloc(self, n: int) -> list[int]:
+        if n > len(self._free):
+            raise MemoryError(f"KV pool exhausted: need {n} pages, {len(self._free)} free")
+        return [self._free.pop() for _ in range(n)]
+
+    def release(self, pages: list[int]) -> None:
+        self._free.extend(pages)
+
+
+class KVPool:
+    """All per-rank KV storage for one model.  Tensors live on `device`."""
+
+    TOKENS_PER_PAGE = abi.RECORDS_PER_PAGE * abi.C4_RATIO  # 256
+    TOKENS_PER_C128_PAGE = abi.RECORDS_PER_PAGE * abi.C128_RATIO  # 8192
+
+    def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, num_pages: int, max_requests: int,
+                 max_context: int, device):
+        ecfg.validate()
+        self.cfg, self.ecfg = cfg, ecfg
+        self.device = torch.device(device)
+        self.kv_format = ecfg.kv_cache_format
+        self.num_pages = num_pages
+        self.max_requests = max_requests
+        self.max_context = max_context
+        self.max_pages_per_req = (max_context + self.TOKENS_PER_PAGE - 1) // self.TOKENS_PER_PAGE
+        self.max_c128_pages_per_req = (max_context + self.TOKENS_PER_C128_PAGE - 1) // self.TOKENS_PER_C128_PAGE
+        # C128 pages are budgeted from the C4 pages (1 C128 page per 32 C4 pages) + 1 per request
+        self.num_c128_pages = num_pages // 32 + max_requests
+        dev = self.device
+        rows = num_pages * abi.RECORDS_PER_PAGE
+        self.c4_native: dict[int, torch.Tensor] = {}
+        self.c4_values: dict[int, torch.Tensor] = {}
+        self.c4_bitmap: dict[int, torch.Tensor] = {}
+        self.c4_scales: dict[int, torch.Tensor] = {}
+        self.index_keys: dict[int, torch.Tensor] = {}
+        self.index_scales: dict[int, torch.Tensor] = {}
+        for layer in cfg.c4_layers:
+            if self.kv_format == "direct":
+                self.c4_values[layer] = torch.zeros(rows, abi.PACKED_KEEP, dtype=torch.uint8, device=dev)
+                self.c4_bitmap[layer] = torch.zeros(rows, abi.BITMAP_WORDS, dtype=torch.int64, device=dev)
+                self.c4_scales[layer] = torch.zeros(rows, abi.NUM_TILES, dtype=torch.uint8, device=dev)
+            else:
+                self.c4_native[layer] = torch.zeros(num_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+            # one extra trailing "trash" row absorbs writes of rows without a destination
+            self.index_keys[layer] = torch.zeros(rows + 1, cfg.index_dim, dtype=torch.uint8, device=dev)
+            self.index_scales[layer] = torch.zeros(rows + 1, dtype=torch.float32, device=dev)
+        self.c128_native = {
+            layer: torch.zeros(self.num_c128_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+            for layer in cfg.c128_layers
+        }
+        swa_pages = max_requests * cfg.window // abi.RECORDS_PER_PAGE
+        self.swa = [torch.zeros(swa_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+                    for _ in range(cfg.num_layers)]
+        # compressor pooling state: [max_requests, 3, dim] = (running max, sum of exp, weighted sum)
+        self.comp_state: dict[int, torch.Tensor] = {}
+        self.index_state: dict[int, torch.Tensor] = {}
+        for layer, r in enumerate(cfg.compress_ratios):
+            if r:
+                self.comp_state[layer] = self._fresh_state(max_requests, abi.LATENT_DIM)
+                if r == abi.C4_RATIO:
+                    self.index_state[layer] = self._fresh_state(max_requests, cfg.index_dim)
+        self.page_table = torch.full((max_requests, self.max_pages_per_req), -1, dtype=torch.int32, device=dev)
+        self.c128_table = torch.full((max_requests, self.max_c128_pages_per_req), -1, dtype=torch.int32, device=dev)
+        self.pages = PageAllocator(num_pages)
+        self.c128_pages = PageAllocator(self.num_c128_pages)
+        self._req_pages: dict[int, list[int]] = {}
+        self._req_c128: dict[int, list[int]] = {}
+        self._free_slots = list(range(max_requests - 1, -1, -1))
+
+    def _fresh_state(self, n: int, dim: int) -> torch.Tensor:
+        st = torch.zeros(n, 3, dim, dtype=torch.float32, device=self.device)
+        st[:, 0] = float("-inf")
+        return st
+
+    # ------------------------------------------------------------------ bytes
+    def device_bytes(self) -> int:
+        total = 0
+        for d in (self.c4_native, self.c4_values, self.c4_bitmap, self.c4_scales, self.index_keys,
+                  self.index_scales, self.c128_native, self.comp_state, self.index_state):
+            total += sum(t.numel() * t.element_size() for t in d.values())
+        total += sum(t.numel() * t.element_size() for t in self.swa)
+        return total
+
+    # ------------------------------------------------------------------ requests
+    def admit(self, tokens: int) -> int:
+        """Reserve a request slot with pages for `tokens` tokens; returns the slot."""
+        if not self._free_slots:
+            raise MemoryError("no free request slot")
+        slot = self._free_slots.pop()
+        self._req_pages[slot] = []
+        self._req_c128[slot] = []
+        try:
+            self.ensure(slot, tokens)
+        except MemoryError:
+            self.release(slot)
+            raise
+        self.comp_state_reset(slot)
+        return slot
+
+    def ensure(self, slot: int, tokens: int) -> None:
+        """Grow the request's page tables to cover `tokens` tokens."""
+        if tokens > self.max_context:
+            raise ValueError(f"context {tokens} exceeds max_context {self.max_context}")
+        need = (tokens + self.TOKENS_PER_PAGE - 1) // self.TOKENS_PER_PAGE - len(self._req_pages[slot])
+        if need > 0:
+            new = self.pages.alloc(need)
+            start = len(self._req_pages[slot])
+            self._req_pages[slot].extend(new)
+            self.page_table[slot, start:start + need] = torch.tensor(new, dtype=torch.int32, device=self.device)
+        need = (tokens + self.TOKENS_PER_C128_PAGE - 1) // self.TOKENS_PER_C128_PAGE - len(self._req_c128[slot])
+        if need > 0:
+            new = self.c128_pages.alloc(need)
+            start = len(self._req_c128[slot])
+            self._req_c128[slot].extend(new)
+            self.c128_table[slot, start:start + need] = torch.tensor(new, dtype=torch.int32, device=self.device)
+
+    def release(self, slot: int) -> None:
+        self.pages.release(self._req_pages.pop(slot, []))
+        self.c128_pages.release(self._req_c128.pop(slot, []))
+        self.page_table[slot] = -1
+        self.c128_table[slot] = -1
+        self._free_slots.append(slot)
+
+    def comp_state_reset(self, slot: int) -> None:
+        for st in list(self.comp_state.values()) + list(self.index_state.values()):
+            st[slot, 0] = float("-inf")
+            st[slot, 1:] = 0
+
+    @property
+    def free_tokens(self) -> int:
+        return self.pages.free * self.TOKENS_PER_PAGE

@@ -1,0 +1,450 @@
+"""DeepSeek-V4-Flash-shape model: MLA over one 512-wide latent with C4/C128 compressed sparse
+attention, SWA, attention sinks, grouped output projection and sigmoid-routed MoE.
+
+Reference behaviour: `srt/models/deepseek_v4.py`, `srt/layers/attention/dsv4/{compressor_v2,indexer}.py`
+and `deepseek_v4_backend.py` of the reference's SGLang fork (third_party/README.md:275-279; the
+fork sources are absent, so the layer internals below are packmla's own design constrained by
+the shapes and contracts the reference records, see packmla/config.py).
+
+Per layer (decode, B tokens of B different requests):
+  h = rmsnorm(x);  [q_lora | kv] = h Wqkv_a;  q = rmsnorm(q_lora) Wq_b (heads x 512), tail RoPE
+  kv -> Native record in the layer's SWA ring (norm kv_norm, RoPE at the token position)
+  compressor (ratio 4 / 128): online-softmax pooling of h Wc_kv with gates h Wc_gate + ape;
+     a completed group -> C4 record (Native or Packed store) / C128 record (Native)
+  indexer (C4): score(r) = sum_h w_h relu(q_idx_h . k_r), top-512 records (k_r FP8, pooled like kv)
+  o = sparse MLA attention over [SWA ring ; selected C4 | all C128 records] with sink
+  x += (o grouped-projected by Wo_a, then Wo_b)              -> TP all-reduce
+  x += shared(rmsnorm(x)) + sum_k w_k expert_k(rmsnorm(x))   -> TP/EP all-reduce
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from ..config import EngineConfig, ModelConfig
+from ..formats import abi, codec
+from ..kv.pool import KVPool
+from ..ops import attention as attn_ops
+from ..ops import kv as kv_ops
+from ..ops import moe as moe_ops
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * w).to(torch.bfloat16)
+
+
+def rotate_q_tail(q: torch.Tensor, freqs_f32: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    """q [B, H, 512] bf16; rotate coords 448..511 by freqs[pos] (fp32 math), round to bf16."""
+    fr = freqs_f32[pos]  # [B, 32, 2]
+    c, s = fr[:, None, :, 0], fr[:, None, :, 1]
+    tail = q[..., abi.NOPE_DIM:].float().unflatten(-1, (abi.ROPE_PAIRS, 2))
+    re, im = tail[..., 0], tail[..., 1]
+    rot = torch.stack((re * c - im * s, re * s + im * c), -1).flatten(-2)
+    return torch.cat((q[..., :abi.NOPE_DIM], rot.to(torch.bfloat16)), -1)
+
+
+@dataclass
+class StepMeta:
+    """Per-step attention metadata shared by all layers of a kind (device tensors)."""
+
+    positions: torch.Tensor  # [B] int64
+    req_slots: torch.Tensor  # [B] int64
+    swa_slots: torch.Tensor  # [B, 128] int32
+    swa_len: torch.Tensor  # [B] int32
+    swa_write: torch.Tensor  # [B] int64 ring slot of this token
+    c4_phys: torch.Tensor  # [B, R4] int32 physical record of logical record r (or -1)
+    c4_count: torch.Tensor  # [B] int64 complete C4 records visible to the query
+    c4_write: torch.Tensor  # [B] int64 physical slot of the record completed now, else -1
+    c128_slots: torch.Tensor  # [B, R128] int32 (masked by count)
+    c128_pos: torch.Tensor  # [B, R128] int32
+    c128_len: torch.Tensor  # [B] int32
+    c128_write: torch.Tensor  # [B] int64
+
+
+class V4FlashModel:
+    def __init__(self, cfg: ModelConfig, weights: dict, pool: KVPool, comm=None):
+        self.cfg = cfg
+        self.W = weights
+        self.pool = pool
+        self.comm = comm
+        self.device = pool.device
+        self.kv_format = pool.kv_format
+        meta = weights["meta"]
+        self.world = meta["world"]
+        self.expert_base = meta["expert_base"]
+        self.local_experts = meta["local_experts"]
+        self.heads = cfg.num_heads // self.world
+        self.groups = cfg.o_groups // self.world
+        self.scale = 1.0 / math.sqrt(cfg.latent_dim)
+        self.freqs = kv_ops.freq_table_f32(codec.rope_table(cfg.max_position, cfg.rope_theta)).to(self.device)
+        self.r4max = pool.max_context // abi.C4_RATIO
+        self.r128max = max(1, pool.max_context // abi.C128_RATIO)
+        self.topk = min(cfg.index_topk, self.r4max)
+        self.ar_hook = None  # optional fused projection + all-reduce (parallel.fused)
+
+    # ------------------------------------------------------------------ helpers
+    def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.comm is None or self.world == 1:
+            return t
+        return self.comm.all_reduce(t)
+
+    def csa_planes(self, layer: int):
+        p = self.pool
+        if self.kv_format == "direct":
+            return None, attn_ops.PackedPlanes(p.c4_values[layer], p.c4_bitmap[layer], p.c4_scales[layer])
+        return p.c4_native[layer], None
+
+    # ------------------------------------------------------------------ metadata
+    def step_meta(self, positions: torch.Tensor, req_slots: torch.Tensor) -> StepMeta:
+        """Decode metadata (graph-capturable: no host synchronization)."""
+        dev = self.device
+        p = self.pool
+        B = positions.shape[0]
+        W = self.cfg.window
+        pos = positions.long()
+        req = req_slots.long()
+        ar = torch.arange(W, device=dev, dtype=torch.int64)
+        swa_slots = (req[:, None] * W + ar[None]).int()
+        swa_len = torch.clamp(pos + 1, max=W).int()
+        swa_write = req * W + pos % W
+        r = torch.arange(self.r4max, device=dev, dtype=torch.int64)
+        pt = p.page_table[req]  # [B, pages]
+        page = pt.gather(1, (r // abi.RECORDS_PER_PAGE).clamp(max=pt.shape[1] - 1)[None].expand(B, -1)).long()
+        c4_phys = torch.where(page >= 0, page * abi.RECORDS_PER_PAGE + r % abi.RECORDS_PER_PAGE, -1)
+        c4_count = (pos + 1) // abi.C4_RATIO
+        rec = pos // abi.C4_RATIO
+        done4 = (pos % abi.C4_RATIO) == abi.C4_RATIO - 1
+        w4 = c4_phys.gather(1, rec.clamp(max=self.r4max - 1)[:, None])[:, 0]
+        c4_write = torch.where(done4 & (rec < self.r4max), w4, torch.full_like(w4, -1))
+        r2 = torch.arange(self.r128max, device=dev, dtype=torch.int64)
+        ct = p.c128_table[req]
+        page2 = ct.gather(1, (r2 // abi.RECORDS_PER_PAGE).clamp(max=ct.shape[1] - 1)[None].expand(B, -1)).long()
+        phys2 = torch.where(page2 >= 0, page2 * abi.RECORDS_PER_PAGE + r2 % abi.RECORDS_PER_PAGE, -1)
+        n128 = (pos + 1) // abi.C128_RATIO
+        c128_slots = torch.where(r2[None] < n128[:, None], phys2, torch.full_like(phys2, -1)).int()
+        c128_pos = (r2 * abi.C128_RATIO).int()[None].expand(B, -1).contiguous()
+        rec2 = pos // abi.C128_RATIO
+        done2 = (pos % abi.C128_RATIO) == abi.C128_RATIO - 1
+        w2 = phys2.gather(1, rec2.clamp(max=self.r128max - 1)[:, None])[:, 0]
+        c128_write = torch.where(done2 & (rec2 < self.r128max), w2, torch.full_like(w2, -1))
+        c128_len = torch.full((B,), self.r128max, dtype=torch.int32, device=dev)
+        return StepMeta(pos, req, swa_slots, swa_len, swa_write, c4_phys.int(), c4_count, c4_write,
+                        c128_slots, c128_pos, c128_len, c128_write)
+
+    # ------------------------------------------------------------------ compressor
+    def _pool_update(self, state: torch.Tensor, req: torch.Tensor, gate: torch.Tensor, val: torch.Tensor,
+                     done: torch.Tensor) -> torch.Tensor:
+        """One token of online-softmax pooling per row; returns the pooled raw row (valid if done)."""
+        st = state[req]  # [B, 3, D]
+        m, l, acc = st[:, 0], st[:, 1], st[:, 2]
+        m_new = torch.maximum(m, gate)
+        a = torch.exp(m - m_new)
+        e = torch.exp(gate - m_new)
+        l = l * a + e
+        acc = acc * a + e * val
+        raw = acc / l
+        keep = (~done)[:, None]
+        new = torch.stack((torch.where(keep, m_new, torch.full_like(m_new, float("-inf"))),
+                           torch.where(keep, l, torch.zeros_like(l)),
+                           torch.where(keep, acc, torch.zeros_like(acc))), 1)
+        state[req] = new
+        return raw
+
+    def _compress_decode(self, layer: int, h: torch.Tensor, meta: StepMeta) -> None:
+        lw = self.W["layers"][layer]
+        ratio = self.cfg.compress_ratios[layer]
+        pos = meta.positions
+        slot = pos % ratio
+        kv = (h @ lw["wc_kv"].T).float()
+        gate = (h @ lw["wc_gate"].T).float() + lw["c_ape"][slot]
+        done = slot == ratio - 1
+        raw = self._pool_update(self.pool.comp_state[layer], meta.req_slots, gate, kv, done).contiguous()
+        if ratio == abi.C4_RATIO:
+            self._store_c4(layer, raw, meta.c4_write, (pos // ratio) * ratio)
+            k = (h @ lw["wi_k"].T).float()
+            kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot]
+            kraw = self._pool_update(self.pool.index_state[layer], meta.req_slots, kg, k, done)
+            self._store_index_keys(layer, kraw, meta.c4_write)
+        else:
+            kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, meta.c128_write, (pos // ratio) * ratio,
+                                self.freqs, self.pool.c128_native[layer])
+
+    def _store_c4(self, layer: int, raw: torch.Tensor, slots: torch.Tensor, rope_pos: torch.Tensor) -> None:
+        lw = self.W["layers"][layer]
+        p = self.pool
+        if self.kv_format == "direct":
+            kv_ops.packed_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, p.c4_values[layer], p.c4_bitmap[layer],
+                                p.c4_scales[layer])
+        else:
+            kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rope_pos, self.freqs, p.c4_native[layer])
+
+    def _store_index_keys(self, layer: int, kraw: torch.Tensor, slots: torch.Tensor) -> None:
+        """FP8 index key + fp32 scale per record; rows with slot -1 go to the pool's trash row."""
+        amax = kraw.abs().amax(-1, keepdim=True)
+        scale = torch.where(amax > 0, amax / abi.E4M3_MAX, torch.ones_like(amax))
+        q8 = (kraw / scale).to(torch.float8_e4m3fn).view(torch.uint8)
+        keys, sc = self.pool.index_keys[layer], self.pool.index_scales[layer]
+        trash = keys.shape[0] - 1
+        idx = torch.where(slots >= 0, slots, torch.full_like(slots, trash))
+        keys[idx] = q8
+        sc[idx] = scale[:, 0]
+
+    # ------------------------------------------------------------------ indexer
+    def _index_topk(self, layer: int, q_lora: torch.Tensor, h: torch.Tensor, phys: torch.Tensor,
+                    count: torch.Tensor, r_limit: int):
+        """Top-k C4 records per query: returns (slots int32 [B,K], rope positions int32 [B,K])."""
+        lw = self.W["layers"][layer]
+        cfg = self.cfg
+        B = q_lora.shape[0]
+        qi = (q_lora @ lw["wi_q"].T).view(B, cfg.index_heads, cfg.index_dim).float()
+        wi = (h @ lw["wi_w"].T).float() * (cfg.index_heads ** -0.5) * (cfg.index_dim ** -0.5)
+        ph = phys[:, :r_limit].long()
+        safe = ph.clamp(min=0)
+        keys = self.pool.index_keys[layer][safe].view(torch.float8_e4m3fn).float()  # [B, R, d]
+        keys = keys * self.pool.index_scales[layer][safe][..., None]
+        s = torch.relu(torch.bmm(qi, keys.transpose(1, 2)))  # [B, Hi, R]
+        score = (s * wi[:, :, None]).sum(1)  # [B, R]
+        r = torch.arange(r_limit, device=self.device)
+        visible = (r[None] < count[:, None]) & (ph >= 0)
+        score = torch.where(visible, score, torch.full_like(score, float("-inf")))
+        k = min(self.topk, r_limit)
+        vals, idx = torch.topk(score, k, dim=1)
+        sel = ph.gather(1, idx)
+        slots = torch.where(vals > float("-inf"), sel, torch.full_like(sel, -1)).int()
+        return slots, (idx * abi.C4_RATIO).int()
+
+    # ------------------------------------------------------------------ layer
+    def _attention_block(self, layer: int, x: torch.Tensor, meta: StepMeta) -> torch.Tensor:
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
+        B = x.shape[0]
+        h = rmsnorm(x, lw["attn_norm"], cfg.rms_eps)
+        qkv = h @ lw["wqkv_a"].T
+        q_lora = rmsnorm(qkv[:, :cfg.q_lora_rank], lw["q_norm"], cfg.rms_eps)
+        kv_raw = qkv[:, cfg.q_lora_rank:].float().contiguous()
+        kv_ops.native_store(kv_raw, lw["kv_norm"], cfg.rms_eps, meta.swa_write, meta.positions, self.freqs,
+                            self.pool.swa[layer])
+        q = (q_lora @ lw["wq_b"].T).view(B, self.heads, cfg.latent_dim)
+        q = rotate_q_tail(q, self.freqs, meta.positions).contiguous()
+        ratio = cfg.compress_ratios[layer]
+        if ratio:
+            self._compress_decode(layer, h, meta)
+        empty = torch.zeros(B, 1, dtype=torch.int32, device=self.device) - 1
+        if ratio == abi.C4_RATIO:
+            csa_slots, csa_pos = self._index_topk(layer, q_lora, h, meta.c4_phys, meta.c4_count, self.r4max)
+            csa_len = torch.full((B,), csa_slots.shape[1], dtype=torch.int32, device=self.device)
+            pool_native, planes = self.csa_planes(layer)
+        elif ratio == abi.C128_RATIO:
+            csa_slots, csa_pos, csa_len = meta.c128_slots, meta.c128_pos, meta.c128_len
+            pool_native, planes = self.pool.c128_native[layer], None
+        else:
+            csa_slots, csa_pos = empty, empty
+            csa_len = torch.zeros(B, dtype=torch.int32, device=self.device)
+            pool_native, planes = self.pool.swa[layer], None
+        o, _ = attn_ops.sparse_mla_decode(
+            q, self.pool.swa[layer], meta.swa_slots, meta.swa_len, csa_slots, csa_pos, csa_len, self.freqs,
+            lw["sink"], self.scale, meta.positions.int(), csa_pool=pool_native, csa_planes=planes)
+        o = o.view(B, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
+        o_lora = torch.bmm(o, lw["wo_a"]).transpose(0, 1).reshape(B, self.groups * cfg.o_lora_rank)
+        if self.ar_hook is not None:
+            return self.ar_hook(o_lora, lw["wo_b"])
+        return self._all_reduce(o_lora @ lw["wo_b"].T)
+
+    def _moe_block(self, layer: int, x: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
+        h = rmsnorm(x, lw["ffn_norm"], cfg.rms_eps)
+        topk_ids, topk_w = moe_ops.route(h, lw["gate"], lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
+        out = moe_ops.experts(h, topk_ids, topk_w, lw, self.expert_base, self.local_experts, cfg.expert_format)
+        g_u = h @ lw["shared_w13"].T
+        il = g_u.shape[1] // 2
+        act = (F.silu(g_u[:, :il].float()) * g_u[:, il:].float()).to(torch.bfloat16)
+        out = out + (act @ lw["shared_w2"].T).float()
+        return self._all_reduce(out.to(torch.bfloat16))
+
+    # ------------------------------------------------------------------ decode
+    def decode(self, tokens: torch.Tensor, positions: torch.Tensor, req_slots: torch.Tensor) -> torch.Tensor:
+        """One decode step for B requests -> logits [B, vocab] (fp32)."""
+        meta = self.step_meta(positions, req_slots)
+        x = self.W["embed"][tokens]
+        for layer in range(self.cfg.num_layers):
+            x = x + self._attention_block(layer, x, meta)
+            x = x + self._moe_block(layer, x)
+        x = rmsnorm(x, self.W["final_norm"], self.cfg.rms_eps)
+        return (x @ self.W["lm_head"].T).float()
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, tokens: torch.Tensor, start: int, req_slot: int) -> torch.Tensor:
+        """Process prompt tokens [T] of one request at positions start..start+T-1 (pages ensured).
+
+        Returns logits of the last token.  Attention of each prompt token uses the same kernel
+        as decode with per-token row lists; SWA rows of the chunk live in a scratch Native pool.
+        """
+        cfg = self.cfg
+        dev = self.device
+        T = tokens.shape[0]
+        W = cfg.window
+        pos = torch.arange(start, start + T, device=dev, dtype=torch.int64)
+        req = torch.full((T,), req_slot, device=dev, dtype=torch.int64)
+        # scratch rows j <-> token start - (W-1) + j
+        n_scr = T + W - 1
+        scr_pages = (n_scr + abi.RECORDS_PER_PAGE - 1) // abi.RECORDS_PER_PAGE
+        j = torch.arange(W, device=dev)
+        swa_slots = (torch.arange(T, device=dev)[:, None] + j[None]).int()
+        tok_of = start - (W - 1) + swa_slots.long()
+        swa_slots = torch.where(tok_of >= 0, swa_slots, torch.full_like(swa_slots, -1)).contiguous()
+        swa_len = torch.full((T,), W, dtype=torch.int32, device=dev)
+        prev = torch.arange(start - (W - 1), start, device=dev)
+        prev_ok = prev >= 0
+        meta_pos = pos
+        x = self.W["embed"][tokens]
+        pt = self.pool.page_table[req_slot].long()
+        r_all = torch.arange(self.r4max, device=dev)
+        pg = pt[(r_all // abi.RECORDS_PER_PAGE).clamp(max=pt.shape[0] - 1)]
+        c4_phys_row = torch.where(pg >= 0, pg * abi.RECORDS_PER_PAGE + r_all % abi.RECORDS_PER_PAGE, -1)
+        ct = self.pool.c128_table[req_slot].long()
+        r2 = torch.arange(self.r128max, device=dev)
+        pg2 = ct[(r2 // abi.RECORDS_PER_PAGE).clamp(max=ct.shape[0] - 1)]
+        c128_phys_row = torch.where(pg2 >= 0, pg2 * abi.RECORDS_PER_PAGE + r2 % abi.RECORDS_PER_PAGE, -1)
+        for layer in range(cfg.num_layers):
+            lw = self.W["layers"][layer]
+            h = rmsnorm(x, lw["attn_norm"], cfg.rms_eps)
+            qkv = h @ lw["wqkv_a"].T
+            q_lora = rmsnorm(qkv[:, :cfg.q_lora_rank], lw["q_norm"], cfg.rms_eps)
+            kv_raw = qkv[:, cfg.q_lora_rank:].float().contiguous()
+            scratch = torch.zeros(scr_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+            if bool(prev_ok.any()):
+                ring = req_slot * W + prev[prev_ok] % W
+                recs = kv_ops.native_pool_read(self.pool.swa[layer], ring)
+                _native_pool_write(scratch, torch.nonzero(prev_ok)[:, 0], recs)
+            kv_ops.native_store(kv_raw, lw["kv_norm"], cfg.rms_eps, torch.arange(W - 1, W - 1 + T, device=dev),
+                                pos, self.freqs, scratch)
+            last = slice(max(0, T - W), T)
+            kv_ops.native_store(kv_raw[last].contiguous(), lw["kv_norm"], cfg.rms_eps, req_slot * W + pos[last] % W,
+                                pos[last], self.freqs, self.pool.swa[layer])
+            q = (q_lora @ lw["wq_b"].T).view(T, self.heads, cfg.latent_dim)
+            q = rotate_q_tail(q, self.freqs, pos).contiguous()
+            ratio = cfg.compress_ratios[layer]
+            if ratio:
+                self._compress_prefill(layer, h, pos, req_slot, c4_phys_row, c128_phys_row)
+            if ratio == abi.C4_RATIO:
+                count = (pos + 1) // abi.C4_RATIO
+                n_vis = int(min(self.r4max, (start + T) // abi.C4_RATIO))
+                lim = max(1, n_vis)
+                csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, h, c4_phys_row, count, lim)
+                csa_len = torch.full((T,), csa_slots.shape[1], dtype=torch.int32, device=dev)
+                pool_native, planes = self.csa_planes(layer)
+            elif ratio == abi.C128_RATIO:
+                n128 = (pos + 1) // abi.C128_RATIO
+                lim = max(1, int(min(self.r128max, (start + T) // abi.C128_RATIO)))
+                rr = torch.arange(lim, device=dev)
+                csa_slots = torch.where(rr[None] < n128[:, None], c128_phys_row[:lim][None].expand(T, -1),
+                                        torch.full((T, lim), -1, device=dev, dtype=torch.int64)).int().contiguous()
+                csa_pos = (rr * abi.C128_RATIO).int()[None].expand(T, -1).contiguous()
+                csa_len = torch.full((T,), lim, dtype=torch.int32, device=dev)
+                pool_native, planes = self.pool.c128_native[layer], None
+            else:
+                csa_slots = torch.full((T, 1), -1, dtype=torch.int32, device=dev)
+                csa_pos = torch.zeros((T, 1), dtype=torch.int32, device=dev)
+                csa_len = torch.zeros(T, dtype=torch.int32, device=dev)
+                pool_native, planes = self.pool.swa[layer], None
+            o, _ = attn_ops.sparse_mla_decode(
+                q, scratch, swa_slots, swa_len, csa_slots, csa_pos, csa_len, self.freqs, lw["sink"], self.scale,
+                meta_pos.int(), csa_pool=pool_native, csa_planes=planes)
+            o = o.view(T, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
+            o_lora = torch.bmm(o, lw["wo_a"]).transpose(0, 1).reshape(T, self.groups * cfg.o_lora_rank)
+            x = x + self._all_reduce(o_lora @ lw["wo_b"].T)
+            x = x + self._moe_block(layer, x)
+        x = rmsnorm(x[-1:], self.W["final_norm"], cfg.rms_eps)
+        return (x @ self.W["lm_head"].T).float()[0]
+
+    def _index_topk_chunked(self, layer, q_lora, h, phys_row, count, lim, block: int = 256):
+        T = q_lora.shape[0]
+        outs_s, outs_p = [], []
+        for t0 in range(0, T, block):
+            t1 = min(T, t0 + block)
+            ph = phys_row[:lim][None].expand(t1 - t0, -1).int()
+            s, p = self._index_topk(layer, q_lora[t0:t1], h[t0:t1], ph, count[t0:t1], lim)
+            outs_s.append(s)
+            outs_p.append(p)
+        return torch.cat(outs_s).contiguous(), torch.cat(outs_p).contiguous()
+
+    def _compress_prefill(self, layer, h, pos, req_slot, c4_phys_row, c128_phys_row):
+        """Sequential-equivalent pooling over the chunk; stores every record completed in it."""
+        lw = self.W["layers"][layer]
+        ratio = self.cfg.compress_ratios[layer]
+        slot_in = pos % ratio
+        kv = (h @ lw["wc_kv"].T).float()
+        gate = (h @ lw["wc_gate"].T).float() + lw["c_ape"][slot_in]
+        raw, rec = _pool_chunk(self.pool.comp_state[layer], req_slot, gate, kv, pos, ratio)
+        if rec.numel():
+            if ratio == abi.C4_RATIO:
+                slots = c4_phys_row[rec.clamp(max=self.r4max - 1)]
+                slots = torch.where(rec < self.r4max, slots, -1)
+                self._store_c4(layer, raw, slots, rec * ratio)
+                k = (h @ lw["wi_k"].T).float()
+                kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot_in]
+                kraw, _ = _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
+                self._store_index_keys(layer, kraw, slots)
+            else:
+                slots = c128_phys_row[rec.clamp(max=self.r128max - 1)]
+                slots = torch.where(rec < self.r128max, slots, -1)
+                kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rec * ratio, self.freqs,
+                                    self.pool.c128_native[layer])
+        elif ratio == abi.C4_RATIO:
+            k = (h @ lw["wi_k"].T).float()
+            kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot_in]
+            _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
+
+
+def _pool_chunk(state: torch.Tensor, req_slot: int, gate: torch.Tensor, val: torch.Tensor, pos: torch.Tensor,
+                ratio: int):
+    """Online-softmax pooling of consecutive tokens into groups of `ratio`.
+
+    Returns (raw rows of groups completed in the chunk [G, D], their record indices [G]);
+    the trailing partial group is left in `state[req_slot]`.
+    """
+    T, D = gate.shape
+    p0 = int(pos[0])
+    first_group = p0 // ratio
+    grp = (pos // ratio) - first_group  # [T] 0-based group ids in the chunk
+    ng = int(grp[-1]) + 1
+    st = state[req_slot]
+    # per-group max over tokens (and the carried state for group 0)
+    gmax = torch.full((ng, D), float("-inf"), device=gate.device)
+    gmax = gmax.scatter_reduce(0, grp[:, None].expand(-1, D), gate, reduce="amax")
+    gmax[0] = torch.maximum(gmax[0], st[0])
+    e = torch.exp(gate - gmax[grp])
+    l = torch.zeros(ng, D, device=gate.device).index_add_(0, grp, e)
+    acc = torch.zeros(ng, D, device=gate.device).index_add_(0, grp, e * val)
+    carry = torch.exp(st[0] - gmax[0])
+    l[0] = l[0] + st[1] * carry
+    acc[0] = acc[0] + st[2] * carry
+    last_pos = p0 + T - 1
+    complete_last = (last_pos % ratio) == ratio - 1
+    n_done = ng if complete_last else ng - 1
+    raw = acc[:n_done] / l[:n_done]
+    rec = torch.arange(first_group, first_group + n_done, device=gate.device)
+    if complete_last:
+        state[req_slot, 0] = float("-inf")
+        state[req_slot, 1:] = 0
+    else:
+        state[req_slot, 0] = gmax[-1]
+        state[req_slot, 1] = l[-1]
+        state[req_slot, 2] = acc[-1]
+    return raw.contiguous(), rec
+
+
+def _native_pool_write(pool: torch.Tensor, slots: torch.Tensor, recs: torch.Tensor) -> None:
+    pages = pool.view(-1, abi.NATIVE_PAGE_BYTES)
+    s = slots.long()
+    page, r = s // abi.RECORDS_PER_PAGE, s % abi.RECORDS_PER_PAGE
+    d_idx = r[:, None] * abi.NATIVE_DATA_BYTES + torch.arange(abi.NATIVE_DATA_BYTES, device=pool.device)[None]
+    s_idx = (abi.RECORDS_PER_PAGE * abi.NATIVE_DATA_BYTES + r[:, None] * abi.NATIVE_SCALE_BYTES
+             + torch.arange(abi.NATIVE_SCALE_BYTES, device=pool.device)[None])
+    pages[page[:, None], d_idx] = recs[:, :abi.NATIVE_DATA_BYTES]
+    pages[page[:, None], s_idx] = recs[:, abi.NATIVE_DATA_BYTES:]

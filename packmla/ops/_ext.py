@@ -11,6 +11,31 @@ _EXT = None
 _ERR: dict[int, torch.Tensor] = {}
 
 
+# kernels launched per extension entry point (for the bench's launch count)
+KERNELS_PER_CALL = {"native_store": 1, "packed_store": 1, "sparse_mla_decode": 2, "moe_fp4": 3, "umma_probe": 1}
+
+
+class _Counting:
+    """Proxy that counts kernel launches of extension calls while `enabled`."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.enabled = False
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not self.enabled:
+            return fn
+        per = KERNELS_PER_CALL.get(name, 1)
+
+        def wrapped(*a, **k):
+            self.launches += per
+            return fn(*a, **k)
+
+        return wrapped
+
+
 def ext():
     global _EXT
     if _EXT is None:
@@ -20,7 +45,7 @@ def ext():
             raise RuntimeError(
                 "packmla CUDA extension is not built; run `python setup.py build_ext --inplace`"
             ) from exc
-        _EXT = _C
+        _EXT = _Counting(_C)
     return _EXT
 
 

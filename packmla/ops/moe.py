@@ -1,0 +1,107 @@
+"""MoE routing and expert computation.
+
+Routing (DeepSeek-style sigmoid scores): s = sigmoid(h G^T); the top-k of s + bias choose the
+experts, their weights are s normalized over the chosen k, times `routed_scaling`.
+
+Experts on this rank are [expert_base, expert_base + local_experts).  Tokens are replicated on
+every TP/EP rank, so each rank computes its local experts' contribution and the caller's
+all-reduce combines ranks (the MoE down-projection partial sums).
+
+* MXFP4 experts on CUDA: csrc/moe_fp4.cu (routing lists, gate/up with SiLU, down + weighted
+  scatter-add), reading E2M1 weights with UE8M0 block scales directly.
+* BF16 experts (tiny CPU configs, tests): PyTorch reference.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import error_word, ext
+
+
+def route(h: torch.Tensor, gate_w: torch.Tensor, bias: torch.Tensor, topk: int, scaling: float):
+    logits = (h @ gate_w.T).float()
+    scores = torch.sigmoid(logits)
+    _, ids = torch.topk(scores + bias, topk, dim=-1)
+    w = scores.gather(1, ids)
+    w = w / w.sum(-1, keepdim=True) * scaling
+    return ids.int(), w
+
+
+def experts_reference(h, topk_ids, topk_w, w13, w2, expert_base, local_experts):
+    """BF16 experts, fp32 accumulation: sum_k w_k * W2 (silu(W1 h) * W3 h) over local experts."""
+    T = h.shape[0]
+    out = torch.zeros(T, w2.shape[1], dtype=torch.float32, device=h.device)
+    I = w13.shape[1] // 2
+    for le in range(local_experts):
+        mask = topk_ids == (expert_base + le)
+        tok, kk = torch.nonzero(mask, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        x = h[tok]
+        gu = (x @ w13[le].T).float()
+        act = (F.silu(gu[:, :I]) * gu[:, I:]).to(torch.bfloat16)
+        y = (act @ w2[le].T).float()
+        out.index_add_(0, tok, y * topk_w[tok, kk][:, None])
+    return out
+
+
+def fp4_dequant(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """MXFP4 [..., K/2] + UE8M0 [..., K/32] -> fp32 [..., K] (reference path, any device)."""
+    lut = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0],
+                       device=w.device)
+    lo = lut[(w & 0xF).long()]
+    hi = lut[(w >> 4).long()]
+    vals = torch.stack((lo, hi), -1).flatten(-2)
+    scale = torch.exp2(s.float() - 127.0).repeat_interleave(32, -1)
+    return vals * scale
+
+
+class MoEWorkspace:
+    """Routing lists and activations with stable pointers (graph-capturable)."""
+
+    def __init__(self, max_tokens: int, topk: int, local_experts: int, inter: int, device):
+        n = max_tokens * topk
+        self.offsets = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
+        self.slot_token = torch.zeros(n, dtype=torch.int32, device=device)
+        self.slot_weight = torch.zeros(n, dtype=torch.float32, device=device)
+        self.active = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
+        self.act = torch.zeros(n, inter, dtype=torch.bfloat16, device=device)
+        self.max_tokens = max_tokens
+
+
+_WS: dict = {}
+
+
+def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, workspace=None):
+    if expert_format != "mxfp4":
+        return experts_reference(h, topk_ids, topk_w, lw["w13"], lw["w2"], expert_base, local_experts)
+    if not h.is_cuda:
+        # CPU: dequantize the touched experts (tests only)
+        T = h.shape[0]
+        out = torch.zeros(T, lw["w2"].shape[1], dtype=torch.float32)
+        I = lw["w13"].shape[1] // 2
+        for le in range(local_experts):
+            tok, kk = torch.nonzero(topk_ids == expert_base + le, as_tuple=True)
+            if tok.numel() == 0:
+                continue
+            w13 = fp4_dequant(lw["w13"][le], lw["s13"][le])
+            w2 = fp4_dequant(lw["w2"][le], lw["s2"][le])
+            gu = h[tok].float() @ w13.T
+            act = (F.silu(gu[:, :I]) * gu[:, I:]).to(torch.bfloat16).float()
+            out.index_add_(0, tok, (act @ w2.T) * topk_w[tok, kk][:, None])
+        return out
+    T, H = h.shape
+    k = topk_ids.shape[1]
+    I = lw["w13"].shape[1] // 2
+    ws = workspace
+    if ws is None:
+        key = (h.device.index, T, k, local_experts, I)
+        ws = _WS.get(key)
+        if ws is None:
+            ws = MoEWorkspace(T, k, local_experts, I, h.device)
+            _WS[key] = ws
+    out = torch.zeros(T, H, dtype=torch.float32, device=h.device)
+    ext().moe_fp4(h, topk_ids, topk_w, expert_base, lw["w13"], lw["s13"], lw["w2"], lw["s2"], ws.offsets,
+                  ws.slot_token, ws.slot_weight, ws.active, ws.act, out, error_word(h.device))
+    return out

@@ -1,0 +1,76 @@
+"""CPU: model prefill/decode consistency, engine scheduling, capacity accounting."""
+import torch
+
+from packmla.config import EngineConfig, ModelConfig
+from packmla.engine.engine import Engine, SamplingParams
+from packmla.kv.pool import KVPool, plan_capacity
+from packmla.models.v4flash import V4FlashModel
+from packmla.models.weights import init_weights
+
+
+def _rel(a, b):
+    return ((a - b).norm() / b.norm()).item()
+
+
+def test_prefill_chunking_and_decode_agree():
+    cfg = ModelConfig.tiny(num_layers=4)
+    W = init_weights(cfg)
+    for fmt in ("direct", "native"):
+        pool = KVPool(cfg, EngineConfig(kv_cache_format=fmt, device="cpu"), 16, 4, 1024, "cpu")
+        m = V4FlashModel(cfg, W, pool)
+        toks = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(0))
+        s1 = pool.admit(300)
+        full = m.prefill(toks, 0, s1)
+        s2 = pool.admit(300)
+        m.prefill(toks[:200], 0, s2)
+        m.prefill(toks[200:299], 200, s2)
+        step = m.decode(toks[299:300], torch.tensor([299]), torch.tensor([s2]))[0]
+        assert _rel(step, full) < 2e-2
+
+
+def test_engine_batch_invariance_and_metrics():
+    cfg = ModelConfig.tiny(num_layers=3)
+    ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=4, cuda_graph_bs=[1, 2, 4])
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (70, 130, 5)]
+    eng = Engine.build(cfg, ecfg, "cpu", max_context=512)
+    outs = eng.generate(prompts, SamplingParams(max_new_tokens=5))
+    assert [len(o) for o in outs] == [5, 5, 5]
+    alone = Engine.build(cfg, ecfg, "cpu", max_context=512).generate([prompts[1]], SamplingParams(max_new_tokens=5))
+    assert alone[0] == outs[1]
+    m = eng.metrics.snapshot()
+    assert m["requests_finished"] == 3 and m["prefill_tokens"] == 205
+    assert eng.pool.pages.free == eng.pool.num_pages  # all pages returned
+
+
+def test_capacity_ratio_packed_vs_native():
+    cfg = ModelConfig()
+    budget = 30 << 30
+    native = plan_capacity(cfg, EngineConfig(kv_cache_format="native"), budget)
+    direct = plan_capacity(cfg, EngineConfig(kv_cache_format="direct"), budget)
+    ratio = direct.max_total_tokens / native.max_total_tokens
+    assert ratio >= 1.21, ratio
+
+
+def test_engine_config_rejects_unsupported():
+    import pytest
+
+    with pytest.raises(ValueError):
+        EngineConfig(kv_cache_format="direct", keep_count=192).validate()
+    with pytest.raises(ValueError):
+        EngineConfig(kv_cache_format="packed").validate()
+    with pytest.raises(ValueError):
+        EngineConfig(kv_cache_format="native", enable_hierarchical_cache=True, keep_count=128).validate()
+
+
+def test_pool_exhaustion_and_release():
+    cfg = ModelConfig.tiny(num_layers=2)
+    pool = KVPool(cfg, EngineConfig(device="cpu"), 4, 3, 2048, "cpu")
+    s = pool.admit(700)  # 3 pages
+    try:
+        pool.admit(600)
+        raise AssertionError("expected exhaustion")
+    except MemoryError:
+        pass
+    pool.release(s)
+    assert pool.pages.free == 4

@@ -1,0 +1,100 @@
+"""GPU: MXFP4 MoE kernel, model/engine on the CUDA kernels vs the CPU oracle path, graph replay."""
+import pytest
+import torch
+
+from helpers import small_gpu_config
+from packmla.config import EngineConfig
+from packmla.engine.engine import Engine, SamplingParams
+from packmla.models.weights import init_weights
+from packmla.ops import check_errors
+from packmla.ops import moe as moe_ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (5, 8, 2), (40, 16, 4), (3, 4, 4)])
+def test_moe_fp4_matches_dequant_reference(cuda, T, E, k):
+    cfg = small_gpu_config(n_routed_experts=E, moe_topk=k)
+    W = init_weights(cfg, device="cpu", seed=T)
+    lw = W["layers"][0]
+    g = torch.Generator().manual_seed(T)
+    h = torch.randn(T, cfg.hidden_size, generator=g).bfloat16()
+    ids, w = moe_ops.route(h.float().bfloat16(), lw["gate"], lw["gate_bias"], k, 1.0)
+    ref = moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4")  # CPU dequant reference
+    glw = {kk: v.cuda() for kk, v in lw.items()}
+    out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), glw, 0, E, "mxfp4")
+    check_errors(cuda)
+    assert _rel(out.cpu(), ref) < 2e-2
+
+
+def test_moe_fp4_expert_parallel_partials_sum(cuda):
+    cfg = small_gpu_config(n_routed_experts=8, moe_topk=2)
+    W1 = init_weights(cfg, 0, 1, "cpu")
+    h = torch.randn(6, cfg.hidden_size).bfloat16()
+    lw = W1["layers"][0]
+    ids, w = moe_ops.route(h, lw["gate"], lw["gate_bias"], 2, 1.0)
+    full = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), {k: v.cuda() for k, v in lw.items()}, 0, 8, "mxfp4")
+    parts = []
+    for r in range(2):
+        Wr = init_weights(cfg, r, 2, "cpu")
+        lr = {k: v.cuda() for k, v in Wr["layers"][0].items()}
+        parts.append(moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), lr, Wr["meta"]["expert_base"], 4, "mxfp4"))
+    assert _rel(parts[0] + parts[1], full) < 1e-5
+
+
+@pytest.mark.parametrize("fmt", ["direct", "native"])
+def test_engine_gpu_matches_cpu_oracle(cuda, fmt):
+    cfg = small_gpu_config()
+    W = init_weights(cfg, device="cpu", seed=3)
+    Wg = {"layers": [{k: v.cuda() for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
+          **{k: v.cuda() for k, v in W.items() if torch.is_tensor(v)}}
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g)
+    res = {}
+    for dev, weights in (("cpu", W), ("cuda", Wg)):
+        ecfg = EngineConfig(kv_cache_format=fmt, device=dev, max_running_requests=2, cuda_graph_bs=[1, 2],
+                            chunked_prefill_size=128, disable_cuda_graph=True)
+        eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
+        slot = eng.pool.admit(400)
+        l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
+        l2 = eng.model.prefill(prompt[200:].to(dev), 200, slot)
+        l3 = eng.model.decode(prompt[:1].to(dev), torch.tensor([300], device=dev), torch.tensor([slot], device=dev))
+        res[dev] = (l1.cpu(), l2.cpu(), l3[0].cpu())
+    check_errors(cuda)
+    for a, b in zip(res["cuda"], res["cpu"]):
+        assert _rel(a, b) < 3e-2
+
+
+def test_decode_graph_replay_matches_eager(cuda):
+    cfg = small_gpu_config()
+    W = init_weights(cfg, device=cuda, seed=5)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (77, 140, 9)]
+    outs = {}
+    for graphs in (False, True):
+        ecfg = EngineConfig(kv_cache_format="direct", max_running_requests=4, cuda_graph_bs=[1, 2, 4],
+                            chunked_prefill_size=64, disable_cuda_graph=not graphs)
+        eng = Engine.build(cfg, ecfg, cuda, max_context=1024, max_requests=4, kv_bytes=64 << 20, weights=W)
+        if graphs:
+            eng.runner.capture()
+        outs[graphs] = eng.generate(prompts, SamplingParams(max_new_tokens=8))
+        eng.runner.release()
+    check_errors(cuda)
+    assert outs[True] == outs[False]
+
+
+def test_moe_fp4_full_width_shapes(cuda):
+    """Hidden 4096 / intermediate 2048 (the V4-Flash widths) with few experts."""
+    cfg = small_gpu_config(hidden_size=4096, moe_intermediate=2048, n_routed_experts=4, moe_topk=2)
+    W = init_weights(cfg, device="cpu", seed=11)
+    lw = W["layers"][0]
+    h = torch.randn(9, 4096, generator=torch.Generator().manual_seed(2)).bfloat16()
+    ids, w = moe_ops.route(h, lw["gate"], lw["gate_bias"], 2, 1.0)
+    ref = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4")
+    out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), {k: v.cuda() for k, v in lw.items()}, 0, 4, "mxfp4")
+    check_errors(cuda)
+    assert _rel(out.cpu(), ref) < 2e-2
