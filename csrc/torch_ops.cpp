@@ -136,7 +136,8 @@ torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::
   TORCH_CHECK(b.is_cuda() && b.scalar_type() == torch::kBFloat16 && b.is_contiguous());
   check_err(err);
   int K, N;
-  if (mode == 0) {
+  TORCH_CHECK(mode >= 0 && mode <= 2, "probe mode 0, 1 or 2");
+  if (mode == 0 || mode == 2) {
     TORCH_CHECK(a.dim() == 2 && a.size(0) == 128 && b.dim() == 2 && b.size(1) == a.size(1));
     K = a.size(1);
     N = b.size(0);

@@ -3,6 +3,8 @@
 // mode 0: D[128 x N] = A[128 x K] * B[N x K]^T   with A, B K-major (SW128), as S^T = K Q^T.
 // mode 1: D[128 x N] = A^T * B                    with A given as [K x 128] (MN-major view) and
 //                                                 B given as [K x N] (MN-major), as O^T = V^T P^T.
+// mode 2: D[128 x N] = A[128 x K] * B[N x K]^T   with A written into TMEM (lane = row, two f16 per
+//                                                 column) by tcgen05.st and B K-major in shared memory.
 // One CTA of 128 threads; K <= 128, N in {16, 32, 64}.  Used only by tests.
 #include "launchers.h"
 #include "common/sm100.cuh"
@@ -19,9 +21,9 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(const __nv_bfloat16*
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 49152);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (warp == 0) { pm::tmem_alloc(tslot, 64); pm::tmem_relinquish(); }
+  if (warp == 0) { pm::tmem_alloc(tslot, 128); pm::tmem_relinquish(); }
   if (tid == 0) { pm::mbar_init(bar, 1); pm::fence_mbar_init(); }
-  if (mode == 0) {
+  if (mode == 0 || mode == 2) {
     // A rows = 128 (M), K contiguous; chunk stride = 128 rows * 128 B
     for (int idx = tid; idx < 128 * (K / 8); idx += 128) {
       const int row = idx / (K / 8), u = idx % (K / 8);
@@ -52,9 +54,29 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(const __nv_bfloat16*
   __syncthreads();
   pm::tc_fence_after();
   const uint32_t tmem = *tslot;
+  if (mode == 2) {
+    // row (32 warp + lane): K bf16 -> K/2 columns starting at column 64
+    for (int c0 = 0; c0 < K / 2; c0 += 16) {
+      uint32_t v[16];
+      for (int i = 0; i < 16; ++i)
+        v[i] = *reinterpret_cast<const uint32_t*>(a + (32 * warp + lane) * K + 2 * (c0 + i));
+      pm::tmem_st16u(tmem + 64 + c0 + ((uint32_t)(32 * warp) << 16), v);
+    }
+    pm::tmem_wait_st();
+    pm::tc_fence_before();
+    __syncthreads();
+    pm::tc_fence_after();
+  }
   if (tid == 0) {
     const uint32_t a0 = pm::smem_u32(sA), b0 = pm::smem_u32(sB);
-    if (mode == 0) {
+    if (mode == 2) {
+      const uint32_t idesc = pm::make_idesc_f16(128, N, 1, 0, 0);
+      for (int k = 0; k < K / 16; ++k) {
+        const uint32_t koff = (k * 32) & 127;
+        const uint64_t bd = pm::make_sdesc(b0 + (k >> 2) * (N * 128) + koff, 16, 1024);
+        pm::umma_f16_tmem_a(tmem, tmem + 64 + 8 * k, bd, idesc, k > 0);
+      }
+    } else if (mode == 0) {
       const uint32_t idesc = pm::make_idesc_f16(128, N, 1, 0, 0);
       for (int k = 0; k < K / 16; ++k) {
         const uint32_t koff = (k * 32) & 127;
@@ -84,7 +106,7 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(const __nv_bfloat16*
   }
   pm::tc_fence_before();
   __syncthreads();
-  if (warp == 0) pm::tmem_dealloc(tmem, 64);
+  if (warp == 0) pm::tmem_dealloc(tmem, 128);
 }
 
 }  // namespace

@@ -55,11 +55,12 @@ def test_packed_store_byte_exact_and_ties(cuda, rows):
     assert torch.equal(gv.cpu(), values)
 
 
-@pytest.mark.parametrize("mode,K,N", [(0, 128, 64), (0, 64, 16), (1, 128, 64), (1, 32, 16), (1, 64, 32)])
+@pytest.mark.parametrize("mode,K,N", [(0, 128, 64), (0, 64, 16), (1, 128, 64), (1, 32, 16), (1, 64, 32),
+                                      (2, 128, 16), (2, 64, 64), (2, 32, 32)])
 def test_umma_operand_layouts(cuda, mode, K, N):
     g = torch.Generator().manual_seed(K + N + mode)
     err = torch.zeros(4, dtype=torch.int32, device=cuda)
-    if mode == 0:
+    if mode in (0, 2):
         a = torch.randn(128, K, generator=g).bfloat16()
         b = torch.randn(N, K, generator=g).bfloat16()
         ref = a.float() @ b.float().T
