@@ -100,7 +100,10 @@ __device__ __forceinline__ RowRef row_ref(const DecodeParams& p, int b, int i, i
 // Raw bytes of one row, as two 16-byte pieces per lane:
 //   A -> stage[16 lane]       (native data units 0..31; packed values 0..15, bitmap 16..19, scales 20)
 //   B -> stage[512 + 16 lane] (native data units 32..35 for lanes 0..3, scales for lane 4)
-__device__ __forceinline__ void load_row_raw(const DecodeParams& p, int kind, int slot, int lane, uint4& A, uint4& B) {
+// Packed rows: lanes 24..31, which rotate the tail units 56..63, also prefetch their four RoPE
+// (cos, sin) pairs into A and B, so no dependent global load sits on the expansion path.
+__device__ __forceinline__ void load_row_raw(const DecodeParams& p, int kind, int slot, int pos, int lane, uint4& A,
+                                             uint4& B) {
   A = zero4();
   B = zero4();
   if (kind == 1 || kind == 2) {
@@ -120,9 +123,16 @@ __device__ __forceinline__ void load_row_raw(const DecodeParams& p, int kind, in
     else if (lane == 20) {
       const uint2 s = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)slot * 8);
       A = make_uint4(s.x, s.y, 0, 0);
+    } else if (lane >= 24) {
+      const float* f = p.freqs + (int64_t)pos * 64 + 8 * (lane - 24);
+      A = *reinterpret_cast<const uint4*>(f);
+      B = *reinterpret_cast<const uint4*>(f + 4);
     }
   }
 }
+
+// Exclusive prefix of kept-coordinate counts over bitmap words: lane w (< 8) holds it for word w.
+__device__ __forceinline__ int wprefix_of(int wpre, int w) { return __shfl_sync(0xffffffffu, wpre, w); }
 
 // Warp-cooperative: staged raw row -> 64 units of 8 BF16 in the swizzled dense tile (row `trow`).
 __device__ __forceinline__ void expand_row(const DecodeParams& p, int kind, int pos, int trow, uint8_t* stage,
@@ -130,6 +140,17 @@ __device__ __forceinline__ void expand_row(const DecodeParams& p, int kind, int 
   *reinterpret_cast<uint4*>(stage + 16 * lane) = A;
   if (lane < 5) *reinterpret_cast<uint4*>(stage + 512 + 16 * lane) = B;
   __syncwarp();
+  int wpre = 0;
+  if (kind == 3) {
+    const int pc = lane < 8 ? __popcll(reinterpret_cast<const uint64_t*>(stage + 256)[lane]) : 0;
+    int incl = pc;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    wpre = incl - pc;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int u = lane + 32 * h;
@@ -146,25 +167,23 @@ __device__ __forceinline__ void expand_row(const DecodeParams& p, int kind, int 
       const uint64_t* words = reinterpret_cast<const uint64_t*>(stage + 256);
       const int w = u >> 3, shift = 8 * (u & 7);
       const uint64_t word = words[w];
-      int rank = __popcll(word & ((1ull << shift) - 1ull));
-      for (int k = 0; k < w; ++k) rank += __popcll(words[k]);
+      const int rank = wprefix_of(wpre, w) + __popcll(word & ((1ull << shift) - 1ull));
       const uint32_t bits = (uint32_t)(word >> shift) & 0xFFu;
       const float s = pm::exp2i((int)stage[320 + w] - 127);
       float v[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        v[i] = 0.f;
-        if (bits & (1u << i)) {
-          const uint16_t c = stage[rank++];
-          v[i] = __half2float(__low2half(pm::e4m3x2_to_h2(c))) * s;
-        }
+        const int k = __popc(bits & ((1u << i) - 1u));
+        const uint16_t c = stage[min(rank + k, 255)];
+        const float f = __half2float(__low2half(pm::e4m3x2_to_h2(c))) * s;
+        v[i] = (bits >> i) & 1u ? f : 0.f;
       }
-      if (u >= 56) {  // RoPE tail: pairs (2i, 2i+1), pair index 4 (u - 56) + i
-        const float* f = p.freqs + (int64_t)pos * 64;
+      if (u >= 56) {  // RoPE tail: pairs (2i, 2i+1), pair index 4 (u - 56) + i; (cos, sin) in A, B
+        const float cs[8] = {__uint_as_float(A.x), __uint_as_float(A.y), __uint_as_float(A.z), __uint_as_float(A.w),
+                             __uint_as_float(B.x), __uint_as_float(B.y), __uint_as_float(B.z), __uint_as_float(B.w)};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int pair = 4 * (u - 56) + i;
-          const float c = f[2 * pair], sn = f[2 * pair + 1];
+          const float c = cs[2 * i], sn = cs[2 * i + 1];
           const float re = __bfloat162float(__float2bfloat16_rn(v[2 * i]));
           const float im = __bfloat162float(__float2bfloat16_rn(v[2 * i + 1]));
           v[2 * i] = __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, sn));
@@ -258,32 +277,42 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   const uint32_t idesc_o = pm::make_idesc_f16(128, kHG, 1, 1, 1);
   bool ok = true;
 
+  uint8_t* stage = smem + kOffStage + warp * kStageBytes;
+  struct Batch {
+    uint4 A[8], B[8];
+    int kind[8], pos[8];
+  } bk;
+  // rows warp + 8 (8 k + j), j = 0..7, of tile tt: index lookups by lanes 0..7, then raw loads
+  auto load_batch = [&](int tt, int k) {
+    const int tb = row0 + tt * kTile;
+    const int tv = min(kTile, row1 - tb);
+    RowRef mine{0, -1, 0};
+    const int r = warp + 8 * (8 * k + (lane & 7));
+    if (lane < 8 && r < tv) mine = row_ref(p, b, tb + r, nswa, ntot);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      bk.kind[j] = __shfl_sync(0xffffffffu, mine.kind, j);
+      const int slot = __shfl_sync(0xffffffffu, mine.slot, j);
+      bk.pos[j] = __shfl_sync(0xffffffffu, mine.pos, j);
+      if (p.debug & 4) { bk.A[j] = zero4(); bk.B[j] = zero4(); }
+      else load_row_raw(p, bk.kind[j], slot, bk.pos[j], lane, bk.A[j], bk.B[j]);
+    }
+  };
+
   for (int t = 0; t < ntiles && ok; ++t) {
     const int tbase = row0 + t * kTile;
     const int tvalid = min(kTile, row1 - tbase);
-    // ---- 1. gather + expand 128 rows (warp w: rows w + 8 i), two batches of 8 rows in flight
-    uint8_t* stage = smem + kOffStage + warp * kStageBytes;
+    // ---- 1. gather + expand 128 rows (warp w: rows w + 8 i), two batches of 8 rows; batch 0 of
+    //         this tile was loaded while the previous tile's P.V MMAs ran
+    if (t == 0) load_batch(0, 0);
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
-      RowRef mine{0, -1, 0};
-      {
-        const int r = warp + 8 * (8 * k + (lane & 7));
-        if (lane < 8 && r < tvalid) mine = row_ref(p, b, tbase + r, nswa, ntot);
-      }
-      uint4 A[8], Bv[8];
-      int kinds[8], poss[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        kinds[j] = __shfl_sync(0xffffffffu, mine.kind, j);
-        const int slot = __shfl_sync(0xffffffffu, mine.slot, j);
-        poss[j] = __shfl_sync(0xffffffffu, mine.pos, j);
-        load_row_raw(p, kinds[j], slot, lane, A[j], Bv[j]);
-      }
+      if (k == 1) load_batch(t, 1);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int r = warp + 8 * (8 * k + j);
-        expand_row(p, kinds[j], poss[j], r, stage, sKV, lane, A[j], Bv[j]);
-        if (lane == 0) rowvalid[r] = kinds[j] != 0;
+        if (!(p.debug & 2)) expand_row(p, bk.kind[j], bk.pos[j], r, stage, sKV, lane, bk.A[j], bk.B[j]);
+        if (lane == 0) rowvalid[r] = bk.kind[j] != 0;
       }
     }
     pm::fence_proxy_async_smem();
@@ -293,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     // ---- 2. S^T = K Q^T
     if (tid == 0) {
 #pragma unroll 1
-      for (int k = 0; k < kD / 16; ++k) {
+      for (int k = 0; k < kD / 16 && !(p.debug & 1); ++k) {
         const uint32_t koff = (k * 32) & 127;
         const uint64_t ad = pm::make_sdesc(kv_base + (k >> 2) * (kTile * 128) + koff, 16, 1024);
         const uint64_t bd = pm::make_sdesc(q_base + (k >> 2) * (kHG * 128) + koff, 16, 1024);
@@ -396,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     // ---- 4. O^T += V^T P^T
     if (tid == 0 && !flags[1]) {
 #pragma unroll 1
-      for (int db = 0; db < 4; ++db) {
+      for (int db = 0; db < 4 && !(p.debug & 1); ++db) {
 #pragma unroll 1
         for (int k = 0; k < kTile / 16; ++k) {
           const uint64_t ad = pm::make_sdesc(kv_base + (2 * db) * (kTile * 128) + k * 2048, kTile * 128, 1024);
@@ -406,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
       }
       pm::umma_commit(bar_o);
     }
+    if (t + 1 < ntiles) load_batch(t + 1, 0);  // overlaps the P.V MMAs
     if (!flags[1]) {
       if (!pm::mbar_wait(bar_o, t & 1, p.err, 2)) flags[1] = 1;
     }

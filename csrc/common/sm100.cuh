@@ -58,12 +58,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and records an error) after `limit` polls.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: try_wait suspends in hardware between polls; gives up (and records an error)
+// once `timeout_ns` of wall time has passed on the GPU's global timer.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site,
-                                          uint32_t limit = (1u << 24)) {
-  for (uint32_t i = 0; i < limit; ++i) {
+                                          uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(32);
+    if ((i & 15) == 0 && globaltimer_ns() - t0 > timeout_ns) break;
   }
   report_error(err, kWaitTimeout, site);
   return false;
@@ -157,6 +166,24 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int ab_bf16,
          | ((uint32_t)b_mn << 16)          // B major
          | ((uint32_t)(N >> 3) << 17)      // N / 8
          | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+
+// Instruction descriptor for kind::f8f6f4 with fp32 accumulation.
+// a_fmt/b_fmt: 0 = E4M3, 1 = E5M2 (3 = E2M3, 4 = E3M2, 5 = E2M1); both operands K-major here.
+__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, int b_fmt) {
+  return (1u << 4) | ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T for 8/6/4-bit operands (K = 32 per instruction), one thread.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.

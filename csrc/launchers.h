@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 void launch_native_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
                          const int64_t* positions, const float* freqs, int64_t freq_rows, uint8_t* pool,
@@ -39,6 +40,7 @@ struct DecodeParams {
   float* part_o;             // [B, splits, H, 512]
   float* part_ml;            // [B, splits, H, 2]
   int* err;
+  int debug;                 // diagnostics only: bit0 skips the MMAs, bit1 skips row expansion
 };
 
 void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,
@@ -50,3 +52,21 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
                     int expert_base, int E, const uint8_t* w13, const uint8_t* s13, const uint8_t* w2,
                     const uint8_t* s2, int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active,
                     __nv_bfloat16* act, float* out, int num_sms, cudaStream_t stream);
+
+void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
+                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, cudaStream_t stream);
+void launch_moe_fp4_tc(const __nv_bfloat16* x, int T, int H, int I, int E, int max_slots, const int32_t* offsets,
+                       const int32_t* slot_token, const float* slot_weight, const int32_t* active, const uint8_t* w13t,
+                       const uint8_t* s13t, const uint8_t* w2t, const uint8_t* s2t, __half* xs, __half* act_s,
+                       float* out, int num_sms, int* err, int debug, cudaStream_t stream);
+
+void launch_index_key_store(const float* kraw, int64_t stride, const int64_t* slots, uint8_t* keys, float* kscales,
+                            int64_t nrows, int R, int* err, cudaStream_t stream);
+void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, const uint8_t* keys,
+                         const float* kscales, int64_t nrows, const int32_t* phys, int64_t phys_stride,
+                         const int64_t* count, int R, float* scores, int64_t score_stride, int num_sms, int* err,
+                         cudaStream_t stream);
+void launch_index_topk(const float* scores, int64_t stride, int B, int R, int k, const int32_t* phys,
+                       int64_t phys_stride, int ratio, int32_t* out_slots, int32_t* out_pos, cudaStream_t stream);
+
+void launch_tc_latency_probe(int iters, int n_mma, int n, long long* out, int* err, cudaStream_t stream);

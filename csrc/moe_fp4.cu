@@ -266,6 +266,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const MoeParams p
 
 }  // namespace
 
+void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
+                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, cudaStream_t stream) {
+  if (T == 0) return;
+  moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
+                                                           slot_token, slot_weight, active);
+}
+
 void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const int32_t* topk_ids, const float* topk_w,
                     int expert_base, int E, const uint8_t* w13, const uint8_t* s13, const uint8_t* w2,
                     const uint8_t* s2, int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active,

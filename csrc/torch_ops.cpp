@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cstdlib>
 #include "launchers.h"
 
 namespace {
@@ -19,6 +20,11 @@ void check_err(const torch::Tensor& err) {
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == torch::kInt32 && err.numel() >= 4, "err must be CUDA int32[4]");
 }
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+// Diagnostic ablation switch read from PACKMLA_KERNEL_DEBUG (0 in normal operation).
+int debug_flags() {
+  const char* v = std::getenv("PACKMLA_KERNEL_DEBUG");
+  return v ? std::atoi(v) : 0;
+}
 }  // namespace
 
 void native_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, torch::Tensor positions,
@@ -126,18 +132,20 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.part_o = part_o.data_ptr<float>();
   p.part_ml = part_ml.data_ptr<float>();
   p.err = err.data_ptr<int>();
+  p.debug = debug_flags();
   launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::Tensor err) {
-  TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.is_contiguous());
-  TORCH_CHECK(b.is_cuda() && b.scalar_type() == torch::kBFloat16 && b.is_contiguous());
+  const auto want = mode == 3 ? torch::kUInt8 : torch::kBFloat16;
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == want && a.is_contiguous());
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == want && b.is_contiguous());
   check_err(err);
   int K, N;
-  TORCH_CHECK(mode >= 0 && mode <= 2, "probe mode 0, 1 or 2");
-  if (mode == 0 || mode == 2) {
+  TORCH_CHECK(mode >= 0 && mode <= 3, "probe mode 0..3");
+  if (mode == 0 || mode == 2 || mode == 3) {
     TORCH_CHECK(a.dim() == 2 && a.size(0) == 128 && b.dim() == 2 && b.size(1) == a.size(1));
     K = a.size(1);
     N = b.size(0);
@@ -146,7 +154,8 @@ torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::
     K = a.size(0);
     N = b.size(1);
   }
-  TORCH_CHECK(K % 16 == 0 && K <= 128 && (N == 16 || N == 32 || N == 64), "probe supports K<=128, N in {16,32,64}");
+  TORCH_CHECK(K % (mode == 3 ? 32 : 16) == 0 && K <= 128 && (N == 16 || N == 32 || N == 64),
+              "probe supports K<=128, N in {16,32,64}");
   const c10::cuda::CUDAGuard g(a.device());
   auto d = torch::zeros({128, N}, a.options().dtype(torch::kFloat32));
   launch_umma_probe(a.data_ptr(), b.data_ptr(), K, N, (int)mode, d.data_ptr<float>(), err.data_ptr<int>(), stream());
@@ -192,11 +201,121 @@ void moe_fp4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int6
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+int num_sms_of(const torch::Device& d) {
+  static int cache[64] = {0};
+  const int idx = d.index() < 0 ? 0 : d.index();
+  if (cache[idx] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&cache[idx], cudaDevAttrMultiProcessorCount, idx));
+  return cache[idx];
+}
+
+// Tiled MXFP4 experts (packmla/ops/moe.py tile_experts): w13t [E, I/64, H/256, 128, 128],
+// s13t [E, I/64, H/256, 128, 8], w2t [E, H/128, I/256, 128, 128], s2t [E, H/128, I/256, 128, 8].
+void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base,
+                torch::Tensor w13t, torch::Tensor s13t, torch::Tensor w2t, torch::Tensor s2t, torch::Tensor offsets,
+                torch::Tensor slot_token, torch::Tensor slot_weight, torch::Tensor active, torch::Tensor xs,
+                torch::Tensor act_s, torch::Tensor out, torch::Tensor err) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
+  check_err(err);
+  const int T = h.size(0), H = h.size(1);
+  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.dim() == 2 && topk_ids.size(0) == T && topk_ids.is_contiguous());
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.sizes() == topk_ids.sizes() && topk_w.is_contiguous());
+  const int k = topk_ids.size(1);
+  TORCH_CHECK(w13t.scalar_type() == torch::kUInt8 && w13t.dim() == 5 && w13t.size(3) == 128 && w13t.size(4) == 128 &&
+              w13t.is_contiguous());
+  const int E = w13t.size(0), I = w13t.size(1) * 64;
+  TORCH_CHECK(w13t.size(2) * 256 == H, "w13t k-tiles do not match hidden size");
+  TORCH_CHECK(s13t.scalar_type() == torch::kUInt8 && s13t.dim() == 5 && s13t.size(0) == E && s13t.size(1) == I / 64 &&
+              s13t.size(2) == H / 256 && s13t.size(3) == 128 && s13t.size(4) == 8 && s13t.is_contiguous());
+  TORCH_CHECK(w2t.scalar_type() == torch::kUInt8 && w2t.dim() == 5 && w2t.size(0) == E && w2t.size(1) * 128 == H &&
+              w2t.size(2) * 256 == I && w2t.size(3) == 128 && w2t.size(4) == 128 && w2t.is_contiguous());
+  TORCH_CHECK(s2t.scalar_type() == torch::kUInt8 && s2t.dim() == 5 && s2t.size(0) == E && s2t.size(1) * 128 == H &&
+              s2t.size(2) * 256 == I && s2t.size(3) == 128 && s2t.size(4) == 8 && s2t.is_contiguous());
+  TORCH_CHECK(H % 256 == 0 && I % 256 == 0 && H % 128 == 0, "hidden and intermediate must be multiples of 256");
+  TORCH_CHECK(E <= 4096, "too many local experts");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() >= E + 1);
+  TORCH_CHECK(active.scalar_type() == torch::kInt32 && active.numel() >= E + 1);
+  TORCH_CHECK(slot_token.scalar_type() == torch::kInt32 && slot_token.numel() >= (int64_t)T * k);
+  TORCH_CHECK(slot_weight.scalar_type() == torch::kFloat32 && slot_weight.numel() >= (int64_t)T * k);
+  TORCH_CHECK(xs.scalar_type() == torch::kFloat16 && xs.is_contiguous() && xs.numel() >= (int64_t)T * k * H);
+  TORCH_CHECK(act_s.scalar_type() == torch::kFloat16 && act_s.is_contiguous() && act_s.numel() >= (int64_t)T * k * I);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == (int64_t)T * H);
+  const c10::cuda::CUDAGuard g(h.device());
+  launch_moe_route(topk_ids.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, k, (int)expert_base, E,
+                   offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
+                   active.data_ptr<int32_t>(), stream());
+  launch_moe_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), T, H, I, E, T * k,
+                    offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
+                    active.data_ptr<int32_t>(), w13t.data_ptr<uint8_t>(), s13t.data_ptr<uint8_t>(),
+                    w2t.data_ptr<uint8_t>(), s2t.data_ptr<uint8_t>(), reinterpret_cast<__half*>(xs.data_ptr()),
+                    reinterpret_cast<__half*>(act_s.data_ptr()), out.data_ptr<float>(), num_sms_of(h.device()),
+                    err.data_ptr<int>(), debug_flags(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, torch::Tensor err) {
+  check_err(err);
+  TORCH_CHECK(n == 16 || n == 32 || n == 64 || n == 128 || n == 256, "n in {16,32,64,128,256}");
+  const c10::cuda::CUDAGuard g(err.device());
+  auto out = torch::zeros({1}, err.options().dtype(torch::kInt64));
+  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                          err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out.item<int64_t>();
+}
+
+void index_key_store(torch::Tensor kraw, torch::Tensor slots, torch::Tensor keys, torch::Tensor kscales,
+                     torch::Tensor err) {
+  TORCH_CHECK(kraw.is_cuda() && kraw.scalar_type() == torch::kFloat32 && kraw.dim() == 2 && kraw.size(1) == 128 &&
+              kraw.stride(1) == 1 && kraw.stride(0) % 4 == 0, "kraw must be float32 [R, 128]");
+  TORCH_CHECK(slots.scalar_type() == torch::kInt64 && slots.numel() == kraw.size(0) && slots.is_contiguous());
+  TORCH_CHECK(keys.scalar_type() == torch::kUInt8 && keys.dim() == 2 && keys.size(1) == 128 && keys.is_contiguous());
+  TORCH_CHECK(kscales.scalar_type() == torch::kFloat32 && kscales.numel() == keys.size(0));
+  check_err(err);
+  const c10::cuda::CUDAGuard g(kraw.device());
+  launch_index_key_store(kraw.data_ptr<float>(), kraw.stride(0), slots.data_ptr<int64_t>(), keys.data_ptr<uint8_t>(),
+                         kscales.data_ptr<float>(), keys.size(0), kraw.size(0), err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// scores[b, r] for r < R; then top-k physical slots / RoPE rows.
+void index_select(torch::Tensor q, torch::Tensor w, torch::Tensor keys, torch::Tensor kscales, torch::Tensor phys,
+                  torch::Tensor count, int64_t R, torch::Tensor scores, torch::Tensor out_slots, torch::Tensor out_pos,
+                  torch::Tensor err) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == 128 && q.is_contiguous());
+  const int B = q.size(0), H = q.size(1);
+  TORCH_CHECK(H <= 64, "at most 64 indexer heads");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.numel() == (int64_t)B * H);
+  TORCH_CHECK(keys.scalar_type() == torch::kUInt8 && keys.dim() == 2 && keys.size(1) == 128 && keys.is_contiguous());
+  TORCH_CHECK(kscales.scalar_type() == torch::kFloat32 && kscales.numel() == keys.size(0) && kscales.is_contiguous());
+  TORCH_CHECK(phys.scalar_type() == torch::kInt32 && phys.dim() == 2 && phys.size(0) == B && phys.stride(1) == 1);
+  TORCH_CHECK(R >= 1 && R <= phys.size(1));
+  TORCH_CHECK(count.scalar_type() == torch::kInt64 && count.numel() == B && count.is_contiguous());
+  TORCH_CHECK(scores.scalar_type() == torch::kFloat32 && scores.dim() == 2 && scores.size(0) == B &&
+              scores.size(1) >= R && scores.stride(1) == 1);
+  TORCH_CHECK(out_slots.scalar_type() == torch::kInt32 && out_slots.dim() == 2 && out_slots.size(0) == B &&
+              out_slots.is_contiguous());
+  TORCH_CHECK(out_pos.scalar_type() == torch::kInt32 && out_pos.sizes() == out_slots.sizes() && out_pos.is_contiguous());
+  check_err(err);
+  const c10::cuda::CUDAGuard g(q.device());
+  // the keys pool keeps one trailing row for writes without a destination: pages use the rest
+  launch_index_logits(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), w.data_ptr<float>(), B, H,
+                      keys.data_ptr<uint8_t>(), kscales.data_ptr<float>(), keys.size(0), phys.data_ptr<int32_t>(),
+                      phys.stride(0), count.data_ptr<int64_t>(), (int)R, scores.data_ptr<float>(), scores.stride(0),
+                      num_sms_of(q.device()), err.data_ptr<int>(), stream());
+  launch_index_topk(scores.data_ptr<float>(), scores.stride(0), B, (int)R, out_slots.size(1), phys.data_ptr<int32_t>(),
+                    phys.stride(0), 4, out_slots.data_ptr<int32_t>(), out_pos.data_ptr<int32_t>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
   m.def("packed_store", &packed_store, "FP32 rows -> Packed 328 B C4 records (planes)");
   m.def("umma_probe", &umma_probe, "tcgen05 operand-layout self-test (one MMA)");
+  m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)");
+  m.def("index_key_store", &index_key_store, "FP8 index keys (swizzled rows) + fp32 scales");
+  m.def("index_select", &index_select, "FP8 tcgen05 indexer logits + radix top-k");
+  m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
   m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine");
 }

@@ -5,6 +5,8 @@
 //                                                 B given as [K x N] (MN-major), as O^T = V^T P^T.
 // mode 2: D[128 x N] = A[128 x K] * B[N x K]^T   with A written into TMEM (lane = row, two f16 per
 //                                                 column) by tcgen05.st and B K-major in shared memory.
+// mode 3: D[128 x N] = A[128 x K] * B[N x K]^T   with E4M3 operands (kind::f8f6f4), K-major SW128;
+//                                                 a, b passed as uint8 codes (K <= 128 bytes per row).
 // One CTA of 128 threads; K <= 128, N in {16, 32, 64}.  Used only by tests.
 #include "launchers.h"
 #include "common/sm100.cuh"
@@ -23,7 +25,21 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(const __nv_bfloat16*
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (warp == 0) { pm::tmem_alloc(tslot, 128); pm::tmem_relinquish(); }
   if (tid == 0) { pm::mbar_init(bar, 1); pm::fence_mbar_init(); }
-  if (mode == 0 || mode == 2) {
+  if (mode == 3) {
+    // 8-bit operands: a row of K <= 128 codes is at most one 128-byte swizzle atom row
+    const uint8_t* a8 = reinterpret_cast<const uint8_t*>(a);
+    const uint8_t* b8 = reinterpret_cast<const uint8_t*>(b);
+    for (int idx = tid; idx < 128 * (K / 16); idx += 128) {
+      const int row = idx / (K / 16), u = idx % (K / 16);
+      *reinterpret_cast<uint4*>(sA + pm::sw128_offset(row, 16 * u, 0)) =
+          *reinterpret_cast<const uint4*>(a8 + row * K + 16 * u);
+    }
+    for (int idx = tid; idx < N * (K / 16); idx += 128) {
+      const int row = idx / (K / 16), u = idx % (K / 16);
+      *reinterpret_cast<uint4*>(sB + pm::sw128_offset(row, 16 * u, 0)) =
+          *reinterpret_cast<const uint4*>(b8 + row * K + 16 * u);
+    }
+  } else if (mode == 0 || mode == 2) {
     // A rows = 128 (M), K contiguous; chunk stride = 128 rows * 128 B
     for (int idx = tid; idx < 128 * (K / 8); idx += 128) {
       const int row = idx / (K / 8), u = idx % (K / 8);
@@ -69,7 +85,14 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(const __nv_bfloat16*
   }
   if (tid == 0) {
     const uint32_t a0 = pm::smem_u32(sA), b0 = pm::smem_u32(sB);
-    if (mode == 2) {
+    if (mode == 3) {
+      const uint32_t idesc = pm::make_idesc_f8(128, N, 0, 0);
+      for (int k = 0; k < K / 32; ++k) {
+        const uint64_t ad = pm::make_sdesc(a0 + 32 * k, 16, 1024);
+        const uint64_t bd = pm::make_sdesc(b0 + 32 * k, 16, 1024);
+        pm::umma_f8(tmem, ad, bd, idesc, k > 0);
+      }
+    } else if (mode == 2) {
       const uint32_t idesc = pm::make_idesc_f16(128, N, 1, 0, 0);
       for (int k = 0; k < K / 16; ++k) {
         const uint32_t koff = (k * 32) & 127;

@@ -1,0 +1,199 @@
+"""Model-free kernel microbenchmarks (device time with CUDA events, L2 flushed between runs).
+
+    python -m packmla.bench.microbench moe   [--tokens 40] [--experts 256] [--topk 8]
+    python -m packmla.bench.microbench decode [--batch 16] [--heads 128] [--context 32768] [--topk 2048]
+    python -m packmla.bench.microbench store  [--rows 24]
+
+Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
+measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
+
+Reference protocol: 30 rounds after 10 warm-ups, CUDA-graph-free device timing of the
+operation only (benchmarks/microbench/dsv4-flash-decode-store/README.md:11-23).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "of measured"
+    return 6650.0, "of fallback"
+
+
+class L2Flush:
+    def __init__(self, device, nbytes: int = 256 << 20):
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def time_op(fn, rounds: int, warmup: int, device, flush: L2Flush | None) -> float:
+    """Mean microseconds over `rounds` (each round timed alone, L2 flushed before it)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    total = 0.0
+    for _ in range(rounds):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize(device)
+        total += s.elapsed_time(e)
+    return total / rounds * 1e3
+
+
+def bench_moe(args, dev):
+    from packmla.config import ModelConfig
+    from packmla.models.weights import _fp4_expert
+    from packmla.ops import check_errors
+    from packmla.ops import moe as moe_ops
+
+    cfg = ModelConfig()
+    H, I, E, k = cfg.hidden_size, cfg.moe_intermediate, args.experts, args.topk
+    g = torch.Generator(device=dev).manual_seed(0)
+    lw = {}
+    lw["w13"], lw["s13"] = _fp4_expert(E, 2 * I, H, g, dev)
+    lw["w2"], lw["s2"] = _fp4_expert(E, H, I, g, dev)
+    moe_ops.prepare_experts(lw)
+    h = torch.randn(args.tokens, H, device=dev, generator=g).bfloat16()
+    gate = torch.randn(E, H, device=dev, generator=g).bfloat16() * H ** -0.5
+    ids, w = moe_ops.route(h, gate, torch.zeros(E, device=dev), k, 1.0)
+    active = int(torch.unique(ids).numel())
+    fn = lambda: moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4")  # noqa: E731
+    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev))
+    check_errors(dev)
+    per_expert = (2 * I * H + H * I) // 2 + (2 * I * H + H * I) // 32
+    nbytes = active * per_expert
+    peak, tag = measured_hbm_gbs()
+    gbs = nbytes / us / 1e3
+    return {"case": "moe_fp4", "tokens": args.tokens, "experts": E, "topk": k, "active_experts": active,
+            "us": round(us, 2), "weight_bytes": nbytes, "GBps": round(gbs, 1),
+            "hbm_fraction": round(gbs / peak, 3), "peak_note": tag}
+
+
+def bench_decode(args, dev):
+    from packmla.formats import abi, codec
+    from packmla.ops import attention as attn_ops
+    from packmla.ops import check_errors
+    from packmla.ops import kv as kv_ops
+
+    B, Hh, K, W = args.batch, args.heads, args.topk, 128
+    records = args.context // abi.C4_RATIO
+    g = torch.Generator(device=dev).manual_seed(0)
+    freqs = kv_ops.freq_table_f32(codec.rope_table(args.context + 1024)).to(dev)
+    w = torch.ones(512, device=dev)
+    rows = B * records  # each query owns its own context
+    swa_rows = B * W
+    swa_pool = torch.zeros(((swa_rows + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+    kv_ops.native_store(torch.randn(swa_rows, 512, device=dev, generator=g), w, 1e-6,
+                        torch.arange(swa_rows, device=dev), torch.arange(swa_rows, device=dev) % args.context, freqs,
+                        swa_pool)
+    planes, pool = None, None
+    chunk = 1 << 18
+    if args.kv_format == "direct":
+        planes = attn_ops.PackedPlanes(torch.zeros(rows, 256, dtype=torch.uint8, device=dev),
+                                       torch.zeros(rows, 8, dtype=torch.int64, device=dev),
+                                       torch.zeros(rows, 8, dtype=torch.uint8, device=dev))
+        for a in range(0, rows, chunk):
+            b = min(rows, a + chunk)
+            kv_ops.packed_store(torch.randn(b - a, 512, device=dev, generator=g), w, 1e-6,
+                                torch.arange(a, b, device=dev), planes.values, planes.bitmap, planes.scales)
+        rec_bytes = abi.PACKED_RECORD_BYTES
+    else:
+        pool = torch.zeros(((rows + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+        for a in range(0, rows, chunk):
+            b = min(rows, a + chunk)
+            kv_ops.native_store(torch.randn(b - a, 512, device=dev, generator=g), w, 1e-6,
+                                torch.arange(a, b, device=dev), (torch.arange(a, b, device=dev) % records) * 4,
+                                freqs, pool)
+        rec_bytes = abi.NATIVE_RECORD_BYTES
+    base = (torch.arange(B, device=dev) * records)[:, None]
+    sel = torch.stack([torch.randperm(records, device=dev, generator=g)[:K] for _ in range(B)])
+    csa_slots = (base + sel).int().contiguous()
+    csa_pos = (sel * 4).int().contiguous()
+    swa_slots = (torch.arange(B, device=dev)[:, None] * W + torch.arange(W, device=dev)[None]).int()
+    q = (torch.randn(B, Hh, 512, device=dev, generator=g) / 2).bfloat16()
+    args_d = dict(swa_slots=swa_slots, swa_len=torch.full((B,), W, dtype=torch.int32, device=dev),
+                  csa_slots=csa_slots, csa_pos=csa_pos, csa_len=torch.full((B,), K, dtype=torch.int32, device=dev),
+                  freqs=freqs, sink=torch.zeros(Hh, device=dev), scale=512 ** -0.5,
+                  q_pos=torch.full((B,), args.context - 1, dtype=torch.int32, device=dev), csa_pool=pool,
+                  csa_planes=planes)
+    ws = attn_ops.DecodeWorkspace(B, Hh, attn_ops.choose_splits(B, Hh, W + K), dev)
+    out = torch.empty(B, Hh, 512, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, Hh, dtype=torch.float32, device=dev)
+    fn = lambda: attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, **args_d)  # noqa: E731
+    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev))
+    check_errors(dev)
+    nbytes = B * (K * rec_bytes + W * abi.NATIVE_RECORD_BYTES) + q.numel() * 2 + out.numel() * 2
+    flops = 4 * B * Hh * (K + W) * 512
+    peak, tag = measured_hbm_gbs()
+    gbs = nbytes / us / 1e3
+    return {"case": "sparse_mla_decode", "kv_format": args.kv_format, "batch": B, "heads": Hh, "topk": K,
+            "swa": W, "context": args.context, "splits": ws.splits, "us": round(us, 2), "bytes": nbytes,
+            "GBps": round(gbs, 1), "hbm_fraction": round(gbs / peak, 3), "TFLOPs": round(flops / us / 1e6, 1),
+            "peak_note": tag}
+
+
+def bench_store(args, dev):
+    from packmla.formats import abi, codec
+    from packmla.ops import kv as kv_ops
+
+    R = args.rows
+    g = torch.Generator(device=dev).manual_seed(0)
+    raw = torch.randn(R, 512, device=dev, generator=g)
+    w = torch.ones(512, device=dev)
+    slots = torch.randperm(R * 4, device=dev, generator=g)[:R]
+    freqs = kv_ops.freq_table_f32(codec.rope_table(1 << 16)).to(dev)
+    pos = torch.randint(0, 1 << 16, (R,), device=dev, generator=g)
+    pool = torch.zeros(((4 * R + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+    v = torch.zeros(4 * R, 256, dtype=torch.uint8, device=dev)
+    bm = torch.zeros(4 * R, 8, dtype=torch.int64, device=dev)
+    sc = torch.zeros(4 * R, 8, dtype=torch.uint8, device=dev)
+    native = time_op(lambda: kv_ops.native_store(raw, w, 1e-6, slots, pos, freqs, pool), args.rounds, args.warmup,
+                     dev, None)
+    packed = time_op(lambda: kv_ops.packed_store(raw, w, 1e-6, slots, v, bm, sc), args.rounds, args.warmup, dev, None)
+    return {"case": "kv_store", "rows": R, "native_us": round(native, 3), "packed_us": round(packed, 3)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["moe", "decode", "store"])
+    ap.add_argument("--tokens", type=int, default=40)
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--topk", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--heads", type=int, default=128)
+    ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
+    ap.add_argument("--rows", type=int, default=24)
+    ap.add_argument("--rounds", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=10)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    if args.case == "moe":
+        args.topk = args.topk or 8
+        out = bench_moe(args, dev)
+    elif args.case == "decode":
+        args.topk = args.topk or 2048
+        out = bench_decode(args, dev)
+    else:
+        out = bench_store(args, dev)
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

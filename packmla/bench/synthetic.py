@@ -12,6 +12,7 @@ import torch
 
 from ..engine.engine import Engine, Request, SamplingParams
 from ..formats import abi
+from ..ops import indexer as idx_ops
 from ..ops import kv as kv_ops
 
 
@@ -61,10 +62,10 @@ def fill_synthetic(engine: Engine, n_requests: int, context: int, max_new_tokens
             for a in range(0, phys4.numel(), chunk_rows):
                 b = min(phys4.numel(), a + chunk_rows)
                 model._store_c4(layer, rand_rows(b - a), phys4[a:b], pos4[a:b])
-            keys = pool.index_keys[layer]
-            rnd = torch.empty(phys4.numel(), cfg.index_dim, device=dev).normal_(generator=gen)
-            keys[phys4] = (rnd * 64).to(torch.float8_e4m3fn).view(torch.uint8)
-            pool.index_scales[layer][phys4] = 1.0 / 64
+            for a in range(0, phys4.numel(), chunk_rows):
+                b = min(phys4.numel(), a + chunk_rows)
+                krows = torch.empty(b - a, cfg.index_dim, device=dev).normal_(generator=gen)
+                idx_ops.index_key_store(krows, phys4[a:b], pool.index_keys[layer], pool.index_scales[layer])
         elif ratio == abi.C128_RATIO:
             for a in range(0, phys2.numel(), chunk_rows):
                 b = min(phys2.numel(), a + chunk_rows)

@@ -72,6 +72,8 @@ class ModelConfig:
             raise ValueError("num_heads must be a multiple of o_groups")
         if self.latent_dim != abi.LATENT_DIM or self.rope_dim != abi.ROPE_DIM:
             raise ValueError("the record ABI fixes latent 512 = 448 + 64")
+        if self.index_dim != 128 or self.index_heads > 64:
+            raise ValueError("the indexer stores 128-wide FP8 keys and scores at most 64 heads")
 
     @property
     def heads_per_group(self) -> int:
@@ -107,7 +109,7 @@ class ModelConfig:
             o_lora_rank=128,
             compress_ratios=ratios,
             index_heads=4,
-            index_dim=64,
+            index_dim=128,
             index_topk=16,
             n_routed_experts=8,
             moe_topk=2,

@@ -172,6 +172,11 @@ class Engine:
         engine_cfg.validate()
         dev = torch.device(device)
         W = weights if weights is not None else init_weights(model_cfg, rank, world, dev, seed)
+        if dev.type == "cuda" and model_cfg.expert_format == "mxfp4":
+            from ..ops.moe import prepare_experts
+
+            for lw in W["layers"]:  # one-time kernel layout of the experts (canonical copy dropped)
+                prepare_experts(lw, drop_canonical=weights is None)
         max_requests = max_requests or engine_cfg.max_running_requests
         max_requests += 1  # + dummy slot for padded graph rows
         if kv_bytes is None:

@@ -29,6 +29,7 @@ from ..formats import abi, codec
 from ..kv.pool import KVPool
 from ..ops import attention as attn_ops
 from ..ops import kv as kv_ops
+from ..ops import indexer as idx_ops
 from ..ops import moe as moe_ops
 
 
@@ -183,15 +184,8 @@ class V4FlashModel:
             kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rope_pos, self.freqs, p.c4_native[layer])
 
     def _store_index_keys(self, layer: int, kraw: torch.Tensor, slots: torch.Tensor) -> None:
-        """FP8 index key + fp32 scale per record; rows with slot -1 go to the pool's trash row."""
-        amax = kraw.abs().amax(-1, keepdim=True)
-        scale = torch.where(amax > 0, amax / abi.E4M3_MAX, torch.ones_like(amax))
-        q8 = (kraw / scale).to(torch.float8_e4m3fn).view(torch.uint8)
-        keys, sc = self.pool.index_keys[layer], self.pool.index_scales[layer]
-        trash = keys.shape[0] - 1
-        idx = torch.where(slots >= 0, slots, torch.full_like(slots, trash))
-        keys[idx] = q8
-        sc[idx] = scale[:, 0]
+        """FP8 index key + fp32 scale per completed record (rows with slot -1 are skipped)."""
+        idx_ops.index_key_store(kraw, slots, self.pool.index_keys[layer], self.pool.index_scales[layer])
 
     # ------------------------------------------------------------------ indexer
     def _index_topk(self, layer: int, q_lora: torch.Tensor, h: torch.Tensor, phys: torch.Tensor,
@@ -200,22 +194,10 @@ class V4FlashModel:
         lw = self.W["layers"][layer]
         cfg = self.cfg
         B = q_lora.shape[0]
-        qi = (q_lora @ lw["wi_q"].T).view(B, cfg.index_heads, cfg.index_dim).float()
+        qi = (q_lora @ lw["wi_q"].T).view(B, cfg.index_heads, cfg.index_dim)
         wi = (h @ lw["wi_w"].T).float() * (cfg.index_heads ** -0.5) * (cfg.index_dim ** -0.5)
-        ph = phys[:, :r_limit].long()
-        safe = ph.clamp(min=0)
-        keys = self.pool.index_keys[layer][safe].view(torch.float8_e4m3fn).float()  # [B, R, d]
-        keys = keys * self.pool.index_scales[layer][safe][..., None]
-        s = torch.relu(torch.bmm(qi, keys.transpose(1, 2)))  # [B, Hi, R]
-        score = (s * wi[:, :, None]).sum(1)  # [B, R]
-        r = torch.arange(r_limit, device=self.device)
-        visible = (r[None] < count[:, None]) & (ph >= 0)
-        score = torch.where(visible, score, torch.full_like(score, float("-inf")))
-        k = min(self.topk, r_limit)
-        vals, idx = torch.topk(score, k, dim=1)
-        sel = ph.gather(1, idx)
-        slots = torch.where(vals > float("-inf"), sel, torch.full_like(sel, -1)).int()
-        return slots, (idx * abi.C4_RATIO).int()
+        return idx_ops.index_select(qi.to(torch.bfloat16).contiguous(), wi, self.pool.index_keys[layer],
+                                    self.pool.index_scales[layer], phys, count, r_limit, min(self.topk, r_limit))
 
     # ------------------------------------------------------------------ layer
     def _attention_block(self, layer: int, x: torch.Tensor, meta: StepMeta) -> torch.Tensor:
@@ -367,7 +349,7 @@ class V4FlashModel:
         outs_s, outs_p = [], []
         for t0 in range(0, T, block):
             t1 = min(T, t0 + block)
-            ph = phys_row[:lim][None].expand(t1 - t0, -1).int()
+            ph = phys_row[:lim][None].expand(t1 - t0, -1).int().contiguous()
             s, p = self._index_topk(layer, q_lora[t0:t1], h[t0:t1], ph, count[t0:t1], lim)
             outs_s.append(s)
             outs_p.append(p)

@@ -28,9 +28,10 @@ class PackedPlanes:
 
 
 def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
+    """KV splits per (query, head group): as many as fit in one wave of one CTA per SM."""
     groups = (heads + HEAD_GROUP - 1) // HEAD_GROUP
     tiles = max(1, math.ceil(max_rows / KV_TILE))
-    want = max(1, math.ceil(num_sms / max(1, batch * groups)))
+    want = max(1, num_sms // max(1, batch * groups))
     return max(1, min(tiles, want))
 
 

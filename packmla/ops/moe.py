@@ -7,8 +7,9 @@ Experts on this rank are [expert_base, expert_base + local_experts).  Tokens are
 every TP/EP rank, so each rank computes its local experts' contribution and the caller's
 all-reduce combines ranks (the MoE down-projection partial sums).
 
-* MXFP4 experts on CUDA: csrc/moe_fp4.cu (routing lists, gate/up with SiLU, down + weighted
-  scatter-add), reading E2M1 weights with UE8M0 block scales directly.
+* MXFP4 experts on CUDA: routing lists (csrc/moe_fp4.cu), then csrc/moe_fp4_tc.cu: tcgen05 with
+  the dequantized weight tile in tensor memory, gate/up with SiLU, down with the routed-weight
+  scatter-add; weights use the tiled layout made once by `prepare_experts`.
 * BF16 experts (tiny CPU configs, tests): PyTorch reference.
 """
 from __future__ import annotations
@@ -57,16 +58,54 @@ def fp4_dequant(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     return vals * scale
 
 
+def tile_fp4(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Canonical MXFP4 [E, R, K/2] + scales [E, R, K/32] -> kernel tiles of 128 rows x 256 k.
+
+    Returns w_t [E, R/128, K/256, 128, 128] with each row's 16-byte units XOR-swizzled by
+    (row % 8), and s_t [E, R/128, K/256, 128, 8].  For gate/up (R = 2I), row tile j holds gate
+    rows [64 j, 64 j + 64) followed by up rows [I + 64 j, I + 64 j + 64).
+    """
+    E, R, Kh = w.shape
+    K = Kh * 2
+    if gate_up:
+        I = R // 2
+        w = torch.cat((w[:, :I].reshape(E, I // 64, 64, Kh), w[:, I:].reshape(E, I // 64, 64, Kh)), 2)
+        s = torch.cat((s[:, :I].reshape(E, I // 64, 64, K // 32), s[:, I:].reshape(E, I // 64, 64, K // 32)), 2)
+    else:
+        w = w.reshape(E, R // 128, 128, Kh)
+        s = s.reshape(E, R // 128, 128, K // 32)
+    nrt = w.shape[1]
+    w = w.reshape(E, nrt, 128, K // 256, 8, 16).permute(0, 1, 3, 2, 4, 5)  # [E, nrt, kt, row, unit, 16]
+    rows = torch.arange(128, device=w.device)
+    units = torch.arange(8, device=w.device)
+    src = (units[None, :] ^ (rows[:, None] % 8))[None, None, None, :, :, None].expand(E, nrt, K // 256, 128, 8, 16)
+    w_t = torch.gather(w, 4, src).reshape(E, nrt, K // 256, 128, 128).contiguous()
+    s_t = s.reshape(E, nrt, 128, K // 256, 8).permute(0, 1, 3, 2, 4).contiguous()
+    return w_t, s_t
+
+
+def prepare_experts(lw: dict, drop_canonical: bool = True) -> None:
+    """Add the kernel layout (w13_t, s13_t, w2_t, s2_t) to a layer's MXFP4 expert weights."""
+    if "w13_t" in lw:
+        return
+    lw["w13_t"], lw["s13_t"] = tile_fp4(lw["w13"], lw["s13"], True)
+    lw["w2_t"], lw["s2_t"] = tile_fp4(lw["w2"], lw["s2"], False)
+    if drop_canonical:
+        for k in ("w13", "s13", "w2", "s2"):
+            lw.pop(k)
+
+
 class MoEWorkspace:
     """Routing lists and activations with stable pointers (graph-capturable)."""
 
-    def __init__(self, max_tokens: int, topk: int, local_experts: int, inter: int, device):
+    def __init__(self, max_tokens: int, topk: int, local_experts: int, inter: int, device, hidden: int = 0):
         n = max_tokens * topk
         self.offsets = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
         self.slot_token = torch.zeros(n, dtype=torch.int32, device=device)
         self.slot_weight = torch.zeros(n, dtype=torch.float32, device=device)
         self.active = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
-        self.act = torch.zeros(n, inter, dtype=torch.bfloat16, device=device)
+        self.act = torch.zeros(n, inter, dtype=torch.float16, device=device)  # slot layout (swizzled)
+        self.xs = torch.zeros(n, hidden, dtype=torch.float16, device=device)  # routed token rows per slot
         self.max_tokens = max_tokens
 
 
@@ -93,15 +132,17 @@ def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, 
         return out
     T, H = h.shape
     k = topk_ids.shape[1]
-    I = lw["w13"].shape[1] // 2
+    I = lw["w13_t"].shape[1] * 64 if "w13_t" in lw else lw["w13"].shape[1] // 2
     ws = workspace
     if ws is None:
         key = (h.device.index, T, k, local_experts, I)
         ws = _WS.get(key)
         if ws is None:
-            ws = MoEWorkspace(T, k, local_experts, I, h.device)
+            ws = MoEWorkspace(T, k, local_experts, I, h.device, hidden=H)
             _WS[key] = ws
     out = torch.zeros(T, H, dtype=torch.float32, device=h.device)
-    ext().moe_fp4(h, topk_ids, topk_w, expert_base, lw["w13"], lw["s13"], lw["w2"], lw["s2"], ws.offsets,
-                  ws.slot_token, ws.slot_weight, ws.active, ws.act, out, error_word(h.device))
+    if "w13_t" not in lw:
+        prepare_experts(lw, drop_canonical=False)
+    ext().moe_fp4_tc(h, topk_ids, topk_w, expert_base, lw["w13_t"], lw["s13_t"], lw["w2_t"], lw["s2_t"], ws.offsets,
+                     ws.slot_token, ws.slot_weight, ws.active, ws.xs, ws.act, out, error_word(h.device))
     return out

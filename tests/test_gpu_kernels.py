@@ -56,7 +56,7 @@ def test_packed_store_byte_exact_and_ties(cuda, rows):
 
 
 @pytest.mark.parametrize("mode,K,N", [(0, 128, 64), (0, 64, 16), (1, 128, 64), (1, 32, 16), (1, 64, 32),
-                                      (2, 128, 16), (2, 64, 64), (2, 32, 32)])
+                                      (2, 128, 16), (2, 64, 64), (2, 32, 32), (3, 128, 64), (3, 64, 16)])
 def test_umma_operand_layouts(cuda, mode, K, N):
     g = torch.Generator().manual_seed(K + N + mode)
     err = torch.zeros(4, dtype=torch.int32, device=cuda)
@@ -68,6 +68,11 @@ def test_umma_operand_layouts(cuda, mode, K, N):
         a = torch.randn(K, 128, generator=g).bfloat16()
         b = torch.randn(K, N, generator=g).bfloat16()
         ref = a.float().T @ b.float()
+    if mode == 3:  # E4M3 codes
+        a8 = (torch.randn(128, K, generator=g) * 4).to(torch.float8_e4m3fn)
+        b8 = (torch.randn(N, K, generator=g) * 4).to(torch.float8_e4m3fn)
+        a, b = a8.view(torch.uint8), b8.view(torch.uint8)
+        ref = a8.float() @ b8.float().T
     d = ext().umma_probe(a.cuda(), b.cuda(), mode, err)
     assert err.cpu()[0] == 0
     torch.testing.assert_close(d.cpu(), ref, atol=1e-2, rtol=1e-2)
