@@ -54,11 +54,12 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
                     __nv_bfloat16* act, float* out, int num_sms, cudaStream_t stream);
 
 void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
-                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, cudaStream_t stream);
+                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
+                      cudaStream_t stream);
 void launch_moe_fp4_tc(const __nv_bfloat16* x, int T, int H, int I, int E, int max_slots, const int32_t* offsets,
-                       const int32_t* slot_token, const float* slot_weight, const int32_t* active, const uint8_t* w13t,
-                       const uint8_t* s13t, const uint8_t* w2t, const uint8_t* s2t, __half* xs, __half* act_s,
-                       float* out, int num_sms, int* err, int debug, cudaStream_t stream);
+                       const int32_t* pad, const int32_t* slot_token, const float* slot_weight, const int32_t* active,
+                       const uint8_t* w13t, const uint8_t* s13t, const uint8_t* w2t, const uint8_t* s2t, __half* xs,
+                       __half* act_s, float* out, int num_sms, int* err, int debug, cudaStream_t stream);
 
 void launch_index_key_store(const float* kraw, int64_t stride, const int64_t* slots, uint8_t* keys, float* kscales,
                             int64_t nrows, int R, int* err, cudaStream_t stream);
@@ -69,4 +70,22 @@ void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, c
 void launch_index_topk(const float* scores, int64_t stride, int B, int R, int k, const int32_t* phys,
                        int64_t phys_stride, int ratio, int32_t* out_slots, int32_t* out_pos, cudaStream_t stream);
 
-void launch_tc_latency_probe(int iters, int n_mma, int n, long long* out, int* err, cudaStream_t stream);
+void launch_tc_latency_probe(int iters, int n_mma, int n, int n_acc, long long* out, int* err, cudaStream_t stream);
+
+void launch_moe_gather_slots(const __nv_bfloat16* x, int K, const int32_t* offsets, const int32_t* pad,
+                             const int32_t* slot_token, int E, __half* xs, int num_sms, cudaStream_t stream);
+void launch_moe_fp4_mma(const __nv_bfloat16* x, int T, int H, int I, int E, const int32_t* offsets, const int32_t* pad,
+                        const int32_t* slot_token, const float* slot_weight, const int32_t* active, const uint8_t* w13f,
+                        const uint8_t* s13f, const uint8_t* w2f, const uint8_t* s2f, __half* xs, __half* act_s,
+                        float* out, int num_sms, int* err, cudaStream_t stream);
+
+void launch_add_rmsnorm(const __nv_bfloat16* x, int64_t xs, const __nv_bfloat16* d, int64_t ds, const float* dfp32,
+                        int64_t dfs, __nv_bfloat16* x_out, int64_t xos, const float* w, float eps, __nv_bfloat16* h,
+                        int64_t hs, int rows, int n, cudaStream_t stream);
+void launch_rope_q(__nv_bfloat16* q, int64_t qs, int B, int H, const int64_t* pos, const float* freqs,
+                   cudaStream_t stream);
+void launch_comp_pool(const __nv_bfloat16* proj, int64_t ps, int off, int D, const float* ape, int ratio, float* state,
+                      const int64_t* req, const int64_t* pos, float* raw, int64_t rs, int B, cudaStream_t stream);
+void launch_route_topk(const __nv_bfloat16* logits, int64_t ls, int T, int E, const float* bias, int k, float scaling,
+                       int32_t* ids, float* wts, cudaStream_t stream);
+void launch_silu_mul(const __nv_bfloat16* gu, int64_t gs, int T, int I, __nv_bfloat16* out, cudaStream_t stream);

@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
                                                          const float* __restrict__ w, int n, int k, int base,
                                                          int E, int32_t* __restrict__ offsets,
                                                          int32_t* __restrict__ slot_token,
-                                                         float* __restrict__ slot_weight, int32_t* __restrict__ active) {
+                                                         float* __restrict__ slot_weight, int32_t* __restrict__ active,
+                                                         int32_t* __restrict__ pad) {
   extern __shared__ int sh[];
   int* cnt = sh;         // [E]
   int* cur = sh + E;     // [E]
@@ -40,14 +41,17 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
   }
   __syncthreads();
   if (tid == 0) {
-    int acc = 0, na = 0;
+    int acc = 0, na = 0, pacc = 0;
     for (int e = 0; e < E; ++e) {
       offsets[e] = acc;
       cur[e] = acc;
+      if (pad) pad[e] = pacc;  // padded rows: each expert's list starts on a multiple of 16
       if (cnt[e] > 0) active[1 + na++] = e;
       acc += cnt[e];
+      pacc += (cnt[e] + 15) & ~15;
     }
     offsets[E] = acc;
+    if (pad) pad[E] = pacc;
     active[0] = na;
   }
   __syncthreads();
@@ -267,10 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(const MoeParams p
 }  // namespace
 
 void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
-                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, cudaStream_t stream) {
+                      int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
+                      cudaStream_t stream) {
   if (T == 0) return;
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
-                                                           slot_token, slot_weight, active);
+                                                           slot_token, slot_weight, active, pad);
 }
 
 void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const int32_t* topk_ids, const float* topk_w,
@@ -279,7 +284,7 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
                     __nv_bfloat16* act, float* out, int num_sms, cudaStream_t stream) {
   if (T == 0) return;
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
-                                                           slot_token, slot_weight, active);
+                                                           slot_token, slot_weight, active, nullptr);
   MoeParams p{x, T, H, I, E, w13, s13, w2, s2, offsets, slot_token, slot_weight, active, act, out};
   const int smem_gu = kMT * H * 2, smem_dn = kMT * I * 2;
   auto gate_up = [&](auto kern) {

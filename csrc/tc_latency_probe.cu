@@ -1,12 +1,13 @@
 // Latency probe of tcgen05 handshakes (used by the kernel design notes, not by the engine):
-// per iteration, thread 0 issues `n_mma` dependent tcgen05.mma (M=128, N=n, K=16, A and B from
-// shared memory) into one accumulator, then tcgen05.commit to an mbarrier that all 128 threads
+// per iteration, thread 0 issues `n_mma` tcgen05.mma (M=128, N=n, K=16, A and B from shared memory)
+// round-robin over `n_acc` accumulators, then tcgen05.commit to an mbarrier that all 128 threads
 // wait on.  Returns the average clock64 cycles per iteration.
 #include "launchers.h"
 #include "common/sm100.cuh"
 
 namespace {
-__global__ void __launch_bounds__(128, 1) tc_latency_kernel(int iters, int n_mma, int n, long long* out, int* err) {
+__global__ void __launch_bounds__(128, 1) tc_latency_kernel(int iters, int n_mma, int n, int n_acc, long long* out,
+                                                            int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (pm::smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 65536);
@@ -26,8 +27,8 @@ __global__ void __launch_bounds__(128, 1) tc_latency_kernel(int iters, int n_mma
   for (int it = 0; it < iters; ++it) {
     if (tid == 0) {
       for (int k = 0; k < n_mma; ++k)
-        pm::umma_f16(tmem, pm::make_sdesc(a0 + (k & 3) * 32, 16, 1024), pm::make_sdesc(b0 + (k & 3) * 32, 16, 1024),
-                     idesc, k > 0);
+        pm::umma_f16(tmem + (k % n_acc) * n, pm::make_sdesc(a0 + (k & 3) * 32, 16, 1024), pm::make_sdesc(b0 + (k & 3) * 32, 16, 1024),
+                     idesc, k >= n_acc);
       pm::umma_commit(bar);
     }
     if (!pm::mbar_wait(bar, it & 1, err, 50)) break;
@@ -41,8 +42,8 @@ __global__ void __launch_bounds__(128, 1) tc_latency_kernel(int iters, int n_mma
 }
 }  // namespace
 
-void launch_tc_latency_probe(int iters, int n_mma, int n, long long* out, int* err, cudaStream_t stream) {
+void launch_tc_latency_probe(int iters, int n_mma, int n, int n_acc, long long* out, int* err, cudaStream_t stream) {
   const int smem = 65536 + 64 + 1024;
   cudaFuncSetAttribute(tc_latency_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  tc_latency_kernel<<<1, 128, smem, stream>>>(iters, n_mma, n, out, err);
+  tc_latency_kernel<<<1, 128, smem, stream>>>(iters, n_mma, n, n_acc, out, err);
 }

@@ -212,8 +212,8 @@ int num_sms_of(const torch::Device& d) {
 // s13t [E, I/64, H/256, 128, 8], w2t [E, H/128, I/256, 128, 128], s2t [E, H/128, I/256, 128, 8].
 void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base,
                 torch::Tensor w13t, torch::Tensor s13t, torch::Tensor w2t, torch::Tensor s2t, torch::Tensor offsets,
-                torch::Tensor slot_token, torch::Tensor slot_weight, torch::Tensor active, torch::Tensor xs,
-                torch::Tensor act_s, torch::Tensor out, torch::Tensor err) {
+                torch::Tensor slot_token, torch::Tensor slot_weight, torch::Tensor active, torch::Tensor pad,
+                torch::Tensor xs, torch::Tensor act_s, torch::Tensor out, torch::Tensor err) {
   TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
   check_err(err);
   const int T = h.size(0), H = h.size(1);
@@ -236,15 +236,18 @@ void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, i
   TORCH_CHECK(active.scalar_type() == torch::kInt32 && active.numel() >= E + 1);
   TORCH_CHECK(slot_token.scalar_type() == torch::kInt32 && slot_token.numel() >= (int64_t)T * k);
   TORCH_CHECK(slot_weight.scalar_type() == torch::kFloat32 && slot_weight.numel() >= (int64_t)T * k);
-  TORCH_CHECK(xs.scalar_type() == torch::kFloat16 && xs.is_contiguous() && xs.numel() >= (int64_t)T * k * H);
-  TORCH_CHECK(act_s.scalar_type() == torch::kFloat16 && act_s.is_contiguous() && act_s.numel() >= (int64_t)T * k * I);
+  TORCH_CHECK(pad.scalar_type() == torch::kInt32 && pad.numel() >= E + 1);
+  const int64_t prow = (int64_t)T * k + 16 * (int64_t)E;  // padded rows upper bound
+  TORCH_CHECK(xs.scalar_type() == torch::kFloat16 && xs.is_contiguous() && xs.numel() >= prow * H);
+  TORCH_CHECK(act_s.scalar_type() == torch::kFloat16 && act_s.is_contiguous() && act_s.numel() >= prow * I);
   TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == (int64_t)T * H);
   const c10::cuda::CUDAGuard g(h.device());
   launch_moe_route(topk_ids.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, k, (int)expert_base, E,
                    offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
-                   active.data_ptr<int32_t>(), stream());
+                   active.data_ptr<int32_t>(), pad.data_ptr<int32_t>(), stream());
   launch_moe_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), T, H, I, E, T * k,
-                    offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
+                    offsets.data_ptr<int32_t>(), pad.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(),
+                    slot_weight.data_ptr<float>(),
                     active.data_ptr<int32_t>(), w13t.data_ptr<uint8_t>(), s13t.data_ptr<uint8_t>(),
                     w2t.data_ptr<uint8_t>(), s2t.data_ptr<uint8_t>(), reinterpret_cast<__half*>(xs.data_ptr()),
                     reinterpret_cast<__half*>(act_s.data_ptr()), out.data_ptr<float>(), num_sms_of(h.device()),
@@ -252,12 +255,13 @@ void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, i
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-int64_t tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, torch::Tensor err) {
+int64_t tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, int64_t n_acc, torch::Tensor err) {
   check_err(err);
   TORCH_CHECK(n == 16 || n == 32 || n == 64 || n == 128 || n == 256, "n in {16,32,64,128,256}");
+  TORCH_CHECK(n_acc >= 1 && n_acc * n <= 256, "n_acc accumulators of n columns must fit 256 columns");
   const c10::cuda::CUDAGuard g(err.device());
   auto out = torch::zeros({1}, err.options().dtype(torch::kInt64));
-  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, (int)n_acc, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
                           err.data_ptr<int>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out.item<int64_t>();
@@ -307,6 +311,135 @@ void index_select(torch::Tensor q, torch::Tensor w, torch::Tensor keys, torch::T
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Fragment-ordered MXFP4 experts (packmla/ops/moe.py tile_fp4_frag): w13f [E, I/64, H/256, 16384],
+// s13f [E, I/64, H/256, 1024], w2f [E, H/128, I/256, 16384], s2f [E, H/128, I/256, 1024].
+void moe_fp4_mma(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base,
+                 torch::Tensor w13f, torch::Tensor s13f, torch::Tensor w2f, torch::Tensor s2f, torch::Tensor offsets,
+                 torch::Tensor slot_token, torch::Tensor slot_weight, torch::Tensor active, torch::Tensor pad,
+                 torch::Tensor xs, torch::Tensor act_s, torch::Tensor out, torch::Tensor err) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
+  check_err(err);
+  const int T = h.size(0), H = h.size(1);
+  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.dim() == 2 && topk_ids.size(0) == T && topk_ids.is_contiguous());
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.sizes() == topk_ids.sizes() && topk_w.is_contiguous());
+  const int k = topk_ids.size(1);
+  TORCH_CHECK(w13f.scalar_type() == torch::kUInt8 && w13f.dim() == 4 && w13f.size(3) == 16384 && w13f.is_contiguous());
+  const int E = w13f.size(0), I = w13f.size(1) * 64;
+  TORCH_CHECK(w13f.size(2) * 256 == H, "w13f k-tiles do not match hidden size");
+  TORCH_CHECK(s13f.scalar_type() == torch::kUInt8 && s13f.dim() == 4 && s13f.size(0) == E && s13f.size(1) == I / 64 &&
+              s13f.size(2) == H / 256 && s13f.size(3) == 1024 && s13f.is_contiguous());
+  TORCH_CHECK(w2f.scalar_type() == torch::kUInt8 && w2f.dim() == 4 && w2f.size(0) == E && w2f.size(1) * 128 == H &&
+              w2f.size(2) * 256 == I && w2f.size(3) == 16384 && w2f.is_contiguous());
+  TORCH_CHECK(s2f.scalar_type() == torch::kUInt8 && s2f.dim() == 4 && s2f.size(0) == E && s2f.size(1) * 128 == H &&
+              s2f.size(2) * 256 == I && s2f.size(3) == 1024 && s2f.is_contiguous());
+  TORCH_CHECK(H % 256 == 0 && I % 256 == 0, "hidden and intermediate must be multiples of 256");
+  TORCH_CHECK(E <= 4096, "too many local experts");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() >= E + 1);
+  TORCH_CHECK(active.scalar_type() == torch::kInt32 && active.numel() >= E + 1);
+  TORCH_CHECK(pad.scalar_type() == torch::kInt32 && pad.numel() >= E + 1);
+  TORCH_CHECK(slot_token.scalar_type() == torch::kInt32 && slot_token.numel() >= (int64_t)T * k);
+  TORCH_CHECK(slot_weight.scalar_type() == torch::kFloat32 && slot_weight.numel() >= (int64_t)T * k);
+  const int64_t prow = (int64_t)T * k + 16 * (int64_t)E;
+  TORCH_CHECK(xs.scalar_type() == torch::kFloat16 && xs.is_contiguous() && xs.numel() >= prow * H);
+  TORCH_CHECK(act_s.scalar_type() == torch::kFloat16 && act_s.is_contiguous() && act_s.numel() >= prow * I);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == (int64_t)T * H);
+  const c10::cuda::CUDAGuard g(h.device());
+  launch_moe_route(topk_ids.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, k, (int)expert_base, E,
+                   offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
+                   active.data_ptr<int32_t>(), pad.data_ptr<int32_t>(), stream());
+  launch_moe_fp4_mma(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), T, H, I, E, offsets.data_ptr<int32_t>(),
+                     pad.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
+                     active.data_ptr<int32_t>(), w13f.data_ptr<uint8_t>(), s13f.data_ptr<uint8_t>(),
+                     w2f.data_ptr<uint8_t>(), s2f.data_ptr<uint8_t>(), reinterpret_cast<__half*>(xs.data_ptr()),
+                     reinterpret_cast<__half*>(act_s.data_ptr()), out.data_ptr<float>(), num_sms_of(h.device()),
+                     err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+namespace {
+const __nv_bfloat16* bf16_ptr(const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+__nv_bfloat16* bf16_mut(const torch::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+void check_rows_bf16(const torch::Tensor& t, int64_t rows, int64_t n, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.size(0) == rows &&
+              t.size(1) == n && t.stride(1) == 1 && t.stride(0) % 2 == 0, name, " must be bf16 [rows, n]");
+}
+}  // namespace
+
+// h = bf16(rmsnorm(x (+ d) (+ dfp32)) * w); x_out (optional) receives the bf16 residual x + d.
+void add_rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> d, c10::optional<torch::Tensor> dfp32,
+                 c10::optional<torch::Tensor> x_out, torch::Tensor w, double eps, torch::Tensor h) {
+  const int64_t rows = x.size(0), n = x.size(1);
+  check_rows_bf16(x, rows, n, "x");
+  check_rows_bf16(h, rows, n, "h");
+  TORCH_CHECK(n % 2 == 0 && n <= 8192, "add_rmsnorm: width must be even and at most 8192");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.numel() == n && w.is_contiguous());
+  if (d) check_rows_bf16(*d, rows, n, "d");
+  if (dfp32) TORCH_CHECK(dfp32->scalar_type() == torch::kFloat32 && dfp32->dim() == 2 && dfp32->size(0) == rows &&
+                         dfp32->size(1) == n && dfp32->stride(1) == 1 && dfp32->stride(0) % 2 == 0);
+  if (x_out) check_rows_bf16(*x_out, rows, n, "x_out");
+  const c10::cuda::CUDAGuard g(x.device());
+  launch_add_rmsnorm(bf16_ptr(x), x.stride(0), d ? bf16_ptr(*d) : nullptr, d ? d->stride(0) : 0,
+                     dfp32 ? dfp32->data_ptr<float>() : nullptr, dfp32 ? dfp32->stride(0) : 0,
+                     x_out ? bf16_mut(*x_out) : nullptr, x_out ? x_out->stride(0) : 0, w.data_ptr<float>(), (float)eps,
+                     bf16_mut(h), h.stride(0), (int)rows, (int)n, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_q(torch::Tensor q, torch::Tensor pos, torch::Tensor freqs) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == 512 &&
+              q.stride(2) == 1 && q.stride(1) == 512);
+  TORCH_CHECK(pos.scalar_type() == torch::kInt64 && pos.numel() == q.size(0) && pos.is_contiguous());
+  TORCH_CHECK(freqs.scalar_type() == torch::kFloat32 && freqs.dim() == 3 && freqs.is_contiguous());
+  const c10::cuda::CUDAGuard g(q.device());
+  launch_rope_q(bf16_mut(q), q.stride(0), q.size(0), q.size(1), pos.data_ptr<int64_t>(), freqs.data_ptr<float>(),
+                stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void comp_pool(torch::Tensor proj, int64_t off, int64_t D, torch::Tensor ape, torch::Tensor state, torch::Tensor req,
+               torch::Tensor pos, torch::Tensor raw) {
+  TORCH_CHECK(proj.is_cuda() && proj.scalar_type() == torch::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1);
+  const int B = proj.size(0);
+  TORCH_CHECK(off >= 0 && off + 2 * D <= proj.size(1));
+  TORCH_CHECK(ape.scalar_type() == torch::kFloat32 && ape.dim() == 2 && ape.size(1) == D && ape.is_contiguous());
+  TORCH_CHECK(state.scalar_type() == torch::kFloat32 && state.dim() == 3 && state.size(1) == 3 && state.size(2) == D &&
+              state.is_contiguous());
+  TORCH_CHECK(req.scalar_type() == torch::kInt64 && req.numel() == B && pos.scalar_type() == torch::kInt64 &&
+              pos.numel() == B);
+  TORCH_CHECK(raw.scalar_type() == torch::kFloat32 && raw.dim() == 2 && raw.size(0) == B && raw.size(1) == D &&
+              raw.stride(1) == 1);
+  const c10::cuda::CUDAGuard g(proj.device());
+  launch_comp_pool(bf16_ptr(proj), proj.stride(0), (int)off, (int)D, ape.data_ptr<float>(), (int)ape.size(0),
+                   state.data_ptr<float>(), req.data_ptr<int64_t>(), pos.data_ptr<int64_t>(), raw.data_ptr<float>(),
+                   raw.stride(0), B, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void route_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, double scaling, torch::Tensor ids,
+                torch::Tensor wts) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kBFloat16 && logits.dim() == 2 &&
+              logits.stride(1) == 1);
+  const int T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(E <= 512 && k >= 1 && k <= 32 && k <= E);
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32 && ids.is_contiguous() && ids.numel() == (int64_t)T * k);
+  TORCH_CHECK(wts.scalar_type() == torch::kFloat32 && wts.is_contiguous() && wts.numel() == (int64_t)T * k);
+  if (bias) TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() == E && bias->is_contiguous());
+  const c10::cuda::CUDAGuard g(logits.device());
+  launch_route_topk(bf16_ptr(logits), logits.stride(0), T, E, bias ? bias->data_ptr<float>() : nullptr, (int)k, (float)scaling,
+                    ids.data_ptr<int32_t>(), wts.data_ptr<float>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void silu_mul(torch::Tensor gu, torch::Tensor out) {
+  TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == torch::kBFloat16 && gu.dim() == 2 && gu.stride(1) == 1);
+  const int T = gu.size(0), I = gu.size(1) / 2;
+  check_rows_bf16(out, T, I, "out");
+  TORCH_CHECK(out.is_contiguous());
+  const c10::cuda::CUDAGuard g(gu.device());
+  launch_silu_mul(bf16_ptr(gu), gu.stride(0), T, I, bf16_mut(out), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -315,6 +448,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)");
   m.def("index_key_store", &index_key_store, "FP8 index keys (swizzled rows) + fp32 scales");
   m.def("index_select", &index_select, "FP8 tcgen05 indexer logits + radix top-k");
+  m.def("add_rmsnorm", &add_rmsnorm, "residual add + RMSNorm (bf16)");
+  m.def("rope_q", &rope_q, "in-place RoPE of query tails");
+  m.def("comp_pool", &comp_pool, "compressor online-softmax pooling of one token per row");
+  m.def("route_topk", &route_topk, "sigmoid top-k MoE routing");
+  m.def("silu_mul", &silu_mul, "silu(gate) * up");
+  m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
   m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine");

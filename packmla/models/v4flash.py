@@ -31,21 +31,11 @@ from ..ops import attention as attn_ops
 from ..ops import kv as kv_ops
 from ..ops import indexer as idx_ops
 from ..ops import moe as moe_ops
+from ..ops import fused as fused_ops
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * w).to(torch.bfloat16)
-
-
-def rotate_q_tail(q: torch.Tensor, freqs_f32: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
-    """q [B, H, 512] bf16; rotate coords 448..511 by freqs[pos] (fp32 math), round to bf16."""
-    fr = freqs_f32[pos]  # [B, 32, 2]
-    c, s = fr[:, None, :, 0], fr[:, None, :, 1]
-    tail = q[..., abi.NOPE_DIM:].float().unflatten(-1, (abi.ROPE_PAIRS, 2))
-    re, im = tail[..., 0], tail[..., 1]
-    rot = torch.stack((re * c - im * s, re * s + im * c), -1).flatten(-2)
-    return torch.cat((q[..., :abi.NOPE_DIM], rot.to(torch.bfloat16)), -1)
+    return fused_ops.add_rmsnorm(x, w, eps)[1]
 
 
 @dataclass
@@ -64,6 +54,10 @@ class StepMeta:
     c128_pos: torch.Tensor  # [B, R128] int32
     c128_len: torch.Tensor  # [B] int32
     c128_write: torch.Tensor  # [B] int64
+    no_rows: torch.Tensor  # [B, 1] int32 filled with -1 (layers without compressed records)
+    zero_len: torch.Tensor  # [B] int32 zeros
+    topk_len: torch.Tensor  # [B] int32 = index top-k
+    positions_i32: torch.Tensor  # [B] int32
 
 
 class V4FlashModel:
@@ -86,6 +80,34 @@ class V4FlashModel:
         self.r128max = max(1, pool.max_context // abi.C128_RATIO)
         self.topk = min(cfg.index_topk, self.r4max)
         self.ar_hook = None  # optional fused projection + all-reduce (parallel.fused)
+        self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
+
+    def _fuse_layer(self, layer: int) -> dict:
+        """Concatenate every projection of the normed residual into one weight per block.
+
+        Attention block: [wqkv_a | wc_kv | wc_gate | wi_k | wi_kgate | wi_w] (the compressor and
+        indexer parts only where the layer compresses); FFN block: [shared_w13 | gate].  The layer's
+        named weights become row views of the concatenation, so no weight is stored twice.
+        """
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
+        ratio = cfg.compress_ratios[layer]
+        names = ["wqkv_a"]
+        if ratio:
+            names += ["wc_kv", "wc_gate"]
+        if ratio == abi.C4_RATIO:
+            names += ["wi_k", "wi_kgate", "wi_w"]
+        out = {}
+        for key, group in (("w_h", names), ("w_ffn", ["shared_w13", "gate"])):
+            w = torch.cat([lw[n] for n in group]).contiguous()
+            off = 0
+            for n in group:
+                rows = lw[n].shape[0]
+                lw[n] = w[off:off + rows]
+                out[n] = off
+                off += rows
+            out[key] = w
+        return out
 
     # ------------------------------------------------------------------ helpers
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
@@ -134,41 +156,28 @@ class V4FlashModel:
         c128_write = torch.where(done2 & (rec2 < self.r128max), w2, torch.full_like(w2, -1))
         c128_len = torch.full((B,), self.r128max, dtype=torch.int32, device=dev)
         return StepMeta(pos, req, swa_slots, swa_len, swa_write, c4_phys.int(), c4_count, c4_write,
-                        c128_slots, c128_pos, c128_len, c128_write)
+                        c128_slots, c128_pos, c128_len, c128_write,
+                        torch.full((B, 1), -1, dtype=torch.int32, device=dev),
+                        torch.zeros(B, dtype=torch.int32, device=dev),
+                        torch.full((B,), self.topk, dtype=torch.int32, device=dev), pos.int())
 
     # ------------------------------------------------------------------ compressor
-    def _pool_update(self, state: torch.Tensor, req: torch.Tensor, gate: torch.Tensor, val: torch.Tensor,
-                     done: torch.Tensor) -> torch.Tensor:
-        """One token of online-softmax pooling per row; returns the pooled raw row (valid if done)."""
-        st = state[req]  # [B, 3, D]
-        m, l, acc = st[:, 0], st[:, 1], st[:, 2]
-        m_new = torch.maximum(m, gate)
-        a = torch.exp(m - m_new)
-        e = torch.exp(gate - m_new)
-        l = l * a + e
-        acc = acc * a + e * val
-        raw = acc / l
-        keep = (~done)[:, None]
-        new = torch.stack((torch.where(keep, m_new, torch.full_like(m_new, float("-inf"))),
-                           torch.where(keep, l, torch.zeros_like(l)),
-                           torch.where(keep, acc, torch.zeros_like(acc))), 1)
-        state[req] = new
-        return raw
+    def _compress_decode(self, layer: int, y: torch.Tensor, meta: StepMeta) -> None:
+        """Pool this token into the layer's compressor (and indexer-key) state; store completed records.
 
-    def _compress_decode(self, layer: int, h: torch.Tensor, meta: StepMeta) -> None:
+        `y` is the attention block's fused projection; the compressor's (value | gate) columns and the
+        indexer's (key | gate) columns are adjacent in it.
+        """
         lw = self.W["layers"][layer]
+        fz = self.fused[layer]
         ratio = self.cfg.compress_ratios[layer]
         pos = meta.positions
-        slot = pos % ratio
-        kv = (h @ lw["wc_kv"].T).float()
-        gate = (h @ lw["wc_gate"].T).float() + lw["c_ape"][slot]
-        done = slot == ratio - 1
-        raw = self._pool_update(self.pool.comp_state[layer], meta.req_slots, gate, kv, done).contiguous()
+        L = self.cfg.latent_dim
+        raw = fused_ops.comp_pool(y, fz["wc_kv"], L, lw["c_ape"], self.pool.comp_state[layer], meta.req_slots, pos)
         if ratio == abi.C4_RATIO:
             self._store_c4(layer, raw, meta.c4_write, (pos // ratio) * ratio)
-            k = (h @ lw["wi_k"].T).float()
-            kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot]
-            kraw = self._pool_update(self.pool.index_state[layer], meta.req_slots, kg, k, done)
+            kraw = fused_ops.comp_pool(y, fz["wi_k"], self.cfg.index_dim, lw["i_ape"], self.pool.index_state[layer],
+                                       meta.req_slots, pos)
             self._store_index_keys(layer, kraw, meta.c4_write)
         else:
             kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, meta.c128_write, (pos // ratio) * ratio,
@@ -188,76 +197,100 @@ class V4FlashModel:
         idx_ops.index_key_store(kraw, slots, self.pool.index_keys[layer], self.pool.index_scales[layer])
 
     # ------------------------------------------------------------------ indexer
-    def _index_topk(self, layer: int, q_lora: torch.Tensor, h: torch.Tensor, phys: torch.Tensor,
+    def _index_topk(self, layer: int, q_lora: torch.Tensor, y: torch.Tensor, phys: torch.Tensor,
                     count: torch.Tensor, r_limit: int):
         """Top-k C4 records per query: returns (slots int32 [B,K], rope positions int32 [B,K])."""
         lw = self.W["layers"][layer]
         cfg = self.cfg
         B = q_lora.shape[0]
         qi = (q_lora @ lw["wi_q"].T).view(B, cfg.index_heads, cfg.index_dim)
-        wi = (h @ lw["wi_w"].T).float() * (cfg.index_heads ** -0.5) * (cfg.index_dim ** -0.5)
-        return idx_ops.index_select(qi.to(torch.bfloat16).contiguous(), wi, self.pool.index_keys[layer],
-                                    self.pool.index_scales[layer], phys, count, r_limit, min(self.topk, r_limit))
+        c = self.fused[layer]["wi_w"]
+        wi = y[:, c:c + cfg.index_heads].float() * ((cfg.index_heads ** -0.5) * (cfg.index_dim ** -0.5))
+        return idx_ops.index_select(qi.contiguous(), wi, self.pool.index_keys[layer], self.pool.index_scales[layer],
+                                    phys, count, r_limit, min(self.topk, r_limit))
 
     # ------------------------------------------------------------------ layer
-    def _attention_block(self, layer: int, x: torch.Tensor, meta: StepMeta) -> torch.Tensor:
+    def _attention_block(self, layer: int, h: torch.Tensor, meta: StepMeta) -> torch.Tensor:
+        """Attention of the normed residual h [B, H] -> bf16 [B, H] (all-reduced over TP)."""
         cfg = self.cfg
         lw = self.W["layers"][layer]
-        B = x.shape[0]
-        h = rmsnorm(x, lw["attn_norm"], cfg.rms_eps)
-        qkv = h @ lw["wqkv_a"].T
-        q_lora = rmsnorm(qkv[:, :cfg.q_lora_rank], lw["q_norm"], cfg.rms_eps)
-        kv_raw = qkv[:, cfg.q_lora_rank:].float().contiguous()
+        B = h.shape[0]
+        y = h @ self.fused[layer]["w_h"].T
+        Q = cfg.q_lora_rank
+        q_lora = rmsnorm(y[:, :Q], lw["q_norm"], cfg.rms_eps)
+        kv_raw = y[:, Q:Q + cfg.latent_dim].float()
         kv_ops.native_store(kv_raw, lw["kv_norm"], cfg.rms_eps, meta.swa_write, meta.positions, self.freqs,
                             self.pool.swa[layer])
-        q = (q_lora @ lw["wq_b"].T).view(B, self.heads, cfg.latent_dim)
-        q = rotate_q_tail(q, self.freqs, meta.positions).contiguous()
+        q = fused_ops.rope_q((q_lora @ lw["wq_b"].T).view(B, self.heads, cfg.latent_dim), meta.positions, self.freqs)
         ratio = cfg.compress_ratios[layer]
         if ratio:
-            self._compress_decode(layer, h, meta)
-        empty = torch.zeros(B, 1, dtype=torch.int32, device=self.device) - 1
+            self._compress_decode(layer, y, meta)
         if ratio == abi.C4_RATIO:
-            csa_slots, csa_pos = self._index_topk(layer, q_lora, h, meta.c4_phys, meta.c4_count, self.r4max)
-            csa_len = torch.full((B,), csa_slots.shape[1], dtype=torch.int32, device=self.device)
+            csa_slots, csa_pos = self._index_topk(layer, q_lora, y, meta.c4_phys, meta.c4_count, self.r4max)
+            csa_len = meta.topk_len
             pool_native, planes = self.csa_planes(layer)
         elif ratio == abi.C128_RATIO:
             csa_slots, csa_pos, csa_len = meta.c128_slots, meta.c128_pos, meta.c128_len
             pool_native, planes = self.pool.c128_native[layer], None
         else:
-            csa_slots, csa_pos = empty, empty
-            csa_len = torch.zeros(B, dtype=torch.int32, device=self.device)
+            csa_slots, csa_pos, csa_len = meta.no_rows, meta.no_rows, meta.zero_len
             pool_native, planes = self.pool.swa[layer], None
         o, _ = attn_ops.sparse_mla_decode(
             q, self.pool.swa[layer], meta.swa_slots, meta.swa_len, csa_slots, csa_pos, csa_len, self.freqs,
-            lw["sink"], self.scale, meta.positions.int(), csa_pool=pool_native, csa_planes=planes)
+            lw["sink"], self.scale, meta.positions_i32, csa_pool=pool_native, csa_planes=planes)
+        return self._o_proj(layer, o, B)
+
+    def _o_proj(self, layer: int, o: torch.Tensor, B: int) -> torch.Tensor:
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
         o = o.view(B, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
         o_lora = torch.bmm(o, lw["wo_a"]).transpose(0, 1).reshape(B, self.groups * cfg.o_lora_rank)
         if self.ar_hook is not None:
             return self.ar_hook(o_lora, lw["wo_b"])
         return self._all_reduce(o_lora @ lw["wo_b"].T)
 
-    def _moe_block(self, layer: int, x: torch.Tensor) -> torch.Tensor:
+    def _moe_block(self, layer: int, h: torch.Tensor):
+        """Routed + shared experts of the normed residual h.
+
+        Returns the residual addends (bf16, fp32 or None): on one rank the shared expert's bf16 output
+        and the routed experts' fp32 sum, added to the residual by the next fused norm; over TP/EP their
+        all-reduced bf16 sum.
+        """
         cfg = self.cfg
         lw = self.W["layers"][layer]
-        h = rmsnorm(x, lw["ffn_norm"], cfg.rms_eps)
-        topk_ids, topk_w = moe_ops.route(h, lw["gate"], lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
+        fz = self.fused[layer]
+        g = h @ fz["w_ffn"].T
+        c = fz["gate"]
+        topk_ids, topk_w = fused_ops.route_topk(g[:, c:], lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
         out = moe_ops.experts(h, topk_ids, topk_w, lw, self.expert_base, self.local_experts, cfg.expert_format)
-        g_u = h @ lw["shared_w13"].T
-        il = g_u.shape[1] // 2
-        act = (F.silu(g_u[:, :il].float()) * g_u[:, il:].float()).to(torch.bfloat16)
-        out = out + (act @ lw["shared_w2"].T).float()
-        return self._all_reduce(out.to(torch.bfloat16))
+        shared = fused_ops.silu_mul(g[:, :c]) @ lw["shared_w2"].T
+        if self.comm is None or self.world == 1:
+            return shared, out
+        return self._all_reduce((out + shared.float()).to(torch.bfloat16)), None
+
+    def _layer_norms(self, layer: int):
+        lw = self.W["layers"][layer]
+        return lw["attn_norm"], lw["ffn_norm"]
 
     # ------------------------------------------------------------------ decode
     def decode(self, tokens: torch.Tensor, positions: torch.Tensor, req_slots: torch.Tensor) -> torch.Tensor:
-        """One decode step for B requests -> logits [B, vocab] (fp32)."""
+        """One decode step for B requests -> logits [B, vocab] (fp32).
+
+        The residual stream is bf16; each block's output is added to it by the fused norm that
+        starts the next block.
+        """
+        eps = self.cfg.rms_eps
         meta = self.step_meta(positions, req_slots)
         x = self.W["embed"][tokens]
+        d = dfp = None
         for layer in range(self.cfg.num_layers):
-            x = x + self._attention_block(layer, x, meta)
-            x = x + self._moe_block(layer, x)
-        x = rmsnorm(x, self.W["final_norm"], self.cfg.rms_eps)
-        return (x @ self.W["lm_head"].T).float()
+            n_attn, n_ffn = self._layer_norms(layer)
+            x, h = fused_ops.add_rmsnorm(x, n_attn, eps, d, dfp, inplace=True)
+            a = self._attention_block(layer, h, meta)
+            x, h = fused_ops.add_rmsnorm(x, n_ffn, eps, a, inplace=True)
+            d, dfp = self._moe_block(layer, h)
+        _, h = fused_ops.add_rmsnorm(x, self.W["final_norm"], eps, d, dfp, inplace=True)
+        return (h @ self.W["lm_head"].T).float()
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, tokens: torch.Tensor, start: int, req_slot: int) -> torch.Tensor:
@@ -292,32 +325,35 @@ class V4FlashModel:
         r2 = torch.arange(self.r128max, device=dev)
         pg2 = ct[(r2 // abi.RECORDS_PER_PAGE).clamp(max=ct.shape[0] - 1)]
         c128_phys_row = torch.where(pg2 >= 0, pg2 * abi.RECORDS_PER_PAGE + r2 % abi.RECORDS_PER_PAGE, -1)
+        eps = cfg.rms_eps
+        d = dfp = None
         for layer in range(cfg.num_layers):
             lw = self.W["layers"][layer]
-            h = rmsnorm(x, lw["attn_norm"], cfg.rms_eps)
-            qkv = h @ lw["wqkv_a"].T
-            q_lora = rmsnorm(qkv[:, :cfg.q_lora_rank], lw["q_norm"], cfg.rms_eps)
-            kv_raw = qkv[:, cfg.q_lora_rank:].float().contiguous()
+            n_attn, n_ffn = self._layer_norms(layer)
+            x, h = fused_ops.add_rmsnorm(x, n_attn, eps, d, dfp, inplace=True)
+            y = h @ self.fused[layer]["w_h"].T
+            Q = cfg.q_lora_rank
+            q_lora = rmsnorm(y[:, :Q], lw["q_norm"], eps)
+            kv_raw = y[:, Q:Q + cfg.latent_dim].float().contiguous()
             scratch = torch.zeros(scr_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
             if bool(prev_ok.any()):
                 ring = req_slot * W + prev[prev_ok] % W
                 recs = kv_ops.native_pool_read(self.pool.swa[layer], ring)
                 _native_pool_write(scratch, torch.nonzero(prev_ok)[:, 0], recs)
-            kv_ops.native_store(kv_raw, lw["kv_norm"], cfg.rms_eps, torch.arange(W - 1, W - 1 + T, device=dev),
+            kv_ops.native_store(kv_raw, lw["kv_norm"], eps, torch.arange(W - 1, W - 1 + T, device=dev),
                                 pos, self.freqs, scratch)
             last = slice(max(0, T - W), T)
-            kv_ops.native_store(kv_raw[last].contiguous(), lw["kv_norm"], cfg.rms_eps, req_slot * W + pos[last] % W,
+            kv_ops.native_store(kv_raw[last].contiguous(), lw["kv_norm"], eps, req_slot * W + pos[last] % W,
                                 pos[last], self.freqs, self.pool.swa[layer])
-            q = (q_lora @ lw["wq_b"].T).view(T, self.heads, cfg.latent_dim)
-            q = rotate_q_tail(q, self.freqs, pos).contiguous()
+            q = fused_ops.rope_q((q_lora @ lw["wq_b"].T).view(T, self.heads, cfg.latent_dim), pos, self.freqs)
             ratio = cfg.compress_ratios[layer]
             if ratio:
-                self._compress_prefill(layer, h, pos, req_slot, c4_phys_row, c128_phys_row)
+                self._compress_prefill(layer, y, pos, req_slot, c4_phys_row, c128_phys_row)
             if ratio == abi.C4_RATIO:
                 count = (pos + 1) // abi.C4_RATIO
                 n_vis = int(min(self.r4max, (start + T) // abi.C4_RATIO))
                 lim = max(1, n_vis)
-                csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, h, c4_phys_row, count, lim)
+                csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, y, c4_phys_row, count, lim)
                 csa_len = torch.full((T,), csa_slots.shape[1], dtype=torch.int32, device=dev)
                 pool_native, planes = self.csa_planes(layer)
             elif ratio == abi.C128_RATIO:
@@ -335,52 +371,54 @@ class V4FlashModel:
                 csa_len = torch.zeros(T, dtype=torch.int32, device=dev)
                 pool_native, planes = self.pool.swa[layer], None
             o, _ = attn_ops.sparse_mla_decode(
-                q, scratch, swa_slots, swa_len, csa_slots, csa_pos, csa_len, self.freqs, lw["sink"], self.scale,
-                meta_pos.int(), csa_pool=pool_native, csa_planes=planes)
-            o = o.view(T, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
-            o_lora = torch.bmm(o, lw["wo_a"]).transpose(0, 1).reshape(T, self.groups * cfg.o_lora_rank)
-            x = x + self._all_reduce(o_lora @ lw["wo_b"].T)
-            x = x + self._moe_block(layer, x)
-        x = rmsnorm(x[-1:], self.W["final_norm"], cfg.rms_eps)
-        return (x @ self.W["lm_head"].T).float()[0]
+                q.contiguous(), scratch, swa_slots, swa_len, csa_slots, csa_pos, csa_len, self.freqs, lw["sink"],
+                self.scale, meta_pos.int(), csa_pool=pool_native, csa_planes=planes)
+            a = self._o_proj(layer, o, T)
+            x, h = fused_ops.add_rmsnorm(x, n_ffn, eps, a, inplace=True)
+            d, dfp = self._moe_block(layer, h)
+        _, h = fused_ops.add_rmsnorm(x[-1:], self.W["final_norm"], eps, d[-1:],
+                                     None if dfp is None else dfp[-1:])
+        return (h @ self.W["lm_head"].T).float()[0]
 
-    def _index_topk_chunked(self, layer, q_lora, h, phys_row, count, lim, block: int = 256):
+    def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int = 256):
         T = q_lora.shape[0]
         outs_s, outs_p = [], []
         for t0 in range(0, T, block):
             t1 = min(T, t0 + block)
             ph = phys_row[:lim][None].expand(t1 - t0, -1).int().contiguous()
-            s, p = self._index_topk(layer, q_lora[t0:t1], h[t0:t1], ph, count[t0:t1], lim)
+            s, p = self._index_topk(layer, q_lora[t0:t1], y[t0:t1], ph, count[t0:t1], lim)
             outs_s.append(s)
             outs_p.append(p)
         return torch.cat(outs_s).contiguous(), torch.cat(outs_p).contiguous()
 
-    def _compress_prefill(self, layer, h, pos, req_slot, c4_phys_row, c128_phys_row):
+    def _compress_prefill(self, layer, y, pos, req_slot, c4_phys_row, c128_phys_row):
         """Sequential-equivalent pooling over the chunk; stores every record completed in it."""
         lw = self.W["layers"][layer]
+        fz = self.fused[layer]
         ratio = self.cfg.compress_ratios[layer]
+        L, D = self.cfg.latent_dim, self.cfg.index_dim
         slot_in = pos % ratio
-        kv = (h @ lw["wc_kv"].T).float()
-        gate = (h @ lw["wc_gate"].T).float() + lw["c_ape"][slot_in]
+        c = fz["wc_kv"]
+        kv = y[:, c:c + L].float()
+        gate = y[:, c + L:c + 2 * L].float() + lw["c_ape"][slot_in]
         raw, rec = _pool_chunk(self.pool.comp_state[layer], req_slot, gate, kv, pos, ratio)
-        if rec.numel():
-            if ratio == abi.C4_RATIO:
-                slots = c4_phys_row[rec.clamp(max=self.r4max - 1)]
-                slots = torch.where(rec < self.r4max, slots, -1)
-                self._store_c4(layer, raw, slots, rec * ratio)
-                k = (h @ lw["wi_k"].T).float()
-                kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot_in]
-                kraw, _ = _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
-                self._store_index_keys(layer, kraw, slots)
-            else:
-                slots = c128_phys_row[rec.clamp(max=self.r128max - 1)]
-                slots = torch.where(rec < self.r128max, slots, -1)
-                kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rec * ratio, self.freqs,
-                                    self.pool.c128_native[layer])
-        elif ratio == abi.C4_RATIO:
-            k = (h @ lw["wi_k"].T).float()
-            kg = (h @ lw["wi_kgate"].T).float() + lw["i_ape"][slot_in]
-            _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
+        if ratio == abi.C4_RATIO:
+            c = fz["wi_k"]
+            k = y[:, c:c + D].float()
+            kg = y[:, c + D:c + 2 * D].float() + lw["i_ape"][slot_in]
+            kraw, _ = _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
+        if not rec.numel():
+            return
+        if ratio == abi.C4_RATIO:
+            slots = c4_phys_row[rec.clamp(max=self.r4max - 1)]
+            slots = torch.where(rec < self.r4max, slots, -1)
+            self._store_c4(layer, raw, slots, rec * ratio)
+            self._store_index_keys(layer, kraw, slots)
+        else:
+            slots = c128_phys_row[rec.clamp(max=self.r128max - 1)]
+            slots = torch.where(rec < self.r128max, slots, -1)
+            kv_ops.native_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rec * ratio, self.freqs,
+                                self.pool.c128_native[layer])
 
 
 def _pool_chunk(state: torch.Tensor, req_slot: int, gate: torch.Tensor, val: torch.Tensor, pos: torch.Tensor,

@@ -7,9 +7,10 @@ Experts on this rank are [expert_base, expert_base + local_experts).  Tokens are
 every TP/EP rank, so each rank computes its local experts' contribution and the caller's
 all-reduce combines ranks (the MoE down-projection partial sums).
 
-* MXFP4 experts on CUDA: routing lists (csrc/moe_fp4.cu), then csrc/moe_fp4_tc.cu: tcgen05 with
-  the dequantized weight tile in tensor memory, gate/up with SiLU, down with the routed-weight
-  scatter-add; weights use the tiled layout made once by `prepare_experts`.
+* MXFP4 experts on CUDA: routing lists (csrc/moe_fp4.cu), then csrc/moe_fp4_mma.cu: bulk-copy
+  weight stream dequantized straight into register MMA fragments, gate/up with SiLU, down with the
+  routed-weight scatter-add; weights use the fragment-ordered layout made once by
+  `prepare_experts`.  csrc/moe_fp4_tc.cu (tcgen05, weight operand in TMEM) uses `tile_fp4`.
 * BF16 experts (tiny CPU configs, tests): PyTorch reference.
 """
 from __future__ import annotations
@@ -84,12 +85,55 @@ def tile_fp4(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torch.Ten
     return w_t, s_t
 
 
+_FRAG_INDEX: dict = {}
+
+
+def _frag_index(device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gather indices of the fragment-ordered tile (row, byte) and scale (row, block) layouts."""
+    key = str(device)
+    if key not in _FRAG_INDEX:
+        ks, rh, mt, lane, s, bi = torch.meshgrid(torch.arange(4), torch.arange(2), torch.arange(4), torch.arange(32),
+                                                 torch.arange(4), torch.arange(4), indexing="ij")
+        g, q = lane // 4, lane % 4
+        rows = 64 * rh + 16 * mt + g + 8 * (bi & 1)
+        byts = 32 * ks + 8 * s + q + 4 * (bi >> 1)
+        ks2, rh2, g2, mt2, blk, rsel = torch.meshgrid(torch.arange(4), torch.arange(2), torch.arange(8), torch.arange(4),
+                                                      torch.arange(2), torch.arange(2), indexing="ij")
+        srows = 64 * rh2 + 16 * mt2 + g2 + 8 * rsel
+        sblk = 2 * ks2 + blk
+        _FRAG_INDEX[key] = tuple(t.reshape(-1).to(device) for t in (rows, byts, srows, sblk))
+    return _FRAG_INDEX[key]
+
+
+def tile_fp4_frag(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Canonical MXFP4 [E, R, K/2] + scales [E, R, K/32] -> register-fragment tiles (csrc/moe_fp4_mma.cu).
+
+    Returns w_f [E, R/128, K/256, 16384] and s_f [E, R/128, K/256, 1024]; row tiles as tile_fp4.
+    """
+    E, R, Kh = w.shape
+    K = Kh * 2
+    if gate_up:
+        I = R // 2
+        w = torch.cat((w[:, :I].reshape(E, I // 64, 64, Kh), w[:, I:].reshape(E, I // 64, 64, Kh)), 2)
+        s = torch.cat((s[:, :I].reshape(E, I // 64, 64, K // 32), s[:, I:].reshape(E, I // 64, 64, K // 32)), 2)
+    else:
+        w = w.reshape(E, R // 128, 128, Kh)
+        s = s.reshape(E, R // 128, 128, K // 32)
+    nrt, kt = w.shape[1], K // 256
+    tiles = w.reshape(E, nrt, 128, kt, 128).permute(0, 1, 3, 2, 4).reshape(E, nrt, kt, 128 * 128)
+    stiles = s.reshape(E, nrt, 128, kt, 8).permute(0, 1, 3, 2, 4).reshape(E, nrt, kt, 128 * 8)
+    rows, byts, srows, sblk = _frag_index(w.device)
+    w_f = tiles[..., rows * 128 + byts].contiguous()
+    s_f = stiles[..., srows * 8 + sblk].contiguous()
+    return w_f, s_f
+
+
 def prepare_experts(lw: dict, drop_canonical: bool = True) -> None:
     """Add the kernel layout (w13_t, s13_t, w2_t, s2_t) to a layer's MXFP4 expert weights."""
-    if "w13_t" in lw:
+    if "w13_f" in lw:
         return
-    lw["w13_t"], lw["s13_t"] = tile_fp4(lw["w13"], lw["s13"], True)
-    lw["w2_t"], lw["s2_t"] = tile_fp4(lw["w2"], lw["s2"], False)
+    lw["w13_f"], lw["s13_f"] = tile_fp4_frag(lw["w13"], lw["s13"], True)
+    lw["w2_f"], lw["s2_f"] = tile_fp4_frag(lw["w2"], lw["s2"], False)
     if drop_canonical:
         for k in ("w13", "s13", "w2", "s2"):
             lw.pop(k)
@@ -104,8 +148,10 @@ class MoEWorkspace:
         self.slot_token = torch.zeros(n, dtype=torch.int32, device=device)
         self.slot_weight = torch.zeros(n, dtype=torch.float32, device=device)
         self.active = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
-        self.act = torch.zeros(n, inter, dtype=torch.float16, device=device)  # slot layout (swizzled)
-        self.xs = torch.zeros(n, hidden, dtype=torch.float16, device=device)  # routed token rows per slot
+        rows = n + 16 * local_experts  # padded per-expert slot rows (each list starts on a multiple of 16)
+        self.pad = torch.zeros(local_experts + 1, dtype=torch.int32, device=device)
+        self.act = torch.zeros(rows, inter, dtype=torch.float16, device=device)  # down-pass token rows
+        self.xs = torch.zeros(rows, hidden, dtype=torch.float16, device=device)  # gate/up token rows
         self.max_tokens = max_tokens
 
 
@@ -132,7 +178,7 @@ def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, 
         return out
     T, H = h.shape
     k = topk_ids.shape[1]
-    I = lw["w13_t"].shape[1] * 64 if "w13_t" in lw else lw["w13"].shape[1] // 2
+    I = lw["w13_f"].shape[1] * 64 if "w13_f" in lw else lw["w13"].shape[1] // 2
     ws = workspace
     if ws is None:
         key = (h.device.index, T, k, local_experts, I)
@@ -141,8 +187,8 @@ def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, 
             ws = MoEWorkspace(T, k, local_experts, I, h.device, hidden=H)
             _WS[key] = ws
     out = torch.zeros(T, H, dtype=torch.float32, device=h.device)
-    if "w13_t" not in lw:
+    if "w13_f" not in lw:
         prepare_experts(lw, drop_canonical=False)
-    ext().moe_fp4_tc(h, topk_ids, topk_w, expert_base, lw["w13_t"], lw["s13_t"], lw["w2_t"], lw["s2_t"], ws.offsets,
-                     ws.slot_token, ws.slot_weight, ws.active, ws.xs, ws.act, out, error_word(h.device))
+    ext().moe_fp4_mma(h, topk_ids, topk_w, expert_base, lw["w13_f"], lw["s13_f"], lw["w2_f"], lw["s2_f"], ws.offsets,
+                      ws.slot_token, ws.slot_weight, ws.active, ws.pad, ws.xs, ws.act, out, error_word(h.device))
     return out
