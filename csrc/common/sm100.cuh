@@ -212,6 +212,44 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Block-scaled D[tmem] (+)= (A * SFA) [smem] * (B * SFB)^T [smem] for 8/6/4-bit operands with UE8M0
+// scales per 32 K values (kind::mxf8f6f4, K = 32 per instruction), one thread.  Scale factors live in
+// TMEM: row m of A at lane m, column sfa + m / 32; column n of B at lane 32 q + n % 32 of every lane
+// quadrant q, column sfb + n / 32; the byte inside the 32-bit cell is the sf_id of the descriptor.
+__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4 with UE8M0 scales: a/b format 0 = E4M3, 5 = E2M1 (both
+// K-major), sf ids select the scale byte of A / B.
+__host__ __device__ constexpr uint32_t make_idesc_mxf8(int M, int N, int a_fmt, int b_fmt, int a_sf, int b_sf) {
+  return ((uint32_t)b_sf << 4) | ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10) | ((uint32_t)(N >> 3) << 17) |
+         (1u << 23) | ((uint32_t)(M >> 4) << 24) | ((uint32_t)a_sf << 29);
+}
+
+// Copy a 32-row x 16-byte matrix from shared memory (no swizzle, rows 16 B apart) into 4 TMEM columns of
+// all four lane quadrants (lane 32 q + r receives row r), asynchronously in the issuing thread's
+// tcgen05 stream (ordered before its later tcgen05.mma).
+__device__ __forceinline__ void tmem_cp_32x128_x4(uint32_t taddr, uint32_t saddr) {
+  const uint64_t desc = (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(512 >> 4) << 16) |
+                        ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) of box (x, y) of `tmap` into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ----------------------------------------------------------------------------- SW128 layout
 // Byte offset of element (row, col16) inside a K-major 128B-swizzled tile whose rows are
 // `row_bytes` long: atoms of 8 rows x 128 B; chunks of 128 B along the row are laid out

@@ -89,3 +89,11 @@ void launch_comp_pool(const __nv_bfloat16* proj, int64_t ps, int off, int D, con
 void launch_route_topk(const __nv_bfloat16* logits, int64_t ls, int T, int E, const float* bias, int k, float scaling,
                        int32_t* ids, float* wts, cudaStream_t stream);
 void launch_silu_mul(const __nv_bfloat16* gu, int64_t gs, int T, int I, __nv_bfloat16* out, cudaStream_t stream);
+void launch_bs_probe(const uint8_t* a_img, const uint8_t* b_img, const uint32_t* sfa, const uint32_t* sfb,
+                     uint32_t idesc, int kind, int N, uint32_t sfa_extra, uint32_t sfb_extra, float* d, int* err,
+                     cudaStream_t stream);
+int make_tmap_fp4_unpacked(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
+                           uint32_t box_rows);
+int launch_bs_probe2(const uint8_t* a_packed, const uint8_t* b_img, const uint8_t* sfa_src, const uint8_t* sfb_src,
+                     int N, int k_steps, uint32_t expect_tx, float* d, uint8_t* a_dump, int* err,
+                     cudaStream_t stream);

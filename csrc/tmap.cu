@@ -1,0 +1,39 @@
+// Host-side TMA tensor-map encoding (driver entry point fetched through the runtime, so the
+// extension needs no direct libcuda symbol at load time).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "launchers.h"
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+// 2-D map over a row-major matrix of packed FP4 (two per byte, K contiguous) that unpacks into the
+// shared-memory layout of the tcgen05 8/6/4-bit kinds (16 values in the first 8 bytes of every 16-byte
+// chunk) with the 128-byte swizzle: a box of 128 values x box_rows rows fills box_rows x 128 bytes.
+int make_tmap_fp4_unpacked(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
+                           uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  const cuuint64_t dims[2] = {k_elems, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return (int)fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2,
+                 const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}

@@ -440,6 +440,50 @@ void silu_mul(torch::Tensor gu, torch::Tensor out) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// One block-scaled tcgen05 MMA on host-supplied shared-memory / TMEM images (layout self-test).
+torch::Tensor bs_probe(torch::Tensor a_img, torch::Tensor b_img, torch::Tensor sfa, torch::Tensor sfb, int64_t idesc,
+                       int64_t kind, int64_t sfa_extra, int64_t sfb_extra, torch::Tensor err) {
+  TORCH_CHECK(a_img.is_cuda() && a_img.scalar_type() == torch::kUInt8 && a_img.is_contiguous() &&
+              a_img.numel() == 128 * 128);
+  TORCH_CHECK(b_img.scalar_type() == torch::kUInt8 && b_img.is_contiguous() && b_img.dim() == 2 &&
+              b_img.size(1) == 128);
+  const int N = b_img.size(0);
+  TORCH_CHECK(N >= 8 && N <= 256 && N % 8 == 0);
+  TORCH_CHECK(sfa.scalar_type() == torch::kInt32 && sfa.is_contiguous() && sfa.numel() == 128 * 16);
+  TORCH_CHECK(sfb.scalar_type() == torch::kInt32 && sfb.is_contiguous() && sfb.numel() == 128 * 16);
+  TORCH_CHECK(kind >= 0 && kind <= 2 && sfa_extra >= 0 && sfa_extra < 16 && sfb_extra >= 0 && sfb_extra < 16);
+  const c10::cuda::CUDAGuard g(a_img.device());
+  auto d = torch::zeros({128, N}, a_img.options().dtype(torch::kFloat32));
+  launch_bs_probe(a_img.data_ptr<uint8_t>(), b_img.data_ptr<uint8_t>(),
+                  reinterpret_cast<const uint32_t*>(sfa.data_ptr<int>()),
+                  reinterpret_cast<const uint32_t*>(sfb.data_ptr<int>()), (uint32_t)idesc, (int)kind, N,
+                  (uint32_t)sfa_extra, (uint32_t)sfb_extra, d.data_ptr<float>(), err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return d;
+}
+
+// TMA-unpacked FP4 A, tcgen05.cp scale factors, k_steps block-scaled MMAs -> (D, shared image of A).
+std::vector<torch::Tensor> bs_probe2(torch::Tensor a_packed, torch::Tensor b_img, torch::Tensor sfa_src,
+                                     torch::Tensor sfb_src, int64_t k_steps, int64_t expect_tx, torch::Tensor err) {
+  TORCH_CHECK(a_packed.is_cuda() && a_packed.scalar_type() == torch::kUInt8 && a_packed.is_contiguous() &&
+              a_packed.numel() == 128 * 64);
+  TORCH_CHECK(b_img.scalar_type() == torch::kUInt8 && b_img.is_contiguous() && b_img.dim() == 2 &&
+              b_img.size(1) == 128);
+  const int N = b_img.size(0);
+  TORCH_CHECK(N >= 8 && N <= 256 && N % 8 == 0 && k_steps >= 1 && k_steps <= 4);
+  TORCH_CHECK(sfa_src.numel() == 512 && sfb_src.numel() == 512 && sfa_src.is_contiguous() && sfb_src.is_contiguous());
+  TORCH_CHECK(expect_tx == 8192 || expect_tx == 16384);
+  const c10::cuda::CUDAGuard g(a_packed.device());
+  auto d = torch::zeros({128, N}, a_packed.options().dtype(torch::kFloat32));
+  auto dump = torch::zeros({128, 128}, a_packed.options());
+  const int rc = launch_bs_probe2(a_packed.data_ptr<uint8_t>(), b_img.data_ptr<uint8_t>(), sfa_src.data_ptr<uint8_t>(),
+                                  sfb_src.data_ptr<uint8_t>(), N, (int)k_steps, (uint32_t)expect_tx,
+                                  d.data_ptr<float>(), dump.data_ptr<uint8_t>(), err.data_ptr<int>(), stream());
+  TORCH_CHECK(rc == 0, "tensor map encoding failed: ", rc);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {d, dump};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -448,6 +492,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)");
   m.def("index_key_store", &index_key_store, "FP8 index keys (swizzled rows) + fp32 scales");
   m.def("index_select", &index_select, "FP8 tcgen05 indexer logits + radix top-k");
+  m.def("bs_probe2", &bs_probe2, "TMA FP4 + tcgen05.cp scale-factor pipeline self-test");
+  m.def("bs_probe", &bs_probe, "block-scaled tcgen05 MMA layout self-test");
   m.def("add_rmsnorm", &add_rmsnorm, "residual add + RMSNorm (bf16)");
   m.def("rope_q", &rope_q, "in-place RoPE of query tails");
   m.def("comp_pool", &comp_pool, "compressor online-softmax pooling of one token per row");
