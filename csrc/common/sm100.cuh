@@ -277,6 +277,14 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// Exact UE8M0 exponent: smallest e with 448 * 2^e >= max(amax, 1e-4).
+__device__ __forceinline__ int ue8m0_exp(float amax) {
+  float a = fmaxf(amax, 1e-4f);
+  uint32_t bits = __float_as_uint(a);
+  int E = (int)((bits >> 23) & 0xFF) - 127;  // a = 1.m * 2^E (normal floats only: a >= 1e-4)
+  uint32_t m = bits & 0x7FFFFF;              // 1.75 -> 0x600000
+  return E - 8 + (m > 0x600000u ? 1 : 0);
+}
 // Packed e4m3x2 -> half2 (exact).
 __device__ __forceinline__ __half2 e4m3x2_to_h2(uint16_t v) {
   uint32_t r;

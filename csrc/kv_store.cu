@@ -18,14 +18,7 @@ constexpr int kNativePageBytes = kPage * 584;
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// Exact UE8M0 exponent: smallest e with 448 * 2^e >= max(amax, 1e-4).
-__device__ __forceinline__ int ue8m0_exp(float amax) {
-  float a = fmaxf(amax, 1e-4f);
-  uint32_t bits = __float_as_uint(a);
-  int E = (int)((bits >> 23) & 0xFF) - 127;  // a = 1.m * 2^E (normal floats only: a >= 1e-4)
-  uint32_t m = bits & 0x7FFFFF;              // 1.75 -> 0x600000
-  return E - 8 + (m > 0x600000u ? 1 : 0);
-}
+using pm::ue8m0_exp;
 
 __device__ __forceinline__ float half_max(float v) {
 #pragma unroll

@@ -97,3 +97,34 @@ int make_tmap_fp4_unpacked(void* out, const void* base, uint64_t k_elems, uint64
 int launch_bs_probe2(const uint8_t* a_packed, const uint8_t* b_img, const uint8_t* sfa_src, const uint8_t* sfb_src,
                      int N, int k_steps, uint32_t expect_tx, float* d, uint8_t* a_dump, int* err,
                      cudaStream_t stream);
+
+void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
+                             int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
+                             int4* chunks, int32_t* n_chunks, cudaStream_t stream);
+
+// MXFP4 experts x MXFP8 activations (csrc/moe_mxf4.cu).  Workspace images: xq [H/128, rows, 128],
+// xs [rows/32, H/128, 512], act_q [I/128, rows, 128], act_s [rows/32, I/128, 512] (rows % 32 == 0).
+struct MoeMxArgs {
+  const __nv_bfloat16* h;
+  int T, H, I, k, E, expert_base, rows_total, num_sms;
+  const int32_t* topk_ids;
+  const float* topk_w;
+  const uint8_t* w13;    // [E, 2I, H/2] packed E2M1
+  const uint8_t* sfa13;  // [E*2I/128, H/128, 512] scale-factor blocks
+  const uint8_t* w2;     // [E, H, I/2]
+  const uint8_t* sfa2;   // [E*H/128, I/128, 512]
+  int32_t* offsets;
+  int32_t* slot_token;
+  float* slot_weight;
+  int32_t* active;
+  int32_t* pad;
+  int4* chunks;
+  int32_t* n_chunks;
+  uint8_t* xq;
+  uint8_t* xs;
+  uint8_t* act_q;
+  uint8_t* act_s;
+  float* out;  // [T, H] fp32 (zeroed by the kernel)
+  int* err;
+};
+int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream);

@@ -28,7 +28,8 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
                                                          int E, int32_t* __restrict__ offsets,
                                                          int32_t* __restrict__ slot_token,
                                                          float* __restrict__ slot_weight, int32_t* __restrict__ active,
-                                                         int32_t* __restrict__ pad) {
+                                                         int32_t* __restrict__ pad, int align,
+                                                         int4* __restrict__ chunks, int32_t* __restrict__ n_chunks) {
   extern __shared__ int sh[];
   int* cnt = sh;         // [E]
   int* cur = sh + E;     // [E]
@@ -41,17 +42,20 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
   }
   __syncthreads();
   if (tid == 0) {
-    int acc = 0, na = 0, pacc = 0;
+    int acc = 0, na = 0, pacc = 0, nc = 0;
     for (int e = 0; e < E; ++e) {
       offsets[e] = acc;
       cur[e] = acc;
-      if (pad) pad[e] = pacc;  // padded rows: each expert's list starts on a multiple of 16
+      if (pad) pad[e] = pacc;  // padded rows: each expert's list starts on a multiple of `align`
       if (cnt[e] > 0) active[1 + na++] = e;
+      if (chunks)  // chunk table: {expert, first padded row, tokens (<= 32), first slot}
+        for (int c = 0; c < cnt[e]; c += 32) chunks[nc++] = make_int4(e, pacc + c, min(32, cnt[e] - c), acc + c);
       acc += cnt[e];
-      pacc += (cnt[e] + 15) & ~15;
+      pacc += (cnt[e] + align - 1) / align * align;
     }
     offsets[E] = acc;
     if (pad) pad[E] = pacc;
+    if (n_chunks) n_chunks[0] = nc;
     active[0] = na;
   }
   __syncthreads();
@@ -275,7 +279,7 @@ void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k
                       cudaStream_t stream) {
   if (T == 0) return;
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
-                                                           slot_token, slot_weight, active, pad);
+                                                           slot_token, slot_weight, active, pad, 16, nullptr, nullptr);
 }
 
 void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const int32_t* topk_ids, const float* topk_w,
@@ -284,7 +288,8 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
                     __nv_bfloat16* act, float* out, int num_sms, cudaStream_t stream) {
   if (T == 0) return;
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
-                                                           slot_token, slot_weight, active, nullptr);
+                                                           slot_token, slot_weight, active, nullptr, 16, nullptr,
+                                                           nullptr);
   MoeParams p{x, T, H, I, E, w13, s13, w2, s2, offsets, slot_token, slot_weight, active, act, out};
   const int smem_gu = kMT * H * 2, smem_dn = kMT * I * 2;
   auto gate_up = [&](auto kern) {
@@ -305,4 +310,11 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
     case 2: down(moe_down_kernel<2>); break;
     default: down(moe_down_kernel<4>); break;
   }
+}
+
+void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
+                             int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
+                             int4* chunks, int32_t* n_chunks, cudaStream_t stream) {
+  moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
+                                                           slot_token, slot_weight, active, pad, 32, chunks, n_chunks);
 }

@@ -484,6 +484,55 @@ std::vector<torch::Tensor> bs_probe2(torch::Tensor a_packed, torch::Tensor b_img
   return {d, dump};
 }
 
+// MXFP4 experts with MXFP8 activations: route + quantize + gate/up + down (4 launches).
+void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base, torch::Tensor w13,
+              torch::Tensor sfa13, torch::Tensor w2, torch::Tensor sfa2, torch::Tensor offsets, torch::Tensor slot_token,
+              torch::Tensor slot_weight, torch::Tensor active, torch::Tensor pad, torch::Tensor chunks,
+              torch::Tensor n_chunks, torch::Tensor xq, torch::Tensor xs, torch::Tensor act_q, torch::Tensor act_s,
+              torch::Tensor out, torch::Tensor err) {
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
+  const int T = h.size(0), H = h.size(1);
+  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.is_contiguous() && topk_ids.size(0) == T);
+  const int k = topk_ids.size(1);
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() && topk_w.numel() == (int64_t)T * k);
+  TORCH_CHECK(w13.scalar_type() == torch::kUInt8 && w13.dim() == 3 && w13.is_contiguous() && w13.size(2) * 2 == H);
+  const int E = w13.size(0), I = w13.size(1) / 2;
+  TORCH_CHECK(H % 512 == 0 && I % 512 == 0 && H <= 4096 && I <= 4096, "moe_mxf4: H, I multiples of 512, <= 4096");
+  TORCH_CHECK(w2.scalar_type() == torch::kUInt8 && w2.is_contiguous() && w2.size(0) == E && w2.size(1) == H &&
+              w2.size(2) * 2 == I);
+  TORCH_CHECK(sfa13.is_contiguous() && sfa13.numel() == (int64_t)E * 2 * I / 128 * (H / 128) * 512);
+  TORCH_CHECK(sfa2.is_contiguous() && sfa2.numel() == (int64_t)E * H / 128 * (I / 128) * 512);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w13.data_ptr()) % 32 == 0 && reinterpret_cast<uintptr_t>(w2.data_ptr()) % 32 == 0);
+  const int rows = xq.dim() == 3 ? xq.size(1) : 0;
+  TORCH_CHECK(rows % 32 == 0 && rows >= T * k + 31 * std::min(E, T * k), "moe_mxf4: workspace rows too small");
+  TORCH_CHECK(xq.is_contiguous() && xq.size(0) == H / 128 && xq.size(2) == 128);
+  TORCH_CHECK(act_q.is_contiguous() && act_q.dim() == 3 && act_q.size(0) == I / 128 && act_q.size(1) == rows);
+  TORCH_CHECK(xs.is_contiguous() && xs.numel() == (int64_t)rows * H / 8);
+  TORCH_CHECK(act_s.is_contiguous() && act_s.numel() == (int64_t)rows * I / 8);
+  TORCH_CHECK(offsets.numel() >= E + 1 && pad.numel() >= E + 1 && active.numel() >= E + 1);
+  TORCH_CHECK(slot_token.numel() >= (int64_t)T * k && slot_weight.numel() >= (int64_t)T * k);
+  TORCH_CHECK(chunks.scalar_type() == torch::kInt32 && chunks.is_contiguous() && chunks.numel() >= (int64_t)T * k * 4);
+  TORCH_CHECK(n_chunks.scalar_type() == torch::kInt32 && n_chunks.numel() >= 1);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.size(0) == T && out.size(1) == H);
+  const c10::cuda::CUDAGuard g(h.device());
+  MoeMxArgs a{};
+  a.h = bf16_ptr(h);
+  a.T = T; a.H = H; a.I = I; a.k = k; a.E = E; a.expert_base = (int)expert_base; a.rows_total = rows;
+  a.num_sms = num_sms_of(h.device());
+  a.topk_ids = topk_ids.data_ptr<int32_t>(); a.topk_w = topk_w.data_ptr<float>();
+  a.w13 = w13.data_ptr<uint8_t>(); a.sfa13 = sfa13.data_ptr<uint8_t>();
+  a.w2 = w2.data_ptr<uint8_t>(); a.sfa2 = sfa2.data_ptr<uint8_t>();
+  a.offsets = offsets.data_ptr<int32_t>(); a.slot_token = slot_token.data_ptr<int32_t>();
+  a.slot_weight = slot_weight.data_ptr<float>(); a.active = active.data_ptr<int32_t>(); a.pad = pad.data_ptr<int32_t>();
+  a.chunks = reinterpret_cast<int4*>(chunks.data_ptr<int32_t>()); a.n_chunks = n_chunks.data_ptr<int32_t>();
+  a.xq = xq.data_ptr<uint8_t>(); a.xs = xs.data_ptr<uint8_t>();
+  a.act_q = act_q.data_ptr<uint8_t>(); a.act_s = act_s.data_ptr<uint8_t>();
+  a.out = out.data_ptr<float>(); a.err = err.data_ptr<int>();
+  const int rc = launch_moe_mxf4(a, stream());
+  TORCH_CHECK(rc == 0, "moe_mxf4 launch failed: ", rc);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -499,6 +548,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comp_pool", &comp_pool, "compressor online-softmax pooling of one token per row");
   m.def("route_topk", &route_topk, "sigmoid top-k MoE routing");
   m.def("silu_mul", &silu_mul, "silu(gate) * up");
+  m.def("moe_mxf4", &moe_mxf4, "MXFP4 experts x MXFP8 activations (tcgen05 block-scaled)");
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");

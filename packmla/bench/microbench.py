@@ -68,19 +68,22 @@ def bench_moe(args, dev):
     lw = {}
     lw["w13"], lw["s13"] = _fp4_expert(E, 2 * I, H, g, dev)
     lw["w2"], lw["s2"] = _fp4_expert(E, H, I, g, dev)
-    moe_ops.prepare_experts(lw)
+    if args.precision == "bf16":
+        moe_ops.prepare_experts(lw)
+    else:
+        moe_ops.prepare_experts_mx(lw)
     h = torch.randn(args.tokens, H, device=dev, generator=g).bfloat16()
     gate = torch.randn(E, H, device=dev, generator=g).bfloat16() * H ** -0.5
     ids, w = moe_ops.route(h, gate, torch.zeros(E, device=dev), k, 1.0)
     active = int(torch.unique(ids).numel())
-    fn = lambda: moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4")  # noqa: E731
+    fn = lambda: moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4", precision=args.precision)  # noqa: E731
     us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev))
     check_errors(dev)
     per_expert = (2 * I * H + H * I) // 2 + (2 * I * H + H * I) // 32
     nbytes = active * per_expert
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
-    return {"case": "moe_fp4", "tokens": args.tokens, "experts": E, "topk": k, "active_experts": active,
+    return {"case": "moe_fp4", "precision": args.precision, "tokens": args.tokens, "experts": E, "topk": k, "active_experts": active,
             "us": round(us, 2), "weight_bytes": nbytes, "GBps": round(gbs, 1),
             "hbm_fraction": round(gbs / peak, 3), "peak_note": tag}
 
@@ -182,6 +185,7 @@ def main():
     ap.add_argument("--rows", type=int, default=24)
     ap.add_argument("--rounds", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--precision", default="default", choices=["default", "bf16"])
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     if args.case == "moe":

@@ -145,6 +145,9 @@ class EngineConfig:
     random_seed: int = 0
     device: str = "cuda"
     fused_collectives: bool = True
+    # MoE activation precision, as the reference's --flashinfer-mxfp4-moe-precision: "default" quantizes
+    # expert inputs to MXFP8 (E4M3 + UE8M0 per 32) on sm_100, "bf16" keeps them in BF16.
+    moe_precision: str = "default"
 
     def validate(self) -> None:
         """Reject unsupported combinations before any pool allocation.
@@ -164,3 +167,5 @@ class EngineConfig:
             raise ValueError("tp and ep must be >= 1")
         if self.hicache_ratio <= 0:
             raise ValueError("hicache_ratio must be positive")
+        if self.moe_precision not in ("default", "bf16"):
+            raise ValueError("moe_precision must be 'default' or 'bf16'")

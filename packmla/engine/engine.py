@@ -173,10 +173,11 @@ class Engine:
         dev = torch.device(device)
         W = weights if weights is not None else init_weights(model_cfg, rank, world, dev, seed)
         if dev.type == "cuda" and model_cfg.expert_format == "mxfp4":
-            from ..ops.moe import prepare_experts
+            from ..ops.moe import prepare_experts, prepare_experts_mx
 
-            for lw in W["layers"]:  # one-time kernel layout of the experts (canonical copy dropped)
-                prepare_experts(lw, drop_canonical=weights is None)
+            prep = prepare_experts if engine_cfg.moe_precision == "bf16" else prepare_experts_mx
+            for lw in W["layers"]:  # one-time kernel layout of the experts (canonical copies dropped)
+                prep(lw, drop_canonical=weights is None)
         max_requests = max_requests or engine_cfg.max_running_requests
         max_requests += 1  # + dummy slot for padded graph rows
         if kv_bytes is None:
@@ -189,6 +190,7 @@ class Engine:
         pages = max(cap.num_pages, 1)
         pool = KVPool(model_cfg, engine_cfg, pages, max_requests, max_context, dev)
         model = V4FlashModel(model_cfg, W, pool, comm)
+        model.moe_precision = engine_cfg.moe_precision
         eng = cls(model_cfg, engine_cfg, model, pool, comm)
         eng.capacity = cap
         return eng

@@ -80,6 +80,7 @@ class V4FlashModel:
         self.r128max = max(1, pool.max_context // abi.C128_RATIO)
         self.topk = min(cfg.index_topk, self.r4max)
         self.ar_hook = None  # optional fused projection + all-reduce (parallel.fused)
+        self.moe_precision = "default"  # MXFP8 expert activations ("bf16": BF16 activations)
         self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
 
     def _fuse_layer(self, layer: int) -> dict:
@@ -262,7 +263,8 @@ class V4FlashModel:
         g = h @ fz["w_ffn"].T
         c = fz["gate"]
         topk_ids, topk_w = fused_ops.route_topk(g[:, c:], lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
-        out = moe_ops.experts(h, topk_ids, topk_w, lw, self.expert_base, self.local_experts, cfg.expert_format)
+        out = moe_ops.experts(h, topk_ids, topk_w, lw, self.expert_base, self.local_experts, cfg.expert_format,
+                              precision=self.moe_precision)
         shared = fused_ops.silu_mul(g[:, :c]) @ lw["shared_w2"].T
         if self.comm is None or self.world == 1:
             return shared, out

@@ -128,15 +128,101 @@ def tile_fp4_frag(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torc
     return w_f, s_f
 
 
+def mx_scale_blocks(s: torch.Tensor) -> torch.Tensor:
+    """UE8M0 scales [E, R, K/32] -> tcgen05.cp source blocks [E*R/128, K/128, 32, 16] (csrc/moe_mxf4.cu).
+
+    Block (tile t, K-group g), row r holds the 4 k-block scales of rows r, 32+r, 64+r, 96+r of the tile.
+    """
+    E, R, KB = s.shape
+    x = s.reshape(E * R // 128, 4, 32, KB // 4, 4)  # tile, quadrant, row, group, k-block
+    return x.permute(0, 3, 2, 1, 4).reshape(E * R // 128, KB // 4, 32, 16).contiguous()
+
+
+def mx_scale_unblock(b: torch.Tensor, E: int) -> torch.Tensor:
+    """Inverse of mx_scale_blocks."""
+    tiles, G = b.shape[0], b.shape[1]
+    return b.reshape(tiles, G, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(E, tiles * 128 // E, G * 4)
+
+
+def prepare_experts_mx(lw: dict, drop_canonical: bool = True) -> None:
+    """Scale-factor blocks of the MXFP8-activation kernel; the packed weights are used as stored."""
+    if "sfa13" in lw:
+        return
+    lw["sfa13"] = mx_scale_blocks(lw["s13"])
+    lw["sfa2"] = mx_scale_blocks(lw["s2"])
+    if drop_canonical:
+        lw.pop("s13")
+        lw.pop("s2")
+
+
+def _scales(lw: dict, name: str) -> torch.Tensor:
+    if name in lw:
+        return lw[name]
+    w = lw["w13" if name == "s13" else "w2"]
+    return mx_scale_unblock(lw["sfa13" if name == "s13" else "sfa2"], w.shape[0])
+
+
+def mx_quant(x: torch.Tensor) -> torch.Tensor:
+    """MXFP8 round trip of x [..., K] (fp32): E4M3 values with one UE8M0 scale per 32 (kernel rule)."""
+    from ..formats import codec
+
+    shp = x.shape
+    xb = x.float().reshape(*shp[:-1], shp[-1] // 32, 32)
+    e = codec.ue8m0_exponent(xb.abs().amax(-1))
+    q = codec.e4m3_decode(codec.e4m3_encode(xb * codec.exp2_int(-e)[..., None]))
+    return (q * codec.exp2_int(e)[..., None]).reshape(shp)
+
+
+def experts_mx_reference(h, topk_ids, topk_w, lw, expert_base, local_experts):
+    """fp32 oracle of the MXFP8-activation path: quantize h, MXFP4 GEMMs, SiLU-mul, quantize, GEMM."""
+    T = h.shape[0]
+    w13, w2 = lw["w13"], lw["w2"]
+    s13, s2 = _scales(lw, "s13"), _scales(lw, "s2")
+    out = torch.zeros(T, w2.shape[1], dtype=torch.float32, device=h.device)
+    I = w13.shape[1] // 2
+    hq = mx_quant(h.float())
+    for le in range(local_experts):
+        tok, kk = torch.nonzero(topk_ids == expert_base + le, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        gu = hq[tok] @ fp4_dequant(w13[le], s13[le]).T
+        act = mx_quant(F.silu(gu[:, :I]) * gu[:, I:])
+        out.index_add_(0, tok, (act @ fp4_dequant(w2[le], s2[le]).T) * topk_w[tok, kk][:, None].float())
+    return out
+
+
+class MoEWorkspaceMX:
+    """Routing lists, chunk table and MXFP8 operand images of csrc/moe_mxf4.cu (stable pointers)."""
+
+    def __init__(self, max_tokens: int, topk: int, local_experts: int, hidden: int, inter: int, device):
+        n = max_tokens * topk
+        E = local_experts
+        rows = (n + 31 * min(E, n) + 31) // 32 * 32
+        i32 = dict(dtype=torch.int32, device=device)
+        self.offsets = torch.zeros(E + 1, **i32)
+        self.slot_token = torch.zeros(n, **i32)
+        self.slot_weight = torch.zeros(n, dtype=torch.float32, device=device)
+        self.active = torch.zeros(E + 1, **i32)
+        self.pad = torch.zeros(E + 1, **i32)
+        self.chunks = torch.zeros(n, 4, **i32)
+        self.n_chunks = torch.zeros(1, **i32)
+        u8 = dict(dtype=torch.uint8, device=device)
+        self.xq = torch.zeros(hidden // 128, rows, 128, **u8)
+        self.xs = torch.zeros(rows // 32, hidden // 128, 512, **u8)
+        self.act_q = torch.zeros(inter // 128, rows, 128, **u8)
+        self.act_s = torch.zeros(rows // 32, inter // 128, 512, **u8)
+        self.max_tokens = max_tokens
+
+
 def prepare_experts(lw: dict, drop_canonical: bool = True) -> None:
     """Add the kernel layout (w13_t, s13_t, w2_t, s2_t) to a layer's MXFP4 expert weights."""
     if "w13_f" in lw:
         return
-    lw["w13_f"], lw["s13_f"] = tile_fp4_frag(lw["w13"], lw["s13"], True)
-    lw["w2_f"], lw["s2_f"] = tile_fp4_frag(lw["w2"], lw["s2"], False)
+    lw["w13_f"], lw["s13_f"] = tile_fp4_frag(lw["w13"], _scales(lw, "s13"), True)
+    lw["w2_f"], lw["s2_f"] = tile_fp4_frag(lw["w2"], _scales(lw, "s2"), False)
     if drop_canonical:
-        for k in ("w13", "s13", "w2", "s2"):
-            lw.pop(k)
+        for k in ("w13", "s13", "w2", "s2", "sfa13", "sfa2"):
+            lw.pop(k, None)
 
 
 class MoEWorkspace:
@@ -158,26 +244,54 @@ class MoEWorkspace:
 _WS: dict = {}
 
 
-def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, workspace=None):
+def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, workspace=None,
+            precision: str = "default"):
+    """Routed experts -> fp32 [T, H] (sum over this rank's experts of w_k * expert_k(h)).
+
+    precision "default": MXFP8 activations (tcgen05 block-scaled kernel, csrc/moe_mxf4.cu);
+    "bf16": BF16 activations (csrc/moe_fp4_mma.cu).  BF16 experts (tiny configs) use PyTorch.
+    """
     if expert_format != "mxfp4":
         return experts_reference(h, topk_ids, topk_w, lw["w13"], lw["w2"], expert_base, local_experts)
+    if precision not in ("default", "bf16"):
+        raise ValueError("moe precision must be 'default' or 'bf16'")
     if not h.is_cuda:
+        if precision == "default":
+            return experts_mx_reference(h, topk_ids, topk_w, lw, expert_base, local_experts)
         # CPU: dequantize the touched experts (tests only)
         T = h.shape[0]
         out = torch.zeros(T, lw["w2"].shape[1], dtype=torch.float32)
         I = lw["w13"].shape[1] // 2
+        s13, s2 = _scales(lw, "s13"), _scales(lw, "s2")
         for le in range(local_experts):
             tok, kk = torch.nonzero(topk_ids == expert_base + le, as_tuple=True)
             if tok.numel() == 0:
                 continue
-            w13 = fp4_dequant(lw["w13"][le], lw["s13"][le])
-            w2 = fp4_dequant(lw["w2"][le], lw["s2"][le])
+            w13 = fp4_dequant(lw["w13"][le], s13[le])
+            w2 = fp4_dequant(lw["w2"][le], s2[le])
             gu = h[tok].float() @ w13.T
             act = (F.silu(gu[:, :I]) * gu[:, I:]).to(torch.bfloat16).float()
             out.index_add_(0, tok, (act @ w2.T) * topk_w[tok, kk][:, None])
         return out
     T, H = h.shape
     k = topk_ids.shape[1]
+    if precision == "default":
+        I = lw["w13"].shape[1] // 2
+        ws = workspace
+        if ws is None or not isinstance(ws, MoEWorkspaceMX):
+            key = ("mx", h.device.index, T, k, local_experts, H, I)
+            ws = _WS.get(key)
+            if ws is None:
+                ws = MoEWorkspaceMX(T, k, local_experts, H, I, h.device)
+                _WS[key] = ws
+        if "sfa13" not in lw:
+            prepare_experts_mx(lw, drop_canonical=False)
+        out = torch.empty(T, H, dtype=torch.float32, device=h.device)
+        ext().moe_mxf4(h.contiguous(), topk_ids.int().contiguous(), topk_w.float().contiguous(), expert_base,
+                       lw["w13"], lw["sfa13"], lw["w2"], lw["sfa2"], ws.offsets, ws.slot_token, ws.slot_weight,
+                       ws.active, ws.pad, ws.chunks, ws.n_chunks, ws.xq, ws.xs, ws.act_q, ws.act_s, out,
+                       error_word(h.device))
+        return out
     I = lw["w13_f"].shape[1] * 64 if "w13_f" in lw else lw["w13"].shape[1] // 2
     ws = workspace
     if ws is None:

@@ -16,19 +16,37 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm()).item()
 
 
-@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (5, 8, 2), (40, 16, 4), (3, 4, 4)])
-def test_moe_fp4_matches_dequant_reference(cuda, T, E, k):
+@pytest.mark.parametrize("precision", ["default", "bf16"])
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (5, 8, 2), (40, 16, 4), (3, 4, 4), (150, 4, 2)])
+def test_moe_fp4_matches_dequant_reference(cuda, T, E, k, precision):
+    """GPU experts vs the CPU oracle of the same precision (MXFP8 or BF16 activations); T=150 over
+    4 experts routes more than 32 tokens to an expert (several chunks, MMA N up to 32)."""
     cfg = small_gpu_config(n_routed_experts=E, moe_topk=k)
     W = init_weights(cfg, device="cpu", seed=T)
     lw = W["layers"][0]
     g = torch.Generator().manual_seed(T)
     h = torch.randn(T, cfg.hidden_size, generator=g).bfloat16()
     ids, w = moe_ops.route(h.float().bfloat16(), lw["gate"], lw["gate_bias"], k, 1.0)
-    ref = moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4")  # CPU dequant reference
+    ref = moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4", precision=precision)  # CPU oracle
     glw = {kk: v.cuda() for kk, v in lw.items()}
-    out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), glw, 0, E, "mxfp4")
+    out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), glw, 0, E, "mxfp4", precision=precision)
     check_errors(cuda)
-    assert _rel(out.cpu(), ref) < 2e-2
+    assert _rel(out.cpu(), ref) < (5e-3 if precision == "default" else 2e-2)
+
+
+def test_moe_mxfp8_activation_error_is_bounded(cuda):
+    """MXFP8 activations stay within a few percent of BF16 activations (full V4-Flash widths)."""
+    cfg = small_gpu_config(hidden_size=4096, moe_intermediate=2048, n_routed_experts=4, moe_topk=2)
+    W = init_weights(cfg, device="cpu", seed=21)
+    lw = W["layers"][0]
+    h = torch.randn(33, 4096, generator=torch.Generator().manual_seed(5)).bfloat16()
+    ids, w = moe_ops.route(h, lw["gate"], lw["gate_bias"], 2, 1.0)
+    ref_bf16 = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4", precision="bf16")
+    ref_mx = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4", precision="default")
+    out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), {k: v.cuda() for k, v in lw.items()}, 0, 4, "mxfp4")
+    check_errors(cuda)
+    assert _rel(out.cpu(), ref_mx) < 5e-3
+    assert _rel(out.cpu(), ref_bf16) < 6e-2
 
 
 def test_moe_fp4_expert_parallel_partials_sum(cuda):
@@ -46,8 +64,15 @@ def test_moe_fp4_expert_parallel_partials_sum(cuda):
     assert _rel(parts[0] + parts[1], full) < 1e-5
 
 
+@pytest.mark.parametrize("precision", ["bf16", "default"])
 @pytest.mark.parametrize("fmt", ["direct", "native"])
-def test_engine_gpu_matches_cpu_oracle(cuda, fmt):
+def test_engine_gpu_matches_cpu_oracle(cuda, fmt, precision):
+    """GPU engine vs the CPU oracle engine.
+
+    The random small model amplifies last-bit differences from layer to layer (in either precision);
+    MXFP8 activations (precision "default") add a step of about 2 % at the first expert layer, because
+    0.2 % input differences flip E4M3 roundings.  So the MXFP8 comparison covers the first prefill only;
+    the kernel's MXFP8 numerics on identical inputs are pinned by the MoE tests above."""
     cfg = small_gpu_config()
     W = init_weights(cfg, device="cpu", seed=3)
     Wg = {"layers": [{k: v.cuda() for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
@@ -57,7 +82,7 @@ def test_engine_gpu_matches_cpu_oracle(cuda, fmt):
     res = {}
     for dev, weights in (("cpu", W), ("cuda", Wg)):
         ecfg = EngineConfig(kv_cache_format=fmt, device=dev, max_running_requests=2, cuda_graph_bs=[1, 2],
-                            chunked_prefill_size=128, disable_cuda_graph=True)
+                            chunked_prefill_size=128, disable_cuda_graph=True, moe_precision=precision)
         eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
         slot = eng.pool.admit(400)
         l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
@@ -65,8 +90,9 @@ def test_engine_gpu_matches_cpu_oracle(cuda, fmt):
         l3 = eng.model.decode(prompt[:1].to(dev), torch.tensor([300], device=dev), torch.tensor([slot], device=dev))
         res[dev] = (l1.cpu(), l2.cpu(), l3[0].cpu())
     check_errors(cuda)
-    for a, b in zip(res["cuda"], res["cpu"]):
-        assert _rel(a, b) < 3e-2
+    pairs = list(zip(res["cuda"], res["cpu"]))
+    for a, b in (pairs if precision == "bf16" else pairs[:1]):
+        assert _rel(a, b) < (3e-2 if precision == "bf16" else 6e-2)
 
 
 def test_decode_graph_replay_matches_eager(cuda):
@@ -109,7 +135,7 @@ def test_moe_fp4_tcgen05_kernel_matches_reference(cuda):
     lw = W["layers"][0]
     h = torch.randn(7, 4096, generator=torch.Generator().manual_seed(3)).bfloat16()
     ids, w = moe_ops.route(h, lw["gate"], lw["gate_bias"], 2, 1.0)
-    ref = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4")
+    ref = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4", precision="bf16")
     w13t, s13t = moe_ops.tile_fp4(lw["w13"], lw["s13"], True)
     w2t, s2t = moe_ops.tile_fp4(lw["w2"], lw["s2"], False)
     ws = moe_ops.MoEWorkspace(7, 2, 4, 2048, cuda, hidden=4096)
