@@ -70,7 +70,8 @@ void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, c
 void launch_index_topk(const float* scores, int64_t stride, int B, int R, int k, const int32_t* phys,
                        int64_t phys_stride, int ratio, int32_t* out_slots, int32_t* out_pos, cudaStream_t stream);
 
-void launch_tc_latency_probe(int iters, int n_mma, int n, int n_acc, long long* out, int* err, cudaStream_t stream);
+void launch_tc_latency_probe(int iters, int n_mma, int n, int n_acc, int kind, long long* out, int* err,
+                             cudaStream_t stream);
 
 void launch_moe_gather_slots(const __nv_bfloat16* x, int K, const int32_t* offsets, const int32_t* pad,
                              const int32_t* slot_token, int E, __half* xs, int num_sms, cudaStream_t stream);
@@ -94,6 +95,8 @@ void launch_bs_probe(const uint8_t* a_img, const uint8_t* b_img, const uint32_t*
                      cudaStream_t stream);
 int make_tmap_fp4_unpacked(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
                            uint32_t box_rows);
+int make_tmap_fp4_unpacked_nd(void* out, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                              const uint32_t* box);
 int launch_bs_probe2(const uint8_t* a_packed, const uint8_t* b_img, const uint8_t* sfa_src, const uint8_t* sfb_src,
                      int N, int k_steps, uint32_t expect_tx, float* d, uint8_t* a_dump, int* err,
                      cudaStream_t stream);
@@ -103,16 +106,16 @@ void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T
                              int4* chunks, int32_t* n_chunks, cudaStream_t stream);
 
 // MXFP4 experts x MXFP8 activations (csrc/moe_mxf4.cu).  Workspace images: xq [H/128, rows, 128],
-// xs [rows/32, H/128, 512], act_q [I/128, rows, 128], act_s [rows/32, I/128, 512] (rows % 32 == 0).
+// xs [rows, H/32], act_q [I/128, rows, 128], act_s [rows, I/32] (rows % 32 == 0).
 struct MoeMxArgs {
   const __nv_bfloat16* h;
   int T, H, I, k, E, expert_base, rows_total, num_sms;
   const int32_t* topk_ids;
   const float* topk_w;
   const uint8_t* w13;    // [E, 2I, H/2] packed E2M1
-  const uint8_t* sfa13;  // [E*2I/128, H/128, 512] scale-factor blocks
+  const uint8_t* sfw13;  // [E*I/128, H/128, 256 (gate 128 | up 128 rows), 4] UE8M0 weight-scale image
   const uint8_t* w2;     // [E, H, I/2]
-  const uint8_t* sfa2;   // [E*H/128, I/128, 512]
+  const uint8_t* sfw2;   // [E*H/256, I/128, 256, 4]
   int32_t* offsets;
   int32_t* slot_token;
   float* slot_weight;
@@ -126,5 +129,11 @@ struct MoeMxArgs {
   uint8_t* act_s;
   float* out;  // [T, H] fp32 (zeroed by the kernel)
   int* err;
+  // optional per-launch counters (SM cycles summed over CTAs): [0] producer waiting for a free stage,
+  // [1] MMA issuer waiting for data, [2] MMA issuer waiting for a free accumulator, [3] epilogue
+  // waiting for an accumulator, [4] producer lifetime, [5] MMA issuer waiting for weight scales,
+  // [6] MMA issuer issuing (fence + MMAs + commit); gate/up at [0..7], down at [8..15]
+  unsigned long long* prof;
+  int debug;  // timing experiments only (PACKMLA_KERNEL_DEBUG), results invalid when set
 };
 int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream);

@@ -48,8 +48,8 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
       cur[e] = acc;
       if (pad) pad[e] = pacc;  // padded rows: each expert's list starts on a multiple of `align`
       if (cnt[e] > 0) active[1 + na++] = e;
-      if (chunks)  // chunk table: {expert, first padded row, tokens (<= 32), first slot}
-        for (int c = 0; c < cnt[e]; c += 32) chunks[nc++] = make_int4(e, pacc + c, min(32, cnt[e] - c), acc + c);
+      if (chunks)  // chunk table: {expert, first padded row, tokens (<= 16), first slot}
+        for (int c = 0; c < cnt[e]; c += 16) chunks[nc++] = make_int4(e, pacc + c, min(16, cnt[e] - c), acc + c);
       acc += cnt[e];
       pacc += (cnt[e] + align - 1) / align * align;
     }
@@ -83,6 +83,90 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
       slot_token[b + 1] = t;
       slot_weight[b + 1] = ww;
     }
+  }
+}
+
+// Block-wide exclusive scan of one int4 per thread (blockDim.x == 1024); returns the prefix and
+// writes the totals to *total (all threads).
+__device__ __forceinline__ int4 block_scan4(int4 v, int4* warp_tot, int4* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int4 inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, inc.x, o), b = __shfl_up_sync(0xffffffffu, inc.y, o);
+    const int c = __shfl_up_sync(0xffffffffu, inc.z, o), d = __shfl_up_sync(0xffffffffu, inc.w, o);
+    if (lane >= o) { inc.x += a; inc.y += b; inc.z += c; inc.w += d; }
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int4 t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, t.x, o), b = __shfl_up_sync(0xffffffffu, t.y, o);
+      const int c = __shfl_up_sync(0xffffffffu, t.z, o), d = __shfl_up_sync(0xffffffffu, t.w, o);
+      if (lane >= o) { t.x += a; t.y += b; t.z += c; t.w += d; }
+    }
+    warp_tot[lane] = t;  // inclusive over warps
+    if (lane == 31) *total = t;
+  }
+  __syncthreads();
+  const int4 before = warp == 0 ? make_int4(0, 0, 0, 0) : warp_tot[warp - 1];
+  return make_int4(before.x + inc.x - v.x, before.y + inc.y - v.y, before.z + inc.z - v.z, before.w + inc.w - v.w);
+}
+
+// Routing for up to 4096 slots and 1024 local experts, all in shared memory: the slot order inside an
+// expert is the slot index order (token-major), found by counting earlier slots of the same expert,
+// so the result is deterministic without a sort.  Writes the same lists as moe_route_kernel.
+__global__ void __launch_bounds__(1024) moe_route_smem_kernel(const int32_t* __restrict__ ids,
+                                                              const float* __restrict__ w, int n, int k, int base,
+                                                              int E, int32_t* __restrict__ offsets,
+                                                              int32_t* __restrict__ slot_token,
+                                                              float* __restrict__ slot_weight,
+                                                              int32_t* __restrict__ active, int32_t* __restrict__ pad,
+                                                              int align, int4* __restrict__ chunks,
+                                                              int32_t* __restrict__ n_chunks) {
+  __shared__ int s_e[4096];
+  __shared__ int cnt[1024];
+  __shared__ int start[1024];
+  __shared__ int4 warp_tot[32];
+  __shared__ int4 total;
+  const int tid = threadIdx.x;
+  if (tid < 1024) cnt[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) {
+    const int e = ids[i] - base;
+    const int le = (e >= 0 && e < E) ? e : -1;
+    s_e[i] = le;
+    if (le >= 0) atomicAdd(&cnt[le], 1);
+  }
+  __syncthreads();
+  const int c = tid < E ? cnt[tid] : 0;
+  const int4 pre = block_scan4(make_int4(c, (c + align - 1) / align * align, (c + 15) / 16, c > 0 ? 1 : 0), warp_tot,
+                               &total);
+  if (tid < E) {
+    offsets[tid] = pre.x;
+    start[tid] = pre.x;
+    if (pad) pad[tid] = pre.y;
+    if (c > 0) active[1 + pre.w] = tid;
+    if (chunks)
+      for (int q = 0; q < c; q += 16) chunks[pre.z + q / 16] = make_int4(tid, pre.y + q, min(16, c - q), pre.x + q);
+  }
+  if (tid == 0) {
+    offsets[E] = total.x;
+    if (pad) pad[E] = total.y;
+    if (n_chunks) n_chunks[0] = total.z;
+    active[0] = total.w;
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) {
+    const int e = s_e[i];
+    if (e < 0) continue;
+    int r = 0;
+    for (int j = 0; j < i; ++j) r += (s_e[j] == e);
+    const int p = start[e] + r;
+    slot_token[p] = i / k;
+    slot_weight[p] = w[i];
   }
 }
 
@@ -315,6 +399,11 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
 void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
                              int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
                              int4* chunks, int32_t* n_chunks, cudaStream_t stream) {
+  if (T * k <= 4096 && E <= 1024) {
+    moe_route_smem_kernel<<<1, 1024, 0, stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets, slot_token,
+                                                  slot_weight, active, pad, 32, chunks, n_chunks);
+    return;
+  }
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,
                                                            slot_token, slot_weight, active, pad, 32, chunks, n_chunks);
 }

@@ -37,3 +37,22 @@ int make_tmap_fp4_unpacked(void* out, const void* base, uint64_t k_elems, uint64
                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
+
+// General tiled map of packed FP4 (K innermost, `rank` <= 5 dims, strides in bytes for dims 1..rank-1)
+// with the same unpacking / swizzle; box[0] must be 128.
+int make_tmap_fp4_unpacked_nd(void* out, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                              const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i) st[i - 1] = strides[i - 1];
+  }
+  return (int)fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (cuuint32_t)rank,
+                 const_cast<void*>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}

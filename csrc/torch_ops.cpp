@@ -255,16 +255,20 @@ void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, i
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-int64_t tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, int64_t n_acc, torch::Tensor err) {
+// Returns (cycles per iteration, cycles spent issuing per iteration).
+std::vector<int64_t> tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, int64_t n_acc, torch::Tensor err,
+                                      int64_t kind) {
   check_err(err);
-  TORCH_CHECK(n == 16 || n == 32 || n == 64 || n == 128 || n == 256, "n in {16,32,64,128,256}");
-  TORCH_CHECK(n_acc >= 1 && n_acc * n <= 256, "n_acc accumulators of n columns must fit 256 columns");
+  TORCH_CHECK(n_acc >= 1, "n_acc >= 1");
   const c10::cuda::CUDAGuard g(err.device());
-  auto out = torch::zeros({1}, err.options().dtype(torch::kInt64));
-  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, (int)n_acc, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+  auto out = torch::zeros({2}, err.options().dtype(torch::kInt64));
+  TORCH_CHECK(kind >= 0 && kind <= 5 && n_acc * n <= 448 && n % 8 == 0 && n >= 8 && n <= 256);
+  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, (int)n_acc, (int)kind,
+                          reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
                           err.data_ptr<int>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return out.item<int64_t>();
+  auto h = out.cpu();
+  return {h[0].item<int64_t>(), h[1].item<int64_t>()};
 }
 
 void index_key_store(torch::Tensor kraw, torch::Tensor slots, torch::Tensor keys, torch::Tensor kscales,
@@ -486,12 +490,13 @@ std::vector<torch::Tensor> bs_probe2(torch::Tensor a_packed, torch::Tensor b_img
 
 // MXFP4 experts with MXFP8 activations: route + quantize + gate/up + down (4 launches).
 void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base, torch::Tensor w13,
-              torch::Tensor sfa13, torch::Tensor w2, torch::Tensor sfa2, torch::Tensor offsets, torch::Tensor slot_token,
+              torch::Tensor sfw13, torch::Tensor w2, torch::Tensor sfw2, torch::Tensor offsets, torch::Tensor slot_token,
               torch::Tensor slot_weight, torch::Tensor active, torch::Tensor pad, torch::Tensor chunks,
               torch::Tensor n_chunks, torch::Tensor xq, torch::Tensor xs, torch::Tensor act_q, torch::Tensor act_s,
-              torch::Tensor out, torch::Tensor err) {
+              torch::Tensor out, torch::Tensor err, c10::optional<torch::Tensor> prof) {
   TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
   const int T = h.size(0), H = h.size(1);
+  if (prof) TORCH_CHECK(prof->scalar_type() == torch::kInt64 && prof->is_contiguous() && prof->numel() >= 16);
   TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.is_contiguous() && topk_ids.size(0) == T);
   const int k = topk_ids.size(1);
   TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() && topk_w.numel() == (int64_t)T * k);
@@ -500,15 +505,16 @@ void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int
   TORCH_CHECK(H % 512 == 0 && I % 512 == 0 && H <= 4096 && I <= 4096, "moe_mxf4: H, I multiples of 512, <= 4096");
   TORCH_CHECK(w2.scalar_type() == torch::kUInt8 && w2.is_contiguous() && w2.size(0) == E && w2.size(1) == H &&
               w2.size(2) * 2 == I);
-  TORCH_CHECK(sfa13.is_contiguous() && sfa13.numel() == (int64_t)E * 2 * I / 128 * (H / 128) * 512);
-  TORCH_CHECK(sfa2.is_contiguous() && sfa2.numel() == (int64_t)E * H / 128 * (I / 128) * 512);
+  TORCH_CHECK(sfw13.scalar_type() == torch::kUInt8 && sfw13.is_contiguous() &&
+              sfw13.numel() == (int64_t)E * 2 * I * (H / 32));
+  TORCH_CHECK(sfw2.scalar_type() == torch::kUInt8 && sfw2.is_contiguous() && sfw2.numel() == (int64_t)E * H * (I / 32));
   TORCH_CHECK(reinterpret_cast<uintptr_t>(w13.data_ptr()) % 32 == 0 && reinterpret_cast<uintptr_t>(w2.data_ptr()) % 32 == 0);
   const int rows = xq.dim() == 3 ? xq.size(1) : 0;
   TORCH_CHECK(rows % 32 == 0 && rows >= T * k + 31 * std::min(E, T * k), "moe_mxf4: workspace rows too small");
   TORCH_CHECK(xq.is_contiguous() && xq.size(0) == H / 128 && xq.size(2) == 128);
   TORCH_CHECK(act_q.is_contiguous() && act_q.dim() == 3 && act_q.size(0) == I / 128 && act_q.size(1) == rows);
-  TORCH_CHECK(xs.is_contiguous() && xs.numel() == (int64_t)rows * H / 8);
-  TORCH_CHECK(act_s.is_contiguous() && act_s.numel() == (int64_t)rows * I / 8);
+  TORCH_CHECK(xs.is_contiguous() && xs.numel() == (int64_t)rows * H / 32);
+  TORCH_CHECK(act_s.is_contiguous() && act_s.numel() == (int64_t)rows * I / 32);
   TORCH_CHECK(offsets.numel() >= E + 1 && pad.numel() >= E + 1 && active.numel() >= E + 1);
   TORCH_CHECK(slot_token.numel() >= (int64_t)T * k && slot_weight.numel() >= (int64_t)T * k);
   TORCH_CHECK(chunks.scalar_type() == torch::kInt32 && chunks.is_contiguous() && chunks.numel() >= (int64_t)T * k * 4);
@@ -520,14 +526,16 @@ void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int
   a.T = T; a.H = H; a.I = I; a.k = k; a.E = E; a.expert_base = (int)expert_base; a.rows_total = rows;
   a.num_sms = num_sms_of(h.device());
   a.topk_ids = topk_ids.data_ptr<int32_t>(); a.topk_w = topk_w.data_ptr<float>();
-  a.w13 = w13.data_ptr<uint8_t>(); a.sfa13 = sfa13.data_ptr<uint8_t>();
-  a.w2 = w2.data_ptr<uint8_t>(); a.sfa2 = sfa2.data_ptr<uint8_t>();
+  a.w13 = w13.data_ptr<uint8_t>(); a.sfw13 = sfw13.data_ptr<uint8_t>();
+  a.w2 = w2.data_ptr<uint8_t>(); a.sfw2 = sfw2.data_ptr<uint8_t>();
   a.offsets = offsets.data_ptr<int32_t>(); a.slot_token = slot_token.data_ptr<int32_t>();
   a.slot_weight = slot_weight.data_ptr<float>(); a.active = active.data_ptr<int32_t>(); a.pad = pad.data_ptr<int32_t>();
   a.chunks = reinterpret_cast<int4*>(chunks.data_ptr<int32_t>()); a.n_chunks = n_chunks.data_ptr<int32_t>();
   a.xq = xq.data_ptr<uint8_t>(); a.xs = xs.data_ptr<uint8_t>();
   a.act_q = act_q.data_ptr<uint8_t>(); a.act_s = act_s.data_ptr<uint8_t>();
   a.out = out.data_ptr<float>(); a.err = err.data_ptr<int>();
+  a.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
+  a.debug = debug_flags();
   const int rc = launch_moe_mxf4(a, stream());
   TORCH_CHECK(rc == 0, "moe_mxf4 launch failed: ", rc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -538,7 +546,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
   m.def("packed_store", &packed_store, "FP32 rows -> Packed 328 B C4 records (planes)");
   m.def("umma_probe", &umma_probe, "tcgen05 operand-layout self-test (one MMA)");
-  m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)");
+  m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)", py::arg("iters"),
+        py::arg("n_mma"), py::arg("n"), py::arg("n_acc"), py::arg("err"), py::arg("kind") = 0);
   m.def("index_key_store", &index_key_store, "FP8 index keys (swizzled rows) + fp32 scales");
   m.def("index_select", &index_select, "FP8 tcgen05 indexer logits + radix top-k");
   m.def("bs_probe2", &bs_probe2, "TMA FP4 + tcgen05.cp scale-factor pipeline self-test");
@@ -548,7 +557,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comp_pool", &comp_pool, "compressor online-softmax pooling of one token per row");
   m.def("route_topk", &route_topk, "sigmoid top-k MoE routing");
   m.def("silu_mul", &silu_mul, "silu(gate) * up");
-  m.def("moe_mxf4", &moe_mxf4, "MXFP4 experts x MXFP8 activations (tcgen05 block-scaled)");
+  m.def("moe_mxf4", &moe_mxf4, "MXFP4 experts x MXFP8 activations (tcgen05 block-scaled)", py::arg("h"),
+        py::arg("topk_ids"), py::arg("topk_w"), py::arg("expert_base"), py::arg("w13"), py::arg("sfw13"), py::arg("w2"),
+        py::arg("sfw2"), py::arg("offsets"), py::arg("slot_token"), py::arg("slot_weight"), py::arg("active"),
+        py::arg("pad"), py::arg("chunks"), py::arg("n_chunks"), py::arg("xq"), py::arg("xs"), py::arg("act_q"),
+        py::arg("act_s"), py::arg("out"), py::arg("err"), py::arg("prof") = py::none());
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");

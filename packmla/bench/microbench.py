@@ -38,11 +38,22 @@ class L2Flush:
         self.buf.fill_(1)
 
 
-def time_op(fn, rounds: int, warmup: int, device, flush: L2Flush | None) -> float:
-    """Mean microseconds over `rounds` (each round timed alone, L2 flushed before it)."""
+def time_op(fn, rounds: int, warmup: int, device, flush: L2Flush | None, graph: bool = False) -> float:
+    """Mean microseconds over `rounds` (each round timed alone, L2 flushed before it).
+
+    graph=True captures fn once in a CUDA graph and times its replays, so the host-side launch work
+    (argument checks, tensor-map encoding) stays out of the measurement, as in the engine's decode graphs.
+    """
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(device)
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        fn = g.replay
+        fn()
+        torch.cuda.synchronize(device)
     total = 0.0
     for _ in range(rounds):
         if flush is not None:
@@ -77,13 +88,24 @@ def bench_moe(args, dev):
     ids, w = moe_ops.route(h, gate, torch.zeros(E, device=dev), k, 1.0)
     active = int(torch.unique(ids).numel())
     fn = lambda: moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4", precision=args.precision)  # noqa: E731
-    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev))
+    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev), graph=True)
     check_errors(dev)
+    waits = None
+    if args.precision == "default" and args.prof:
+        prof = torch.zeros(16, dtype=torch.int64, device=dev)
+        moe_ops.experts(h, ids, w, lw, 0, E, "mxfp4", precision="default", prof=prof)
+        torch.cuda.synchronize(dev)
+        pv = prof.tolist()
+        names = ["producer_wait_stage", "mma_wait_data", "mma_wait_accum", "epilogue_wait_accum", "producer_life",
+                 "mma_wait_scales", "mma_issue", "producer_issue"]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        waits = {f"{tag}_{n}_kcycles_per_cta": round(pv[o + i] / 1e3 / sms, 1)
+                 for o, tag in ((0, "gateup"), (8, "down")) for i, n in enumerate(names)}
     per_expert = (2 * I * H + H * I) // 2 + (2 * I * H + H * I) // 32
     nbytes = active * per_expert
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
-    return {"case": "moe_fp4", "precision": args.precision, "tokens": args.tokens, "experts": E, "topk": k, "active_experts": active,
+    return {"case": "moe_fp4", "precision": args.precision, "waits": waits, "tokens": args.tokens, "experts": E, "topk": k, "active_experts": active,
             "us": round(us, 2), "weight_bytes": nbytes, "GBps": round(gbs, 1),
             "hbm_fraction": round(gbs / peak, 3), "peak_note": tag}
 
@@ -186,6 +208,7 @@ def main():
     ap.add_argument("--rounds", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--precision", default="default", choices=["default", "bf16"])
+    ap.add_argument("--prof", action="store_true", help="MoE: report per-role wait times of the expert kernel")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     if args.case == "moe":

@@ -128,28 +128,36 @@ def tile_fp4_frag(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torc
     return w_f, s_f
 
 
-def mx_scale_blocks(s: torch.Tensor) -> torch.Tensor:
-    """UE8M0 scales [E, R, K/32] -> tcgen05.cp source blocks [E*R/128, K/128, 32, 16] (csrc/moe_mxf4.cu).
-
-    Block (tile t, K-group g), row r holds the 4 k-block scales of rows r, 32+r, 64+r, 96+r of the tile.
-    """
+def mx_weight_scales(s: torch.Tensor, gate_up: bool) -> torch.Tensor:
+    """UE8M0 scales [E, R, K/32] -> [units, K/128, 256, 4] (csrc/moe_mxf4.cu): per unit's 256 weight rows
+    (gate/up: the 128 gate rows of intermediate block j, then the matching 128 up rows; down: output
+    rows 256 j .. 256 j + 255) and K-group, the 4 k-block scales of each row, rows contiguous."""
     E, R, KB = s.shape
-    x = s.reshape(E * R // 128, 4, 32, KB // 4, 4)  # tile, quadrant, row, group, k-block
-    return x.permute(0, 3, 2, 1, 4).reshape(E * R // 128, KB // 4, 32, 16).contiguous()
+    G = KB // 4
+    if gate_up:
+        I = R // 2
+        x = s.reshape(E, 2, I // 128, 128, G, 4).permute(0, 2, 4, 1, 3, 5)  # E, j, g, tile, row, 4
+    else:
+        x = s.reshape(E, R // 256, 256, G, 4).permute(0, 1, 3, 2, 4)  # E, j, g, row, 4
+    return x.reshape(-1, G, 256, 4).contiguous()
 
 
-def mx_scale_unblock(b: torch.Tensor, E: int) -> torch.Tensor:
-    """Inverse of mx_scale_blocks."""
-    tiles, G = b.shape[0], b.shape[1]
-    return b.reshape(tiles, G, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(E, tiles * 128 // E, G * 4)
+def mx_weight_scales_inverse(img: torch.Tensor, E: int, gate_up: bool) -> torch.Tensor:
+    units, G = img.shape[0], img.shape[1]
+    J = units // E
+    if gate_up:
+        x = img.reshape(E, J, G, 2, 128, 4).permute(0, 3, 1, 4, 2, 5)  # E, tile, j, row, g, 4
+        return x.reshape(E, 2 * J * 128, G * 4)
+    x = img.reshape(E, J, G, 256, 4).permute(0, 1, 3, 2, 4)
+    return x.reshape(E, J * 256, G * 4)
 
 
 def prepare_experts_mx(lw: dict, drop_canonical: bool = True) -> None:
-    """Scale-factor blocks of the MXFP8-activation kernel; the packed weights are used as stored."""
-    if "sfa13" in lw:
+    """Weight-scale images of the MXFP8-activation kernel; the packed weights are streamed as stored."""
+    if "sfw13" in lw:
         return
-    lw["sfa13"] = mx_scale_blocks(lw["s13"])
-    lw["sfa2"] = mx_scale_blocks(lw["s2"])
+    lw["sfw13"] = mx_weight_scales(lw["s13"], True)
+    lw["sfw2"] = mx_weight_scales(lw["s2"], False)
     if drop_canonical:
         lw.pop("s13")
         lw.pop("s2")
@@ -159,7 +167,7 @@ def _scales(lw: dict, name: str) -> torch.Tensor:
     if name in lw:
         return lw[name]
     w = lw["w13" if name == "s13" else "w2"]
-    return mx_scale_unblock(lw["sfa13" if name == "s13" else "sfa2"], w.shape[0])
+    return mx_weight_scales_inverse(lw["sfw13" if name == "s13" else "sfw2"], w.shape[0], name == "s13")
 
 
 def mx_quant(x: torch.Tensor) -> torch.Tensor:
@@ -208,9 +216,9 @@ class MoEWorkspaceMX:
         self.n_chunks = torch.zeros(1, **i32)
         u8 = dict(dtype=torch.uint8, device=device)
         self.xq = torch.zeros(hidden // 128, rows, 128, **u8)
-        self.xs = torch.zeros(rows // 32, hidden // 128, 512, **u8)
+        self.xs = torch.zeros(rows, hidden // 32, **u8)
         self.act_q = torch.zeros(inter // 128, rows, 128, **u8)
-        self.act_s = torch.zeros(rows // 32, inter // 128, 512, **u8)
+        self.act_s = torch.zeros(rows, inter // 32, **u8)
         self.max_tokens = max_tokens
 
 
@@ -221,7 +229,7 @@ def prepare_experts(lw: dict, drop_canonical: bool = True) -> None:
     lw["w13_f"], lw["s13_f"] = tile_fp4_frag(lw["w13"], _scales(lw, "s13"), True)
     lw["w2_f"], lw["s2_f"] = tile_fp4_frag(lw["w2"], _scales(lw, "s2"), False)
     if drop_canonical:
-        for k in ("w13", "s13", "w2", "s2", "sfa13", "sfa2"):
+        for k in ("w13", "s13", "w2", "s2", "sfw13", "sfw2"):
             lw.pop(k, None)
 
 
@@ -245,7 +253,7 @@ _WS: dict = {}
 
 
 def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, workspace=None,
-            precision: str = "default"):
+            precision: str = "default", prof: torch.Tensor | None = None):
     """Routed experts -> fp32 [T, H] (sum over this rank's experts of w_k * expert_k(h)).
 
     precision "default": MXFP8 activations (tcgen05 block-scaled kernel, csrc/moe_mxf4.cu);
@@ -284,13 +292,13 @@ def experts(h, topk_ids, topk_w, lw, expert_base, local_experts, expert_format, 
             if ws is None:
                 ws = MoEWorkspaceMX(T, k, local_experts, H, I, h.device)
                 _WS[key] = ws
-        if "sfa13" not in lw:
+        if "sfw13" not in lw:
             prepare_experts_mx(lw, drop_canonical=False)
         out = torch.empty(T, H, dtype=torch.float32, device=h.device)
         ext().moe_mxf4(h.contiguous(), topk_ids.int().contiguous(), topk_w.float().contiguous(), expert_base,
-                       lw["w13"], lw["sfa13"], lw["w2"], lw["sfa2"], ws.offsets, ws.slot_token, ws.slot_weight,
+                       lw["w13"], lw["sfw13"], lw["w2"], lw["sfw2"], ws.offsets, ws.slot_token, ws.slot_weight,
                        ws.active, ws.pad, ws.chunks, ws.n_chunks, ws.xq, ws.xs, ws.act_q, ws.act_s, out,
-                       error_word(h.device))
+                       error_word(h.device), prof)
         return out
     I = lw["w13_f"].shape[1] * 64 if "w13_f" in lw else lw["w13"].shape[1] // 2
     ws = workspace

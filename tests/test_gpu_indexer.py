@@ -61,6 +61,6 @@ def test_tcgen05_handshake_latency_probe(cuda):
     lat = {}
     for n_mma, n, acc in ((0, 64, 1), (1, 16, 1), (16, 16, 1), (16, 16, 4), (16, 16, 8), (16, 64, 1), (16, 64, 4),
                           (16, 256, 1), (32, 64, 1)):
-        lat[(n_mma, n, acc)] = ext().tc_latency_probe(200, n_mma, n, acc, err)
+        lat[(n_mma, n, acc)] = ext().tc_latency_probe(200, n_mma, n, acc, err)[0]
     assert err.cpu()[0] == 0
     print("tcgen05 cycles per (n_mma, N, accumulators) round trip:", lat)
