@@ -8,7 +8,12 @@
 // Design (sm_100a): one CTA = (query b, group of 64 heads, KV split).  Per tile of 128 KV rows:
 //   1. 8 warps gather the rows (Native 584 B or Packed 328 B) and expand them into a dense BF16
 //      tile [128 x 512] in shared memory, 128-byte swizzled (Packed: bitmap POPC prefix,
-//      E4M3 x UE8M0 dequant, BF16 round, tail RoPE with the record position).
+//      E4M3 x UE8M0 dequant, BF16 round, tail RoPE with the record position).  A warp takes 4 rows
+//      per step with 8 lanes per row: the lanes copy the raw record (and a Packed row's RoPE
+//      table row) into the warp's staging, then each lane expands one 64-coordinate word (one
+//      UE8M0 scale tile) 8 coordinates at a time: the unit's kept bytes are placed with one byte
+//      permute from a mask-indexed table; the next step's record loads are in flight meanwhile.
+//      A query's rows are split over the CTAs of its splits in whole tiles, as evenly as possible.
 //   2. one thread issues S^T = K Q^T   (tcgen05.mma kind::f16, M=128 rows, N=64 heads, K=512)
 //      into TMEM columns [256, 320).
 //   3. 8 warps read S^T with tcgen05.ld, do the online softmax per head (column reductions by
@@ -37,16 +42,21 @@ constexpr float kRescaleThreshold = 8.0f;
 constexpr int kQBytes = kHG * kD * 2;        // 65536
 constexpr int kKVBytes = kTile * kD * 2;     // 131072
 constexpr int kPBytes = kTile * kHG * 2;     // 16384
-constexpr int kStageBytes = 592;             // per-warp raw row staging
+constexpr int kStageRow = 592;               // raw row staging: record (<= 584 B) or packed + RoPE row
+constexpr int kStageBytes = 4 * kStageRow;   // per warp: 4 rows
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kQBytes;
 constexpr int kOffP = kOffKV + kKVBytes;
-constexpr int kOffStage = kOffP + kPBytes;
-constexpr int kOffRed = kOffStage + 8 * kStageBytes;  // float red[8][32]
+// the gather staging is live only during a tile's gather, P only from its softmax to its P.V MMA
+// (complete before the next gather starts): the two share one region
+constexpr int kOffStage = kOffP;
+constexpr int kPStageBytes = kPBytes > 8 * kStageBytes ? kPBytes : 8 * kStageBytes;
+constexpr int kOffRed = kOffP + kPStageBytes;  // float red[8][32]
 constexpr int kOffHead = kOffRed + 8 * 32 * 4;          // m_used[64], l[64], alpha[64]
 constexpr int kOffMisc = kOffHead + 3 * 64 * 4;         // bars, tmem addr, flags
 constexpr int kOffRowValid = kOffMisc + 64;            // uint8 rowvalid[128]
-constexpr int kSmemBytes = kOffRowValid + 128 + 1024;   // + alignment slack
+constexpr int kOffExpand = kOffRowValid + 128;         // uint4 expand_lut[256]
+constexpr int kSmemBytes = kOffExpand + 256 * 16 + 1024;  // + alignment slack
 
 constexpr uint32_t kTmemO = 0;
 constexpr uint32_t kTmemS = 256;
@@ -66,6 +76,33 @@ __device__ __forceinline__ uint4 dequant8(uint2 codes, float s) {
     out[k] = __floats2bfloat162_rn(f.x * s, f.y * s);
   }
   return *reinterpret_cast<uint4*>(out);
+}
+
+// 8 E4M3 bytes (little-endian in codes.x, codes.y) * s -> 8 floats (exact).
+__device__ __forceinline__ void dequant8f(uint2 codes, float s, float (&f)[8]) {
+  const uint32_t w[2] = {codes.x, codes.y};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 v = __half22float2(pm::e4m3x2_to_h2((uint16_t)(w[k >> 1] >> (16 * (k & 1)))));
+    f[2 * k] = v.x * s;
+    f[2 * k + 1] = v.y * s;
+  }
+}
+
+// Byte expansion of a Packed 8-coordinate unit with kept-mask m: the unit's kept values are the 8
+// bytes starting at its rank (lo, hi); entry m = {selector of coords 0-3, selector of coords 4-7,
+// mask 0-3, mask 4-7} for __byte_perm, so codes = perm(lo, hi, sel) & mask (E4M3 zero = 0x00).
+__device__ __forceinline__ uint4 expand_lut_entry(int m) {
+  uint32_t sel[2] = {0, 0}, msk[2] = {0, 0};
+  int r = 0;
+  for (int i = 0; i < 8; ++i) {
+    if ((m >> i) & 1) {
+      sel[i >> 2] |= (uint32_t)r << (4 * (i & 3));
+      msk[i >> 2] |= 0xFFu << (8 * (i & 3));
+      ++r;
+    }
+  }
+  return make_uint4(sel[0], sel[1], msk[0], msk[1]);
 }
 
 struct RowRef {
@@ -97,105 +134,128 @@ __device__ __forceinline__ RowRef row_ref(const DecodeParams& p, int b, int i, i
   return r;
 }
 
-// Raw bytes of one row, as two 16-byte pieces per lane:
-//   A -> stage[16 lane]       (native data units 0..31; packed values 0..15, bitmap 16..19, scales 20)
-//   B -> stage[512 + 16 lane] (native data units 32..35 for lanes 0..3, scales for lane 4)
-// Packed rows: lanes 24..31, which rotate the tail units 56..63, also prefetch their four RoPE
-// (cos, sin) pairs into A and B, so no dependent global load sits on the expansion path.
-__device__ __forceinline__ void load_row_raw(const DecodeParams& p, int kind, int slot, int pos, int lane, uint4& A,
-                                             uint4& B) {
-  A = zero4();
-  B = zero4();
-  if (kind == 1 || kind == 2) {
-    const uint8_t* pool = kind == 1 ? p.swa_pool : p.csa_pool;
-    const int64_t page = slot / kPage, rip = slot % kPage;
+// ----------------------------------------------------------------------------- tile gather
+// One gather step of a warp: rows 4 warp + j + 32 k (j = lane / 8) of the tile, lane v = lane % 8 of
+// the row.  Raw 16-byte units of the row are spread over its 8 lanes (unit v + 8 i).
+//   Native (584 B): units 0..35 = data (448 E4M3 + 128 B BF16 tail), scale row (8 B) by lane v = 0.
+//   Packed (328 B): units 0..15 values, 16..19 bitmap, scales by v = 0; the record's RoPE table row
+//   (64 floats) staged at byte 336 (a staged row is 592 bytes).
+struct StepRegs {
+  uint4 U[5];
+  uint2 sc;
+  int kind, pos;
+};
+
+__device__ __forceinline__ RowRef step_ref(const DecodeParams& p, int b, int tbase, int tvalid, int nswa, int ntot,
+                                           int r) {
+  return r < tvalid ? row_ref(p, b, tbase + r, nswa, ntot) : RowRef{0, -1, 0};
+}
+
+// Raw loads of one step from its (already resolved) row reference.
+__device__ __forceinline__ void fetch_step(const DecodeParams& p, const RowRef& rr, int v, StepRegs& R) {
+  R.kind = rr.kind;
+  R.pos = rr.pos;
+  R.sc = make_uint2(0, 0);
+#pragma unroll
+  for (int i = 0; i < 5; ++i) R.U[i] = zero4();
+  if (p.debug & 4) {  // timing experiment: expansion of an all-zero Packed row, no loads
+    R.kind = rr.kind ? 3 : 0;
+    R.sc = make_uint2(0x7f7f7f7fu, 0x7f7f7f7fu);
+    return;
+  }
+  if (rr.kind == 1 || rr.kind == 2) {
+    const uint8_t* pool = rr.kind == 1 ? p.swa_pool : p.csa_pool;
+    const int64_t page = rr.slot / kPage, rip = rr.slot % kPage;
     const uint8_t* data = pool + page * kNativePageBytes + rip * kNativeData;
-    A = *reinterpret_cast<const uint4*>(data + 16 * lane);
-    if (lane < 4) B = *reinterpret_cast<const uint4*>(data + 512 + 16 * lane);
-    if (lane == 4) {
-      const uint2 s = *reinterpret_cast<const uint2*>(pool + page * kNativePageBytes + kPage * kNativeData + rip * 8);
-      B = make_uint4(s.x, s.y, 0, 0);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const int u = v + 8 * i;
+      if (u < 36) R.U[i] = *reinterpret_cast<const uint4*>(data + 16 * u);
     }
-  } else if (kind == 3) {
-    if (lane < 16) A = *reinterpret_cast<const uint4*>(p.csa_values + (int64_t)slot * 256 + 16 * lane);
-    else if (lane < 20)
-      A = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.csa_bitmap + (int64_t)slot * 8) + 16 * (lane - 16));
-    else if (lane == 20) {
-      const uint2 s = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)slot * 8);
-      A = make_uint4(s.x, s.y, 0, 0);
-    } else if (lane >= 24) {
-      const float* f = p.freqs + (int64_t)pos * 64 + 8 * (lane - 24);
-      A = *reinterpret_cast<const uint4*>(f);
-      B = *reinterpret_cast<const uint4*>(f + 4);
-    }
+    if (v == 0) R.sc = *reinterpret_cast<const uint2*>(pool + page * kNativePageBytes + kPage * kNativeData + rip * 8);
+  } else if (rr.kind == 3) {
+    const uint4* vals = reinterpret_cast<const uint4*>(p.csa_values + (int64_t)rr.slot * 256);
+    const uint4* bits = reinterpret_cast<const uint4*>(p.csa_bitmap + (int64_t)rr.slot * 8);
+    const uint4* fq = reinterpret_cast<const uint4*>(p.freqs + (int64_t)rr.pos * 64);
+    R.U[0] = vals[v];
+    R.U[1] = vals[v + 8];
+    if (v < 4) R.U[2] = bits[v];
+    R.U[3] = fq[v];
+    R.U[4] = fq[v + 8];
+    if (v == 0) R.sc = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)rr.slot * 8);
   }
 }
 
-// Exclusive prefix of kept-coordinate counts over bitmap words: lane w (< 8) holds it for word w.
-__device__ __forceinline__ int wprefix_of(int wpre, int w) { return __shfl_sync(0xffffffffu, wpre, w); }
-
-// Warp-cooperative: staged raw row -> 64 units of 8 BF16 in the swizzled dense tile (row `trow`).
-__device__ __forceinline__ void expand_row(const DecodeParams& p, int kind, int pos, int trow, uint8_t* stage,
-                                           uint8_t* kv, int lane, const uint4& A, const uint4& B) {
-  *reinterpret_cast<uint4*>(stage + 16 * lane) = A;
-  if (lane < 5) *reinterpret_cast<uint4*>(stage + 512 + 16 * lane) = B;
-  __syncwarp();
-  int wpre = 0;
-  if (kind == 3) {
-    const int pc = lane < 8 ? __popcll(reinterpret_cast<const uint64_t*>(stage + 256)[lane]) : 0;
-    int incl = pc;
+// Stage the row, then expand word v (coordinates 64 v .. 64 v + 63) of it into tile row `trow`, one
+// 16-byte unit (8 coordinates) at a time (rolled loops keep the kernel within the instruction cache).
+__device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, uint8_t* __restrict__ srow,
+                                            uint8_t* __restrict__ kv, uint8_t* __restrict__ rowvalid,
+                                            const uint4* __restrict__ expand_lut) {
+  if (R.kind == 1 || R.kind == 2) {
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
+    for (int i = 0; i < 5; ++i) {
+      const int u = v + 8 * i;
+      if (u < 36) *reinterpret_cast<uint4*>(srow + 16 * u) = R.U[i];
     }
-    wpre = incl - pc;
+    if (v == 0) *reinterpret_cast<uint2*>(srow + 576) = R.sc;
+  } else if (R.kind == 3) {
+    *reinterpret_cast<uint4*>(srow + 16 * v) = R.U[0];
+    *reinterpret_cast<uint4*>(srow + 16 * (v + 8)) = R.U[1];
+    if (v < 4) *reinterpret_cast<uint4*>(srow + 256 + 16 * v) = R.U[2];
+    if (v == 0) *reinterpret_cast<uint2*>(srow + 320) = R.sc;
+    *reinterpret_cast<uint4*>(srow + 336 + 16 * v) = R.U[3];
+    *reinterpret_cast<uint4*>(srow + 336 + 16 * (v + 8)) = R.U[4];
   }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int u = lane + 32 * h;
-    uint4 outv = zero4();
-    if (kind == 1 || kind == 2) {
-      if (u < 56) {
-        const uint2 codes = *reinterpret_cast<const uint2*>(stage + 8 * u);
-        const int e = (int)stage[576 + (u >> 3)] - 127;
-        outv = dequant8(codes, pm::exp2i(e));
-      } else {
-        outv = *reinterpret_cast<const uint4*>(stage + 448 + 16 * (u - 56));
-      }
-    } else if (kind == 3) {
-      const uint64_t* words = reinterpret_cast<const uint64_t*>(stage + 256);
-      const int w = u >> 3, shift = 8 * (u & 7);
-      const uint64_t word = words[w];
-      const int rank = wprefix_of(wpre, w) + __popcll(word & ((1ull << shift) - 1ull));
-      const uint32_t bits = (uint32_t)(word >> shift) & 0xFFu;
-      const float s = pm::exp2i((int)stage[320 + w] - 127);
-      float v[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int k = __popc(bits & ((1u << i) - 1u));
-        const uint16_t c = stage[min(rank + k, 255)];
-        const float f = __half2float(__low2half(pm::e4m3x2_to_h2(c))) * s;
-        v[i] = (bits >> i) & 1u ? f : 0.f;
-      }
-      if (u >= 56) {  // RoPE tail: pairs (2i, 2i+1), pair index 4 (u - 56) + i; (cos, sin) in A, B
-        const float cs[8] = {__uint_as_float(A.x), __uint_as_float(A.y), __uint_as_float(A.z), __uint_as_float(A.w),
-                             __uint_as_float(B.x), __uint_as_float(B.y), __uint_as_float(B.z), __uint_as_float(B.w)};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float c = cs[2 * i], sn = cs[2 * i + 1];
-          const float re = __bfloat162float(__float2bfloat16_rn(v[2 * i]));
-          const float im = __bfloat162float(__float2bfloat16_rn(v[2 * i + 1]));
-          v[2 * i] = __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, sn));
-          v[2 * i + 1] = __fadd_rn(__fmul_rn(re, sn), __fmul_rn(im, c));
-        }
-      }
+  __syncwarp();
+  if (v == 0) rowvalid[trow] = R.kind != 0;
+  if (R.kind == 1 || R.kind == 2) {
+    const float s = v < 7 ? pm::exp2i((int)srow[576 + v] - 127) : 1.f;
+#pragma unroll 2
+    for (int u = 0; u < 8; ++u) {
+      const uint4 o = v < 7 ? dequant8(*reinterpret_cast<const uint2*>(srow + 64 * v + 8 * u), s)
+                            : *reinterpret_cast<const uint4*>(srow + 448 + 16 * u);
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) = o;
+    }
+  } else if (R.kind == 3) {
+    const uint64_t* words = reinterpret_cast<const uint64_t*>(srow + 256);
+    int rank = 0;
+    for (int w = 0; w < v; ++w) rank += __popcll(words[w]);
+    const uint64_t word = words[v];
+    const float s = pm::exp2i((int)srow[320 + v] - 127);
+    const float* cs = reinterpret_cast<const float*>(srow + 336);
+    const bool tail = v == 7;
+    // one instruction path for all lanes (no divergence): every unit goes through the rotation, with
+    // (cos, sin) = (1, 0) outside the RoPE tail, which returns the BF16-rounded value unchanged
+#pragma unroll 2
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t bits = (uint32_t)(word >> (8 * u)) & 0xFFu;
+      // the 8 value bytes from `rank` (reads may run past the values into the staged bitmap: masked)
+      const uint32_t* vw = reinterpret_cast<const uint32_t*>(srow + (rank & ~3));
+      const uint32_t sh = 8u * (uint32_t)(rank & 3);
+      const uint32_t lo = __funnelshift_r(vw[0], vw[1], sh), hi = __funnelshift_r(vw[1], vw[2], sh);
+      const uint4 e = expand_lut[bits];
+      const uint2 codes = make_uint2(__byte_perm(lo, hi, e.x) & e.z, __byte_perm(lo, hi, e.y) & e.w);
+      rank += __popc(bits);
+      float f[8];
+      dequant8f(codes, s, f);
+      const float4 cs01 = tail ? *reinterpret_cast<const float4*>(cs + 8 * u) : make_float4(1.f, 0.f, 1.f, 0.f);
+      const float4 cs23 = tail ? *reinterpret_cast<const float4*>(cs + 8 * u + 4) : make_float4(1.f, 0.f, 1.f, 0.f);
+      const float cc[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, ss[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
       __nv_bfloat162 o2[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-      outv = *reinterpret_cast<uint4*>(o2);
+      for (int i = 0; i < 4; ++i) {  // pair index 4 u + i of the table row
+        const float re = __bfloat162float(__float2bfloat16_rn(f[2 * i]));
+        const float im = __bfloat162float(__float2bfloat16_rn(f[2 * i + 1]));
+        o2[i] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(re, cc[i]), __fmul_rn(im, ss[i])),
+                                      __fadd_rn(__fmul_rn(re, ss[i]), __fmul_rn(im, cc[i])));
+      }
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) =
+          *reinterpret_cast<uint4*>(o2);
     }
-    *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * u, kTile * 128)) = outv;
+  } else {
+#pragma unroll 2
+    for (int u = 0; u < 8; ++u)
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) = zero4();
   }
   __syncwarp();
 }
@@ -232,8 +292,22 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] rescale needed, [1] abort
   uint8_t* rowvalid = smem + kOffRowValid;
+  uint4* expand_lut = reinterpret_cast<uint4*>(smem + kOffExpand);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // optional phase counters (thread 0, ns of the GPU global timer): [0] setup, [1] gather + expand,
+  // [2] S MMA, [3] softmax, [4] O MMA (with the next tile's first gather), [5] epilogue, [6] CTAs,
+  // [7] tiles, [8] earliest CTA start, [9] latest CTA end; [16 + 2 i] CTA i's total, [17 + 2 i] gather
+  unsigned long long ph[6] = {0, 0, 0, 0, 0, 0};
+  uint64_t tp = p.prof ? pm::globaltimer_ns() : 0;
+  const uint64_t t_cta0 = tp;
+  auto mark = [&](int i) {
+    if (p.prof && tid == 0) {
+      const uint64_t t = pm::globaltimer_ns();
+      ph[i] += t - tp;
+      tp = t;
+    }
+  };
   const int unit = blockIdx.x;
   const int split = unit % p.num_splits;
   const int g = (unit / p.num_splits) % p.num_groups;
@@ -252,14 +326,24 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     flags[1] = 0;
   }
   if (tid < 64) { m_used[tid] = -INFINITY; l_sum[tid] = 0.f; alpha[tid] = 1.f; }
+  for (int m = tid; m < 256; m += kThreads) expand_lut[m] = expand_lut_entry(m);
 
-  // Q group -> shared (K-major, SW128, chunk stride 64 rows * 128 B)
-  for (int idx = tid; idx < kHG * 64; idx += kThreads) {
-    const int row = idx >> 6, u = idx & 63;
-    uint4 v = zero4();
-    if (h0 + row < p.H)
-      v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride_b + (int64_t)(h0 + row) * p.q_stride_h + 8 * u);
-    *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(row, 16 * u, kHG * 128)) = v;
+  // Q group -> shared (K-major, SW128, chunk stride 64 rows * 128 B): all 16 loads of a thread in
+  // flight before the first store
+  {
+    uint4 qv[kHG * 64 / kThreads];
+#pragma unroll
+    for (int i = 0; i < kHG * 64 / kThreads; ++i) {
+      const int idx = tid + kThreads * i, row = idx >> 6, u = idx & 63;
+      qv[i] = h0 + row < p.H ? *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_stride_b +
+                                                               (int64_t)(h0 + row) * p.q_stride_h + 8 * u)
+                             : zero4();
+    }
+#pragma unroll
+    for (int i = 0; i < kHG * 64 / kThreads; ++i) {
+      const int idx = tid + kThreads * i, row = idx >> 6, u = idx & 63;
+      *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(row, 16 * u, kHG * 128)) = qv[i];
+    }
   }
   pm::tc_fence_before();
   __syncthreads();
@@ -268,57 +352,72 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
 
   const int nswa = min(p.swa_len[b], p.swa_cap);
   const int ntot = nswa + min(p.csa_len[b], p.csa_cap);
-  const int row0 = split * p.rows_per_split;
-  const int row1 = min(ntot, row0 + p.rows_per_split);
-  const int ntiles = row1 > row0 ? (row1 - row0 + kTile - 1) / kTile : 0;
+  // this query's rows split into whole tiles of `trows` rows (128, or 64 when a small batch needs more
+  // CTAs), as evenly as the split count allows; a 64-row tile leaves MMA rows 64-127 zero and masked
+  const int trows = p.tile_rows == 64 ? 64 : kTile;
+  const int tiles_q = (ntot + trows - 1) / trows;
+  const int tiles_per_split = (tiles_q + p.num_splits - 1) / p.num_splits;
+  const int row0 = split * tiles_per_split * trows;
+  const int row1 = min(ntot, row0 + tiles_per_split * trows);
+  const int ntiles = row1 > row0 ? (row1 - row0 + trows - 1) / trows : 0;
 
+  mark(0);
   const uint32_t q_base = pm::smem_u32(sQ), kv_base = pm::smem_u32(sKV), p_base = pm::smem_u32(sP);
   const uint32_t idesc_s = pm::make_idesc_f16(128, kHG, 1, 0, 0);
   const uint32_t idesc_o = pm::make_idesc_f16(128, kHG, 1, 1, 1);
   bool ok = true;
 
-  uint8_t* stage = smem + kOffStage + warp * kStageBytes;
-  struct Batch {
-    uint4 A[8], B[8];
-    int kind[8], pos[8];
-  } bk;
-  // rows warp + 8 (8 k + j), j = 0..7, of tile tt: index lookups by lanes 0..7, then raw loads
-  auto load_batch = [&](int tt, int k) {
-    const int tb = row0 + tt * kTile;
-    const int tv = min(kTile, row1 - tb);
-    RowRef mine{0, -1, 0};
-    const int r = warp + 8 * (8 * k + (lane & 7));
-    if (lane < 8 && r < tv) mine = row_ref(p, b, tb + r, nswa, ntot);
+  uint8_t* srow = smem + kOffStage + warp * kStageBytes + (lane >> 3) * kStageRow;
+  const int v8 = lane & 7;
+  // step k of a tile: rows 4 warp + lane / 8 + 32 k
+  auto step_row = [&](int k) { return 4 * warp + (lane >> 3) + 32 * k; };
+  // row references of the 4 steps of tile tt (4 independent index loads in flight together)
+  RowRef rr[4];
+  auto resolve = [&](int tt) {
+    const int tb = row0 + tt * trows, tv = min(trows, row1 - tb);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      bk.kind[j] = __shfl_sync(0xffffffffu, mine.kind, j);
-      const int slot = __shfl_sync(0xffffffffu, mine.slot, j);
-      bk.pos[j] = __shfl_sync(0xffffffffu, mine.pos, j);
-      if (p.debug & 4) { bk.A[j] = zero4(); bk.B[j] = zero4(); }
-      else load_row_raw(p, bk.kind[j], slot, bk.pos[j], lane, bk.A[j], bk.B[j]);
-    }
+    for (int k = 0; k < 4; ++k) rr[k] = step_ref(p, b, tb, tv, nswa, ntot, step_row(k));
   };
+  // two register sets in ping-pong: a step's record loads are issued while the previous step expands,
+  // and no register copy ever waits on loads still in flight
+  StepRegs ra, rb;
 
   for (int t = 0; t < ntiles && ok; ++t) {
-    const int tbase = row0 + t * kTile;
-    const int tvalid = min(kTile, row1 - tbase);
-    // ---- 1. gather + expand 128 rows (warp w: rows w + 8 i), two batches of 8 rows; batch 0 of
-    //         this tile was loaded while the previous tile's P.V MMAs ran
-    if (t == 0) load_batch(0, 0);
-#pragma unroll 1
-    for (int k = 0; k < 2; ++k) {
-      if (k == 1) load_batch(t, 1);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = warp + 8 * (8 * k + j);
-        if (!(p.debug & 2)) expand_row(p, bk.kind[j], bk.pos[j], r, stage, sKV, lane, bk.A[j], bk.B[j]);
-        if (lane == 0) rowvalid[r] = bk.kind[j] != 0;
+    // ---- 1. gather + expand 128 rows; step 0 of this tile was fetched while the previous tile's
+    //         P.V MMAs ran
+    if (t == 0) {
+      resolve(0);
+      fetch_step(p, rr[0], v8, ra);
+    }
+    // 4 steps of 32 rows; a 64-row tile runs steps 2-3 only on its first tile (zero rows, no loads)
+    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;
+    uint64_t tg = p.prof && tid == 0 ? pm::globaltimer_ns() : 0;
+    auto sub = [&](int slot) {  // finer split of the gather for thread 0: [10] fetch, [11] expand
+      if (p.prof && tid == 0) {
+        const uint64_t tn = pm::globaltimer_ns();
+        atomicAdd(p.prof + slot, (unsigned long long)(tn - tg));
+        tg = tn;
       }
+    };
+#pragma unroll 1
+    for (int k = 0; k < nsteps; k += 2) {
+      fetch_step(p, rr[k + 1], v8, rb);
+      sub(10);
+      if (!(p.debug & 2)) expand_step(ra, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
+      else if (v8 == 0) rowvalid[step_row(k)] = ra.kind != 0;
+      sub(11);
+      if (k + 2 < nsteps) fetch_step(p, rr[k + 2], v8, ra);
+      sub(10);
+      if (!(p.debug & 2)) expand_step(rb, step_row(k + 1), v8, srow, sKV, rowvalid, expand_lut);
+      else if (v8 == 0) rowvalid[step_row(k + 1)] = rb.kind != 0;
+      sub(11);
     }
     pm::fence_proxy_async_smem();
     pm::tc_fence_before();
     __syncthreads();
     pm::tc_fence_after();
+    sub(12);  // [12] waiting for the other warps at the end of the gather
+    mark(1);
     // ---- 2. S^T = K Q^T
     if (tid == 0) {
 #pragma unroll 1
@@ -332,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     }
     if (!pm::mbar_wait(bar_s, t & 1, p.err, 1)) { flags[1] = 1; }
     pm::tc_fence_after();
+    mark(2);
     // ---- 3. softmax over rows (lanes) per head (columns)
     const int quarter = warp & 3, chalf = warp >> 2;
     const int n = 32 * quarter + lane;  // KV row within tile
@@ -422,12 +522,13 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
       l_sum[h] = l_sum[h] * alpha[h] + ts;
       if (h == 0) flags[0] = 0;
     }
+    mark(3);
     // ---- 4. O^T += V^T P^T
     if (tid == 0 && !flags[1]) {
 #pragma unroll 1
       for (int db = 0; db < 4 && !(p.debug & 1); ++db) {
 #pragma unroll 1
-        for (int k = 0; k < kTile / 16; ++k) {
+        for (int k = 0; k < trows / 16; ++k) {
           const uint64_t ad = pm::make_sdesc(kv_base + (2 * db) * (kTile * 128) + k * 2048, kTile * 128, 1024);
           const uint64_t bd = pm::make_sdesc(p_base + k * 2048, 8192, 1024);
           pm::umma_f16(tmem + kTmemO + db * kHG, ad, bd, idesc_o, (t > 0 || k > 0) ? 1u : 0u);
@@ -435,13 +536,17 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
       }
       pm::umma_commit(bar_o);
     }
-    if (t + 1 < ntiles) load_batch(t + 1, 0);  // overlaps the P.V MMAs
+    if (t + 1 < ntiles) {  // overlaps the P.V MMAs
+      resolve(t + 1);
+      fetch_step(p, rr[0], v8, ra);
+    }
     if (!flags[1]) {
       if (!pm::mbar_wait(bar_o, t & 1, p.err, 2)) flags[1] = 1;
     }
     pm::tc_fence_after();
     __syncthreads();
     ok = !flags[1];
+    mark(4);
   }
 
   // ---- epilogue: partial O (unnormalized, relative to m_used), m, l
@@ -462,6 +567,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
           if (h < p.H) p.part_o[(part * p.H + h) * kD + d] = v[i];
         }
       }
+    }
+  }
+  mark(5);
+  if (p.prof && tid == 0) {
+    for (int i = 0; i < 6; ++i) atomicAdd(p.prof + i, ph[i]);
+    atomicAdd(p.prof + 6, 1ull);
+    atomicAdd(p.prof + 7, (unsigned long long)ntiles);
+    atomicMin(p.prof + 8, (unsigned long long)t_cta0);
+    atomicMax(p.prof + 9, (unsigned long long)pm::globaltimer_ns());
+    if (blockIdx.x < 1024) {
+      p.prof[16 + 2 * blockIdx.x] = pm::globaltimer_ns() - t_cta0;
+      p.prof[17 + 2 * blockIdx.x] = ph[1];
     }
   }
   if (tid < 64 && h0 + tid < p.H) {

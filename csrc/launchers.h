@@ -16,7 +16,8 @@ void launch_packed_store(const float* raw, int64_t raw_stride, const float* weig
 struct DecodeParams {
   const __nv_bfloat16* q;  // [B, H, 512]
   int64_t q_stride_b, q_stride_h;
-  int B, H, num_groups, num_splits, rows_per_split;
+  int B, H, num_groups, num_splits, rows_per_split;  // rows_per_split: informational (the kernel splits
+                                                     // each query's own rows into whole tiles)
   // SWA (Native) rows
   const uint8_t* swa_pool;
   int64_t swa_pool_slots;
@@ -40,7 +41,10 @@ struct DecodeParams {
   float* part_o;             // [B, splits, H, 512]
   float* part_ml;            // [B, splits, H, 2]
   int* err;
-  int debug;                 // diagnostics only: bit0 skips the MMAs, bit1 skips row expansion
+  int debug;                 // diagnostics only: bit0 skips the MMAs, bit1 skips row expansion, bit2 expands
+                             // all-zero Packed rows without loading records
+  unsigned long long* prof;  // optional phase counters (ns, summed over CTAs), see attention_decode.cu
+  int tile_rows;             // KV rows per tile: 128 (default, also for 0) or 64
 };
 
 void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,

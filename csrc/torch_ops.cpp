@@ -70,8 +70,10 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
                        torch::Tensor csa_scales, torch::Tensor csa_slots, torch::Tensor csa_pos, torch::Tensor csa_len,
                        torch::Tensor freqs, torch::Tensor sink, double scale, torch::Tensor q_pos, int64_t num_splits,
                        torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse,
-                       torch::Tensor err) {
+                       torch::Tensor err, c10::optional<torch::Tensor> prof, int64_t tile_rows) {
+  TORCH_CHECK(tile_rows == 64 || tile_rows == 128, "tile_rows must be 64 or 128");
   constexpr int kHG = 64, kTile = 128;
+  if (prof) TORCH_CHECK(prof->scalar_type() == torch::kInt64 && prof->is_contiguous() && prof->numel() >= 16 + 2 * 1024);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
   TORCH_CHECK(q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
               "q rows must be 16-byte aligned");
@@ -133,6 +135,8 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.part_ml = part_ml.data_ptr<float>();
   p.err = err.data_ptr<int>();
   p.debug = debug_flags();
+  p.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
+  p.tile_rows = (int)tile_rows;
   launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -565,5 +569,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
-  m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine");
+  m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine", py::arg("q"),
+        py::arg("swa_pool"), py::arg("swa_slots"), py::arg("swa_len"), py::arg("csa_packed"), py::arg("csa_pool"),
+        py::arg("csa_values"), py::arg("csa_bitmap"), py::arg("csa_scales"), py::arg("csa_slots"), py::arg("csa_pos"),
+        py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
+        py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
+        py::arg("prof") = py::none(), py::arg("tile_rows") = 128);
 }

@@ -17,6 +17,8 @@ import json
 import math
 import os
 
+import time
+
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -38,6 +40,9 @@ class L2Flush:
         self.buf.fill_(1)
 
 
+LAST_CLOCKS: dict = {}
+
+
 def time_op(fn, rounds: int, warmup: int, device, flush: L2Flush | None, graph: bool = False) -> float:
     """Mean microseconds over `rounds` (each round timed alone, L2 flushed before it).
 
@@ -54,16 +59,26 @@ def time_op(fn, rounds: int, warmup: int, device, flush: L2Flush | None, graph: 
         fn = g.replay
         fn()
         torch.cuda.synchronize(device)
+    from .timing import ClockSampler
+
     total = 0.0
-    for _ in range(rounds):
-        if flush is not None:
-            flush()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        fn()
-        e.record()
-        torch.cuda.synchronize(device)
-        total += s.elapsed_time(e)
+    # timed rounds first; then more untimed rounds until the 200 ms clock sampler has seen the work
+    with ClockSampler(torch.device(device).index or 0) as clk:
+        t_end = time.perf_counter() + 0.8
+        n = 0
+        while n < rounds or time.perf_counter() < t_end:
+            if flush is not None:
+                flush()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            if n < rounds:
+                total += s.elapsed_time(e)
+            n += 1
+    LAST_CLOCKS.clear()
+    LAST_CLOCKS.update(clk.summary())
     return total / rounds * 1e3
 
 
@@ -116,13 +131,13 @@ def bench_decode(args, dev):
     from packmla.ops import check_errors
     from packmla.ops import kv as kv_ops
 
-    B, Hh, K, W = args.batch, args.heads, args.topk, 128
+    B, Hh, K, W = args.batch, args.heads, args.topk, args.swa
     records = args.context // abi.C4_RATIO
     g = torch.Generator(device=dev).manual_seed(0)
     freqs = kv_ops.freq_table_f32(codec.rope_table(args.context + 1024)).to(dev)
     w = torch.ones(512, device=dev)
     rows = B * records  # each query owns its own context
-    swa_rows = B * W
+    swa_rows = max(1, B * W)
     swa_pool = torch.zeros(((swa_rows + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
     kv_ops.native_store(torch.randn(swa_rows, 512, device=dev, generator=g), w, 1e-6,
                         torch.arange(swa_rows, device=dev), torch.arange(swa_rows, device=dev) % args.context, freqs,
@@ -150,25 +165,46 @@ def bench_decode(args, dev):
     sel = torch.stack([torch.randperm(records, device=dev, generator=g)[:K] for _ in range(B)])
     csa_slots = (base + sel).int().contiguous()
     csa_pos = (sel * 4).int().contiguous()
-    swa_slots = (torch.arange(B, device=dev)[:, None] * W + torch.arange(W, device=dev)[None]).int()
+    swa_slots = (torch.arange(B, device=dev)[:, None] * W + torch.arange(max(W, 1), device=dev)[None]).int()
     q = (torch.randn(B, Hh, 512, device=dev, generator=g) / 2).bfloat16()
     args_d = dict(swa_slots=swa_slots, swa_len=torch.full((B,), W, dtype=torch.int32, device=dev),
                   csa_slots=csa_slots, csa_pos=csa_pos, csa_len=torch.full((B,), K, dtype=torch.int32, device=dev),
                   freqs=freqs, sink=torch.zeros(Hh, device=dev), scale=512 ** -0.5,
                   q_pos=torch.full((B,), args.context - 1, dtype=torch.int32, device=dev), csa_pool=pool,
                   csa_planes=planes)
-    ws = attn_ops.DecodeWorkspace(B, Hh, attn_ops.choose_splits(B, Hh, W + K), dev)
+    splits, tile_rows = attn_ops.choose_tiling(B, Hh, max(W, 1) + K)
+    ws = attn_ops.DecodeWorkspace(B, Hh, splits, dev, tile_rows)
     out = torch.empty(B, Hh, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, Hh, dtype=torch.float32, device=dev)
     fn = lambda: attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, **args_d)  # noqa: E731
-    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev))
+    us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev), graph=True)
     check_errors(dev)
+    phases = None
+    if args.prof:
+        prof = torch.zeros(16 + 2 * 1024, dtype=torch.int64, device=dev)
+        prof[8] = 2 ** 62
+        L2Flush(dev)()
+        attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, prof=prof, **args_d)
+        torch.cuda.synchronize(dev)
+        pv = prof.tolist()
+        ctas = max(1, pv[6])
+        phases = {n: round(pv[i] / ctas / 1e3, 2) for i, n in
+                  enumerate(["setup", "gather_expand", "s_mma", "softmax", "o_mma", "epilogue"])}
+        phases["unit"] = "us per CTA"
+        phases["tiles_per_cta"] = round(pv[7] / ctas, 2)
+        phases["cta_span_us"] = round((pv[9] - pv[8]) / 1e3, 2)
+        phases["gather_split_us"] = {n: round(pv[i] / ctas / 1e3, 2) for i, n in
+                                     ((10, "fetch"), (11, "expand"), (12, "barrier"))}
+        per = torch.tensor(pv[16:16 + 2 * min(ctas, 1024)]).view(-1, 2).float() / 1e3
+        phases["cta_total_us_min_med_max"] = [round(float(x), 1) for x in
+                                              (per[:, 0].min(), per[:, 0].median(), per[:, 0].max())]
     nbytes = B * (K * rec_bytes + W * abi.NATIVE_RECORD_BYTES) + q.numel() * 2 + out.numel() * 2
     flops = 4 * B * Hh * (K + W) * 512
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
-    return {"case": "sparse_mla_decode", "kv_format": args.kv_format, "batch": B, "heads": Hh, "topk": K,
-            "swa": W, "context": args.context, "splits": ws.splits, "us": round(us, 2), "bytes": nbytes,
+    return {"case": "sparse_mla_decode", "phases": phases, "kv_format": args.kv_format, "batch": B,
+            "heads": Hh, "topk": K,
+            "swa": W, "context": args.context, "splits": ws.splits, "tile_rows": ws.tile_rows, "us": round(us, 2), "bytes": nbytes,
             "GBps": round(gbs, 1), "hbm_fraction": round(gbs / peak, 3), "TFLOPs": round(flops / us / 1e6, 1),
             "peak_note": tag}
 
@@ -203,12 +239,13 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--swa", type=int, default=128, help="decode: SWA rows per query (0 = selected records only)")
     ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
     ap.add_argument("--rows", type=int, default=24)
     ap.add_argument("--rounds", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--precision", default="default", choices=["default", "bf16"])
-    ap.add_argument("--prof", action="store_true", help="MoE: report per-role wait times of the expert kernel")
+    ap.add_argument("--prof", action="store_true", help="report kernel phase / wait-time counters")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     if args.case == "moe":
@@ -219,6 +256,7 @@ def main():
         out = bench_decode(args, dev)
     else:
         out = bench_store(args, dev)
+    out["clocks"] = dict(LAST_CLOCKS)
     print(json.dumps(out), flush=True)
 
 

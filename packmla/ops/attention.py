@@ -27,19 +27,31 @@ class PackedPlanes:
     scales: torch.Tensor  # uint8 [rows, 8]
 
 
-def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
-    """KV splits per (query, head group): as many as fit in one wave of one CTA per SM."""
+def choose_tiling(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> tuple[int, int]:
+    """(KV splits per (query, head group), KV rows per tile).
+
+    As many splits as fit in one wave of one CTA per SM.  A CTA's latency is dominated by gathering
+    and expanding its rows, so when even 64-row tiles fit in one wave the tiles are 64 rows (twice the
+    CTAs, half the chain per CTA)."""
     groups = (heads + HEAD_GROUP - 1) // HEAD_GROUP
-    tiles = max(1, math.ceil(max_rows / KV_TILE))
-    want = max(1, num_sms // max(1, batch * groups))
-    return max(1, min(tiles, want))
+    work = max(1, batch * groups)
+    tile = KV_TILE
+    if work * max(1, math.ceil(max_rows / KV_TILE)) * 2 <= num_sms:
+        tile = KV_TILE // 2
+    tiles = max(1, math.ceil(max_rows / tile))
+    return max(1, min(tiles, num_sms // work)), tile
+
+
+def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
+    return choose_tiling(batch, heads, max_rows, num_sms)[0]
 
 
 class DecodeWorkspace:
     """Split-KV partials with stable pointers (safe to capture in CUDA graphs)."""
 
-    def __init__(self, batch: int, heads: int, splits: int, device):
+    def __init__(self, batch: int, heads: int, splits: int, device, tile_rows: int = KV_TILE):
         self.splits = splits
+        self.tile_rows = tile_rows
         self.part_o = torch.empty(batch * splits * heads * abi.LATENT_DIM, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(batch * splits * heads * 2, dtype=torch.float32, device=device)
 
@@ -62,6 +74,7 @@ def sparse_mla_decode(
     workspace: DecodeWorkspace | None = None,
     out: torch.Tensor | None = None,
     lse: torch.Tensor | None = None,
+    prof: torch.Tensor | None = None,
 ):
     """q [B,H,512] bf16 (tail rotated by the query position) -> (out bf16 [B,H,512], lse fp32 [B,H]).
 
@@ -76,11 +89,16 @@ def sparse_mla_decode(
     if not q.is_cuda:
         return _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos,
                            csa_pool, csa_planes)
+    tile_rows = KV_TILE
     if num_splits is None:
-        num_splits = workspace.splits if workspace is not None else choose_splits(
-            B, H, swa_slots.shape[1] + csa_slots.shape[1])
+        if workspace is not None:
+            num_splits, tile_rows = workspace.splits, workspace.tile_rows
+        else:
+            num_splits, tile_rows = choose_tiling(B, H, swa_slots.shape[1] + csa_slots.shape[1])
+    elif workspace is not None and workspace.splits == num_splits:
+        tile_rows = workspace.tile_rows
     if workspace is None or workspace.splits != num_splits:
-        workspace = DecodeWorkspace(B, H, num_splits, q.device)
+        workspace = DecodeWorkspace(B, H, num_splits, q.device, tile_rows)
     if out is None:
         out = torch.empty(B, H, abi.LATENT_DIM, dtype=torch.bfloat16, device=q.device)
     if lse is None:
@@ -94,7 +112,7 @@ def sparse_mla_decode(
     ext().sparse_mla_decode(
         q, swa_pool, swa_slots, swa_len, packed, native_pool, values, bitmap, scales,
         csa_slots, csa_pos, csa_len, freqs, sink, float(scale), q_pos, int(num_splits),
-        workspace.part_o, workspace.part_ml, out, lse, error_word(dev),
+        workspace.part_o, workspace.part_ml, out, lse, error_word(dev), prof, int(tile_rows),
     )
     return out, lse
 

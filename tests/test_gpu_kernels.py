@@ -102,8 +102,11 @@ def _build_cache(seed, n_swa_rows, n_csa_rows, packed):
 
 
 @pytest.mark.parametrize("packed", [False, True])
-@pytest.mark.parametrize("B,H,K,splits", [(2, 64, 512, None), (3, 16, 317, 1), (2, 128, 512, 3), (1, 8, 40, None)])
-def test_sparse_decode_matches_oracle(cuda, packed, B, H, K, splits):
+@pytest.mark.parametrize("B,H,K,splits,tile_rows", [(2, 64, 512, None, None), (3, 16, 317, 1, None),
+                                                     (2, 128, 512, 3, None), (1, 8, 40, None, None),
+                                                     (2, 64, 512, 1, 64), (3, 64, 317, 2, 128)])
+def test_sparse_decode_matches_oracle(cuda, packed, B, H, K, splits, tile_rows):
+    """GPU decode vs the fp32 oracle; tile_rows 64 with one split runs many half tiles per CTA."""
     seed = B * 1000 + H + K + int(packed)
     g = torch.Generator().manual_seed(seed)
     W = 128
@@ -126,9 +129,10 @@ def test_sparse_decode_matches_oracle(cuda, packed, B, H, K, splits):
     dev = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in args.items()}
     gplanes = None if planes is None else attn_ops.PackedPlanes(planes.values.cuda(), planes.bitmap.cuda(),
                                                                 planes.scales.cuda())
+    ws = None if tile_rows is None else attn_ops.DecodeWorkspace(B, H, splits, cuda, tile_rows)
     o, lse = attn_ops.sparse_mla_decode(q.cuda(), swa_pool.cuda(), freqs=freqs.cuda(),
                                         csa_pool=None if csa_pool is None else csa_pool.cuda(), csa_planes=gplanes,
-                                        num_splits=splits, **dev)
+                                        num_splits=splits, workspace=ws, **dev)
     check_errors(cuda)
     torch.testing.assert_close(o.float().cpu(), ref_o.float(), atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=2e-2, rtol=2e-2)
