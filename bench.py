@@ -183,14 +183,28 @@ def main() -> None:
         "clocks": clk.summary(),
         "setup_s": round(t_build, 1),
     }
+    # graphs hold NCCL calls under TP: drop every reference and destroy them before the group
+    del g, device_step
     eng.runner.release()
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize(device)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
+        import os
+        import threading
+
         import torch.distributed as dist
 
         dist.barrier()
-        dist.destroy_process_group()
+        # bounded teardown: a communicator that does not shut down must not hold the GPUs
+        t = threading.Thread(target=dist.destroy_process_group, daemon=True)
+        t.start()
+        t.join(60)
+        sys.stdout.flush()
+        os._exit(0 if not t.is_alive() else 3)
 
 
 if __name__ == "__main__":

@@ -122,6 +122,9 @@ class DecodeGraphRunner:
         return self.out_tokens[:b]
 
     def release(self) -> None:
+        """Destroy the captured graphs (they hold NCCL calls under TP: release before destroying the group)."""
+        for g in self.graphs.values():
+            g.reset()
         self.graphs.clear()
         self.pool_handle = None
 
