@@ -50,6 +50,8 @@ def main() -> None:
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--collectives", default="fused", choices=["fused", "nccl"],
+                    help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -72,9 +74,14 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    comm = TPComm()
     cfg = ModelConfig()
     C = args.concurrency * world
+    if world > 1 and args.collectives == "fused":
+        from packmla.parallel.fused import FusedComm
+
+        comm = FusedComm(device, cfg.hidden_size)
+    else:
+        comm = TPComm()
     steps_total = args.warmup + 2 * args.steps + 4
     if steps_total > args.output_len:
         raise SystemExit(f"warmup + 2*steps + 4 = {steps_total} exceeds the {args.output_len}-token output")
@@ -173,6 +180,7 @@ def main() -> None:
             "seq_len": args.context,
             "output_len": args.output_len,
             "parallelism": f"tp{world}ep{world}",
+            "collectives": args.collectives if world > 1 else "none",
             "kv_cache_format": args.kv_format,
             "l2": "inputs larger than L2 (all ~150 GB of weights and the KV cache are read every step)",
             "kv_capacity_vs_native": round(direct_cap / native_cap, 4),
@@ -199,6 +207,8 @@ def main() -> None:
         import torch.distributed as dist
 
         dist.barrier()
+        if hasattr(comm, "close"):
+            comm.close()
         # bounded teardown: a communicator that does not shut down must not hold the GPUs
         t = threading.Thread(target=dist.destroy_process_group, daemon=True)
         t.start()

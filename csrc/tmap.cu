@@ -56,3 +56,18 @@ int make_tmap_fp4_unpacked_nd(void* out, const void* base, int rank, const uint6
                  const_cast<void*>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
+
+// 2-D map over a row-major bf16 matrix (K contiguous) with the 128-byte swizzle: a box of 64 values x
+// box_rows rows fills box_rows x 128 bytes in the K-major SW128 layout of tcgen05 operands.
+int make_tmap_bf16_sw128(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
+                         uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  const cuuint64_t dims[2] = {k_elems, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return (int)fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}

@@ -3,6 +3,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cstdlib>
+#include <cstring>
+#include <algorithm>
 #include "launchers.h"
 
 namespace {
@@ -545,6 +547,120 @@ void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+// ----------------------------------------------------------------------------- symmetric memory (CUDA IPC)
+// A buffer every rank of a TP group allocates with the same size; the IPC handles are exchanged by the
+// caller (torch.distributed) and opened here, so kernels can load and store a peer's copy over NVLink.
+std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t bytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&ptr, (size_t)bytes));
+  C10_CUDA_CHECK(cudaMemset(ptr, 0, (size_t)bytes));
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, ptr));
+  auto t = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  std::memcpy(t.data_ptr(), &h, sizeof(h));
+  return {reinterpret_cast<int64_t>(ptr), t};
+}
+int64_t symm_open(torch::Tensor handle, int64_t device) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t) && handle.scalar_type() == torch::kUInt8);
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.contiguous().data_ptr(), sizeof(h));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(ptr);
+}
+void symm_close(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
+}
+void symm_free(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr)));
+}
+
+namespace {
+// layout = [recv_off, recv_elems, gath_off, flag_rs_off, flag_ag_off, max_src, max_tiles] (bytes / counts)
+SymmComm make_comm(const torch::Tensor& peers, int64_t rank, int64_t world, const std::vector<int64_t>& layout,
+                   const torch::Tensor& epoch, const torch::Tensor& err, int64_t timeout_ns) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64 && peers.numel() == world && peers.is_contiguous(),
+              "peers must be CUDA int64[world]");
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == torch::kInt32 && epoch.numel() >= 2, "epoch must be CUDA int32[2]");
+  check_err(err);
+  TORCH_CHECK(layout.size() == 7, "layout must have 7 entries");
+  TORCH_CHECK(rank >= 0 && rank < world && world >= 1 && world <= layout[5], "bad rank/world");
+  SymmComm c;
+  c.peers = reinterpret_cast<const unsigned long long*>(peers.data_ptr<int64_t>());
+  c.rank = (int)rank;
+  c.world = (int)world;
+  c.recv_off = layout[0];
+  c.recv_elems = layout[1];
+  c.gath_off = layout[2];
+  c.flag_rs_off = layout[3];
+  c.flag_ag_off = layout[4];
+  c.max_src = (int)layout[5];
+  c.max_tiles = (int)layout[6];
+  c.epoch = reinterpret_cast<unsigned int*>(epoch.data_ptr<int>());
+  c.err = err.data_ptr<int>();
+  c.timeout_ns = timeout_ns;
+  return c;
+}
+}  // namespace
+
+void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor peers, int64_t rank,
+                    int64_t world, std::vector<int64_t> layout, torch::Tensor epoch, torch::Tensor err, int64_t splits,
+                    int64_t timeout_ns) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+              "x must be CUDA bf16 [B, K] contiguous");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.dim() == 2 && w.is_contiguous() && w.size(1) == x.size(1),
+              "w must be bf16 [N, K] contiguous");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) == x.size(0) &&
+              out.size(1) == w.size(0), "out must be bf16 [B, N]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0 && (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) == 0,
+              "x and w must be 16-byte aligned");
+  GemmArParams p;
+  p.c = make_comm(peers, rank, world, layout, epoch, err, timeout_ns);
+  p.B = (int)x.size(0);
+  p.K = (int)x.size(1);
+  p.N = (int)w.size(0);
+  p.S = (int)splits;
+  p.Bpad = p.B <= 256 ? (p.B + 15) / 16 * 16 : (p.B + 31) / 32 * 32;
+  const int stage_bytes = 128 * 128 + p.Bpad * 128;
+  p.stages = std::min(8, (232448 - 1280) / stage_bytes);
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  const int rc = launch_gemm_allreduce(p, w.data_ptr(), x.data_ptr(), num_sms_of(x.device()), stream());
+  TORCH_CHECK(rc == 0, "gemm_allreduce: unsupported shape or launch failure (code ", rc, ", B=", p.B, " N=", p.N,
+              " K=", p.K, " splits=", p.S, ")");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void allreduce(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> f, torch::Tensor out, torch::Tensor peers,
+               int64_t rank, int64_t world, std::vector<int64_t> layout, torch::Tensor epoch, torch::Tensor err,
+               int64_t chunk, int64_t timeout_ns) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be CUDA bf16");
+  ArParams p;
+  p.c = make_comm(peers, rank, world, layout, epoch, err, timeout_ns);
+  p.n = out.numel();
+  p.chunk = chunk;
+  p.a = nullptr;
+  p.f = nullptr;
+  if (a) {
+    TORCH_CHECK(a->scalar_type() == torch::kBFloat16 && a->is_contiguous() && a->numel() == p.n);
+    p.a = reinterpret_cast<const __nv_bfloat16*>(a->data_ptr());
+  }
+  if (f) {
+    TORCH_CHECK(f->scalar_type() == torch::kFloat32 && f->is_contiguous() && f->numel() == p.n);
+    p.f = f->data_ptr<float>();
+  }
+  for (const void* q : {(const void*)p.a, (const void*)p.f, (const void*)out.data_ptr()})
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(q) % 16) == 0, "all-reduce operands must be 16-byte aligned");
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  const int rc = launch_allreduce(p, num_sms_of(out.device()), stream());
+  TORCH_CHECK(rc == 0, "allreduce: unsupported size or launch failure (code ", rc, ")");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -575,4 +691,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
         py::arg("prof") = py::none(), py::arg("tile_rows") = 128);
+  m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");
+  m.def("symm_open", &symm_open, "map a peer's symmetric buffer from its IPC handle");
+  m.def("symm_close", &symm_close, "unmap a peer's symmetric buffer");
+  m.def("symm_free", &symm_free, "free a symmetric buffer");
+  m.def("gemm_allreduce", &gemm_allreduce, "tcgen05 row-parallel GEMM fused with a two-shot all-reduce over peers");
+  m.def("allreduce", &allreduce, "two-shot all-reduce of (bf16 + fp32) addends over peers");
 }

@@ -79,7 +79,8 @@ class V4FlashModel:
         self.r4max = pool.max_context // abi.C4_RATIO
         self.r128max = max(1, pool.max_context // abi.C128_RATIO)
         self.topk = min(cfg.index_topk, self.r4max)
-        self.ar_hook = None  # optional fused projection + all-reduce (parallel.fused)
+        # fused output projection + all-reduce over peer memory (parallel.fused.FusedComm) when available
+        self.ar_hook = getattr(comm, "gemm_all_reduce", None) if self.world > 1 else None
         self.moe_precision = "default"  # MXFP8 expert activations ("bf16": BF16 activations)
         self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
 
@@ -268,6 +269,8 @@ class V4FlashModel:
         shared = fused_ops.silu_mul(g[:, :c]) @ lw["shared_w2"].T
         if self.comm is None or self.world == 1:
             return shared, out
+        if hasattr(self.comm, "all_reduce_sum"):
+            return self.comm.all_reduce_sum(out, shared), None
         return self._all_reduce((out + shared.float()).to(torch.bfloat16)), None
 
     def _layer_norms(self, layer: int):
