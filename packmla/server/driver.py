@@ -1,0 +1,191 @@
+"""Engine driver: the one thread that owns an `Engine`, fed by HTTP handlers through queues.
+
+Reference behaviour (SGLang scheduler process behind the tokenizer manager, R8/R9): requests enter a
+queue, the scheduler loop admits them and steps the model, and tokens stream back per request.
+Here the loop runs on a thread of the server process; handlers await per-request asyncio queues
+that the loop fills with `loop.call_soon_threadsafe`.
+
+Tensor parallelism: rank 0 serves HTTP and, once per loop iteration, broadcasts the operations it
+applies (add / abort / flush / stop) to the other ranks over a CPU (gloo) group; every rank applies
+the same operations in the same order and then takes the same `Engine.step()`, so the schedules
+and the KV pools stay identical in lockstep (reference: Gloo CPU broadcast of the batch each step).
+"""
+from __future__ import annotations
+
+import asyncio
+import itertools
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+
+from ..engine.engine import Engine, SamplingParams
+
+
+@dataclass
+class Stream:
+    """Handle of one submitted request: tokens arrive on `queue`; `None` marks the end."""
+
+    ext_id: int
+    prompt_len: int
+    loop: asyncio.AbstractEventLoop | None
+    queue: asyncio.Queue | None
+    tokens: list[int] = field(default_factory=list)
+    finish_reason: str | None = None
+    done: threading.Event = field(default_factory=threading.Event)
+    t_submit: float = 0.0
+    t_first: float | None = None
+
+
+class EngineDriver:
+    IDLE_WAIT_S = 0.02
+
+    def __init__(self, engine: Engine, rank: int = 0, world: int = 1, cpu_group=None):
+        self.engine = engine
+        self.rank = rank
+        self.world = world
+        self.cpu_group = cpu_group
+        self._inbox: queue.Queue = queue.Queue()
+        self._streams: dict[int, Stream] = {}
+        self._rid_to_ext: dict[int, int] = {}
+        self._ext_ids = itertools.count()
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        self.error: BaseException | None = None
+
+    # ------------------------------------------------------------------ public (any thread)
+    def start(self) -> "EngineDriver":
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._run, name="packmla-engine", daemon=True)
+            self._thread.start()
+        return self
+
+    def stop(self, timeout: float = 30.0) -> None:
+        self._inbox.put(("stop",))
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+
+    def submit(self, prompt: list[int], params: SamplingParams, loop: asyncio.AbstractEventLoop | None = None
+               ) -> Stream:
+        if self.error is not None:
+            raise RuntimeError(f"engine loop failed: {self.error!r}")
+        if not prompt:
+            raise ValueError("empty prompt")
+        need = len(prompt) + params.max_new_tokens
+        if need > self.engine.pool.max_context:
+            raise ValueError(f"prompt + max_tokens = {need} exceeds the context limit {self.engine.pool.max_context}")
+        ext = next(self._ext_ids)
+        st = Stream(ext, len(prompt), loop, asyncio.Queue() if loop is not None else None, t_submit=time.perf_counter())
+        self._streams[ext] = st
+        self._inbox.put(("add", ext, list(prompt), params))
+        return st
+
+    def abort(self, ext: int) -> None:
+        self._inbox.put(("abort", ext))
+
+    def flush_cache(self) -> None:
+        self._inbox.put(("flush",))
+
+    def generate(self, prompt: list[int], params: SamplingParams, timeout: float = 600.0) -> Stream:
+        """Blocking convenience: submit and wait for the end of the request."""
+        st = self.submit(prompt, params)
+        if not st.done.wait(timeout):
+            raise TimeoutError("request did not finish")
+        return st
+
+    # ------------------------------------------------------------------ engine thread
+    def _collect_ops(self) -> list[tuple]:
+        ops = []
+        block = not self.engine.has_work()
+        try:
+            ops.append(self._inbox.get(timeout=self.IDLE_WAIT_S) if block else self._inbox.get_nowait())
+            while True:
+                ops.append(self._inbox.get_nowait())
+        except queue.Empty:
+            pass
+        return ops
+
+    def _sync_ops(self, ops: list[tuple]) -> list[tuple]:
+        if self.world == 1:
+            return ops
+        import torch.distributed as dist
+
+        box = [ops if self.rank == 0 else None]
+        dist.broadcast_object_list(box, src=0, group=self.cpu_group)
+        return box[0]
+
+    def _apply(self, ops: list[tuple]) -> bool:
+        eng = self.engine
+        for op in ops:
+            kind = op[0]
+            if kind == "stop":
+                return False
+            if kind == "add":
+                _, ext, prompt, params = op
+                rid = eng.add_request(prompt, params)
+                self._rid_to_ext[rid] = ext
+            elif kind == "abort":
+                ext = op[1]
+                for rid, e in list(self._rid_to_ext.items()):
+                    if e == ext and eng.abort(rid):
+                        eng.done.pop(rid, None)
+                        self._finish(rid, "abort")
+            elif kind == "flush":
+                flush = getattr(eng, "flush_cache", None)
+                if flush is not None:
+                    flush()
+        return True
+
+    def _finish(self, rid: int, reason: str) -> None:
+        ext = self._rid_to_ext.pop(rid, None)
+        st = self._streams.pop(ext, None) if ext is not None else None
+        if st is None:
+            return
+        st.finish_reason = reason
+        st.done.set()
+        self._deliver_to(st, None)
+
+    def _deliver_to(self, st: Stream, item) -> None:
+        if st.queue is not None and st.loop is not None:
+            st.loop.call_soon_threadsafe(st.queue.put_nowait, item)
+
+    def _run(self) -> None:
+        eng = self.engine
+        try:
+            while True:
+                ops = self._collect_ops() if self.rank == 0 else []
+                ops = self._sync_ops(ops)
+                if not self._apply(ops):
+                    break
+                if not eng.has_work():
+                    continue
+                for rid, tok in eng.step():
+                    ext = self._rid_to_ext.get(rid)
+                    st = self._streams.get(ext) if ext is not None else None
+                    if st is not None:
+                        if st.t_first is None:
+                            st.t_first = time.perf_counter()
+                            eng.metrics.inc("ttft_seconds_sum", st.t_first - st.t_submit)
+                        st.tokens.append(tok)
+                        self._deliver_to(st, tok)
+                    req = eng.done.pop(rid, None)  # the driver keeps no history of finished requests
+                    if req is not None and req.finished:
+                        p = req.params
+                        hit_eos = (not p.ignore_eos and p.eos_token_id is not None and req.output_ids
+                                   and req.output_ids[-1] == p.eos_token_id)
+                        if st is not None:
+                            eng.metrics.inc("e2e_seconds_sum", time.perf_counter() - st.t_submit)
+                        self._finish(rid, "stop" if hit_eos else "length")
+        except BaseException as exc:  # surface to handlers instead of dying silently
+            self.error = exc
+            for ext, st in list(self._streams.items()):
+                st.finish_reason = "error"
+                st.done.set()
+                self._deliver_to(st, None)
+            self._streams.clear()
+            raise
+
+    def run_worker(self) -> None:
+        """Ranks > 0: follow rank 0's operations until it sends `stop`."""
+        self._run()

@@ -1,0 +1,116 @@
+"""CPU: the OpenAI-compatible HTTP API over the engine driver (tiny random-init model)."""
+import json
+import threading
+
+import pytest
+import torch
+from fastapi.testclient import TestClient
+
+from packmla.config import EngineConfig, ModelConfig
+from packmla.engine.engine import Engine, SamplingParams
+from packmla.server.app import create_app
+from packmla.server.driver import EngineDriver
+from packmla.server.tokenizer import ByteTokenizer
+
+
+@pytest.fixture(scope="module")
+def served():
+    cfg = ModelConfig.tiny(num_layers=2)
+    ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=4, cuda_graph_bs=[1, 2, 4])
+    eng = Engine.build(cfg, ecfg, "cpu", max_context=512)
+    driver = EngineDriver(eng).start()
+    tok = ByteTokenizer(cfg.vocab_size)
+    app = create_app(driver, tok, "tiny")
+    with TestClient(app) as client:
+        yield client, eng, tok, cfg
+    driver.stop()
+
+
+def _reference_tokens(cfg, prompt, n):
+    """Greedy tokens of the same model through a fresh engine (same seed => same weights)."""
+    ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=4, cuda_graph_bs=[1, 2, 4])
+    eng = Engine.build(cfg, ecfg, "cpu", max_context=512)
+    return eng.generate([prompt], SamplingParams(max_new_tokens=n, eos_token_id=2, ignore_eos=False))[0]
+
+
+def test_health_models_info_metrics(served):
+    client, eng, tok, cfg = served
+    assert client.get("/health").text == "ok"
+    assert client.get("/health_generate").status_code == 200
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    info = client.get("/server_info").json()
+    assert info["kv_cache_format"] == "direct" and info["max_total_num_tokens"] > 0
+    assert client.post("/flush_cache").status_code == 200
+    assert "packmla_requests_finished" in client.get("/metrics").text
+
+
+def test_completions_match_engine_generate(served):
+    client, eng, tok, cfg = served
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "hello world", "max_tokens": 5})
+    assert r.status_code == 200, r.text
+    body = r.json()
+    ids = body["choices"][0]["token_ids"]
+    assert body["usage"] == {"prompt_tokens": 12, "completion_tokens": len(ids), "total_tokens": 12 + len(ids)}
+    assert ids == _reference_tokens(cfg, tok.encode("hello world"), 5)
+    assert body["choices"][0]["text"] == tok.decode(ids)
+    # token-id prompt, two prompts in one call
+    r2 = client.post("/v1/completions", json={"prompt": [tok.encode("hello world"), [1, 50, 60]], "max_tokens": 5})
+    ch = r2.json()["choices"]
+    assert ch[0]["token_ids"] == ids and len(ch) == 2
+
+
+def test_streaming_completions_and_chat(served):
+    client, eng, tok, cfg = served
+    with client.stream("POST", "/v1/completions", json={"prompt": "stream me", "max_tokens": 4, "stream": True,
+                                                       "ignore_eos": True}) as r:
+        events = [l[6:] for l in r.iter_lines() if l.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    chunks = [json.loads(e) for e in events[:-1]]
+    streamed = [c["choices"][0]["token_ids"][0] for c in chunks if c["choices"][0].get("token_ids")]
+    assert len(streamed) == 4 and chunks[-1]["choices"][0]["finish_reason"] == "length"
+    full = client.post("/v1/completions", json={"prompt": "stream me", "max_tokens": 4, "ignore_eos": True}).json()
+    assert full["choices"][0]["token_ids"] == streamed
+
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+    c = client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 3, "ignore_eos": True}).json()
+    assert c["object"] == "chat.completion" and c["usage"]["completion_tokens"] == 3
+    with client.stream("POST", "/v1/chat/completions", json={"messages": msgs, "max_tokens": 3, "stream": True,
+                                                            "ignore_eos": True}) as r:
+        ev = [json.loads(l[6:]) for l in r.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+    text = "".join(e["choices"][0]["delta"].get("content", "") for e in ev)
+    assert ev[0]["choices"][0]["delta"]["role"] == "assistant"
+    assert text == c["choices"][0]["message"]["content"]
+
+
+def test_generate_native_and_errors(served):
+    client, eng, tok, cfg = served
+    g = client.post("/generate", json={"input_ids": [1, 70, 80], "sampling_params": {"max_new_tokens": 2,
+                                                                                    "ignore_eos": True}}).json()
+    assert len(g["output_ids"]) == 2 and g["meta_info"]["prompt_tokens"] == 3
+    assert client.post("/v1/completions", json={"prompt": "x", "max_tokens": 0}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": "x" * 600, "max_tokens": 4}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": [cfg.vocab_size + 5], "max_tokens": 1}).status_code == 400
+    assert client.post("/v1/chat/completions", json={"messages": []}).status_code == 400
+
+
+def test_concurrent_requests_batch_and_match(served):
+    client, eng, tok, cfg = served
+    prompts = ["alpha", "beta beta", "gamma gamma gamma"]
+    out = {}
+
+    def run(p):
+        out[p] = client.post("/v1/completions", json={"prompt": p, "max_tokens": 6, "ignore_eos": True}
+                             ).json()["choices"][0]["token_ids"]
+
+    threads = [threading.Thread(target=run, args=(p,)) for p in prompts]
+    before = eng.metrics.snapshot().get("decode_steps", 0)
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for p in prompts:
+        ref = Engine.build(cfg, EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=4,
+                                             cuda_graph_bs=[1, 2, 4]), "cpu", max_context=512).generate(
+            [tok.encode(p)], SamplingParams(max_new_tokens=6))[0]
+        assert out[p] == ref
+    assert eng.metrics.snapshot()["decode_steps"] - before < 3 * 5  # decode steps were shared
