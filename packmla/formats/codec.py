@@ -56,11 +56,11 @@ def _lane_order_sumsq(x: torch.Tensor) -> torch.Tensor:
     sq = (x * x).to(_F32)  # each square rounded to fp32
     # coordinate 128 j + 4 l + i -> [R, j, l, i]
     lanes = sq.view(r, 4, 32, 4)
-    acc = torch.zeros(r, 32, dtype=_F32)
+    acc = torch.zeros(r, 32, dtype=_F32, device=x.device)
     for j in range(4):
         for i in range(4):
             acc = acc + lanes[:, j, :, i]
-    idx = torch.arange(32)
+    idx = torch.arange(32, device=x.device)
     for off in (16, 8, 4, 2, 1):
         acc = acc + acc[:, idx ^ off]
     return acc[:, 0]
@@ -122,7 +122,7 @@ def native_encode(raw: torch.Tensor, weight: torch.Tensor, eps: float, freqs: to
     y = rms_normalize(raw, weight, eps)
     q, sc = quantize_tiles(y[:, : abi.NOPE_DIM], abi.NOPE_TILES)
     tail = rotate_tail(y, freqs)[:, abi.NOPE_DIM :].to(_BF16)
-    out = torch.zeros(raw.shape[0], abi.NATIVE_RECORD_BYTES, dtype=torch.uint8)
+    out = torch.zeros(raw.shape[0], abi.NATIVE_RECORD_BYTES, dtype=torch.uint8, device=raw.device)
     out[:, : abi.NOPE_DIM] = q
     out[:, abi.NOPE_DIM : abi.NATIVE_DATA_BYTES] = tail.contiguous().view(torch.uint8)
     out[:, abi.NATIVE_DATA_BYTES : abi.NATIVE_DATA_BYTES + abi.NOPE_TILES] = sc
@@ -150,13 +150,14 @@ def topmag_mask(raw: torch.Tensor, keep: int = abi.PACKED_KEEP) -> torch.Tensor:
 def bitmap_from_mask(mask: torch.Tensor) -> torch.Tensor:
     """bool [R, 512] -> int64 [R, 8] words (LSB-first), bit pattern identical to uint64."""
     bits = mask.view(mask.shape[0], abi.BITMAP_WORDS, 64).to(torch.int64)
-    weights = torch.ones(64, dtype=torch.int64) << torch.arange(64, dtype=torch.int64)
+    weights = torch.ones(64, dtype=torch.int64, device=mask.device) << torch.arange(64, dtype=torch.int64,
+                                                                                    device=mask.device)
     return (bits * weights).sum(-1)  # wraps to the two's-complement bit pattern
 
 
 def mask_from_bitmap(words: torch.Tensor) -> torch.Tensor:
     w = words.to(torch.int64)
-    shifts = torch.arange(64, dtype=torch.int64)
+    shifts = torch.arange(64, dtype=torch.int64, device=words.device)
     bits = (w[..., None] >> shifts) & 1
     return bits.reshape(w.shape[0], abi.LATENT_DIM).bool()
 
@@ -185,7 +186,7 @@ def packed_decode(values: torch.Tensor, bitmap: torch.Tensor, scales: torch.Tens
     """Planes -> fp32 [R, 512] bf16-valued, pre-RoPE, pruned coordinates zero."""
     r = values.shape[0]
     mask = mask_from_bitmap(bitmap)
-    codes = torch.zeros(r, abi.LATENT_DIM, dtype=torch.uint8)
+    codes = torch.zeros(r, abi.LATENT_DIM, dtype=torch.uint8, device=values.device)
     codes[mask] = values.reshape(-1)
     dense = dequant_tiles(codes, scales).masked_fill(~mask, 0.0)
     return dense.to(_BF16).to(_F32)

@@ -82,6 +82,9 @@ class V4FlashModel:
         # fused output projection + all-reduce over peer memory (parallel.fused.FusedComm) when available
         self.ar_hook = getattr(comm, "gemm_all_reduce", None) if self.world > 1 else None
         self.moe_precision = "default"  # MXFP8 expert activations ("bf16": BF16 activations)
+        # optional capture observer (packmla.training.data.capture): sees every C4 store and every decode
+        # query of a C4 layer; None on the serving path
+        self.observer = None
         self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
 
     def _fuse_layer(self, layer: int) -> dict:
@@ -188,6 +191,8 @@ class V4FlashModel:
     def _store_c4(self, layer: int, raw: torch.Tensor, slots: torch.Tensor, rope_pos: torch.Tensor) -> None:
         lw = self.W["layers"][layer]
         p = self.pool
+        if self.observer is not None:
+            self.observer.observe_raw(layer, raw, slots)
         if self.kv_format == "direct":
             kv_ops.packed_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, p.c4_values[layer], p.c4_bitmap[layer],
                                 p.c4_scales[layer])
@@ -231,6 +236,8 @@ class V4FlashModel:
             csa_slots, csa_pos = self._index_topk(layer, q_lora, y, meta.c4_phys, meta.c4_count, self.r4max)
             csa_len = meta.topk_len
             pool_native, planes = self.csa_planes(layer)
+            if self.observer is not None:
+                self.observer.observe_query(self, layer, q, csa_slots, csa_pos, meta)
         elif ratio == abi.C128_RATIO:
             csa_slots, csa_pos, csa_len = meta.c128_slots, meta.c128_pos, meta.c128_len
             pool_native, planes = self.pool.c128_native[layer], None

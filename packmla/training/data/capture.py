@@ -1,0 +1,148 @@
+"""Capture observer and cache builder: training states from packmla's own model.
+
+Reference: the opt-in capture observer of the serving fork (`srt/remnant/capture.py`, hooks
+`observe_raw` / `observe_attention` in the compressor and attention backend, R10) records raw C4
+latents and decode queries of a Native-format server, and `training/data/dataset.py` turns them into
+training states.  Here `CaptureObserver` attaches to `V4FlashModel.observer`:
+
+* `observe_raw(layer, raw, slots)` keeps the FP32 compressor row of every stored C4 record, keyed by
+  physical record id (what the Packed writer would select from);
+* `observe_query(model, layer, q, csa_slots, csa_pos, meta)` turns each targeted decode query of a
+  C4 layer into a state: the selected records' raw rows and RoPE, the query, the decoded Native SWA
+  rows, sink/scale, and the Native target (attention over the Native codec of the same records).
+
+`capture_cache` drives an `Engine` in Native mode over random prompts and writes a cache
+(packmla.training.data.cache) with a frozen train/development split.  Captures need no GPU: the CPU
+engine runs the same model.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import torch
+
+from ...formats import abi, codec
+from ..calibration import Math
+from ..losses import rounded_output
+from .cache import frozen_split, write_cache
+
+
+def _complex_table(freqs_f32: torch.Tensor) -> torch.Tensor:
+    """Model RoPE table float [P, 32, 2] (cos, sin) -> complex64 [P, 32]."""
+    return torch.complex(freqs_f32[..., 0].float(), freqs_f32[..., 1].float())
+
+
+class CaptureObserver:
+    def __init__(self, layers: tuple[int, ...]):
+        self.layers = set(layers)
+        self.raw: dict[int, dict[int, torch.Tensor]] = {layer: {} for layer in layers}
+        self.targets: dict[int, tuple[str, int]] = {}  # request slot -> (rid, position to capture)
+        self.ordinals: dict[str, int] = {}
+        self.states: dict[int, list[dict]] = {layer: [] for layer in layers}
+        self.skipped = 0
+
+    # ------------------------------------------------------------------ hooks
+    def observe_raw(self, layer: int, raw: torch.Tensor, slots: torch.Tensor) -> None:
+        if layer not in self.layers:
+            return
+        slots = slots.detach().long().cpu()
+        rows = raw.detach().float().cpu()
+        keep = (slots >= 0).nonzero()[:, 0].tolist()
+        store = self.raw[layer]
+        for i in keep:
+            store[int(slots[i])] = rows[i].clone()
+
+    def observe_query(self, model, layer: int, q: torch.Tensor, csa_slots: torch.Tensor, csa_pos: torch.Tensor,
+                      meta) -> None:
+        if layer not in self.layers or not self.targets:
+            return
+        req = meta.req_slots.detach().cpu().tolist()
+        pos = meta.positions.detach().cpu().tolist()
+        for b, (slot, p) in enumerate(zip(req, pos)):
+            tgt = self.targets.get(slot)
+            if tgt is None or tgt[1] != p:
+                continue
+            self._capture(model, layer, tgt[0], b, p, q, csa_slots, csa_pos, meta)
+
+    # ------------------------------------------------------------------ state
+    def _capture(self, model, layer, rid, b, p, q, csa_slots, csa_pos, meta) -> None:
+        lw = model.W["layers"][layer]
+        cfg = model.cfg
+        slots = csa_slots[b].detach().long().cpu()
+        if bool((slots < 0).any()) or any(int(s) not in self.raw[layer] for s in slots):
+            self.skipped += 1  # only fully admitted queries (every selected record present)
+            return
+        table = _complex_table(model.freqs.detach().cpu())
+        raw = torch.stack([self.raw[layer][int(s)] for s in slots])
+        freq = table[csa_pos[b].detach().long().cpu()]
+        weight = lw["c_norm"].detach().float().cpu()
+        eps = float(cfg.rms_eps)
+        W = int(meta.swa_len[b])
+        ring = meta.swa_slots[b, :W].detach().long()
+        from ...ops import kv as kv_ops
+
+        swa = codec.native_decode(kv_ops.native_pool_read(model.pool.swa[layer], ring.to(model.device)).cpu())
+        qf = q[b].detach().float().cpu()
+        sink = lw["sink"].detach().float().cpu()
+        scale = float(model.scale)
+        query_freq = table[p]
+        native = codec.native_rows(raw, weight, eps, freq)
+        out = Math.attention(qf, torch.cat((swa, native)), sink, scale)[0]
+        target = rounded_output(Math, out, query_freq)
+        ordinal = self.ordinals.get(f"{rid}/{layer}", 0)
+        self.ordinals[f"{rid}/{layer}"] = ordinal + 1
+        self.states[layer].append({
+            "rid": rid, "ordinal": ordinal, "layer": layer, "raw": raw.contiguous(), "freq": freq.contiguous(),
+            "weight": weight.contiguous(), "eps": eps, "q": qf.contiguous(), "sink": sink.contiguous(),
+            "scale": scale, "swa": swa.contiguous(), "query_freq": query_freq.contiguous(),
+            "target": target.contiguous(), "reference_squared_norm": float(target.square().sum())})
+
+
+def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int = 2, train_queries: int = 2,
+                  dev_queries: int = 3, prompt_len: int = 300, seed: int = 0, device: str = "cpu",
+                  layers: tuple[int, ...] | None = None) -> dict:
+    """Run `issues` random requests through a Native-format engine and cache their C4-layer queries.
+
+    Each issue contributes `train_queries` (train split) or `dev_queries` (development split) decode
+    positions per layer; the split is frozen by `frozen_split`.
+    """
+    from ...config import EngineConfig
+    from ...engine.engine import Engine, SamplingParams
+
+    layers = tuple(layers) if layers is not None else tuple(model_cfg.c4_layers)
+    ids = [f"issue-{i:03d}" for i in range(issues)]
+    split = frozen_split(ids, development, seed)
+    role_of = {rid: role for role in ("train", "development") for rid in split[role]}
+    per = {"train": train_queries, "development": dev_queries}
+    steps = max(train_queries, dev_queries)
+    ecfg = EngineConfig(kv_cache_format="native", device=device, max_running_requests=2, cuda_graph_bs=[1],
+                        disable_cuda_graph=True, chunked_prefill_size=8192)
+    eng = Engine.build(model_cfg, ecfg, device, max_context=prompt_len + steps + 8, max_requests=2, seed=seed)
+    obs = CaptureObserver(layers)
+    eng.model.observer = obs
+    g = torch.Generator().manual_seed(seed)
+    for rid in ids:
+        prompt = torch.randint(3, model_cfg.vocab_size, (prompt_len,), generator=g).tolist()
+        n_q = per[role_of[rid]]
+        eng.add_request(prompt, SamplingParams(max_new_tokens=n_q + 1))
+        req = eng.waiting[-1]
+        while eng.has_work():
+            if req.slot >= 0 and req.prefilled >= len(req.prompt):
+                # the next decode step feeds position context_len - 1
+                p = req.context_len - 1
+                obs.targets = {req.slot: (rid, p)} if len(req.output_ids) <= n_q else {}
+            eng.step()
+        obs.targets = {}
+    states_by_layer = {}
+    for layer in layers:
+        roles = {"train": [], "development": []}
+        for s in obs.states[layer]:
+            role = role_of[s["rid"]]
+            s["role"] = role
+            s["split"] = role
+            roles[role].append(s)
+        states_by_layer[layer] = roles
+    write_cache(Path(output), states_by_layer, split, per,
+                {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native"})
+    return {"cache": str(output), "layers": list(layers), "split": split, "skipped": obs.skipped,
+            "states": {layer: {r: len(v) for r, v in roles.items()} for layer, roles in states_by_layer.items()}}

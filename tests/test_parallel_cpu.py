@@ -64,3 +64,45 @@ def test_tp2_matches_single_rank(tmp_path):
     # each rank's partial sums are rounded to bf16 before the all-reduce (one rank adds its fp32 expert
     # sum directly), which the random model amplifies from layer to layer
     assert max(rels) < 4e-2, rels
+
+
+def _serve_worker(rank: int, world: int, port: int, out_path: str):
+    import torch.distributed as dist
+
+    from packmla.config import EngineConfig
+    from packmla.engine.engine import Engine, SamplingParams
+    from packmla.parallel.comm import TPComm
+    from packmla.server.driver import EngineDriver
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = ModelConfig.tiny(num_layers=2)
+        ecfg = EngineConfig(device="cpu", tp=world, ep=world, chunked_prefill_size=64, max_running_requests=4,
+                            cuda_graph_bs=[1, 2, 4])
+        eng = Engine.build(cfg, ecfg, "cpu", rank, world, TPComm(), max_context=512)
+        drv = EngineDriver(eng, rank, world, cpu_group=dist.new_group(backend="gloo"))
+        if rank == 0:
+            drv.start()
+            streams = [drv.submit(p, SamplingParams(max_new_tokens=4)) for p in ([1, 5, 9, 12], [1, 7] * 40)]
+            for st in streams:
+                assert st.done.wait(120)
+            toks = [st.tokens for st in streams]
+            drv.stop()
+            torch.save({"tokens": toks, "metrics": eng.metrics.snapshot()}, out_path)
+        else:
+            drv.run_worker()
+            torch.save({"metrics": eng.metrics.snapshot()}, out_path + ".r1")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_server_driver_keeps_tp_ranks_in_lockstep(tmp_path):
+    out = str(tmp_path / "serve.pt")
+    mp.spawn(_serve_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    r0 = torch.load(out)
+    r1 = torch.load(out + ".r1")
+    assert [len(t) for t in r0["tokens"]] == [4, 4]
+    for key in ("decode_steps", "prefill_tokens", "requests_finished"):
+        assert r0["metrics"][key] == r1["metrics"][key], key
