@@ -147,12 +147,13 @@ int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream);
 struct SymmComm {
   const unsigned long long* peers;  // [world] device array: base address of each rank's buffer (own included)
   int rank, world;
-  int64_t recv_off;     // bytes: bf16 [max_src][recv_elems] partial sums, one slot per source
+  int64_t recv_off;     // bytes: bf16 [2][max_src][recv_elems] partial sums (call parity, source)
   int64_t recv_elems;
   int64_t gath_off;     // bytes: bf16 [recv_elems] reduced values (all-gather target)
   int64_t flag_rs_off;  // bytes: u32 [max_src][max_tiles]
   int64_t flag_ag_off;  // bytes: u32 [max_tiles]
   int max_src, max_tiles;
+  int64_t lpart_off;    // bytes: fp32 [max_splits - 1][recv_elems] split-K partials (read by this GPU only)
   unsigned int* epoch;  // local u32[2]: [0] completed calls, [1] CTA arrival counter
   int* err;
   int64_t timeout_ns;   // limit of every wait on a peer
@@ -160,8 +161,10 @@ struct SymmComm {
 
 struct GemmArParams {
   SymmComm c;
-  int B, Bpad, N, K, S, stages;  // K: local reduction width; S: K splits per tile (one CTA each)
-  __nv_bfloat16* out;            // [B, N]
+  int B, N, K, S, stages, nmb;  // K: local reduction width; S: K splits per tile; nmb: 128-token blocks
+  int one_shot;                 // 1: every rank reduces (one hop); 0: reduce-scatter + all-gather
+  __nv_bfloat16* out;           // [B, N]
+  unsigned long long* prof;     // optional phase counters (ns): see comm_fused.cu
 };
 
 struct ArParams {
@@ -169,11 +172,15 @@ struct ArParams {
   const __nv_bfloat16* a;  // optional bf16 addend [n]
   const float* f;          // optional fp32 addend [n]
   int64_t n, chunk;        // elements; elements per CTA (tile)
+  int one_shot;
   __nv_bfloat16* out;      // [n]
 };
 
 int make_tmap_bf16_sw128(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
                          uint32_t box_rows);
-int gemm_ar_smem_bytes(int Bpad, int stages);
+int gemm_ar_smem_bytes(int stages);
 int launch_gemm_allreduce(const GemmArParams& p, const void* w, const void* x, int num_sms, cudaStream_t stream);
 int launch_allreduce(const ArParams& p, int num_sms, cudaStream_t stream);
+
+// HiCache: copy segments (src, dst, bytes) x nseg between device and mapped host memory.
+int launch_segment_copy(const int64_t* segs_dev, int nseg, int num_sms, cudaStream_t stream);

@@ -581,14 +581,14 @@ void symm_free(int64_t ptr, int64_t device) {
 }
 
 namespace {
-// layout = [recv_off, recv_elems, gath_off, flag_rs_off, flag_ag_off, max_src, max_tiles] (bytes / counts)
+// layout = [recv_off, recv_elems, gath_off, flag_rs_off, flag_ag_off, max_src, max_tiles, lpart_off]
 SymmComm make_comm(const torch::Tensor& peers, int64_t rank, int64_t world, const std::vector<int64_t>& layout,
                    const torch::Tensor& epoch, const torch::Tensor& err, int64_t timeout_ns) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64 && peers.numel() == world && peers.is_contiguous(),
               "peers must be CUDA int64[world]");
   TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == torch::kInt32 && epoch.numel() >= 2, "epoch must be CUDA int32[2]");
   check_err(err);
-  TORCH_CHECK(layout.size() == 7, "layout must have 7 entries");
+  TORCH_CHECK(layout.size() == 8, "layout must have 8 entries");
   TORCH_CHECK(rank >= 0 && rank < world && world >= 1 && world <= layout[5], "bad rank/world");
   SymmComm c;
   c.peers = reinterpret_cast<const unsigned long long*>(peers.data_ptr<int64_t>());
@@ -601,6 +601,7 @@ SymmComm make_comm(const torch::Tensor& peers, int64_t rank, int64_t world, cons
   c.flag_ag_off = layout[4];
   c.max_src = (int)layout[5];
   c.max_tiles = (int)layout[6];
+  c.lpart_off = layout[7];
   c.epoch = reinterpret_cast<unsigned int*>(epoch.data_ptr<int>());
   c.err = err.data_ptr<int>();
   c.timeout_ns = timeout_ns;
@@ -610,25 +611,30 @@ SymmComm make_comm(const torch::Tensor& peers, int64_t rank, int64_t world, cons
 
 void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor peers, int64_t rank,
                     int64_t world, std::vector<int64_t> layout, torch::Tensor epoch, torch::Tensor err, int64_t splits,
-                    int64_t timeout_ns) {
+                    int64_t one_shot, int64_t timeout_ns, c10::optional<torch::Tensor> prof) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
               "x must be CUDA bf16 [B, K] contiguous");
   TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.dim() == 2 && w.is_contiguous() && w.size(1) == x.size(1),
               "w must be bf16 [N, K] contiguous");
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) == x.size(0) &&
               out.size(1) == w.size(0), "out must be bf16 [B, N]");
-  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0 && (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) == 0,
-              "x and w must be 16-byte aligned");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0 && (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) == 0 &&
+              (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0, "x, w and out must be 16-byte aligned");
   GemmArParams p;
   p.c = make_comm(peers, rank, world, layout, epoch, err, timeout_ns);
   p.B = (int)x.size(0);
   p.K = (int)x.size(1);
   p.N = (int)w.size(0);
   p.S = (int)splits;
-  p.Bpad = p.B <= 256 ? (p.B + 15) / 16 * 16 : (p.B + 31) / 32 * 32;
-  const int stage_bytes = 128 * 128 + p.Bpad * 128;
-  p.stages = std::min(8, (232448 - 1280) / stage_bytes);
+  p.nmb = (p.B + 127) / 128;
+  p.stages = 4;
+  p.one_shot = one_shot ? 1 : 0;
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.prof = nullptr;
+  if (prof) {
+    TORCH_CHECK(prof->is_cuda() && prof->scalar_type() == torch::kInt64 && prof->numel() >= 8);
+    p.prof = reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>());
+  }
   const int rc = launch_gemm_allreduce(p, w.data_ptr(), x.data_ptr(), num_sms_of(x.device()), stream());
   TORCH_CHECK(rc == 0, "gemm_allreduce: unsupported shape or launch failure (code ", rc, ", B=", p.B, " N=", p.N,
               " K=", p.K, " splits=", p.S, ")");
@@ -637,12 +643,13 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::
 
 void allreduce(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> f, torch::Tensor out, torch::Tensor peers,
                int64_t rank, int64_t world, std::vector<int64_t> layout, torch::Tensor epoch, torch::Tensor err,
-               int64_t chunk, int64_t timeout_ns) {
+               int64_t chunk, int64_t one_shot, int64_t timeout_ns) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be CUDA bf16");
   ArParams p;
   p.c = make_comm(peers, rank, world, layout, epoch, err, timeout_ns);
   p.n = out.numel();
   p.chunk = chunk;
+  p.one_shot = one_shot ? 1 : 0;
   p.a = nullptr;
   p.f = nullptr;
   if (a) {
@@ -658,6 +665,15 @@ void allreduce(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> f, t
   p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   const int rc = launch_allreduce(p, num_sms_of(out.device()), stream());
   TORCH_CHECK(rc == 0, "allreduce: unsupported size or launch failure (code ", rc, ")");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void segment_copy(torch::Tensor segs) {
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == torch::kInt64 && segs.dim() == 2 && segs.size(1) == 3 &&
+              segs.is_contiguous(), "segs must be CUDA int64 [n, 3] (src, dst, bytes)");
+  const int rc = launch_segment_copy(segs.data_ptr<int64_t>(), (int)segs.size(0), num_sms_of(segs.device()),
+                                     stream());
+  TORCH_CHECK(rc == 0, "segment_copy launch failed");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -691,10 +707,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
         py::arg("prof") = py::none(), py::arg("tile_rows") = 128);
+  m.def("segment_copy", &segment_copy, "batched 16-byte-aligned copies between device and mapped host memory");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");
   m.def("symm_open", &symm_open, "map a peer's symmetric buffer from its IPC handle");
   m.def("symm_close", &symm_close, "unmap a peer's symmetric buffer");
   m.def("symm_free", &symm_free, "free a symmetric buffer");
-  m.def("gemm_allreduce", &gemm_allreduce, "tcgen05 row-parallel GEMM fused with a two-shot all-reduce over peers");
-  m.def("allreduce", &allreduce, "two-shot all-reduce of (bf16 + fp32) addends over peers");
+  m.def("gemm_allreduce", &gemm_allreduce, "tcgen05 row-parallel GEMM fused with an all-reduce over peers",
+        py::arg("x"), py::arg("w"), py::arg("out"), py::arg("peers"), py::arg("rank"), py::arg("world"),
+        py::arg("layout"), py::arg("epoch"), py::arg("err"), py::arg("splits"), py::arg("one_shot"),
+        py::arg("timeout_ns"), py::arg("prof") = py::none());
+  m.def("allreduce", &allreduce, "one- or two-shot all-reduce of (bf16 + fp32) addends over peers");
 }

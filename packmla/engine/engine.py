@@ -166,6 +166,11 @@ class Engine:
         self._h_out = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
+        self.hicache = None
+        if engine_cfg.enable_hierarchical_cache:
+            from ..kv.hicache import HostKVCache
+
+            self.hicache = HostKVCache(pool, engine_cfg.hicache_ratio)
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -241,6 +246,11 @@ class Engine:
             if pages_needed > self.pool.pages.free:
                 return None
             req.slot = self.pool.admit(need)
+            if self.hicache is not None:
+                entry = self.hicache.match(req.prompt)
+                if entry is not None:  # earlier turn of this context: restore its KV, prefill the rest
+                    req.prefilled = self.hicache.restore(entry, req.slot)
+                    self.metrics.inc("hicache_hit_tokens", req.prefilled)
         return req
 
     def step(self) -> list[tuple[int, int]]:
@@ -308,6 +318,8 @@ class Engine:
                                                                  and tok == eos):
             req.finished = True
             req.t_finish = time.perf_counter()
+            if self.hicache is not None:  # write through: every token but the last has its KV stored
+                self.hicache.save(req.slot, req.prompt + req.output_ids[:-1])
             self.pool.release(req.slot)
             self.done[req.rid] = req
             self.metrics.inc("requests_finished")
@@ -318,6 +330,11 @@ class Engine:
             self.step()
         return [self.result(r).output_ids for r in rids]
 
+    def flush_cache(self) -> None:
+        """Drop cached KV of finished requests (the HiCache host tier)."""
+        if self.hicache is not None:
+            self.hicache.flush()
+
     def server_info(self) -> dict:
         return {
             "kv_cache_format": self.ecfg.kv_cache_format,
@@ -327,4 +344,6 @@ class Engine:
             "max_running_requests": self.pool.max_requests - 1,
             "cuda_graph_bs": self.runner.buckets,
             "tp": self.ecfg.tp,
+            "enable_hierarchical_cache": self.hicache is not None,
+            "hicache_host_bytes": self.hicache.host_bytes() if self.hicache is not None else 0,
         }
