@@ -52,6 +52,9 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--collectives", default="fused", choices=["fused", "nccl"],
                     help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL")
+    ap.add_argument("--oproj-gemm", default="auto", choices=["auto", "fused", "library"],
+                    help="with fused collectives: projection inside the all-reduce kernel, cuBLAS first, or "
+                         "by token count")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -79,7 +82,7 @@ def main() -> None:
     if world > 1 and args.collectives == "fused":
         from packmla.parallel.fused import FusedComm
 
-        comm = FusedComm(device, cfg.hidden_size)
+        comm = FusedComm(device, cfg.hidden_size, gemm=args.oproj_gemm)
     else:
         comm = TPComm()
     steps_total = args.warmup + 2 * args.steps + 4
@@ -180,7 +183,8 @@ def main() -> None:
             "seq_len": args.context,
             "output_len": args.output_len,
             "parallelism": f"tp{world}ep{world}",
-            "collectives": args.collectives if world > 1 else "none",
+            "collectives": (f"{args.collectives}/oproj-{args.oproj_gemm}" if args.collectives == "fused"
+                            else args.collectives) if world > 1 else "none",
             "kv_cache_format": args.kv_format,
             "l2": "inputs larger than L2 (all ~150 GB of weights and the KV cache are read every step)",
             "kv_capacity_vs_native": round(direct_cap / native_cap, 4),

@@ -6,21 +6,21 @@
 //   allreduce_kernel       Y[n] = sum over ranks r of (A_r[n] + F_r[n])  (bf16 A, fp32 F, both optional;
 //                          the MoE block's routed fp32 sum plus the shared expert's bf16 output)
 //
-// Both are two-shot all-reduces written into the producing kernel.  Every rank maps every peer's
-// symmetric buffer (CUDA IPC), so plain ld/st reach a peer's HBM over NVLink:
-//   1. reduce-scatter: output tile t is owned by rank t % world.  The CTA computing tile t stores
-//      its bf16 partial straight from registers into the owner's `recv[src]` slot, then publishes
-//      flag_rs[src][t] = epoch with a system-scope release;
-//   2. the owner's CTA acquires all sources' flags, sums the partials in fp32 in source order (the
-//      sum is computed once, so every rank receives bitwise the same result), and stores the bf16
-//      result into every rank's `gath` (all-gather), publishing flag_ag[t];
-//   3. every rank's CTA acquires flag_ag[t] and copies the tile into the caller's output tensor.
-// Transfers overlap the tensor-core work tile by tile: tiles finish at different times.
+// The all-reduce is written into the producing kernel.  Every rank maps every peer's symmetric buffer
+// (CUDA IPC), so plain ld/st reach a peer's HBM over NVLink.  Output tile t (a 256-column x 128-token
+// block, or a chunk of the flat all-reduce) is handled by the CTA with the same index on every rank:
+//   one-shot (small messages): the CTA stores its bf16 partial straight from registers into every
+//     rank's `recv[rank]` slot and publishes flag_rs[rank][t] = epoch with a system-scope release;
+//     each rank then acquires all ranks' flags and sums the partials in fp32 in rank order;
+//   two-shot (large messages): partials go only to the tile owner (rank t % world), which reduces
+//     and stores the bf16 result into every rank's `gath` (flag_ag[t]); every rank copies it out.
+// Either way each rank sums the same bf16 partials in the same order, so all ranks hold bitwise the
+// same result.  Transfers overlap the tensor-core work tile by tile: tiles finish at different times.
 //
-// No buffer needs double-buffering: a rank can only start call n+1 after every tile of call n has
-// been reduced and gathered on every owner, so no peer can still be reading what call n+1 writes.
-// Flags hold the per-rank call counter `epoch` (device memory, advanced by the last CTA of each
-// launch), so the kernels replay inside CUDA graphs.  Every wait has a time limit; on expiry the
+// The partial slots alternate by the parity of the call counter: in one-shot mode a rank may push call
+// n+1 while a peer still reduces call n, but it cannot reach call n+2 before that peer has sent its
+// call n+1 partials, i.e. finished call n.  Flags hold the per-rank call counter `epoch` (device memory, advanced by the last CTA of
+// each launch), so the kernels replay inside CUDA graphs.  Every wait has a time limit; on expiry the
 // CTA records kPeerTimeout in the error word and goes on.  All CTAs of a launch are co-resident
 // (grid <= SM count), so waits between CTAs of one launch cannot deadlock.  No TMA load here reads
 // peer memory; X and W are local and loaded with plain (non-multicast) TMA.
@@ -31,10 +31,12 @@
 
 namespace {
 constexpr int kThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue
-constexpr int kTileN = 128;    // weight rows per tile (MMA M)
-constexpr int kWBytes = kTileN * 128;
+constexpr int kTileN = 256;    // weight rows per tile (MMA N)
+constexpr int kXBytes = 128 * 128;              // 128 token rows x 64 K (bf16)
+constexpr int kStageBytes = kXBytes + kTileN * 128;
+constexpr int kSRow = kTileN + 4;               // fp32 row stride of the epilogue tile in shared memory
 constexpr int kEpiBar = 1;     // named barrier of the 128 epilogue threads
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 4;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -44,16 +46,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync %0, 128;" ::"n"(kEpiBar) : "memory"); }
 
 // Wait until *f >= s (wrap-safe), bounded by timeout_ns of GPU time.
 __device__ bool wait_flag(const uint32_t* f, uint32_t s, int64_t timeout_ns) {
   if ((int32_t)(ld_acquire_sys(f) - s) >= 0) return true;
   const uint64_t t0 = pm::globaltimer_ns();
-  while (true) {
-    __nanosleep(32);
+  for (uint32_t i = 1;; ++i) {
     if ((int32_t)(ld_acquire_sys(f) - s) >= 0) return true;
-    if ((int64_t)(pm::globaltimer_ns() - t0) > timeout_ns) return false;
+    if ((i & 63) == 0 && (int64_t)(pm::globaltimer_ns() - t0) > timeout_ns) return false;
   }
 }
 
@@ -61,8 +65,10 @@ struct Sym {
   const SymmComm& c;
   __device__ explicit Sym(const SymmComm& cc) : c(cc) {}
   __device__ uint8_t* base(int r) const { return reinterpret_cast<uint8_t*>(__ldg(c.peers + r)); }
-  __device__ __nv_bfloat16* recv(int r, int src) const {
-    return reinterpret_cast<__nv_bfloat16*>(base(r) + c.recv_off) + (int64_t)src * c.recv_elems;
+  // two parity slots: in one-shot mode a peer may push call n+1 while this rank still reduces call n
+  __device__ __nv_bfloat16* recv(int r, int src, uint32_t s) const {
+    return reinterpret_cast<__nv_bfloat16*>(base(r) + c.recv_off) +
+           ((int64_t)(s & 1) * c.max_src + src) * c.recv_elems;
   }
   __device__ __nv_bfloat16* gath(int r) const { return reinterpret_cast<__nv_bfloat16*>(base(r) + c.gath_off); }
   __device__ uint32_t* flag_rs(int r, int src, int t) const {
@@ -103,15 +109,17 @@ __device__ __forceinline__ void finish_epoch(const SymmComm& c, uint32_t s) {
 }
 
 // ----------------------------------------------------------------------------- GEMM + all-reduce
+// Operand roles: the (padded) tokens are the M = 128 operand and 256 weight rows the N operand, so each
+// tcgen05.mma consumes 256 x 16 weights (the issue cost of one instruction barely depends on N).
+// CTA (tile, mb, ks): output columns [256 tile, +256), tokens [128 mb, +128), K slice ks of S.
+// Split-K partials stay on this GPU: CTAs ks > 0 store fp32 partials in the local `lpart` slots and
+// the ks = 0 CTA adds them to its accumulators before anything crosses NVLink.
 __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_constant__ CUtensorMap tmW,
                                                               const __grid_constant__ CUtensorMap tmX,
                                                               const GemmArParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (pm::smem_u32(smem_raw) & 1023)) & 1023);
-  const int xbox = p.Bpad <= 256 ? p.Bpad : p.Bpad / 2;  // rows per X box = MMA N
-  const int nx = p.Bpad / xbox;
-  const int stage_bytes = kWBytes + p.Bpad * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * kStageBytes);
   uint64_t* empty = full + p.stages;
   uint64_t* d_full = empty + p.stages;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(d_full + 1);
@@ -119,15 +127,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const SymmComm& c = p.c;
   const Sym sym(c);
-  const int tile = blockIdx.x / p.S, ks = blockIdx.x % p.S;
+  const int ks = blockIdx.x % p.S, tm = blockIdx.x / p.S;  // tm = tile * nmb + mb (flag index)
+  const int tile = tm / p.nmb, mb = tm % p.nmb;
+  const int n0 = tile * kTileN, b0 = mb * 128;
   const int nk = p.K / 64 / p.S, k0 = ks * nk;
-  const int owner = tile % c.world, src = c.rank * p.S + ks, nsrc = c.world * p.S;
+  const int owner = tm % c.world;
   const uint32_t s = *reinterpret_cast<volatile const uint32_t*>(c.epoch) + 1;
-  uint32_t tcols = 32;
-  while ((int)tcols < p.Bpad) tcols <<= 1;
+  uint64_t t0 = 0;
+  if (p.prof && tid == 64) t0 = pm::globaltimer_ns();
 
   if (warp == 0) {
-    pm::tmem_alloc(tslot, tcols);
+    pm::tmem_alloc(tslot, kTileN);
     pm::tmem_relinquish();
   }
   if (tid == 32) {
@@ -151,11 +161,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
       uint32_t issued_ph[kMaxStages];
       for (int i = 0; i < nk; ++i) {
         if (!pm::mbar_wait(empty + st, ph ^ 1, c.err, 301)) { *abort_flag = 1; break; }
-        uint8_t* sb = smem + st * stage_bytes;
-        pm::mbar_arrive_expect_tx(full + st, stage_bytes);
+        uint8_t* sb = smem + st * kStageBytes;
+        pm::mbar_arrive_expect_tx(full + st, kStageBytes);
         const int kx = (k0 + i) * 64;  // element offset: a multiple of 64 (128 B)
-        pm::tma_load_2d(sb, &tmW, kx, tile * kTileN, full + st);
-        for (int h = 0; h < nx; ++h) pm::tma_load_2d(sb + kWBytes + h * xbox * 128, &tmX, kx, h * xbox, full + st);
+        pm::tma_load_2d(sb, &tmX, kx, b0, full + st);
+        pm::tma_load_2d(sb + kXBytes, &tmW, kx, n0, full + st);
         issued_ph[st] = ph;
         ++issued;
         if (++st == p.stages) { st = 0; ph ^= 1; }
@@ -171,18 +181,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
     if (lane == 0) {
       int st = 0;
       uint32_t ph = 0;
-      const uint32_t idesc = pm::make_idesc_f16(128, xbox, 1, 0, 0);
+      const uint32_t idesc = pm::make_idesc_f16(128, kTileN, 1, 0, 0);
       for (int i = 0; i < nk && !*abort_flag; ++i) {
         if (!pm::mbar_wait(full + st, ph, c.err, 302)) { *abort_flag = 1; break; }
         pm::tc_fence_after();
-        const uint32_t sb = pm::smem_u32(smem + st * stage_bytes);
+        const uint32_t sb = pm::smem_u32(smem + st * kStageBytes);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = pm::make_sdesc(sb + 32 * k, 16, 1024);
-          for (int h = 0; h < nx; ++h)
-            pm::umma_f16(tmem + h * xbox, a, pm::make_sdesc(sb + kWBytes + h * xbox * 128 + 32 * k, 16, 1024), idesc,
-                         (i | k) ? 1u : 0u);
-        }
+        for (int k = 0; k < 4; ++k)
+          pm::umma_f16(tmem, pm::make_sdesc(sb + 32 * k, 16, 1024), pm::make_sdesc(sb + kXBytes + 32 * k, 16, 1024),
+                       idesc, (i | k) ? 1u : 0u);
         pm::umma_commit(empty + st);
         if (++st == p.stages) { st = 0; ph ^= 1; }
       }
@@ -190,68 +197,113 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2-5)
-    const int q = warp & 3, r = 32 * q + lane, n = tile * kTileN + r;
+    // The accumulator rows (one token per TMEM lane) go to shared memory first (the drained stage
+    // buffers), so every later step works on 8-column chunks spread over all 128 threads: a tile with
+    // few tokens must not serialize its split-K sums and pushes on one thread per row.
+    const int q = warp & 3, r = 32 * q + lane;
     const int et = tid - 64;  // 0..127
     const bool ok = pm::mbar_wait(d_full, 0, c.err, 303);
     pm::tc_fence_after();
-    // 1. partial -> owner's recv[src][n][b]
-    __nv_bfloat16* dst = sym.recv(owner, src) + (int64_t)n * p.Bpad;
-    for (int c0 = 0; c0 < p.B; c0 += 16) {
-      float v[16];
-      pm::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
-      if (!ok || nk == 0) {
+    const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+    const int rows = min(128, p.B - b0);
+    const int nchunks = rows * (kTileN / 8);
+    float* stile = reinterpret_cast<float*>(smem);
+    uint64_t t1 = 0, t2 = 0, t3 = 0;
+    if (32 * q < rows) {  // warp-uniform: tcgen05.ld is a warp-collective instruction
+      for (int c0 = 0; c0 < kTileN; c0 += 16) {
+        float v[16];
+        pm::tmem_ld16(trow + c0, v);
+        float* dst = stile + r * kSRow + c0;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(dst + j) = ok ? make_float4(v[j], v[j + 1], v[j + 2], v[j + 3])
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      uint4 lo = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
-      uint4 hi = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]), pack_bf16(v[12], v[13]),
-                            pack_bf16(v[14], v[15]));
-      reinterpret_cast<uint4*>(dst + c0)[0] = lo;
-      reinterpret_cast<uint4*>(dst + c0)[1] = hi;
     }
     epi_sync();
-    if (et == 0) {
-      __threadfence_system();
-      st_release_sys(sym.flag_rs(owner, src, tile), s);
-    }
-    if (ks == 0) {
-      // 2. owner: reduce all sources, all-gather the bf16 result
-      if (c.rank == owner) {
-        if (et < nsrc && !wait_flag(sym.flag_rs(c.rank, et, tile), s, c.timeout_ns))
+    const float* lpart = reinterpret_cast<const float*>(sym.base(c.rank) + c.lpart_off);
+    if (ks != 0) {
+      // split-K partial -> local fp32 slot, then a local flag
+      float* lp = const_cast<float*>(lpart) + (int64_t)(ks - 1) * c.recv_elems;
+      for (int id = et; id < nchunks; id += 128) {
+        const int row = id / (kTileN / 8), col = (id % (kTileN / 8)) * 8;
+        const int64_t off = (int64_t)(b0 + row) * p.N + n0 + col;
+        const float* src = stile + row * kSRow + col;
+        *reinterpret_cast<float4*>(lp + off) = *reinterpret_cast<const float4*>(src);
+        *reinterpret_cast<float4*>(lp + off + 4) = *reinterpret_cast<const float4*>(src + 4);
+      }
+      epi_sync();
+      if (et == 0) st_release_gpu(sym.flag_rs(c.rank, c.world + ks - 1, tm), s);
+    } else {
+      // 1. wait for this GPU's split-K partials
+      if (et >= 1 && et < p.S && !wait_flag(sym.flag_rs(c.rank, c.world + et - 1, tm), s, c.timeout_ns))
+        pm::report_error(c.err, pm::kPeerTimeout, 330 + et);
+      epi_sync();
+      if (p.prof && et == 0) t1 = pm::globaltimer_ns();
+      // 2. full local sum (fp32, split order) -> bf16 partial of this rank -> destination(s)
+      const int d_lo = p.one_shot ? 0 : owner, d_hi = p.one_shot ? c.world : owner + 1;
+      for (int id = et; id < nchunks; id += 128) {
+        const int row = id / (kTileN / 8), col = (id % (kTileN / 8)) * 8;
+        const int64_t off = (int64_t)(b0 + row) * p.N + n0 + col;
+        const float* src = stile + row * kSRow + col;
+        float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+        for (int k2 = 1; k2 < p.S; ++k2) {
+          const float* lp = lpart + (int64_t)(k2 - 1) * c.recv_elems + off;
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(lp)), y = __ldcg(reinterpret_cast<const float4*>(lp + 4));
+          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+          b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
+        }
+        const uint4 o = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+        for (int d = d_lo; d < d_hi; ++d) *reinterpret_cast<uint4*>(sym.recv(d, c.rank, s) + off) = o;
+      }
+      epi_sync();
+      if (et < d_hi - d_lo) st_release_sys(sym.flag_rs(d_lo + et, c.rank, tm), s);
+      if (p.prof && et == 0) t2 = pm::globaltimer_ns();
+      // 3. reduce over ranks in rank order (every rank computes identical bits)
+      if (p.one_shot || c.rank == owner) {
+        if (et < c.world && !wait_flag(sym.flag_rs(c.rank, et, tm), s, c.timeout_ns))
           pm::report_error(c.err, pm::kPeerTimeout, 310 + et);
         epi_sync();
-        for (int c0 = 0; c0 < p.B; c0 += 8) {
+        for (int id = et; id < nchunks; id += 128) {
+          const int64_t off = (int64_t)(b0 + id / (kTileN / 8)) * p.N + n0 + (id % (kTileN / 8)) * 8;
           float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int sr = 0; sr < nsrc; ++sr)
-            add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr) + (int64_t)n * p.Bpad + c0)));
+          for (int sr = 0; sr < c.world; ++sr) add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr, s) + off)));
           const uint4 o = pack8(acc);
-          for (int d = 0; d < c.world; ++d)
-            *reinterpret_cast<uint4*>(sym.gath(d) + (int64_t)n * p.Bpad + c0) = o;
+          if (p.one_shot) {
+            *reinterpret_cast<uint4*>(p.out + off) = o;
+          } else {
+            for (int d = 0; d < c.world; ++d) *reinterpret_cast<uint4*>(sym.gath(d) + off) = o;
+          }
         }
-        epi_sync();
-        if (et == 0) {
-          __threadfence_system();
-          for (int d = 0; d < c.world; ++d) st_release_sys(sym.flag_ag(d, tile), s);
+        if (!p.one_shot) {
+          epi_sync();
+          if (et < c.world) st_release_sys(sym.flag_ag(et, tm), s);
         }
       }
-      // 3. every rank: wait for the gathered tile, copy it out as Y[b][n]
-      if (et == 0 && !wait_flag(sym.flag_ag(c.rank, tile), s, c.timeout_ns))
-        pm::report_error(c.err, pm::kPeerTimeout, 309);
-      epi_sync();
-      const __nv_bfloat16* g = sym.gath(c.rank) + (int64_t)n * p.Bpad;
-      for (int c0 = 0; c0 < p.B; c0 += 8) {
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(g + c0));
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (c0 + j < p.B) p.out[(int64_t)(c0 + j) * p.N + n] = e[j];
+      if (!p.one_shot) {
+        // 4. two-shot: every rank copies the gathered tile out
+        if (et == 0 && !wait_flag(sym.flag_ag(c.rank, tm), s, c.timeout_ns))
+          pm::report_error(c.err, pm::kPeerTimeout, 309);
+        epi_sync();
+        for (int id = et; id < nchunks; id += 128) {
+          const int64_t off = (int64_t)(b0 + id / (kTileN / 8)) * p.N + n0 + (id % (kTileN / 8)) * 8;
+          *reinterpret_cast<uint4*>(p.out + off) = __ldcg(reinterpret_cast<const uint4*>(sym.gath(c.rank) + off));
+        }
+      }
+      if (p.prof && et == 0) {
+        t3 = pm::globaltimer_ns();
+        atomicAdd(p.prof + 0, (unsigned long long)(t1 - t0));
+        atomicAdd(p.prof + 1, (unsigned long long)(t2 - t1));
+        atomicAdd(p.prof + 2, (unsigned long long)(t3 - t2));
+        atomicAdd(p.prof + 3, 1ull);
+        atomicMax(p.prof + 4, (unsigned long long)(t3 - t0));
       }
     }
   }
   pm::tc_fence_before();
   finish_epoch(c, s);  // contains __syncthreads
   pm::tc_fence_after();
-  if (warp == 0) pm::tmem_dealloc(tmem, tcols);
+  if (warp == 0) pm::tmem_dealloc(tmem, kTileN);
 }
 
 // ----------------------------------------------------------------------------- all-reduce
@@ -261,8 +313,8 @@ __global__ void __launch_bounds__(256) allreduce_kernel(const ArParams p) {
   const int t = blockIdx.x, owner = t % c.world;
   const uint32_t s = *reinterpret_cast<volatile const uint32_t*>(c.epoch) + 1;
   const int64_t lo = (int64_t)t * p.chunk, hi = min(p.n, lo + p.chunk);
-  // 1. local addends -> owner's recv[rank]
-  __nv_bfloat16* dst = sym.recv(owner, c.rank);
+  const int d_lo = p.one_shot ? 0 : owner, d_hi = p.one_shot ? c.world : owner + 1;
+  // 1. local addends -> recv[rank] of the destination(s)
   for (int64_t i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x) {
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (p.a) add_bf16x8(v, *reinterpret_cast<const uint4*>(p.a + i));
@@ -271,59 +323,60 @@ __global__ void __launch_bounds__(256) allreduce_kernel(const ArParams p) {
       v[0] += f0.x; v[1] += f0.y; v[2] += f0.z; v[3] += f0.w;
       v[4] += f1.x; v[5] += f1.y; v[6] += f1.z; v[7] += f1.w;
     }
-    *reinterpret_cast<uint4*>(dst + i) = pack8(v);
+    const uint4 o = pack8(v);
+    for (int d = d_lo; d < d_hi; ++d) *reinterpret_cast<uint4*>(sym.recv(d, c.rank, s) + i) = o;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    st_release_sys(sym.flag_rs(owner, c.rank, t), s);
-  }
-  // 2. owner: reduce + all-gather
-  if (c.rank == owner) {
-    if (threadIdx.x < c.world && !wait_flag(sym.flag_rs(c.rank, threadIdx.x, t), s, c.timeout_ns)) {
+  if ((int)threadIdx.x < d_hi - d_lo) st_release_sys(sym.flag_rs(d_lo + threadIdx.x, c.rank, t), s);
+  // 2. reduce over ranks in rank order: every rank (one-shot) or the owner (two-shot, then all-gather)
+  if (p.one_shot || c.rank == owner) {
+    if ((int)threadIdx.x < c.world && !wait_flag(sym.flag_rs(c.rank, threadIdx.x, t), s, c.timeout_ns))
       pm::report_error(c.err, pm::kPeerTimeout, 320 + threadIdx.x);
-    }
     __syncthreads();
     for (int64_t i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int sr = 0; sr < c.world; ++sr) add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr) + i)));
+      for (int sr = 0; sr < c.world; ++sr) add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr, s) + i)));
       const uint4 o = pack8(acc);
-      for (int d = 0; d < c.world; ++d) *reinterpret_cast<uint4*>(sym.gath(d) + i) = o;
+      if (p.one_shot) {
+        *reinterpret_cast<uint4*>(p.out + i) = o;
+      } else {
+        for (int d = 0; d < c.world; ++d) *reinterpret_cast<uint4*>(sym.gath(d) + i) = o;
+      }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int d = 0; d < c.world; ++d) st_release_sys(sym.flag_ag(d, t), s);
+    if (!p.one_shot) {
+      __syncthreads();
+      if ((int)threadIdx.x < c.world) st_release_sys(sym.flag_ag(threadIdx.x, t), s);
     }
   }
-  // 3. every rank: gathered chunk -> out
-  if (threadIdx.x == 0 && !wait_flag(sym.flag_ag(c.rank, t), s, c.timeout_ns))
-    pm::report_error(c.err, pm::kPeerTimeout, 319);
-  __syncthreads();
-  const __nv_bfloat16* g = sym.gath(c.rank);
-  for (int64_t i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x)
-    *reinterpret_cast<uint4*>(p.out + i) = __ldcg(reinterpret_cast<const uint4*>(g + i));
+  if (!p.one_shot) {
+    // 3. two-shot: gathered chunk -> out
+    if (threadIdx.x == 0 && !wait_flag(sym.flag_ag(c.rank, t), s, c.timeout_ns))
+      pm::report_error(c.err, pm::kPeerTimeout, 319);
+    __syncthreads();
+    const __nv_bfloat16* g = sym.gath(c.rank);
+    for (int64_t i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x)
+      *reinterpret_cast<uint4*>(p.out + i) = __ldcg(reinterpret_cast<const uint4*>(g + i));
+  }
   finish_epoch(c, s);
 }
 }  // namespace
 
-int gemm_ar_smem_bytes(int Bpad, int stages) { return stages * (kWBytes + Bpad * 128) + 1024 + 256; }
+int gemm_ar_smem_bytes(int stages) { return stages * kStageBytes + 1024 + 256; }
 
 int launch_gemm_allreduce(const GemmArParams& p, const void* w, const void* x, int num_sms, cudaStream_t stream) {
-  if (p.B < 1 || p.Bpad < p.B || p.Bpad % 16 || p.Bpad > 512 || (p.Bpad > 256 && p.Bpad % 32) || p.N % kTileN ||
-      p.S < 1 || p.K % (64 * p.S) || p.stages < 2 || p.stages > kMaxStages)
+  if (p.B < 1 || p.B > 128 * p.nmb || p.nmb < 1 || p.nmb > 4 || p.N % kTileN || p.S < 1 || p.K % (64 * p.S) ||
+      p.stages < 2 || p.stages > kMaxStages || p.stages * kStageBytes < 128 * kSRow * 4)
     return 1;
-  const int ntiles = p.N / kTileN;
-  if (ntiles * p.S > num_sms || ntiles > p.c.max_tiles || p.c.world * p.S > p.c.max_src ||
-      (int64_t)p.N * p.Bpad > p.c.recv_elems)
+  const int ntm = p.N / kTileN * p.nmb;
+  if (ntm * p.S > num_sms || ntm > p.c.max_tiles || p.c.world + p.S - 1 > p.c.max_src ||
+      (int64_t)p.N * p.B > p.c.recv_elems)
     return 2;
   alignas(64) CUtensorMap mw, mx;
-  const int xbox = p.Bpad <= 256 ? p.Bpad : p.Bpad / 2;
   if (make_tmap_bf16_sw128(&mw, w, p.K, p.N, (uint64_t)p.K * 2, kTileN)) return 3;
-  if (make_tmap_bf16_sw128(&mx, x, p.K, p.B, (uint64_t)p.K * 2, xbox)) return 3;
-  const int smem = gemm_ar_smem_bytes(p.Bpad, p.stages);
+  if (make_tmap_bf16_sw128(&mx, x, p.K, p.B, (uint64_t)p.K * 2, 128)) return 3;
+  const int smem = gemm_ar_smem_bytes(p.stages);
   cudaFuncSetAttribute(gemm_ar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  gemm_ar_kernel<<<ntiles * p.S, kThreads, smem, stream>>>(mw, mx, p);
+  gemm_ar_kernel<<<ntm * p.S, kThreads, smem, stream>>>(mw, mx, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -25,7 +25,7 @@ def _comm(hidden=4096, timeout_s=2.0):
 
 
 @pytest.mark.parametrize("B,N,K", [(1, 4096, 1024), (7, 256, 128), (40, 4096, 4096), (300, 4096, 1024),
-                                   (512, 1024, 512), (129, 2048, 2048)])
+                                   (512, 1024, 512), (129, 2048, 2048), (80, 4096, 4096)])
 def test_gemm_allreduce_world1(B, N, K):
     comm = _comm()
     g = torch.Generator(device="cuda").manual_seed(B * 7 + K)
@@ -33,15 +33,14 @@ def test_gemm_allreduce_world1(B, N, K):
     w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
     ref = x.float() @ w.float().T
     try:
-        for s in (1, 2, 4):
-            if K % (64 * s) or (N // 128) * s > comm.num_sms:
+        for s in (1, 2, 4, 8):
+            if K % (64 * s) or (N // 256) * -(-B // 128) * s > comm.num_sms:
                 continue
-            out = torch.empty(B, N, dtype=torch.bfloat16, device="cuda")
-            ext().gemm_allreduce(x, w, out, comm.buf.peers, 0, 1, comm.layout, comm.epoch, comm.err, s,
-                                 comm.timeout_ns)
-            check_errors(torch.device("cuda", 0))
-            rel = ((out.float() - ref).norm() / ref.norm()).item()
-            assert rel < 8e-3, (s, rel)
+            for one_shot in (True, False):
+                out = comm.gemm_all_reduce(x, w, splits=s, one_shot=one_shot)
+                check_errors(torch.device("cuda", 0))
+                rel = ((out.float() - ref).norm() / ref.norm()).item()
+                assert rel < 8e-3, (s, one_shot, rel)
     finally:
         comm.close()
 
@@ -53,9 +52,10 @@ def test_allreduce_world1_exact(n):
     a = torch.randn(n, device="cuda", generator=g).bfloat16()
     f = torch.randn(n, device="cuda", generator=g)
     try:
-        out = comm.all_reduce_sum(f, a)
-        check_errors(torch.device("cuda", 0))
-        assert torch.equal(out, (a.float() + f).bfloat16())
+        for one_shot in (True, False):
+            out = comm.all_reduce_sum(f, a, one_shot=one_shot)
+            check_errors(torch.device("cuda", 0))
+            assert torch.equal(out, (a.float() + f).bfloat16())
         out2 = comm.all_reduce(a.clone())
         check_errors(torch.device("cuda", 0))
         assert torch.equal(out2, a)
@@ -107,7 +107,7 @@ def test_peer_wait_times_out_with_error_status():
         layout[5] = max(layout[5], 2)
         a = torch.ones(8192, dtype=torch.bfloat16, device="cuda")
         out = torch.empty_like(a)
-        ext().allreduce(a, None, out, peers, 0, 2, layout, comm.epoch, err, 2048, int(0.05e9))
+        ext().allreduce(a, None, out, peers, 0, 2, layout, comm.epoch, err, 2048, 1, int(0.05e9))
         torch.cuda.synchronize()
         vals = err.tolist()
         assert vals[0] == 4 and vals[3] >= 1, vals
@@ -151,13 +151,14 @@ def _mp_worker(rank: int, world: int, port: int, out_dir: str):
             ws = [(torch.randn(4096, K, generator=torch.Generator().manual_seed(1000 * r + K)) / K ** 0.5).bfloat16()
                   for r in range(world)]
             ref = sum(x.float() @ w.float().T for x, w in zip(xs, ws))
-            y = comm.gemm_all_reduce(xs[rank].to(dev), ws[rank].to(dev))
-            torch.cuda.synchronize()
-            res[f"gemm_{B}_{K}"] = (y.cpu(), ref)
             fs = [torch.randn(B, 4096, generator=torch.Generator().manual_seed(7 * r + B)) for r in range(world)]
-            z = comm.all_reduce_sum(fs[rank].to(dev), y)
-            torch.cuda.synchronize()
-            res[f"ar_{B}"] = (z.cpu(), sum(f for f in fs) + world * y.cpu().float())
+            for one_shot in (True, False):
+                y = comm.gemm_all_reduce(xs[rank].to(dev), ws[rank].to(dev), one_shot=one_shot)
+                torch.cuda.synchronize()
+                res[f"gemm_{B}_{K}_{one_shot}"] = (y.cpu(), ref)
+                z = comm.all_reduce_sum(fs[rank].to(dev), y, one_shot=one_shot)
+                torch.cuda.synchronize()
+                res[f"ar_{B}_{one_shot}"] = (z.cpu(), sum(f for f in fs) + world * y.cpu().float())
         check_errors(dev)
         torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
