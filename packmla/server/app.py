@@ -91,7 +91,9 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
     @app.get("/health")
     async def health():
         if driver.error is not None:
-            return PlainTextResponse("engine failed", status_code=503)
+            return PlainTextResponse(f"engine failed: {driver.error!r}", status_code=503)
+        if driver.stalled():
+            return PlainTextResponse("engine step exceeded the watchdog timeout", status_code=503)
         return PlainTextResponse("ok")
 
     @app.get("/health_generate")

@@ -40,8 +40,17 @@ class Stream:
 class EngineDriver:
     IDLE_WAIT_S = 0.02
 
-    def __init__(self, engine: Engine, rank: int = 0, world: int = 1, cpu_group=None):
+    def __init__(self, engine: Engine, rank: int = 0, world: int = 1, cpu_group=None, watchdog_s: float = 1800.0,
+                 error_check_every: int = 16, fault_hook=None):
+        """`watchdog_s`: a step running longer marks the server unhealthy (reference: --watchdog-timeout);
+        `error_check_every`: steps between reads of the kernels' device error word (CUDA engines);
+        `fault_hook(step)`: host-side fault injection for tests, called before every step."""
         self.engine = engine
+        self.watchdog_s = watchdog_s
+        self.error_check_every = error_check_every
+        self.fault_hook = fault_hook
+        self.steps = 0
+        self._step_started: float | None = None
         self.rank = rank
         self.world = world
         self.cpu_group = cpu_group
@@ -80,6 +89,13 @@ class EngineDriver:
         self._streams[ext] = st
         self._inbox.put(("add", ext, list(prompt), params))
         return st
+
+    def stalled(self) -> bool:
+        t = self._step_started
+        return t is not None and time.perf_counter() - t > self.watchdog_s
+
+    def healthy(self) -> bool:
+        return self.error is None and not self.stalled()
 
     def abort(self, ext: int) -> None:
         self._inbox.put(("abort", ext))
@@ -150,7 +166,7 @@ class EngineDriver:
         if st.queue is not None and st.loop is not None:
             st.loop.call_soon_threadsafe(st.queue.put_nowait, item)
 
-    def _run(self) -> None:
+    def _run(self, reraise: bool = False) -> None:
         eng = self.engine
         try:
             while True:
@@ -160,7 +176,17 @@ class EngineDriver:
                     break
                 if not eng.has_work():
                     continue
-                for rid, tok in eng.step():
+                self._step_started = time.perf_counter()
+                if self.fault_hook is not None:
+                    self.fault_hook(self.steps)
+                produced = eng.step()
+                self.steps += 1
+                if eng.device.type == "cuda" and self.steps % self.error_check_every == 0:
+                    from ..ops._ext import check_errors
+
+                    check_errors(eng.device)  # a kernel's bounded wait or bounds check failed: stop serving
+                self._step_started = None
+                for rid, tok in produced:
                     ext = self._rid_to_ext.get(rid)
                     st = self._streams.get(ext) if ext is not None else None
                     if st is not None:
@@ -179,13 +205,16 @@ class EngineDriver:
                         self._finish(rid, "stop" if hit_eos else "length")
         except BaseException as exc:  # surface to handlers instead of dying silently
             self.error = exc
+            self._step_started = None
+            eng.metrics.inc("engine_failures")
             for ext, st in list(self._streams.items()):
                 st.finish_reason = "error"
                 st.done.set()
                 self._deliver_to(st, None)
             self._streams.clear()
-            raise
+            if reraise:
+                raise
 
     def run_worker(self) -> None:
-        """Ranks > 0: follow rank 0's operations until it sends `stop`."""
-        self._run()
+        """Ranks > 0: follow rank 0's operations until it sends `stop` (errors propagate to the caller)."""
+        self._run(reraise=True)
