@@ -153,7 +153,7 @@ struct SymmComm {
   int64_t flag_rs_off;  // bytes: u32 [max_src][max_tiles]
   int64_t flag_ag_off;  // bytes: u32 [max_tiles]
   int max_src, max_tiles;
-  int64_t lpart_off;    // bytes: fp32 [max_splits - 1][recv_elems] split-K partials (read by this GPU only)
+  int64_t lpart_off;    // bytes: fp32 [max_splits][recv_elems] split-K partials (read by this GPU only)
   unsigned int* epoch;  // local u32[2]: [0] completed calls, [1] CTA arrival counter
   int* err;
   int64_t timeout_ns;   // limit of every wait on a peer
@@ -184,3 +184,9 @@ int launch_allreduce(const ArParams& p, int num_sms, cudaStream_t stream);
 
 // HiCache: copy segments (src, dst, bytes) x nseg between device and mapped host memory.
 int launch_segment_copy(const int64_t* segs_dev, int nseg, int num_sms, cudaStream_t stream);
+
+// Adapter: Packed planes rows -> Native records at dst slots of a paged workspace.
+void launch_packed_to_native(const uint8_t* values, const uint64_t* bitmap, const uint8_t* scales, int64_t src_rows,
+                             const int32_t* rows, const int32_t* positions, const float* freqs, int64_t freq_rows,
+                             uint8_t* out, const int64_t* dst, int64_t out_slots, int n, int* err,
+                             cudaStream_t stream);

@@ -677,6 +677,31 @@ void segment_copy(torch::Tensor segs) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void packed_to_native(torch::Tensor values, torch::Tensor bitmap, torch::Tensor scales, torch::Tensor rows,
+                      torch::Tensor positions, torch::Tensor freqs, torch::Tensor out, torch::Tensor dst,
+                      torch::Tensor err) {
+  check_err(err);
+  TORCH_CHECK(values.is_cuda() && values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.size(1) == 256 &&
+              values.is_contiguous(), "values must be CUDA uint8 [rows, 256]");
+  TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.is_contiguous() && bitmap.size(0) == values.size(0) &&
+              bitmap.size(1) == 8, "bitmap must be int64 [rows, 8]");
+  TORCH_CHECK(scales.scalar_type() == torch::kUInt8 && scales.is_contiguous() && scales.size(0) == values.size(0) &&
+              scales.size(1) == 8, "scales must be uint8 [rows, 8]");
+  TORCH_CHECK(rows.scalar_type() == torch::kInt32 && positions.scalar_type() == torch::kInt32 && rows.is_contiguous() &&
+              positions.is_contiguous() && rows.numel() == positions.numel(), "rows/positions must be int32 [n]");
+  TORCH_CHECK(dst.scalar_type() == torch::kInt64 && dst.is_contiguous() && dst.numel() == rows.numel(),
+              "dst must be int64 [n]");
+  TORCH_CHECK(freqs.scalar_type() == torch::kFloat32 && freqs.dim() == 3 && freqs.size(1) == 32 && freqs.is_contiguous());
+  TORCH_CHECK(out.scalar_type() == torch::kUInt8 && out.is_contiguous() && out.numel() % kNativePageBytes == 0,
+              "out must be uint8 Native pages");
+  launch_packed_to_native(values.data_ptr<uint8_t>(), reinterpret_cast<const uint64_t*>(bitmap.data_ptr<int64_t>()),
+                          scales.data_ptr<uint8_t>(), values.size(0), rows.data_ptr<int32_t>(),
+                          positions.data_ptr<int32_t>(), freqs.data_ptr<float>(), freqs.size(0), out.data_ptr<uint8_t>(),
+                          dst.data_ptr<int64_t>(), out.numel() / kNativePageBytes * kPage, (int)rows.numel(),
+                          err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -707,6 +732,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
         py::arg("prof") = py::none(), py::arg("tile_rows") = 128);
+  m.def("packed_to_native", &packed_to_native, "Adapter: Packed planes rows -> Native records (paged workspace)");
   m.def("segment_copy", &segment_copy, "batched 16-byte-aligned copies between device and mapped host memory");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");
   m.def("symm_open", &symm_open, "map a peer's symmetric buffer from its IPC handle");

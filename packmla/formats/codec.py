@@ -119,10 +119,23 @@ def dequant_tiles(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 # --------------------------------------------------------------------------- native
 def native_encode(raw: torch.Tensor, weight: torch.Tensor, eps: float, freqs: torch.Tensor) -> torch.Tensor:
     """FP32 compressor rows [R,512] -> Native records uint8 [R, 584] (logical order)."""
-    y = rms_normalize(raw, weight, eps)
+    return _native_pack(rms_normalize(raw, weight, eps), freqs)
+
+
+def native_from_packed(values, bitmap, scales, freqs) -> torch.Tensor:
+    """Adapter view of Packed records: the Native record of the decoded (pruned) row.
+
+    NoPE tiles are re-quantized from the exactly decoded values (UE8M0 of the tile's amax); the tail
+    is rotated by `freqs` [R, 32] and rounded to BF16.
+    """
+    return _native_pack(packed_decode(values, bitmap, scales), freqs)
+
+
+def _native_pack(y: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """bf16-valued rows [R, 512] -> Native records [R, 584]."""
     q, sc = quantize_tiles(y[:, : abi.NOPE_DIM], abi.NOPE_TILES)
     tail = rotate_tail(y, freqs)[:, abi.NOPE_DIM :].to(_BF16)
-    out = torch.zeros(raw.shape[0], abi.NATIVE_RECORD_BYTES, dtype=torch.uint8, device=raw.device)
+    out = torch.zeros(y.shape[0], abi.NATIVE_RECORD_BYTES, dtype=torch.uint8, device=y.device)
     out[:, : abi.NOPE_DIM] = q
     out[:, abi.NOPE_DIM : abi.NATIVE_DATA_BYTES] = tail.contiguous().view(torch.uint8)
     out[:, abi.NATIVE_DATA_BYTES : abi.NATIVE_DATA_BYTES + abi.NOPE_TILES] = sc

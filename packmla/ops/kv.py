@@ -82,3 +82,25 @@ def native_pool_read(pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
     data = pages[page[:, None], d_idx]
     sc = pages[page[:, None], s_idx]
     return torch.cat((data, sc), -1)
+
+
+def packed_to_native(values: torch.Tensor, bitmap: torch.Tensor, scales: torch.Tensor, rows: torch.Tensor,
+                     positions: torch.Tensor, freqs: torch.Tensor, out: torch.Tensor, dst: torch.Tensor) -> None:
+    """Adapter: write the Native record of Packed row `rows[i]` (RoPE at `positions[i]`) at slot `dst[i]`
+    of the Native pages `out` (dst -1 = skip).  `freqs` is float32 [P, 32, 2]."""
+    if values.is_cuda:
+        ext().packed_to_native(values, bitmap, scales, rows.to(torch.int32).contiguous(),
+                               positions.to(torch.int32).contiguous(), freqs, out, dst.to(torch.int64).contiguous(),
+                               error_word(values.device))
+        return
+    keep = dst >= 0
+    r, p, d = rows[keep].long(), positions[keep].long(), dst[keep].long()
+    fr = torch.complex(freqs[p, :, 0], freqs[p, :, 1])
+    recs = codec.native_from_packed(values[r], bitmap[r], scales[r], fr)
+    pages = out.view(-1, abi.NATIVE_PAGE_BYTES)
+    page, rr = d // abi.RECORDS_PER_PAGE, d % abi.RECORDS_PER_PAGE
+    for i in range(recs.shape[0]):
+        base_d = int(rr[i]) * abi.NATIVE_DATA_BYTES
+        base_s = abi.RECORDS_PER_PAGE * abi.NATIVE_DATA_BYTES + int(rr[i]) * abi.NATIVE_SCALE_BYTES
+        pages[page[i], base_d:base_d + abi.NATIVE_DATA_BYTES] = recs[i, :abi.NATIVE_DATA_BYTES]
+        pages[page[i], base_s:base_s + abi.NATIVE_SCALE_BYTES] = recs[i, abi.NATIVE_DATA_BYTES:]

@@ -84,3 +84,17 @@ def test_native_encode_layout():
     assert torch.equal(dec[:, 448:], codec.rotate_tail(y, fr)[:, 448:].bfloat16().float())
     rel = (dec[:, :448] - y[:, :448]).norm() / y[:, :448].norm()
     assert rel < 0.05
+
+
+def test_adapter_native_view_decodes_to_the_packed_read():
+    """Re-quantizing exactly decoded Packed values is lossless: the Adapter's Native record decodes to
+    the same rows a Direct reader sees."""
+    g = torch.Generator().manual_seed(11)
+    raw = torch.randn(40, 512, generator=g) * torch.linspace(0.01, 30, 512)
+    raw[3] = 0  # all-zero row: every tile at the amax floor
+    w = torch.rand(512, generator=g) + 0.5
+    vals, bits, sc = codec.packed_encode(raw, w, 1e-6)
+    ang = torch.rand(40, 32, generator=g) * 6.28
+    fr = torch.polar(torch.ones_like(ang), ang).to(torch.complex64)
+    native = codec.native_from_packed(vals, bits, sc, fr)
+    assert torch.equal(codec.native_decode(native), codec.packed_read(vals, bits, sc, fr))
