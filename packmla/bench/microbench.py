@@ -144,7 +144,7 @@ def bench_decode(args, dev):
                         swa_pool)
     planes, pool = None, None
     chunk = 1 << 18
-    if args.kv_format == "direct":
+    if args.kv_format in ("direct", "adapter"):
         planes = attn_ops.PackedPlanes(torch.zeros(rows, 256, dtype=torch.uint8, device=dev),
                                        torch.zeros(rows, 8, dtype=torch.int64, device=dev),
                                        torch.zeros(rows, 8, dtype=torch.uint8, device=dev))
@@ -177,6 +177,19 @@ def bench_decode(args, dev):
     out = torch.empty(B, Hh, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, Hh, dtype=torch.float32, device=dev)
     fn = lambda: attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, **args_d)  # noqa: E731
+    if args.kv_format == "adapter":
+        # reference "Adapter" mode: reconstruct the selected Packed rows into a Native workspace, then the
+        # Native decode reads the workspace
+        n = B * K
+        wsn = torch.zeros(((n + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+        dst = torch.arange(n, device=dev, dtype=torch.int64)
+        src_rows, src_pos = csa_slots.reshape(-1).contiguous(), csa_pos.reshape(-1).contiguous()
+        args_a = dict(args_d, csa_pool=wsn, csa_planes=None,
+                      csa_slots=dst.view(B, K).int().contiguous())
+
+        def fn():
+            kv_ops.packed_to_native(planes.values, planes.bitmap, planes.scales, src_rows, src_pos, freqs, wsn, dst)
+            return attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, **args_a)
     us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev), graph=True)
     check_errors(dev)
     phases = None
@@ -240,7 +253,7 @@ def main():
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--swa", type=int, default=128, help="decode: SWA rows per query (0 = selected records only)")
-    ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
+    ap.add_argument("--kv-format", default="direct", choices=["direct", "native", "adapter"])
     ap.add_argument("--rows", type=int, default=24)
     ap.add_argument("--rounds", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)

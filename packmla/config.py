@@ -148,6 +148,9 @@ class EngineConfig:
     # MoE activation precision, as the reference's --flashinfer-mxfp4-moe-precision: "default" quantizes
     # expert inputs to MXFP8 (E4M3 + UE8M0 per 32) on sm_100, "bf16" keeps them in BF16.
     moe_precision: str = "default"
+    # C4 attention over Packed KV: "direct" reads the planes inside the attention kernel; "adapter"
+    # first reconstructs the selected rows as Native records (the reference's Adapter mode)
+    decode_impl: str = "direct"
 
     def validate(self) -> None:
         """Reject unsupported combinations before any pool allocation.
@@ -169,3 +172,7 @@ class EngineConfig:
             raise ValueError("hicache_ratio must be positive")
         if self.moe_precision not in ("default", "bf16"):
             raise ValueError("moe_precision must be 'default' or 'bf16'")
+        if self.decode_impl not in ("direct", "adapter"):
+            raise ValueError("decode_impl must be 'direct' or 'adapter'")
+        if self.decode_impl == "adapter" and self.kv_cache_format != "direct":
+            raise ValueError("the adapter decode reads Packed KV: it needs kv_cache_format direct")

@@ -85,6 +85,11 @@ class V4FlashModel:
         # optional capture observer (packmla.training.data.capture): sees every C4 store and every decode
         # query of a C4 layer; None on the serving path
         self.observer = None
+        self.adapter_ws = None
+        if self.kv_format == "direct" and pool.ecfg.decode_impl == "adapter":
+            rows = pool.max_requests * self.topk
+            self.adapter_ws = torch.zeros(-(-rows // abi.RECORDS_PER_PAGE) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8,
+                                          device=self.device)
         self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
 
     def _fuse_layer(self, layer: int) -> dict:
@@ -238,6 +243,8 @@ class V4FlashModel:
             pool_native, planes = self.csa_planes(layer)
             if self.observer is not None:
                 self.observer.observe_query(self, layer, q, csa_slots, csa_pos, meta)
+            if self.adapter_ws is not None:
+                csa_slots, pool_native, planes = self._adapter_rows(planes, csa_slots, csa_pos)
         elif ratio == abi.C128_RATIO:
             csa_slots, csa_pos, csa_len = meta.c128_slots, meta.c128_pos, meta.c128_len
             pool_native, planes = self.pool.c128_native[layer], None
@@ -248,6 +255,17 @@ class V4FlashModel:
             q, self.pool.swa[layer], meta.swa_slots, meta.swa_len, csa_slots, csa_pos, csa_len, self.freqs,
             lw["sink"], self.scale, meta.positions_i32, csa_pool=pool_native, csa_planes=planes)
         return self._o_proj(layer, o, B)
+
+    def _adapter_rows(self, planes, csa_slots: torch.Tensor, csa_pos: torch.Tensor):
+        """Adapter decode: selected Packed rows -> Native records in a workspace (slot b * K + k)."""
+        B, K = csa_slots.shape
+        n = B * K
+        idx = torch.arange(n, device=self.device, dtype=torch.int64)
+        flat = csa_slots.reshape(-1)
+        dst = torch.where(flat >= 0, idx, torch.full_like(idx, -1))
+        kv_ops.packed_to_native(planes.values, planes.bitmap, planes.scales, flat.clamp_min(0), csa_pos.reshape(-1),
+                                self.freqs, self.adapter_ws, dst)
+        return dst.view(B, K).int().contiguous(), self.adapter_ws, None
 
     def _o_proj(self, layer: int, o: torch.Tensor, B: int) -> torch.Tensor:
         cfg = self.cfg

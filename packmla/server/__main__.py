@@ -34,6 +34,7 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--enable-hierarchical-cache", action="store_true")
     ap.add_argument("--hicache-ratio", type=float, default=2.0)
     ap.add_argument("--moe-precision", default="default", choices=["default", "bf16"])
+    ap.add_argument("--decode-impl", default="direct", choices=["direct", "adapter"])
     ap.add_argument("--collectives", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--seed", type=int, default=0)
     return ap
@@ -72,7 +73,8 @@ def build_engine(args, rank: int, local: int, world: int, comm):
                         chunked_prefill_size=args.chunked_prefill_size, context_length=args.context_length,
                         disable_cuda_graph=args.disable_cuda_graph or args.device == "cpu",
                         enable_hierarchical_cache=args.enable_hierarchical_cache, hicache_ratio=args.hicache_ratio,
-                        moe_precision=args.moe_precision, device=args.device, random_seed=args.seed, **kw)
+                        moe_precision=args.moe_precision, decode_impl=args.decode_impl, device=args.device,
+                        random_seed=args.seed, **kw)
     dev = torch.device(args.device, local) if args.device == "cuda" else torch.device("cpu")
     if W is not None and dev.type == "cuda":
         W = {"layers": [{k: v.to(dev) for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],

@@ -74,3 +74,17 @@ def test_pool_exhaustion_and_release():
         pass
     pool.release(s)
     assert pool.pages.free == 4
+
+
+def test_adapter_decode_matches_direct():
+    """Adapter mode (Packed rows reconstructed as Native records before attention) gives the Direct
+    mode's tokens: the reconstruction is lossless."""
+    cfg = ModelConfig.tiny(num_layers=3)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (90, 150)]
+    outs = {}
+    for impl in ("direct", "adapter"):
+        ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=2, cuda_graph_bs=[1, 2],
+                            decode_impl=impl)
+        outs[impl] = Engine.build(cfg, ecfg, "cpu", max_context=512).generate(prompts, SamplingParams(max_new_tokens=6))
+    assert outs["adapter"] == outs["direct"]
