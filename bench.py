@@ -30,6 +30,25 @@ sys.path.insert(0, ROOT)
 METRIC = "decode output tok/s (32k in/256 out)"
 
 
+def build_identity() -> dict:
+    """git commit (when the checkout has one) and sha256 of the loaded extension."""
+    import glob
+    import hashlib
+    import subprocess
+
+    out = {}
+    try:
+        out["git_sha"] = subprocess.run(["git", "rev-parse", "HEAD"], cwd=ROOT, capture_output=True, text=True,
+                                        timeout=10).stdout.strip() or None
+    except (OSError, subprocess.SubprocessError):
+        out["git_sha"] = None
+    so = sorted(glob.glob(os.path.join(ROOT, "packmla", "_C*.so")))
+    if so:
+        with open(so[0], "rb") as f:
+            out["extension_sha256"] = hashlib.sha256(f.read()).hexdigest()[:16]
+    return out
+
+
 def reference_arm(args) -> None:
     out = {"impl": "reference", "metric": METRIC, "n_gpus": args.gpus,
            "unavailable": ("the reference (winstonxcai/flash-optimizations) is not installable: no setup.py or "
@@ -194,6 +213,7 @@ def main() -> None:
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "setup_s": round(t_build, 1),
+        "build": build_identity(),
     }
     # graphs hold NCCL calls under TP: drop every reference and destroy them before the group
     del g, device_step

@@ -14,7 +14,9 @@ identical on all ranks after the all-reduces, so sampling needs no broadcast.
 """
 from __future__ import annotations
 
+import contextlib
 import itertools
+import os
 import time
 from collections import deque
 from dataclasses import dataclass, field
@@ -26,6 +28,17 @@ from ..kv.pool import KVPool, plan_capacity
 from ..models.v4flash import V4FlashModel
 from ..models.weights import init_weights
 from ..utils.metrics import Metrics
+
+
+# NVTX ranges around scheduler steps and graph replays (PACKMLA_NVTX=1; reference: SGLang's
+# SGLANG_ENABLE_NVTX_SCHEDULER batch/rank/step ranges)
+NVTX = os.environ.get("PACKMLA_NVTX", "0") == "1"
+
+
+def nvtx_range(name: str):
+    if NVTX and torch.cuda.is_available():
+        return torch.cuda.nvtx.range(name)
+    return contextlib.nullcontext()
 
 
 @dataclass
@@ -115,10 +128,11 @@ class DecodeGraphRunner:
             self.slots[b:bp] = self.dummy_slot
             self.positions[b:bp] = 0
             self.tokens[b:bp] = 0
-        if self.enabled and bp in self.graphs:
-            self.graphs[bp].replay()
-        else:
-            self._forward(bp)
+        with nvtx_range(f"decode.{'graph' if self.enabled and bp in self.graphs else 'eager'} b={b} padded={bp}"):
+            if self.enabled and bp in self.graphs:
+                self.graphs[bp].replay()
+            else:
+                self._forward(bp)
         return self.out_tokens[:b]
 
     def release(self) -> None:
@@ -259,10 +273,13 @@ class Engine:
         Returns the (rid, token) pairs produced by this step.
         """
         req = self._admit()
+        rank = getattr(self.comm, "rank", 0)
         if req is not None:
-            return self._prefill_chunk(req)
+            with nvtx_range(f"scheduler.batch rank={rank} prefill rid={req.rid} start={req.prefilled}"):
+                return self._prefill_chunk(req)
         if self.running:
-            return self._decode()
+            with nvtx_range(f"scheduler.batch rank={rank} decode b={len(self.running)}"):
+                return self._decode()
         return []
 
     def _prefill_chunk(self, req: Request) -> list[tuple[int, int]]:

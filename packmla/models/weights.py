@@ -152,9 +152,66 @@ def save_checkpoint(path: str, W: dict, cfg: ModelConfig) -> None:
                 "tensors": {k: v.detach().cpu() for k, v in flatten(W).items()}}, path)
 
 
+def save_safetensors(directory: str, W: dict, cfg: ModelConfig, shard_bytes: int = 4 << 30) -> list[str]:
+    """Sharded safetensors checkpoint (HF layout: model-0000X-of-0000N.safetensors + an index with the
+    weight map; config and rank metadata in `packmla_config.json`).  Views that share storage (the
+    fused per-layer projections) are saved as independent tensors."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+
+    os.makedirs(directory, exist_ok=True)
+    flat = {k: v.detach().cpu().contiguous().clone() for k, v in flatten(W).items()}
+    shards: list[dict] = [{}]
+    size = 0
+    for k in sorted(flat):
+        n = flat[k].numel() * flat[k].element_size()
+        if shards[-1] and size + n > shard_bytes:
+            shards.append({})
+            size = 0
+        shards[-1][k] = flat[k]
+        size += n
+    names, weight_map = [], {}
+    for i, sh in enumerate(shards):
+        name = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, os.path.join(directory, name))
+        names.append(name)
+        weight_map.update({k: name for k in sh})
+    total = sum(v.numel() * v.element_size() for v in flat.values())
+    with open(os.path.join(directory, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
+    with open(os.path.join(directory, "packmla_config.json"), "w") as f:
+        json.dump({"config": json.loads(cfg.to_json()), "meta": W["meta"]}, f, indent=1)
+    return names
+
+
+def load_safetensors(directory: str, device="cpu") -> tuple[dict, ModelConfig]:
+    import json
+    import os
+
+    from safetensors.torch import load_file
+
+    with open(os.path.join(directory, "model.safetensors.index.json")) as f:
+        index = json.load(f)
+    with open(os.path.join(directory, "packmla_config.json")) as f:
+        meta = json.load(f)
+    cfg = ModelConfig.from_dict(meta["config"])
+    flat = {}
+    for name in sorted(set(index["weight_map"].values())):
+        flat.update(load_file(os.path.join(directory, name), device=str(device)))
+    missing = set(index["weight_map"]) - set(flat)
+    if missing:
+        raise ValueError(f"checkpoint shards miss tensors: {sorted(missing)[:5]}")
+    return unflatten(flat, cfg, meta["meta"]), cfg
+
+
 def load_checkpoint(path: str, device="cpu") -> tuple[dict, ModelConfig]:
     import json
+    import os
 
+    if os.path.isdir(path):
+        return load_safetensors(path, device)
     blob = torch.load(path, map_location="cpu", weights_only=False)
     cfg = ModelConfig.from_dict(json.loads(blob["config"]))
     flat = {k: v.to(device) for k, v in blob["tensors"].items()}

@@ -88,3 +88,16 @@ def test_adapter_decode_matches_direct():
                             decode_impl=impl)
         outs[impl] = Engine.build(cfg, ecfg, "cpu", max_context=512).generate(prompts, SamplingParams(max_new_tokens=6))
     assert outs["adapter"] == outs["direct"]
+
+
+def test_safetensors_checkpoint_round_trip(tmp_path):
+    from packmla.models.weights import flatten, load_checkpoint, save_safetensors
+
+    cfg = ModelConfig.tiny(num_layers=2)
+    W = init_weights(cfg)
+    names = save_safetensors(str(tmp_path / "ckpt"), W, cfg, shard_bytes=1 << 20)
+    assert len(names) > 1  # sharded
+    W2, cfg2 = load_checkpoint(str(tmp_path / "ckpt"))
+    assert cfg2 == cfg and W2["meta"] == W["meta"]
+    a, b = flatten(W), flatten(W2)
+    assert set(a) == set(b) and all(torch.equal(a[k], b[k]) for k in a)
