@@ -245,7 +245,9 @@ def bench_store(args, dev):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "decode", "store"])
+    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite"],
+                    help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
+                         "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--topk", type=int, default=None)
@@ -267,6 +269,18 @@ def main():
     elif args.case == "decode":
         args.topk = args.topk or 2048
         out = bench_decode(args, dev)
+    elif args.case == "decode-suite":
+        args.topk = args.topk or 2048
+        args.heads = 128
+        for ctx in (32768, 131072):
+            for batch in (1, 16, 64):
+                for fmt in ("native", "direct"):
+                    args.context, args.batch, args.kv_format = ctx, batch, fmt
+                    row = bench_decode(args, dev)
+                    row["clocks"] = dict(LAST_CLOCKS)
+                    print(json.dumps(row), flush=True)
+                    torch.cuda.empty_cache()
+        return
     else:
         out = bench_store(args, dev)
     out["clocks"] = dict(LAST_CLOCKS)

@@ -98,3 +98,16 @@ def test_adapter_native_view_decodes_to_the_packed_read():
     fr = torch.polar(torch.ones_like(ang), ang).to(torch.complex64)
     native = codec.native_from_packed(vals, bits, sc, fr)
     assert torch.equal(codec.native_decode(native), codec.packed_read(vals, bits, sc, fr))
+
+
+def test_oracle_experiment_config():
+    """CPU oracle experiment: byte accounting, mask geometry, Native close to unquantized rows, and the
+    capacity ratio of Direct over Native."""
+    from packmla.bench.oracle_experiment import run
+
+    out = run(batch=2, heads=8, context=2048, topk=128)
+    assert out["records"] == 512 and out["mask"] == {"rope_kept": 64, "nope_kept": 192}
+    assert out["bytes"]["packed_layer"] == 512 * 328 and out["bytes"]["native_layer"] == 512 * 584
+    assert out["relative_output_error"]["native_vs_exact"]["max"] < 0.05
+    assert out["relative_output_error"]["topmag_vs_native"]["mean"] < out["relative_output_error"]["packed_vs_native"]["mean"]
+    assert out["capacity_tokens_30GiB"]["ratio"] >= 1.21
