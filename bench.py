@@ -69,8 +69,9 @@ def main() -> None:
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--collectives", default="fused", choices=["fused", "nccl"],
-                    help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL")
+    ap.add_argument("--collectives", default="auto", choices=["auto", "fused", "nccl"],
+                    help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL; auto = fused "
+                         "at the world sizes the fused kernels were validated on (2), NCCL otherwise")
     ap.add_argument("--oproj-gemm", default="auto", choices=["auto", "fused", "library"],
                     help="with fused collectives: projection inside the all-reduce kernel, cuBLAS first, or "
                          "by token count")
@@ -98,6 +99,8 @@ def main() -> None:
     torch.cuda.set_device(device)
     cfg = ModelConfig()
     C = args.concurrency * world
+    if args.collectives == "auto":
+        args.collectives = "fused" if world == 2 else "nccl"
     if world > 1 and args.collectives == "fused":
         from packmla.parallel.fused import FusedComm
 
