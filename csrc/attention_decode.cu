@@ -378,40 +378,45 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
 #pragma unroll
     for (int k = 0; k < 4; ++k) rr[k] = step_ref(p, b, tb, tv, nswa, ntot, step_row(k));
   };
-  // two register sets in ping-pong: a step's record loads are issued while the previous step expands,
-  // and no register copy ever waits on loads still in flight
-  StepRegs ra, rb;
+  // four register sets, one per gather step: all record loads of a tile are in flight together, and the
+  // loads of tile t + 1 are issued while the P.V MMAs of tile t run; no register copy ever waits on loads
+  // still in flight
+  StepRegs ra, rb, rc, rd;
+  auto fetch_all = [&](int n) {
+    fetch_step(p, rr[0], v8, ra);
+    fetch_step(p, rr[1], v8, rb);
+    if (n == 4) {
+      fetch_step(p, rr[2], v8, rc);
+      fetch_step(p, rr[3], v8, rd);
+    }
+  };
 
   for (int t = 0; t < ntiles && ok; ++t) {
-    // ---- 1. gather + expand 128 rows; step 0 of this tile was fetched while the previous tile's
-    //         P.V MMAs ran
+    // ---- 1. gather + expand 128 rows (64-row tiles: steps 2-3 only on the first tile, zero rows)
+    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;
     if (t == 0) {
       resolve(0);
-      fetch_step(p, rr[0], v8, ra);
+      fetch_all(nsteps);
     }
-    // 4 steps of 32 rows; a 64-row tile runs steps 2-3 only on its first tile (zero rows, no loads)
-    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;
     uint64_t tg = p.prof && tid == 0 ? pm::globaltimer_ns() : 0;
-    auto sub = [&](int slot) {  // finer split of the gather for thread 0: [10] fetch, [11] expand
+    auto sub = [&](int slot) {  // finer split of the gather for thread 0: [11] expand
       if (p.prof && tid == 0) {
         const uint64_t tn = pm::globaltimer_ns();
         atomicAdd(p.prof + slot, (unsigned long long)(tn - tg));
         tg = tn;
       }
     };
-#pragma unroll 1
-    for (int k = 0; k < nsteps; k += 2) {
-      fetch_step(p, rr[k + 1], v8, rb);
-      sub(10);
-      if (!(p.debug & 2)) expand_step(ra, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
-      else if (v8 == 0) rowvalid[step_row(k)] = ra.kind != 0;
-      sub(11);
-      if (k + 2 < nsteps) fetch_step(p, rr[k + 2], v8, ra);
-      sub(10);
-      if (!(p.debug & 2)) expand_step(rb, step_row(k + 1), v8, srow, sKV, rowvalid, expand_lut);
-      else if (v8 == 0) rowvalid[step_row(k + 1)] = rb.kind != 0;
-      sub(11);
+    auto expand = [&](const StepRegs& R, int k) {
+      if (!(p.debug & 2)) expand_step(R, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
+      else if (v8 == 0) rowvalid[step_row(k)] = R.kind != 0;
+    };
+    expand(ra, 0);
+    expand(rb, 1);
+    if (nsteps == 4) {
+      expand(rc, 2);
+      expand(rd, 3);
     }
+    sub(11);
     pm::fence_proxy_async_smem();
     pm::tc_fence_before();
     __syncthreads();
@@ -538,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     }
     if (t + 1 < ntiles) {  // overlaps the P.V MMAs
       resolve(t + 1);
-      fetch_step(p, rr[0], v8, ra);
+      fetch_all(trows == kTile ? 4 : 2);
     }
     if (!flags[1]) {
       if (!pm::mbar_wait(bar_o, t & 1, p.err, 2)) flags[1] = 1;
