@@ -3,7 +3,7 @@
     python bench.py [--gpus N --steps K --warmup W]                  (N=1)
     torchrun --nproc-per-node N bench.py --gpus N --steps K --warmup W
 
-Metric (BASELINE.json): decode output tokens/s at 32k input / 256 output for the random-init
+Metric: decode output tokens/s at 32k input / 256 output for the random-init
 DeepSeek-V4-Flash-shape model (43 layers, 64 heads x 512 latent, C4/C128 compressed sparse
 attention, 256 MXFP4 routed experts + 1 shared), Direct (Packed 328 B) KV, TP=N attention and
 EP=N experts.  Every request holds a 32768-token context written by the engine's own store

@@ -1,6 +1,6 @@
 // Adapter: Packed C4 records (values / bitmap / scales planes) -> Native 584 B records in a paged
 // workspace, so a Native reader can consume Packed KV (reference: `packed_to_native.cu`, the CUDA
-// Adapter mode that reconstructs the selected rows before stock FlashMLA, K9; 256 survivors only,
+// Adapter mode that reconstructs the selected rows before stock FlashMLA; 256 survivors only,
 // 64-bit addressing).
 //
 // One warp per record.  Lane l owns the 16 consecutive coordinates [16 l, 16 l + 16): bits

@@ -1,7 +1,7 @@
 // Sparse MLA decode attention on tcgen05 (Native and Direct-Packed KV), plus split combine.
 //
 // Reference behaviour: FlashMLA sparse FP8 decode, Native <1,64,0> and Direct Packed <1,64,1>
-// (K1/K2, third_party/README.md:355-361) and `flash_fwd_mla_combine_kernel` (K3).  Semantics:
+// (third_party/README.md:355-361) and `flash_fwd_mla_combine_kernel`.  Semantics:
 // joint softmax over [SWA rows ; selected C4 rows] with a per-head sink, K = V = latent row,
 // output tail inverse-rotated with the query position (training/losses.py:121-126).
 //

@@ -112,8 +112,9 @@ __device__ __forceinline__ void finish_epoch(const SymmComm& c, uint32_t s) {
 // Operand roles: the (padded) tokens are the M = 128 operand and 256 weight rows the N operand, so each
 // tcgen05.mma consumes 256 x 16 weights (the issue cost of one instruction barely depends on N).
 // CTA (tile, mb, ks): output columns [256 tile, +256), tokens [128 mb, +128), K slice ks of S.
-// Split-K partials stay on this GPU: CTAs ks > 0 store fp32 partials in the local `lpart` slots and
-// the ks = 0 CTA adds them to its accumulators before anything crosses NVLink.
+// Split-K partials stay on this GPU: every split CTA stores its fp32 partial in a local `lpart` slot,
+// then CTA ks sums the S partials of column slice ks (width 256 / S) and alone moves that slice across
+// NVLink, so the sums and the pushes of a tile run on all S CTAs in parallel.
 __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_constant__ CUtensorMap tmW,
                                                               const __grid_constant__ CUtensorMap tmX,
                                                               const GemmArParams p) {
@@ -131,7 +132,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
   const int tile = tm / p.nmb, mb = tm % p.nmb;
   const int n0 = tile * kTileN, b0 = mb * 128;
   const int nk = p.K / 64 / p.S, k0 = ks * nk;
-  const int owner = tm % c.world;
   const uint32_t s = *reinterpret_cast<volatile const uint32_t*>(c.epoch) + 1;
   uint64_t t0 = 0;
   if (p.prof && tid == 64) t0 = pm::globaltimer_ns();
@@ -221,10 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
       }
     }
     epi_sync();
-    const float* lpart = reinterpret_cast<const float*>(sym.base(c.rank) + c.lpart_off);
-    if (ks != 0) {
-      // split-K partial -> local fp32 slot, then a local flag
-      float* lp = const_cast<float*>(lpart) + (int64_t)(ks - 1) * c.recv_elems;
+    // 1. this CTA's fp32 partial -> local slot ks; every split CTA of the tile then owns one column
+    //    slice of width 256 / S for the rest of the epilogue (split sum, NVLink push, rank reduction)
+    float* lpart = reinterpret_cast<float*>(sym.base(c.rank) + c.lpart_off);
+    {
+      float* lp = lpart + (int64_t)ks * c.recv_elems;
       for (int id = et; id < nchunks; id += 128) {
         const int row = id / (kTileN / 8), col = (id % (kTileN / 8)) * 8;
         const int64_t off = (int64_t)(b0 + row) * p.N + n0 + col;
@@ -232,72 +233,74 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_ar_kernel(const __grid_const
         *reinterpret_cast<float4*>(lp + off) = *reinterpret_cast<const float4*>(src);
         *reinterpret_cast<float4*>(lp + off + 4) = *reinterpret_cast<const float4*>(src + 4);
       }
-      epi_sync();
-      if (et == 0) st_release_gpu(sym.flag_rs(c.rank, c.world + ks - 1, tm), s);
-    } else {
-      // 1. wait for this GPU's split-K partials
-      if (et >= 1 && et < p.S && !wait_flag(sym.flag_rs(c.rank, c.world + et - 1, tm), s, c.timeout_ns))
-        pm::report_error(c.err, pm::kPeerTimeout, 330 + et);
-      epi_sync();
-      if (p.prof && et == 0) t1 = pm::globaltimer_ns();
-      // 2. full local sum (fp32, split order) -> bf16 partial of this rank -> destination(s)
-      const int d_lo = p.one_shot ? 0 : owner, d_hi = p.one_shot ? c.world : owner + 1;
-      for (int id = et; id < nchunks; id += 128) {
-        const int row = id / (kTileN / 8), col = (id % (kTileN / 8)) * 8;
-        const int64_t off = (int64_t)(b0 + row) * p.N + n0 + col;
-        const float* src = stile + row * kSRow + col;
-        float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
-        for (int k2 = 1; k2 < p.S; ++k2) {
-          const float* lp = lpart + (int64_t)(k2 - 1) * c.recv_elems + off;
-          const float4 x = __ldcg(reinterpret_cast<const float4*>(lp)), y = __ldcg(reinterpret_cast<const float4*>(lp + 4));
-          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-          b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
-        }
-        const uint4 o = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
-        for (int d = d_lo; d < d_hi; ++d) *reinterpret_cast<uint4*>(sym.recv(d, c.rank, s) + off) = o;
+    }
+    epi_sync();
+    if (et == 0) st_release_gpu(sym.flag_rs(c.rank, c.world + ks, tm), s);
+    if (et < p.S && !wait_flag(sym.flag_rs(c.rank, c.world + et, tm), s, c.timeout_ns))
+      pm::report_error(c.err, pm::kPeerTimeout, 330 + et);
+    epi_sync();
+    if (p.prof && et == 0) t1 = pm::globaltimer_ns();
+    const int sw = kTileN / p.S;            // slice width (a multiple of 8)
+    const int sc = sw / 8;                  // 8-column chunks per slice row
+    const int slice = tm * p.S + ks;        // flag index of this slice
+    const int owner = slice % c.world;
+    const int nsl = rows * sc;
+    // 2. split sum (fp32, split order) -> bf16 partial of this rank -> destination(s)
+    const int d_lo = p.one_shot ? 0 : owner, d_hi = p.one_shot ? c.world : owner + 1;
+    for (int id = et; id < nsl; id += 128) {
+      const int row = id / sc, col = ks * sw + (id % sc) * 8;
+      const int64_t off = (int64_t)(b0 + row) * p.N + n0 + col;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      for (int k2 = 0; k2 < p.S; ++k2) {
+        const float* lp = lpart + (int64_t)k2 * c.recv_elems + off;
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(lp)), y = __ldcg(reinterpret_cast<const float4*>(lp + 4));
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
       }
+      const uint4 o = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+      for (int d = d_lo; d < d_hi; ++d) *reinterpret_cast<uint4*>(sym.recv(d, c.rank, s) + off) = o;
+    }
+    epi_sync();
+    if (et < d_hi - d_lo) st_release_sys(sym.flag_rs(d_lo + et, c.rank, slice), s);
+    if (p.prof && et == 0) t2 = pm::globaltimer_ns();
+    // 3. reduce the slice over ranks in rank order (every rank computes identical bits)
+    if (p.one_shot || c.rank == owner) {
+      if (et < c.world && !wait_flag(sym.flag_rs(c.rank, et, slice), s, c.timeout_ns))
+        pm::report_error(c.err, pm::kPeerTimeout, 310 + et);
       epi_sync();
-      if (et < d_hi - d_lo) st_release_sys(sym.flag_rs(d_lo + et, c.rank, tm), s);
-      if (p.prof && et == 0) t2 = pm::globaltimer_ns();
-      // 3. reduce over ranks in rank order (every rank computes identical bits)
-      if (p.one_shot || c.rank == owner) {
-        if (et < c.world && !wait_flag(sym.flag_rs(c.rank, et, tm), s, c.timeout_ns))
-          pm::report_error(c.err, pm::kPeerTimeout, 310 + et);
-        epi_sync();
-        for (int id = et; id < nchunks; id += 128) {
-          const int64_t off = (int64_t)(b0 + id / (kTileN / 8)) * p.N + n0 + (id % (kTileN / 8)) * 8;
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int sr = 0; sr < c.world; ++sr) add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr, s) + off)));
-          const uint4 o = pack8(acc);
-          if (p.one_shot) {
-            *reinterpret_cast<uint4*>(p.out + off) = o;
-          } else {
-            for (int d = 0; d < c.world; ++d) *reinterpret_cast<uint4*>(sym.gath(d) + off) = o;
-          }
-        }
-        if (!p.one_shot) {
-          epi_sync();
-          if (et < c.world) st_release_sys(sym.flag_ag(et, tm), s);
+      for (int id = et; id < nsl; id += 128) {
+        const int64_t off = (int64_t)(b0 + id / sc) * p.N + n0 + ks * sw + (id % sc) * 8;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int sr = 0; sr < c.world; ++sr) add_bf16x8(acc, __ldcg(reinterpret_cast<const uint4*>(sym.recv(c.rank, sr, s) + off)));
+        const uint4 o = pack8(acc);
+        if (p.one_shot) {
+          *reinterpret_cast<uint4*>(p.out + off) = o;
+        } else {
+          for (int d = 0; d < c.world; ++d) *reinterpret_cast<uint4*>(sym.gath(d) + off) = o;
         }
       }
       if (!p.one_shot) {
-        // 4. two-shot: every rank copies the gathered tile out
-        if (et == 0 && !wait_flag(sym.flag_ag(c.rank, tm), s, c.timeout_ns))
-          pm::report_error(c.err, pm::kPeerTimeout, 309);
         epi_sync();
-        for (int id = et; id < nchunks; id += 128) {
-          const int64_t off = (int64_t)(b0 + id / (kTileN / 8)) * p.N + n0 + (id % (kTileN / 8)) * 8;
-          *reinterpret_cast<uint4*>(p.out + off) = __ldcg(reinterpret_cast<const uint4*>(sym.gath(c.rank) + off));
-        }
+        if (et < c.world) st_release_sys(sym.flag_ag(et, slice), s);
       }
-      if (p.prof && et == 0) {
-        t3 = pm::globaltimer_ns();
-        atomicAdd(p.prof + 0, (unsigned long long)(t1 - t0));
-        atomicAdd(p.prof + 1, (unsigned long long)(t2 - t1));
-        atomicAdd(p.prof + 2, (unsigned long long)(t3 - t2));
-        atomicAdd(p.prof + 3, 1ull);
-        atomicMax(p.prof + 4, (unsigned long long)(t3 - t0));
+    }
+    if (!p.one_shot) {
+      // 4. two-shot: every rank copies the gathered slice out
+      if (et == 0 && !wait_flag(sym.flag_ag(c.rank, slice), s, c.timeout_ns))
+        pm::report_error(c.err, pm::kPeerTimeout, 309);
+      epi_sync();
+      for (int id = et; id < nsl; id += 128) {
+        const int64_t off = (int64_t)(b0 + id / sc) * p.N + n0 + ks * sw + (id % sc) * 8;
+        *reinterpret_cast<uint4*>(p.out + off) = __ldcg(reinterpret_cast<const uint4*>(sym.gath(c.rank) + off));
       }
+    }
+    if (p.prof && et == 0) {
+      t3 = pm::globaltimer_ns();
+      atomicAdd(p.prof + 0, (unsigned long long)(t1 - t0));
+      atomicAdd(p.prof + 1, (unsigned long long)(t2 - t1));
+      atomicAdd(p.prof + 2, (unsigned long long)(t3 - t2));
+      atomicAdd(p.prof + 3, 1ull);
+      atomicMax(p.prof + 4, (unsigned long long)(t3 - t0));
     }
   }
   pm::tc_fence_before();
@@ -368,7 +371,7 @@ int launch_gemm_allreduce(const GemmArParams& p, const void* w, const void* x, i
       p.stages < 2 || p.stages > kMaxStages || p.stages * kStageBytes < 128 * kSRow * 4)
     return 1;
   const int ntm = p.N / kTileN * p.nmb;
-  if (ntm * p.S > num_sms || ntm > p.c.max_tiles || p.c.world + p.S - 1 > p.c.max_src ||
+  if (ntm * p.S > num_sms || ntm * p.S > p.c.max_tiles || p.c.world + p.S > p.c.max_src || kTileN % (8 * p.S) ||
       (int64_t)p.N * p.B > p.c.recv_elems)
     return 2;
   alignas(64) CUtensorMap mw, mx;

@@ -1,7 +1,7 @@
 // Sparse-attention indexer on tcgen05: FP8 index keys, per-query top-k C4 records.
 //
-// Reference behaviour: the DSV4 indexer selects the top-512 C4 records per query (K12;
-// `srt/layers/attention/dsv4/indexer.py`, server `dsa_topk_backend "sgl-kernel"`, FP8 indexer by
+// Reference behaviour: the DSV4 indexer selects the top-512 C4 records per query
+// (`srt/layers/attention/dsv4/indexer.py`, server `dsa_topk_backend "sgl-kernel"`, FP8 indexer by
 // default: `enable_deepseek_v4_fp4_indexer false`).  Score of record r for query b:
 //     score(b, r) = sum_h w[b, h] * relu(q[b, h] . k[r])
 // Key storage (one row per C4 record, same physical id as the C4 KV record): 128 E4M3 codes

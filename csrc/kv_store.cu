@@ -6,8 +6,8 @@
 // squares rounded then summed in (j, i) order, butterfly over lanes, r = 1/sqrt(ss/512 + eps)
 // with IEEE ops, y = bf16((x*r)*w), UE8M0 from the exact exponent rule, E4M3 via cvt.rn.satfinite.
 //
-// Reference behaviour: Native store = `fused_norm_rope_flashmla` (K4), Packed store =
-// `_pack_fused_fp32_kernel` (K5) (third_party/README.md:257; docs/agents/numerical-and-validation.md:22-26).
+// Reference behaviour: Native store = `fused_norm_rope_flashmla`, Packed store =
+// `_pack_fused_fp32_kernel` (third_party/README.md:257; docs/agents/numerical-and-validation.md:22-26).
 #include "launchers.h"
 #include "common/sm100.cuh"
 

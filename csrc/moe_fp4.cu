@@ -1,6 +1,6 @@
 // MXFP4 routed experts for decode-sized batches (memory-bound on the expert weights).
 //
-// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod` (K18; server log
+// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod` (server log
 // "Preparing DSv4 MXFP4 experts").  Weights: E2M1 nibbles (low nibble = even k) with one
 // UE8M0 scale per 32 consecutive k; activations BF16.
 //

@@ -1,6 +1,6 @@
 // MXFP4 routed experts for decode-sized token counts (<= 16 tokens per expert per pass).
 //
-// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod` (K18).  At decode batch sizes
+// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod`.  At decode batch sizes
 // an expert sees ~1-4 tokens, so the layer is a stream of the active experts' E2M1 weights.  The
 // tcgen05 kernel (moe_fp4_tc.cu) pays ~110 cycles per M=128/N=16/K=16 MMA with its weight operand
 // in tensor memory, i.e. ~1 us per 16 KB weight tile, 2.6x the HBM time of the tile.  This kernel

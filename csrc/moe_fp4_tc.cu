@@ -1,6 +1,6 @@
 // MXFP4 routed experts on tcgen05 with the weight operand in tensor memory.
 //
-// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod` (K18), which also re-lays out
+// Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod`, which also re-lays out
 // the MXFP4 experts at load time ("Preparing DSv4 MXFP4 experts" in the serve log).  Weights are
 // E2M1 nibbles (low nibble = even k) with one UE8M0 scale per 32 k; activations BF16 (FP16 here).
 //

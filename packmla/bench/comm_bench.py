@@ -99,7 +99,7 @@ def main() -> None:
             link = ((world - 1) * out_bytes if shot else 2 * (world - 1) / world * out_bytes) / (NVLINK_GBS * 1e3)
             for sp in args.splits:
                 s = sp or choose_splits(hidden, K, B)
-                if K % (64 * s) or (hidden // 256) * -(-B // 128) * s > comm.num_sms or world + s - 1 > comm.max_src:
+                if K % (64 * s) or (hidden // 256) * -(-B // 128) * s > comm.num_sms or world + s > comm.max_src:
                     continue
                 t_f = _graph_time(lambda: comm.gemm_all_reduce(x, w, s, one), args.calls, args.replays)
                 prof = torch.zeros(8, dtype=torch.int64, device=dev)

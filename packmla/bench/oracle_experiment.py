@@ -2,7 +2,7 @@
 
     python -m packmla.bench.oracle_experiment [--batch 4 --heads 64 --context 8192 --topk 512 --seed 0]
 
-Setup (the BASELINE.json CPU config): latent rows ~ N(0, 1) of width 512 (448 NoPE coordinates stored
+Setup (the reference's CPU format experiment): latent rows ~ N(0, 1) of width 512 (448 NoPE coordinates stored
 as E4M3 with per-64-coordinate UE8M0 scales, 64 RoPE coordinates in BF16); queries ~ N(0, 1) / sqrt(576);
 a context of `context` tokens compressed 4:1 into C4 records; a fixed seeded mask keeps all 64 RoPE
 coordinates plus 192 seeded NoPE coordinates (256 of 512).  Every record is written as a Native 584 B

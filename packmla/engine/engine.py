@@ -7,7 +7,7 @@ Public API (what the HTTP server and bench.py call):
     while eng.has_work(): eng.step()                             # one prefill chunk or one decode step
     eng.result(rid).output_ids
 
-Reference behaviour: SGLang scheduler + `decode_cuda_graph_runner.py` (R8, third_party/README.md:294-298):
+Reference behaviour: SGLang scheduler + `decode_cuda_graph_runner.py` (third_party/README.md:294-298):
 chunked prefill (8192), full decode CUDA graphs for padded batch sizes, FCFS admission bounded by
 the KV pool.  Multi-rank: every rank runs the same deterministic schedule in lockstep; logits are
 identical on all ranks after the all-reduces, so sampling needs no broadcast.

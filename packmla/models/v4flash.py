@@ -11,7 +11,7 @@ Per layer (decode, B tokens of B different requests):
   kv -> Native record in the layer's SWA ring (norm kv_norm, RoPE at the token position)
   compressor (ratio 4 / 128): online-softmax pooling of h Wc_kv with gates h Wc_gate + ape;
      a completed group -> C4 record (Native or Packed store) / C128 record (Native)
-  indexer (C4): score(r) = sum_h w_h relu(q_idx_h . k_r), top-512 records (k_r FP8, pooled like kv)
+  indexer: score(r) = sum_h w_h relu(q_idx_h . k_r), top-512 records (k_r FP8, pooled like kv)
   o = sparse MLA attention over [SWA ring ; selected C4 | all C128 records] with sink
   x += (o grouped-projected by Wo_a, then Wo_b)              -> TP all-reduce
   x += shared(rmsnorm(x)) + sum_k w_k expert_k(rmsnorm(x))   -> TP/EP all-reduce

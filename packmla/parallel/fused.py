@@ -70,7 +70,8 @@ class SymmetricBuffer:
 
 def choose_splits(n: int, k: int, tokens: int, num_sms: int = NUM_SMS_B200, max_splits: int = 8) -> int:
     """K splits per output tile: enough CTAs to stream the weights from every SM.  Split partials are
-    added on this GPU before anything crosses NVLink, so splitting costs no link traffic."""
+    added on this GPU (each split CTA sums one column slice) before anything crosses NVLink, so
+    splitting costs no link traffic."""
     tiles = (n // TILE_N) * -(-tokens // 128)
     best = 1
     for s in (2, 4, 8):
@@ -104,7 +105,7 @@ class FusedComm(TPComm):
         self.device = device
         self.hidden = hidden
         self.max_splits = max_splits
-        self.max_src = self.world + max_splits - 1  # cross-rank partials + this GPU's split-K partials
+        self.max_src = self.world + max_splits  # flag slots: cross-rank partials + this GPU's split-K partials
         self.max_tiles = 256
         self.recv_elems = hidden * MAX_BPAD
         recv_bytes = 2 * self.max_src * self.recv_elems * 2  # two call parities
@@ -123,7 +124,7 @@ class FusedComm(TPComm):
         off += flag_ag
         off = -(-off // 256) * 256
         lpart_off = off
-        off += (max_splits - 1) * self.recv_elems * 4
+        off += max_splits * self.recv_elems * 4
         self.layout = [recv_off, self.recv_elems, gath_off, flag_rs_off, flag_ag_off, self.max_src, self.max_tiles,
                        lpart_off]
         self.buf = SymmetricBuffer(off, device, group)

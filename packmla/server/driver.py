@@ -1,6 +1,6 @@
 """Engine driver: the one thread that owns an `Engine`, fed by HTTP handlers through queues.
 
-Reference behaviour (SGLang scheduler process behind the tokenizer manager, R8/R9): requests enter a
+Reference behaviour (SGLang scheduler process behind the tokenizer manager): requests enter a
 queue, the scheduler loop admits them and steps the model, and tokens stream back per request.
 Here the loop runs on a thread of the server process; handlers await per-request asyncio queues
 that the loop fills with `loop.call_soon_threadsafe`.

@@ -1,9 +1,9 @@
 """Reference math for training and evaluation, built on packmla's fp32 oracle.
 
 The reference loads these functions from its SGLang fork's calibration runner (`calibrate.py`:
-normalize / attention / rotate / decode_native / atomic_json / reference(), SURVEY R11) and its
+normalize / attention / rotate / decode_native / atomic_json / reference()) and its
 reference codec (`srt/remnant/reference.py`: pack_rows_ref / unpack_rows_ref / topmag_keep_mask /
-_ue8m0_quantize, R3).  packmla's codec (packmla.formats.codec) is the byte-exact oracle of its own
+_ue8m0_quantize).  packmla's codec (packmla.formats.codec) is the byte-exact oracle of its own
 store kernels, so training, evaluation and serving share one codec.
 """
 from __future__ import annotations

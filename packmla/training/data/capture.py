@@ -1,7 +1,7 @@
 """Capture observer and cache builder: training states from packmla's own model.
 
 Reference: the opt-in capture observer of the serving fork (`srt/remnant/capture.py`, hooks
-`observe_raw` / `observe_attention` in the compressor and attention backend, R10) records raw C4
+`observe_raw` / `observe_attention` in the compressor and attention backend) records raw C4
 latents and decode queries of a Native-format server, and `training/data/dataset.py` turns them into
 training states.  Here `CaptureObserver` attaches to `V4FlashModel.observer`:
 
