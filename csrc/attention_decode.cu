@@ -217,39 +217,43 @@ __device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, 
       *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) = o;
     }
   } else if (R.kind == 3) {
+    // lane v expands unit v of every 64-coordinate word i (coordinates 64 i + 8 v .. + 7): each lane
+    // rotates exactly one RoPE unit (word 7) and the seven NoPE units skip the rotation, with the
+    // branch uniform across the warp
     const uint64_t* words = reinterpret_cast<const uint64_t*>(srow + 256);
-    int rank = 0;
-    for (int w = 0; w < v; ++w) rank += __popcll(words[w]);
-    const uint64_t word = words[v];
-    const float s = pm::exp2i((int)srow[320 + v] - 127);
-    const float* cs = reinterpret_cast<const float*>(srow + 336);
-    const bool tail = v == 7;
-    // one instruction path for all lanes (no divergence): every unit goes through the rotation, with
-    // (cos, sin) = (1, 0) outside the RoPE tail, which returns the BF16-rounded value unchanged
+    const uint64_t below = (1ull << (8 * v)) - 1ull;  // bits of the word before this lane's unit
+    int prefix = 0;                                    // kept values before word i
 #pragma unroll 2
-    for (int u = 0; u < 8; ++u) {
-      const uint32_t bits = (uint32_t)(word >> (8 * u)) & 0xFFu;
+    for (int i = 0; i < 8; ++i) {
+      const uint64_t word = words[i];
+      const uint32_t bits = (uint32_t)(word >> (8 * v)) & 0xFFu;
+      const int rank = prefix + __popcll(word & below);
+      prefix += __popcll(word);
       // the 8 value bytes from `rank` (reads may run past the values into the staged bitmap: masked)
       const uint32_t* vw = reinterpret_cast<const uint32_t*>(srow + (rank & ~3));
       const uint32_t sh = 8u * (uint32_t)(rank & 3);
       const uint32_t lo = __funnelshift_r(vw[0], vw[1], sh), hi = __funnelshift_r(vw[1], vw[2], sh);
       const uint4 e = expand_lut[bits];
       const uint2 codes = make_uint2(__byte_perm(lo, hi, e.x) & e.z, __byte_perm(lo, hi, e.y) & e.w);
-      rank += __popc(bits);
       float f[8];
-      dequant8f(codes, s, f);
-      const float4 cs01 = tail ? *reinterpret_cast<const float4*>(cs + 8 * u) : make_float4(1.f, 0.f, 1.f, 0.f);
-      const float4 cs23 = tail ? *reinterpret_cast<const float4*>(cs + 8 * u + 4) : make_float4(1.f, 0.f, 1.f, 0.f);
-      const float cc[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, ss[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
+      dequant8f(codes, pm::exp2i((int)srow[320 + i] - 127), f);
       __nv_bfloat162 o2[4];
+      if (i < 7) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {  // pair index 4 u + i of the table row
-        const float re = __bfloat162float(__float2bfloat16_rn(f[2 * i]));
-        const float im = __bfloat162float(__float2bfloat16_rn(f[2 * i + 1]));
-        o2[i] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(re, cc[i]), __fmul_rn(im, ss[i])),
-                                      __fadd_rn(__fmul_rn(re, ss[i]), __fmul_rn(im, cc[i])));
+        for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+      } else {
+        const float* cs = reinterpret_cast<const float*>(srow + 336) + 8 * v;  // pairs 4 v .. 4 v + 3
+        const float4 cs01 = *reinterpret_cast<const float4*>(cs), cs23 = *reinterpret_cast<const float4*>(cs + 4);
+        const float cc[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, ss[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float re = __bfloat162float(__float2bfloat16_rn(f[2 * k]));
+          const float im = __bfloat162float(__float2bfloat16_rn(f[2 * k + 1]));
+          o2[k] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(re, cc[k]), __fmul_rn(im, ss[k])),
+                                        __fadd_rn(__fmul_rn(re, ss[k]), __fmul_rn(im, cc[k])));
+        }
       }
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) =
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) =
           *reinterpret_cast<uint4*>(o2);
     }
   } else {
