@@ -209,12 +209,15 @@ __device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, 
   __syncwarp();
   if (v == 0) rowvalid[trow] = R.kind != 0;
   if (R.kind == 1 || R.kind == 2) {
-    const float s = v < 7 ? pm::exp2i((int)srow[576 + v] - 127) : 1.f;
+    // lane v expands unit v of every 64-coordinate word i: seven dequantized NoPE units and one copied
+    // (already rotated) BF16 tail unit per lane, uniform across the warp; the 8 lanes of a row store
+    // 128 contiguous bytes per word
 #pragma unroll 2
-    for (int u = 0; u < 8; ++u) {
-      const uint4 o = v < 7 ? dequant8(*reinterpret_cast<const uint2*>(srow + 64 * v + 8 * u), s)
-                            : *reinterpret_cast<const uint4*>(srow + 448 + 16 * u);
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) = o;
+    for (int i = 0; i < 8; ++i) {
+      const uint4 o = i < 7 ? dequant8(*reinterpret_cast<const uint2*>(srow + 64 * i + 8 * v),
+                                       pm::exp2i((int)srow[576 + i] - 127))
+                            : *reinterpret_cast<const uint4*>(srow + 448 + 16 * v);
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) = o;
     }
   } else if (R.kind == 3) {
     // lane v expands unit v of every 64-coordinate word i (coordinates 64 i + 8 v .. + 7): each lane
@@ -258,8 +261,8 @@ __device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, 
     }
   } else {
 #pragma unroll 2
-    for (int u = 0; u < 8; ++u)
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * v + u), kTile * 128)) = zero4();
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) = zero4();
   }
   __syncwarp();
 }
