@@ -321,6 +321,49 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   const int b = unit / (p.num_splits * p.num_groups);
   const int h0 = g * kHG;
 
+  const int nswa = min(p.swa_len[b], p.swa_cap);
+  const int ntot = nswa + min(p.csa_len[b], p.csa_cap);
+  // this query's rows split into whole tiles of `trows` rows (128, or 64 when a small batch needs more
+  // CTAs), as evenly as the split count allows; a 64-row tile leaves MMA rows 64-127 zero and masked
+  const int trows = p.tile_rows == 64 ? 64 : kTile;
+  const int tiles_q = (ntot + trows - 1) / trows;
+  const int tiles_per_split = (tiles_q + p.num_splits - 1) / p.num_splits;
+  const int row0 = split * tiles_per_split * trows;
+  const int row1 = min(ntot, row0 + tiles_per_split * trows);
+  const int ntiles = row1 > row0 ? (row1 - row0 + trows - 1) / trows : 0;
+
+  uint8_t* srow = smem + kOffStage + warp * kStageBytes + (lane >> 3) * kStageRow;
+  const int v8 = lane & 7;
+  // step k of a tile: rows 4 warp + lane / 8 + 32 k
+  auto step_row = [&](int k) { return 4 * warp + (lane >> 3) + 32 * k; };
+  // row references of the 4 steps of tile tt (4 independent index loads in flight together)
+  RowRef rr[4];
+  auto resolve = [&](int tt) {
+    const int tb = row0 + tt * trows, tv = min(trows, row1 - tb);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rr[k] = step_ref(p, b, tb, tv, nswa, ntot, step_row(k));
+  };
+  // four register sets, one per gather step: all record loads of a tile are in flight together, and the
+  // loads of tile t + 1 are issued while the P.V MMAs of tile t run; no register copy ever waits on loads
+  // still in flight
+  StepRegs ra, rb, rc, rd;
+  auto fetch_all = [&](int n) {
+    fetch_step(p, rr[0], v8, ra);
+    fetch_step(p, rr[1], v8, rb);
+    if (n == 4) {
+      fetch_step(p, rr[2], v8, rc);
+      fetch_step(p, rr[3], v8, rd);
+    }
+  };
+
+  // tile 0's index and record loads go out first: their latency overlaps the TMEM allocation, the
+  // LUT set-up and the Q load below
+  if (ntiles > 0) {
+    resolve(0);
+    fetch_all(4);
+  }
+  __syncwarp();  // the lanes took row-dependent branches; tcgen05.alloc is warp-collective
+
   if (warp == 0) {
     pm::tmem_alloc(tmem_slot, kTmemCols);
     pm::tmem_relinquish();
@@ -357,54 +400,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   pm::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int nswa = min(p.swa_len[b], p.swa_cap);
-  const int ntot = nswa + min(p.csa_len[b], p.csa_cap);
-  // this query's rows split into whole tiles of `trows` rows (128, or 64 when a small batch needs more
-  // CTAs), as evenly as the split count allows; a 64-row tile leaves MMA rows 64-127 zero and masked
-  const int trows = p.tile_rows == 64 ? 64 : kTile;
-  const int tiles_q = (ntot + trows - 1) / trows;
-  const int tiles_per_split = (tiles_q + p.num_splits - 1) / p.num_splits;
-  const int row0 = split * tiles_per_split * trows;
-  const int row1 = min(ntot, row0 + tiles_per_split * trows);
-  const int ntiles = row1 > row0 ? (row1 - row0 + trows - 1) / trows : 0;
-
   mark(0);
   const uint32_t q_base = pm::smem_u32(sQ), kv_base = pm::smem_u32(sKV), p_base = pm::smem_u32(sP);
   const uint32_t idesc_s = pm::make_idesc_f16(128, kHG, 1, 0, 0);
   const uint32_t idesc_o = pm::make_idesc_f16(128, kHG, 1, 1, 1);
   bool ok = true;
 
-  uint8_t* srow = smem + kOffStage + warp * kStageBytes + (lane >> 3) * kStageRow;
-  const int v8 = lane & 7;
-  // step k of a tile: rows 4 warp + lane / 8 + 32 k
-  auto step_row = [&](int k) { return 4 * warp + (lane >> 3) + 32 * k; };
-  // row references of the 4 steps of tile tt (4 independent index loads in flight together)
-  RowRef rr[4];
-  auto resolve = [&](int tt) {
-    const int tb = row0 + tt * trows, tv = min(trows, row1 - tb);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) rr[k] = step_ref(p, b, tb, tv, nswa, ntot, step_row(k));
-  };
-  // four register sets, one per gather step: all record loads of a tile are in flight together, and the
-  // loads of tile t + 1 are issued while the P.V MMAs of tile t run; no register copy ever waits on loads
-  // still in flight
-  StepRegs ra, rb, rc, rd;
-  auto fetch_all = [&](int n) {
-    fetch_step(p, rr[0], v8, ra);
-    fetch_step(p, rr[1], v8, rb);
-    if (n == 4) {
-      fetch_step(p, rr[2], v8, rc);
-      fetch_step(p, rr[3], v8, rd);
-    }
-  };
-
   for (int t = 0; t < ntiles && ok; ++t) {
     // ---- 1. gather + expand 128 rows (64-row tiles: steps 2-3 only on the first tile, zero rows)
-    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;
-    if (t == 0) {
-      resolve(0);
-      fetch_all(nsteps);
-    }
+    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;  // tile 0's loads were issued at set-up
     uint64_t tg = p.prof && tid == 0 ? pm::globaltimer_ns() : 0;
     auto sub = [&](int slot) {  // finer split of the gather for thread 0: [11] expand
       if (p.prof && tid == 0) {
