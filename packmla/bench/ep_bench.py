@@ -1,6 +1,7 @@
 """Expert-parallel MoE layer of the V4-Flash shape: dispatch / local experts / combine, per-phase time.
 
     torchrun --nproc-per-node N -m packmla.bench.ep_bench [--tokens 4096 --iters 5]
+    python -m packmla.bench.ep_bench                # one GPU: all experts local, no exchange
 
 Workload: every rank holds `tokens` tokens (hidden 4096, BF16) routed top-8 over 256 routed experts from
 seeded Gaussian gate logits (weights: softmax over the chosen 8), plus one shared expert (intermediate
@@ -60,9 +61,11 @@ def main() -> None:
         x = h @ shared_w13.T
         return (torch.nn.functional.silu(x[:, :I]) * x[:, I:]) @ shared_w2.T
 
+    multi = dist.is_initialized()
     total = None
     for it in range(a.iters + 1):
-        dist.barrier()
+        if multi:
+            dist.barrier()
         torch.cuda.synchronize(dev)
         box = {}
 
@@ -91,7 +94,8 @@ def main() -> None:
     res = {}
     for key, vals in phases.items():
         t = torch.tensor([sum(vals) / len(vals)], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if multi:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
         res[key + "_ms"] = round(float(t.item()), 3)
     sent = sum(c for r, c in enumerate(ep.last_counts["sent"]) if r != rank)
     if rank == 0:
@@ -100,8 +104,9 @@ def main() -> None:
                           **res, "tokens_per_s_per_rank": round(T / (res["total_ms"] / 1e3), 1),
                           "offrank_rows_sent_rank0": sent, "offrank_bytes_rank0": sent * H * 2 * 2,
                           "finite": bool(torch.isfinite(total).all())}), flush=True)
-    dist.barrier()
-    dist.destroy_process_group()
+    if multi:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
