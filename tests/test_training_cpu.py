@@ -138,4 +138,10 @@ def test_capture_train_evaluate_end_to_end(tmp_path):
                        str(tmp_path / "cmp.json"), "--compare-masks"])
     diag = evaluate.main(["--cache", str(tmp_path / "cache"), "--policy", out["policy"], "--output",
                           str(tmp_path / "diag.json")])
+    from packmla.training.data import storage
+
+    aud = storage.main(["--cache", str(tmp_path / "cache"), "--repeat", "1"])
+    lay = aud["layers"][str(layer)]
+    assert lay["states"] == {"train": 6, "development": 4}
+    assert lay["by_kind"]["raw"] == 10 * cfg.index_topk * 512 * 4 and 0 < lay["tensor_bytes"] <= lay["file_bytes"]
     assert diag["mean_learned"] <= diag["mean_topmag"] * 1.5
