@@ -135,6 +135,9 @@ class EngineConfig:
     mem_fraction_static: float = 0.88
     max_running_requests: int = 256
     chunked_prefill_size: int = 8192
+    # alternate prefill chunks and decode steps while both are pending (False: prefill first, as long as
+    # a waiting request fits)
+    prefill_decode_interleave: bool = True
     context_length: int = 1 << 20
     cuda_graph_bs: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16, 24, 32, 40, 48, 64, 96, 128])
     disable_cuda_graph: bool = False

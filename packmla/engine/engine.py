@@ -180,6 +180,7 @@ class Engine:
         self._h_out = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
+        self._last_prefill = False
         self.hicache = None
         if engine_cfg.enable_hierarchical_cache:
             from ..kv.hicache import HostKVCache
@@ -268,16 +269,25 @@ class Engine:
         return req
 
     def step(self) -> list[tuple[int, int]]:
-        """Run one prefill chunk (if a request is waiting and fits) or one decode step.
+        """Run one prefill chunk (if a request is waiting and fits) or one decode step; when both are
+        pending they alternate (`EngineConfig.prefill_decode_interleave`).
 
         Returns the (rid, token) pairs produced by this step.
         """
-        req = self._admit()
         rank = getattr(self.comm, "rank", 0)
+        # with both kinds of work pending, prefill chunks and decode steps alternate: a queue of long
+        # prompts must not stall the running requests' token streams for many steps
+        if self.running and self._last_prefill and self.ecfg.prefill_decode_interleave:
+            self._last_prefill = False
+            with nvtx_range(f"scheduler.batch rank={rank} decode b={len(self.running)}"):
+                return self._decode()
+        req = self._admit()
         if req is not None:
+            self._last_prefill = True
             with nvtx_range(f"scheduler.batch rank={rank} prefill rid={req.rid} start={req.prefilled}"):
                 return self._prefill_chunk(req)
         if self.running:
+            self._last_prefill = False
             with nvtx_range(f"scheduler.batch rank={rank} decode b={len(self.running)}"):
                 return self._decode()
         return []

@@ -101,3 +101,29 @@ def test_safetensors_checkpoint_round_trip(tmp_path):
     assert cfg2 == cfg and W2["meta"] == W["meta"]
     a, b = flatten(W), flatten(W2)
     assert set(a) == set(b) and all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_prefill_chunks_and_decode_steps_alternate():
+    """A long prompt arriving while a request decodes must not stall that request's tokens until its
+    whole prefill is done; the tokens themselves do not depend on the schedule."""
+    cfg = ModelConfig.tiny(num_layers=2)
+    g = torch.Generator().manual_seed(9)
+    short = torch.randint(0, cfg.vocab_size, (20,), generator=g).tolist()
+    long = torch.randint(0, cfg.vocab_size, (400,), generator=g).tolist()
+    outs = {}
+    for interleave in (True, False):
+        ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=2, cuda_graph_bs=[1, 2],
+                            prefill_decode_interleave=interleave)
+        eng = Engine.build(cfg, ecfg, "cpu", max_context=1024)
+        a = eng.add_request(short, SamplingParams(max_new_tokens=6))
+        eng.step()  # prefill of the short prompt: it is now decoding
+        b = eng.add_request(long, SamplingParams(max_new_tokens=2))
+        kinds = []
+        while eng.has_work():
+            before = eng.metrics.snapshot().get("decode_steps", 0)
+            eng.step()
+            kinds.append("d" if eng.metrics.snapshot().get("decode_steps", 0) > before else "p")
+        outs[interleave] = (eng.result(a).output_ids, eng.result(b).output_ids, "".join(kinds))
+    assert outs[True][:2] == outs[False][:2]
+    assert outs[True][2].startswith("dpdpdp")  # alternating while the long prompt is prefilled
+    assert outs[False][2].startswith("ppppppp")  # prefill first: the short request waits
