@@ -3,10 +3,13 @@
     python -m packmla.server --model tiny --device cpu --port 30000
     torchrun --nproc-per-node 4 -m packmla.server --model v4-flash --kv-cache-format direct --tp 4
 
-Flags mirror the reference's launcher (scripts/local/run-server.sh:55-139): --kv-cache-format
+Flags mirror the reference's launcher (scripts/local/run-server.sh:55-161): --kv-cache-format
 native|direct, --tp, --mem-fraction-static, --max-running-requests, --context-length,
 --chunked-prefill-size, --cuda-graph-bs, --disable-cuda-graph, --enable-hierarchical-cache,
---hicache-ratio, --moe-precision (the reference's flashinfer MXFP4 MoE precision option).
+--hicache-ratio, --moe-precision (the reference's flashinfer MXFP4 MoE precision option); the
+reference's own flag names (--model-path, --random-seed, --cuda-graph-config, --kv-cache-dtype,
+--moe-runner-backend, --ep, the --dsv4-c4-cache-* selectors, the HiCache policy flags, ...) are
+accepted and mapped by `resolve_args`, so a reference launch line runs unchanged.
 Rank 0 serves HTTP; the other ranks follow its schedule (packmla.server.driver).
 """
 from __future__ import annotations
@@ -18,7 +21,8 @@ import os
 
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m packmla.server")
-    ap.add_argument("--model", default="tiny", help="tiny | small | v4-flash | path to a packmla checkpoint")
+    ap.add_argument("--model", "--model-path", dest="model", default="tiny",
+                    help="tiny | small | v4-flash | path to a packmla checkpoint")
     ap.add_argument("--served-model-name", default=None)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=30000)
@@ -36,8 +40,80 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--moe-precision", default="default", choices=["default", "bf16"])
     ap.add_argument("--decode-impl", default="direct", choices=["direct", "adapter"])
     ap.add_argument("--collectives", default="fused", choices=["fused", "nccl"])
-    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--seed", "--random-seed", dest="seed", type=int, default=0)
+    ap.add_argument("--watchdog-timeout", type=float, default=1800.0,
+                    help="seconds one engine step may take before /health reports the server unhealthy")
+    ap.add_argument("--no-prefill-decode-interleave", action="store_true",
+                    help="run waiting prefills before decode steps instead of alternating them")
+    ap.add_argument("--max-total-tokens", type=int, default=None, help="cap the KV pool at this many tokens")
+    # the reference launcher's flags (scripts/local/run-server.sh:55-161), mapped onto packmla's options
+    ref = ap.add_argument_group("reference launcher flags")
+    ref.add_argument("--kv-cache-dtype", default="fp8_e4m3", choices=["fp8_e4m3"],
+                     help="C4 records are E4M3 + UE8M0 (the only supported cache dtype)")
+    ref.add_argument("--cuda-graph-config", default=None,
+                     help='JSON such as {"decode": {"backend": "full", "bs": [1, 2, 4]}, "prefill": {"backend": '
+                          '"disabled"}}: decode graph batch sizes, or "disabled"')
+    ref.add_argument("--moe-runner-backend", default="flashinfer_mxfp4", choices=["flashinfer_mxfp4"],
+                     help="MXFP4 experts (packmla's tcgen05 MXFP4 x MXFP8 kernel)")
+    ref.add_argument("--ep", "--ep-size", dest="ep", type=int, default=None,
+                     help="expert-parallel size; packmla shards experts over the TP ranks, so it must equal --tp")
+    ref.add_argument("--dsv4-c4-cache-format", default=None, choices=["native", "remnant"],
+                     help="older selector: remnant = --kv-cache-format direct")
+    ref.add_argument("--dsv4-c4-cache-implementation", default=None, choices=["kernel", "adapter"],
+                     help="kernel = Direct Packed attention, adapter = Packed rows rebuilt as Native records")
+    ref.add_argument("--dsv4-c4-cache-store-implementation", default="kernel", choices=["kernel"],
+                     help="Packed records are written by the fused CUDA store kernel")
+    ref.add_argument("--dsv4-c4-cache-keep-count", type=int, default=256)
+    ref.add_argument("--dsv4-c4-cache-layer-keep-counts", default=None,
+                     help="per-layer survivor counts: evaluation only (packmla.training.evaluate "
+                          "--retention-sweep); serving accepts 256 for every layer")
+    ref.add_argument("--hicache-io-backend", default="kernel", choices=["kernel", "direct"],
+                     help="both move pages with packmla's segment-copy kernel")
+    ref.add_argument("--hicache-mem-layout", default="page_first", choices=["page_first", "layer_first"],
+                     help="accepted; packmla's host tier is page-first")
+    ref.add_argument("--hicache-write-policy", default="write_through", choices=["write_through"])
+    for flag in ("--enable-metrics", "--log-requests", "--skip-server-warmup", "--trust-remote-code",
+                 "--disable-radix-cache", "--disable-overlap-schedule", "--disable-flashinfer-autotune",
+                 "--language-model-only"):
+        ref.add_argument(flag, action="store_true", help="accepted; no effect in packmla")
+    for flag in ("--log-requests-level", "--export-metrics-to-file-dir", "--reasoning-parser", "--tool-call-parser",
+                 "--model-type", "--dsa-decode-backend", "--dsa-prefill-backend", "--dsv4-attn-backend"):
+        ref.add_argument(flag, default=None, help="accepted; no effect in packmla")
+    ref.add_argument("--export-metrics-to-file", action="store_true", help="accepted; no effect in packmla")
     return ap
+
+
+def resolve_args(args) -> dict:
+    """EngineConfig settings of the parsed flags (reference flags folded in); raises SystemExit on a
+    combination packmla does not serve."""
+    fmt = args.kv_cache_format
+    if args.dsv4_c4_cache_format is not None:
+        fmt = "direct" if args.dsv4_c4_cache_format == "remnant" else "native"
+    impl = args.decode_impl
+    if args.dsv4_c4_cache_implementation is not None:
+        impl = "adapter" if args.dsv4_c4_cache_implementation == "adapter" else "direct"
+    if args.ep is not None and args.ep != args.tp:
+        raise SystemExit(f"--ep {args.ep}: packmla shards the routed experts over the TP ranks (EP = TP = {args.tp})")
+    if args.dsv4_c4_cache_layer_keep_counts:
+        counts = {int(x.split(":")[-1]) for x in args.dsv4_c4_cache_layer_keep_counts.replace(" ", "").split(",") if x}
+        if counts != {256}:
+            raise SystemExit("per-layer keep counts other than 256 are evaluation-only "
+                             "(python -m packmla.training.evaluate --retention-sweep)")
+    kw = dict(kv_cache_format=fmt, decode_impl=impl, keep_count=args.dsv4_c4_cache_keep_count,
+              prefill_decode_interleave=not args.no_prefill_decode_interleave)
+    disable_graphs = args.disable_cuda_graph or args.device == "cpu"
+    bs = args.cuda_graph_bs
+    if args.cuda_graph_config:
+        gc = json.loads(args.cuda_graph_config)
+        dec = gc.get("decode", {})
+        if dec.get("backend", "full") == "disabled":
+            disable_graphs = True
+        elif dec.get("bs"):
+            bs = [int(b) for b in dec["bs"]]
+    if bs:
+        kw["cuda_graph_bs"] = bs
+    kw["disable_cuda_graph"] = disable_graphs
+    return kw
 
 
 def model_config(name: str):
@@ -65,21 +141,27 @@ def build_engine(args, rank: int, local: int, world: int, comm):
     from ..engine.engine import Engine
 
     cfg, W = model_config(args.model)
-    kw = {}
-    if args.cuda_graph_bs:
-        kw["cuda_graph_bs"] = args.cuda_graph_bs
-    ecfg = EngineConfig(kv_cache_format=args.kv_cache_format, tp=world, ep=world,
-                        mem_fraction_static=args.mem_fraction_static, max_running_requests=args.max_running_requests,
+    ecfg = EngineConfig(tp=world, ep=world, mem_fraction_static=args.mem_fraction_static,
+                        max_running_requests=args.max_running_requests,
                         chunked_prefill_size=args.chunked_prefill_size, context_length=args.context_length,
-                        disable_cuda_graph=args.disable_cuda_graph or args.device == "cpu",
                         enable_hierarchical_cache=args.enable_hierarchical_cache, hicache_ratio=args.hicache_ratio,
-                        moe_precision=args.moe_precision, decode_impl=args.decode_impl, device=args.device,
-                        random_seed=args.seed, **kw)
+                        moe_precision=args.moe_precision, device=args.device, random_seed=args.seed,
+                        **resolve_args(args))
+    try:
+        ecfg.validate()
+    except ValueError as exc:
+        raise SystemExit(f"unsupported configuration: {exc}") from exc
     dev = torch.device(args.device, local) if args.device == "cuda" else torch.device("cpu")
     if W is not None and dev.type == "cuda":
         W = {"layers": [{k: v.to(dev) for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
              **{k: v.to(dev) for k, v in W.items() if torch.is_tensor(v)}}
     kv_bytes = None if dev.type == "cuda" else 256 << 20
+    if args.max_total_tokens:
+        from ..kv.pool import bytes_per_full_token, fixed_bytes
+
+        kv_bytes = int(args.max_total_tokens * bytes_per_full_token(cfg, ecfg.kv_cache_format,
+                                                                    ecfg.swa_full_tokens_ratio)
+                       + fixed_bytes(cfg, args.max_running_requests + 1))
     eng = Engine.build(cfg, ecfg, dev, rank, world, comm, max_context=args.context_length,
                        max_requests=args.max_running_requests, kv_bytes=kv_bytes, seed=args.seed, weights=W)
     if dev.type == "cuda" and not ecfg.disable_cuda_graph:
@@ -110,7 +192,7 @@ def main(argv=None) -> None:
         else:
             comm = TPComm()
     eng, ecfg = build_engine(args, rank, local, world, comm)
-    driver = EngineDriver(eng, rank, world, cpu_group)
+    driver = EngineDriver(eng, rank, world, cpu_group, watchdog_s=args.watchdog_timeout)
     name = args.served_model_name or os.path.basename(str(args.model))
     if rank != 0:
         driver.run_worker()

@@ -1,0 +1,46 @@
+"""CPU: the server launcher accepts the reference launcher's flags and maps them onto packmla's options."""
+import json
+
+import pytest
+
+from packmla.config import EngineConfig
+from packmla.server.__main__ import build_parser, resolve_args
+
+GRAPHS = {"decode": {"backend": "full", "max_bs": 136, "bs": [1, 2, 4, 8, 16]}, "prefill": {"backend": "disabled"}}
+
+
+def _resolve(*argv):
+    args = build_parser().parse_args(list(argv))
+    return args, resolve_args(args)
+
+
+def test_reference_launch_line_maps_onto_engine_config():
+    args, kw = _resolve("--model-path", "v4-flash", "--tp", "4", "--ep", "4", "--kv-cache-dtype", "fp8_e4m3",
+                        "--cuda-graph-config", json.dumps(GRAPHS), "--watchdog-timeout", "1800",
+                        "--moe-runner-backend", "flashinfer_mxfp4", "--dsv4-c4-cache-format", "remnant",
+                        "--dsv4-c4-cache-implementation", "kernel", "--dsv4-c4-cache-keep-count", "256",
+                        "--enable-hierarchical-cache", "--hicache-ratio", "2.0", "--hicache-write-policy",
+                        "write_through", "--hicache-io-backend", "kernel", "--hicache-mem-layout", "layer_first",
+                        "--enable-metrics", "--log-requests", "--random-seed", "7", "--max-running-requests", "40",
+                        "--device", "cpu")
+    assert args.model == "v4-flash" and args.seed == 7 and args.watchdog_timeout == 1800
+    assert kw["kv_cache_format"] == "direct" and kw["decode_impl"] == "direct" and kw["keep_count"] == 256
+    assert kw["cuda_graph_bs"] == [1, 2, 4, 8, 16] and kw["disable_cuda_graph"]  # CPU: no graphs
+    EngineConfig(tp=4, ep=4, enable_hierarchical_cache=True, **kw).validate()
+
+
+def test_selectors_and_rejections():
+    _, kw = _resolve("--dsv4-c4-cache-format", "native", "--device", "cuda",
+                     "--cuda-graph-config", json.dumps({"decode": {"backend": "disabled"}}))
+    assert kw["kv_cache_format"] == "native" and kw["disable_cuda_graph"]
+    _, kw = _resolve("--dsv4-c4-cache-implementation", "adapter", "--device", "cuda")
+    assert kw["decode_impl"] == "adapter" and not kw["disable_cuda_graph"]
+    with pytest.raises(SystemExit):
+        _resolve("--tp", "2", "--ep", "4")
+    with pytest.raises(SystemExit):
+        _resolve("--dsv4-c4-cache-layer-keep-counts", "2:256,4:192")
+    with pytest.raises(SystemExit):  # unsupported choice
+        _resolve("--moe-runner-backend", "deep_gemm")
+    _, kw = _resolve("--dsv4-c4-cache-keep-count", "192")
+    with pytest.raises(ValueError):  # Direct serving keeps 256 survivors only
+        EngineConfig(**kw).validate()

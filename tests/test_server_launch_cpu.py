@@ -20,9 +20,12 @@ def _free_port() -> int:
 
 def test_server_process_end_to_end():
     port = _free_port()
-    proc = subprocess.Popen([sys.executable, "-m", "packmla.server", "--model", "tiny", "--device", "cpu",
+    # launched with the reference launcher's flag names
+    proc = subprocess.Popen([sys.executable, "-m", "packmla.server", "--model-path", "tiny", "--device", "cpu",
                              "--port", str(port), "--max-running-requests", "4", "--context-length", "1024",
-                             "--enable-hierarchical-cache"],
+                             "--kv-cache-format", "direct", "--kv-cache-dtype", "fp8_e4m3", "--random-seed", "3",
+                             "--watchdog-timeout", "600", "--enable-hierarchical-cache", "--hicache-ratio", "2.0",
+                             "--hicache-write-policy", "write_through", "--enable-metrics"],
                             cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
                             start_new_session=True)
     url = f"http://127.0.0.1:{port}"
