@@ -6,8 +6,11 @@ server-info records in every benchmark directory):
 
     GET  /health, /health_generate     liveness; the second runs a one-token generation
     GET  /v1/models
-    POST /v1/completions               prompt: str | [str] | [int] | [[int]]; stream via SSE
-    POST /v1/chat/completions          messages; stream via SSE (chat.completion.chunk deltas)
+    POST /v1/completions               prompt: str | [str] | [int] | [[int]]; n; stop / stop_token_ids; SSE
+    POST /v1/chat/completions          messages; n; stop / stop_token_ids; SSE (chat.completion.chunk deltas)
+
+A stop string or stop token ends a choice early (the engine request is aborted) and is not returned.
+While streaming, text already sent before a multi-token stop string completes is not withdrawn.
     POST /generate                     SGLang native: text | input_ids + sampling_params
     GET  /server_info (/get_server_info)
     POST /flush_cache
@@ -56,6 +59,41 @@ def _check_ids(ids: list[int], vocab: int) -> None:
         raise HTTPException(400, f"token ids must be non-empty and in [0, {vocab})")
 
 
+class _StopRule:
+    """OpenAI `stop` strings and `stop_token_ids` of one choice: the token that completes a stop string,
+    or a stop token, ends the choice and is not returned; the text ends before the stop string."""
+
+    def __init__(self, body: dict, tok: ByteTokenizer):
+        stop = body.get("stop")
+        strings = [stop] if isinstance(stop, str) else list(stop or [])
+        if not all(isinstance(x, str) for x in strings):
+            raise HTTPException(400, "stop must be a string or a list of strings")
+        self.strings = [x for x in strings if x]
+        try:
+            self.ids = {int(t) for t in (body.get("stop_token_ids") or [])}
+        except (TypeError, ValueError) as exc:
+            raise HTTPException(400, "stop_token_ids must be token ids") from exc
+        self.tok = tok
+        self.tokens: list[int] = []
+        self.text: str | None = None  # final text when a stop string ended the choice
+
+    @property
+    def active(self) -> bool:
+        return bool(self.strings or self.ids)
+
+    def accept(self, token: int) -> bool:
+        if token in self.ids:
+            return False
+        if self.strings:
+            full = self.tok.decode(self.tokens + [token])
+            hits = [full.find(x) for x in self.strings if x in full]
+            if hits:
+                self.text = full[:min(hits)]
+                return False
+        self.tokens.append(token)
+        return True
+
+
 def _sse(obj) -> bytes:
     return f"data: {json.dumps(obj)}\n\n".encode()
 
@@ -75,14 +113,39 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         except RuntimeError as exc:
             raise HTTPException(503, str(exc)) from exc
 
-    async def _collect(st) -> list[int]:
+    async def _tokens(st, rule: _StopRule | None):
+        """Tokens of one request as they arrive; a stop rule that fires aborts the request early."""
+        stopped = False
         while True:
             item = await st.queue.get()
             if item is None:
                 break
+            if stopped:
+                continue  # produced before the abort reached the engine
+            if rule is not None and rule.active and not rule.accept(item):
+                stopped = True
+                driver.abort(st.ext_id)
+                continue
+            yield item
+        if stopped:
+            st.finish_reason = "stop"
+
+    async def _collect(st, rule: _StopRule | None = None) -> list[int]:
+        toks = [t async for t in _tokens(st, rule)]
         if st.finish_reason == "error":
             raise HTTPException(500, f"engine failed: {driver.error!r}")
-        return st.tokens
+        return toks
+
+    def _text(toks: list[int], rule: _StopRule | None) -> str:
+        return rule.text if rule is not None and rule.text is not None else tokenizer.decode(toks)
+
+    def _n(body: dict) -> int:
+        n = body.get("n", 1)
+        if not isinstance(n, int) or not 1 <= n <= 16:
+            raise HTTPException(400, "n must be an integer in [1, 16]")
+        if n > 1 and body.get("stream"):
+            raise HTTPException(400, "streaming supports n = 1")
+        return n
 
     def _usage(prompt_tokens: int, completion_tokens: int) -> dict:
         return {"prompt_tokens": prompt_tokens, "completion_tokens": completion_tokens,
@@ -112,19 +175,19 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         body = await req.json()
         params = _params(body, tokenizer)
         prompts = _prompts(body.get("prompt"), tokenizer)
+        n_choices = _n(body)
+        _StopRule(body, tokenizer)  # validate before submitting anything
         rid = f"cmpl-{uuid.uuid4().hex}"
         created = int(time.time())
         if body.get("stream"):
             if len(prompts) != 1:
                 raise HTTPException(400, "streaming supports one prompt")
             st = await _submit(prompts[0], params)
+            rule = _StopRule(body, tokenizer)
 
             async def gen():
                 n = 0
-                while True:
-                    item = await st.queue.get()
-                    if item is None:
-                        break
+                async for item in _tokens(st, rule):
                     n += 1
                     yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
                                 "choices": [{"index": 0, "text": tokenizer.decode([item]), "token_ids": [item],
@@ -136,13 +199,14 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
-        streams = [await _submit(p, params) for p in prompts]
+        streams = [await _submit(p, params) for p in prompts for _ in range(n_choices)]
         choices = []
         ntok = 0
         for i, st in enumerate(streams):
-            toks = await _collect(st)
+            rule = _StopRule(body, tokenizer)
+            toks = await _collect(st, rule)
             ntok += len(toks)
-            choices.append({"index": i, "text": tokenizer.decode(toks), "token_ids": toks, "logprobs": None,
+            choices.append({"index": i, "text": _text(toks, rule), "token_ids": toks, "logprobs": None,
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": choices, "usage": _usage(sum(len(p) for p in prompts), ntok)}
@@ -154,19 +218,20 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         if not isinstance(msgs, list) or not msgs:
             raise HTTPException(400, "messages must be a non-empty list")
         params = _params(body, tokenizer)
+        n_choices = _n(body)
+        _StopRule(body, tokenizer)
         ids = tokenizer.apply_chat_template(msgs)
         rid = f"chatcmpl-{uuid.uuid4().hex}"
         created = int(time.time())
-        st = await _submit(ids, params)
         if body.get("stream"):
+            st = await _submit(ids, params)
+            rule = _StopRule(body, tokenizer)
+
             async def gen():
                 yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                             "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]})
                 n = 0
-                while True:
-                    item = await st.queue.get()
-                    if item is None:
-                        break
+                async for item in _tokens(st, rule):
                     n += 1
                     yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
                                 "model": model_name,
@@ -178,11 +243,16 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
-        toks = await _collect(st)
+        streams = [await _submit(ids, params) for _ in range(n_choices)]
+        choices, ntok = [], 0
+        for i, st in enumerate(streams):
+            rule = _StopRule(body, tokenizer)
+            toks = await _collect(st, rule)
+            ntok += len(toks)
+            choices.append({"index": i, "message": {"role": "assistant", "content": _text(toks, rule)},
+                            "finish_reason": st.finish_reason})
         return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": tokenizer.decode(toks)},
-                             "finish_reason": st.finish_reason}],
-                "usage": _usage(len(ids), len(toks))}
+                "choices": choices, "usage": _usage(len(ids), ntok)}
 
     @app.post("/generate")
     async def generate(req: Request):
@@ -196,9 +266,10 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         else:
             raise HTTPException(400, "give text or input_ids")
         st = await _submit(ids, params)
-        toks = await _collect(st)
+        rule = _StopRule(sp, tokenizer)
+        toks = await _collect(st, rule)
         now = time.perf_counter()
-        return {"text": tokenizer.decode(toks), "output_ids": toks,
+        return {"text": _text(toks, rule), "output_ids": toks,
                 "meta_info": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
                               "finish_reason": {"type": st.finish_reason},
                               "e2e_latency": now - st.t_submit,

@@ -114,3 +114,37 @@ def test_concurrent_requests_batch_and_match(served):
             [tok.encode(p)], SamplingParams(max_new_tokens=6))[0]
         assert out[p] == ref
     assert eng.metrics.snapshot()["decode_steps"] - before < 3 * 5  # decode steps were shared
+
+
+def test_stop_strings_stop_tokens_and_n(served):
+    client, eng, tok, cfg = served
+    base = client.post("/v1/completions", json={"prompt": "stop here", "max_tokens": 8, "ignore_eos": True}).json()
+    ids = base["choices"][0]["token_ids"]
+    # stop token: the output ends before its first occurrence, the request is cut short
+    r = client.post("/v1/completions", json={"prompt": "stop here", "max_tokens": 8, "ignore_eos": True,
+                                             "stop_token_ids": [ids[3]]}).json()["choices"][0]
+    assert r["token_ids"] == ids[:ids.index(ids[3])] and r["finish_reason"] == "stop"
+    # stop string: the text ends before it (same rule as the server: first completion of the string)
+    stop = tok.decode([ids[4]])
+    kept, expect = [], None
+    for t in ids:
+        full = tok.decode(kept + [t])
+        if stop in full:
+            expect = full[:full.find(stop)]
+            break
+        kept.append(t)
+    r = client.post("/v1/completions", json={"prompt": "stop here", "max_tokens": 8, "ignore_eos": True,
+                                             "stop": [stop]}).json()["choices"][0]
+    assert r["text"] == expect and r["token_ids"] == kept and r["finish_reason"] == "stop"
+    # streaming ends with finish_reason stop
+    with client.stream("POST", "/v1/completions", json={"prompt": "stop here", "max_tokens": 8, "stream": True,
+                                                       "ignore_eos": True, "stop_token_ids": [ids[3]]}) as s:
+        ev = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ") and l != "data: [DONE]"]
+    assert ev[-1]["choices"][0]["finish_reason"] == "stop"
+    # n choices (greedy: identical), indexed in order
+    c = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}], "max_tokens": 2,
+                                                  "n": 3, "ignore_eos": True}).json()
+    assert [ch["index"] for ch in c["choices"]] == [0, 1, 2] and c["usage"]["completion_tokens"] == 6
+    assert len({ch["message"]["content"] for ch in c["choices"]}) == 1
+    assert client.post("/v1/completions", json={"prompt": "x", "n": 2, "stream": True}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": "x", "stop": [3]}).status_code == 400
