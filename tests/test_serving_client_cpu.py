@@ -1,4 +1,5 @@
 """CPU: the serving benchmark client against a live packmla HTTP server (tiny model, HiCache on)."""
+import json
 import socket
 import threading
 import time
@@ -58,3 +59,21 @@ def test_multi_turn_hits_host_cache(server_url):
     out = bench(url, "multi-turn", input_len=80, output_len=4, concurrency=2, turns=3, sessions=2)
     assert [t["success_rate"] for t in out["turns"]] == [1.0, 1.0, 1.0]
     assert eng.metrics.snapshot().get("hicache_hit_tokens", 0) > before
+
+
+def test_replay_of_recorded_sessions(server_url, tmp_path):
+    from packmla.bench import replay
+
+    url, eng = server_url
+    path = tmp_path / "sessions.jsonl"
+    with open(path, "w") as f:
+        for s in range(3):
+            history = [{"role": "user", "content": f"session {s} opening"}]
+            for turn in range(2):
+                f.write(json.dumps({"session": f"s{s}", "turn": turn, "messages": history, "max_tokens": 3}) + "\n")
+                history = history + [{"role": "assistant", "content": "ok"}, {"role": "user", "content": "more"}]
+    out = replay.main(["--base-url", url, "--requests", str(path), "--users", "2"])
+    assert out["sessions"] == 3 and out["requests"] == 6 and out["success_rate"] == 1.0 and out["passed"]
+    assert out["output_tokens"] >= 6 and out["ttft_ms"]["p50"] is not None
+    sessions = replay.load_sessions(str(path))
+    assert [[t["turn"] for t in s] for s in sessions] == [[0, 1]] * 3
