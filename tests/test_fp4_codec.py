@@ -1,0 +1,124 @@
+"""FP4 C4 record codec (packmla.formats.fp4): E2M1 rounding, per-16 E4M3 scales, Packed survivor
+selection, MSB-first bitmap, nibble order and page layout, against direct restatements in fp32."""
+import torch
+
+from packmla.formats import abi, codec, fp4
+
+
+def _rows(n=6, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, abi.LATENT_DIM, generator=g) * torch.rand(n, 1, generator=g) * 3
+    return x.to(torch.bfloat16).float()
+
+
+def test_record_sizes():
+    assert fp4.NATIVE_RECORD_BYTES == 288 and fp4.PACKED_RECORD_BYTES == 224
+    assert fp4.record_bytes("native") == 288 and fp4.record_bytes("direct") == 224
+    assert abs(1 - 224 / 288 - 0.2222) < 1e-4  # global records shrink 22.22%
+
+
+def test_e2m1_grid_ties_and_saturation():
+    grid = fp4.E2M1_GRID
+    assert torch.equal(fp4.e2m1_decode(fp4.e2m1_encode(grid)), grid)
+    assert torch.equal(fp4.e2m1_decode(fp4.e2m1_encode(-grid[1:])), -grid[1:])
+    # midpoints go to the even code: 0.25->0, 0.75->1.0, 1.25->1.0, 1.75->2, 2.5->2, 3.5->4, 5->4
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    assert fp4.e2m1_decode(fp4.e2m1_encode(mids)).tolist() == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0]
+    assert fp4.e2m1_decode(fp4.e2m1_encode(torch.tensor([7.0, -100.0]))).tolist() == [6.0, -6.0]
+    assert int(fp4.e2m1_encode(torch.tensor([-0.1]))[0]) == 0  # no negative zero code
+    # off-midpoint values: nearest grid point by brute force
+    x = torch.linspace(-6, 6, 1201)
+    ref = grid[(x.abs()[:, None] - grid).abs().argmin(-1)] * x.sign()
+    near_mid = ((x.abs()[:, None] - (grid[:-1] + grid[1:]) / 2).abs() < 1e-6).any(-1)
+    got = fp4.e2m1_decode(fp4.e2m1_encode(x))
+    assert torch.equal(got[~near_mid], ref[~near_mid])
+
+
+def test_native_roundtrip_within_one_scale_step():
+    rows = _rows()
+    codes, scales = fp4.native_encode(rows)
+    assert codes.shape == (rows.shape[0], 256) and scales.shape == (rows.shape[0], 32)
+    dec = fp4.native_decode(codes, scales)
+    s = scales.view(torch.float8_e4m3fn).float().repeat_interleave(16, -1)
+    # half the widest E2M1 gap (1) plus scale-rounding saturation (< 0.4) in units of the scale
+    assert bool(((dec - rows).abs() <= s + 1e-6).all())
+    # even coordinates in low nibbles
+    c0 = fp4.e2m1_encode(rows[:, 0] / s[:, 0])
+    assert torch.equal(codes[:, 0] & 0xF, c0)
+
+
+def test_scale_is_e4m3_of_group_amax_over_six():
+    rows = _rows(3, 1)
+    _, scales = fp4.native_encode(rows)
+    amax = rows.view(3, 32, 16).abs().amax(-1)
+    assert torch.equal(scales, (amax / 6).to(torch.float8_e4m3fn).view(torch.uint8))
+
+
+def test_packed_keeps_top_dequantized_with_lower_coordinate_ties():
+    rows = _rows(4, 2)
+    codes, scales = fp4.native_encode(rows)
+    native = fp4.native_decode(codes, scales)
+    pc, words, ps = fp4.packed_encode(rows)
+    assert pc.shape == (4, 128) and words.shape == (4, 8) and torch.equal(ps, scales)
+    mask = fp4.mask_from_msb_bitmap(words)
+    assert bool((mask.sum(-1) == 256).all())
+    for r in range(4):
+        mag = native[r].abs()
+        kept, dropped = mag[mask[r]], mag[~mask[r]]
+        assert float(kept.min()) >= float(dropped.max())
+        # among equal magnitudes at the threshold, every kept coordinate precedes every dropped one
+        t = float(kept.min())
+        idx = torch.arange(512)
+        at_t = mag == t
+        if bool((at_t & ~mask[r]).any()):
+            assert int(idx[at_t & mask[r]].max()) < int(idx[at_t & ~mask[r]].min())
+    assert torch.equal(fp4.packed_decode(pc, words, ps), native * mask)
+
+
+def test_all_equal_row_keeps_first_256_coordinates():
+    rows = torch.full((1, 512), 0.5)
+    pc, words, ps = fp4.packed_encode(rows)
+    mask = fp4.mask_from_msb_bitmap(words)[0]
+    assert bool(mask[:256].all()) and not bool(mask[256:].any())
+    assert words[0, :4].tolist() == [-1] * 4 and words[0, 4:].tolist() == [0] * 4
+
+
+def test_bitmap_is_msb_first_and_ranks_pack_low_nibble_first():
+    rows = torch.zeros(1, 512)
+    keep = list(range(0, 512, 2))  # 256 survivors: every even coordinate
+    vals = torch.linspace(1, 6, 256)
+    rows[0, keep] = vals
+    pc, words, ps = fp4.packed_encode(rows)
+    mask = fp4.mask_from_msb_bitmap(words)[0]
+    assert mask.nonzero()[:, 0].tolist() == keep
+    # coordinate 64w + b is bit 63 - b: even coordinates set bits 63, 61, ..., 1
+    expect = sum(1 << (63 - b) for b in range(0, 64, 2))
+    expect -= 1 << 64  # two's complement of a word with bit 63 set
+    assert words[0].tolist() == [expect] * 8
+    native_codes, _ = fp4.native_encode(rows)
+    nib = torch.stack((native_codes[0] & 0xF, native_codes[0] >> 4), -1).reshape(-1)
+    surv = nib[keep]
+    assert torch.equal(pc[0] & 0xF, surv[0::2]) and torch.equal(pc[0] >> 4, surv[1::2])
+
+
+def test_rotated_rows_apply_rope_then_bf16():
+    rows = _rows(2, 3)
+    table = codec.rope_table(64)
+    freqs = table[torch.tensor([5, 17])]
+    y = fp4.rotated_rows(rows, freqs)
+    assert torch.equal(y[:, :448], rows[:, :448])
+    assert torch.equal(y, codec.rotate_tail(rows, freqs).to(torch.bfloat16).float())
+
+
+def test_page_layout_data_rows_then_scale_rows():
+    rows = _rows(abi.RECORDS_PER_PAGE, 4)
+    for fmt, data_row in (("native", 256), ("direct", 192)):
+        page = fp4.write_page(fmt, rows)
+        assert page.numel() == fp4.page_bytes(fmt) == abi.RECORDS_PER_PAGE * (data_row + 32)
+        _, scales = fp4.native_encode(rows)
+        assert torch.equal(page[abi.RECORDS_PER_PAGE * data_row:].view(-1, 32), scales)
+        back = fp4.read_page(fmt, page)
+        if fmt == "native":
+            assert torch.equal(back, fp4.native_decode(*fp4.native_encode(rows)))
+        else:
+            assert torch.equal(back, fp4.packed_decode(*fp4.packed_encode(rows)))
