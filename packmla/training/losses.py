@@ -12,7 +12,7 @@ The hard mask has no gradient.  Three training objectives differentiate a surrog
                     mask is replaced by BudgetGate (a sigmoid gate whose threshold keeps sum = 256);
   relaxed:          forward and backward both on the continuous gated path (no codec rounding);
   anchored:         the relaxed path plus fixed codec residuals measured at the warm scorer's mask.
-The exact scalar replay (`forward_error` without temperature) stays the judge of every candidate.
+The exact scalar replay (`forward_error` without temperature) decides between candidates.
 Every objective has a scalar and an independent batched implementation; `preflight` checks that both
 agree in value and gradient before a fit uses the batched one.
 """
@@ -108,7 +108,7 @@ def _relative(output, target, denom):
     return (sq / denom).clamp_min(1e-30).sqrt()
 
 
-# ----------------------------------------------------------------------------- scalar (the judge)
+# ----------------------------------------------------------------------------- scalar (the deciding replay)
 def forward_error(math, ref, state: dict, model, temperature: float | None = None, *,
                   retained_features: int = KEEP, keep_mask: torch.Tensor | None = None) -> torch.Tensor:
     """Exact Packed attention error of one state; with `temperature`, straight-through gradients."""

@@ -252,11 +252,22 @@ def run(cache: Path, policy: Path, output: Path, *, recipe: str, layers: tuple[i
     for layer, e in sorted(selected.items()):
         read_checkpoint(e)
         published.append({**e, "path": Path(e["path"]).name} if layer in layers else e)
-    # the policy is the completion marker: written to a temporary name, then linked into place
+    # the policy is the completion marker: staged under a temporary name, hard-linked into place and
+    # checked to be the staged file; any failure (interrupts included) leaves no policy.json behind
+    # (reference: training/train.py:448-509)
     tmp = output / ".policy.json.tmp"
+    final = output / "policy.json"
     Math.atomic_json(tmp, {"selected": published, "trained_layers": list(layers)})
+    linked = False
     try:
-        os.link(tmp, output / "policy.json")
+        os.link(tmp, final)
+        linked = True
+        if os.stat(tmp).st_ino != os.stat(final).st_ino:
+            raise RuntimeError("published policy is not the staged file")
+    except BaseException:
+        if linked:
+            final.unlink(missing_ok=True)
+        raise
     finally:
         tmp.unlink(missing_ok=True)
     Math.atomic_json(output / "progress.json", {"layers": done, "complete": True})

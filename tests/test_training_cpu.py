@@ -108,7 +108,7 @@ def test_parse_layers():
             parse_layers(bad)
 
 
-def test_capture_train_evaluate_end_to_end(tmp_path):
+def test_capture_train_evaluate_end_to_end(tmp_path, monkeypatch):
     from packmla.training import evaluate, train
     from packmla.training.data.cache import load_cached_layer
     from packmla.training.data.capture import capture_cache
@@ -126,6 +126,24 @@ def test_capture_train_evaluate_end_to_end(tmp_path):
                       str(tmp_path / "fit"), "--recipe", "rank64", "--epochs", "2", "--threads", "2"])
     policy = json.loads((tmp_path / "fit" / "policy.json").read_text())
     assert policy["trained_layers"] == [layer] and out["layers"] == [layer]
+    # a publish whose linked file is not the staged one is rolled back: no policy.json, progress incomplete
+    import os
+    import types
+
+    real_stat = os.stat
+
+    def fake_stat(p, *a, **k):
+        st = real_stat(p, *a, **k)
+        return types.SimpleNamespace(st_ino=st.st_ino + 1) if str(p).endswith("fit2/policy.json") else st
+
+    monkeypatch.setattr(os, "stat", fake_stat)
+    with pytest.raises(RuntimeError):
+        train.main(["--cache", str(tmp_path / "cache"), "--policy", init["policy"], "--output",
+                    str(tmp_path / "fit2"), "--recipe", "rank64", "--epochs", "1", "--threads", "2"])
+    monkeypatch.undo()
+    assert not (tmp_path / "fit2" / "policy.json").exists()
+    assert not (tmp_path / "fit2" / ".policy.json.tmp").exists()
+    assert json.loads((tmp_path / "fit2" / "progress.json").read_text())["complete"] is False
     sel = json.loads((tmp_path / "fit" / f"selected-layer-{layer:02d}.json").read_text())
     assert sel["development_selected"]["mean"] <= sel["development_baseline"]["mean"] + 1e-12
     res = evaluate.main(["--cache", str(tmp_path / "cache"), "--policy", out["policy"], "--output",
