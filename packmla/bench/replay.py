@@ -1,7 +1,10 @@
 """Replay of recorded multi-turn sessions against an OpenAI-compatible server, fixed active-user pool.
 
     python -m packmla.bench.replay --base-url http://127.0.0.1:30000 --requests sessions.jsonl \
-        --users 24 [--min-success 0.99] [--output summary.json]
+        --users 24 [--min-success 0.99] [--duration-s 1200] [--ttft-slo-ms 10000] [--output summary.json]
+    python -m packmla.bench.replay sweep --requests sessions.jsonl --concurrencies 20,22,24 \
+        --repeats 1 --duration-s 1200 --out-dir results/sweep-direct
+    python -m packmla.bench.replay plan --requests sessions.jsonl --pool-tokens 800512 --concurrencies 16,20,24
 
 Reference behaviour (the reference's LongSWE replay, scripts/local/business_replay/runner.py): a fixed
 pool of active users; each user takes the next unreplayed session and sends its turns in order
@@ -13,14 +16,34 @@ the requests complete.  Input: one JSON object per line,
 
 The summary also reports the server's HiCache restored-token counter delta (from /metrics), the share
 of prompt work that a host-tier restore saved.
+
+`--duration-s` is the dispatch window: after it no user starts a new session, sessions already
+started finish (the drain), and rates divide by the whole wall time, drain included.  Completeness
+(every started session finished), response success (>= `min_success`, inclusive) and TTFT p90
+(strictly below `ttft_slo_ms`) are separate fields; `passed` needs all three.
+
+`sweep` (reference: scripts/local/sweep-lswb.sh, scripts/local/business_replay/sweep.py) replays one
+running server at an ordered ladder of concurrencies, `repeats` consecutive replays per point, each
+after the server is idle and its cache flushed.  Every point's summary lands in
+`<out-dir>/c<N>/repeat-<NN>/summary.json` and the incremental `summary.json` / `summary.csv`; a failed
+gate is recorded and later points still run, while an unhealthy server or a failed flush stops the
+sweep.  No best point is chosen.
+
+`plan` (reference: scripts/local/business_replay/capacity_plan.py) replays the scheduler offline: C
+slots each hold one session and send its requests one per tick; the live context of a tick is the
+sum of the active requests' sizes (prompt + completion tokens), and the peak over the first `ticks`
+ticks must fit the KV pool for the run to avoid eviction.
 """
 from __future__ import annotations
 
 import argparse
 import asyncio
+import csv
 import json
+import os
 import time
-from collections import defaultdict
+from collections import defaultdict, deque
+from pathlib import Path
 
 import numpy as np
 
@@ -71,27 +94,31 @@ async def _turn(session, url: str, model: str, rec: dict) -> dict:
     return out
 
 
-async def _replay(url: str, model: str, sessions: list[list[dict]], users: int) -> tuple[list[dict], float]:
+async def _replay(url: str, model: str, sessions: list[list[dict]], users: int,
+                  duration_s: float | None = None) -> tuple[list[dict], float, int]:
     import aiohttp
 
     queue: asyncio.Queue = asyncio.Queue()
     for s in sessions:
         queue.put_nowait(s)
     results: list[dict] = []
+    started = [0]
     timeout = aiohttp.ClientTimeout(total=None, sock_read=3600)
     async with aiohttp.ClientSession(timeout=timeout) as http:
+        t0 = time.perf_counter()
+
         async def user():
-            while True:
+            while duration_s is None or time.perf_counter() - t0 < duration_s:
                 try:
                     turns = queue.get_nowait()
                 except asyncio.QueueEmpty:
                     return
+                started[0] += 1
                 for rec in turns:  # a session's turns run in order
                     results.append(await _turn(http, url, model, rec))
 
-        t0 = time.perf_counter()
         await asyncio.gather(*(user() for _ in range(max(1, users))))
-        return results, time.perf_counter() - t0
+        return results, time.perf_counter() - t0, started[0]
 
 
 def _metric(url: str, name: str) -> float:
@@ -106,10 +133,11 @@ def _metric(url: str, name: str) -> float:
     return 0.0
 
 
-def replay(url: str, requests_path: str, users: int, model: str = "default", min_success: float = 0.99) -> dict:
+def replay(url: str, requests_path: str, users: int, model: str = "default", min_success: float = 0.99,
+           duration_s: float | None = None, ttft_slo_ms: float | None = None) -> dict:
     sessions = load_sessions(requests_path)
     hits0 = _metric(url, "packmla_hicache_hit_tokens")
-    results, wall = asyncio.run(_replay(url, model, sessions, users))
+    results, wall, started = asyncio.run(_replay(url, model, sessions, users, duration_s))
     ok = [r for r in results if r["ok"]]
 
     def pct(xs, q):
@@ -118,32 +146,184 @@ def replay(url: str, requests_path: str, users: int, model: str = "default", min
     ttft = [r["ttft"] for r in ok if r["ttft"] is not None]
     e2e = [r["e2e"] for r in ok]
     success = len(ok) / max(1, len(results))
-    return {"sessions": len(sessions), "requests": len(results), "completed": len(ok), "success_rate": success,
-            "passed": success >= min_success, "users": users, "wall_s": wall,
-            "output_tokens": sum(r["tokens"] for r in ok),
+    expected = sum(len(s) for s in sessions[:started])
+    complete = len(results) == expected
+    p90 = pct(ttft, 90)
+    slo_ok = ttft_slo_ms is None or (p90 is not None and p90 < ttft_slo_ms)
+    return {"sessions": len(sessions), "sessions_started": started, "requests": len(results),
+            "completed": len(ok), "complete": complete, "success_rate": success,
+            "success_passed": success >= min_success, "ttft_slo_ms": ttft_slo_ms, "ttft_slo_passed": slo_ok,
+            "passed": complete and success >= min_success and slo_ok, "users": users, "duration_s": duration_s,
+            "wall_s": wall, "output_tokens": sum(r["tokens"] for r in ok),
             "output_throughput_tok_s": sum(r["tokens"] for r in ok) / wall if wall > 0 else 0.0,
-            "ttft_ms": {"p50": pct(ttft, 50), "p99": pct(ttft, 99)}, "e2e_ms": {"p50": pct(e2e, 50), "p99": pct(e2e, 99)},
+            "successful_requests_per_s": len(ok) / wall if wall > 0 else 0.0,
+            "ttft_ms": {"p50": pct(ttft, 50), "p90": p90, "p99": pct(ttft, 99)},
+            "e2e_ms": {"p50": pct(e2e, 50), "p99": pct(e2e, 99)},
             "hicache_restored_tokens": _metric(url, "packmla_hicache_hit_tokens") - hits0,
             "errors": [r.get("error") for r in results if not r["ok"]][:5]}
 
 
+# --------------------------------------------------------------------------- sweep
+def _idle_and_flush(url: str, timeout_s: float) -> None:
+    """Wait until the server is healthy and idle, then flush its cache; raises RuntimeError otherwise."""
+    import requests
+
+    deadline = time.monotonic() + timeout_s
+    while True:
+        try:
+            healthy = requests.get(url + "/health", timeout=30).status_code == 200
+        except requests.RequestException:
+            healthy = False
+        if not healthy:
+            raise RuntimeError("server unhealthy")
+        if _metric(url, "packmla_num_running_reqs") == 0 and _metric(url, "packmla_num_queue_reqs") == 0:
+            break
+        if time.monotonic() > deadline:
+            raise RuntimeError("server did not become idle")
+        time.sleep(0.2)
+    try:
+        r = requests.post(url + "/flush_cache", timeout=60)
+    except requests.RequestException as exc:
+        raise RuntimeError(f"flush failed: {exc!r}") from exc
+    if r.status_code != 200:
+        raise RuntimeError(f"flush failed: HTTP {r.status_code}")
+
+
+_CSV_FIELDS = ("concurrency", "repeat", "passed", "complete", "success_rate", "ttft_p90_ms", "ttft_slo_passed",
+               "successful_requests_per_s", "output_throughput_tok_s", "requests", "completed", "wall_s")
+
+
+def sweep(url: str, requests_path: str, concurrencies: list[int], out_dir: str, *, repeats: int = 1,
+          model: str = "default", duration_s: float | None = 1200.0, ttft_slo_ms: float = 10000.0,
+          min_success: float = 0.99, idle_timeout_s: float = 600.0) -> dict:
+    if not concurrencies or any(c <= 0 for c in concurrencies) or len(set(concurrencies)) != len(concurrencies):
+        raise ValueError("concurrencies must be distinct positive integers")
+    if list(concurrencies) != sorted(concurrencies):
+        raise ValueError("concurrencies must be in increasing order")
+    if repeats < 1 or not 0.0 <= min_success <= 1.0:
+        raise ValueError("repeats >= 1 and min_success in [0, 1] required")
+    root = Path(out_dir)
+    root.mkdir(parents=True, exist_ok=False)  # a fresh directory per sweep
+    manifest = {"base_url": url, "requests": os.path.abspath(requests_path), "concurrencies": list(concurrencies),
+                "repeats": repeats, "duration_s": duration_s, "ttft_slo_ms": ttft_slo_ms,
+                "min_success": min_success, "model": model}
+    (root / "manifest.json").write_text(json.dumps(manifest, indent=2))
+    points: list[dict] = []
+    stopped = None
+    for c in concurrencies:
+        for rep in range(1, repeats + 1):
+            try:
+                _idle_and_flush(url, idle_timeout_s)
+            except RuntimeError as exc:
+                stopped = f"c{c} repeat {rep}: {exc}"
+                break
+            out = replay(url, requests_path, c, model, min_success, duration_s, ttft_slo_ms)
+            d = root / f"c{c}" / f"repeat-{rep:02d}"
+            d.mkdir(parents=True)
+            (d / "summary.json").write_text(json.dumps(out, indent=2))
+            points.append({"concurrency": c, "repeat": rep, **out})
+            _write_summaries(root, points, stopped)
+        if stopped:
+            break
+    _write_summaries(root, points, stopped)
+    return {"out_dir": str(root), "points": len(points), "stopped": stopped,
+            "operational_complete": stopped is None and len(points) == len(concurrencies) * repeats}
+
+
+def _write_summaries(root: Path, points: list[dict], stopped: str | None) -> None:
+    (root / "summary.json").write_text(json.dumps({"points": points, "stopped": stopped}, indent=2))
+    with open(root / "summary.csv", "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=_CSV_FIELDS)
+        w.writeheader()
+        for p in points:
+            w.writerow({k: (p["ttft_ms"]["p90"] if k == "ttft_p90_ms" else p.get(k)) for k in _CSV_FIELDS})
+
+
+# --------------------------------------------------------------------------- capacity plan
+def request_tokens(rec: dict) -> int:
+    """Prompt + completion tokens of one recorded request: the record's own counts when present
+    (`prompt_tokens`), else the UTF-8 bytes of its message contents (the byte tokenizer's count)."""
+    prompt = rec.get("prompt_tokens")
+    if prompt is None:
+        prompt = sum(len(str(m.get("content", "")).encode()) for m in rec["messages"])
+    return int(prompt) + int(rec.get("max_tokens", 256))
+
+
+def peak_live_tokens(sessions: list[list[dict]], concurrency: int, ticks: int | None = None) -> int:
+    """Largest sum of the active requests' sizes over the first `ticks` ticks of C session slots."""
+    pending = deque([request_tokens(r) for r in s] for s in sessions)
+    slots: list[deque] = []
+    peak = tick = 0
+    while (pending or slots) and (ticks is None or tick < ticks):
+        while len(slots) < concurrency and pending:
+            slots.append(deque(pending.popleft()))
+        peak = max(peak, sum(s[0] for s in slots))
+        for s in slots:
+            s.popleft()
+        slots = [s for s in slots if s]
+        tick += 1
+    return peak
+
+
+def plan(requests_path: str, concurrencies: list[int], pool_tokens: int, ticks: int | None = None) -> dict:
+    sessions = load_sessions(requests_path)
+    rows = [{"concurrency": c, "peak_live_tokens": peak_live_tokens(sessions, c, ticks)} for c in concurrencies]
+    for r in rows:
+        r["utilization"] = r["peak_live_tokens"] / pool_tokens
+        r["fits"] = r["peak_live_tokens"] <= pool_tokens
+    fitting = [r["concurrency"] for r in rows if r["fits"]]
+    return {"pool_tokens": pool_tokens, "ticks": ticks, "points": rows,
+            "largest_fitting_concurrency": max(fitting) if fitting else None}
+
+
+def _ints(text: str) -> list[int]:
+    return [int(x) for x in text.split(",") if x.strip()]
+
+
 def main(argv=None) -> dict:
+    import sys
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    cmd = argv.pop(0) if argv and argv[0] in ("sweep", "plan") else "replay"
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--base-url", default="http://127.0.0.1:30000")
     ap.add_argument("--requests", required=True)
-    ap.add_argument("--users", type=int, default=24)
+    if cmd == "plan":
+        ap.add_argument("--concurrencies", type=_ints, required=True)
+        ap.add_argument("--pool-tokens", type=int, required=True)
+        ap.add_argument("--ticks", type=int, default=None)
+        a = ap.parse_args(argv)
+        out = plan(a.requests, a.concurrencies, a.pool_tokens, a.ticks)
+        print(json.dumps(out, indent=2))
+        return out
+    ap.add_argument("--base-url", default="http://127.0.0.1:30000")
     ap.add_argument("--model", default="default")
     ap.add_argument("--min-success", type=float, default=0.99)
+    ap.add_argument("--duration-s", type=float, default=None)
+    ap.add_argument("--ttft-slo-ms", type=float, default=None)
+    if cmd == "sweep":
+        ap.add_argument("--concurrencies", type=_ints, required=True)
+        ap.add_argument("--repeats", type=int, default=1)
+        ap.add_argument("--out-dir", required=True)
+        a = ap.parse_args(argv)
+        out = sweep(a.base_url, a.requests, a.concurrencies, a.out_dir, repeats=a.repeats, model=a.model,
+                    duration_s=a.duration_s if a.duration_s is not None else 1200.0,
+                    ttft_slo_ms=a.ttft_slo_ms if a.ttft_slo_ms is not None else 10000.0, min_success=a.min_success)
+        print(json.dumps(out, indent=2))
+        if not out["operational_complete"]:
+            raise SystemExit(f"sweep stopped: {out['stopped']}")
+        return out
+    ap.add_argument("--users", type=int, default=24)
     ap.add_argument("--output", default=None)
     a = ap.parse_args(argv)
-    out = replay(a.base_url, a.requests, a.users, a.model, a.min_success)
+    out = replay(a.base_url, a.requests, a.users, a.model, a.min_success, a.duration_s, a.ttft_slo_ms)
     text = json.dumps(out, indent=2)
     if a.output:
         with open(a.output, "x") as f:
             f.write(text)
     print(text)
     if not out["passed"]:
-        raise SystemExit(f"success rate {out['success_rate']:.4f} below {a.min_success}")
+        raise SystemExit(f"replay gates failed: complete={out['complete']} success={out['success_rate']:.4f} "
+                         f"ttft_p90_ms={out['ttft_ms']['p90']}")
     return out
 
 

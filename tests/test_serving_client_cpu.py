@@ -77,3 +77,56 @@ def test_replay_of_recorded_sessions(server_url, tmp_path):
     assert out["output_tokens"] >= 6 and out["ttft_ms"]["p50"] is not None
     sessions = replay.load_sessions(str(path))
     assert [[t["turn"] for t in s] for s in sessions] == [[0, 1]] * 3
+
+
+def test_replay_sweep_ladder_and_stop(server_url, tmp_path):
+    import csv
+
+    from packmla.bench import replay
+
+    url, eng = server_url
+    path = tmp_path / "sessions.jsonl"
+    with open(path, "w") as f:
+        for s in range(3):
+            f.write(json.dumps({"session": f"s{s}", "turn": 0, "max_tokens": 2,
+                                "messages": [{"role": "user", "content": f"sweep {s}"}]}) + "\n")
+    out = replay.main(["sweep", "--base-url", url, "--requests", str(path), "--concurrencies", "1,2",
+                       "--repeats", "2", "--out-dir", str(tmp_path / "sw"), "--min-success", "1.0"])
+    assert out["operational_complete"] and out["points"] == 4
+    for c in (1, 2):
+        for r in (1, 2):
+            point = json.loads((tmp_path / "sw" / f"c{c}" / f"repeat-{r:02d}" / "summary.json").read_text())
+            assert point["users"] == c and point["complete"] and point["ttft_ms"]["p90"] is not None
+    rows = list(csv.DictReader(open(tmp_path / "sw" / "summary.csv")))
+    assert [(r["concurrency"], r["repeat"]) for r in rows] == [("1", "1"), ("1", "2"), ("2", "1"), ("2", "2")]
+    assert json.loads((tmp_path / "sw" / "manifest.json").read_text())["concurrencies"] == [1, 2]
+    # a zero dispatch window starts no session; the gates report it
+    win = replay.replay(url, str(path), 2, duration_s=0.0)
+    assert win["sessions_started"] == 0 and win["requests"] == 0 and not win["passed"]
+    # an unreachable server stops the sweep before its first point
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        dead = f"http://127.0.0.1:{s.getsockname()[1]}"
+    res = replay.sweep(dead, str(path), [1], str(tmp_path / "sw2"))
+    assert res["points"] == 0 and "unhealthy" in res["stopped"] and not res["operational_complete"]
+    with pytest.raises(ValueError):
+        replay.sweep(url, str(path), [2, 1], str(tmp_path / "sw3"))
+
+
+def test_replay_capacity_plan(tmp_path):
+    from packmla.bench import replay
+
+    path = tmp_path / "plan.jsonl"
+    sizes = {"s0": [10, 20], "s1": [5], "s2": [7, 7, 7]}
+    with open(path, "w") as f:
+        for sid, turns in sizes.items():
+            for t, n in enumerate(turns):
+                f.write(json.dumps({"session": sid, "turn": t, "messages": [], "prompt_tokens": n,
+                                    "max_tokens": 0}) + "\n")
+    out = replay.main(["plan", "--requests", str(path), "--concurrencies", "1,2,3", "--pool-tokens", "25"])
+    peaks = {p["concurrency"]: p["peak_live_tokens"] for p in out["points"]}
+    assert peaks == {1: 20, 2: 27, 3: 27}
+    assert out["largest_fitting_concurrency"] == 1
+    sessions = replay.load_sessions(str(path))
+    assert replay.peak_live_tokens(sessions, 2, ticks=1) == 15
+    assert replay.request_tokens({"messages": [{"content": "abc"}], "max_tokens": 4}) == 7
