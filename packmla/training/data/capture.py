@@ -13,10 +13,15 @@ training states.  Here `CaptureObserver` attaches to `V4FlashModel.observer`:
 
 `capture_cache` drives an `Engine` in Native mode over random prompts and writes a cache
 (packmla.training.data.cache) with a frozen train/development split.  Captures need no GPU: the CPU
-engine runs the same model.
+engine runs the same model.  Command line (the counterpart of the reference's
+scripts/local/capture-latent.sh, which captures from a live Native server):
+
+    python -m packmla.training.data.capture --output cache/ --model small --issues 32 --development 8
 """
 from __future__ import annotations
 
+import argparse
+import json
 from pathlib import Path
 
 import torch
@@ -146,3 +151,33 @@ def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int 
                 {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native"})
     return {"cache": str(output), "layers": list(layers), "split": split, "skipped": obs.skipped,
             "states": {layer: {r: len(v) for r, v in roles.items()} for layer, roles in states_by_layer.items()}}
+
+
+def main(argv=None) -> dict:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--output", type=Path, required=True, help="new cache directory")
+    ap.add_argument("--model", default="tiny", help="tiny | small | v4-flash | path to a packmla checkpoint")
+    ap.add_argument("--issues", type=int, default=6)
+    ap.add_argument("--development", type=int, default=2)
+    ap.add_argument("--train-queries", type=int, default=2)
+    ap.add_argument("--dev-queries", type=int, default=3)
+    ap.add_argument("--prompt-len", type=int, default=300)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--device", default="cpu", choices=["cpu", "cuda"])
+    ap.add_argument("--layers", default=None, help="comma-separated C4 layers (default: all)")
+    a = ap.parse_args(argv)
+    if a.output.exists():
+        raise SystemExit(f"{a.output} exists: captures are written to a new directory")
+    from ...server.__main__ import model_config
+
+    cfg, weights = model_config(a.model)
+    if weights is not None:
+        raise SystemExit("capture runs random-init models only (tiny | small | v4-flash)")
+    layers = tuple(int(x) for x in a.layers.split(",")) if a.layers else None
+    return capture_cache(a.output, cfg, issues=a.issues, development=a.development, train_queries=a.train_queries,
+                         dev_queries=a.dev_queries, prompt_len=a.prompt_len, seed=a.seed, device=a.device,
+                         layers=layers)
+
+
+if __name__ == "__main__":
+    print(json.dumps(main(), indent=2))

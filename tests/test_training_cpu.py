@@ -163,3 +163,13 @@ def test_capture_train_evaluate_end_to_end(tmp_path, monkeypatch):
     assert lay["states"] == {"train": 6, "development": 4}
     assert lay["by_kind"]["raw"] == 10 * cfg.index_topk * 512 * 4 and 0 < lay["tensor_bytes"] <= lay["file_bytes"]
     assert diag["mean_learned"] <= diag["mean_topmag"] * 1.5
+
+
+def test_capture_cli_writes_fresh_cache(tmp_path):
+    from packmla.training.data import capture
+
+    out = capture.main(["--output", str(tmp_path / "c"), "--issues", "2", "--development", "1",
+                        "--train-queries", "1", "--dev-queries", "1", "--prompt-len", "64"])
+    assert out["skipped"] == 0 and all(v == {"train": 1, "development": 1} for v in out["states"].values())
+    with pytest.raises(SystemExit):  # caches are never overwritten
+        capture.main(["--output", str(tmp_path / "c")])
