@@ -29,6 +29,9 @@ after the server is idle and its cache flushed.  Every point's summary lands in
 gate is recorded and later points still run, while an unhealthy server or a failed flush stops the
 sweep.  No best point is chosen.
 
+`--scheduler request-slot` replays the closed-loop request-slot FIFO (`request_slot_replay`): a fixed
+window, throughput inside it, and a queue-inclusive ready-to-first-output SLO.
+
 `plan` (reference: scripts/local/business_replay/capacity_plan.py) replays the scheduler offline: C
 slots each hold one session and send its requests one per tick; the live context of a tick is the
 sum of the active requests' sizes (prompt + completion tokens), and the peak over the first `ticks`
@@ -161,6 +164,117 @@ def replay(url: str, requests_path: str, users: int, model: str = "default", min
             "e2e_ms": {"p50": pct(e2e, 50), "p99": pct(e2e, 99)},
             "hicache_restored_tokens": _metric(url, "packmla_hicache_hit_tokens") - hits0,
             "errors": [r.get("error") for r in results if not r["ok"]][:5]}
+
+
+# --------------------------------------------------------------------------- request-slot FIFO
+async def _request_slots(url: str, model: str, sessions: list[list[dict]], population: int, concurrency: int,
+                         window_s: float, drain_s: float) -> tuple[list[dict], list[float]]:
+    """`population` sessions are active at once, each with at most one ready turn; ready turns queue in
+    FIFO order for `concurrency` request slots.  A finished turn puts its session's next turn at the
+    tail (ready at that moment); a finished session admits the next one.  Dispatch stops at
+    `window_s`; the drain waits up to `drain_s` for turns already dispatched.  Returns the finished
+    turns (with ready / dispatch / completion offsets) and the ready offsets of unresolved turns."""
+    import aiohttp
+
+    origin = time.perf_counter()
+
+    def now() -> float:
+        return time.perf_counter() - origin
+
+    pending = deque(sessions)
+    ready: deque = deque()
+    results: list[dict] = []
+
+    def admit() -> None:
+        if pending:
+            ready.append((deque(pending.popleft()), now()))
+
+    for _ in range(min(population, len(sessions))):
+        admit()
+    active: dict = {}
+    timeout = aiohttp.ClientTimeout(total=None, sock_read=3600)
+    async with aiohttp.ClientSession(timeout=timeout) as http:
+        async def run_one(turns: deque, ready_s: float):
+            rec = turns.popleft()
+            dispatch = now()
+            out = await _turn(http, url, model, rec)
+            out.update(ready_s=ready_s, dispatch_s=dispatch, completed_s=dispatch + out["e2e"],
+                       client_queue_ms=(dispatch - ready_s) * 1000,
+                       ready_ttft_ms=None if out["ttft"] is None else (dispatch + out["ttft"] - ready_s) * 1000)
+            return out, turns
+
+        while now() < window_s and (active or ready):
+            while ready and len(active) < concurrency and now() < window_s:
+                turns, ready_s = ready.popleft()
+                active[asyncio.ensure_future(run_one(turns, ready_s))] = ready_s
+            done, _ = await asyncio.wait(list(active), timeout=max(0.0, window_s - now()),
+                                         return_when=asyncio.FIRST_COMPLETED)
+            for task in done:
+                active.pop(task)
+                out, turns = task.result()
+                results.append(out)
+                if turns:
+                    ready.append((turns, now()))
+                else:
+                    admit()
+        unresolved = [r for _, r in ready]
+        if active:
+            done, still = await asyncio.wait(list(active), timeout=drain_s)
+            results.extend(task.result()[0] for task in done)
+            unresolved.extend(active[task] for task in still)
+            for task in still:
+                task.cancel()
+            await asyncio.gather(*still, return_exceptions=True)
+    return results, unresolved
+
+
+def slo_status(good: int, unknown: int, total: int, percentile: float = 90.0) -> str:
+    """`pass` if the known-good turns alone reach the percentile, `fail` if they cannot even with every
+    unknown turn good, else `indeterminate`."""
+    need = percentile / 100.0 * total
+    return "pass" if good >= need else ("fail" if good + unknown < need else "indeterminate")
+
+
+def request_slot_replay(url: str, requests_path: str, concurrency: int, population: int, window_s: float,
+                        model: str = "default", min_success: float = 0.99, ttft_slo_ms: float = 10000.0,
+                        drain_s: float = 600.0) -> dict:
+    """Closed-loop request-slot FIFO replay with fixed-window throughput and a ready-to-first-output SLO.
+
+    Reference: scripts/local/business_replay/request_slots.py (`run`, `summarize`).  Throughput counts
+    successful turns completed inside the window.  The SLO is the 90th percentile of the time from a
+    turn becoming ready (client queue included) to its first output token, over every ready turn:
+    failed or empty responses are violations, and a turn still unresolved at the end counts as a
+    violation when it had already waited `ttft_slo_ms` by the cutoff, else as unknown.  The status is
+    `pass` when the known-good turns alone reach 90 %, `fail` when they cannot even with every unknown
+    good, and `indeterminate` otherwise."""
+    if not (population >= concurrency > 0) or window_s <= 0 or drain_s <= 0:
+        raise ValueError("population >= concurrency > 0 and positive window / drain required")
+    sessions = load_sessions(requests_path)
+    results, unresolved = asyncio.run(_request_slots(url, model, sessions, population, concurrency, window_s,
+                                                     drain_s))
+    ok = [r for r in results if r["ok"]]
+    in_window = [r for r in ok if r["completed_s"] <= window_s]
+    good = sum(1 for r in results if r["ok"] and r["ready_ttft_ms"] is not None and r["ready_ttft_ms"] < ttft_slo_ms)
+    late = sum(1 for r in unresolved if (window_s - r) * 1000 >= ttft_slo_ms)
+    total = len(results) + len(unresolved)
+    unknown = len(unresolved) - late
+    status = slo_status(good, unknown, total)
+
+    def dist(xs):
+        return {"p50": float(np.percentile(xs, 50)), "p90": float(np.percentile(xs, 90))} if xs else None
+
+    success = len(ok) / max(1, len(results))
+    return {"scheduler": "request-slot-fifo", "concurrency": concurrency, "population": population,
+            "window_s": window_s, "ready_requests": total, "finished": len(results), "unresolved": len(unresolved),
+            "completed": len(ok), "completed_in_window": len(in_window),
+            "successful_requests_per_s": len(in_window) / window_s,
+            "output_throughput_tok_s": sum(r["tokens"] for r in in_window) / window_s,
+            "success_rate": success, "success_passed": success >= min_success,
+            "ready_ttft_ms": dist([r["ready_ttft_ms"] for r in ok if r["ready_ttft_ms"] is not None]),
+            "client_queue_ms": dist([r["client_queue_ms"] for r in results]),
+            "slo": {"threshold_ms": ttft_slo_ms, "percentile": 90, "status": status, "good": good,
+                    "late_unresolved": late, "unknown": unknown},
+            "passed": status == "pass" and success >= min_success}
 
 
 # --------------------------------------------------------------------------- sweep
@@ -312,9 +426,21 @@ def main(argv=None) -> dict:
         if not out["operational_complete"]:
             raise SystemExit(f"sweep stopped: {out['stopped']}")
         return out
-    ap.add_argument("--users", type=int, default=24)
+    ap.add_argument("--users", type=int, default=24, help="active users (session) or request slots (request-slot)")
+    ap.add_argument("--scheduler", choices=["session", "request-slot"], default="session")
+    ap.add_argument("--population", type=int, default=None, help="request-slot: active sessions (default: --users)")
+    ap.add_argument("--drain-s", type=float, default=600.0)
     ap.add_argument("--output", default=None)
     a = ap.parse_args(argv)
+    if a.scheduler == "request-slot":
+        if a.duration_s is None:
+            ap.error("--scheduler request-slot needs --duration-s (the fixed measurement window)")
+        out = request_slot_replay(a.base_url, a.requests, a.users, a.population or a.users, a.duration_s, a.model,
+                                  a.min_success, a.ttft_slo_ms if a.ttft_slo_ms is not None else 10000.0, a.drain_s)
+        print(json.dumps(out, indent=2))
+        if not out["passed"]:
+            raise SystemExit(f"replay gates failed: slo={out['slo']['status']} success={out['success_rate']:.4f}")
+        return out
     out = replay(a.base_url, a.requests, a.users, a.model, a.min_success, a.duration_s, a.ttft_slo_ms)
     text = json.dumps(out, indent=2)
     if a.output:

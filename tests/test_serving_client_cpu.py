@@ -130,3 +130,25 @@ def test_replay_capacity_plan(tmp_path):
     sessions = replay.load_sessions(str(path))
     assert replay.peak_live_tokens(sessions, 2, ticks=1) == 15
     assert replay.request_tokens({"messages": [{"content": "abc"}], "max_tokens": 4}) == 7
+
+
+def test_request_slot_fifo_replay(server_url, tmp_path):
+    from packmla.bench import replay
+
+    url, eng = server_url
+    path = tmp_path / "slots.jsonl"
+    with open(path, "w") as f:
+        for s in range(4):
+            for t in range(2):
+                f.write(json.dumps({"session": f"s{s}", "turn": t, "max_tokens": 2,
+                                    "messages": [{"role": "user", "content": f"slot {s}/{t}"}]}) + "\n")
+    out = replay.main(["--base-url", url, "--requests", str(path), "--scheduler", "request-slot", "--users", "2",
+                       "--population", "3", "--duration-s", "120", "--min-success", "1.0"])
+    assert out["finished"] == 8 and out["unresolved"] == 0 and out["completed_in_window"] == 8
+    assert out["slo"]["status"] == "pass" and out["passed"]
+    assert out["client_queue_ms"]["p50"] >= 0
+    with pytest.raises(ValueError):
+        replay.request_slot_replay(url, str(path), 3, 2, 10.0)  # population below concurrency
+    assert replay.slo_status(9, 0, 10) == "pass"
+    assert replay.slo_status(8, 0, 10) == "fail"
+    assert replay.slo_status(8, 1, 10) == "indeterminate"
