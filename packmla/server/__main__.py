@@ -72,14 +72,19 @@ def build_parser() -> argparse.ArgumentParser:
     ref.add_argument("--hicache-mem-layout", default="page_first", choices=["page_first", "layer_first"],
                      help="accepted; packmla's host tier is page-first")
     ref.add_argument("--hicache-write-policy", default="write_through", choices=["write_through"])
-    for flag in ("--enable-metrics", "--log-requests", "--skip-server-warmup", "--trust-remote-code",
-                 "--disable-radix-cache", "--disable-overlap-schedule", "--disable-flashinfer-autotune",
-                 "--language-model-only"):
+    ref.add_argument("--enable-metrics", action="store_true", help="accepted; /metrics is always served")
+    ref.add_argument("--log-requests", action="store_true", help="log every finished request (JSON)")
+    ref.add_argument("--log-requests-level", type=int, default=0, choices=[0, 1, 2, 3],
+                     help="0 timing, 1 + sampling parameters, 2 + first 64 output ids, 3 + all token ids")
+    ref.add_argument("--export-metrics-to-file", action="store_true",
+                     help="append per-request metrics as JSON lines under --export-metrics-to-file-dir")
+    ref.add_argument("--export-metrics-to-file-dir", default=None)
+    for flag in ("--skip-server-warmup", "--trust-remote-code", "--disable-radix-cache", "--disable-overlap-schedule",
+                 "--disable-flashinfer-autotune", "--language-model-only"):
         ref.add_argument(flag, action="store_true", help="accepted; no effect in packmla")
-    for flag in ("--log-requests-level", "--export-metrics-to-file-dir", "--reasoning-parser", "--tool-call-parser",
-                 "--model-type", "--dsa-decode-backend", "--dsa-prefill-backend", "--dsv4-attn-backend"):
+    for flag in ("--reasoning-parser", "--tool-call-parser", "--model-type", "--dsa-decode-backend",
+                 "--dsa-prefill-backend", "--dsv4-attn-backend"):
         ref.add_argument(flag, default=None, help="accepted; no effect in packmla")
-    ref.add_argument("--export-metrics-to-file", action="store_true", help="accepted; no effect in packmla")
     return ap
 
 
@@ -114,6 +119,22 @@ def resolve_args(args) -> dict:
         kw["cuda_graph_bs"] = bs
     kw["disable_cuda_graph"] = disable_graphs
     return kw
+
+
+def request_logger(args):
+    """The `RequestLogger` of the --log-requests / --export-metrics-to-file flags (None when both are off)."""
+    from .request_log import RequestLogger
+
+    if args.export_metrics_to_file and not args.export_metrics_to_file_dir:
+        raise SystemExit("--export-metrics-to-file needs --export-metrics-to-file-dir")
+    export = args.export_metrics_to_file_dir if args.export_metrics_to_file else None
+    if not args.log_requests and export is None:
+        return None
+    if args.log_requests:
+        import logging
+
+        logging.basicConfig(level=logging.INFO, format="%(asctime)s %(name)s %(message)s")
+    return RequestLogger(args.log_requests, args.log_requests_level, export)
 
 
 def model_config(name: str):
@@ -192,7 +213,8 @@ def main(argv=None) -> None:
         else:
             comm = TPComm()
     eng, ecfg = build_engine(args, rank, local, world, comm)
-    driver = EngineDriver(eng, rank, world, cpu_group, watchdog_s=args.watchdog_timeout)
+    driver = EngineDriver(eng, rank, world, cpu_group, watchdog_s=args.watchdog_timeout,
+                          request_logger=request_logger(args) if rank == 0 else None)
     name = args.served_model_name or os.path.basename(str(args.model))
     if rank != 0:
         driver.run_worker()

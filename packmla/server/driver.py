@@ -35,17 +35,21 @@ class Stream:
     done: threading.Event = field(default_factory=threading.Event)
     t_submit: float = 0.0
     t_first: float | None = None
+    params: SamplingParams | None = None
+    prompt: list[int] | None = None  # kept only when the request log records prompt ids
 
 
 class EngineDriver:
     IDLE_WAIT_S = 0.02
 
     def __init__(self, engine: Engine, rank: int = 0, world: int = 1, cpu_group=None, watchdog_s: float = 1800.0,
-                 error_check_every: int = 16, fault_hook=None):
+                 error_check_every: int = 16, fault_hook=None, request_logger=None):
         """`watchdog_s`: a step running longer marks the server unhealthy (reference: --watchdog-timeout);
         `error_check_every`: steps between reads of the kernels' device error word (CUDA engines);
-        `fault_hook(step)`: host-side fault injection for tests, called before every step."""
+        `fault_hook(step)`: host-side fault injection for tests, called before every step;
+        `request_logger`: a `RequestLogger` given every finished request."""
         self.engine = engine
+        self.request_logger = request_logger
         self.watchdog_s = watchdog_s
         self.error_check_every = error_check_every
         self.fault_hook = fault_hook
@@ -85,7 +89,9 @@ class EngineDriver:
         if need > self.engine.pool.max_context:
             raise ValueError(f"prompt + max_tokens = {need} exceeds the context limit {self.engine.pool.max_context}")
         ext = next(self._ext_ids)
-        st = Stream(ext, len(prompt), loop, asyncio.Queue() if loop is not None else None, t_submit=time.perf_counter())
+        keep_prompt = self.request_logger is not None and self.request_logger.log_level >= 3
+        st = Stream(ext, len(prompt), loop, asyncio.Queue() if loop is not None else None, t_submit=time.perf_counter(),
+                    params=params, prompt=list(prompt) if keep_prompt else None)
         self._streams[ext] = st
         self._inbox.put(("add", ext, list(prompt), params))
         return st
@@ -161,6 +167,14 @@ class EngineDriver:
         st.finish_reason = reason
         st.done.set()
         self._deliver_to(st, None)
+        self._log(st)
+
+    def _log(self, st: Stream) -> None:
+        if self.request_logger is not None:
+            try:
+                self.request_logger.finished(st, st.prompt)
+            except OSError:  # a full or vanished export directory must not stop serving
+                self.engine.metrics.inc("request_log_errors")
 
     def _deliver_to(self, st: Stream, item) -> None:
         if st.queue is not None and st.loop is not None:
@@ -211,6 +225,7 @@ class EngineDriver:
                 st.finish_reason = "error"
                 st.done.set()
                 self._deliver_to(st, None)
+                self._log(st)
             self._streams.clear()
             if reraise:
                 raise

@@ -44,3 +44,38 @@ def test_selectors_and_rejections():
     _, kw = _resolve("--dsv4-c4-cache-keep-count", "192")
     with pytest.raises(ValueError):  # Direct serving keeps 256 survivors only
         EngineConfig(**kw).validate()
+
+
+def test_request_log_and_metric_export(tmp_path, caplog):
+    import logging
+
+    from packmla.config import ModelConfig
+    from packmla.engine.engine import Engine, SamplingParams
+    from packmla.server.__main__ import request_logger
+    from packmla.server.driver import EngineDriver
+
+    args, _ = _resolve("--log-requests", "--log-requests-level", "3", "--export-metrics-to-file",
+                       "--export-metrics-to-file-dir", str(tmp_path / "m"), "--device", "cpu")
+    rl = request_logger(args)
+    assert rl.log_requests and rl.log_level == 3 and rl.export_dir == str(tmp_path / "m")
+    assert request_logger(_resolve("--device", "cpu")[0]) is None
+    with pytest.raises(SystemExit):  # export without a directory
+        request_logger(_resolve("--export-metrics-to-file")[0])
+    cfg = ModelConfig.tiny(num_layers=2)
+    eng = Engine.build(cfg, EngineConfig(device="cpu", max_running_requests=2, cuda_graph_bs=[1, 2]), "cpu",
+                       max_context=256)
+    driver = EngineDriver(eng, request_logger=rl).start()
+    try:
+        with caplog.at_level(logging.INFO, logger="packmla.requests"):
+            for n in (3, 5):
+                driver.generate([5, 6, 7, 8], SamplingParams(max_new_tokens=n))
+    finally:
+        driver.stop()
+    files = list((tmp_path / "m").glob("request-metrics-*.jsonl"))
+    assert len(files) == 1
+    recs = [json.loads(line) for line in files[0].read_text().splitlines()]
+    assert [r["completion_tokens"] for r in recs] == [3, 5] and all(r["finish_reason"] == "length" for r in recs)
+    assert recs[1]["prompt_ids"] == [5, 6, 7, 8] and len(recs[1]["output_ids"]) == 5
+    assert recs[1]["sampling_params"]["max_new_tokens"] == 5
+    assert all(r["ttft_s"] is not None and r["e2e_s"] >= r["ttft_s"] for r in recs) and recs[1]["tpot_s"] > 0
+    assert sum("request finished" in m for m in caplog.messages) == 2
