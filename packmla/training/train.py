@@ -269,7 +269,10 @@ def run(cache: Path, policy: Path, output: Path, *, recipe: str, layers: tuple[i
             final.unlink(missing_ok=True)
         raise
     finally:
-        tmp.unlink(missing_ok=True)
+        try:
+            tmp.unlink(missing_ok=True)
+        except OSError:  # a staging name left behind does not invalidate the published policy
+            pass
     Math.atomic_json(output / "progress.json", {"layers": done, "complete": True})
     return {"layers": done, "output": str(output), "policy": str(output / "policy.json")}
 

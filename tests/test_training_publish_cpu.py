@@ -1,0 +1,114 @@
+"""CPU: publication of a trained policy fails closed.  Every injected failure (staging, link,
+interrupt, a competing writer, an interrupt after the link) leaves no policy.json of this run and
+keeps the finished layers' files; a failed clean-up of the staging name leaves the policy valid."""
+import json
+import os
+from pathlib import Path
+
+import pytest
+
+from packmla.config import ModelConfig
+from packmla.training import train
+from packmla.training.calibration import Math
+
+
+@pytest.fixture(scope="module")
+def prepared(tmp_path_factory):
+    from packmla.training.data.capture import capture_cache
+
+    root = tmp_path_factory.mktemp("publish")
+    capture_cache(root / "cache", ModelConfig.tiny(num_layers=2), issues=3, development=1, train_queries=1,
+                  dev_queries=1, prompt_len=64)
+    init = train.main(["--cache", str(root / "cache"), "--init-policy", str(root / "init")])
+    return root, init["policy"]
+
+
+def _run(root, policy, name):
+    return train.main(["--cache", str(root / "cache"), "--policy", policy, "--output", str(root / name),
+                       "--recipe", "rank64", "--epochs", "1", "--threads", "2"])
+
+
+def _fail_stage(monkeypatch):
+    real = Math.atomic_json
+
+    def atomic_json(path, obj):
+        if Path(path).name == ".policy.json.tmp":
+            raise OSError("disk full while staging")
+        real(path, obj)
+
+    monkeypatch.setattr(Math, "atomic_json", staticmethod(atomic_json))
+    return OSError
+
+
+def _fail_link(monkeypatch):
+    def link(src, dst, *a, **k):
+        raise OSError("link refused")
+
+    monkeypatch.setattr(os, "link", link)
+    return OSError
+
+
+def _interrupt_link(monkeypatch):
+    def link(src, dst, *a, **k):
+        raise KeyboardInterrupt
+
+    monkeypatch.setattr(os, "link", link)
+    return KeyboardInterrupt
+
+
+def _interrupt_after_link(monkeypatch):
+    real = os.stat
+
+    def stat(p, *a, **k):
+        if str(p).endswith(os.path.join("_interrupt_after_link", "policy.json")):
+            raise KeyboardInterrupt
+        return real(p, *a, **k)
+
+    monkeypatch.setattr(os, "stat", stat)
+    return KeyboardInterrupt
+
+
+@pytest.mark.parametrize("inject", [_fail_stage, _fail_link, _interrupt_link, _interrupt_after_link])
+def test_failed_publication_leaves_no_policy(prepared, monkeypatch, inject):
+    root, policy = prepared
+    name = inject.__name__
+    exc = inject(monkeypatch)
+    with pytest.raises(exc):
+        _run(root, policy, name)
+    monkeypatch.undo()
+    out = root / name
+    assert not (out / "policy.json").exists() and not (out / ".policy.json.tmp").exists()
+    assert json.loads((out / "progress.json").read_text())["complete"] is False
+    assert list(out.glob("selected-layer-*.json"))  # finished layers are kept
+
+
+def test_competing_writer_is_not_overwritten(prepared, monkeypatch):
+    root, policy = prepared
+    real = os.link
+
+    def link(src, dst, *a, **k):
+        Path(dst).write_text('{"competitor": true}')
+        return real(src, dst, *a, **k)
+
+    monkeypatch.setattr(os, "link", link)
+    with pytest.raises(FileExistsError):
+        _run(root, policy, "competitor")
+    monkeypatch.undo()
+    assert json.loads((root / "competitor" / "policy.json").read_text()) == {"competitor": True}
+
+
+def test_failed_cleanup_keeps_published_policy(prepared, monkeypatch):
+    root, policy = prepared
+    real = Path.unlink
+
+    def unlink(self, *a, **k):
+        if self.name == ".policy.json.tmp":
+            raise OSError("cannot remove staging name")
+        return real(self, *a, **k)
+
+    monkeypatch.setattr(Path, "unlink", unlink)
+    out = _run(root, policy, "cleanup")
+    monkeypatch.undo()
+    pub = json.loads(Path(out["policy"]).read_text())
+    assert pub["trained_layers"] == out["layers"]
+    assert json.loads((root / "cleanup" / "progress.json").read_text())["complete"] is True
