@@ -112,3 +112,28 @@ def test_failed_cleanup_keeps_published_policy(prepared, monkeypatch):
     pub = json.loads(Path(out["policy"]).read_text())
     assert pub["trained_layers"] == out["layers"]
     assert json.loads((root / "cleanup" / "progress.json").read_text())["complete"] is True
+
+
+def test_cache_rejects_corrupt_incomplete_and_reused(prepared, tmp_path):
+    import shutil
+
+    from packmla.training.data.cache import layer_file, load_cached_layer, write_cache
+
+    root, _ = prepared
+    layer = json.loads((root / "cache" / "config.json").read_text())["layers"][0]
+    assert set(load_cached_layer(root / "cache", layer)) == {"train", "development"}
+    bad = tmp_path / "bad"
+    shutil.copytree(root / "cache", bad)
+    payload = bad / layer_file(layer)
+    data = bytearray(payload.read_bytes())
+    data[len(data) // 2] ^= 0xFF  # one flipped byte in the middle of the payload
+    payload.write_bytes(bytes(data))
+    with pytest.raises(ValueError, match="payload changed"):
+        load_cached_layer(bad, layer)
+    partial = tmp_path / "partial"
+    shutil.copytree(root / "cache", partial)
+    (partial / "progress.json").write_text(json.dumps({"status": "writing"}))
+    with pytest.raises(ValueError, match="complete"):
+        load_cached_layer(partial, layer)
+    with pytest.raises(ValueError, match="fresh cache directory"):
+        write_cache(root / "cache", {}, {"train": [], "development": []}, {})
