@@ -170,11 +170,12 @@ def main() -> None:
     # ---------------- end-to-end through Engine.step()
     comm.barrier()
     torch.cuda.synchronize(device)
-    t1 = time.perf_counter()
-    for _ in range(args.steps):
-        eng.step()
-    torch.cuda.synchronize(device)
-    e2e_s = time.perf_counter() - t1
+    with ClockSampler(local) as clk_e2e:  # its own clock record: the two windows can run at different clocks
+        t1 = time.perf_counter()
+        for _ in range(args.steps):
+            eng.step()
+        torch.cuda.synchronize(device)
+        e2e_s = time.perf_counter() - t1
     comm.barrier()
     e2e_s = comm.max_over_ranks(e2e_s, device)
     check_errors(device)
@@ -212,7 +213,8 @@ def main() -> None:
             "kv_capacity_vs_native": round(direct_cap / native_cap, 4),
         },
         "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": eng.h2d_bytes_last,
-                "d2h_bytes_per_step": eng.d2h_bytes_last},
+                "d2h_bytes_per_step": eng.d2h_bytes_last, "ms_per_step": round(e2e_s * 1000 / args.steps, 4),
+                "clocks": clk_e2e.summary()},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "setup_s": round(t_build, 1),
