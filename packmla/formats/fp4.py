@@ -62,7 +62,7 @@ def e2m1_decode(codes: torch.Tensor) -> torch.Tensor:
 def _scales(rows: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-16 E4M3 scale codes (uint8) and their fp32 values."""
     amax = rows.view(rows.shape[0], GROUPS, GROUP).abs().amax(-1)
-    s = (amax / 6.0).to(torch.float8_e4m3fn)
+    s = (amax / 6.0).clamp(max=448.0).to(torch.float8_e4m3fn)  # E4M3 has no infinity: saturate
     return s.view(torch.uint8), s.float()
 
 

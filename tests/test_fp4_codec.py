@@ -122,3 +122,11 @@ def test_page_layout_data_rows_then_scale_rows():
             assert torch.equal(back, fp4.native_decode(*fp4.native_encode(rows)))
         else:
             assert torch.equal(back, fp4.packed_decode(*fp4.packed_encode(rows)))
+
+
+def test_huge_groups_saturate_the_scale():
+    rows = torch.zeros(1, 512)
+    rows[0, :16] = 1e6
+    codes, scales = fp4.native_encode(rows)
+    assert scales[0, 0].view(torch.float8_e4m3fn).float().item() == 448.0
+    assert bool(torch.isfinite(fp4.native_decode(codes, scales)).all())
