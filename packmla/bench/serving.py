@@ -128,10 +128,28 @@ def server_info(url: str) -> dict:
     return requests.get(url + "/server_info", timeout=60).json()
 
 
-def bench(url: str, dataset: str, input_len: int, output_len: int, concurrency: int, *, vocab: int | None = None,
+def resolve_concurrency(requested, info: dict, input_len: int, output_len: int) -> int:
+    """`auto`: as many complete requests as the running server's KV pool holds (reference:
+    scripts/local/bench-serving.sh `auto`); rejects a request that exceeds the server's context."""
+    ctx = info.get("context_length")
+    if ctx is not None and input_len + output_len > ctx:
+        raise SystemExit(f"input + output = {input_len + output_len} exceeds the server's context {ctx}")
+    if requested == "auto":
+        c = int(info["max_total_num_tokens"]) // (input_len + output_len)
+        if c < 1:
+            raise SystemExit("the server's KV pool cannot hold one complete request")
+        return c
+    c = int(requested)
+    if c < 1:
+        raise SystemExit("concurrency must be a positive integer or auto")
+    return c
+
+
+def bench(url: str, dataset: str, input_len: int, output_len: int, concurrency: int | str, *, vocab: int | None = None,
           model: str = "default", flush_cache: bool = True, seed: int = 0, prefix_len: int = 0, num_groups: int = 1,
           turns: int = 1, sessions: int = 0) -> dict:
     info = server_info(url)
+    concurrency = resolve_concurrency(concurrency, info, input_len, output_len)
     vocab = vocab or info.get("model_config", {}).get("vocab_size", 32000)
     n_warm, n_meas = concurrency, 3 * concurrency
     out = {"dataset": dataset, "concurrency": concurrency, "input_len": input_len, "output_len": output_len,
@@ -170,7 +188,7 @@ def main(argv=None) -> None:
     ap.add_argument("--dataset", choices=["random", "shared-prefix", "multi-turn"], default="random")
     ap.add_argument("--input-len", type=int, default=32768)
     ap.add_argument("--output-len", type=int, default=256)
-    ap.add_argument("--concurrency", type=int, default=8)
+    ap.add_argument("--concurrency", default="8", help="a positive integer, or auto (what the KV pool holds)")
     ap.add_argument("--prefix-len", type=int, default=0)
     ap.add_argument("--num-groups", type=int, default=1)
     ap.add_argument("--turns", type=int, default=4)

@@ -368,6 +368,7 @@ class Engine:
             "max_total_num_tokens": self.capacity.max_total_tokens,
             "bytes_per_full_token": self.capacity.bytes_per_full_token,
             "num_pages": self.pool.num_pages,
+            "context_length": self.pool.max_context,
             "max_running_requests": self.pool.max_requests - 1,
             "cuda_graph_bs": self.runner.buckets,
             "tp": self.ecfg.tp,

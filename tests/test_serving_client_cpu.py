@@ -152,3 +152,19 @@ def test_request_slot_fifo_replay(server_url, tmp_path):
     assert replay.slo_status(9, 0, 10) == "pass"
     assert replay.slo_status(8, 0, 10) == "fail"
     assert replay.slo_status(8, 1, 10) == "indeterminate"
+
+
+def test_auto_concurrency_from_the_server_pool(server_url):
+    import requests
+
+    from packmla.bench.serving import resolve_concurrency
+
+    url, eng = server_url
+    info = requests.get(url + "/server_info", timeout=30).json()
+    assert info["context_length"] == eng.pool.max_context
+    assert resolve_concurrency("auto", info, 100, 28) == info["max_total_num_tokens"] // 128
+    assert resolve_concurrency("3", info, 100, 28) == 3
+    with pytest.raises(SystemExit):  # longer than the server's context
+        resolve_concurrency("1", info, info["context_length"], 1)
+    with pytest.raises(SystemExit):  # the pool cannot hold one request
+        resolve_concurrency("auto", {"max_total_num_tokens": 10}, 100, 28)
