@@ -168,3 +168,41 @@ def test_auto_concurrency_from_the_server_pool(server_url):
         resolve_concurrency("1", info, info["context_length"], 1)
     with pytest.raises(SystemExit):  # the pool cannot hold one request
         resolve_concurrency("auto", {"max_total_num_tokens": 10}, 100, 28)
+
+
+def test_convert_recorded_traffic(tmp_path):
+    from packmla.bench import convert, replay
+
+    raw = tmp_path / "raw.jsonl"
+    recs = [
+        {"id": "b2", "token_name": "u2", "created": 5.0, "messages": [{"role": "user", "content": "b second"}],
+         "usage": {"prompt_tokens": 40, "completion_tokens": 7}},
+        {"id": "a1", "token_name": "u1", "created": 1.0, "messages": [{"role": "user", "content": "a first"}],
+         "usage": {"prompt_tokens": 10, "completion_tokens": 3}, "tools": [{"type": "function"}]},
+        {"id": "b1", "token_name": "u2", "created": 2.0, "messages": [{"role": "user", "content": "b first"}],
+         "usage": {"prompt_tokens": 20}},
+        {"id": "solo", "created": 3.0, "messages": [{"role": "user", "content": "alone"}], "usage": {}},
+    ]
+    raw.write_text("\n".join(json.dumps(r) for r in recs) + "\n\n")
+    out = convert.main(["--input", str(raw), "--output-dir", str(tmp_path / "prep")])
+    assert out == {"output_dir": str((tmp_path / "prep").resolve()), "requests": 4, "sessions": 3}
+    sessions = replay.load_sessions(str(tmp_path / "prep" / "sessions.jsonl"))
+    assert [[t["request_id"] for t in s] for s in sessions] == [["a1"], ["b1", "b2"], ["solo"]]
+    assert [t["turn"] for t in sessions[1]] == [0, 1]
+    assert sessions[1][0]["max_tokens"] == 256 and sessions[1][1]["max_tokens"] == 7  # default cap when unrecorded
+    assert sessions[0][0]["tools"] == [{"type": "function"}] and sessions[0][0]["ignore_eos"] is False
+    lines = (tmp_path / "prep" / "requests.jsonl").read_text().splitlines()
+    assert [json.loads(x)["request_id"] for x in lines] == ["b2", "a1", "b1", "solo"]  # source order
+    man = json.loads((tmp_path / "prep" / "manifest.json").read_text())
+    assert man["requests"] == 4 and [e["used_default_output_cap"] for e in man["records"]] == [False, False, True, True]
+    # tick 0: a1 (10 + 3) and b1 (20 + 256); tick 1: b2 (40 + 7) and solo (5 content bytes + 256)
+    assert replay.peak_live_tokens(sessions, 2) == max(13 + 276, 47 + 261)
+    for bad, msg in ((dict(recs[1], id="b2"), "duplicate"), (dict(recs[1], created=float("nan")), "created"),
+                     (dict(recs[1], messages=[]), "messages"), (dict(recs[1], usage=None), "usage")):
+        p = tmp_path / "bad.jsonl"
+        p.write_text(json.dumps(recs[0]) + "\n" + json.dumps(bad) + "\n")
+        with pytest.raises(ValueError, match=msg):
+            convert.convert(str(p), str(tmp_path / f"o-{msg}"))
+        assert not (tmp_path / f"o-{msg}").exists()
+    with pytest.raises(ValueError, match="exists"):
+        convert.convert(str(raw), str(tmp_path / "prep"))
