@@ -3,12 +3,18 @@
     python -m packmla.bench.microbench moe   [--tokens 40] [--experts 256] [--topk 8]
     python -m packmla.bench.microbench decode [--batch 16] [--heads 128] [--context 32768] [--topk 2048]
     python -m packmla.bench.microbench store  [--rows 24]
+    python -m packmla.bench.microbench decode-paired [--batch 16] [--context 32768] [--with-adapter]
+    python -m packmla.bench.microbench decode-suite [--paired]
 
 Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
 measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
 
 Reference protocol: 30 rounds after 10 warm-ups, CUDA-graph-free device timing of the
-operation only (benchmarks/microbench/dsv4-flash-decode-store/README.md:11-23).
+operation only (benchmarks/microbench/dsv4-flash-decode-store/README.md:11-23).  Paired rounds
+(`decode-paired`, `decode-suite --paired`; reference: the balanced paired timing loop of its
+GLM/V4.1 suites) time every mode once per round, in an order rotated each round so drift and
+position effects cancel, and report each mode's mean and the per-round latency ratios against the
+first mode (geometric mean, min, max).
 """
 from __future__ import annotations
 
@@ -190,6 +196,9 @@ def bench_decode(args, dev):
         def fn():
             kv_ops.packed_to_native(planes.values, planes.bitmap, planes.scales, src_rows, src_pos, freqs, wsn, dst)
             return attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, **args_a)
+    nbytes = B * (K * rec_bytes + W * abi.NATIVE_RECORD_BYTES) + q.numel() * 2 + out.numel() * 2
+    if getattr(args, "build_only", False):
+        return fn, {"kv_format": args.kv_format, "bytes": nbytes, "splits": ws.splits, "tile_rows": ws.tile_rows}
     us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev), graph=True)
     check_errors(dev)
     phases = None
@@ -211,7 +220,6 @@ def bench_decode(args, dev):
         per = torch.tensor(pv[16:16 + 2 * min(ctas, 1024)]).view(-1, 2).float() / 1e3
         phases["cta_total_us_min_med_max"] = [round(float(x), 1) for x in
                                               (per[:, 0].min(), per[:, 0].median(), per[:, 0].max())]
-    nbytes = B * (K * rec_bytes + W * abi.NATIVE_RECORD_BYTES) + q.numel() * 2 + out.numel() * 2
     flops = 4 * B * Hh * (K + W) * 512
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
@@ -220,6 +228,71 @@ def bench_decode(args, dev):
             "swa": W, "context": args.context, "splits": ws.splits, "tile_rows": ws.tile_rows, "us": round(us, 2), "bytes": nbytes,
             "GBps": round(gbs, 1), "hbm_fraction": round(gbs / peak, 3), "TFLOPs": round(flops / us / 1e6, 1),
             "peak_note": tag}
+
+
+def paired_rounds(timers: dict, rounds: int) -> dict:
+    """Run every timer once per round, the order rotated by one mode each round; timers return
+    microseconds.  Ratios are per round against the first mode."""
+    modes = list(timers)
+    if rounds < 1 or not modes:
+        raise ValueError("at least one round and one mode required")
+    samples = {m: [] for m in modes}
+    for r in range(rounds):
+        k = r % len(modes)
+        for m in modes[k:] + modes[:k]:
+            samples[m].append(float(timers[m]()))
+    base = modes[0]
+    out = {"rounds": rounds, "order": "rotated", "baseline": base,
+           "mean_us": {m: round(sum(v) / len(v), 3) for m, v in samples.items()}, "ratio": {}}
+    for m in modes[1:]:
+        ratios = [a / b for a, b in zip(samples[m], samples[base])]
+        geo = math.exp(sum(math.log(x) for x in ratios) / len(ratios))
+        out["ratio"][f"{m}/{base}"] = {"geomean": round(geo, 5), "change_pct": round((geo - 1) * 100, 3),
+                                       "min": round(min(ratios), 5), "max": round(max(ratios), 5)}
+    return out
+
+
+def bench_decode_paired(args, dev, modes=("native", "direct")) -> dict:
+    """Decode modes built side by side, each captured in a CUDA graph, timed in paired rounds."""
+    import copy
+
+    from packmla.ops import check_errors
+
+    from .timing import ClockSampler
+
+    flush = L2Flush(dev)
+    graphs, meta = {}, {}
+    for m in modes:
+        a = copy.copy(args)
+        a.kv_format, a.build_only = m, True
+        fn, meta[m] = bench_decode(a, dev)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        graphs[m] = g
+    check_errors(dev)
+
+    def timer(g):
+        def run() -> float:
+            flush()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            g.replay()
+            e.record()
+            torch.cuda.synchronize(dev)
+            return s.elapsed_time(e) * 1e3
+        return run
+
+    with ClockSampler(torch.device(dev).index or 0) as clk:
+        res = paired_rounds({m: timer(graphs[m]) for m in modes}, args.rounds)
+    check_errors(dev)
+    for g in graphs.values():
+        g.reset()
+    return {"case": "sparse_mla_decode_paired", "batch": args.batch, "heads": args.heads, "topk": args.topk,
+            "swa": args.swa, "context": args.context, "modes": meta, **res, "clocks": clk.summary()}
 
 
 def bench_store(args, dev):
@@ -245,7 +318,7 @@ def bench_store(args, dev):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite"],
+    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite", "decode-paired"],
                     help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
                          "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
@@ -261,6 +334,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--precision", default="default", choices=["default", "bf16"])
     ap.add_argument("--prof", action="store_true", help="report kernel phase / wait-time counters")
+    ap.add_argument("--paired", action="store_true", help="decode-suite: native and direct in paired rounds")
+    ap.add_argument("--with-adapter", action="store_true", help="decode-paired: add the adapter mode")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     if args.case == "moe":
@@ -269,11 +344,21 @@ def main():
     elif args.case == "decode":
         args.topk = args.topk or 2048
         out = bench_decode(args, dev)
+    elif args.case == "decode-paired":
+        args.topk = args.topk or 2048
+        modes = ("native", "direct", "adapter") if args.with_adapter else ("native", "direct")
+        print(json.dumps(bench_decode_paired(args, dev, modes)), flush=True)
+        return
     elif args.case == "decode-suite":
         args.topk = args.topk or 2048
         args.heads = 128
         for ctx in (32768, 131072):
             for batch in (1, 16, 64):
+                if args.paired:
+                    args.context, args.batch = ctx, batch
+                    print(json.dumps(bench_decode_paired(args, dev)), flush=True)
+                    torch.cuda.empty_cache()
+                    continue
                 for fmt in ("native", "direct"):
                     args.context, args.batch, args.kv_format = ctx, batch, fmt
                     row = bench_decode(args, dev)
