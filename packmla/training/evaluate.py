@@ -122,9 +122,12 @@ def _fresh(paths: list[Path]) -> None:
         raise ValueError(f"fresh output paths required (exists: {', '.join(taken)})")
 
 
-def _write_reports(output: Path, result: dict) -> list[str]:
+def _write_reports(output: Path, result: dict, created: list[Path]) -> list[str]:
+    """CSV, Markdown and (retention sweep, with matplotlib) PNG reports; every file is appended to
+    `created` as soon as it exists so that a failure can remove the partial report."""
     fields = ("method", "retained_features", "mean", "p95")
     with output.with_suffix(".csv").open("x", newline="") as f:
+        created.append(output.with_suffix(".csv"))  # only after the exclusive create succeeded
         w = csv.DictWriter(f, fieldnames=fields)
         w.writeheader()
         w.writerows({k: row[k] for k in fields} for row in result["summary"])
@@ -140,6 +143,7 @@ def _write_reports(output: Path, result: dict) -> list[str]:
                   "query-layer examples per method.",
               "The learned scorer was trained at 256 survivors and is reused unchanged at other budgets.", ""]
     with output.with_suffix(".md").open("x") as f:
+        created.append(output.with_suffix(".md"))
         f.write("\n".join(lines))
     files = [str(output.with_suffix(".csv")), str(output.with_suffix(".md"))]
     if result.get("retention_sweep"):
@@ -160,6 +164,7 @@ def _write_reports(output: Path, result: dict) -> list[str]:
             ax.set(xlabel="retained latent coordinates (of 512)", ylabel=f"{metric} relative output error (%)")
             ax.legend()
             path = output.parent / f"{output.stem}-{metric}.png"
+            created.append(path)
             fig.savefig(path, dpi=150)
             plt.close(fig)
             files.append(str(path))
@@ -180,7 +185,8 @@ def compare_masks(cache: Path, policy: Path, output: Path, *, layers: tuple[int,
     output = Path(output)
     if output.suffix != ".json":
         raise ValueError("output must be a .json path")
-    _fresh([output, output.with_suffix(".csv"), output.with_suffix(".md")])
+    _fresh([output, output.with_suffix(".csv"), output.with_suffix(".md")]
+           + ([output.parent / f"{output.stem}-{m}.png" for m in ("mean", "p95")] if retention_sweep else []))
     torch.set_num_threads(threads)
     math, ref = Math(), reference()
     allowed = tuple(json.loads((Path(cache) / "config.json").read_text())["layers"])
@@ -216,8 +222,16 @@ def compare_masks(cache: Path, policy: Path, output: Path, *, layers: tuple[int,
                            "query_layer_examples": len(expected)},
               "settings": {"cache": str(Path(cache).resolve()), "policy": str(Path(policy).resolve()),
                            "torch": torch.__version__, "threads": threads}}
-    result["files"] = _write_reports(output, result)
-    Math.atomic_json(output, result)
+    # the JSON is the completion marker, written last; any failure removes the partial report
+    # (reference: training/evaluate.py report publication, tested by its report-rollback case)
+    created: list[Path] = []
+    try:
+        result["files"] = _write_reports(output, result, created)
+        Math.atomic_json(output, result)
+    except BaseException:
+        for path in created + [output]:
+            path.unlink(missing_ok=True)
+        raise
     return {"output": str(output), "summary": [{k: r[k] for k in ("method", "mean", "p95")} for r in summary]}
 
 

@@ -137,3 +137,26 @@ def test_cache_rejects_corrupt_incomplete_and_reused(prepared, tmp_path):
         load_cached_layer(partial, layer)
     with pytest.raises(ValueError, match="fresh cache directory"):
         write_cache(root / "cache", {}, {"train": [], "development": []}, {})
+
+
+def test_failed_report_is_rolled_back(prepared, monkeypatch, tmp_path):
+    from packmla.training import evaluate
+
+    root, init = prepared
+    policy = _run(root, init, "for-report")["policy"]  # evaluation needs a trained rank-64 policy
+    real = Math.atomic_json
+
+    def atomic_json(path, obj):
+        if Path(path).name == "cmp.json":
+            raise KeyboardInterrupt
+        real(path, obj)
+
+    monkeypatch.setattr(Math, "atomic_json", staticmethod(atomic_json))
+    with pytest.raises(KeyboardInterrupt):
+        evaluate.main(["--cache", str(root / "cache"), "--policy", policy, "--output", str(tmp_path / "cmp.json"),
+                       "--compare-masks", "--threads", "2"])
+    monkeypatch.undo()
+    assert sorted(p.name for p in tmp_path.iterdir()) == []  # no partial csv / md / json
+    out = evaluate.main(["--cache", str(root / "cache"), "--policy", policy, "--output", str(tmp_path / "cmp.json"),
+                         "--compare-masks", "--threads", "2"])
+    assert {p.name for p in tmp_path.iterdir()} == {"cmp.json", "cmp.csv", "cmp.md"} and out["summary"]
