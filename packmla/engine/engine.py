@@ -242,6 +242,7 @@ class Engine:
                         self.pool.release(r.slot)
                     r.finished = True
                     self.done[rid] = r
+                    self.metrics.inc("requests_aborted")
                     return True
         return False
 

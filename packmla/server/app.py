@@ -114,19 +114,25 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             raise HTTPException(503, str(exc)) from exc
 
     async def _tokens(st, rule: _StopRule | None):
-        """Tokens of one request as they arrive; a stop rule that fires aborts the request early."""
-        stopped = False
-        while True:
-            item = await st.queue.get()
-            if item is None:
-                break
-            if stopped:
-                continue  # produced before the abort reached the engine
-            if rule is not None and rule.active and not rule.accept(item):
-                stopped = True
+        """Tokens of one request as they arrive; a stop rule that fires aborts the request early, and so
+        does a consumer that goes away first (a client that disconnected, a cancelled handler)."""
+        stopped = ended = False
+        try:
+            while True:
+                item = await st.queue.get()
+                if item is None:
+                    ended = True
+                    break
+                if stopped:
+                    continue  # produced before the abort reached the engine
+                if rule is not None and rule.active and not rule.accept(item):
+                    stopped = True
+                    driver.abort(st.ext_id)
+                    continue
+                yield item
+        finally:
+            if not ended and not stopped:
                 driver.abort(st.ext_id)
-                continue
-            yield item
         if stopped:
             st.finish_reason = "stop"
 

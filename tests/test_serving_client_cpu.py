@@ -206,3 +206,30 @@ def test_convert_recorded_traffic(tmp_path):
         assert not (tmp_path / f"o-{msg}").exists()
     with pytest.raises(ValueError, match="exists"):
         convert.convert(str(raw), str(tmp_path / "prep"))
+
+
+def test_client_disconnect_aborts_the_request(server_url):
+    import asyncio
+
+    import aiohttp
+
+    url, eng = server_url
+    before = eng.metrics.snapshot().get("requests_aborted", 0)
+
+    async def go():
+        async with aiohttp.ClientSession() as http:
+            body = {"model": "tiny", "prompt": "abandon me", "max_tokens": 600, "stream": True, "ignore_eos": True}
+            async with http.post(url + "/v1/completions", json=body) as resp:
+                assert resp.status == 200
+                async for raw in resp.content:
+                    if raw.startswith(b"data: {"):
+                        break  # one token seen; leave without reading the rest
+
+    asyncio.run(go())
+    deadline = time.time() + 30
+    while time.time() < deadline:
+        if eng.metrics.snapshot().get("requests_aborted", 0) > before and not eng.running and not eng.waiting:
+            break
+        time.sleep(0.05)
+    assert eng.metrics.snapshot().get("requests_aborted", 0) == before + 1
+    assert not eng.running and not eng.waiting
