@@ -140,6 +140,7 @@ def replay(url: str, requests_path: str, users: int, model: str = "default", min
            duration_s: float | None = None, ttft_slo_ms: float | None = None) -> dict:
     sessions = load_sessions(requests_path)
     hits0 = _metric(url, "packmla_hicache_hit_tokens")
+    prefix0 = _metric(url, "packmla_prefix_cache_hit_tokens")
     results, wall, started = asyncio.run(_replay(url, model, sessions, users, duration_s))
     ok = [r for r in results if r["ok"]]
 
@@ -163,6 +164,7 @@ def replay(url: str, requests_path: str, users: int, model: str = "default", min
             "ttft_ms": {"p50": pct(ttft, 50), "p90": p90, "p99": pct(ttft, 99)},
             "e2e_ms": {"p50": pct(e2e, 50), "p99": pct(e2e, 99)},
             "hicache_restored_tokens": _metric(url, "packmla_hicache_hit_tokens") - hits0,
+            "prefix_cache_hit_tokens": _metric(url, "packmla_prefix_cache_hit_tokens") - prefix0,
             "errors": [r.get("error") for r in results if not r["ok"]][:5]}
 
 

@@ -143,6 +143,10 @@ class EngineConfig:
     disable_cuda_graph: bool = False
     enable_hierarchical_cache: bool = False
     hicache_ratio: float = 2.0
+    # keep a finished request's KV on the device (its slot and pages) until the space is needed; a later
+    # prompt that extends it adopts the slot and prefills only the new tokens (the reference serves with
+    # SGLang's radix prefix cache on; the server turns this on unless --disable-radix-cache)
+    prefix_cache: bool = False
     keep_count: int = abi.PACKED_KEEP
     swa_full_tokens_ratio: float = 0.1
     random_seed: int = 0

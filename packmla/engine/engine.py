@@ -18,7 +18,7 @@ import contextlib
 import itertools
 import os
 import time
-from collections import deque
+from collections import OrderedDict, deque
 from dataclasses import dataclass, field
 
 import torch
@@ -181,6 +181,8 @@ class Engine:
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self._last_prefill = False
+        # device prefix cache: processed tokens of a finished request -> its retained slot (LRU order)
+        self.retained: OrderedDict[tuple, int] = OrderedDict()
         self.hicache = None
         if engine_cfg.enable_hierarchical_cache:
             from ..kv.hicache import HostKVCache
@@ -247,6 +249,58 @@ class Engine:
         return False
 
     # ------------------------------------------------------------------ scheduling
+    # ------------------------------------------------------------------ device prefix cache
+    def _retain(self, req: Request) -> None:
+        """Keep a finished request's slot: its KV covers every token but the last output."""
+        key = tuple(req.prompt + req.output_ids[:-1])
+        old = self.retained.pop(key, None)
+        if old is not None:
+            self.pool.release(old)
+        self.retained[key] = req.slot
+
+    def _evict_retained(self) -> bool:
+        """Release the least recently used retained slot; False when none is left."""
+        if not self.retained:
+            return False
+        _, slot = self.retained.popitem(last=False)
+        self.pool.release(slot)
+        self.metrics.inc("prefix_cache_evictions")
+        return True
+
+    def _match_retained(self, prompt: list[int]) -> tuple | None:
+        """Longest retained context that is a strict prefix of `prompt` (at least one token to prefill)."""
+        best = None
+        for key in self.retained:
+            if len(key) < len(prompt) and (best is None or len(key) > len(best)) and tuple(prompt[:len(key)]) == key:
+                best = key
+        return best
+
+    def flush_prefix_cache(self) -> None:
+        while self._evict_retained():
+            pass
+
+    def _adopt(self, req: Request, need: int) -> bool | None:
+        """Continue `req` in the retained slot of its longest cached prefix, growing its pages.
+        True: adopted; False: no cached prefix; None: cached, but the pages do not fit yet (a full
+        admission would need more, so the request waits for running requests to finish)."""
+        key = self._match_retained(req.prompt)
+        if key is None:
+            return False
+        slot = self.retained.pop(key)
+        grow = ((need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
+                - len(self.pool._req_pages[slot]))
+        grow128 = ((need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
+                   - len(self.pool._req_c128[slot]))
+        while (grow > self.pool.pages.free or grow128 > self.pool.c128_pages.free) and self._evict_retained():
+            pass
+        if grow > self.pool.pages.free or grow128 > self.pool.c128_pages.free:
+            self.retained[key] = slot  # keep it for later; admission waits for running requests to finish
+            return None
+        self.pool.ensure(slot, need)
+        req.slot, req.prefilled = slot, len(key)
+        self.metrics.inc("prefix_cache_hit_tokens", len(key))
+        return True
+
     def _admit(self) -> Request | None:
         if not self.waiting:
             return None
@@ -256,10 +310,20 @@ class Engine:
             if need > self.pool.max_context:
                 self.waiting.popleft()
                 raise ValueError(f"request {req.rid} needs {need} tokens > max_context {self.pool.max_context}")
-            if len(self.running) >= self.runner.max_b or not self.pool._free_slots:
+            if len(self.running) >= self.runner.max_b:
                 return None
+            if self.retained:
+                adopted = self._adopt(req, need)
+                if adopted is None:
+                    return None
+                if adopted:
+                    return req
             pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
-            if pages_needed > self.pool.pages.free:
+            c128_needed = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
+            while ((not self.pool._free_slots or pages_needed > self.pool.pages.free
+                    or c128_needed > self.pool.c128_pages.free) and self._evict_retained()):
+                pass
+            if not self.pool._free_slots or pages_needed > self.pool.pages.free:
                 return None
             req.slot = self.pool.admit(need)
             if self.hicache is not None:
@@ -348,7 +412,10 @@ class Engine:
             req.t_finish = time.perf_counter()
             if self.hicache is not None:  # write through: every token but the last has its KV stored
                 self.hicache.save(req.slot, req.prompt + req.output_ids[:-1])
-            self.pool.release(req.slot)
+            if self.ecfg.prefix_cache:
+                self._retain(req)
+            else:
+                self.pool.release(req.slot)
             self.done[req.rid] = req
             self.metrics.inc("requests_finished")
 
@@ -359,7 +426,8 @@ class Engine:
         return [self.result(r).output_ids for r in rids]
 
     def flush_cache(self) -> None:
-        """Drop cached KV of finished requests (the HiCache host tier)."""
+        """Drop cached KV of finished requests (device prefix cache and the HiCache host tier)."""
+        self.flush_prefix_cache()
         if self.hicache is not None:
             self.hicache.flush()
 
@@ -373,6 +441,8 @@ class Engine:
             "max_running_requests": self.pool.max_requests - 1,
             "cuda_graph_bs": self.runner.buckets,
             "tp": self.ecfg.tp,
+            "prefix_cache": self.ecfg.prefix_cache,
+            "prefix_cache_retained": len(self.retained),
             "enable_hierarchical_cache": self.hicache is not None,
             "hicache_host_bytes": self.hicache.host_bytes() if self.hicache is not None else 0,
         }

@@ -79,7 +79,10 @@ def build_parser() -> argparse.ArgumentParser:
     ref.add_argument("--export-metrics-to-file", action="store_true",
                      help="append per-request metrics as JSON lines under --export-metrics-to-file-dir")
     ref.add_argument("--export-metrics-to-file-dir", default=None)
-    for flag in ("--skip-server-warmup", "--trust-remote-code", "--disable-radix-cache", "--disable-overlap-schedule",
+    ref.add_argument("--disable-radix-cache", action="store_true",
+                     help="release a finished request's KV at once instead of keeping it on the device for a "
+                          "later prompt that extends it")
+    for flag in ("--skip-server-warmup", "--trust-remote-code", "--disable-overlap-schedule",
                  "--disable-flashinfer-autotune", "--language-model-only"):
         ref.add_argument(flag, action="store_true", help="accepted; no effect in packmla")
     for flag in ("--reasoning-parser", "--tool-call-parser", "--model-type", "--dsa-decode-backend",
@@ -105,7 +108,8 @@ def resolve_args(args) -> dict:
             raise SystemExit("per-layer keep counts other than 256 are evaluation-only "
                              "(python -m packmla.training.evaluate --retention-sweep)")
     kw = dict(kv_cache_format=fmt, decode_impl=impl, keep_count=args.dsv4_c4_cache_keep_count,
-              prefill_decode_interleave=not args.no_prefill_decode_interleave)
+              prefill_decode_interleave=not args.no_prefill_decode_interleave,
+              prefix_cache=not args.disable_radix_cache)
     disable_graphs = args.disable_cuda_graph or args.device == "cpu"
     bs = args.cuda_graph_bs
     if args.cuda_graph_config:

@@ -1,0 +1,62 @@
+"""CPU: device prefix cache (finished requests keep their KV slot until the space is needed; a later
+prompt that extends one adopts the slot and prefills only its new tokens)."""
+import torch
+
+from packmla.config import EngineConfig, ModelConfig
+from packmla.engine.engine import Engine, SamplingParams
+
+
+def _engine(fmt="direct", prefix=True, max_running=2):
+    cfg = ModelConfig.tiny(num_layers=3)
+    ecfg = EngineConfig(kv_cache_format=fmt, device="cpu", chunked_prefill_size=64, max_running_requests=max_running,
+                        cuda_graph_bs=[1, 2], prefix_cache=prefix)
+    return Engine.build(cfg, ecfg, "cpu", max_context=1024)
+
+
+def _toks(n, seed):
+    return torch.randint(3, 512, (n,), generator=torch.Generator().manual_seed(seed)).tolist()
+
+
+def test_next_turn_adopts_the_retained_slot_and_matches_recompute():
+    for fmt in ("direct", "native"):
+        turn1, follow = _toks(300, 1), _toks(37, 2)
+        eng = _engine(fmt)
+        out1 = eng.generate([turn1], SamplingParams(max_new_tokens=5))[0]
+        assert len(eng.retained) == 1
+        slot = next(iter(eng.retained.values()))
+        turn2 = turn1 + out1 + follow
+        before = eng.metrics.snapshot().get("prefill_tokens", 0)
+        rid = eng.add_request(turn2, SamplingParams(max_new_tokens=5))
+        while eng.has_work():
+            eng.step()
+        out2 = eng.result(rid).output_ids
+        m = eng.metrics.snapshot()
+        cached = len(turn1) + len(out1) - 1
+        assert m["prefix_cache_hit_tokens"] == cached
+        assert m["prefill_tokens"] - before == len(turn2) - cached
+        assert eng.result(rid).slot == slot  # the same slot continued
+        ref = _engine(fmt, prefix=False).generate([turn2], SamplingParams(max_new_tokens=5))[0]
+        assert out2 == ref, fmt
+
+
+def test_unrelated_prompt_does_not_adopt_and_lru_evicts():
+    eng = _engine(max_running=2)
+    prompts = [_toks(100, s) for s in (3, 4, 5)]
+    outs = [eng.generate([p], SamplingParams(max_new_tokens=3))[0] for p in prompts]
+    # two request slots: the third request evicted the least recently used retained slot
+    assert len(eng.retained) == 2 and eng.metrics.snapshot()["prefix_cache_evictions"] == 1
+    assert tuple(prompts[0] + outs[0][:-1]) not in eng.retained
+    ref = _engine(prefix=False)
+    assert outs == [ref.generate([p], SamplingParams(max_new_tokens=3))[0] for p in prompts]
+    assert not eng.metrics.snapshot().get("prefix_cache_hit_tokens")
+    eng.flush_cache()
+    assert not eng.retained and eng.pool.pages.free == eng.pool.num_pages
+
+
+def test_identical_prompt_is_not_a_strict_prefix_and_repeats_exactly():
+    eng = _engine()
+    p = _toks(80, 7)
+    a = eng.generate([p], SamplingParams(max_new_tokens=4))[0]
+    b = eng.generate([p], SamplingParams(max_new_tokens=4))[0]
+    assert a == b and not eng.metrics.snapshot().get("prefix_cache_hit_tokens")
+    assert len(eng.retained) == 1  # the same key replaces its older slot

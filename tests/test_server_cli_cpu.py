@@ -26,6 +26,7 @@ def test_reference_launch_line_maps_onto_engine_config():
     assert args.model == "v4-flash" and args.seed == 7 and args.watchdog_timeout == 1800
     assert kw["kv_cache_format"] == "direct" and kw["decode_impl"] == "direct" and kw["keep_count"] == 256
     assert kw["cuda_graph_bs"] == [1, 2, 4, 8, 16] and kw["disable_cuda_graph"]  # CPU: no graphs
+    assert kw["prefix_cache"] and not _resolve("--disable-radix-cache")[1]["prefix_cache"]
     EngineConfig(tp=4, ep=4, enable_hierarchical_cache=True, **kw).validate()
 
 
