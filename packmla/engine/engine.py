@@ -33,10 +33,11 @@ from ..utils.metrics import Metrics
 # NVTX ranges around scheduler steps and graph replays (PACKMLA_NVTX=1; reference: SGLang's
 # SGLANG_ENABLE_NVTX_SCHEDULER batch/rank/step ranges)
 NVTX = os.environ.get("PACKMLA_NVTX", "0") == "1"
+_PROFILING = [False]  # set between /start_profile and /stop_profile: ranges are emitted then too
 
 
 def nvtx_range(name: str):
-    if NVTX and torch.cuda.is_available():
+    if (NVTX or _PROFILING[0]) and torch.cuda.is_available():
         return torch.cuda.nvtx.range(name)
     return contextlib.nullcontext()
 
@@ -424,6 +425,19 @@ class Engine:
         while self.has_work():
             self.step()
         return [self.result(r).output_ids for r in rids]
+
+    def profile(self, on: bool) -> bool:
+        """Open (on) or close the CUDA profiler capture range (cudaProfilerStart / Stop), which Nsight
+        Systems / Compute honour with `--capture-range=cudaProfilerApi`, and emit NVTX ranges while it is
+        open (reference: SGLang's /start_profile, /stop_profile).  Returns whether the state changed."""
+        if on == _PROFILING[0]:
+            return False
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            (torch.cuda.profiler.start if on else torch.cuda.profiler.stop)()
+        _PROFILING[0] = on
+        self.metrics.inc("profile_ranges_opened" if on else "profile_ranges_closed")
+        return True
 
     def flush_cache(self) -> None:
         """Drop cached KV of finished requests (device prefix cache and the HiCache host tier)."""

@@ -14,6 +14,7 @@ While streaming, text already sent before a multi-token stop string completes is
     POST /generate                     SGLang native: text | input_ids + sampling_params
     GET  /server_info (/get_server_info)
     POST /flush_cache
+    POST /start_profile, /stop_profile  CUDA profiler capture range (Nsight --capture-range=cudaProfilerApi)
     GET  /metrics                      Prometheus text
 """
 from __future__ import annotations
@@ -293,6 +294,16 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
     async def flush_cache():
         driver.flush_cache()
         return PlainTextResponse("Cache flushed.")
+
+    @app.post("/start_profile")
+    async def start_profile():
+        driver.profile(True)
+        return PlainTextResponse("Start profiling.")
+
+    @app.post("/stop_profile")
+    async def stop_profile():
+        driver.profile(False)
+        return PlainTextResponse("Stop profiling.")
 
     @app.get("/metrics")
     async def metrics():

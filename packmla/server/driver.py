@@ -109,6 +109,10 @@ class EngineDriver:
     def flush_cache(self) -> None:
         self._inbox.put(("flush",))
 
+    def profile(self, on: bool) -> None:
+        """Open or close the profiler capture range on every rank, between engine steps."""
+        self._inbox.put(("profile", bool(on)))
+
     def generate(self, prompt: list[int], params: SamplingParams, timeout: float = 600.0) -> Stream:
         """Blocking convenience: submit and wait for the end of the request."""
         st = self.submit(prompt, params)
@@ -157,6 +161,8 @@ class EngineDriver:
                 flush = getattr(eng, "flush_cache", None)
                 if flush is not None:
                     flush()
+            elif kind == "profile":
+                eng.profile(op[1])
         return True
 
     def _finish(self, rid: int, reason: str) -> None:

@@ -148,3 +148,25 @@ def test_stop_strings_stop_tokens_and_n(served):
     assert len({ch["message"]["content"] for ch in c["choices"]}) == 1
     assert client.post("/v1/completions", json={"prompt": "x", "n": 2, "stream": True}).status_code == 400
     assert client.post("/v1/completions", json={"prompt": "x", "stop": [3]}).status_code == 400
+
+
+def test_profile_range_endpoints(served):
+    import time
+
+    client, eng, tok, cfg = served
+
+    def wait_for(key, n):
+        for _ in range(200):
+            if eng.metrics.snapshot().get(key, 0) == n:
+                return True
+            time.sleep(0.02)
+        return False
+
+    assert client.post("/start_profile").status_code == 200
+    assert wait_for("profile_ranges_opened", 1)
+    client.post("/start_profile")  # already open: no second range
+    assert client.post("/stop_profile").status_code == 200
+    assert wait_for("profile_ranges_closed", 1)
+    assert eng.metrics.snapshot()["profile_ranges_opened"] == 1
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "after profiling", "max_tokens": 2})
+    assert r.status_code == 200
