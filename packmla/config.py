@@ -143,6 +143,7 @@ class EngineConfig:
     disable_cuda_graph: bool = False
     enable_hierarchical_cache: bool = False
     hicache_ratio: float = 2.0
+    hicache_mem_layout: str = "page_first"  # page_first | layer_first
     # keep a finished request's KV on the device (its slot and pages) until the space is needed; a later
     # prompt that extends it adopts the slot and prefills only the new tokens (the reference serves with
     # SGLang's radix prefix cache on; the server turns this on unless --disable-radix-cache)
@@ -175,6 +176,8 @@ class EngineConfig:
             raise ValueError("mem_fraction_static must be in (0, 0.98]")
         if self.tp < 1 or self.ep < 1:
             raise ValueError("tp and ep must be >= 1")
+        if self.hicache_mem_layout not in ("page_first", "layer_first"):
+            raise ValueError("--hicache-mem-layout must be page_first or layer_first")
         if self.hicache_ratio <= 0:
             raise ValueError("hicache_ratio must be positive")
         if self.moe_precision not in ("default", "bf16"):

@@ -188,7 +188,7 @@ class Engine:
         if engine_cfg.enable_hierarchical_cache:
             from ..kv.hicache import HostKVCache
 
-            self.hicache = HostKVCache(pool, engine_cfg.hicache_ratio)
+            self.hicache = HostKVCache(pool, engine_cfg.hicache_ratio, engine_cfg.hicache_mem_layout)
 
     # ------------------------------------------------------------------ construction
     @classmethod

@@ -10,8 +10,10 @@ state) is written through to host memory, keyed by the processed tokens.  A new 
 starts with such a key gets the KV copied back into its freshly allocated pages and prefills only the
 remaining tokens (a multi-turn conversation re-sends its history every turn).
 
-Layout: host pages are page-first (one host page holds the page's planes of all layers contiguously);
-`ratio` x the device page count host pages exist; entries are evicted least-recently-used.  Moves are
+Layout: `page_first` (default: one host page holds the page's planes of all layers contiguously, so a
+request's pages are few large segments) or `layer_first` (each plane of each layer has its own host
+region indexed by host page, as SGLang's layer-first host pool); `ratio` x the device page count host
+pages exist; entries are evicted least-recently-used.  Moves are
 one `segment_copy` kernel launch per direction on a side stream (pinned host memory is device-mapped);
 on CPU pools the same segments are plain tensor copies.
 """
@@ -52,9 +54,12 @@ class _Plane:
 
 
 class HostKVCache:
-    def __init__(self, pool: KVPool, ratio: float = 2.0):
+    def __init__(self, pool: KVPool, ratio: float = 2.0, layout: str = "page_first"):
         if pool.kv_format == "direct" and pool.ecfg.keep_count != abi.PACKED_KEEP:
             raise ValueError("HiCache requires the 256-survivor layout")
+        if layout not in ("page_first", "layer_first"):
+            raise ValueError("HiCache layout must be page_first or layer_first")
+        self.layout = layout
         self.pool = pool
         self.dev = pool.device
         R = abi.RECORDS_PER_PAGE
@@ -89,6 +94,11 @@ class HostKVCache:
                                  + sum(t[0].numel() * 4 for t in self.state_tensors))
         self.num_host_pages = max(1, math.ceil(ratio * pool.num_pages))
         self.num_host_c128 = max(1, math.ceil(ratio * pool.num_c128_pages))
+        if layout == "layer_first":  # plane regions: region start = host_off x number of host pages
+            for p in self.planes:
+                p.host_off *= self.num_host_pages
+            for p in self.c128_planes:
+                p.host_off *= self.num_host_c128
         pin = self.dev.type == "cuda"
         self.host = torch.zeros(self.num_host_pages * self.page_bytes, dtype=torch.uint8, pin_memory=pin)
         self.host_c128 = torch.zeros(max(1, self.num_host_c128 * self.c128_page_bytes), dtype=torch.uint8,
@@ -106,16 +116,16 @@ class HostKVCache:
         pairs = []
         for i in range(n_pages):
             dpage = pool._req_pages[slot][i]
-            hbase = entry.host_pages[i] * self.page_bytes
             for p in self.planes:
+                h = self._host_start(p, entry.host_pages[i], self.page_bytes)
                 pairs.append((p.dev[dpage * p.page_bytes:(dpage + 1) * p.page_bytes],
-                              self.host[hbase + p.host_off:hbase + p.host_off + p.page_bytes]))
+                              self.host[h:h + p.page_bytes]))
         for i in range(n_c128):
             dpage = pool._req_c128[slot][i]
-            hbase = entry.host_c128[i] * self.c128_page_bytes
             for p in self.c128_planes:
+                h = self._host_start(p, entry.host_c128[i], self.c128_page_bytes)
                 pairs.append((p.dev[dpage * p.page_bytes:(dpage + 1) * p.page_bytes],
-                              self.host_c128[hbase + p.host_off:hbase + p.host_off + p.page_bytes]))
+                              self.host_c128[h:h + p.page_bytes]))
         off = 0
         for swa in pool.swa:
             b = _bytes(swa)
@@ -128,7 +138,15 @@ class HostKVCache:
             off += row.numel()
         return pairs
 
+    def _host_start(self, p: _Plane, host_page: int, page_bytes: int) -> int:
+        """Byte offset of plane `p` of `host_page` in the host buffer."""
+        if self.layout == "layer_first":
+            return p.host_off + host_page * p.page_bytes
+        return host_page * page_bytes + p.host_off
+
     def _run(self, pairs: list[tuple], to_host: bool) -> int:
+        if any(d.numel() != h.numel() for d, h in pairs):  # a clipped view would make the kernel overrun
+            raise ValueError("HiCache segment views differ in size")
         nbytes = sum(d.numel() for d, _ in pairs)
         if self.stream is None:
             for d, h in pairs:

@@ -70,7 +70,7 @@ def build_parser() -> argparse.ArgumentParser:
     ref.add_argument("--hicache-io-backend", default="kernel", choices=["kernel", "direct"],
                      help="both move pages with packmla's segment-copy kernel")
     ref.add_argument("--hicache-mem-layout", default="page_first", choices=["page_first", "layer_first"],
-                     help="accepted; packmla's host tier is page-first")
+                     help="host tier layout: all planes of a page together, or one region per plane")
     ref.add_argument("--hicache-write-policy", default="write_through", choices=["write_through"])
     ref.add_argument("--enable-metrics", action="store_true", help="accepted; /metrics is always served")
     ref.add_argument("--log-requests", action="store_true", help="log every finished request (JSON)")
@@ -109,7 +109,7 @@ def resolve_args(args) -> dict:
                              "(python -m packmla.training.evaluate --retention-sweep)")
     kw = dict(kv_cache_format=fmt, decode_impl=impl, keep_count=args.dsv4_c4_cache_keep_count,
               prefill_decode_interleave=not args.no_prefill_decode_interleave,
-              prefix_cache=not args.disable_radix_cache)
+              prefix_cache=not args.disable_radix_cache, hicache_mem_layout=args.hicache_mem_layout)
     disable_graphs = args.disable_cuda_graph or args.device == "cpu"
     bs = args.cuda_graph_bs
     if args.cuda_graph_config:

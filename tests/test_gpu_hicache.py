@@ -25,7 +25,8 @@ def test_segment_copy_round_trip(cuda):
     assert torch.equal(back[:off], dev[:off])
 
 
-def test_engine_restores_previous_turn(cuda):
+@pytest.mark.parametrize("layout", ["page_first", "layer_first"])
+def test_engine_restores_previous_turn(cuda, layout):
     from helpers import small_gpu_config
 
     from packmla.config import EngineConfig
@@ -33,7 +34,8 @@ def test_engine_restores_previous_turn(cuda):
 
     cfg = small_gpu_config()
     ecfg = EngineConfig(kv_cache_format="direct", max_running_requests=2, cuda_graph_bs=[1, 2],
-                        chunked_prefill_size=128, disable_cuda_graph=True, enable_hierarchical_cache=True)
+                        chunked_prefill_size=128, disable_cuda_graph=True, enable_hierarchical_cache=True,
+                        hicache_mem_layout=layout)
     eng = Engine.build(cfg, ecfg, cuda, max_context=1024, max_requests=2, kv_bytes=64 << 20)
     g = torch.Generator().manual_seed(0)
     turn1 = torch.randint(3, cfg.vocab_size, (300,), generator=g).tolist()

@@ -27,6 +27,7 @@ def test_reference_launch_line_maps_onto_engine_config():
     assert kw["kv_cache_format"] == "direct" and kw["decode_impl"] == "direct" and kw["keep_count"] == 256
     assert kw["cuda_graph_bs"] == [1, 2, 4, 8, 16] and kw["disable_cuda_graph"]  # CPU: no graphs
     assert kw["prefix_cache"] and not _resolve("--disable-radix-cache")[1]["prefix_cache"]
+    assert kw["hicache_mem_layout"] == "layer_first"
     EngineConfig(tp=4, ep=4, enable_hierarchical_cache=True, **kw).validate()
 
 
