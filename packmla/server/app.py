@@ -39,6 +39,14 @@ def _params(body: dict, tok: ByteTokenizer, default_max: int = 16) -> SamplingPa
     temp = float(body.get("temperature", 0.0) or 0.0)
     if temp < 0:
         raise HTTPException(400, "temperature must be >= 0")
+    sp = body.get("sampling_params") if isinstance(body.get("sampling_params"), dict) else body
+    # the sampler is greedy or temperature-scaled over the full vocabulary; other knobs are rejected rather
+    # than silently ignored (their neutral values pass)
+    for name, neutral in (("top_p", 1.0), ("top_k", -1), ("min_p", 0.0), ("frequency_penalty", 0.0),
+                          ("presence_penalty", 0.0), ("repetition_penalty", 1.0)):
+        v = sp.get(name)
+        if v is not None and not (v == neutral or (name == "top_k" and v == 0)):
+            raise HTTPException(400, f"{name}={v} is not supported (greedy or temperature sampling only)")
     return SamplingParams(max_new_tokens=int(max_tokens), temperature=temp,
                           ignore_eos=bool(body.get("ignore_eos", False)), eos_token_id=tok.eos_token_id)
 

@@ -170,3 +170,14 @@ def test_profile_range_endpoints(served):
     assert eng.metrics.snapshot()["profile_ranges_opened"] == 1
     r = client.post("/v1/completions", json={"model": "tiny", "prompt": "after profiling", "max_tokens": 2})
     assert r.status_code == 200
+
+
+def test_unsupported_sampling_knobs_are_rejected(served):
+    client, eng, tok, cfg = served
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "x", "max_tokens": 2, "top_p": 0.9})
+    assert r.status_code == 400 and "top_p" in r.text
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "x", "max_tokens": 2, "top_p": 1.0,
+                                             "top_k": -1, "frequency_penalty": 0})
+    assert r.status_code == 200
+    r = client.post("/generate", json={"text": "x", "sampling_params": {"max_new_tokens": 2, "top_k": 20}})
+    assert r.status_code == 400
