@@ -165,3 +165,32 @@ def read_page(kv_format: str, page: torch.Tensor, records: int = abi.RECORDS_PER
         words = data[:, PACKED_CODE_BYTES:].contiguous().view(torch.int64)
         return packed_decode(data[:, :PACKED_CODE_BYTES].contiguous(), words, scales.contiguous())
     return native_decode(data.contiguous(), scales.contiguous())
+
+
+# --------------------------------------------------------------------------- Direct decode (reference)
+def gather_rows(pool: torch.Tensor, kv_format: str, indices: torch.Tensor,
+                records: int = abi.RECORDS_PER_PAGE) -> torch.Tensor:
+    """Paged FP4 pool uint8 [num_pages, page bytes] and record ids [N] -> rotated rows fp32 [N, 512]
+    (record id = page * records + row; ids < 0 give zero rows)."""
+    out = torch.zeros(indices.numel(), abi.LATENT_DIM)
+    for i, rid in enumerate(indices.reshape(-1).tolist()):
+        if rid >= 0:
+            out[i] = read_page(kv_format, pool[rid // records], records)[rid % records]
+    return out
+
+
+def sparse_decode_reference(q: torch.Tensor, pool: torch.Tensor, kv_format: str, indices: torch.Tensor,
+                            lens: torch.Tensor, swa_rows: list[torch.Tensor], sink: torch.Tensor, scale: float,
+                            q_freqs: torch.Tensor):
+    """fp32 reference of sparse MLA decode over FP4 global records beside BF16 SWA rows (the V4.1 FP4
+    Native / Direct read, reference: third_party/README.md:135-141): query b attends to its SWA rows and
+    to the first lens[b] selected records that are not -1 (records hold RoPE-rotated values, so no
+    rotation happens at read).  Returns (out bf16 [B, H, 512], lse [B, H])."""
+    from ..oracle.attention import sparse_mla_decode
+
+    rows = []
+    for b in range(q.shape[0]):
+        sel = indices[b, : int(lens[b])]
+        sel = sel[sel >= 0]
+        rows.append(torch.cat((swa_rows[b].float(), gather_rows(pool, kv_format, sel))))
+    return sparse_mla_decode(q, rows, sink, scale, q_freqs)

@@ -130,3 +130,30 @@ def test_huge_groups_saturate_the_scale():
     codes, scales = fp4.native_encode(rows)
     assert scales[0, 0].view(torch.float8_e4m3fn).float().item() == 448.0
     assert bool(torch.isfinite(fp4.native_decode(codes, scales)).all())
+
+
+def test_fp4_sparse_decode_reference_matches_dense_attention():
+    from packmla.oracle.attention import sparse_mla_decode
+
+    g = torch.Generator().manual_seed(5)
+    n_pages, R = 3, abi.RECORDS_PER_PAGE
+    for fmt in ("native", "direct"):
+        rows = _rows(n_pages * R, 6)
+        pool = torch.stack([fp4.write_page(fmt, rows[p * R:(p + 1) * R]) for p in range(n_pages)])
+        B, H, K = 2, 4, 20
+        idx = torch.randint(0, n_pages * R, (B, K), generator=g)
+        idx[0, 3] = -1
+        lens = torch.tensor([K, 13])
+        swa = [torch.randn(5, 512, generator=g).bfloat16().float() for _ in range(B)]
+        q = torch.randn(B, H, 512, generator=g)
+        sink, freqs = torch.randn(H, generator=g), codec.rope_table(16)[torch.tensor([3, 9])]
+        out, lse = fp4.sparse_decode_reference(q, pool, fmt, idx, lens, swa, sink, 512 ** -0.5, freqs)
+        decoded = fp4.native_decode(*fp4.native_encode(rows)) if fmt == "native" else \
+            fp4.packed_decode(*fp4.packed_encode(rows))
+        kv = []
+        for b in range(B):
+            sel = idx[b, :int(lens[b])]
+            kv.append(torch.cat((swa[b], decoded[sel[sel >= 0]])))
+        ref_o, ref_l = sparse_mla_decode(q, kv, sink, 512 ** -0.5, freqs)
+        assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)
+        assert kv[0].shape[0] == 5 + K - 1 and kv[1].shape[0] == 5 + 13
