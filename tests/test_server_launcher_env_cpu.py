@@ -1,0 +1,50 @@
+"""CPU: the environment-driven launcher (reference serve.sh / launch-config.sh names) resolves the
+server command, owns the server's process group, waits for health and reads the pool out."""
+import json
+import os
+import socket
+
+import pytest
+
+from packmla.server import launch
+
+
+def test_env_names_map_onto_server_flags(tmp_path):
+    env = {"MODE": "native", "TP": "4", "EP": "4", "PORT": "31000", "MASTER_PORT": "29700", "MEM_FRAC": "0.85",
+           "CTX_LEN": "65536", "MAX_RUN": "40", "CHUNK": "4096", "SERVER_SEED": "42", "HICACHE_RATIO": "2",
+           "DECODE_CFG": '{"decode": {"bs": [1, 2]}}', "C4_KEEP_COUNT": "256",
+           "REQUEST_METRICS_DIR": str(tmp_path)}
+    cmd, extra = launch.resolve(None, env)
+    assert cmd[1:3] == ["-m", "torch.distributed.run"] and "--nproc-per-node" in cmd
+    assert cmd[cmd.index("--nproc-per-node") + 1] == "4" and cmd[cmd.index("--master-addr") + 1] == "127.0.0.1"
+    assert cmd[cmd.index("--master-port") + 1] == "29700"
+    i = cmd.index("packmla.server")
+    from packmla.server.__main__ import build_parser, resolve_args
+
+    args = build_parser().parse_args(cmd[i + 1:])
+    kw = resolve_args(args)
+    assert args.tp == 4 and args.ep == 4 and args.port == 31000 and args.seed == 42 and args.context_length == 65536
+    assert kw["kv_cache_format"] == "native" and kw["cuda_graph_bs"] == [1, 2]
+    assert args.enable_hierarchical_cache and args.hicache_ratio == 2.0 and args.log_requests
+    assert args.export_metrics_to_file_dir == str(tmp_path) and extra["NCCL_SOCKET_IFNAME"] == "lo"
+    cmd1, _ = launch.resolve("direct", {"MODE": "native"})  # the positional mode wins; TP=1 runs directly
+    assert cmd1[1:3] == ["-m", "packmla.server"] and cmd1[cmd1.index("--kv-cache-format") + 1] == "direct"
+    with pytest.raises(SystemExit):
+        launch.resolve(None, {"REQUEST_METRICS_DIR": str(tmp_path / "missing")})
+
+
+def test_smoke_start_wait_readout_stop(monkeypatch, tmp_path, capsys):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    for k, v in {"MODEL": "tiny", "DEVICE": "cpu", "PORT": str(port), "MAX_RUN": "4", "CTX_LEN": "2048"}.items():
+        monkeypatch.setenv(k, v)
+    for k in ("TP", "WORLD_SIZE", "RANK", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        monkeypatch.delenv(k, raising=False)
+    out = launch.main(["direct", "--smoke", "--wait-timeout", "300", "--log", str(tmp_path / "server.log")])
+    assert out["event"] == "ready" and out["kv_cache_format"] == "direct" and out["max_total_num_tokens"] > 0
+    assert out["prefix_cache"] is True and out["context_length"] == 2048
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["pgid"] == out["pgid"]
+    with pytest.raises(ProcessLookupError):  # the whole group is gone
+        os.killpg(out["pgid"], 0)
