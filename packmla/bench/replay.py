@@ -346,6 +346,28 @@ def sweep(url: str, requests_path: str, concurrencies: list[int], out_dir: str, 
             "operational_complete": stopped is None and len(points) == len(concurrencies) * repeats}
 
 
+def owned_sweep(mode: str, requests_path: str, concurrencies: list[int], out_dir: str,
+                startup_timeout_s: float = 1800.0, **kwargs) -> dict:
+    """`sweep` against a server this call starts (packmla.server.launch with the environment's settings)
+    and stops on every exit path (reference: scripts/local/sweep-lswb.sh owns one server per mode).
+    The server's output goes to `<out-dir>.server.log`; the ready read-out lands in the result."""
+    from ..server import launch
+
+    env = dict(os.environ)
+    cmd, extra = launch.resolve(mode, env)
+    env.update(extra)
+    group = launch.ServerGroup(cmd, env, f"{out_dir.rstrip('/')}.server.log")
+    url = f"http://127.0.0.1:{env.get('PORT', '30000')}"
+    try:
+        info = launch.wait_ready(url, group, startup_timeout_s)
+        out = sweep(url, requests_path, concurrencies, out_dir, **kwargs)
+        out["server"] = {"mode": mode, "command": cmd,
+                         **{k: info.get(k) for k in ("kv_cache_format", "max_total_num_tokens", "prefix_cache")}}
+        return out
+    finally:
+        group.stop()
+
+
 def _write_summaries(root: Path, points: list[dict], stopped: str | None) -> None:
     (root / "summary.json").write_text(json.dumps({"points": points, "stopped": stopped}, indent=2))
     with open(root / "summary.csv", "w", newline="") as f:
@@ -420,10 +442,18 @@ def main(argv=None) -> dict:
         ap.add_argument("--concurrencies", type=_ints, required=True)
         ap.add_argument("--repeats", type=int, default=1)
         ap.add_argument("--out-dir", required=True)
+        ap.add_argument("--launch", choices=["native", "direct"], default=None,
+                        help="own one server of this mode for the sweep (packmla.server.launch, its environment "
+                             "names), stopped on every exit path; --base-url is then derived from PORT")
+        ap.add_argument("--startup-timeout", type=float, default=1800.0)
         a = ap.parse_args(argv)
-        out = sweep(a.base_url, a.requests, a.concurrencies, a.out_dir, repeats=a.repeats, model=a.model,
-                    duration_s=a.duration_s if a.duration_s is not None else 1200.0,
-                    ttft_slo_ms=a.ttft_slo_ms if a.ttft_slo_ms is not None else 10000.0, min_success=a.min_success)
+        kwargs = dict(repeats=a.repeats, model=a.model,
+                      duration_s=a.duration_s if a.duration_s is not None else 1200.0,
+                      ttft_slo_ms=a.ttft_slo_ms if a.ttft_slo_ms is not None else 10000.0, min_success=a.min_success)
+        if a.launch:
+            out = owned_sweep(a.launch, a.requests, a.concurrencies, a.out_dir, a.startup_timeout, **kwargs)
+        else:
+            out = sweep(a.base_url, a.requests, a.concurrencies, a.out_dir, **kwargs)
         print(json.dumps(out, indent=2))
         if not out["operational_complete"]:
             raise SystemExit(f"sweep stopped: {out['stopped']}")

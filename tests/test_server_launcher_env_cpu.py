@@ -48,3 +48,27 @@ def test_smoke_start_wait_readout_stop(monkeypatch, tmp_path, capsys):
     assert line["pgid"] == out["pgid"]
     with pytest.raises(ProcessLookupError):  # the whole group is gone
         os.killpg(out["pgid"], 0)
+
+
+def test_sweep_owns_its_server(monkeypatch, tmp_path):
+    import requests
+
+    from packmla.bench import replay
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    for k, v in {"MODEL": "tiny", "DEVICE": "cpu", "PORT": str(port), "MAX_RUN": "4", "CTX_LEN": "2048"}.items():
+        monkeypatch.setenv(k, v)
+    for k in ("TP", "WORLD_SIZE", "RANK", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        monkeypatch.delenv(k, raising=False)
+    path = tmp_path / "s.jsonl"
+    path.write_text("".join(json.dumps({"session": f"s{i}", "turn": 0, "max_tokens": 2,
+                                        "messages": [{"role": "user", "content": f"owned {i}"}]}) + "\n"
+                            for i in range(2)))
+    out = replay.main(["sweep", "--launch", "native", "--requests", str(path), "--concurrencies", "1,2",
+                       "--out-dir", str(tmp_path / "sw"), "--min-success", "1.0", "--startup-timeout", "300"])
+    assert out["operational_complete"] and out["points"] == 2 and out["server"]["kv_cache_format"] == "native"
+    assert (tmp_path / "sw.server.log").exists()
+    with pytest.raises(requests.RequestException):  # the owned server is gone
+        requests.get(f"http://127.0.0.1:{port}/health", timeout=2)
