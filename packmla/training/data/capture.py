@@ -37,6 +37,20 @@ def _complex_table(freqs_f32: torch.Tensor) -> torch.Tensor:
     return torch.complex(freqs_f32[..., 0].float(), freqs_f32[..., 1].float())
 
 
+def _gather_heads(t: torch.Tensor, comm) -> torch.Tensor:
+    """Under tensor parallelism each rank holds the contiguous head block [rank * H/world, ...): gather
+    the blocks in rank order so that every rank sees all heads (reference: its capture assembles the 64
+    heads from 4 ranks).  Without a multi-rank communicator the tensor is returned as is."""
+    world = getattr(comm, "world", 1)
+    if world <= 1:
+        return t
+    import torch.distributed as dist
+
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous(), group=getattr(comm, "group", None))
+    return torch.cat(parts, 0)
+
+
 class CaptureObserver:
     def __init__(self, layers: tuple[int, ...]):
         self.layers = set(layers)
@@ -87,8 +101,8 @@ class CaptureObserver:
         from ...ops import kv as kv_ops
 
         swa = codec.native_decode(kv_ops.native_pool_read(model.pool.swa[layer], ring.to(model.device)).cpu())
-        qf = q[b].detach().float().cpu()
-        sink = lw["sink"].detach().float().cpu()
+        qf = _gather_heads(q[b].detach().float().cpu(), getattr(model, "comm", None))
+        sink = _gather_heads(lw["sink"].detach().float().cpu(), getattr(model, "comm", None))
         scale = float(model.scale)
         query_freq = table[p]
         native = codec.native_rows(raw, weight, eps, freq)
@@ -105,11 +119,13 @@ class CaptureObserver:
 
 def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int = 2, train_queries: int = 2,
                   dev_queries: int = 3, prompt_len: int = 300, seed: int = 0, device: str = "cpu",
-                  layers: tuple[int, ...] | None = None) -> dict:
+                  layers: tuple[int, ...] | None = None, comm=None) -> dict:
     """Run `issues` random requests through a Native-format engine and cache their C4-layer queries.
 
     Each issue contributes `train_queries` (train split) or `dev_queries` (development split) decode
-    positions per layer; the split is frozen by `frozen_split`.
+    positions per layer; the split is frozen by `frozen_split`.  With a multi-rank `comm` (every rank
+    calls this in lockstep with the same arguments), the engine runs tensor parallel, the observer
+    gathers the heads of every captured query, and rank 0 alone writes the cache.
     """
     from ...config import EngineConfig
     from ...engine.engine import Engine, SamplingParams
@@ -120,9 +136,11 @@ def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int 
     role_of = {rid: role for role in ("train", "development") for rid in split[role]}
     per = {"train": train_queries, "development": dev_queries}
     steps = max(train_queries, dev_queries)
+    world, rank = getattr(comm, "world", 1), getattr(comm, "rank", 0)
     ecfg = EngineConfig(kv_cache_format="native", device=device, max_running_requests=2, cuda_graph_bs=[1],
-                        disable_cuda_graph=True, chunked_prefill_size=8192)
-    eng = Engine.build(model_cfg, ecfg, device, max_context=prompt_len + steps + 8, max_requests=2, seed=seed)
+                        disable_cuda_graph=True, chunked_prefill_size=8192, tp=world, ep=world)
+    eng = Engine.build(model_cfg, ecfg, device, rank, world, comm if world > 1 else None,
+                       max_context=prompt_len + steps + 8, max_requests=2, seed=seed)
     obs = CaptureObserver(layers)
     eng.model.observer = obs
     g = torch.Generator().manual_seed(seed)
@@ -147,8 +165,10 @@ def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int 
             s["split"] = role
             roles[role].append(s)
         states_by_layer[layer] = roles
-    write_cache(Path(output), states_by_layer, split, per,
-                {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native"})
+    if rank == 0:
+        write_cache(Path(output), states_by_layer, split, per,
+                    {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native",
+                     "capture_tp": world})
     return {"cache": str(output), "layers": list(layers), "split": split, "skipped": obs.skipped,
             "states": {layer: {r: len(v) for r, v in roles.items()} for layer, roles in states_by_layer.items()}}
 

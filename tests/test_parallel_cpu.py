@@ -156,3 +156,40 @@ def test_expert_parallel_dispatch_combine_matches_all_experts(tmp_path):
         torch.testing.assert_close(got["fp32"], ref, atol=1e-4, rtol=1e-4)
         assert ((got["bf16"] - ref).norm() / ref.norm()).item() < 1e-2  # bf16 combine rows
         assert sum(got["counts"]["sent"]) == h.shape[0] * cfg.moe_topk
+
+
+def _capture_worker(rank: int, world: int, port: int, out_dir: str):
+    import torch.distributed as dist
+
+    from packmla.parallel.comm import TPComm
+    from packmla.training.data.capture import capture_cache
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        capture_cache(os.path.join(out_dir, "tp2"), ModelConfig.tiny(num_layers=2), issues=3, development=1,
+                      train_queries=1, dev_queries=1, prompt_len=64, comm=TPComm())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_capture_gathers_all_heads(tmp_path):
+    """Capture under TP=2: every query state holds all heads (gathered in rank order) and matches the
+    single-rank capture of the same model; only rank 0 writes the cache."""
+    from packmla.training.data.cache import load_cached_layer
+    from packmla.training.data.capture import capture_cache
+
+    cfg = ModelConfig.tiny(num_layers=2)
+    capture_cache(tmp_path / "tp1", cfg, issues=3, development=1, train_queries=1, dev_queries=1, prompt_len=64)
+    mp.spawn(_capture_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    layer = cfg.c4_layers[0]
+    one, two = load_cached_layer(tmp_path / "tp1", layer), load_cached_layer(tmp_path / "tp2", layer)
+    for role in ("train", "development"):
+        assert len(one[role]) == len(two[role]) > 0
+        for a, b in zip(one[role], two[role]):
+            assert b["q"].shape == (cfg.num_heads, 512) and b["sink"].shape == (cfg.num_heads,)
+            assert torch.equal(a["sink"], b["sink"])  # replicated init, gathered in head order
+            for k in ("q", "raw", "target"):
+                rel = ((a[k] - b[k]).norm() / a[k].norm()).item()
+                assert rel < 5e-2, (role, k, rel)
