@@ -113,7 +113,25 @@ def summarize(results: list[Result], wall: float) -> dict:
             "request_throughput": len(ok) / wall if wall > 0 else 0.0,
             "total_input_tokens": sum(r.prompt_len for r in ok), "total_output_tokens": out_tokens,
             "ttft_ms": stats([r.ttft for r in ok]), "tpot_ms": stats(tpot), "e2e_ms": stats([r.e2e for r in ok]),
+            "output_lens": [len(r.output_ids) for r in results],
+            "validated": len(ok) == len(results) > 0,  # every request completed with exactly output-len tokens
             "errors": [r.error for r in results if not r.ok][:5]}
+
+
+def phase_summaries(out: dict) -> list[tuple[str, dict]]:
+    """(name, summary) of every measured wave of a `bench` result."""
+    if "turns" in out:
+        return [(f"turn{i}", t) for i, t in enumerate(out["turns"])]
+    return [(k, out[k]) for k in ("warmup", "measured") if k in out]
+
+
+def write_records(path: str, out: dict) -> None:
+    """One JSON line per wave (reference: bench-serving.sh writes and validates one record per wave);
+    the file must not exist."""
+    with open(path, "x") as f:
+        for name, summary in phase_summaries(out):
+            f.write(json.dumps({"phase": name, "dataset": out["dataset"], "concurrency": out["concurrency"],
+                                "input_len": out["input_len"], "output_len": out["output_len"], **summary}) + "\n")
 
 
 def flush(url: str) -> None:
@@ -181,7 +199,7 @@ def bench(url: str, dataset: str, input_len: int, output_len: int, concurrency: 
     return out
 
 
-def main(argv=None) -> None:
+def main(argv=None) -> dict:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--base-url", default="http://127.0.0.1:30000")
     ap.add_argument("--model", default="default")
@@ -195,10 +213,18 @@ def main(argv=None) -> None:
     ap.add_argument("--sessions", type=int, default=0)
     ap.add_argument("--flush-cache", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--output-file", default=None, help="write one JSON record per wave here (a new file)")
     a = ap.parse_args(argv)
-    print(json.dumps(bench(a.base_url, a.dataset, a.input_len, a.output_len, a.concurrency, model=a.model,
-                           flush_cache=a.flush_cache, seed=a.seed, prefix_len=a.prefix_len, num_groups=a.num_groups,
-                           turns=a.turns, sessions=a.sessions), indent=2))
+    out = bench(a.base_url, a.dataset, a.input_len, a.output_len, a.concurrency, model=a.model,
+                flush_cache=a.flush_cache, seed=a.seed, prefix_len=a.prefix_len, num_groups=a.num_groups,
+                turns=a.turns, sessions=a.sessions)
+    print(json.dumps(out, indent=2))
+    if a.output_file:
+        write_records(a.output_file, out)
+    bad = [name for name, summary in phase_summaries(out) if not summary["validated"]]
+    if bad:  # incomplete requests, wrong output lengths or request errors fail the run
+        raise SystemExit(f"waves failed validation: {', '.join(bad)}")
+    return out
 
 
 if __name__ == "__main__":

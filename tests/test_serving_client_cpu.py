@@ -233,3 +233,22 @@ def test_client_disconnect_aborts_the_request(server_url):
         time.sleep(0.05)
     assert eng.metrics.snapshot().get("requests_aborted", 0) == before + 1
     assert not eng.running and not eng.waiting
+
+
+def test_serving_cli_writes_validated_wave_records(server_url, tmp_path):
+    from packmla.bench import serving
+
+    url, eng = server_url
+    path = tmp_path / "waves.jsonl"
+    serving.main(["--base-url", url, "--input-len", "50", "--output-len", "3", "--concurrency", "2",
+                  "--output-file", str(path)])
+    recs = [json.loads(x) for x in path.read_text().splitlines()]
+    assert [r["phase"] for r in recs] == ["warmup", "measured"]
+    assert recs[1]["completed"] == 6 and recs[1]["output_lens"] == [3] * 6 and recs[1]["validated"]
+    with pytest.raises(FileExistsError):  # records are never overwritten
+        serving.write_records(str(path), {"dataset": "random", "concurrency": 1, "input_len": 1, "output_len": 1})
+    with pytest.raises(SystemExit, match="context"):  # longer than the server's context: refused up front
+        serving.main(["--base-url", url, "--input-len", str(eng.pool.max_context), "--output-len", "3"])
+    # a short response makes its wave invalid
+    bad = serving.summarize([serving.Result(True, 5, [1, 2, 3]), serving.Result(False, 5, [1], error="short")], 1.0)
+    assert not bad["validated"] and bad["output_lens"] == [3, 1]
