@@ -4,7 +4,8 @@
     python -m packmla.bench.microbench decode [--batch 16] [--heads 128] [--context 32768] [--topk 2048]
     python -m packmla.bench.microbench store  [--rows 24]
     python -m packmla.bench.microbench decode-paired [--batch 16] [--context 32768] [--with-adapter]
-    python -m packmla.bench.microbench decode-suite [--paired]
+    python -m packmla.bench.microbench decode-suite [--paired] > suite.jsonl
+    python -m packmla.bench.microbench judge --results suite.jsonl [--paired] [--rounds 30]
 
 Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
 measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
@@ -223,7 +224,7 @@ def bench_decode(args, dev):
     flops = 4 * B * Hh * (K + W) * 512
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
-    return {"case": "sparse_mla_decode", "phases": phases, "kv_format": args.kv_format, "batch": B,
+    return {"case": "sparse_mla_decode", "rounds": args.rounds, "phases": phases, "kv_format": args.kv_format, "batch": B,
             "heads": Hh, "topk": K,
             "swa": W, "context": args.context, "splits": ws.splits, "tile_rows": ws.tile_rows, "us": round(us, 2), "bytes": nbytes,
             "GBps": round(gbs, 1), "hbm_fraction": round(gbs / peak, 3), "TFLOPs": round(flops / us / 1e6, 1),
@@ -295,6 +296,46 @@ def bench_decode_paired(args, dev, modes=("native", "direct")) -> dict:
             "swa": args.swa, "context": args.context, "modes": meta, **res, "clocks": clk.summary()}
 
 
+SUITE_CONTEXTS, SUITE_BATCHES, SUITE_FORMATS = (32768, 131072), (1, 16, 64), ("native", "direct")
+BAD_CLOCK_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown")
+
+
+def judge(rows: list[dict], rounds: int, paired: bool = False, min_clock_fraction: float = 0.8) -> dict:
+    """Accept or reject a decode-suite run: every case of the grid present once, each timed over
+    `rounds` rounds with finite positive times, and a clock record without hardware or thermal
+    slowdown and not stuck below `min_clock_fraction` of the maximum with no reason given (a leftover
+    clock lock).  `sw_power_cap` is accepted and noted.  Returns the verdict with its reasons."""
+    key = (lambda r: (r["context"], r["batch"])) if paired else (lambda r: (r["context"], r["batch"], r["kv_format"]))
+    expected = ({(c, b) for c in SUITE_CONTEXTS for b in SUITE_BATCHES} if paired else
+                {(c, b, f) for c in SUITE_CONTEXTS for b in SUITE_BATCHES for f in SUITE_FORMATS})
+    seen: dict = {}
+    rejected, notes = [], []
+    for r in rows:
+        k = key(r)
+        if k in seen:
+            rejected.append({"case": list(k), "reason": "duplicate case"})
+        seen[k] = r
+        times = list(r["mean_us"].values()) if paired else [r.get("us")]
+        if r.get("rounds") != rounds:
+            rejected.append({"case": list(k), "reason": f"rounds {r.get('rounds')} != {rounds}"})
+        if any(t is None or not math.isfinite(t) or t <= 0 for t in times):
+            rejected.append({"case": list(k), "reason": "non-finite or non-positive time"})
+        clk = r.get("clocks") or {}
+        reasons = clk.get("reasons") or []
+        bad = [x for x in reasons if x in BAD_CLOCK_REASONS]
+        if bad:
+            rejected.append({"case": list(k), "reason": "clock slowdown: " + ", ".join(bad)})
+        elif "unavailable" in reasons or not clk.get("sm_mhz") or not clk.get("sm_max_mhz"):
+            rejected.append({"case": list(k), "reason": "no clock record"})
+        elif clk["sm_mhz"] < min_clock_fraction * clk["sm_max_mhz"] and "sw_power_cap" not in reasons:
+            rejected.append({"case": list(k), "reason": f"SM clock {clk['sm_mhz']} MHz well below max with no reason"})
+        if "sw_power_cap" in reasons:
+            notes.append({"case": list(k), "note": "sw_power_cap active"})
+    missing = sorted(list(k) for k in expected - set(seen))
+    return {"passed": not missing and not rejected, "cases": len(seen), "expected": len(expected),
+            "missing": missing, "rejected": rejected, "notes": notes}
+
+
 def bench_store(args, dev):
     from packmla.formats import abi, codec
     from packmla.ops import kv as kv_ops
@@ -316,9 +357,9 @@ def bench_store(args, dev):
     return {"case": "kv_store", "rows": R, "native_us": round(native, 3), "packed_us": round(packed, 3)}
 
 
-def main():
+def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite", "decode-paired"],
+    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite", "decode-paired", "judge"],
                     help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
                          "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
@@ -336,7 +377,16 @@ def main():
     ap.add_argument("--prof", action="store_true", help="report kernel phase / wait-time counters")
     ap.add_argument("--paired", action="store_true", help="decode-suite: native and direct in paired rounds")
     ap.add_argument("--with-adapter", action="store_true", help="decode-paired: add the adapter mode")
-    args = ap.parse_args()
+    ap.add_argument("--results", default=None, help="judge: the JSON lines of a decode-suite run")
+    args = ap.parse_args(argv)
+    if args.case == "judge":
+        with open(args.results) as f:
+            rows = [json.loads(x) for x in f if x.strip().startswith("{")]
+        verdict = judge(rows, args.rounds, paired=args.paired)
+        print(json.dumps(verdict))
+        if not verdict["passed"]:
+            raise SystemExit("suite rejected")
+        return verdict
     dev = torch.device("cuda", 0)
     if args.case == "moe":
         args.topk = args.topk or 8

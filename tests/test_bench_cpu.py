@@ -24,3 +24,41 @@ def test_paired_rounds_rotate_order_and_report_ratios():
     assert r["min"] == 0.9 and r["max"] == 1.1 and out["baseline"] == "native"
     with pytest.raises(ValueError):
         paired_rounds({}, 3)
+
+
+def _suite(rounds=30, clocks=None):
+    from packmla.bench.microbench import SUITE_BATCHES, SUITE_CONTEXTS, SUITE_FORMATS
+
+    clk = clocks or {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": []}
+    return [{"case": "sparse_mla_decode", "context": c, "batch": b, "kv_format": f, "us": 50.0, "rounds": rounds,
+             "clocks": dict(clk)} for c in SUITE_CONTEXTS for b in SUITE_BATCHES for f in SUITE_FORMATS]
+
+
+def test_judge_accepts_a_complete_clean_suite(tmp_path):
+    import json
+
+    from packmla.bench import microbench
+
+    path = tmp_path / "suite.jsonl"
+    path.write_text("".join(json.dumps(r) + "\n" for r in _suite()))
+    v = microbench.main(["judge", "--results", str(path)])
+    assert v["passed"] and v["cases"] == v["expected"] == 12
+
+
+def test_judge_rejects_missing_short_slow_and_locked_runs():
+    from packmla.bench.microbench import judge
+
+    rows = _suite()
+    v = judge(rows[:-1], 30)
+    assert not v["passed"] and v["missing"] == [[131072, 64, "direct"]]
+    assert not judge(_suite(rounds=10), 30)["passed"]
+    v = judge(_suite(clocks={"sm_mhz": 1500.0, "sm_max_mhz": 1965.0, "reasons": ["hw_thermal_slowdown"]}), 30)
+    assert not v["passed"] and "hw_thermal_slowdown" in v["rejected"][0]["reason"]
+    v = judge(_suite(clocks={"sm_mhz": 1000.0, "sm_max_mhz": 1965.0, "reasons": []}), 30)
+    assert not v["passed"] and "well below" in v["rejected"][0]["reason"]
+    v = judge(_suite(clocks={"sm_mhz": 1300.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}), 30)
+    assert v["passed"] and len(v["notes"]) == 12  # power capping is kept and noted
+    bad = _suite()
+    bad[3]["us"] = float("nan")
+    assert not judge(bad, 30)["passed"]
+    assert not judge(_suite() + _suite()[:1], 30)["passed"]  # a duplicate case
