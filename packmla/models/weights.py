@@ -183,14 +183,47 @@ def save_safetensors(directory: str, W: dict, cfg: ModelConfig, shard_bytes: int
         json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
     with open(os.path.join(directory, "packmla_config.json"), "w") as f:
         json.dump({"config": json.loads(cfg.to_json()), "meta": W["meta"]}, f, indent=1)
+    # receipt: sha256 of every shard and of the config file, checked before the weights are used
+    # (reference: its model profiles pin a revision and config hash, and receipts verify shard bytes)
+    receipt = {"files": {n: _sha256(os.path.join(directory, n)) for n in names + ["packmla_config.json"]}}
+    with open(os.path.join(directory, "receipt.json"), "w") as f:
+        json.dump(receipt, f, indent=1)
     return names
 
 
-def load_safetensors(directory: str, device="cpu") -> tuple[dict, ModelConfig]:
+def _sha256(path: str) -> str:
+    import hashlib
+
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 24), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def verify_receipt(directory: str) -> None:
+    """Raise ValueError if a shard or the config differs from the checkpoint's receipt."""
+    import json
+    import os
+
+    with open(os.path.join(directory, "receipt.json")) as f:
+        files = json.load(f)["files"]
+    for name, digest in files.items():
+        path = os.path.join(directory, name)
+        if not os.path.exists(path) or _sha256(path) != digest:
+            raise ValueError(f"checkpoint file changed or missing: {path}")
+
+
+def load_safetensors(directory: str, device="cpu", verify: bool = True) -> tuple[dict, ModelConfig]:
+    """Load a sharded checkpoint; with `verify` (default) and a receipt present, every shard and the
+    config are hash-checked first."""
     import json
     import os
 
     from safetensors.torch import load_file
+
+    if verify and os.path.exists(os.path.join(directory, "receipt.json")):
+        verify_receipt(directory)
 
     with open(os.path.join(directory, "model.safetensors.index.json")) as f:
         index = json.load(f)
@@ -212,7 +245,7 @@ def load_checkpoint(path: str, device="cpu") -> tuple[dict, ModelConfig]:
 
     if os.path.isdir(path):
         return load_safetensors(path, device)
-    blob = torch.load(path, map_location="cpu", weights_only=False)
+    blob = torch.load(path, map_location="cpu", weights_only=True)  # tensors, strings and dicts only
     cfg = ModelConfig.from_dict(json.loads(blob["config"]))
     flat = {k: v.to(device) for k, v in blob["tensors"].items()}
     return unflatten(flat, cfg, blob["meta"]), cfg

@@ -1,4 +1,5 @@
 """CPU: model prefill/decode consistency, engine scheduling, capacity accounting."""
+import pytest
 import torch
 
 from packmla.config import EngineConfig, ModelConfig
@@ -101,6 +102,24 @@ def test_safetensors_checkpoint_round_trip(tmp_path):
     assert cfg2 == cfg and W2["meta"] == W["meta"]
     a, b = flatten(W), flatten(W2)
     assert set(a) == set(b) and all(torch.equal(a[k], b[k]) for k in a)
+    # the receipt catches a changed shard before the weights are used
+    shard = tmp_path / "ckpt" / names[0]
+    data = bytearray(shard.read_bytes())
+    data[-1] ^= 0x01
+    shard.write_bytes(bytes(data))
+    with pytest.raises(ValueError, match="changed"):
+        load_checkpoint(str(tmp_path / "ckpt"))
+
+
+def test_torch_checkpoint_round_trip_loads_weights_only(tmp_path):
+    from packmla.models.weights import flatten, load_checkpoint, save_checkpoint
+
+    cfg = ModelConfig.tiny(num_layers=2)
+    W = init_weights(cfg)
+    save_checkpoint(str(tmp_path / "w.pt"), W, cfg)
+    W2, cfg2 = load_checkpoint(str(tmp_path / "w.pt"))
+    a, b = flatten(W), flatten(W2)
+    assert cfg2 == cfg and all(torch.equal(a[k], b[k]) for k in a)
 
 
 def test_prefill_chunks_and_decode_steps_alternate():
