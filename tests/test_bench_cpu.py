@@ -62,3 +62,15 @@ def test_judge_rejects_missing_short_slow_and_locked_runs():
     bad[3]["us"] = float("nan")
     assert not judge(bad, 30)["passed"]
     assert not judge(_suite() + _suite()[:1], 30)["passed"]  # a duplicate case
+
+
+def test_validation_tier_of_a_diff():
+    from packmla.utils.validation_tier import classify, main
+
+    assert classify(["README.md", "tests/test_codec.py"])["tier"] == "low"
+    assert classify(["packmla/server/app.py", "packmla/engine/engine.py"])["tier"] == "medium"
+    out = classify(["packmla/training/train.py", "csrc/kv_store.cu"])
+    assert out["tier"] == "high" and out["files"]["packmla/training/train.py"] == "low"
+    assert any("ncu" in c for c in out["required"])
+    assert classify([])["tier"] == "low"
+    assert main(["bench.py"])["tier"] == "medium"
