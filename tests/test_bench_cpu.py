@@ -74,3 +74,32 @@ def test_validation_tier_of_a_diff():
     assert any("ncu" in c for c in out["required"])
     assert classify([])["tier"] == "low"
     assert main(["bench.py"])["tier"] == "medium"
+
+
+def _hold_lock(root, ready, release):
+    from packmla.utils.build_lock import build_lock
+
+    with build_lock(root):
+        ready.set()
+        release.wait(30)
+
+
+def test_build_lock_is_exclusive_and_released_on_exit(tmp_path):
+    import multiprocessing as mp
+
+    from packmla.utils.build_lock import BuildLocked, build_lock
+
+    ctx = mp.get_context("spawn")
+    ready, release = ctx.Event(), ctx.Event()
+    p = ctx.Process(target=_hold_lock, args=(str(tmp_path), ready, release))
+    p.start()
+    try:
+        assert ready.wait(60)
+        with pytest.raises(BuildLocked, match="pid"):
+            with build_lock(str(tmp_path), timeout_s=0.5, poll_s=0.1):
+                pass
+    finally:
+        release.set()
+        p.join(30)
+    with build_lock(str(tmp_path), timeout_s=5):  # free again once the holder is gone
+        pass
