@@ -45,6 +45,14 @@ def ext():
             raise RuntimeError(
                 "packmla CUDA extension is not built; run `python setup.py build_ext --inplace`"
             ) from exc
+        import os
+        import warnings
+
+        from ..utils.source_digest import check_record
+
+        stale = check_record(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        if stale:
+            warnings.warn(stale, RuntimeWarning, stacklevel=2)
         _EXT = _Counting(_C)
     return _EXT
 

@@ -22,6 +22,21 @@ NVCC_FLAGS = [
     "-Xptxas", "-v" if os.environ.get("PACKMLA_PTXAS_VERBOSE") else "-O3",
 ]
 
+
+class _RecordingBuild(BuildExtension.with_options(use_ninja=True)):
+    """Records the digest of the built sources beside the library (packmla/_C.sources.json)."""
+
+    def run(self):
+        super().run()
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location("source_digest",
+                                                      os.path.join(ROOT, "packmla", "utils", "source_digest.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.write_record(ROOT)
+
+
 setup(
     name="packmla",
     version="0.1.0",
@@ -35,5 +50,5 @@ setup(
             libraries=["cuda"],
         )
     ],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": _RecordingBuild},
 )

@@ -103,3 +103,18 @@ def test_build_lock_is_exclusive_and_released_on_exit(tmp_path):
         p.join(30)
     with build_lock(str(tmp_path), timeout_s=5):  # free again once the holder is gone
         pass
+
+
+def test_source_digest_record_detects_a_stale_library(tmp_path):
+    from packmla.utils.source_digest import check_record, source_digest, write_record
+
+    (tmp_path / "csrc" / "common").mkdir(parents=True)
+    (tmp_path / "packmla").mkdir()
+    (tmp_path / "csrc" / "k.cu").write_text("kernel v1")
+    (tmp_path / "csrc" / "common" / "h.cuh").write_text("header")
+    (tmp_path / "setup.py").write_text("setup")
+    assert check_record(str(tmp_path)) is None  # no record yet: nothing to compare
+    d = write_record(str(tmp_path))
+    assert check_record(str(tmp_path)) is None and d == source_digest(str(tmp_path))
+    (tmp_path / "csrc" / "common" / "h.cuh").write_text("header v2")
+    assert "rebuild" in check_record(str(tmp_path))
