@@ -118,3 +118,29 @@ def test_source_digest_record_detects_a_stale_library(tmp_path):
     assert check_record(str(tmp_path)) is None and d == source_digest(str(tmp_path))
     (tmp_path / "csrc" / "common" / "h.cuh").write_text("header v2")
     assert "rebuild" in check_record(str(tmp_path))
+
+
+def _sweep_dir(root, name, points):
+    import json
+
+    d = root / name
+    d.mkdir()
+    pts = [{"concurrency": c, "repeat": r, "successful_requests_per_s": rps, "output_throughput_tok_s": tok,
+            "ttft_ms": {"p90": p90}, "passed": True, "success_rate": 1.0} for c, r, rps, tok, p90 in points]
+    (d / "summary.json").write_text(json.dumps({"points": pts, "stopped": None}))
+    return d
+
+
+def test_analyze_pairs_points_and_reports_geomean(tmp_path):
+    import math
+
+    from packmla.bench import analyze
+
+    a = _sweep_dir(tmp_path, "native", [(20, 1, 1.0, 100.0, 500.0), (24, 1, 2.0, 200.0, 800.0), (28, 1, 2.5, 250, 900)])
+    b = _sweep_dir(tmp_path, "direct", [(20, 1, 1.1, 110.0, 450.0), (24, 1, 2.4, 220.0, 800.0), (32, 1, 3.0, 300, 1e3)])
+    out = analyze.main([str(a), str(b), "--output", str(tmp_path / "cmp.json")])
+    assert [p["concurrency"] for p in out["points"]] == [20, 24]
+    assert math.isclose(out["geomean_ratio"]["successful_requests_per_s"], math.sqrt(1.1 * 1.2))
+    assert math.isclose(out["geomean_ratio"]["ttft_p90_ms"], math.sqrt(0.9 * 1.0))
+    assert out["only_baseline"] == [[28, 1]] and out["only_candidate"] == [[32, 1]]
+    assert (tmp_path / "cmp.json").exists()
