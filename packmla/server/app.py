@@ -20,6 +20,7 @@ While streaming, text already sent before a multi-token stop string completes is
 from __future__ import annotations
 
 import asyncio
+import contextlib
 import json
 import time
 import uuid
@@ -109,9 +110,31 @@ def _sse(obj) -> bytes:
 
 def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, server_args: dict | None = None
                ) -> FastAPI:
-    app = FastAPI(title="packmla")
     eng = driver.engine
     vocab = eng.cfg.vocab_size
+
+    @contextlib.asynccontextmanager
+    async def lifespan(_app):
+        # event-loop lag probe (reference: its frontend event-loop probe): a 100 ms sleep that wakes late
+        # means request handlers or token delivery are blocking the loop
+        async def probe():
+            loop = asyncio.get_running_loop()
+            worst = 0.0
+            while True:
+                t = loop.time()
+                await asyncio.sleep(0.1)
+                lag = max(0.0, (loop.time() - t - 0.1) * 1000)
+                worst = max(worst, lag)
+                eng.metrics.set("event_loop_lag_ms_last", round(lag, 3))
+                eng.metrics.set("event_loop_lag_ms_max", round(worst, 3))
+
+        task = asyncio.create_task(probe())
+        try:
+            yield
+        finally:
+            task.cancel()
+
+    app = FastAPI(title="packmla", lifespan=lifespan)
 
     async def _submit(ids: list[int], params: SamplingParams):
         _check_ids(ids, vocab)

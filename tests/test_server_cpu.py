@@ -181,3 +181,15 @@ def test_unsupported_sampling_knobs_are_rejected(served):
     assert r.status_code == 200
     r = client.post("/generate", json={"text": "x", "sampling_params": {"max_new_tokens": 2, "top_k": 20}})
     assert r.status_code == 400
+
+
+def test_event_loop_lag_probe_is_exported(served):
+    import time
+
+    client, eng, tok, cfg = served
+    for _ in range(50):
+        if "event_loop_lag_ms_max" in eng.metrics.snapshot():
+            break
+        time.sleep(0.05)
+    text = client.get("/metrics").text
+    assert "packmla_event_loop_lag_ms_last" in text and "packmla_event_loop_lag_ms_max" in text
