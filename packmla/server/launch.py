@@ -9,7 +9,8 @@ Environment (all optional): MODE (native | direct; the positional mode wins), MO
 DEVICE (cuda | cpu), TP, EP, PORT (30000), MASTER_PORT (29500), MEM_FRAC, CTX_LEN, MAX_RUN, CHUNK,
 DECODE_CFG (the --cuda-graph-config JSON), SERVER_SEED, HICACHE_RATIO (turns HiCache on),
 C4_KEEP_COUNT, C4_LAYER_KEEP_COUNTS, STORE_IMPLEMENTATION, REQUEST_METRICS_DIR (request log and
-per-request metric files; the directory must exist).  TP > 1 runs one process per GPU under torchrun
+per-request metric files; the directory must exist), NSYS_OUTPUT (run under Nsight Systems, which
+records only between POST /start_profile and /stop_profile).  TP > 1 runs one process per GPU under torchrun
 on 127.0.0.1.
 
 The launcher owns the server's process group: it starts the server in a new session, waits for
@@ -65,6 +66,14 @@ def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
                "-m", "packmla.server"]
     else:
         cmd = [sys.executable, "-m", "packmla.server"]
+    if env.get("NSYS_OUTPUT"):  # Nsight Systems attached at launch, collecting between /start_profile and /stop_profile
+        import shutil
+
+        nsys = shutil.which("nsys", path=env.get("PATH"))
+        if nsys is None:
+            raise SystemExit("NSYS_OUTPUT is set but nsys is not on PATH")
+        cmd = [nsys, "profile", "-o", env["NSYS_OUTPUT"], "--trace=cuda,nvtx", "--capture-range=cudaProfilerApi",
+               "--capture-range-end=stop", "--force-overwrite=false"] + cmd
     extra = {"NCCL_SOCKET_IFNAME": env.get("NCCL_SOCKET_IFNAME", "lo"),
              "GLOO_SOCKET_IFNAME": env.get("GLOO_SOCKET_IFNAME", "lo")}
     return cmd + flags, extra

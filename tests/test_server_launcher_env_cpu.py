@@ -72,3 +72,15 @@ def test_sweep_owns_its_server(monkeypatch, tmp_path):
     assert (tmp_path / "sw.server.log").exists()
     with pytest.raises(requests.RequestException):  # the owned server is gone
         requests.get(f"http://127.0.0.1:{port}/health", timeout=2)
+
+
+def test_nsys_output_wraps_the_server(tmp_path):
+    fake = tmp_path / "bin"
+    fake.mkdir()
+    (fake / "nsys").write_text("#!/bin/sh\nexit 0\n")
+    (fake / "nsys").chmod(0o755)
+    cmd, _ = launch.resolve("direct", {"NSYS_OUTPUT": str(tmp_path / "trace"), "PATH": str(fake)})
+    assert cmd[0] == str(fake / "nsys") and "--capture-range=cudaProfilerApi" in cmd
+    assert cmd[cmd.index("-o") + 1] == str(tmp_path / "trace") and "packmla.server" in cmd
+    with pytest.raises(SystemExit, match="nsys"):
+        launch.resolve("direct", {"NSYS_OUTPUT": "x", "PATH": str(tmp_path / "empty")})
