@@ -24,6 +24,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--model", "--model-path", dest="model", default="tiny",
                     help="tiny | small | v4-flash | path to a packmla checkpoint")
     ap.add_argument("--served-model-name", default=None)
+    ap.add_argument("--tokenizer", "--tokenizer-path", dest="tokenizer", default=None,
+                    help="directory with Hugging Face tokenizer files (local only); default: byte-level tokenizer")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=30000)
     ap.add_argument("--device", default="cuda")
@@ -201,7 +203,7 @@ def main(argv=None) -> None:
 
     from ..parallel.comm import TPComm, init_from_env
     from .driver import EngineDriver
-    from .tokenizer import ByteTokenizer
+    from .tokenizer import load_tokenizer
 
     backend = "nccl" if args.device == "cuda" else "gloo"
     rank, world, local = init_from_env(backend)
@@ -227,7 +229,7 @@ def main(argv=None) -> None:
 
     from .app import create_app
 
-    app = create_app(driver, ByteTokenizer(eng.cfg.vocab_size), name, {"server_args": vars(args)})
+    app = create_app(driver, load_tokenizer(args.tokenizer, eng.cfg.vocab_size), name, {"server_args": vars(args)})
     driver.start()
     print(json.dumps({"event": "server_ready", "host": args.host, "port": args.port,
                       "max_total_num_tokens": eng.capacity.max_total_tokens}), flush=True)

@@ -50,3 +50,37 @@ def _content(c) -> str:
     if isinstance(c, list):  # OpenAI content parts
         return "".join(p.get("text", "") for p in c if isinstance(p, dict))
     return str(c)
+
+
+class HFTokenizer:
+    """A local Hugging Face tokenizer (a checkpoint's tokenizer.json / tokenizer_config.json) behind the
+    interface of `ByteTokenizer`; loaded with `local_files_only`, so nothing is downloaded.  The chat
+    template is the tokenizer's own when it has one, else the plain concatenation above."""
+
+    def __init__(self, path: str, vocab_size: int):
+        from transformers import AutoTokenizer
+
+        self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+        if len(self.tok) > vocab_size:
+            raise ValueError(f"tokenizer has {len(self.tok)} tokens, the model's vocabulary {vocab_size}")
+        self.vocab_size = vocab_size
+        self.bos_token_id = self.tok.bos_token_id if self.tok.bos_token_id is not None else 0
+        self.eos_token_id = self.tok.eos_token_id
+
+    def encode(self, text: str, add_bos: bool = True) -> list[int]:
+        ids = self.tok.encode(text, add_special_tokens=False)
+        return ([self.bos_token_id] if add_bos and self.tok.bos_token_id is not None else []) + ids
+
+    def decode(self, ids: list[int]) -> str:
+        return self.tok.decode([i for i in ids if i < len(self.tok)], skip_special_tokens=True)
+
+    def apply_chat_template(self, messages: list[dict]) -> list[int]:
+        msgs = [{"role": m.get("role", "user"), "content": _content(m.get("content", ""))} for m in messages]
+        if getattr(self.tok, "chat_template", None):
+            return list(self.tok.apply_chat_template(msgs, add_generation_prompt=True, tokenize=True))
+        return self.encode("".join(f"<|{m['role']}|>{m['content']}" for m in msgs) + "<|assistant|>")
+
+
+def load_tokenizer(path: str | None, vocab_size: int):
+    """`--tokenizer PATH` (a directory with Hugging Face tokenizer files), or the byte tokenizer."""
+    return HFTokenizer(path, vocab_size) if path else ByteTokenizer(vocab_size)
