@@ -213,6 +213,7 @@ class EngineDriver:
                         if st.t_first is None:
                             st.t_first = time.perf_counter()
                             eng.metrics.inc("ttft_seconds_sum", st.t_first - st.t_submit)
+                            eng.metrics.observe("time_to_first_token_seconds", st.t_first - st.t_submit)
                         st.tokens.append(tok)
                         self._deliver_to(st, tok)
                     req = eng.done.pop(rid, None)  # the driver keeps no history of finished requests
@@ -221,7 +222,12 @@ class EngineDriver:
                         hit_eos = (not p.ignore_eos and p.eos_token_id is not None and req.output_ids
                                    and req.output_ids[-1] == p.eos_token_id)
                         if st is not None:
-                            eng.metrics.inc("e2e_seconds_sum", time.perf_counter() - st.t_submit)
+                            now = time.perf_counter()
+                            eng.metrics.inc("e2e_seconds_sum", now - st.t_submit)
+                            eng.metrics.observe("e2e_request_latency_seconds", now - st.t_submit)
+                            if st.t_first is not None and len(st.tokens) > 1:
+                                eng.metrics.observe("time_per_output_token_seconds",
+                                                    (now - st.t_first) / (len(st.tokens) - 1))
                         self._finish(rid, "stop" if hit_eos else "length")
         except BaseException as exc:  # surface to handlers instead of dying silently
             self.error = exc

@@ -144,3 +144,18 @@ def test_analyze_pairs_points_and_reports_geomean(tmp_path):
     assert math.isclose(out["geomean_ratio"]["ttft_p90_ms"], math.sqrt(0.9 * 1.0))
     assert out["only_baseline"] == [[28, 1]] and out["only_candidate"] == [[32, 1]]
     assert (tmp_path / "cmp.json").exists()
+
+
+def test_latency_histograms_export_cumulative_buckets():
+    from packmla.utils.metrics import LATENCY_BUCKETS, Metrics
+
+    m = Metrics()
+    for v in (0.003, 0.02, 0.02, 7.0, 1000.0):
+        m.observe("ttft", v)
+    h = m.histogram("ttft")
+    assert h["count"] == 5 and abs(h["sum"] - 1007.043) < 1e-9
+    assert h["buckets"]["0.005"] == 1 and h["buckets"]["0.025"] == 3 and h["buckets"]["10.0"] == 4
+    assert h["buckets"]["+Inf"] == 5 and len(h["buckets"]) == len(LATENCY_BUCKETS) + 1
+    text = m.prometheus()
+    assert 'packmla_ttft_bucket{le="+Inf"} 5' in text and "packmla_ttft_count 5" in text
+    assert "# TYPE packmla_ttft histogram" in text

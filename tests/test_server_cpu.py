@@ -193,3 +193,11 @@ def test_event_loop_lag_probe_is_exported(served):
         time.sleep(0.05)
     text = client.get("/metrics").text
     assert "packmla_event_loop_lag_ms_last" in text and "packmla_event_loop_lag_ms_max" in text
+
+
+def test_latency_histograms_on_metrics(served):
+    client, eng, tok, cfg = served
+    client.post("/v1/completions", json={"model": "tiny", "prompt": "histogram", "max_tokens": 3, "ignore_eos": True})
+    text = client.get("/metrics").text
+    for name in ("time_to_first_token_seconds", "e2e_request_latency_seconds", "time_per_output_token_seconds"):
+        assert f'packmla_{name}_bucket{{le="+Inf"}}' in text and f"packmla_{name}_count" in text
