@@ -84,3 +84,26 @@ def test_nsys_output_wraps_the_server(tmp_path):
     assert cmd[cmd.index("-o") + 1] == str(tmp_path / "trace") and "packmla.server" in cmd
     with pytest.raises(SystemExit, match="nsys"):
         launch.resolve("direct", {"NSYS_OUTPUT": "x", "PATH": str(tmp_path / "empty")})
+
+
+def test_capacity_stress_compares_reuse_tiers(monkeypatch, tmp_path):
+    from packmla.bench import capacity_stress
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    for k, v in {"MODEL": "tiny", "DEVICE": "cpu", "PORT": str(port), "MAX_RUN": "4", "CTX_LEN": "1024"}.items():
+        monkeypatch.setenv(k, v)
+    for k in ("TP", "WORLD_SIZE", "RANK", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "HICACHE_RATIO"):
+        monkeypatch.delenv(k, raising=False)
+    out = capacity_stress.main(["direct", "--settings", "none,prefix,hicache", "--sessions", "2", "--turns", "2",
+                                "--input-len", "64", "--output-len", "4", "--concurrency", "2",
+                                "--startup-timeout", "300", "--log-dir", str(tmp_path)])
+    r = {x["setting"]: x for x in out["results"]}
+    assert all(t["validated"] for x in r.values() for t in x["turns"])
+    assert r["none"]["prefix_cache_hit_tokens"] == 0 and r["none"]["hicache_hit_tokens"] == 0
+    assert r["prefix"]["prefix_cache_hit_tokens"] > 0 and r["prefix"]["hicache_hit_tokens"] == 0
+    assert r["hicache"]["hicache_hit_tokens"] > 0 and r["hicache"]["prefix_cache_hit_tokens"] == 0
+    # reuse means less prefill work for the same conversation
+    assert r["prefix"]["prefill_tokens"] < r["none"]["prefill_tokens"]
+    assert r["hicache"]["prefill_tokens"] < r["none"]["prefill_tokens"]
