@@ -20,7 +20,10 @@ class ClockSampler:
 
     def __init__(self, gpu_index: int, out_path: str | None = None):
         self.gpu = gpu_index
-        self.path = out_path or tempfile.mktemp(suffix=".csv")
+        if out_path is None:  # a file created here (no name race), removed by nobody: a few KB of samples
+            fd, out_path = tempfile.mkstemp(suffix=".csv", prefix="packmla-clocks-")
+            os.close(fd)
+        self.path = out_path
         self.proc = None
 
     def __enter__(self):
