@@ -194,3 +194,15 @@ def sparse_decode_reference(q: torch.Tensor, pool: torch.Tensor, kv_format: str,
         sel = sel[sel >= 0]
         rows.append(torch.cat((swa_rows[b].float(), gather_rows(pool, kv_format, sel))))
     return sparse_mla_decode(q, rows, sink, scale, q_freqs)
+
+
+# --------------------------------------------------------------------------- capacity
+def capacity_tokens(model_cfg, kv_format: str, budget_bytes: int, swa_ratio: float = 0.1) -> int:
+    """KV token capacity of `budget_bytes` with FP4 C4 records (Native 288 B or Packed 224 B) and
+    everything else as the FP8 pool accounts it (indexer keys, C128 records, SWA share)."""
+    from ..kv.pool import bytes_per_full_token
+
+    fp8 = bytes_per_full_token(model_cfg, "native", swa_ratio)
+    c4_layers = len(model_cfg.c4_layers)
+    bpt = fp8 + c4_layers * (record_bytes(kv_format) - abi.NATIVE_RECORD_BYTES) / abi.C4_RATIO
+    return int(budget_bytes // bpt)

@@ -157,3 +157,13 @@ def test_fp4_sparse_decode_reference_matches_dense_attention():
         ref_o, ref_l = sparse_mla_decode(q, kv, sink, 512 ** -0.5, freqs)
         assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)
         assert kv[0].shape[0] == 5 + K - 1 and kv[1].shape[0] == 5 + 13
+
+
+def test_fp4_capacity_gain_is_below_the_record_shrink():
+    from packmla.config import ModelConfig
+
+    cfg = ModelConfig()
+    native = fp4.capacity_tokens(cfg, "native", 1 << 30)
+    direct = fp4.capacity_tokens(cfg, "direct", 1 << 30)
+    gain = direct / native
+    assert 1.0 < gain < 288 / 224  # indexer keys, C128 records and the SWA share do not shrink
