@@ -72,7 +72,7 @@ def load_sessions(path: str) -> list[list[dict]]:
 async def _turn(session, url: str, model: str, rec: dict) -> dict:
     body = {"model": model, "messages": rec["messages"], "max_tokens": int(rec.get("max_tokens", 256)),
             "temperature": float(rec.get("temperature", 0.0)), "stream": True,
-            "ignore_eos": bool(rec.get("ignore_eos", True))}
+            "stream_options": {"include_usage": True}, "ignore_eos": bool(rec.get("ignore_eos", True))}
     t0 = time.perf_counter()
     out = {"session": str(rec["session"]), "turn": rec.get("turn", 0), "ok": False, "ttft": None, "tokens": 0}
     try:
@@ -84,7 +84,13 @@ async def _turn(session, url: str, model: str, rec: dict) -> dict:
                 line = raw.decode().strip()
                 if not line.startswith("data: ") or line == "data: [DONE]":
                     continue
-                delta = json.loads(line[6:])["choices"][0]
+                chunk = json.loads(line[6:])
+                if chunk.get("usage"):
+                    out["prompt_tokens"] = chunk["usage"].get("prompt_tokens", 0)
+                    out["cached_tokens"] = (chunk["usage"].get("prompt_tokens_details") or {}).get("cached_tokens", 0)
+                if not chunk.get("choices"):
+                    continue
+                delta = chunk["choices"][0]
                 if delta.get("delta", {}).get("content"):
                     if out["ttft"] is None:
                         out["ttft"] = time.perf_counter() - t0
@@ -163,6 +169,8 @@ def replay(url: str, requests_path: str, users: int, model: str = "default", min
             "successful_requests_per_s": len(ok) / wall if wall > 0 else 0.0,
             "ttft_ms": {"p50": pct(ttft, 50), "p90": p90, "p99": pct(ttft, 99)},
             "e2e_ms": {"p50": pct(e2e, 50), "p99": pct(e2e, 99)},
+            "cache_hit_rate": (sum(r.get("cached_tokens", 0) for r in ok) / max(1, sum(r.get("prompt_tokens", 0)
+                                                                                          for r in ok))),
             "hicache_restored_tokens": _metric(url, "packmla_hicache_hit_tokens") - hits0,
             "prefix_cache_hit_tokens": _metric(url, "packmla_prefix_cache_hit_tokens") - prefix0,
             "errors": [r.get("error") for r in results if not r["ok"]][:5]}

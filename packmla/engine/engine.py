@@ -62,6 +62,7 @@ class Request:
     t_arrival: float = 0.0
     t_first_token: float | None = None
     t_finish: float | None = None
+    cached_tokens: int = 0  # prompt tokens whose KV came from the device prefix cache or the host tier
 
     @property
     def context_len(self) -> int:
@@ -299,6 +300,7 @@ class Engine:
             return None
         self.pool.ensure(slot, need)
         req.slot, req.prefilled = slot, len(key)
+        req.cached_tokens = len(key)
         self.metrics.inc("prefix_cache_hit_tokens", len(key))
         return True
 
@@ -331,6 +333,7 @@ class Engine:
                 entry = self.hicache.match(req.prompt)
                 if entry is not None:  # earlier turn of this context: restore its KV, prefill the rest
                     req.prefilled = self.hicache.restore(entry, req.slot)
+                    req.cached_tokens = req.prefilled
                     self.metrics.inc("hicache_hit_tokens", req.prefilled)
         return req
 

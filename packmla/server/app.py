@@ -185,9 +185,10 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             raise HTTPException(400, "streaming supports n = 1")
         return n
 
-    def _usage(prompt_tokens: int, completion_tokens: int) -> dict:
+    def _usage(prompt_tokens: int, completion_tokens: int, cached_tokens: int = 0) -> dict:
         return {"prompt_tokens": prompt_tokens, "completion_tokens": completion_tokens,
-                "total_tokens": prompt_tokens + completion_tokens}
+                "total_tokens": prompt_tokens + completion_tokens,
+                "prompt_tokens_details": {"cached_tokens": cached_tokens}}
 
     @app.get("/health")
     async def health():
@@ -233,7 +234,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
                             "choices": [{"index": 0, "text": "", "logprobs": None,
                                          "finish_reason": st.finish_reason}],
-                            "usage": _usage(st.prompt_len, n)})
+                            "usage": _usage(st.prompt_len, n, st.cached_tokens)})
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
@@ -247,7 +248,8 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             choices.append({"index": i, "text": _text(toks, rule), "token_ids": toks, "logprobs": None,
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": choices, "usage": _usage(sum(len(p) for p in prompts), ntok)}
+                "choices": choices,
+                "usage": _usage(sum(len(p) for p in prompts), ntok, sum(st.cached_tokens for st in streams))}
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
@@ -277,7 +279,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                                              "finish_reason": None}]})
                 yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                             "choices": [{"index": 0, "delta": {}, "finish_reason": st.finish_reason}],
-                            "usage": _usage(len(ids), n)})
+                            "usage": _usage(len(ids), n, st.cached_tokens)})
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
@@ -290,7 +292,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             choices.append({"index": i, "message": {"role": "assistant", "content": _text(toks, rule)},
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": choices, "usage": _usage(len(ids), ntok)}
+                "choices": choices, "usage": _usage(len(ids), ntok, sum(st.cached_tokens for st in streams))}
 
     @app.post("/generate")
     async def generate(req: Request):
@@ -309,6 +311,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         now = time.perf_counter()
         return {"text": _text(toks, rule), "output_ids": toks,
                 "meta_info": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
+                              "cached_tokens": st.cached_tokens,
                               "finish_reason": {"type": st.finish_reason},
                               "e2e_latency": now - st.t_submit,
                               "ttft": (st.t_first - st.t_submit) if st.t_first else None}}

@@ -37,6 +37,7 @@ class Stream:
     t_first: float | None = None
     params: SamplingParams | None = None
     prompt: list[int] | None = None  # kept only when the request log records prompt ids
+    cached_tokens: int = 0  # prompt tokens served from a KV cache tier (known when the request ends)
 
 
 class EngineDriver:
@@ -222,6 +223,7 @@ class EngineDriver:
                         hit_eos = (not p.ignore_eos and p.eos_token_id is not None and req.output_ids
                                    and req.output_ids[-1] == p.eos_token_id)
                         if st is not None:
+                            st.cached_tokens = req.cached_tokens
                             now = time.perf_counter()
                             eng.metrics.inc("e2e_seconds_sum", now - st.t_submit)
                             eng.metrics.observe("e2e_request_latency_seconds", now - st.t_submit)

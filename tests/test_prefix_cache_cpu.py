@@ -35,6 +35,7 @@ def test_next_turn_adopts_the_retained_slot_and_matches_recompute():
         assert m["prefix_cache_hit_tokens"] == cached
         assert m["prefill_tokens"] - before == len(turn2) - cached
         assert eng.result(rid).slot == slot  # the same slot continued
+        assert eng.result(rid).cached_tokens == cached
         ref = _engine(fmt, prefix=False).generate([turn2], SamplingParams(max_new_tokens=5))[0]
         assert out2 == ref, fmt
 

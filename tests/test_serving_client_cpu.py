@@ -252,3 +252,23 @@ def test_serving_cli_writes_validated_wave_records(server_url, tmp_path):
     # a short response makes its wave invalid
     bad = serving.summarize([serving.Result(True, 5, [1, 2, 3]), serving.Result(False, 5, [1], error="short")], 1.0)
     assert not bad["validated"] and bad["output_lens"] == [3, 1]
+
+
+def test_usage_reports_cached_prompt_tokens(server_url):
+    import requests
+
+    url, eng = server_url
+    requests.post(url + "/flush_cache", timeout=30)
+    p1 = [100 + (i * 7) % 200 for i in range(150)]
+    r1 = requests.post(url + "/v1/completions", json={"model": "tiny", "prompt": p1, "max_tokens": 4,
+                                                       "ignore_eos": True}, timeout=120).json()
+    assert r1["usage"]["prompt_tokens_details"]["cached_tokens"] == 0
+    out1 = r1["choices"][0]["token_ids"]
+    p2 = p1 + out1 + [50, 51, 52]
+    r2 = requests.post(url + "/v1/completions", json={"model": "tiny", "prompt": p2, "max_tokens": 2,
+                                                       "ignore_eos": True}, timeout=120).json()
+    assert r2["usage"]["prompt_tokens_details"]["cached_tokens"] == len(p1) + len(out1) - 1
+    g = requests.post(url + "/generate", json={"input_ids": p2 + r2["choices"][0]["token_ids"] + [9],
+                                               "sampling_params": {"max_new_tokens": 1, "ignore_eos": True}},
+                      timeout=120).json()
+    assert g["meta_info"]["cached_tokens"] == len(p2) + 1
