@@ -50,7 +50,8 @@ def test_completions_match_engine_generate(served):
     assert r.status_code == 200, r.text
     body = r.json()
     ids = body["choices"][0]["token_ids"]
-    assert body["usage"] == {"prompt_tokens": 12, "completion_tokens": len(ids), "total_tokens": 12 + len(ids)}
+    assert body["usage"] == {"prompt_tokens": 12, "completion_tokens": len(ids), "total_tokens": 12 + len(ids),
+                             "prompt_tokens_details": {"cached_tokens": 0}}
     assert ids == _reference_tokens(cfg, tok.encode("hello world"), 5)
     assert body["choices"][0]["text"] == tok.decode(ids)
     # token-id prompt, two prompts in one call
