@@ -185,6 +185,8 @@ class Engine:
         self._last_prefill = False
         # device prefix cache: processed tokens of a finished request -> its retained slot (LRU order)
         self.retained: OrderedDict[tuple, int] = OrderedDict()
+        # prompt forks: leader rid -> requests with the same prompt that copy its KV once it is prefilled
+        self.forks: dict[int, list[Request]] = {}
         self.hicache = None
         if engine_cfg.enable_hierarchical_cache:
             from ..kv.hicache import HostKVCache
@@ -231,13 +233,62 @@ class Engine:
         self.metrics.inc("requests_received")
         return req.rid
 
+    def add_group(self, prompt: list[int], params: SamplingParams | None = None, n: int = 1) -> list[int]:
+        """`n` requests with one prompt (the OpenAI `n`): the first is prefilled, the others copy its KV
+        when its prefill ends and sample their own first token from the same logits, so the prompt is
+        prefilled once.  A copy that finds no free slot or pages then is prefilled on its own later."""
+        lead = self.add_request(prompt, params)
+        if n <= 1:
+            return [lead]
+        followers = [Request(next(self._ids), list(prompt), params or SamplingParams(), t_arrival=time.perf_counter())
+                     for _ in range(n - 1)]
+        self.forks[lead] = followers
+        self.metrics.inc("requests_received", n - 1)
+        return [lead] + [f.rid for f in followers]
+
+    def _fork(self, leader: Request, logits: torch.Tensor) -> list[tuple[int, int]]:
+        """Start the followers of `leader` (just prefilled, slot intact) from copies of its KV."""
+        produced = []
+        n = len(leader.prompt)
+        for f in self.forks.pop(leader.rid, []):
+            need = n + f.params.max_new_tokens
+            pages = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
+            while (not self.pool._free_slots or pages > self.pool.pages.free) and self._evict_retained():
+                pass
+            if (len(self.running) + 1 >= self.runner.max_b or not self.pool._free_slots
+                    or pages > self.pool.pages.free):
+                self.waiting.append(f)  # no room now: an ordinary prefill later
+                continue
+            f.slot = self.pool.admit(need)
+            self.pool.clone_kv(leader.slot, f.slot, n)
+            f.prefilled = f.cached_tokens = n
+            self.metrics.inc("fork_copied_tokens", n)
+            temp = torch.tensor([f.params.temperature], device=self.device)
+            tok = int(sample(logits[None], temp)[0])
+            self._emit(f, tok)
+            if not f.finished:
+                self.running.append(f)
+            produced.append((f.rid, tok))
+        return produced
+
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.forks)
 
     def result(self, rid: int) -> Request:
         return self.done[rid]
 
     def abort(self, rid: int) -> bool:
+        followers = self.forks.pop(rid, None)
+        if followers:  # the copies of an aborted leader are prefilled on their own
+            self.waiting.extend(followers)
+        for lead, fs in list(self.forks.items()):
+            for f in fs:
+                if f.rid == rid:
+                    fs.remove(f)
+                    f.finished = True
+                    self.done[rid] = f
+                    self.metrics.inc("requests_aborted")
+                    return True
         for q in (self.waiting, self.running):
             for r in list(q):
                 if r.rid == rid:
@@ -376,10 +427,11 @@ class Engine:
         self.waiting.popleft()
         temp = torch.tensor([req.params.temperature], device=self.device)
         tok = int(sample(logits[None], temp)[0])
+        forked = self._fork(req, logits) if req.rid in self.forks else []  # before the leader can finish
         self._emit(req, tok)
         if not req.finished:
             self.running.append(req)
-        return [(req.rid, tok)]
+        return [(req.rid, tok)] + forked
 
     def _decode(self) -> list[tuple[int, int]]:
         reqs = self.running

@@ -208,6 +208,40 @@ class KVPool:
         self.c128_table[slot] = -1
         self._free_slots.append(slot)
 
+    def clone_kv(self, src: int, dst: int, tokens: int) -> None:
+        """Copy the KV of the first `tokens` tokens of request slot `src` into slot `dst` (pages already
+        reserved for both): C4 planes and indexer keys of the covering pages, C128 records, the SWA ring
+        and the compressor / indexer pooling state, so `dst` continues exactly where `src` stands."""
+        R, PB = abi.RECORDS_PER_PAGE, abi.NATIVE_PAGE_BYTES
+        n = (tokens + self.TOKENS_PER_PAGE - 1) // self.TOKENS_PER_PAGE
+        n128 = (tokens + self.TOKENS_PER_C128_PAGE - 1) // self.TOKENS_PER_C128_PAGE
+        dev = self.device
+        sp = torch.tensor(self._req_pages[src][:n], dtype=torch.int64, device=dev)
+        dp = torch.tensor(self._req_pages[dst][:n], dtype=torch.int64, device=dev)
+        j = torch.arange(R, device=dev)
+        srow, drow = (sp[:, None] * R + j).reshape(-1), (dp[:, None] * R + j).reshape(-1)
+        for layer in self.cfg.c4_layers:
+            if self.kv_format == "direct":
+                for t in (self.c4_values[layer], self.c4_bitmap[layer], self.c4_scales[layer]):
+                    t[drow] = t[srow]
+            else:
+                pages = self.c4_native[layer].view(-1, PB)
+                pages[dp] = pages[sp]
+            self.index_keys[layer][drow] = self.index_keys[layer][srow]
+            self.index_scales[layer][drow] = self.index_scales[layer][srow]
+        if n128:
+            s128 = torch.tensor(self._req_c128[src][:n128], dtype=torch.int64, device=dev)
+            d128 = torch.tensor(self._req_c128[dst][:n128], dtype=torch.int64, device=dev)
+            for t in self.c128_native.values():
+                pages = t.view(-1, PB)
+                pages[d128] = pages[s128]
+        slot_bytes = (self.cfg.window // R) * PB
+        for t in self.swa:
+            ring = t.view(-1, slot_bytes)
+            ring[dst] = ring[src]
+        for st in list(self.comp_state.values()) + list(self.index_state.values()):
+            st[dst] = st[src]
+
     def comp_state_reset(self, slot: int) -> None:
         for st in list(self.comp_state.values()) + list(self.index_state.values()):
             st[slot, 0] = float("-inf")

@@ -145,6 +145,16 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         except RuntimeError as exc:
             raise HTTPException(503, str(exc)) from exc
 
+    async def _submit_group(ids: list[int], params: SamplingParams, n: int):
+        """n choices of one prompt: prefilled once, the other choices copy its KV."""
+        _check_ids(ids, vocab)
+        try:
+            return driver.submit_group(ids, params, n, asyncio.get_running_loop())
+        except ValueError as exc:
+            raise HTTPException(400, str(exc)) from exc
+        except RuntimeError as exc:
+            raise HTTPException(503, str(exc)) from exc
+
     async def _tokens(st, rule: _StopRule | None):
         """Tokens of one request as they arrive; a stop rule that fires aborts the request early, and so
         does a consumer that goes away first (a client that disconnected, a cancelled handler)."""
@@ -238,7 +248,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
-        streams = [await _submit(p, params) for p in prompts for _ in range(n_choices)]
+        streams = [st for p in prompts for st in await _submit_group(p, params, n_choices)]
         choices = []
         ntok = 0
         for i, st in enumerate(streams):
@@ -283,7 +293,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
-        streams = [await _submit(ids, params) for _ in range(n_choices)]
+        streams = await _submit_group(ids, params, n_choices)
         choices, ntok = [], 0
         for i, st in enumerate(streams):
             rule = _StopRule(body, tokenizer)

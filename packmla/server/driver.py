@@ -97,6 +97,28 @@ class EngineDriver:
         self._inbox.put(("add", ext, list(prompt), params))
         return st
 
+    def submit_group(self, prompt: list[int], params: SamplingParams, n: int,
+                     loop: asyncio.AbstractEventLoop | None = None) -> list[Stream]:
+        """`n` streams of one prompt, prefilled once (the other requests copy its KV)."""
+        if n <= 1:
+            return [self.submit(prompt, params, loop)]
+        if self.error is not None:
+            raise RuntimeError(f"engine loop failed: {self.error!r}")
+        if not prompt:
+            raise ValueError("empty prompt")
+        need = len(prompt) + params.max_new_tokens
+        if need > self.engine.pool.max_context:
+            raise ValueError(f"prompt + max_tokens = {need} exceeds the context limit {self.engine.pool.max_context}")
+        streams = []
+        for _ in range(n):
+            ext = next(self._ext_ids)
+            st = Stream(ext, len(prompt), loop, asyncio.Queue() if loop is not None else None,
+                        t_submit=time.perf_counter(), params=params)
+            self._streams[ext] = st
+            streams.append(st)
+        self._inbox.put(("add_group", [st.ext_id for st in streams], list(prompt), params))
+        return streams
+
     def stalled(self) -> bool:
         t = self._step_started
         return t is not None and time.perf_counter() - t > self.watchdog_s
@@ -152,6 +174,10 @@ class EngineDriver:
                 _, ext, prompt, params = op
                 rid = eng.add_request(prompt, params)
                 self._rid_to_ext[rid] = ext
+            elif kind == "add_group":
+                _, exts, prompt, params = op
+                for rid, ext in zip(eng.add_group(prompt, params, len(exts)), exts):
+                    self._rid_to_ext[rid] = ext
             elif kind == "abort":
                 ext = op[1]
                 for rid, e in list(self._rid_to_ext.items()):

@@ -9,7 +9,7 @@ from packmla.engine.engine import Engine, SamplingParams
 def _engine(fmt="direct", prefix=True, max_running=2):
     cfg = ModelConfig.tiny(num_layers=3)
     ecfg = EngineConfig(kv_cache_format=fmt, device="cpu", chunked_prefill_size=64, max_running_requests=max_running,
-                        cuda_graph_bs=[1, 2], prefix_cache=prefix)
+                        cuda_graph_bs=[1, 2, 4], prefix_cache=prefix)
     return Engine.build(cfg, ecfg, "cpu", max_context=1024)
 
 
@@ -61,3 +61,41 @@ def test_identical_prompt_is_not_a_strict_prefix_and_repeats_exactly():
     b = eng.generate([p], SamplingParams(max_new_tokens=4))[0]
     assert a == b and not eng.metrics.snapshot().get("prefix_cache_hit_tokens")
     assert len(eng.retained) == 1  # the same key replaces its older slot
+
+
+def test_group_prefills_once_and_copies_match():
+    for fmt in ("direct", "native"):
+        p = _toks(270, 11)
+        eng = _engine(fmt, prefix=False, max_running=4)
+        rids = eng.add_group(p, SamplingParams(max_new_tokens=5), n=3)
+        while eng.has_work():
+            eng.step()
+        outs = [eng.result(r).output_ids for r in rids]
+        m = eng.metrics.snapshot()
+        assert m["prefill_tokens"] == len(p) and m["fork_copied_tokens"] == 2 * len(p)
+        ref = _engine(fmt, prefix=False).generate([p], SamplingParams(max_new_tokens=5))[0]
+        assert outs == [ref] * 3, fmt  # greedy copies continue exactly like the prefilled request
+        assert [eng.result(r).cached_tokens for r in rids] == [0, len(p), len(p)]
+        assert eng.pool.pages.free == eng.pool.num_pages
+
+
+def test_group_without_room_falls_back_to_prefill_and_sampling_is_independent():
+    p = _toks(90, 12)
+    eng = _engine(prefix=False, max_running=1)  # one running request: the copies wait and prefill alone
+    rids = eng.add_group(p, SamplingParams(max_new_tokens=3), n=3)
+    while eng.has_work():
+        eng.step()
+    outs = [eng.result(r).output_ids for r in rids]
+    assert outs[0] == outs[1] == outs[2] and eng.metrics.snapshot()["prefill_tokens"] == 3 * len(p)
+    eng2 = _engine(prefix=False, max_running=4)
+    rids = eng2.add_group(p, SamplingParams(max_new_tokens=6, temperature=1.0), n=4)
+    while eng2.has_work():
+        eng2.step()
+    assert all(len(eng2.result(r).output_ids) == 6 for r in rids)
+    # aborting a leader before its prefill hands its copies to ordinary prefill
+    eng3 = _engine(prefix=False, max_running=4)
+    rids = eng3.add_group(p, SamplingParams(max_new_tokens=2), n=2)
+    assert eng3.abort(rids[0])
+    while eng3.has_work():
+        eng3.step()
+    assert len(eng3.result(rids[1]).output_ids) == 2

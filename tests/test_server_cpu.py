@@ -202,3 +202,14 @@ def test_latency_histograms_on_metrics(served):
     text = client.get("/metrics").text
     for name in ("time_to_first_token_seconds", "e2e_request_latency_seconds", "time_per_output_token_seconds"):
         assert f'packmla_{name}_bucket{{le="+Inf"}}' in text and f"packmla_{name}_count" in text
+
+
+def test_n_choices_share_one_prefill(served):
+    client, eng, tok, cfg = served
+    before = eng.metrics.snapshot().get("prefill_tokens", 0)
+    body = {"model": "tiny", "prompt": "one prefill for three choices", "max_tokens": 4, "n": 3, "ignore_eos": True}
+    c = client.post("/v1/completions", json=body).json()
+    plen = c["usage"]["prompt_tokens"]
+    assert len(c["choices"]) == 3 and len({ch["text"] for ch in c["choices"]}) == 1  # greedy copies agree
+    assert eng.metrics.snapshot()["prefill_tokens"] - before == plen
+    assert c["usage"]["prompt_tokens_details"]["cached_tokens"] == 2 * plen
