@@ -155,6 +155,29 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         except RuntimeError as exc:
             raise HTTPException(503, str(exc)) from exc
 
+    async def _merge(streams, body: dict):
+        """Events of several streams as they arrive: ("tok", index, token) and, once per stream after its
+        last token, ("end", index, None).  Leaving early cancels the readers, whose requests are aborted."""
+        q: asyncio.Queue = asyncio.Queue()
+
+        async def pump(i, st):
+            try:
+                async for item in _tokens(st, _StopRule(body, tokenizer)):
+                    q.put_nowait(("tok", i, item))
+            finally:
+                q.put_nowait(("end", i, None))
+
+        tasks = [asyncio.create_task(pump(i, st)) for i, st in enumerate(streams)]
+        ended = 0
+        try:
+            while ended < len(streams):
+                ev = await q.get()
+                ended += ev[0] == "end"
+                yield ev
+        finally:
+            for t in tasks:
+                t.cancel()
+
     async def _tokens(st, rule: _StopRule | None):
         """Tokens of one request as they arrive; a stop rule that fires aborts the request early, and so
         does a consumer that goes away first (a client that disconnected, a cancelled handler)."""
@@ -191,8 +214,6 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         n = body.get("n", 1)
         if not isinstance(n, int) or not 1 <= n <= 16:
             raise HTTPException(400, "n must be an integer in [1, 16]")
-        if n > 1 and body.get("stream"):
-            raise HTTPException(400, "streaming supports n = 1")
         return n
 
     def _usage(prompt_tokens: int, completion_tokens: int, cached_tokens: int = 0) -> dict:
@@ -231,20 +252,23 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         if body.get("stream"):
             if len(prompts) != 1:
                 raise HTTPException(400, "streaming supports one prompt")
-            st = await _submit(prompts[0], params)
-            rule = _StopRule(body, tokenizer)
+            streams = await _submit_group(prompts[0], params, n_choices)
 
             async def gen():
-                n = 0
-                async for item in _tokens(st, rule):
-                    n += 1
+                n, ended = 0, 0
+                async for kind, i, item in _merge(streams, body):
+                    if kind == "tok":
+                        n += 1
+                        yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                                    "choices": [{"index": i, "text": tokenizer.decode([item]), "token_ids": [item],
+                                                 "logprobs": None, "finish_reason": None}]})
+                        continue
+                    ended += 1
+                    last = {"usage": _usage(len(prompts[0]), n, sum(st.cached_tokens for st in streams))} \
+                        if ended == len(streams) else {}
                     yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
-                                "choices": [{"index": 0, "text": tokenizer.decode([item]), "token_ids": [item],
-                                             "logprobs": None, "finish_reason": None}]})
-                yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
-                            "choices": [{"index": 0, "text": "", "logprobs": None,
-                                         "finish_reason": st.finish_reason}],
-                            "usage": _usage(st.prompt_len, n, st.cached_tokens)})
+                                "choices": [{"index": i, "text": "", "logprobs": None,
+                                             "finish_reason": streams[i].finish_reason}], **last})
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")
@@ -274,22 +298,27 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         rid = f"chatcmpl-{uuid.uuid4().hex}"
         created = int(time.time())
         if body.get("stream"):
-            st = await _submit(ids, params)
-            rule = _StopRule(body, tokenizer)
+            streams = await _submit_group(ids, params, n_choices)
 
             async def gen():
-                yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
-                            "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]})
-                n = 0
-                async for item in _tokens(st, rule):
-                    n += 1
-                    yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
-                                "model": model_name,
-                                "choices": [{"index": 0, "delta": {"content": tokenizer.decode([item])},
-                                             "finish_reason": None}]})
-                yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
-                            "choices": [{"index": 0, "delta": {}, "finish_reason": st.finish_reason}],
-                            "usage": _usage(len(ids), n, st.cached_tokens)})
+                for i in range(len(streams)):
+                    yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                                "choices": [{"index": i, "delta": {"role": "assistant"}, "finish_reason": None}]})
+                n, ended = 0, 0
+                async for kind, i, item in _merge(streams, body):
+                    if kind == "tok":
+                        n += 1
+                        yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
+                                    "model": model_name,
+                                    "choices": [{"index": i, "delta": {"content": tokenizer.decode([item])},
+                                                 "finish_reason": None}]})
+                        continue
+                    ended += 1
+                    last = {"usage": _usage(len(ids), n, sum(st.cached_tokens for st in streams))} \
+                        if ended == len(streams) else {}
+                    yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                                "choices": [{"index": i, "delta": {}, "finish_reason": streams[i].finish_reason}],
+                                **last})
                 yield b"data: [DONE]\n\n"
 
             return StreamingResponse(gen(), media_type="text/event-stream")

@@ -147,7 +147,7 @@ def test_stop_strings_stop_tokens_and_n(served):
                                                   "n": 3, "ignore_eos": True}).json()
     assert [ch["index"] for ch in c["choices"]] == [0, 1, 2] and c["usage"]["completion_tokens"] == 6
     assert len({ch["message"]["content"] for ch in c["choices"]}) == 1
-    assert client.post("/v1/completions", json={"prompt": "x", "n": 2, "stream": True}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": "x", "n": 17}).status_code == 400
     assert client.post("/v1/completions", json={"prompt": "x", "stop": [3]}).status_code == 400
 
 
@@ -213,3 +213,28 @@ def test_n_choices_share_one_prefill(served):
     assert len(c["choices"]) == 3 and len({ch["text"] for ch in c["choices"]}) == 1  # greedy copies agree
     assert eng.metrics.snapshot()["prefill_tokens"] - before == plen
     assert c["usage"]["prompt_tokens_details"]["cached_tokens"] == 2 * plen
+
+
+def test_streaming_with_n_choices(served):
+    client, eng, tok, cfg = served
+    for path, body in (("/v1/completions", {"prompt": "stream three", "max_tokens": 3, "ignore_eos": True}),
+                       ("/v1/chat/completions", {"messages": [{"role": "user", "content": "stream three"}],
+                                                 "max_tokens": 3, "ignore_eos": True})):
+        r = client.post(path, json={"model": "tiny", "n": 3, "stream": True, **body})
+        assert r.status_code == 200
+        chunks = [json.loads(line[6:]) for line in r.text.splitlines()
+                  if line.startswith("data: {")]
+        assert r.text.rstrip().endswith("data: [DONE]")
+        per = {i: [] for i in range(3)}
+        finished = {}
+        for c in chunks:
+            ch = c["choices"][0]
+            piece = ch.get("text") if "text" in ch else ch.get("delta", {}).get("content")
+            if piece:
+                per[ch["index"]].append(piece)
+            if ch.get("finish_reason"):
+                finished[ch["index"]] = ch["finish_reason"]
+        assert finished == {0: "length", 1: "length", 2: "length"}
+        assert all(len(v) == 3 for v in per.values()) and per[0] == per[1] == per[2]  # greedy copies
+        usage = [c["usage"] for c in chunks if c.get("usage")]
+        assert len(usage) == 1 and usage[0]["completion_tokens"] == 9
