@@ -30,7 +30,9 @@ SETTINGS = {"none": {"radix": False, "hicache": False}, "hicache": {"radix": Fal
 def _metric(url: str, name: str) -> float:
     import requests
 
-    for line in requests.get(url + "/metrics", timeout=30).text.splitlines():
+    from .serving import auth_headers
+
+    for line in requests.get(url + "/metrics", timeout=30, headers=auth_headers()).text.splitlines():
         if line.startswith(f"packmla_{name} "):
             return float(line.split()[1])
     return 0.0

@@ -50,6 +50,8 @@ from pathlib import Path
 
 import numpy as np
 
+from .serving import auth_headers
+
 
 def load_sessions(path: str) -> list[list[dict]]:
     """JSONL -> sessions (lists of turns in turn order), sessions in first-appearance order."""
@@ -113,7 +115,7 @@ async def _replay(url: str, model: str, sessions: list[list[dict]], users: int,
     results: list[dict] = []
     started = [0]
     timeout = aiohttp.ClientTimeout(total=None, sock_read=3600)
-    async with aiohttp.ClientSession(timeout=timeout) as http:
+    async with aiohttp.ClientSession(timeout=timeout, headers=auth_headers()) as http:
         t0 = time.perf_counter()
 
         async def user():
@@ -134,7 +136,7 @@ def _metric(url: str, name: str) -> float:
     import requests
 
     try:
-        for line in requests.get(url + "/metrics", timeout=30).text.splitlines():
+        for line in requests.get(url + "/metrics", timeout=30, headers=auth_headers()).text.splitlines():
             if line.startswith(name + " "):
                 return float(line.split()[1])
     except requests.RequestException:
@@ -203,7 +205,7 @@ async def _request_slots(url: str, model: str, sessions: list[list[dict]], popul
         admit()
     active: dict = {}
     timeout = aiohttp.ClientTimeout(total=None, sock_read=3600)
-    async with aiohttp.ClientSession(timeout=timeout) as http:
+    async with aiohttp.ClientSession(timeout=timeout, headers=auth_headers()) as http:
         async def run_one(turns: deque, ready_s: float):
             rec = turns.popleft()
             dispatch = now()
@@ -306,7 +308,7 @@ def _idle_and_flush(url: str, timeout_s: float) -> None:
             raise RuntimeError("server did not become idle")
         time.sleep(0.2)
     try:
-        r = requests.post(url + "/flush_cache", timeout=60)
+        r = requests.post(url + "/flush_cache", timeout=60, headers=auth_headers())
     except requests.RequestException as exc:
         raise RuntimeError(f"flush failed: {exc!r}") from exc
     if r.status_code != 200:

@@ -87,7 +87,7 @@ async def run_phase(url: str, model: str, prompts: list[list[int]], output_len: 
 
     sem = asyncio.Semaphore(concurrency)
     timeout = aiohttp.ClientTimeout(total=None, sock_read=3600)
-    async with aiohttp.ClientSession(timeout=timeout) as session:
+    async with aiohttp.ClientSession(timeout=timeout, headers=auth_headers()) as session:
         async def one(p):
             async with sem:
                 return await _request(session, url, model, p, output_len)
@@ -134,16 +134,25 @@ def write_records(path: str, out: dict) -> None:
                                 "input_len": out["input_len"], "output_len": out["output_len"], **summary}) + "\n")
 
 
+def auth_headers() -> dict:
+    """`Authorization: Bearer ...` from PACKMLA_API_KEY (or OPENAI_API_KEY) for a server started with
+    --api-key; empty otherwise."""
+    import os
+
+    key = os.environ.get("PACKMLA_API_KEY") or os.environ.get("OPENAI_API_KEY")
+    return {"Authorization": f"Bearer {key}"} if key else {}
+
+
 def flush(url: str) -> None:
     import requests
 
-    requests.post(url + "/flush_cache", timeout=60).raise_for_status()
+    requests.post(url + "/flush_cache", timeout=60, headers=auth_headers()).raise_for_status()
 
 
 def server_info(url: str) -> dict:
     import requests
 
-    return requests.get(url + "/server_info", timeout=60).json()
+    return requests.get(url + "/server_info", timeout=60, headers=auth_headers()).json()
 
 
 def resolve_concurrency(requested, info: dict, input_len: int, output_len: int) -> int:

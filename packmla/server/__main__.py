@@ -24,6 +24,7 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--model", "--model-path", dest="model", default="tiny",
                     help="tiny | small | v4-flash | path to a packmla checkpoint")
     ap.add_argument("--served-model-name", default=None)
+    ap.add_argument("--api-key", default=None, help="require `Authorization: Bearer KEY` on every route but /health")
     ap.add_argument("--tokenizer", "--tokenizer-path", dest="tokenizer", default=None,
                     help="directory with Hugging Face tokenizer files (local only); default: byte-level tokenizer")
     ap.add_argument("--host", default="127.0.0.1")
@@ -229,7 +230,8 @@ def main(argv=None) -> None:
 
     from .app import create_app
 
-    app = create_app(driver, load_tokenizer(args.tokenizer, eng.cfg.vocab_size), name, {"server_args": vars(args)})
+    app = create_app(driver, load_tokenizer(args.tokenizer, eng.cfg.vocab_size), name,
+                     {"server_args": {k: v for k, v in vars(args).items() if k != "api_key"}}, api_key=args.api_key)
     driver.start()
     print(json.dumps({"event": "server_ready", "host": args.host, "port": args.port,
                       "max_total_num_tokens": eng.capacity.max_total_tokens}), flush=True)

@@ -108,8 +108,10 @@ def _sse(obj) -> bytes:
     return f"data: {json.dumps(obj)}\n\n".encode()
 
 
-def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, server_args: dict | None = None
-               ) -> FastAPI:
+def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, server_args: dict | None = None,
+               api_key: str | None = None) -> FastAPI:
+    """`api_key`: when set, every route but /health answers 401 unless the request carries
+    `Authorization: Bearer <api_key>` (SGLang's --api-key)."""
     eng = driver.engine
     vocab = eng.cfg.vocab_size
 
@@ -135,6 +137,17 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             task.cancel()
 
     app = FastAPI(title="packmla", lifespan=lifespan)
+
+    if api_key:
+        import hmac
+
+        @app.middleware("http")
+        async def require_key(request: Request, call_next):
+            if request.url.path != "/health":
+                given = request.headers.get("authorization", "")
+                if not hmac.compare_digest(given.encode(), f"Bearer {api_key}".encode()):
+                    return JSONResponse({"error": "invalid or missing API key"}, status_code=401)
+            return await call_next(request)
 
     async def _submit(ids: list[int], params: SamplingParams):
         _check_ids(ids, vocab)

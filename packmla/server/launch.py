@@ -120,7 +120,9 @@ def wait_ready(url: str, group: ServerGroup, timeout_s: float) -> dict:
             raise RuntimeError(f"server exited with code {group.proc.returncode} before it was healthy")
         try:
             if requests.get(url + "/health", timeout=5).status_code == 200:
-                return requests.get(url + "/server_info", timeout=30).json()
+                from ..bench.serving import auth_headers
+
+                return requests.get(url + "/server_info", timeout=30, headers=auth_headers()).json()
         except requests.RequestException:
             pass
         time.sleep(0.5)

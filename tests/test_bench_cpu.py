@@ -159,3 +159,15 @@ def test_latency_histograms_export_cumulative_buckets():
     text = m.prometheus()
     assert 'packmla_ttft_bucket{le="+Inf"} 5' in text and "packmla_ttft_count 5" in text
     assert "# TYPE packmla_ttft histogram" in text
+
+
+def test_clients_send_the_api_key_from_the_environment(monkeypatch):
+    from packmla.bench.serving import auth_headers
+
+    monkeypatch.delenv("OPENAI_API_KEY", raising=False)
+    monkeypatch.delenv("PACKMLA_API_KEY", raising=False)
+    assert auth_headers() == {}
+    monkeypatch.setenv("OPENAI_API_KEY", "k1")
+    assert auth_headers() == {"Authorization": "Bearer k1"}
+    monkeypatch.setenv("PACKMLA_API_KEY", "k2")
+    assert auth_headers() == {"Authorization": "Bearer k2"}

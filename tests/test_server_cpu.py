@@ -238,3 +238,22 @@ def test_streaming_with_n_choices(served):
         assert all(len(v) == 3 for v in per.values()) and per[0] == per[1] == per[2]  # greedy copies
         usage = [c["usage"] for c in chunks if c.get("usage")]
         assert len(usage) == 1 and usage[0]["completion_tokens"] == 9
+
+
+def test_api_key_guards_every_route_but_health():
+    from packmla.server.app import create_app
+
+    cfg = ModelConfig.tiny(num_layers=2)
+    eng = Engine.build(cfg, EngineConfig(device="cpu", max_running_requests=2, cuda_graph_bs=[1, 2]), "cpu",
+                       max_context=256)
+    driver = EngineDriver(eng).start()
+    try:
+        with TestClient(create_app(driver, ByteTokenizer(cfg.vocab_size), "tiny", api_key="s3cret")) as client:
+            assert client.get("/health").status_code == 200
+            body = {"model": "tiny", "prompt": "x", "max_tokens": 1}
+            assert client.post("/v1/completions", json=body).status_code == 401
+            assert client.get("/v1/models", headers={"Authorization": "Bearer wrong"}).status_code == 401
+            ok = client.post("/v1/completions", json=body, headers={"Authorization": "Bearer s3cret"})
+            assert ok.status_code == 200
+    finally:
+        driver.stop()
