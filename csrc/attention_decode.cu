@@ -158,11 +158,6 @@ __device__ __forceinline__ void fetch_step(const DecodeParams& p, const RowRef& 
   R.sc = make_uint2(0, 0);
 #pragma unroll
   for (int i = 0; i < 5; ++i) R.U[i] = zero4();
-  if (p.debug & 4) {  // timing experiment: expansion of an all-zero Packed row, no loads
-    R.kind = rr.kind ? 3 : 0;
-    R.sc = make_uint2(0x7f7f7f7fu, 0x7f7f7f7fu);
-    return;
-  }
   if (rr.kind == 1 || rr.kind == 2) {
     const uint8_t* pool = rr.kind == 1 ? p.swa_pool : p.csa_pool;
     const int64_t page = rr.slot / kPage, rip = rr.slot % kPage;
@@ -418,8 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
       }
     };
     auto expand = [&](const StepRegs& R, int k) {
-      if (!(p.debug & 2)) expand_step(R, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
-      else if (v8 == 0) rowvalid[step_row(k)] = R.kind != 0;
+      expand_step(R, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
     };
     expand(ra, 0);
     expand(rb, 1);
@@ -437,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     // ---- 2. S^T = K Q^T
     if (tid == 0) {
 #pragma unroll 1
-      for (int k = 0; k < kD / 16 && !(p.debug & 1); ++k) {
+      for (int k = 0; k < kD / 16; ++k) {
         const uint32_t koff = (k * 32) & 127;
         const uint64_t ad = pm::make_sdesc(kv_base + (k >> 2) * (kTile * 128) + koff, 16, 1024);
         const uint64_t bd = pm::make_sdesc(q_base + (k >> 2) * (kHG * 128) + koff, 16, 1024);
@@ -542,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     // ---- 4. O^T += V^T P^T
     if (tid == 0 && !flags[1]) {
 #pragma unroll 1
-      for (int db = 0; db < 4 && !(p.debug & 1); ++db) {
+      for (int db = 0; db < 4; ++db) {
 #pragma unroll 1
         for (int k = 0; k < trows / 16; ++k) {
           const uint64_t ad = pm::make_sdesc(kv_base + (2 * db) * (kTile * 128) + k * 2048, kTile * 128, 1024);

@@ -41,8 +41,6 @@ struct DecodeParams {
   float* part_o;             // [B, splits, H, 512]
   float* part_ml;            // [B, splits, H, 2]
   int* err;
-  int debug;                 // diagnostics only: bit0 skips the MMAs, bit1 skips row expansion, bit2 expands
-                             // all-zero Packed rows without loading records
   unsigned long long* prof;  // optional phase counters (ns, summed over CTAs), see attention_decode.cu
   int tile_rows;             // KV rows per tile: 128 (default, also for 0) or 64
 };
@@ -60,11 +58,6 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
 void launch_moe_route(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
                       int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
                       cudaStream_t stream);
-void launch_moe_fp4_tc(const __nv_bfloat16* x, int T, int H, int I, int E, int max_slots, const int32_t* offsets,
-                       const int32_t* pad, const int32_t* slot_token, const float* slot_weight, const int32_t* active,
-                       const uint8_t* w13t, const uint8_t* s13t, const uint8_t* w2t, const uint8_t* s2t, __half* xs,
-                       __half* act_s, float* out, int num_sms, int* err, int debug, cudaStream_t stream);
-
 void launch_index_key_store(const float* kraw, int64_t stride, const int64_t* slots, uint8_t* keys, float* kscales,
                             int64_t nrows, int R, int* err, cudaStream_t stream);
 void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, const uint8_t* keys,
@@ -73,9 +66,6 @@ void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, c
                          cudaStream_t stream);
 void launch_index_topk(const float* scores, int64_t stride, int B, int R, int k, const int32_t* phys,
                        int64_t phys_stride, int ratio, int32_t* out_slots, int32_t* out_pos, cudaStream_t stream);
-
-void launch_tc_latency_probe(int iters, int n_mma, int n, int n_acc, int kind, long long* out, int* err,
-                             cudaStream_t stream);
 
 void launch_moe_gather_slots(const __nv_bfloat16* x, int K, const int32_t* offsets, const int32_t* pad,
                              const int32_t* slot_token, int E, __half* xs, int num_sms, cudaStream_t stream);
@@ -138,7 +128,6 @@ struct MoeMxArgs {
   // waiting for an accumulator, [4] producer lifetime, [5] MMA issuer waiting for weight scales,
   // [6] MMA issuer issuing (fence + MMAs + commit); gate/up at [0..7], down at [8..15]
   unsigned long long* prof;
-  int debug;  // timing experiments only (PACKMLA_KERNEL_DEBUG), results invalid when set
 };
 int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream);
 

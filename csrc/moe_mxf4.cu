@@ -77,7 +77,6 @@ struct MxParams {
   float* out;                            // mode 1: [T, H]
   int* err;
   unsigned long long* prof;              // optional wait-time counters (ns), see launch_moe_mxf4
-  int debug;                             // timing experiments only (results invalid): 4 = no MMAs
 };
 
 // Bounded wait that adds the SM cycles it spent to *acc (when profiling).
@@ -279,7 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_con
           const uint32_t sf_col = tmem + kColSf + 16 * st;
 #pragma unroll
           for (int s = 0; s < 4; ++s) {
-            if (p.debug & 4) break;
             const uint32_t idesc = pm::make_idesc_mxf8(128, 256, 0, 5, s, s);
             pm::umma_mxf8(tmem + kColD, pm::make_sdesc(sb + 32 * s, 16, 1024),
                           pm::make_sdesc(sb + kOffW + 32 * s, 16, 1024), idesc, sf_col, sf_col + 8, (g | s) ? 1u : 0u);
@@ -473,11 +471,10 @@ int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream) {
        reinterpret_cast<uintptr_t>(a.chunks) | reinterpret_cast<uintptr_t>(a.out)) & 15)
     return -3;
   MxParams p0{a.H, a.H / 128, a.I / 128, 2 * a.I, a.rows_total, a.I, a.E * 2 * a.I, a.sfw13, a.xq, a.xs, a.chunks, a.n_chunks,
-              a.act_q, a.act_s, a.slot_token, a.slot_weight, a.out, a.err, a.prof, a.debug};
+              a.act_q, a.act_s, a.slot_token, a.slot_weight, a.out, a.err, a.prof};
   mx_expert_kernel<0><<<a.num_sms, kThreads, kSmemBytes, stream>>>(m13, p0);
   MxParams p1{a.I, a.I / 128, a.H / 256, a.H, a.rows_total, a.H, a.E * a.H, a.sfw2, a.act_q, a.act_s, a.chunks, a.n_chunks,
-              nullptr, nullptr, a.slot_token, a.slot_weight, a.out, a.err, a.prof ? a.prof + 8 : nullptr,
-              a.debug};
+              nullptr, nullptr, a.slot_token, a.slot_weight, a.out, a.err, a.prof ? a.prof + 8 : nullptr};
   mx_expert_kernel<1><<<a.num_sms, kThreads, kSmemBytes, stream>>>(m2, p1);
   return 0;
 }

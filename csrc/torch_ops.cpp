@@ -22,11 +22,6 @@ void check_err(const torch::Tensor& err) {
   TORCH_CHECK(err.is_cuda() && err.scalar_type() == torch::kInt32 && err.numel() >= 4, "err must be CUDA int32[4]");
 }
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
-// Diagnostic ablation switch read from PACKMLA_KERNEL_DEBUG (0 in normal operation).
-int debug_flags() {
-  const char* v = std::getenv("PACKMLA_KERNEL_DEBUG");
-  return v ? std::atoi(v) : 0;
-}
 }  // namespace
 
 void native_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, torch::Tensor positions,
@@ -136,7 +131,6 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.part_o = part_o.data_ptr<float>();
   p.part_ml = part_ml.data_ptr<float>();
   p.err = err.data_ptr<int>();
-  p.debug = debug_flags();
   p.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
   p.tile_rows = (int)tile_rows;
   launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
@@ -212,69 +206,6 @@ int num_sms_of(const torch::Device& d) {
   const int idx = d.index() < 0 ? 0 : d.index();
   if (cache[idx] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&cache[idx], cudaDevAttrMultiProcessorCount, idx));
   return cache[idx];
-}
-
-// Tiled MXFP4 experts (packmla/ops/moe.py tile_experts): w13t [E, I/64, H/256, 128, 128],
-// s13t [E, I/64, H/256, 128, 8], w2t [E, H/128, I/256, 128, 128], s2t [E, H/128, I/256, 128, 8].
-void moe_fp4_tc(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int64_t expert_base,
-                torch::Tensor w13t, torch::Tensor s13t, torch::Tensor w2t, torch::Tensor s2t, torch::Tensor offsets,
-                torch::Tensor slot_token, torch::Tensor slot_weight, torch::Tensor active, torch::Tensor pad,
-                torch::Tensor xs, torch::Tensor act_s, torch::Tensor out, torch::Tensor err) {
-  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.dim() == 2 && h.is_contiguous());
-  check_err(err);
-  const int T = h.size(0), H = h.size(1);
-  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.dim() == 2 && topk_ids.size(0) == T && topk_ids.is_contiguous());
-  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.sizes() == topk_ids.sizes() && topk_w.is_contiguous());
-  const int k = topk_ids.size(1);
-  TORCH_CHECK(w13t.scalar_type() == torch::kUInt8 && w13t.dim() == 5 && w13t.size(3) == 128 && w13t.size(4) == 128 &&
-              w13t.is_contiguous());
-  const int E = w13t.size(0), I = w13t.size(1) * 64;
-  TORCH_CHECK(w13t.size(2) * 256 == H, "w13t k-tiles do not match hidden size");
-  TORCH_CHECK(s13t.scalar_type() == torch::kUInt8 && s13t.dim() == 5 && s13t.size(0) == E && s13t.size(1) == I / 64 &&
-              s13t.size(2) == H / 256 && s13t.size(3) == 128 && s13t.size(4) == 8 && s13t.is_contiguous());
-  TORCH_CHECK(w2t.scalar_type() == torch::kUInt8 && w2t.dim() == 5 && w2t.size(0) == E && w2t.size(1) * 128 == H &&
-              w2t.size(2) * 256 == I && w2t.size(3) == 128 && w2t.size(4) == 128 && w2t.is_contiguous());
-  TORCH_CHECK(s2t.scalar_type() == torch::kUInt8 && s2t.dim() == 5 && s2t.size(0) == E && s2t.size(1) * 128 == H &&
-              s2t.size(2) * 256 == I && s2t.size(3) == 128 && s2t.size(4) == 8 && s2t.is_contiguous());
-  TORCH_CHECK(H % 256 == 0 && I % 256 == 0 && H % 128 == 0, "hidden and intermediate must be multiples of 256");
-  TORCH_CHECK(E <= 4096, "too many local experts");
-  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() >= E + 1);
-  TORCH_CHECK(active.scalar_type() == torch::kInt32 && active.numel() >= E + 1);
-  TORCH_CHECK(slot_token.scalar_type() == torch::kInt32 && slot_token.numel() >= (int64_t)T * k);
-  TORCH_CHECK(slot_weight.scalar_type() == torch::kFloat32 && slot_weight.numel() >= (int64_t)T * k);
-  TORCH_CHECK(pad.scalar_type() == torch::kInt32 && pad.numel() >= E + 1);
-  const int64_t prow = (int64_t)T * k + 16 * (int64_t)E;  // padded rows upper bound
-  TORCH_CHECK(xs.scalar_type() == torch::kFloat16 && xs.is_contiguous() && xs.numel() >= prow * H);
-  TORCH_CHECK(act_s.scalar_type() == torch::kFloat16 && act_s.is_contiguous() && act_s.numel() >= prow * I);
-  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == (int64_t)T * H);
-  const c10::cuda::CUDAGuard g(h.device());
-  launch_moe_route(topk_ids.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, k, (int)expert_base, E,
-                   offsets.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(), slot_weight.data_ptr<float>(),
-                   active.data_ptr<int32_t>(), pad.data_ptr<int32_t>(), stream());
-  launch_moe_fp4_tc(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), T, H, I, E, T * k,
-                    offsets.data_ptr<int32_t>(), pad.data_ptr<int32_t>(), slot_token.data_ptr<int32_t>(),
-                    slot_weight.data_ptr<float>(),
-                    active.data_ptr<int32_t>(), w13t.data_ptr<uint8_t>(), s13t.data_ptr<uint8_t>(),
-                    w2t.data_ptr<uint8_t>(), s2t.data_ptr<uint8_t>(), reinterpret_cast<__half*>(xs.data_ptr()),
-                    reinterpret_cast<__half*>(act_s.data_ptr()), out.data_ptr<float>(), num_sms_of(h.device()),
-                    err.data_ptr<int>(), debug_flags(), stream());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-// Returns (cycles per iteration, cycles spent issuing per iteration).
-std::vector<int64_t> tc_latency_probe(int64_t iters, int64_t n_mma, int64_t n, int64_t n_acc, torch::Tensor err,
-                                      int64_t kind) {
-  check_err(err);
-  TORCH_CHECK(n_acc >= 1, "n_acc >= 1");
-  const c10::cuda::CUDAGuard g(err.device());
-  auto out = torch::zeros({2}, err.options().dtype(torch::kInt64));
-  TORCH_CHECK(kind >= 0 && kind <= 5 && n_acc * n <= 448 && n % 8 == 0 && n >= 8 && n <= 256);
-  launch_tc_latency_probe((int)iters, (int)n_mma, (int)n, (int)n_acc, (int)kind,
-                          reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
-                          err.data_ptr<int>(), stream());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  auto h = out.cpu();
-  return {h[0].item<int64_t>(), h[1].item<int64_t>()};
 }
 
 void index_key_store(torch::Tensor kraw, torch::Tensor slots, torch::Tensor keys, torch::Tensor kscales,
@@ -541,7 +472,6 @@ void moe_mxf4(torch::Tensor h, torch::Tensor topk_ids, torch::Tensor topk_w, int
   a.act_q = act_q.data_ptr<uint8_t>(); a.act_s = act_s.data_ptr<uint8_t>();
   a.out = out.data_ptr<float>(); a.err = err.data_ptr<int>();
   a.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
-  a.debug = debug_flags();
   const int rc = launch_moe_mxf4(a, stream());
   TORCH_CHECK(rc == 0, "moe_mxf4 launch failed: ", rc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -707,8 +637,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
   m.def("packed_store", &packed_store, "FP32 rows -> Packed 328 B C4 records (planes)");
   m.def("umma_probe", &umma_probe, "tcgen05 operand-layout self-test (one MMA)");
-  m.def("tc_latency_probe", &tc_latency_probe, "tcgen05 MMA + commit round-trip latency (cycles)", py::arg("iters"),
-        py::arg("n_mma"), py::arg("n"), py::arg("n_acc"), py::arg("err"), py::arg("kind") = 0);
   m.def("index_key_store", &index_key_store, "FP8 index keys (swizzled rows) + fp32 scales");
   m.def("index_select", &index_select, "FP8 tcgen05 indexer logits + radix top-k");
   m.def("bs_probe2", &bs_probe2, "TMA FP4 + tcgen05.cp scale-factor pipeline self-test");
@@ -724,7 +652,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pad"), py::arg("chunks"), py::arg("n_chunks"), py::arg("xq"), py::arg("xs"), py::arg("act_q"),
         py::arg("act_s"), py::arg("out"), py::arg("err"), py::arg("prof") = py::none());
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
-  m.def("moe_fp4_tc", &moe_fp4_tc, "MXFP4 routed experts on tcgen05 (tiled weights, A operand in TMEM)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
   m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine", py::arg("q"),
         py::arg("swa_pool"), py::arg("swa_slots"), py::arg("swa_len"), py::arg("csa_packed"), py::arg("csa_pool"),

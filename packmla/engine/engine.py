@@ -253,10 +253,12 @@ class Engine:
         for f in self.forks.pop(leader.rid, []):
             need = n + f.params.max_new_tokens
             pages = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
-            while (not self.pool._free_slots or pages > self.pool.pages.free) and self._evict_retained():
+            c128 = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
+            while ((not self.pool._free_slots or pages > self.pool.pages.free or c128 > self.pool.c128_pages.free)
+                   and self._evict_retained()):
                 pass
             if (len(self.running) + 1 >= self.runner.max_b or not self.pool._free_slots
-                    or pages > self.pool.pages.free):
+                    or pages > self.pool.pages.free or c128 > self.pool.c128_pages.free):
                 self.waiting.append(f)  # no room now: an ordinary prefill later
                 continue
             f.slot = self.pool.admit(need)
@@ -377,7 +379,8 @@ class Engine:
             while ((not self.pool._free_slots or pages_needed > self.pool.pages.free
                     or c128_needed > self.pool.c128_pages.free) and self._evict_retained()):
                 pass
-            if not self.pool._free_slots or pages_needed > self.pool.pages.free:
+            if (not self.pool._free_slots or pages_needed > self.pool.pages.free
+                    or c128_needed > self.pool.c128_pages.free):
                 return None
             req.slot = self.pool.admit(need)
             if self.hicache is not None:

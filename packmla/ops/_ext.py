@@ -12,7 +12,7 @@ _ERR: dict[int, torch.Tensor] = {}
 
 
 # kernels launched per extension entry point (for the bench's launch count)
-KERNELS_PER_CALL = {"native_store": 1, "packed_store": 1, "sparse_mla_decode": 2, "moe_fp4": 3, "moe_fp4_tc": 4, "moe_fp4_mma": 4, "add_rmsnorm": 1, "bs_probe": 1, "moe_mxf4": 4, "bs_probe2": 1, "rope_q": 1, "comp_pool": 1, "route_topk": 1, "silu_mul": 1, "index_key_store": 1, "index_select": 2, "tc_latency_probe": 1, "umma_probe": 1, "gemm_allreduce": 1, "allreduce": 1}
+KERNELS_PER_CALL = {"native_store": 1, "packed_store": 1, "sparse_mla_decode": 2, "moe_fp4": 3, "moe_fp4_mma": 4, "add_rmsnorm": 1, "bs_probe": 1, "moe_mxf4": 4, "bs_probe2": 1, "rope_q": 1, "comp_pool": 1, "route_topk": 1, "silu_mul": 1, "index_key_store": 1, "index_select": 2, "umma_probe": 1, "gemm_allreduce": 1, "allreduce": 1}
 
 
 class _Counting:

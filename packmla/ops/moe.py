@@ -10,7 +10,7 @@ all-reduce combines ranks (the MoE down-projection partial sums).
 * MXFP4 experts on CUDA: routing lists (csrc/moe_fp4.cu), then csrc/moe_fp4_mma.cu: bulk-copy
   weight stream dequantized straight into register MMA fragments, gate/up with SiLU, down with the
   routed-weight scatter-add; weights use the fragment-ordered layout made once by
-  `prepare_experts`.  csrc/moe_fp4_tc.cu (tcgen05, weight operand in TMEM) uses `tile_fp4`.
+  `prepare_experts`.
 * BF16 experts (tiny CPU configs, tests): PyTorch reference.
 """
 from __future__ import annotations
@@ -59,32 +59,6 @@ def fp4_dequant(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     return vals * scale
 
 
-def tile_fp4(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torch.Tensor, torch.Tensor]:
-    """Canonical MXFP4 [E, R, K/2] + scales [E, R, K/32] -> kernel tiles of 128 rows x 256 k.
-
-    Returns w_t [E, R/128, K/256, 128, 128] with each row's 16-byte units XOR-swizzled by
-    (row % 8), and s_t [E, R/128, K/256, 128, 8].  For gate/up (R = 2I), row tile j holds gate
-    rows [64 j, 64 j + 64) followed by up rows [I + 64 j, I + 64 j + 64).
-    """
-    E, R, Kh = w.shape
-    K = Kh * 2
-    if gate_up:
-        I = R // 2
-        w = torch.cat((w[:, :I].reshape(E, I // 64, 64, Kh), w[:, I:].reshape(E, I // 64, 64, Kh)), 2)
-        s = torch.cat((s[:, :I].reshape(E, I // 64, 64, K // 32), s[:, I:].reshape(E, I // 64, 64, K // 32)), 2)
-    else:
-        w = w.reshape(E, R // 128, 128, Kh)
-        s = s.reshape(E, R // 128, 128, K // 32)
-    nrt = w.shape[1]
-    w = w.reshape(E, nrt, 128, K // 256, 8, 16).permute(0, 1, 3, 2, 4, 5)  # [E, nrt, kt, row, unit, 16]
-    rows = torch.arange(128, device=w.device)
-    units = torch.arange(8, device=w.device)
-    src = (units[None, :] ^ (rows[:, None] % 8))[None, None, None, :, :, None].expand(E, nrt, K // 256, 128, 8, 16)
-    w_t = torch.gather(w, 4, src).reshape(E, nrt, K // 256, 128, 128).contiguous()
-    s_t = s.reshape(E, nrt, 128, K // 256, 8).permute(0, 1, 3, 2, 4).contiguous()
-    return w_t, s_t
-
-
 _FRAG_INDEX: dict = {}
 
 
@@ -108,7 +82,9 @@ def _frag_index(device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch
 def tile_fp4_frag(w: torch.Tensor, s: torch.Tensor, gate_up: bool) -> tuple[torch.Tensor, torch.Tensor]:
     """Canonical MXFP4 [E, R, K/2] + scales [E, R, K/32] -> register-fragment tiles (csrc/moe_fp4_mma.cu).
 
-    Returns w_f [E, R/128, K/256, 16384] and s_f [E, R/128, K/256, 1024]; row tiles as tile_fp4.
+    Returns w_f [E, R/128, K/256, 16384] and s_f [E, R/128, K/256, 1024].  Row tile j of gate/up (R = 2I)
+    holds gate rows [64 j, 64 j + 64) followed by up rows [I + 64 j, I + 64 j + 64); the down projection's
+    row tiles are 128 consecutive rows.
     """
     E, R, Kh = w.shape
     K = Kh * 2

@@ -229,6 +229,13 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             raise HTTPException(400, "n must be an integer in [1, 16]")
         return n
 
+    def _cached(streams: list, n_choices: int) -> int:
+        """Prompt tokens served from a cache, counted once per prompt.
+
+        The streams of one prompt are its leader followed by its n - 1 forks; the forks copy the leader's
+        prefilled KV, which is not a cache hit of the prompt, so only the leaders' counts are summed."""
+        return sum(st.cached_tokens for st in streams[::max(1, n_choices)])
+
     def _usage(prompt_tokens: int, completion_tokens: int, cached_tokens: int = 0) -> dict:
         return {"prompt_tokens": prompt_tokens, "completion_tokens": completion_tokens,
                 "total_tokens": prompt_tokens + completion_tokens,
@@ -277,7 +284,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                                                  "logprobs": None, "finish_reason": None}]})
                         continue
                     ended += 1
-                    last = {"usage": _usage(len(prompts[0]), n, sum(st.cached_tokens for st in streams))} \
+                    last = {"usage": _usage(len(prompts[0]), n, _cached(streams, n_choices))} \
                         if ended == len(streams) else {}
                     yield _sse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
                                 "choices": [{"index": i, "text": "", "logprobs": None,
@@ -296,7 +303,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": choices,
-                "usage": _usage(sum(len(p) for p in prompts), ntok, sum(st.cached_tokens for st in streams))}
+                "usage": _usage(sum(len(p) for p in prompts), ntok, _cached(streams, n_choices))}
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
@@ -327,7 +334,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                                                  "finish_reason": None}]})
                         continue
                     ended += 1
-                    last = {"usage": _usage(len(ids), n, sum(st.cached_tokens for st in streams))} \
+                    last = {"usage": _usage(len(ids), n, _cached(streams, n_choices))} \
                         if ended == len(streams) else {}
                     yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                                 "choices": [{"index": i, "delta": {}, "finish_reason": streams[i].finish_reason}],
@@ -344,7 +351,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             choices.append({"index": i, "message": {"role": "assistant", "content": _text(toks, rule)},
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": choices, "usage": _usage(len(ids), ntok, sum(st.cached_tokens for st in streams))}
+                "choices": choices, "usage": _usage(len(ids), ntok, _cached(streams, n_choices))}
 
     @app.post("/generate")
     async def generate(req: Request):

@@ -54,13 +54,3 @@ def test_index_select_matches_oracle(cuda, B, H, R, topk, pages):
         rec = p[b][: n_valid] // 4
         assert torch.all(rec[1:] > rec[:-1])
         assert torch.equal(s[b][:n_valid], phys[b][rec.long()])
-
-
-def test_tcgen05_handshake_latency_probe(cuda):
-    err = torch.zeros(4, dtype=torch.int32, device=cuda)
-    lat = {}
-    for n_mma, n, acc in ((0, 64, 1), (1, 16, 1), (16, 16, 1), (16, 16, 4), (16, 16, 8), (16, 64, 1), (16, 64, 4),
-                          (16, 256, 1), (32, 64, 1)):
-        lat[(n_mma, n, acc)] = ext().tc_latency_probe(200, n_mma, n, acc, err)[0]
-    assert err.cpu()[0] == 0
-    print("tcgen05 cycles per (n_mma, N, accumulators) round trip:", lat)

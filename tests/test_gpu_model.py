@@ -124,23 +124,3 @@ def test_moe_fp4_full_width_shapes(cuda):
     out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), {k: v.cuda() for k, v in lw.items()}, 0, 4, "mxfp4")
     check_errors(cuda)
     assert _rel(out.cpu(), ref) < 2e-2
-
-
-def test_moe_fp4_tcgen05_kernel_matches_reference(cuda):
-    """The tcgen05 (TMEM weight operand) expert kernel on its own tiled layout."""
-    from packmla.ops import ext, error_word
-
-    cfg = small_gpu_config(hidden_size=4096, moe_intermediate=2048, n_routed_experts=4, moe_topk=2)
-    W = init_weights(cfg, device="cpu", seed=12)
-    lw = W["layers"][0]
-    h = torch.randn(7, 4096, generator=torch.Generator().manual_seed(3)).bfloat16()
-    ids, w = moe_ops.route(h, lw["gate"], lw["gate_bias"], 2, 1.0)
-    ref = moe_ops.experts(h, ids, w, lw, 0, 4, "mxfp4", precision="bf16")
-    w13t, s13t = moe_ops.tile_fp4(lw["w13"], lw["s13"], True)
-    w2t, s2t = moe_ops.tile_fp4(lw["w2"], lw["s2"], False)
-    ws = moe_ops.MoEWorkspace(7, 2, 4, 2048, cuda, hidden=4096)
-    out = torch.zeros(7, 4096, device=cuda)
-    ext().moe_fp4_tc(h.cuda(), ids.cuda(), w.cuda(), 0, w13t.cuda(), s13t.cuda(), w2t.cuda(), s2t.cuda(), ws.offsets,
-                     ws.slot_token, ws.slot_weight, ws.active, ws.pad, ws.xs, ws.act, out, error_word(cuda))
-    check_errors(cuda)
-    assert _rel(out.cpu(), ref) < 2e-2
