@@ -1,37 +1,45 @@
 // Sparse MLA decode attention on tcgen05 (Native and Direct-Packed KV), plus split combine.
 //
 // Reference behaviour: FlashMLA sparse FP8 decode, Native <1,64,0> and Direct Packed <1,64,1>
-// (third_party/README.md:355-361) and `flash_fwd_mla_combine_kernel`.  Semantics:
-// joint softmax over [SWA rows ; selected C4 rows] with a per-head sink, K = V = latent row,
-// output tail inverse-rotated with the query position (training/losses.py:121-126).
+// (third_party/README.md:355-361) and `flash_fwd_mla_combine_kernel`.  Semantics: joint softmax over
+// [SWA rows ; selected C4 rows] with a per-head sink, K = V = latent row, output tail inverse-rotated
+// with the query position (training/losses.py:121-126).
 //
-// Design (sm_100a): one CTA = (query b, group of 64 heads, KV split).  Per tile of 128 KV rows:
-//   1. 8 warps gather the rows (Native 584 B or Packed 328 B) and expand them into a dense BF16
-//      tile [128 x 512] in shared memory, 128-byte swizzled (Packed: bitmap POPC prefix,
-//      E4M3 x UE8M0 dequant, BF16 round, tail RoPE with the record position).  A warp takes 4 rows
-//      per step with 8 lanes per row: the lanes copy the raw record (and a Packed row's RoPE
-//      table row) into the warp's staging, then each lane expands one 64-coordinate word (one
-//      UE8M0 scale tile) 8 coordinates at a time: the unit's kept bytes are placed with one byte
-//      permute from a mask-indexed table; the next step's record loads are in flight meanwhile.
-//      A query's rows are split over the CTAs of its splits in whole tiles, as evenly as possible.
-//   2. one thread issues S^T = K Q^T   (tcgen05.mma kind::f16, M=128 rows, N=64 heads, K=512)
-//      into TMEM columns [256, 320).
-//   3. 8 warps read S^T with tcgen05.ld, do the online softmax per head (column reductions by
-//      shuffles), write P^T (BF16) to shared memory; O^T is rescaled in TMEM only when a head's
-//      running max grows by more than 2^8 (exact: the final division uses the same reference max).
-//   4. one thread issues O^T += V^T P^T (four M=128 d-blocks, N=64, K=128) into TMEM [0, 256);
-//      V^T is the same shared tile read through an MN-major descriptor.
-// The partial (O unnormalized, m, l) per split goes to global memory; the combine kernel merges
-// splits, adds the sink, normalizes, inverse-rotates the tail and writes BF16 O and LSE.
+// Design (sm_100a).  One CTA = (query b, group of 64 heads, KV split); 256 threads:
+//   * all 8 warps gather and expand the KV rows into shared memory, 128-row tiles at a time, and run each
+//     tile's softmax; warp 0 owns TMEM and issues the MMAs from one elected lane of the converged warp.
+// Per tile (a 128-row, 128-byte-swizzled K-major FP16 buffer):
+//   S^T (128 rows x 64 heads, fp32) = K Q^T: tcgen05.mma kind::f16 M=128 N=64, 32 instructions over K = 512;
+//   softmax over the tile (one thread per row and 32 heads: 8 warps cover the four TMEM lane quadrants and
+//     both head halves), P^T in FP16 to shared memory;
+//   O^T (512 d x 64 heads, fp32, 256 TMEM columns) += V^T P^T: four d-blocks of M=128, K = 128 rows, V^T
+//     read through an MN-major descriptor of the same buffer.
+// The next tile's rows are resolved, prefetched into L2 and loaded into registers while the current tile's
+// softmax and P.V run, and the indices of the tile after it are loaded, so a tile's expansion starts with its
+// data at hand.  O^T is rescaled in TMEM only when a head's running max grows by more than 2^8 (exact: the
+// final division uses the same reference max).
+//
+// Expansion (8 lanes per row, four rows per lane and tile):
+//   Native 584 B rows: each lane loads the 16-byte units v, v + 8, v + 16, v + 24, v + 32 of the record
+//     and expands exactly those bytes (E4M3 x UE8M0 -> FP16, the BF16 tail -> FP16), so no staging.
+//   Packed 328 B rows: the values and bitmap are staged per row; lane v expands the 8-coordinate unit v of
+//     every 64-coordinate word (bitmap POPC prefix, one byte permute from a mask-indexed table, E4M3 x
+//     UE8M0), and the tail word is rounded to BF16, rotated with the record's RoPE row and rounded again.
+// FP16 operands: E4M3 x 2^e is exact in FP16 for e in [-15, 7], and the BF16 tail values are exact in
+// FP16 in its normal range, so S and O are the same sums the BF16 dequantization gives; a scale outside
+// that range takes an fp32 path (values below FP16's range round, above it saturate and report an error).
+// With one split the epilogue normalizes (sink included), inverse-rotates the tail and writes BF16 O and
+// the LSE; with several, it writes fp32 partials that the combine kernel merges.
 #include "launchers.h"
 #include "common/sm100.cuh"
 
 namespace {
 
 constexpr int kD = 512;
-constexpr int kHG = 64;           // heads per CTA group
-constexpr int kTile = 128;        // KV rows per tile
-constexpr int kThreads = 256;
+constexpr int kHG = 64;            // heads per CTA (N of the MMAs)
+constexpr int kTileRows = 128;     // KV rows per tile (the M of the score MMA)
+constexpr int kBufRows = 128;
+constexpr int kThreads = 256;      // 8 warps: all expand, all run the softmax, warp 0 also issues the MMAs
 constexpr int kPage = 64;
 constexpr int kNativeData = 576;
 constexpr int kNativePageBytes = kPage * 584;
@@ -39,59 +47,37 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
 // shared memory map (bytes, from a 1024-aligned base)
-constexpr int kQBytes = kHG * kD * 2;        // 65536
-constexpr int kKVBytes = kTile * kD * 2;     // 131072
-constexpr int kPBytes = kTile * kHG * 2;     // 16384
-constexpr int kStageRow = 592;               // raw row staging: record (<= 584 B) or packed + RoPE row
-constexpr int kStageBytes = 4 * kStageRow;   // per warp: 4 rows
+constexpr int kQBytes = kHG * kD * 2;          // 65536: Q, FP16, K-major SW128, chunk stride 64 x 128 B
+constexpr int kKBytes = kBufRows * kD * 2;     // 131072: K, chunk stride 128 x 128 B
+constexpr int kKChunk = kBufRows * 128;        // 16384
+constexpr int kQChunk = kHG * 128;             // 8192
+constexpr int kPBytes = kBufRows * kHG * 2;    // 16384: P^T, FP16, one 128 B row per buffer row
+constexpr int kStgRow = 320;                   // Packed staging: 256 value bytes + 64 bitmap bytes
+constexpr int kStgBytes = 8 * 4 * kStgRow;     // per warp: 4 rows
 constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + kQBytes;
-constexpr int kOffP = kOffKV + kKVBytes;
-// the gather staging is live only during a tile's gather, P only from its softmax to its P.V MMA
-// (complete before the next gather starts): the two share one region
-constexpr int kOffStage = kOffP;
-constexpr int kPStageBytes = kPBytes > 8 * kStageBytes ? kPBytes : 8 * kStageBytes;
-constexpr int kOffRed = kOffP + kPStageBytes;  // float red[8][32]
-constexpr int kOffHead = kOffRed + 8 * 32 * 4;          // m_used[64], l[64], alpha[64]
-constexpr int kOffMisc = kOffHead + 3 * 64 * 4;         // bars, tmem addr, flags
-constexpr int kOffRowValid = kOffMisc + 64;            // uint8 rowvalid[128]
-constexpr int kOffExpand = kOffRowValid + 128;         // uint4 expand_lut[256]
-constexpr int kSmemBytes = kOffExpand + 256 * 16 + 1024;  // + alignment slack
+constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kOffP = kOffK + kKBytes;
+constexpr int kOffStg = kOffP + kPBytes;
+constexpr int kOffRed = kOffStg + kStgBytes;            // float red[4][64]
+constexpr int kOffHead = kOffRed + 4 * 64 * 4;          // m_used[64], l[64], alpha[64], fac[64]
+constexpr int kOffBar = kOffHead + 4 * 64 * 4;          // 9 mbarriers
+constexpr int kOffMisc = kOffBar + 16 * 8;              // tmem slot, flags
+constexpr int kOffRowValid = kOffMisc + 32;             // uint8[128]
+constexpr int kOffLut = kOffRowValid + 128;             // uint4[256] byte-expansion table
+constexpr int kSmemBytes = kOffLut + 256 * 16 + 1024;   // + alignment slack
 
 constexpr uint32_t kTmemO = 0;
 constexpr uint32_t kTmemS = 256;
 constexpr uint32_t kTmemCols = 512;
 
+// barrier indices
+enum : int { kBarSFull = 0, kBarPvDone = 1 };
 
 __device__ __forceinline__ uint4 zero4() { return make_uint4(0, 0, 0, 0); }
 
-// 8 E4M3 bytes * 2^e -> 8 BF16 packed in uint4 (exact).
-__device__ __forceinline__ uint4 dequant8(uint2 codes, float s) {
-  uint32_t w[2] = {codes.x, codes.y};
-  __nv_bfloat162 out[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint16_t pair = (uint16_t)(w[k >> 1] >> (16 * (k & 1)));
-    const float2 f = __half22float2(pm::e4m3x2_to_h2(pair));
-    out[k] = __floats2bfloat162_rn(f.x * s, f.y * s);
-  }
-  return *reinterpret_cast<uint4*>(out);
-}
-
-// 8 E4M3 bytes (little-endian in codes.x, codes.y) * s -> 8 floats (exact).
-__device__ __forceinline__ void dequant8f(uint2 codes, float s, float (&f)[8]) {
-  const uint32_t w[2] = {codes.x, codes.y};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float2 v = __half22float2(pm::e4m3x2_to_h2((uint16_t)(w[k >> 1] >> (16 * (k & 1)))));
-    f[2 * k] = v.x * s;
-    f[2 * k + 1] = v.y * s;
-  }
-}
-
-// Byte expansion of a Packed 8-coordinate unit with kept-mask m: the unit's kept values are the 8
-// bytes starting at its rank (lo, hi); entry m = {selector of coords 0-3, selector of coords 4-7,
-// mask 0-3, mask 4-7} for __byte_perm, so codes = perm(lo, hi, sel) & mask (E4M3 zero = 0x00).
+// Byte expansion of a Packed 8-coordinate unit with kept-mask m: the unit's kept values are the 8 bytes
+// starting at its rank (lo, hi); entry m = {selector of coords 0-3, selector of coords 4-7, mask 0-3,
+// mask 4-7} for __byte_perm, so codes = perm(lo, hi, sel) & mask (E4M3 zero = 0x00).
 __device__ __forceinline__ uint4 expand_lut_entry(int m) {
   uint32_t sel[2] = {0, 0}, msk[2] = {0, 0};
   int r = 0;
@@ -105,120 +91,193 @@ __device__ __forceinline__ uint4 expand_lut_entry(int m) {
   return make_uint4(sel[0], sel[1], msk[0], msk[1]);
 }
 
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// 2^x with the hardware approximation (ex2.approx.f32: subnormal results kept, 2 ulp), as exp2f promises.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Scale exponents e whose products with E4M3 values are exact in FP16 (see the header comment).
+__device__ __forceinline__ bool fast_scale(int e) { return e >= -15 && e <= 7; }
+
+// 2^e as an FP16 bit pattern, e in [-15, 7] (2^-15 is subnormal).
+__device__ __forceinline__ unsigned short f16_pow2(int e) {
+  return (unsigned short)(e >= -14 ? (e + 15) << 10 : 1u << (e + 24));
+}
+
+// 8 E4M3 codes (little-endian in c.x, c.y) x 2^e -> 8 FP16 (uint4).
+__device__ __forceinline__ uint4 dq8(uint2 c, int e, int* err) {
+  const uint32_t w[2] = {c.x, c.y};
+  uint32_t o[4];
+  if (fast_scale(e)) {
+    const __half2 s2 = __half2half2(__ushort_as_half(f16_pow2(e)));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = h2_bits(__hmul2(pm::e4m3x2_to_h2((uint16_t)(w[k >> 1] >> (16 * (k & 1)))), s2));
+  } else {
+    if (e > 7) pm::report_error(err, pm::kBadArgument, e);
+    const float s = pm::exp2i(e);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(pm::e4m3x2_to_h2((uint16_t)(w[k >> 1] >> (16 * (k & 1)))));
+      asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(o[k]) : "f"(f.y * s), "f"(f.x * s));
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// 8 BF16 (uint4) -> 8 FP16 (exact in FP16's normal range; saturating).
+__device__ __forceinline__ uint4 bf16x8_to_f16(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float lo = __uint_as_float(w[k] << 16), hi = __uint_as_float(w[k] & 0xFFFF0000u);
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(o[k]) : "f"(hi), "f"(lo));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 struct RowRef {
   int kind;  // 0 = masked, 1 = native (swa pool), 2 = native (csa pool), 3 = packed
   int slot;
   int pos;
 };
 
-__device__ __forceinline__ RowRef row_ref(const DecodeParams& p, int b, int i, int nswa, int ntot) {
+// Row i of query b's list [SWA rows ; C4 rows], in two steps so the index loads can be issued long
+// before their values are needed: idx_load only loads (no use of the values), idx_resolve checks them.
+struct RowIdx {
+  int slot;  // raw slot (SWA or C4)
+  int pos;   // raw RoPE position (Packed C4 rows)
+};
+__device__ __forceinline__ RowIdx idx_load(const DecodeParams& p, int b, int i, int nswa, int ntot) {
+  RowIdx x{-1, 0};
+  if (i >= ntot) return x;
+  if (i < nswa) {
+    x.slot = p.swa_slots[(int64_t)b * p.swa_cap + i];
+  } else {
+    const int64_t j = (int64_t)b * p.csa_cap + (i - nswa);
+    x.slot = p.csa_slots[j];
+    if (p.csa_packed) x.pos = p.csa_pos[j];
+  }
+  return x;
+}
+// `i` is the row's index in the list (the same one given to idx_load).
+__device__ __forceinline__ RowRef idx_resolve(const DecodeParams& p, const RowIdx& x, int i, int nswa, int ntot) {
   RowRef r{0, -1, 0};
   if (i >= ntot) return r;
+  const int s = x.slot;
   if (i < nswa) {
-    const int s = p.swa_slots[(int64_t)b * p.swa_cap + i];
     if (s >= 0 && s < p.swa_pool_slots) { r.kind = 1; r.slot = s; }
     else if (s >= p.swa_pool_slots) pm::report_error(p.err, pm::kIndexOutOfRange, i);
     return r;
   }
-  const int j = i - nswa;
-  const int s = p.csa_slots[(int64_t)b * p.csa_cap + j];
-  const int pos = p.csa_pos[(int64_t)b * p.csa_cap + j];
   if (s < 0) return r;
-  if (s >= p.csa_pool_rows || (p.csa_packed && (pos < 0 || pos >= p.freq_rows))) {
+  if (s >= p.csa_pool_rows || (p.csa_packed && (x.pos < 0 || x.pos >= p.freq_rows))) {
     pm::report_error(p.err, pm::kIndexOutOfRange, i);
     return r;
   }
   r.kind = p.csa_packed ? 3 : 2;
   r.slot = s;
-  r.pos = pos;
+  r.pos = x.pos;
   return r;
 }
 
-// ----------------------------------------------------------------------------- tile gather
-// One gather step of a warp: rows 4 warp + j + 32 k (j = lane / 8) of the tile, lane v = lane % 8 of
-// the row.  Raw 16-byte units of the row are spread over its 8 lanes (unit v + 8 i).
-//   Native (584 B): units 0..35 = data (448 E4M3 + 128 B BF16 tail), scale row (8 B) by lane v = 0.
-//   Packed (328 B): units 0..15 values, 16..19 bitmap, scales by v = 0; the record's RoPE table row
-//   (64 floats) staged at byte 336 (a staged row is 592 bytes).
-struct StepRegs {
-  uint4 U[5];
+// Raw bytes of one row held by one of its 8 lanes (lane v):
+//   Native: u[i] = 16-byte unit v + 8 i of the record (units 0..27 E4M3, 28..35 BF16 tail; i = 4 only v < 4).
+//   Packed: u[0], u[1] = value units v, v + 8; u[2] = bitmap unit v (v < 4); u[3], u[4] = 16-byte units
+//           2 v, 2 v + 1 of the record's RoPE row (the cos/sin of pairs 4 v .. 4 v + 3).
+//   sc: the row's 8 UE8M0 scale bytes.
+struct Raw {
+  uint4 u[5];
   uint2 sc;
-  int kind, pos;
+  int kind;
 };
 
-__device__ __forceinline__ RowRef step_ref(const DecodeParams& p, int b, int tbase, int tvalid, int nswa, int ntot,
-                                           int r) {
-  return r < tvalid ? row_ref(p, b, tbase + r, nswa, ntot) : RowRef{0, -1, 0};
-}
-
-// Raw loads of one step from its (already resolved) row reference.
-__device__ __forceinline__ void fetch_step(const DecodeParams& p, const RowRef& rr, int v, StepRegs& R) {
+__device__ __forceinline__ void fetch(const DecodeParams& p, const RowRef& rr, int v, Raw& R) {
   R.kind = rr.kind;
-  R.pos = rr.pos;
   R.sc = make_uint2(0, 0);
 #pragma unroll
-  for (int i = 0; i < 5; ++i) R.U[i] = zero4();
+  for (int i = 0; i < 5; ++i) R.u[i] = zero4();
   if (rr.kind == 1 || rr.kind == 2) {
     const uint8_t* pool = rr.kind == 1 ? p.swa_pool : p.csa_pool;
     const int64_t page = rr.slot / kPage, rip = rr.slot % kPage;
-    const uint8_t* data = pool + page * kNativePageBytes + rip * kNativeData;
+    const uint4* data = reinterpret_cast<const uint4*>(pool + page * kNativePageBytes + rip * kNativeData);
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const int u = v + 8 * i;
-      if (u < 36) R.U[i] = *reinterpret_cast<const uint4*>(data + 16 * u);
-    }
-    if (v == 0) R.sc = *reinterpret_cast<const uint2*>(pool + page * kNativePageBytes + kPage * kNativeData + rip * 8);
+    for (int i = 0; i < 4; ++i) R.u[i] = data[v + 8 * i];
+    if (v < 4) R.u[4] = data[v + 32];
+    R.sc = *reinterpret_cast<const uint2*>(pool + page * kNativePageBytes + kPage * kNativeData + rip * 8);
   } else if (rr.kind == 3) {
     const uint4* vals = reinterpret_cast<const uint4*>(p.csa_values + (int64_t)rr.slot * 256);
     const uint4* bits = reinterpret_cast<const uint4*>(p.csa_bitmap + (int64_t)rr.slot * 8);
     const uint4* fq = reinterpret_cast<const uint4*>(p.freqs + (int64_t)rr.pos * 64);
-    R.U[0] = vals[v];
-    R.U[1] = vals[v + 8];
-    if (v < 4) R.U[2] = bits[v];
-    R.U[3] = fq[v];
-    R.U[4] = fq[v + 8];
-    if (v == 0) R.sc = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)rr.slot * 8);
+    R.u[0] = vals[v];
+    R.u[1] = vals[v + 8];
+    if (v < 4) R.u[2] = bits[v];
+    R.u[3] = fq[2 * v];
+    R.u[4] = fq[2 * v + 1];
+    R.sc = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)rr.slot * 8);
   }
 }
 
-// Stage the row, then expand word v (coordinates 64 v .. 64 v + 63) of it into tile row `trow`, one
-// 16-byte unit (8 coordinates) at a time (rolled loops keep the kernel within the instruction cache).
-__device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, uint8_t* __restrict__ srow,
-                                            uint8_t* __restrict__ kv, uint8_t* __restrict__ rowvalid,
-                                            const uint4* __restrict__ expand_lut) {
-  if (R.kind == 1 || R.kind == 2) {
-#pragma unroll
-    for (int i = 0; i < 5; ++i) {
-      const int u = v + 8 * i;
-      if (u < 36) *reinterpret_cast<uint4*>(srow + 16 * u) = R.U[i];
+// L2 prefetch of one row's bytes, shared by its lanes 0, 1, 3 (bulk prefetches: 16-byte aligned ranges that
+// lie inside the row's allocation; the 8 scale bytes are left to the demand load).
+__device__ __forceinline__ void prefetch_row(const DecodeParams& p, const RowRef& rr, int v) {
+  if (rr.kind == 1 || rr.kind == 2) {
+    if (v == 0) {
+      const uint8_t* pool = rr.kind == 1 ? p.swa_pool : p.csa_pool;
+      pm::bulk_prefetch_l2(pool + (int64_t)(rr.slot / kPage) * kNativePageBytes + (rr.slot % kPage) * kNativeData,
+                           kNativeData);
     }
-    if (v == 0) *reinterpret_cast<uint2*>(srow + 576) = R.sc;
-  } else if (R.kind == 3) {
-    *reinterpret_cast<uint4*>(srow + 16 * v) = R.U[0];
-    *reinterpret_cast<uint4*>(srow + 16 * (v + 8)) = R.U[1];
-    if (v < 4) *reinterpret_cast<uint4*>(srow + 256 + 16 * v) = R.U[2];
-    if (v == 0) *reinterpret_cast<uint2*>(srow + 320) = R.sc;
-    *reinterpret_cast<uint4*>(srow + 336 + 16 * v) = R.U[3];
-    *reinterpret_cast<uint4*>(srow + 336 + 16 * (v + 8)) = R.U[4];
+  } else if (rr.kind == 3) {
+    if (v == 0) pm::bulk_prefetch_l2(p.csa_values + (int64_t)rr.slot * 256, 256);
+    else if (v == 1) pm::bulk_prefetch_l2(p.csa_bitmap + (int64_t)rr.slot * 8, 64);
+    else if (v == 3) pm::bulk_prefetch_l2(p.freqs + (int64_t)rr.pos * 64, 256);
   }
-  __syncwarp();
-  if (v == 0) rowvalid[trow] = R.kind != 0;
+}
+
+__device__ __forceinline__ int scale_exp(uint2 sc, int word) {
+  const uint32_t w = word < 4 ? sc.x : sc.y;
+  return (int)((w >> (8 * (word & 3))) & 0xFF) - 127;
+}
+
+// Expand one row (lane v of its 8 lanes) into K-buffer row `brow`.  Out of line: the four passes of a stage
+// share one copy of this code, which keeps the kernel small enough for the instruction cache.
+__device__ __noinline__ void expand_row(const Raw R, int brow, int v, uint8_t* __restrict__ stg,
+                                           uint8_t* __restrict__ sK, uint8_t* __restrict__ rowvalid,
+                                           const uint4* __restrict__ lut, int* err) {
+  // 128-byte swizzle: 16-byte unit u of a row's 64-coordinate chunk c sits at
+  // c * kKChunk + (row / 8) * 1024 + (row % 8) * 128 + ((u ^ row % 8) * 16)
+  uint8_t* const row_base = sK + (brow >> 3) * 1024 + (brow & 7) * 128;
+  const int rsw = brow & 7;
+  auto out = [&](int byte_in_row) -> uint4* {
+    return reinterpret_cast<uint4*>(row_base + (byte_in_row >> 7) * kKChunk + (((byte_in_row >> 4) & 7) ^ rsw) * 16);
+  };
+  // unit v of every chunk (the Packed and masked paths): one swizzled column, chunk i at + i * kKChunk
+  uint8_t* const col_v = row_base + ((v ^ rsw) << 4);
+  if (v == 0) rowvalid[brow] = R.kind != 0;
   if (R.kind == 1 || R.kind == 2) {
-    // lane v expands unit v of every 64-coordinate word i: seven dequantized NoPE units and one copied
-    // (already rotated) BF16 tail unit per lane, uniform across the warp; the 8 lanes of a row store
-    // 128 contiguous bytes per word
-#pragma unroll 2
-    for (int i = 0; i < 8; ++i) {
-      const uint4 o = i < 7 ? dequant8(*reinterpret_cast<const uint2*>(srow + 64 * i + 8 * v),
-                                       pm::exp2i((int)srow[576 + i] - 127))
-                            : *reinterpret_cast<const uint4*>(srow + 448 + 16 * v);
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) = o;
+    // NoPE units v + 8 i (16 codes = coordinates 16 u .. 16 u + 15 of word u / 4)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int u = v + 8 * i;
+      if (u < 28) {
+        const int e = scale_exp(R.sc, u >> 2);
+        *out(32 * u) = dq8(make_uint2(R.u[i].x, R.u[i].y), e, err);
+        *out(32 * u + 16) = dq8(make_uint2(R.u[i].z, R.u[i].w), e, err);
+      }
     }
+    // the lane's tail unit (8 BF16 coordinates, already rotated)
+    const int ut = v >= 4 ? v + 24 : v + 32;
+    *out(896 + 16 * (ut - 28)) = bf16x8_to_f16(v >= 4 ? R.u[3] : R.u[4]);
   } else if (R.kind == 3) {
-    // lane v expands unit v of every 64-coordinate word i (coordinates 64 i + 8 v .. + 7): each lane
-    // rotates exactly one RoPE unit (word 7) and the seven NoPE units skip the rotation, with the
-    // branch uniform across the warp
-    const uint64_t* words = reinterpret_cast<const uint64_t*>(srow + 256);
+    *reinterpret_cast<uint4*>(stg + 16 * v) = R.u[0];
+    *reinterpret_cast<uint4*>(stg + 16 * (v + 8)) = R.u[1];
+    if (v < 4) *reinterpret_cast<uint4*>(stg + 256 + 16 * v) = R.u[2];
+    __syncwarp(0xFFu << (8 * ((threadIdx.x & 31) >> 3)));
+    const uint64_t* words = reinterpret_cast<const uint64_t*>(stg + 256);
     const uint64_t below = (1ull << (8 * v)) - 1ull;  // bits of the word before this lane's unit
     int prefix = 0;                                    // kept values before word i
 #pragma unroll 2
@@ -227,39 +286,43 @@ __device__ __forceinline__ void expand_step(const StepRegs& R, int trow, int v, 
       const uint32_t bits = (uint32_t)(word >> (8 * v)) & 0xFFu;
       const int rank = prefix + __popcll(word & below);
       prefix += __popcll(word);
-      // the 8 value bytes from `rank` (reads may run past the values into the staged bitmap: masked)
-      const uint32_t* vw = reinterpret_cast<const uint32_t*>(srow + (rank & ~3));
+      // the 8 value bytes from `rank` (reads past the values land in the staged bitmap: masked off)
+      const uint32_t* vw = reinterpret_cast<const uint32_t*>(stg + (rank & ~3));
       const uint32_t sh = 8u * (uint32_t)(rank & 3);
       const uint32_t lo = __funnelshift_r(vw[0], vw[1], sh), hi = __funnelshift_r(vw[1], vw[2], sh);
-      const uint4 e = expand_lut[bits];
+      const uint4 e = lut[bits];
       const uint2 codes = make_uint2(__byte_perm(lo, hi, e.x) & e.z, __byte_perm(lo, hi, e.y) & e.w);
-      float f[8];
-      dequant8f(codes, pm::exp2i((int)srow[320 + i] - 127), f);
-      __nv_bfloat162 o2[4];
+      const int ex = scale_exp(R.sc, i);
+      uint4 o;
       if (i < 7) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+        o = dq8(codes, ex, err);
       } else {
-        const float* cs = reinterpret_cast<const float*>(srow + 336) + 8 * v;  // pairs 4 v .. 4 v + 3
-        const float4 cs01 = *reinterpret_cast<const float4*>(cs), cs23 = *reinterpret_cast<const float4*>(cs + 4);
-        const float cc[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, ss[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
+        // dequantize (exact in fp32), round to BF16, rotate with the record's pair (cos, sin), round again
+        const float s = pm::exp2i(ex);
+        const uint32_t cw[2] = {codes.x, codes.y};
+        const float cs[8] = {__uint_as_float(R.u[3].x), __uint_as_float(R.u[3].y), __uint_as_float(R.u[3].z),
+                             __uint_as_float(R.u[3].w), __uint_as_float(R.u[4].x), __uint_as_float(R.u[4].y),
+                             __uint_as_float(R.u[4].z), __uint_as_float(R.u[4].w)};
+        uint32_t ow[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float re = __bfloat162float(__float2bfloat16_rn(f[2 * k]));
-          const float im = __bfloat162float(__float2bfloat16_rn(f[2 * k + 1]));
-          o2[k] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(re, cc[k]), __fmul_rn(im, ss[k])),
-                                        __fadd_rn(__fmul_rn(re, ss[k]), __fmul_rn(im, cc[k])));
+          const float2 f = __half22float2(pm::e4m3x2_to_h2((uint16_t)(cw[k >> 1] >> (16 * (k & 1)))));
+          const float re = __bfloat162float(__float2bfloat16_rn(f.x * s));
+          const float im = __bfloat162float(__float2bfloat16_rn(f.y * s));
+          const float c = cs[2 * k], sn = cs[2 * k + 1];
+          const float rr = __bfloat162float(__float2bfloat16_rn(__fsub_rn(__fmul_rn(re, c), __fmul_rn(im, sn))));
+          const float ri = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(re, sn), __fmul_rn(im, c))));
+          asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(ow[k]) : "f"(ri), "f"(rr));
         }
+        o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) =
-          *reinterpret_cast<uint4*>(o2);
+      *reinterpret_cast<uint4*>(col_v + i * kKChunk) = o;
     }
+    __syncwarp(0xFFu << (8 * ((threadIdx.x & 31) >> 3)));
   } else {
-#pragma unroll 2
-    for (int i = 0; i < 8; ++i)
-      *reinterpret_cast<uint4*>(kv + pm::sw128_offset(trow, 16 * (8 * i + v), kTile * 128)) = zero4();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(col_v + i * kKChunk) = zero4();
   }
-  __syncwarp();
 }
 
 // Lane L returns op-reduction over the 32 lanes of v[L] (31 shuffles instead of 160).
@@ -283,34 +346,28 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (pm::smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem + kOffQ;
-  uint8_t* sKV = smem + kOffKV;
+  uint8_t* sK = smem + kOffK;
   uint8_t* sP = smem + kOffP;
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* m_used = reinterpret_cast<float*>(smem + kOffHead);
   float* l_sum = m_used + 64;
   float* alpha = l_sum + 64;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + kOffMisc);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] rescale needed, [1] abort
+  float* fac = alpha + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* flags = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);  // [0] rescale, [1] abort
   uint8_t* rowvalid = smem + kOffRowValid;
-  uint4* expand_lut = reinterpret_cast<uint4*>(smem + kOffExpand);
+  uint4* lut = reinterpret_cast<uint4*>(smem + kOffLut);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // optional phase counters (thread 0, ns of the GPU global timer): [0] setup, [1] gather + expand,
-  // [2] S MMA, [3] softmax, [4] O MMA (with the next tile's first gather), [5] epilogue, [6] CTAs,
-  // [7] tiles, [8] earliest CTA start, [9] latest CTA end; [16 + 2 i] CTA i's total, [17 + 2 i] gather
-  unsigned long long ph[6] = {0, 0, 0, 0, 0, 0};
-  uint64_t tp = p.prof ? pm::globaltimer_ns() : 0;
-  const uint64_t t_cta0 = tp;
-  auto mark = [&](int i) {
-    if (p.prof && tid == 0) {
-      const uint64_t t = pm::globaltimer_ns();
-      ph[i] += t - tp;
-      tp = t;
-    }
-  };
   const int unit = blockIdx.x;
+  // optional global-timer stamps of CTA 0 (ns): [0] start, [1] set-up done, [2 + 2 t] tile t expanded,
+  // [3 + 2 t] its softmax done, [18 + t] S(t) issued, [26 + t] P.V(t) issued, [34] epilogue start, [35] end,
+  // [36..39] inside tile 0's softmax: start, scores ready, maxima reduced, probabilities written
+  auto stamp = [&](int i) {
+    if (p.prof != nullptr && blockIdx.x == 0 && i < 48) p.prof[i] = pm::globaltimer_ns();
+  };
+  if (tid == 0) stamp(0);
   const int split = unit % p.num_splits;
   const int g = (unit / p.num_splits) % p.num_groups;
   const int b = unit / (p.num_splits * p.num_groups);
@@ -318,63 +375,64 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
 
   const int nswa = min(p.swa_len[b], p.swa_cap);
   const int ntot = nswa + min(p.csa_len[b], p.csa_cap);
-  // this query's rows split into whole tiles of `trows` rows (128, or 64 when a small batch needs more
-  // CTAs), as evenly as the split count allows; a 64-row tile leaves MMA rows 64-127 zero and masked
-  const int trows = p.tile_rows == 64 ? 64 : kTile;
-  const int tiles_q = (ntot + trows - 1) / trows;
-  const int tiles_per_split = (tiles_q + p.num_splits - 1) / p.num_splits;
-  const int row0 = split * tiles_per_split * trows;
-  const int row1 = min(ntot, row0 + tiles_per_split * trows);
-  const int ntiles = row1 > row0 ? (row1 - row0 + trows - 1) / trows : 0;
+  const int tiles_q = (ntot + kTileRows - 1) / kTileRows;
+  const int t0 = (int)(((int64_t)split * tiles_q) / p.num_splits);
+  const int t1 = (int)(((int64_t)(split + 1) * tiles_q) / p.num_splits);
+  const int nt = t1 - t0;
 
-  uint8_t* srow = smem + kOffStage + warp * kStageBytes + (lane >> 3) * kStageRow;
-  const int v8 = lane & 7;
-  // step k of a tile: rows 4 warp + lane / 8 + 32 k
-  auto step_row = [&](int k) { return 4 * warp + (lane >> 3) + 32 * k; };
-  // row references of the 4 steps of tile tt (4 independent index loads in flight together)
-  RowRef rr[4];
-  auto resolve = [&](int tt) {
-    const int tb = row0 + tt * trows, tv = min(trows, row1 - tb);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) rr[k] = step_ref(p, b, tb, tv, nswa, ntot, step_row(k));
-  };
-  // four register sets, one per gather step: all record loads of a tile are in flight together, and the
-  // loads of tile t + 1 are issued while the P.V MMAs of tile t run; no register copy ever waits on loads
-  // still in flight
-  StepRegs ra, rb, rc, rd;
-  auto fetch_all = [&](int n) {
-    fetch_step(p, rr[0], v8, ra);
-    fetch_step(p, rr[1], v8, rb);
-    if (n == 4) {
-      fetch_step(p, rr[2], v8, rc);
-      fetch_step(p, rr[3], v8, rd);
-    }
+  // bounded wait; after the first timeout every later wait returns at once (the CTA runs to its end
+  // on garbage data instead of waiting again)
+  auto wait = [&](int bar, uint32_t parity, int site) {
+    if (flags[1]) return;
+    if (!pm::mbar_wait(&bars[bar], parity, p.err, site)) flags[1] = 1;
   };
 
-  // tile 0's index and record loads go out first: their latency overlaps the TMEM allocation, the
-  // LUT set-up and the Q load below
-  if (ntiles > 0) {
-    resolve(0);
-    fetch_all(4);
-  }
-  __syncwarp();  // the lanes took row-dependent branches; tcgen05.alloc is warp-collective
+  const int wq = warp & 3, v8 = lane & 7, rsub = lane >> 3;
+  uint8_t* stg = smem + kOffStg + (warp & 7) * (4 * kStgRow) + rsub * kStgRow;
+
+  // A tile's 128 rows: pass pp of warp w holds rows 32 pp + 4 w + lane / 8 (8 lanes per row).  The raw
+  // indices of the next tile are loaded a tile ahead (ix0..ix3); they are resolved, prefetched into L2 and
+  // their rows loaded into ra..rd while the current tile's softmax and P.V run.
+  const int lrow = 4 * (warp & 7) + rsub;
+  RowIdx ix0, ix1, ix2, ix3;
+  Raw ra, rb, rc, rd;
+  auto idx4 = [&](int t) {
+    const int base = (t0 + t) * kTileRows + lrow;
+    ix0 = idx_load(p, b, base, nswa, ntot);
+    ix1 = idx_load(p, b, base + 32, nswa, ntot);
+    ix2 = idx_load(p, b, base + 64, nswa, ntot);
+    ix3 = idx_load(p, b, base + 96, nswa, ntot);
+  };
+  auto load4 = [&](int t) {
+    const int base = (t0 + t) * kTileRows + lrow;
+    const RowRef f0 = idx_resolve(p, ix0, base, nswa, ntot), f1 = idx_resolve(p, ix1, base + 32, nswa, ntot);
+    const RowRef f2 = idx_resolve(p, ix2, base + 64, nswa, ntot), f3 = idx_resolve(p, ix3, base + 96, nswa, ntot);
+    prefetch_row(p, f0, v8);
+    prefetch_row(p, f1, v8);
+    prefetch_row(p, f2, v8);
+    prefetch_row(p, f3, v8);
+    fetch(p, f0, v8, ra);
+    fetch(p, f1, v8, rb);
+    fetch(p, f2, v8, rc);
+    fetch(p, f3, v8, rd);
+  };
+  if (nt > 0) idx4(0);  // the first tile's indices go out before the set-up
 
   if (warp == 0) {
     pm::tmem_alloc(tmem_slot, kTmemCols);
     pm::tmem_relinquish();
   }
   if (tid == 0) {
-    pm::mbar_init(bar_s, 1);
-    pm::mbar_init(bar_o, 1);
+    pm::mbar_init(&bars[kBarSFull], 1);
+    pm::mbar_init(&bars[kBarPvDone], 1);
     pm::fence_mbar_init();
     flags[0] = 0;
     flags[1] = 0;
   }
   if (tid < 64) { m_used[tid] = -INFINITY; l_sum[tid] = 0.f; alpha[tid] = 1.f; }
-  for (int m = tid; m < 256; m += kThreads) expand_lut[m] = expand_lut_entry(m);
+  for (int m = tid; m < 256; m += kThreads) lut[m] = expand_lut_entry(m);
 
-  // Q group -> shared (K-major, SW128, chunk stride 64 rows * 128 B): all 16 loads of a thread in
-  // flight before the first store
+  // Q group -> shared FP16 (K-major SW128): 16 loads of a thread in flight before the stores
   {
     uint4 qv[kHG * 64 / kThreads];
 #pragma unroll
@@ -384,228 +442,251 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
                                                                (int64_t)(h0 + row) * p.q_stride_h + 8 * u)
                              : zero4();
     }
+    if (nt > 0) {  // the first tile's rows are in flight while Q is converted, the second tile's indices too
+      load4(0);
+      if (nt > 1) idx4(1);
+    }
 #pragma unroll
     for (int i = 0; i < kHG * 64 / kThreads; ++i) {
       const int idx = tid + kThreads * i, row = idx >> 6, u = idx & 63;
-      *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(row, 16 * u, kHG * 128)) = qv[i];
+      *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(row, 16 * u, kQChunk)) = bf16x8_to_f16(qv[i]);
     }
+    pm::fence_proxy_async_smem();
   }
   pm::tc_fence_before();
   __syncthreads();
   pm::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) stamp(1);
 
-  mark(0);
-  const uint32_t q_base = pm::smem_u32(sQ), kv_base = pm::smem_u32(sKV), p_base = pm::smem_u32(sP);
-  const uint32_t idesc_s = pm::make_idesc_f16(128, kHG, 1, 0, 0);
-  const uint32_t idesc_o = pm::make_idesc_f16(128, kHG, 1, 1, 1);
-  bool ok = true;
-
-  for (int t = 0; t < ntiles && ok; ++t) {
-    // ---- 1. gather + expand 128 rows (64-row tiles: steps 2-3 only on the first tile, zero rows)
-    const int nsteps = (trows == kTile || t == 0) ? 4 : 2;  // tile 0's loads were issued at set-up
-    uint64_t tg = p.prof && tid == 0 ? pm::globaltimer_ns() : 0;
-    auto sub = [&](int slot) {  // finer split of the gather for thread 0: [11] expand
-      if (p.prof && tid == 0) {
-        const uint64_t tn = pm::globaltimer_ns();
-        atomicAdd(p.prof + slot, (unsigned long long)(tn - tg));
-        tg = tn;
-      }
-    };
-    auto expand = [&](const StepRegs& R, int k) {
-      expand_step(R, step_row(k), v8, srow, sKV, rowvalid, expand_lut);
-    };
-    expand(ra, 0);
-    expand(rb, 1);
-    if (nsteps == 4) {
-      expand(rc, 2);
-      expand(rd, 3);
+  const uint32_t q_base = pm::smem_u32(sQ), k_base = pm::smem_u32(sK), p_base = pm::smem_u32(sP);
+  const uint32_t idesc_s = pm::make_idesc_f16(128, kHG, 0, 0, 0);
+  const uint32_t idesc_o = pm::make_idesc_f16(128, kHG, 0, 1, 1);
+  const int ch = warp >> 2;         // softmax: this warp's head columns 32 ch .. 32 ch + 31
+  const int brow = 32 * wq + lane;  // softmax: this thread's tile row (TMEM lane)
+#pragma unroll 1
+  for (int t = 0; t < nt; ++t) {
+    if (t > 0) {  // the buffer and P are free once the previous tile's P.V MMAs complete
+      wait(kBarPvDone, (t - 1) & 1, 32);
+      pm::tc_fence_after();
     }
-    sub(11);
+    expand_row(ra, lrow, v8, stg, sK, rowvalid, lut, p.err);
+    expand_row(rb, lrow + 32, v8, stg, sK, rowvalid, lut, p.err);
+    expand_row(rc, lrow + 64, v8, stg, sK, rowvalid, lut, p.err);
+    expand_row(rd, lrow + 96, v8, stg, sK, rowvalid, lut, p.err);
     pm::fence_proxy_async_smem();
     pm::tc_fence_before();
-    __syncthreads();
-    pm::tc_fence_after();
-    sub(12);  // [12] waiting for the other warps at the end of the gather
-    mark(1);
-    // ---- 2. S^T = K Q^T
-    if (tid == 0) {
+    pm::named_bar_sync(1, kThreads);  // every row (and row flag) of the tile is written
+    if (tid == 0 && t < 8) stamp(2 + 2 * t);
+    if (warp == 0) {  // S^T = K Q^T, issued by one elected lane of the converged warp
+      pm::tc_fence_after();
+      if (lane == 0 && t < 8) stamp(18 + t);
 #pragma unroll 1
-      for (int k = 0; k < kD / 16; ++k) {
-        const uint32_t koff = (k * 32) & 127;
-        const uint64_t ad = pm::make_sdesc(kv_base + (k >> 2) * (kTile * 128) + koff, 16, 1024);
-        const uint64_t bd = pm::make_sdesc(q_base + (k >> 2) * (kHG * 128) + koff, 16, 1024);
-        pm::umma_f16(tmem + kTmemS, ad, bd, idesc_s, k > 0);
+      for (int c = 0; c < 8; ++c) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = pm::make_sdesc(k_base + c * kKChunk + 32 * k, 16, 1024);
+          const uint64_t bd = pm::make_sdesc(q_base + c * kQChunk + 32 * k, 16, 1024);
+          pm::umma_f16_warp(tmem + kTmemS, ad, bd, idesc_s, (c | k) ? 1u : 0u);
+        }
       }
-      pm::umma_commit(bar_s);
+      pm::umma_commit_warp(&bars[kBarSFull]);
     }
-    if (!pm::mbar_wait(bar_s, t & 1, p.err, 1)) { flags[1] = 1; }
+    // the next tile's rows go out now (they land during this tile's scores, softmax and P.V), and the
+    // indices of the tile after it
+    if (t + 1 < nt) {
+      load4(t + 1);
+      if (t + 2 < nt) idx4(t + 2);
+    }
+    // ---- softmax of the tile
+    if (tid == 0 && t == 0) stamp(36);
+    wait(kBarSFull, t & 1, 33);
     pm::tc_fence_after();
-    mark(2);
-    // ---- 3. softmax over rows (lanes) per head (columns)
-    const int quarter = warp & 3, chalf = warp >> 2;
-    const int n = 32 * quarter + lane;  // KV row within tile
-    float s[32];
-    {
-      float a[16], c[16];
-      const uint32_t ta = tmem + kTmemS + 32 * chalf + ((uint32_t)(32 * quarter) << 16);
-      pm::tmem_ld16(ta, a);
-      pm::tmem_ld16(ta + 16, c);
-      pm::tmem_wait_ld();
+    if (tid == 0 && t == 0) stamp(37);
+    const bool row_ok = rowvalid[brow] != 0;
+    const uint32_t s_addr = tmem + kTmemS + 32 * ch + ((uint32_t)(32 * wq) << 16);
+    float sv[32];
+    pm::tmem_ld32(s_addr, sv);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) { s[i] = a[i]; s[16 + i] = c[i]; }
-    }
-    const bool row_ok = rowvalid[n] != 0;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) s[i] = row_ok ? s[i] * p.scale_log2 : -INFINITY;
-    // column max: transpose-reduce over lanes, then across the 4 quarter-warps of this column half
-    {
+    for (int i = 0; i < 32; ++i) sv[i] = row_ok ? sv[i] * p.scale_log2 : -INFINITY;
+    {  // per-head maxima over the tile's rows (scores in log2 units, masked rows -inf)
       float mx[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mx[i] = s[i];
-      red[warp * 32 + lane] = transpose_reduce<true>(mx, lane);
+      for (int i = 0; i < 32; ++i) mx[i] = sv[i];
+      red[wq * 64 + 32 * ch + lane] = transpose_reduce<true>(mx, lane);
     }
-    __syncthreads();
+    pm::named_bar_sync(1, kThreads);
+    if (tid == 0 && t == 0) stamp(38);
     if (tid < 64) {
-      const int h = tid, hc = h >> 5, hl = h & 31;
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmax = fmaxf(tmax, red[(hc * 4 + q4) * 32 + hl]);
-      const float mu = m_used[h];
+      const int hh = tid;
+      const float tmax = fmaxf(fmaxf(red[hh], red[64 + hh]), fmaxf(red[128 + hh], red[192 + hh]));
+      const float mu = m_used[hh];
       float a = 1.f;
       if (tmax > mu + kRescaleThreshold || mu == -INFINITY) {
         a = (mu == -INFINITY) ? 0.f : exp2f(mu - tmax);
-        m_used[h] = tmax;
+        m_used[hh] = tmax;
         if (mu != -INFINITY) flags[0] = 1;
       }
-      alpha[h] = a;
+      alpha[hh] = a;
     }
-    __syncthreads();
-    // p = 2^(s - m_used), write P^T (MN-major SW128: row n = 64 heads * 2 B)
-    float psum[32];
-    {
-      __nv_bfloat162 pk[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float m0 = m_used[32 * chalf + i], m1 = m_used[32 * chalf + i + 1];
-        const float p0 = (s[i] == -INFINITY || m0 == -INFINITY) ? 0.f : exp2f(s[i] - m0);
-        const float p1 = (s[i + 1] == -INFINITY || m1 == -INFINITY) ? 0.f : exp2f(s[i + 1] - m1);
-        pk[i >> 1] = __floats2bfloat162_rn(p0, p1);
-        // sum the BF16-rounded probabilities so l matches what the PV MMA accumulates
-        const float2 r = __bfloat1622float2(pk[i >> 1]);
-        psum[i] = r.x;
-        psum[i + 1] = r.y;
-      }
-#pragma unroll
-      for (int uu = 0; uu < 4; ++uu)
-        *reinterpret_cast<uint4*>(sP + pm::sw128_offset(n, 64 * chalf + 16 * uu, 0)) =
-            *reinterpret_cast<uint4*>(&pk[4 * uu]);
-    }
-    red[warp * 32 + lane] = transpose_reduce<false>(psum, lane);
-    // rescale O^T columns if some head's reference max moved (rare)
-    if (flags[0] && t > 0) {
-      // warp w: lane quarter w%4, d-blocks 2*(w/4) .. +1, 64 head columns each
+    pm::named_bar_sync(1, kThreads);
+    if (tid == 0 && t == 0) stamp(40);
+    if (flags[0]) {
+      // O^T is complete once the previous tile's P.V is (waited above); this warp rescales its lane
+      // quadrant's columns of its head half in every d-block
 #pragma unroll 1
-      for (int db = 2 * chalf; db < 2 * chalf + 2; ++db) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < kHG; c0 += 16) {
-          float v[16];
-          const uint32_t ta = tmem + kTmemO + db * kHG + c0 + ((uint32_t)(32 * quarter) << 16);
-          pm::tmem_ld16(ta, v);
-          pm::tmem_wait_ld();
+      for (int db = 0; db < 4; ++db) {
+        float o[32];
+        const uint32_t ta = tmem + kTmemO + db * kHG + 32 * ch + ((uint32_t)(32 * wq) << 16);
+        pm::tmem_ld32(ta, o);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] *= alpha[c0 + i];
-          pm::tmem_st16(ta, v);
-        }
+        for (int i = 0; i < 32; ++i) o[i] *= alpha[32 * ch + i];
+        pm::tmem_st32(ta, o);
       }
       pm::tmem_wait_st();
     }
+    {  // P = 2^(s - m_used) in FP16 (row = tile row, this warp's 32 heads) and the per-head sums of the
+       // FP16-rounded values (what the P.V MMA accumulates); red now takes the sums
+      __half2 pk[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float m0 = m_used[32 * ch + i], m1 = m_used[32 * ch + i + 1];
+        // a masked row (-inf) or a head without any row yet (-inf max) contributes 0
+        const float p0 = (sv[i] == -INFINITY || m0 == -INFINITY) ? 0.f : fast_exp2(sv[i] - m0);
+        const float p1 = (sv[i + 1] == -INFINITY || m1 == -INFINITY) ? 0.f : fast_exp2(sv[i + 1] - m1);
+        pk[i >> 1] = __floats2half2_rn(p0, p1);
+        const float2 r = __half22float2(pk[i >> 1]);
+        sv[i] = r.x;
+        sv[i + 1] = r.y;
+      }
+      if (tid == 0 && t == 0) stamp(41);
+#pragma unroll
+      for (int uu = 0; uu < 4; ++uu)
+        *reinterpret_cast<uint4*>(sP + pm::sw128_offset(brow, 64 * ch + 16 * uu, 0)) =
+            *reinterpret_cast<uint4*>(&pk[4 * uu]);
+      red[wq * 64 + 32 * ch + lane] = transpose_reduce<false>(sv, lane);
+    }
+    if (tid == 0 && t == 0) stamp(39);
     pm::fence_proxy_async_smem();
     pm::tc_fence_before();
-    __syncthreads();
-    pm::tc_fence_after();
-    if (tid < 64) {
-      const int h = tid, hc = h >> 5, hl = h & 31;
-      float ts = 0.f;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) ts += red[(hc * 4 + q4) * 32 + hl];
-      l_sum[h] = l_sum[h] * alpha[h] + ts;
-      if (h == 0) flags[0] = 0;
-    }
-    mark(3);
-    // ---- 4. O^T += V^T P^T
-    if (tid == 0 && !flags[1]) {
+    pm::named_bar_sync(1, kThreads);
+    if (warp == 0) {  // O^T += V^T P^T over the tile's 128 rows
+      pm::tc_fence_after();
+      if (lane == 0 && t < 8) stamp(26 + t);
 #pragma unroll 1
       for (int db = 0; db < 4; ++db) {
-#pragma unroll 1
-        for (int k = 0; k < trows / 16; ++k) {
-          const uint64_t ad = pm::make_sdesc(kv_base + (2 * db) * (kTile * 128) + k * 2048, kTile * 128, 1024);
-          const uint64_t bd = pm::make_sdesc(p_base + k * 2048, 8192, 1024);
-          pm::umma_f16(tmem + kTmemO + db * kHG, ad, bd, idesc_o, (t > 0 || k > 0) ? 1u : 0u);
-        }
-      }
-      pm::umma_commit(bar_o);
-    }
-    if (t + 1 < ntiles) {  // overlaps the P.V MMAs
-      resolve(t + 1);
-      fetch_all(trows == kTile ? 4 : 2);
-    }
-    if (!flags[1]) {
-      if (!pm::mbar_wait(bar_o, t & 1, p.err, 2)) flags[1] = 1;
-    }
-    pm::tc_fence_after();
-    __syncthreads();
-    ok = !flags[1];
-    mark(4);
-  }
-
-  // ---- epilogue: partial O (unnormalized, relative to m_used), m, l
-  const int64_t part = ((int64_t)b * p.num_splits + split);
-  if (ok && ntiles > 0) {
-    const int quarter = warp & 3, chalf = warp >> 2;
-#pragma unroll 1
-    for (int db = 2 * chalf; db < 2 * chalf + 2; ++db) {
-      const int d = 128 * db + 32 * quarter + lane;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kHG; c0 += 16) {
-        float v[16];
-        pm::tmem_ld16(tmem + kTmemO + db * kHG + c0 + ((uint32_t)(32 * quarter) << 16), v);
-        pm::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int h = h0 + c0 + i;
-          if (h < p.H) p.part_o[(part * p.H + h) * kD + d] = v[i];
+        for (int k16 = 0; k16 < 8; ++k16) {  // 16-row groups of the tile
+          const uint64_t ad = pm::make_sdesc(k_base + (2 * db) * kKChunk + k16 * 2048, kKChunk, 1024);
+          const uint64_t bd = pm::make_sdesc(p_base + k16 * 2048, 8192, 1024);
+          pm::umma_f16_warp(tmem + kTmemO + db * kHG, ad, bd, idesc_o, (t > 0 || k16 > 0) ? 1u : 0u);
         }
       }
+      pm::umma_commit_warp(&bars[kBarPvDone]);
     }
-  }
-  mark(5);
-  if (p.prof && tid == 0) {
-    for (int i = 0; i < 6; ++i) atomicAdd(p.prof + i, ph[i]);
-    atomicAdd(p.prof + 6, 1ull);
-    atomicAdd(p.prof + 7, (unsigned long long)ntiles);
-    atomicMin(p.prof + 8, (unsigned long long)t_cta0);
-    atomicMax(p.prof + 9, (unsigned long long)pm::globaltimer_ns());
-    if (blockIdx.x < 1024) {
-      p.prof[16 + 2 * blockIdx.x] = pm::globaltimer_ns() - t_cta0;
-      p.prof[17 + 2 * blockIdx.x] = ph[1];
+    if (tid < 64) {
+      const int hh = tid;
+      l_sum[hh] = l_sum[hh] * alpha[hh] + (red[hh] + red[64 + hh]) + (red[128 + hh] + red[192 + hh]);
+      if (hh == 0) flags[0] = 0;
     }
+    if (tid == 0 && t < 8) stamp(3 + 2 * t);
   }
-  if (tid < 64 && h0 + tid < p.H) {
-    const bool empty = !(ok && ntiles > 0);
-    p.part_ml[(part * p.H + h0 + tid) * 2 + 0] = empty ? -INFINITY : m_used[tid];
-    p.part_ml[(part * p.H + h0 + tid) * 2 + 1] = empty ? 0.f : l_sum[tid];
+  {
+    // ------------------------------------------------------------------ epilogue (all 8 warps)
+    const bool direct = p.num_splits == 1;
+    if (nt > 0) {
+      wait(kBarPvDone, (nt - 1) & 1, 36);
+      pm::tc_fence_after();
+    }
+    pm::named_bar_sync(1, kThreads);  // the last tile's sums are in l
+    const int64_t part = (int64_t)b * p.num_splits + split;
+    if (tid == 0) stamp(34);
+    if (tid < 64) {
+      const int hh = tid, head = h0 + hh;
+      const float m = m_used[hh], l = l_sum[hh];
+      if (direct) {
+        const float sink2 = (p.sink && head < p.H) ? p.sink[head] * kLog2e : -INFINITY;
+        const float M = fmaxf(m, sink2);
+        const float w = (m == -INFINITY) ? 0.f : exp2f(m - M);
+        const float L = l * w + ((sink2 == -INFINITY) ? 0.f : exp2f(sink2 - M));
+        fac[hh] = L > 0.f ? w / L : 0.f;
+        if (head < p.H && p.lse) p.lse[(int64_t)b * p.H + head] = L > 0.f ? (M + log2f(L)) / kLog2e : -INFINITY;
+      } else if (head < p.H) {
+        const bool empty = nt == 0 || m == -INFINITY;
+        p.part_ml[(part * p.H + head) * 2 + 0] = empty ? -INFINITY : m;
+        p.part_ml[(part * p.H + head) * 2 + 1] = empty ? 0.f : l;
+      }
+    }
+    pm::named_bar_sync(1, kThreads);
+    // O^T: warp w reads lane quadrant w % 4 (d = 128 db + 32 (w % 4) + lane) of d-blocks 2 (w / 4), +1
+    __nv_bfloat16* sOut = reinterpret_cast<__nv_bfloat16*>(sK);  // [64 heads][512] BF16 (the K buffer is free)
+    int qp = 0;
+    if (direct) {
+      qp = p.q_pos ? p.q_pos[b] : 0;
+      if (qp < 0 || qp >= p.freq_rows) { pm::report_error(p.err, pm::kIndexOutOfRange, b); qp = 0; }
+    }
+#pragma unroll 1
+    for (int db = 2 * ch; db < 2 * ch + 2; ++db) {
+      const int d = 128 * db + 32 * wq + lane;
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float o[32];
+        if (nt > 0) {
+          pm::tmem_ld32(tmem + kTmemO + db * kHG + 32 * hf + ((uint32_t)(32 * wq) << 16), o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (!direct) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int head = h0 + 32 * hf + i;
+            if (head < p.H) p.part_o[(part * p.H + head) * kD + d] = o[i];
+          }
+          continue;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __bfloat162float(__float2bfloat16_rn(o[i] * fac[32 * hf + i]));
+        if (d >= 448) {  // inverse RoPE of the tail: pair (d, d + 1) = lanes (2 k, 2 k + 1)
+          const int pair = (d - 448) >> 1;
+          const float c = p.freqs[(int64_t)qp * 64 + 2 * pair], sn = -p.freqs[(int64_t)qp * 64 + 2 * pair + 1];
+          const bool odd = d & 1;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float other = __shfl_xor_sync(0xffffffffu, o[i], 1);
+            const float re = odd ? other : o[i], im = odd ? o[i] : other;
+            o[i] = odd ? __fadd_rn(__fmul_rn(re, sn), __fmul_rn(im, c))
+                       : __fsub_rn(__fmul_rn(re, c), __fmul_rn(im, sn));
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sOut[(32 * hf + i) * kD + d] = __float2bfloat16_rn(o[i]);
+      }
+    }
+    if (direct) {
+      pm::named_bar_sync(1, kThreads);
+      const int nh = min(kHG, p.H - h0);
+#pragma unroll 4
+      for (int idx = tid; idx < nh * 64; idx += 256) {
+        const int hh = idx >> 6, u = idx & 63;
+        *reinterpret_cast<uint4*>(p.out + ((int64_t)b * p.H + h0 + hh) * kD + 8 * u) =
+            *reinterpret_cast<const uint4*>(sOut + hh * kD + 8 * u);
+      }
+    }
   }
   pm::tc_fence_before();
   __syncthreads();
+  if (tid == 0) stamp(35);
   if (warp == 0) pm::tmem_dealloc(tmem, kTmemCols);
+#undef PM_RESOLVE
+#undef PM_IDX_LOAD
 }
 
 // ----------------------------------------------------------------------------- combine
 // One warp per (b, h): lane owns 16 coordinates.
 __global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restrict__ part_o,
                                                           const float* __restrict__ part_ml,
-                                                          const float* __restrict__ sink, float scale_log2_unused,
+                                                          const float* __restrict__ sink,
                                                           const int32_t* __restrict__ q_pos,
                                                           const float* __restrict__ freqs, int64_t freq_rows, int B,
                                                           int H, int splits, __nv_bfloat16* __restrict__ out,
@@ -664,13 +745,20 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restric
 
 }  // namespace
 
-void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,
+void launch_sparse_mla_decode(const DecodeParams& params, const float* sink, const int32_t* q_pos,
                               __nv_bfloat16* out, float* lse, cudaStream_t stream) {
-  if (p.B == 0) return;
+  if (params.B == 0) return;
+  DecodeParams p = params;
+  p.sink = sink;
+  p.q_pos = q_pos;
+  p.out = out;
+  p.lse = lse;
   cudaFuncSetAttribute(sparse_mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   const int grid = p.B * p.num_groups * p.num_splits;
   sparse_mla_decode_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  const int warps = p.B * p.H;
-  mla_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(p.part_o, p.part_ml, sink, p.scale_log2, q_pos, p.freqs,
-                                                          p.freq_rows, p.B, p.H, p.num_splits, out, lse, p.err);
+  if (p.num_splits > 1) {
+    const int warps = p.B * p.H;
+    mla_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(p.part_o, p.part_ml, sink, q_pos, p.freqs, p.freq_rows,
+                                                            p.B, p.H, p.num_splits, out, lse, p.err);
+  }
 }

@@ -13,11 +13,12 @@ void launch_packed_store(const float* raw, int64_t raw_stride, const float* weig
                          uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int rows, int* err,
                          cudaStream_t stream);
 
+// Sparse MLA decode (csrc/attention_decode.cu).  A query's rows [SWA ; C4] are split into 64-row
+// stages; split s of num_splits takes an even share of whole stages.
 struct DecodeParams {
   const __nv_bfloat16* q;  // [B, H, 512]
   int64_t q_stride_b, q_stride_h;
-  int B, H, num_groups, num_splits, rows_per_split;  // rows_per_split: informational (the kernel splits
-                                                     // each query's own rows into whole tiles)
+  int B, H, num_groups, num_splits;
   // SWA (Native) rows
   const uint8_t* swa_pool;
   int64_t swa_pool_slots;
@@ -38,11 +39,16 @@ struct DecodeParams {
   const float* freqs;        // [P, 32, 2]
   int64_t freq_rows;
   float scale_log2;          // softmax scale * log2(e)
-  float* part_o;             // [B, splits, H, 512]
-  float* part_ml;            // [B, splits, H, 2]
+  float* part_o;             // [B, splits, H, 512] (num_splits > 1)
+  float* part_ml;            // [B, splits, H, 2]   (num_splits > 1)
   int* err;
-  unsigned long long* prof;  // optional phase counters (ns, summed over CTAs), see attention_decode.cu
-  int tile_rows;             // KV rows per tile: 128 (default, also for 0) or 64
+  // set by launch_sparse_mla_decode from its arguments
+  const float* sink;         // [H]
+  const int32_t* q_pos;      // [B]
+  __nv_bfloat16* out;        // [B, H, 512]
+  float* lse;                // [B, H]
+  // optional: global-timer stamps of CTA 0 (ns, 40 entries; see attention_decode.cu), null otherwise
+  unsigned long long* prof;
 };
 
 void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,
@@ -97,7 +103,7 @@ int launch_bs_probe2(const uint8_t* a_packed, const uint8_t* b_img, const uint8_
 
 void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
                              int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
-                             int4* chunks, int32_t* n_chunks, cudaStream_t stream);
+                             int4* chunks, int32_t* n_chunks, int max_tok, cudaStream_t stream);
 
 // MXFP4 experts x MXFP8 activations (csrc/moe_mxf4.cu).  Workspace images: xq [H/128, rows, 128],
 // xs [rows, H/32], act_q [I/128, rows, 128], act_s [rows, I/32] (rows % 32 == 0).

@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(1024) moe_route_smem_kernel(const int32_t* __r
                                                               float* __restrict__ slot_weight,
                                                               int32_t* __restrict__ active, int32_t* __restrict__ pad,
                                                               int align, int4* __restrict__ chunks,
-                                                              int32_t* __restrict__ n_chunks) {
+                                                              int32_t* __restrict__ n_chunks, int max_tok) {
   __shared__ int s_e[4096];
   __shared__ int cnt[1024];
   __shared__ int start[1024];
@@ -142,15 +142,16 @@ __global__ void __launch_bounds__(1024) moe_route_smem_kernel(const int32_t* __r
   }
   __syncthreads();
   const int c = tid < E ? cnt[tid] : 0;
-  const int4 pre = block_scan4(make_int4(c, (c + align - 1) / align * align, (c + 15) / 16, c > 0 ? 1 : 0), warp_tot,
-                               &total);
+  const int4 pre = block_scan4(make_int4(c, (c + align - 1) / align * align, (c + max_tok - 1) / max_tok, c > 0 ? 1 : 0),
+                               warp_tot, &total);
   if (tid < E) {
     offsets[tid] = pre.x;
     start[tid] = pre.x;
     if (pad) pad[tid] = pre.y;
     if (c > 0) active[1 + pre.w] = tid;
     if (chunks)
-      for (int q = 0; q < c; q += 16) chunks[pre.z + q / 16] = make_int4(tid, pre.y + q, min(16, c - q), pre.x + q);
+      for (int q = 0; q < c; q += max_tok)
+        chunks[pre.z + q / max_tok] = make_int4(tid, pre.y + q, min(max_tok, c - q), pre.x + q);
   }
   if (tid == 0) {
     offsets[E] = total.x;
@@ -167,6 +168,82 @@ __global__ void __launch_bounds__(1024) moe_route_smem_kernel(const int32_t* __r
     const int p = start[e] + r;
     slot_token[p] = i / k;
     slot_weight[p] = w[i];
+  }
+}
+
+// Routing for any number of slots, deterministic without a sort, in three launches:
+//   count (CTA per local expert) -> plan (one CTA: offsets, padded rows, active list, chunk table)
+//   -> place (CTA per local expert: an ordered stream compaction of the expert's slots, so each expert's
+//   list is in slot order, i.e. sorted by token).  Every CTA reads all slot ids (L2 resident).
+__global__ void __launch_bounds__(256) moe_count_kernel(const int32_t* __restrict__ ids, int n, int base,
+                                                        int32_t* __restrict__ cnt) {
+  __shared__ int wsum[8];
+  const int e = blockIdx.x;
+  int c = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) c += (ids[i] - base == e);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < 8; ++w) t += wsum[w];
+    cnt[e] = t;
+  }
+}
+
+// `pad` holds the counts on entry and the padded row starts on exit (each thread reads its count before
+// the scan's barriers and writes its start after them).
+__global__ void __launch_bounds__(1024) moe_plan_kernel(int E, int align, int max_tok, int32_t* __restrict__ offsets,
+                                                        int32_t* __restrict__ active, int32_t* __restrict__ pad,
+                                                        int4* __restrict__ chunks, int32_t* __restrict__ n_chunks) {
+  __shared__ int4 warp_tot[32];
+  __shared__ int4 total;
+  const int tid = threadIdx.x;
+  const int c = tid < E ? pad[tid] : 0;
+  const int4 pre = block_scan4(make_int4(c, (c + align - 1) / align * align, (c + max_tok - 1) / max_tok, c > 0 ? 1 : 0),
+                               warp_tot, &total);
+  if (tid < E) {
+    offsets[tid] = pre.x;
+    pad[tid] = pre.y;
+    if (c > 0) active[1 + pre.w] = tid;
+    for (int q = 0; q < c; q += max_tok)
+      chunks[pre.z + q / max_tok] = make_int4(tid, pre.y + q, min(max_tok, c - q), pre.x + q);
+  }
+  if (tid == 0) {
+    offsets[E] = total.x;
+    pad[E] = total.y;
+    n_chunks[0] = total.z;
+    active[0] = total.w;
+  }
+}
+
+__global__ void __launch_bounds__(1024) moe_place_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                         int n, int k, int base, const int32_t* __restrict__ offsets,
+                                                         int32_t* __restrict__ slot_token,
+                                                         float* __restrict__ slot_weight) {
+  __shared__ int wcnt[32];
+  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int out = offsets[e];
+  for (int i0 = 0; i0 < n; i0 += 1024) {
+    const int i = i0 + tid;
+    const bool hit = i < n && ids[i] - base == e;
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (lane == 0) wcnt[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, all = 0;
+    for (int ww = 0; ww < 32; ++ww) {
+      const int v = wcnt[ww];
+      before += ww < warp ? v : 0;
+      all += v;
+    }
+    if (hit) {
+      const int p = out + before + __popc(m & ((1u << lane) - 1u));
+      slot_token[p] = i / k;
+      slot_weight[p] = w[i];
+    }
+    out += all;
+    __syncthreads();
   }
 }
 
@@ -398,10 +475,17 @@ void launch_moe_fp4(const __nv_bfloat16* x, int T, int H, int I, int k, const in
 
 void launch_moe_route_chunks(const int32_t* topk_ids, const float* topk_w, int T, int k, int expert_base, int E,
                              int32_t* offsets, int32_t* slot_token, float* slot_weight, int32_t* active, int32_t* pad,
-                             int4* chunks, int32_t* n_chunks, cudaStream_t stream) {
+                             int4* chunks, int32_t* n_chunks, int max_tok, cudaStream_t stream) {
   if (T * k <= 4096 && E <= 1024) {
     moe_route_smem_kernel<<<1, 1024, 0, stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets, slot_token,
-                                                  slot_weight, active, pad, 32, chunks, n_chunks);
+                                                  slot_weight, active, pad, 32, chunks, n_chunks, max_tok);
+    return;
+  }
+  if (E <= 1024) {
+    moe_count_kernel<<<E, 256, 0, stream>>>(topk_ids, T * k, expert_base, pad);
+    moe_plan_kernel<<<1, 1024, 0, stream>>>(E, 32, max_tok, offsets, active, pad, chunks, n_chunks);
+    moe_place_kernel<<<E, 1024, 0, stream>>>(topk_ids, topk_w, T * k, k, expert_base, offsets, slot_token,
+                                             slot_weight);
     return;
   }
   moe_route_kernel<<<1, 1024, 2 * E * sizeof(int), stream>>>(topk_ids, topk_w, T * k, k, expert_base, E, offsets,

@@ -254,8 +254,39 @@ __global__ void __launch_bounds__(kThreads, 1) moe_fp4_mma_kernel(const MmaParam
   __syncthreads();
 }
 
+// Gather the routed token rows (bf16) into the padded fp16 slot layout of `xs_offset`.
+__global__ void moe_gather_slots_kernel(const __nv_bfloat16* __restrict__ x, int K, const int32_t* __restrict__ offsets,
+                                        const int32_t* __restrict__ pad, const int32_t* __restrict__ slot_token, int E,
+                                        __half* __restrict__ xs) {
+  const int units = K / 8;
+  const int n = offsets[E];
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * units; idx += gridDim.x * blockDim.x) {
+    const int slot = idx / units, u = idx % units;
+    int lo = 0, hi = E;  // expert of this slot: offsets[lo] <= slot < offsets[lo + 1]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (offsets[mid] <= slot) lo = mid; else hi = mid;
+    }
+    const int row = pad[lo] + (slot - offsets[lo]);
+    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)slot_token[slot] * K + 8 * u);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+    __half2 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(b[i]);
+      h[i] = __floats2half2_rn(f.x, f.y);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xs) + xs_offset(row, 8 * u, K)) =
+        *reinterpret_cast<uint4*>(h);
+  }
+}
+
 }  // namespace
 
+void launch_moe_gather_slots(const __nv_bfloat16* x, int K, const int32_t* offsets, const int32_t* pad,
+                             const int32_t* slot_token, int E, __half* xs, int num_sms, cudaStream_t stream) {
+  moe_gather_slots_kernel<<<num_sms * 4, 256, 0, stream>>>(x, K, offsets, pad, slot_token, E, xs);
+}
 void launch_moe_fp4_mma(const __nv_bfloat16* x, int T, int H, int I, int E, const int32_t* offsets, const int32_t* pad,
                         const int32_t* slot_token, const float* slot_weight, const int32_t* active, const uint8_t* w13f,
                         const uint8_t* s13f, const uint8_t* w2f, const uint8_t* s2f, __half* xs, __half* act_s,

@@ -7,7 +7,8 @@
 // file does: the weights stay packed MXFP4 in HBM and are never dequantized in registers.
 //
 //   1. route (csrc/moe_fp4.cu, align 32): per-expert slot lists sorted by token, padded row ranges that
-//      start on multiples of 32, and the chunk table {expert, first row, tokens <= 16, first slot}.
+//      start on multiples of 32, and the chunk table {expert, first row, tokens <= MT, first slot} with
+//      MT = 16 for decode-sized batches and 128 for prefill-sized ones (see MxCfg).
 //   2. quant (CTA per slot): h[token] -> E4M3 + UE8M0 per 32 values, written straight into the operand
 //      images the MMA kernel streams; also zeroes `out` for the scatter-add of pass 4.
 //   3. gate/up (persistent, one CTA per SM): unit = (chunk, 128 gate rows + the matching 128 up rows).
@@ -45,22 +46,29 @@
 
 namespace {
 
-constexpr int kStages = 6;
 constexpr int kPrefetch = 10;  // stages fetched into L2 ahead of the shared-memory ring
 constexpr int kThreads = 320;  // warp 0 TMA producer, 1 MMA issuer, 2-5 epilogue, 6-9 scale factors
-constexpr int kMaxTok = 16;    // tokens per chunk (A rows with data)
 constexpr int kMaxG = 32;      // K-groups of 128 (K <= 4096)
-constexpr uint32_t kStageA = kMaxTok * 128;   // activation rows (A operand)
 constexpr uint32_t kStageW = 32768;           // 256 weight rows x 128 B (B operand)
 constexpr uint32_t kStageS = 1024;            // weight scales: 256 rows x 4 B
-constexpr uint32_t kOffW = 2048;              // A first (its descriptor reads 16 KB from there), then B
-constexpr uint32_t kStageBytes = kOffW + kStageW + kStageS;  // 35840 (multiple of 1024)
-constexpr uint32_t kBarOff = kStages * kStageBytes;
-constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
-static_assert(kStageA <= kOffW && kOffW % 1024 == 0 && kStageBytes % 1024 == 0, "stage layout");
-// TMEM columns: D [128 token lanes x 256] fp32, scale ring (kStages x {tokens: 4, unused: 4, weights: 8}).
 constexpr uint32_t kColD = 0, kColSf = 256, kTmemCols = 512;
-static_assert(kColSf + 16 * kStages <= kTmemCols, "TMEM budget");
+
+// Stage geometry for chunks of at most MT tokens (A rows with data).  MT = 16 serves decode: the A copy is
+// 2 KB and six stages keep the weight stream deep.  MT = 128 serves prefill (hundreds of tokens per
+// expert): each 256-row weight tile then feeds a full 128-row A operand, so an expert's weights are
+// streamed once per 128 routed tokens instead of once per 16; four stages fit.
+template <int MT>
+struct MxCfg {
+  static constexpr int kStages = MT <= 16 ? 6 : 4;
+  static constexpr uint32_t kOffW = MT <= 16 ? 2048 : (uint32_t)MT * 128;  // A first, then B
+  static constexpr uint32_t kStageBytes = kOffW + kStageW + kStageS;      // multiple of 1024
+  static constexpr uint32_t kBarOff = kStages * kStageBytes;
+  static constexpr uint32_t kSmemBytes = kBarOff + 256 + 1024;
+  static_assert((uint32_t)MT * 128 <= kOffW && kOffW % 1024 == 0 && kStageBytes % 1024 == 0, "stage layout");
+  // TMEM columns: D [128 token lanes x 256] fp32, scale ring (kStages x {tokens: 4, unused: 4, weights: 8}).
+  static_assert(kColSf + 16 * kStages <= kTmemCols, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
 
 struct MxParams {
   int K, G, J, rows_exp, rows_total, H;  // H: output row stride (mode 1) / act K (mode 0, = I)
@@ -139,9 +147,12 @@ __global__ void __launch_bounds__(128) mx_quant_kernel(const __nv_bfloat16* __re
 }
 
 // ----------------------------------------------------------------------------- expert GEMM
-template <int MODE>
+template <int MODE, int MT>
 __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_constant__ CUtensorMap tmW,
                                                                 const MxParams p) {
+  using C = MxCfg<MT>;
+  constexpr int kStages = C::kStages;
+  constexpr uint32_t kStageBytes = C::kStageBytes, kOffW = C::kOffW, kBarOff = C::kBarOff;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (pm::smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
@@ -215,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_con
         if (u + (int)gridDim.x < nunits) ct_next = p.chunks[(u + gridDim.x) / p.J];
         const int n8 = (ct.z + 7) & ~7, j = u % p.J;
         // self-check of the copy geometry (records the unit and skips instead of faulting)
-        if ((ct.y & 15) || ct.z < 1 || ct.z > kMaxTok || ct.y + kMaxTok > p.rows_total ||
+        if ((ct.y & 15) || ct.z < 1 || ct.z > MT || ct.y + n8 > p.rows_total ||
             (ct.x + 1) * p.rows_exp > p.rows_total_w || (reinterpret_cast<uintptr_t>(p.b_img) & 15)) {
           pm::report_error(p.err, pm::kBadArgument, 100000 + u);
           *abort_flag = 1;
@@ -328,10 +339,10 @@ __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_con
           // the stage's weight scales arrive with its data; the slot is free once its MMAs are done
           if (!pm::mbar_wait(full + st, ph, p.err, 29)) { *abort_flag = 1; break; }
           const uint32_t* ws = reinterpret_cast<const uint32_t*>(smem + st * kStageBytes + kOffW + kStageW);
+          // token m = 32 q + lane lives at lane m, column base + m / 32 = base + q
           uint32_t v[16];
-          v[0] = tk[g];
 #pragma unroll
-          for (int i = 1; i < 8; ++i) v[i] = 0;
+          for (int i = 0; i < 8; ++i) v[i] = i == q ? tk[g] : 0u;
 #pragma unroll
           for (int c = 0; c < 8; ++c) v[8 + c] = ws[32 * c + lane];  // weight row 32 c + lane
           pm::tc_fence_after();
@@ -421,9 +432,11 @@ __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_con
             __syncwarp();
             if (lane == 0) pm::mbar_arrive(d_empty);
           }
-          if (live) {
+          if (live) {  // vector fp32 reductions (sm_90+), 4 outputs per instruction
 #pragma unroll
-            for (int i = 0; i < 128; ++i) atomicAdd(o + 128 * h + i, w * v[i]);
+            for (int i = 0; i < 128; i += 4)
+              atomicAdd(reinterpret_cast<float4*>(o + 128 * h + i),
+                        make_float4(w * v[i], w * v[i + 1], w * v[i + 2], w * v[i + 3]));
           }
         }
       }
@@ -440,11 +453,12 @@ __global__ void __launch_bounds__(kThreads, 1) mx_expert_kernel(const __grid_con
 int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream) {
   if (a.T == 0) return 0;
   if (a.H % 512 || a.I % 512 || a.H / 128 > kMaxG || a.I / 128 > kMaxG || a.rows_total % 32) return -2;
-  static_assert(kMaxTok == 16, "the route kernel builds 16-token chunks");
   if ((reinterpret_cast<uintptr_t>(a.w13) | reinterpret_cast<uintptr_t>(a.w2)) & 31) return -4;
   const int n = a.T * a.k;
+  // chunks of 128 tokens once experts average 64 or more routed tokens (prefill), else of 16 (decode)
+  const int mt = n >= 64 * a.E ? 128 : 16;
   launch_moe_route_chunks(a.topk_ids, a.topk_w, a.T, a.k, a.expert_base, a.E, a.offsets, a.slot_token,
-                          a.slot_weight, a.active, a.pad, a.chunks, a.n_chunks, stream);
+                          a.slot_weight, a.active, a.pad, a.chunks, a.n_chunks, mt, stream);
   mx_quant_kernel<<<max(n, a.T), 128, 0, stream>>>(a.h, a.H, a.E, a.offsets, a.pad, a.slot_token, a.rows_total, a.xq,
                                                    a.xs, a.out, a.T);
   CUtensorMap m13, m2;
@@ -462,8 +476,12 @@ int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream) {
   }
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(mx_expert_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    cudaFuncSetAttribute(mx_expert_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaFuncSetAttribute(mx_expert_kernel<0, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MxCfg<16>::kSmemBytes);
+    cudaFuncSetAttribute(mx_expert_kernel<1, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, MxCfg<16>::kSmemBytes);
+    cudaFuncSetAttribute(mx_expert_kernel<0, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         MxCfg<128>::kSmemBytes);
+    cudaFuncSetAttribute(mx_expert_kernel<1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         MxCfg<128>::kSmemBytes);
     attr = true;
   }
   if ((reinterpret_cast<uintptr_t>(a.xq) | reinterpret_cast<uintptr_t>(a.xs) | reinterpret_cast<uintptr_t>(a.act_q) |
@@ -472,9 +490,11 @@ int launch_moe_mxf4(const MoeMxArgs& a, cudaStream_t stream) {
     return -3;
   MxParams p0{a.H, a.H / 128, a.I / 128, 2 * a.I, a.rows_total, a.I, a.E * 2 * a.I, a.sfw13, a.xq, a.xs, a.chunks, a.n_chunks,
               a.act_q, a.act_s, a.slot_token, a.slot_weight, a.out, a.err, a.prof};
-  mx_expert_kernel<0><<<a.num_sms, kThreads, kSmemBytes, stream>>>(m13, p0);
+  if (mt == 128) mx_expert_kernel<0, 128><<<a.num_sms, kThreads, MxCfg<128>::kSmemBytes, stream>>>(m13, p0);
+  else mx_expert_kernel<0, 16><<<a.num_sms, kThreads, MxCfg<16>::kSmemBytes, stream>>>(m13, p0);
   MxParams p1{a.I, a.I / 128, a.H / 256, a.H, a.rows_total, a.H, a.E * a.H, a.sfw2, a.act_q, a.act_s, a.chunks, a.n_chunks,
               nullptr, nullptr, a.slot_token, a.slot_weight, a.out, a.err, a.prof ? a.prof + 8 : nullptr};
-  mx_expert_kernel<1><<<a.num_sms, kThreads, kSmemBytes, stream>>>(m2, p1);
+  if (mt == 128) mx_expert_kernel<1, 128><<<a.num_sms, kThreads, MxCfg<128>::kSmemBytes, stream>>>(m2, p1);
+  else mx_expert_kernel<1, 16><<<a.num_sms, kThreads, MxCfg<16>::kSmemBytes, stream>>>(m2, p1);
   return 0;
 }

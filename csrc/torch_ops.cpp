@@ -67,10 +67,9 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
                        torch::Tensor csa_scales, torch::Tensor csa_slots, torch::Tensor csa_pos, torch::Tensor csa_len,
                        torch::Tensor freqs, torch::Tensor sink, double scale, torch::Tensor q_pos, int64_t num_splits,
                        torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse,
-                       torch::Tensor err, c10::optional<torch::Tensor> prof, int64_t tile_rows) {
-  TORCH_CHECK(tile_rows == 64 || tile_rows == 128, "tile_rows must be 64 or 128");
-  constexpr int kHG = 64, kTile = 128;
-  if (prof) TORCH_CHECK(prof->scalar_type() == torch::kInt64 && prof->is_contiguous() && prof->numel() >= 16 + 2 * 1024);
+                       torch::Tensor err, c10::optional<torch::Tensor> prof) {
+  constexpr int kHG = 64;
+  if (prof) TORCH_CHECK(prof->is_cuda() && prof->scalar_type() == torch::kInt64 && prof->numel() >= 48);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
   TORCH_CHECK(q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
               "q rows must be 16-byte aligned");
@@ -86,8 +85,12 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   TORCH_CHECK(sink.scalar_type() == torch::kFloat32 && sink.numel() == H && sink.is_contiguous());
   TORCH_CHECK(q_pos.scalar_type() == torch::kInt32 && q_pos.numel() == B && q_pos.is_contiguous());
   TORCH_CHECK(num_splits >= 1);
-  TORCH_CHECK(part_o.scalar_type() == torch::kFloat32 && part_o.numel() >= (int64_t)B * num_splits * H * kD);
-  TORCH_CHECK(part_ml.scalar_type() == torch::kFloat32 && part_ml.numel() >= (int64_t)B * num_splits * H * 2);
+  if (num_splits > 1) {
+    TORCH_CHECK(part_o.is_cuda() && part_o.scalar_type() == torch::kFloat32 &&
+                part_o.numel() >= (int64_t)B * num_splits * H * kD, "part_o too small for the split partials");
+    TORCH_CHECK(part_ml.is_cuda() && part_ml.scalar_type() == torch::kFloat32 &&
+                part_ml.numel() >= (int64_t)B * num_splits * H * 2, "part_ml too small for the split partials");
+  }
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)B * H * kD);
   TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.numel() == (int64_t)B * H);
   if (B == 0) return;
@@ -100,8 +103,6 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.H = H;
   p.num_groups = (H + kHG - 1) / kHG;
   p.num_splits = (int)num_splits;
-  const int cap = swa_slots.size(1) + csa_slots.size(1);
-  p.rows_per_split = ((cap + num_splits - 1) / num_splits + kTile - 1) / kTile * kTile;
   p.swa_pool = swa_pool.data_ptr<uint8_t>();
   p.swa_pool_slots = swa_pool.numel() / kNativePageBytes * kPage;
   p.swa_slots = swa_slots.data_ptr<int32_t>();
@@ -128,11 +129,10 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.freqs = freqs.data_ptr<float>();
   p.freq_rows = freqs.size(0);
   p.scale_log2 = (float)scale * 1.4426950408889634f;
-  p.part_o = part_o.data_ptr<float>();
-  p.part_ml = part_ml.data_ptr<float>();
+  p.part_o = num_splits > 1 ? part_o.data_ptr<float>() : nullptr;
+  p.part_ml = num_splits > 1 ? part_ml.data_ptr<float>() : nullptr;
   p.err = err.data_ptr<int>();
   p.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
-  p.tile_rows = (int)tile_rows;
   launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -658,7 +658,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_values"), py::arg("csa_bitmap"), py::arg("csa_scales"), py::arg("csa_slots"), py::arg("csa_pos"),
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
-        py::arg("prof") = py::none(), py::arg("tile_rows") = 128);
+        py::arg("prof") = py::none());
   m.def("packed_to_native", &packed_to_native, "Adapter: Packed planes rows -> Native records (paged workspace)");
   m.def("segment_copy", &segment_copy, "batched 16-byte-aligned copies between device and mapped host memory");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");

@@ -16,7 +16,7 @@ from ._ext import error_word, ext
 from .kv import native_pool_read
 
 NUM_SMS_B200 = 148
-KV_TILE = 128
+TILE_ROWS = 128
 HEAD_GROUP = 64
 
 
@@ -30,16 +30,12 @@ class PackedPlanes:
 def choose_tiling(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> tuple[int, int]:
     """(KV splits per (query, head group), KV rows per tile).
 
-    As many splits as fit in one wave of one CTA per SM.  A CTA's latency is dominated by gathering
-    and expanding its rows, so when even 64-row tiles fit in one wave the tiles are 64 rows (twice the
-    CTAs, half the chain per CTA)."""
+    As many splits as fill one wave of one CTA per SM, each at least one 128-row tile; with one split the
+    kernel writes the output itself (no partials, no combine launch)."""
     groups = (heads + HEAD_GROUP - 1) // HEAD_GROUP
     work = max(1, batch * groups)
-    tile = KV_TILE
-    if work * max(1, math.ceil(max_rows / KV_TILE)) * 2 <= num_sms:
-        tile = KV_TILE // 2
-    tiles = max(1, math.ceil(max_rows / tile))
-    return max(1, min(tiles, num_sms // work)), tile
+    tiles = max(1, math.ceil(max_rows / TILE_ROWS))
+    return max(1, min(tiles, num_sms // work)), TILE_ROWS
 
 
 def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
@@ -47,13 +43,14 @@ def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_
 
 
 class DecodeWorkspace:
-    """Split-KV partials with stable pointers (safe to capture in CUDA graphs)."""
+    """Split-KV partials with stable pointers (safe to capture in CUDA graphs); empty with one split."""
 
-    def __init__(self, batch: int, heads: int, splits: int, device, tile_rows: int = KV_TILE):
+    def __init__(self, batch: int, heads: int, splits: int, device, tile_rows: int = TILE_ROWS):
         self.splits = splits
         self.tile_rows = tile_rows
-        self.part_o = torch.empty(batch * splits * heads * abi.LATENT_DIM, dtype=torch.float32, device=device)
-        self.part_ml = torch.empty(batch * splits * heads * 2, dtype=torch.float32, device=device)
+        n = batch * splits * heads if splits > 1 else 0
+        self.part_o = torch.empty(n * abi.LATENT_DIM, dtype=torch.float32, device=device)
+        self.part_ml = torch.empty(n * 2, dtype=torch.float32, device=device)
 
 
 def sparse_mla_decode(
@@ -81,7 +78,8 @@ def sparse_mla_decode(
     SWA rows: Native records at `swa_slots` [B, W] (first `swa_len[b]` used; -1 = masked).
     C4 rows: `csa_slots` [B, K] physical records, `csa_pos` [B, K] token positions (RoPE rows
     for Packed), first `csa_len[b]` used.  Exactly one of csa_pool (Native pages) /
-    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].
+    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].  `prof` (optional int64 [48] on the
+    device) receives global-timer stamps of the first CTA's pipeline steps, for latency analysis.
     """
     if (csa_pool is None) == (csa_planes is None):
         raise ValueError("give exactly one of csa_pool (native) or csa_planes (packed)")
@@ -89,16 +87,13 @@ def sparse_mla_decode(
     if not q.is_cuda:
         return _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos,
                            csa_pool, csa_planes)
-    tile_rows = KV_TILE
     if num_splits is None:
         if workspace is not None:
-            num_splits, tile_rows = workspace.splits, workspace.tile_rows
+            num_splits = workspace.splits
         else:
-            num_splits, tile_rows = choose_tiling(B, H, swa_slots.shape[1] + csa_slots.shape[1])
-    elif workspace is not None and workspace.splits == num_splits:
-        tile_rows = workspace.tile_rows
+            num_splits = choose_splits(B, H, swa_slots.shape[1] + csa_slots.shape[1])
     if workspace is None or workspace.splits != num_splits:
-        workspace = DecodeWorkspace(B, H, num_splits, q.device, tile_rows)
+        workspace = DecodeWorkspace(B, H, num_splits, q.device)
     if out is None:
         out = torch.empty(B, H, abi.LATENT_DIM, dtype=torch.bfloat16, device=q.device)
     if lse is None:
@@ -112,7 +107,7 @@ def sparse_mla_decode(
     ext().sparse_mla_decode(
         q, swa_pool, swa_slots, swa_len, packed, native_pool, values, bitmap, scales,
         csa_slots, csa_pos, csa_len, freqs, sink, float(scale), q_pos, int(num_splits),
-        workspace.part_o, workspace.part_ml, out, lse, error_word(dev), prof, int(tile_rows),
+        workspace.part_o, workspace.part_ml, out, lse, error_word(dev), prof,
     )
     return out, lse
 

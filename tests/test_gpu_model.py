@@ -17,10 +17,13 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("precision", ["default", "bf16"])
-@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (5, 8, 2), (40, 16, 4), (3, 4, 4), (150, 4, 2)])
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (5, 8, 2), (40, 16, 4), (3, 4, 4), (150, 4, 2), (600, 8, 2),
+                                   (1200, 8, 4)])
 def test_moe_fp4_matches_dequant_reference(cuda, T, E, k, precision):
     """GPU experts vs the CPU oracle of the same precision (MXFP8 or BF16 activations); T=150 over
-    4 experts routes more than 32 tokens to an expert (several chunks, MMA N up to 32)."""
+    4 experts routes more than 32 tokens to an expert (several chunks, MMA N up to 32).  T=600 and
+    T=1200 route hundreds of tokens to each expert: the prefill form with 128-token chunks, routed by
+    the single-CTA kernel (600 x 2 slots) and by the count / plan / place kernels (1200 x 4 slots)."""
     cfg = small_gpu_config(n_routed_experts=E, moe_topk=k)
     W = init_weights(cfg, device="cpu", seed=T)
     lw = W["layers"][0]
