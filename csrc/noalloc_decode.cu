@@ -1,45 +1,37 @@
 // Allocation-free entry point of the sparse MLA decode kernel.
 //
 // This entry point has no counterpart in the reference project; it is an addition of packmla.
+// Its C interface and contract (who it is for, the scratch limit, the first-call set-up, the shared
+// scratch and its race) are declared in csrc/packmla_noalloc.h.
 //
-// Who needs it: callers that cannot allocate GPU memory at the point where they run attention,
-// for example a host runtime that reserved all device memory up front for its own allocator,
-// a plugin interface that only hands out input and output buffers, or code that must not call
-// cudaMalloc while another framework is recording a stream.  The regular entry point needs a
-// split-KV scratch buffer (partial outputs and softmax statistics) that its caller allocates;
-// this one keeps that scratch in a fixed array compiled into the library instead.
-//
-// Contract:
-//   * The caller passes inputs and outputs; this function calls no cudaMalloc, cudaFree or any
-//     allocating library routine.
-//   * Scratch lives in file-scope __device__ arrays of a fixed maximum size: at most
-//     PACKMLA_NOALLOC_MAX_PARTS = 4096 partial rows, where one partial row is one
-//     (query, KV split, head) triple, i.e. B * num_splits * H <= 4096 (8 MiB of partial outputs
-//     plus 32 KiB of statistics).  Every GPU that loads the library holds this memory until the
-//     process exits.  Larger requests are rejected with an error code and message.
-//   * The first call on a device resolves the scratch address on that device with
-//     cudaGetSymbolAddress (host code cannot use the array's name as a device pointer).  Make that
-//     first call before any stream capture on the device.  The caller's current device must be
-//     the device that owns the tensors.
-//   * Every call shares the one scratch array, which keeps the previous call's contents.  Nothing
-//     in it needs to start at zero: the kernel writes the statistics of every (query, split, head)
-//     it covers, and the combine step only reads partial outputs of splits that wrote them.
-//     Calls that overlap on the GPU (for example on two streams without ordering between them)
-//     race on the scratch and produce wrong results; order them on one stream.
+// Implementation notes: the split-KV scratch (partial outputs and softmax statistics of every
+// (query, split, head) triple) is two file-scope __device__ arrays.  Host code cannot pass their
+// names to a kernel: the name is a host-side stand-in for the symbol, so the device address is looked
+// up once per device with cudaGetSymbolAddress (with that device current) and cached.
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 
 #include "launchers.h"
+#include "packmla_noalloc.h"
 
-#define PACKMLA_NOALLOC_MAX_PARTS 4096
 #define PACKMLA_NOALLOC_MAX_DEVICES 64
+
+// The struct is also restated by bindings in other languages (tests/test_zz_no_alloc.py uses ctypes):
+// pin its layout on the usual 64-bit ABI.
+static_assert(sizeof(void*) == 8, "64-bit ABI expected");
+static_assert(offsetof(PackmlaNoallocDecodeArgs, B) == 24 && offsetof(PackmlaNoallocDecodeArgs, swa_pool) == 32,
+              "PackmlaNoallocDecodeArgs layout changed");
+static_assert(offsetof(PackmlaNoallocDecodeArgs, csa_packed) == 72 && offsetof(PackmlaNoallocDecodeArgs, freqs) == 160,
+              "PackmlaNoallocDecodeArgs layout changed");
+static_assert(offsetof(PackmlaNoallocDecodeArgs, num_splits) == 200 && sizeof(PackmlaNoallocDecodeArgs) == 232,
+              "PackmlaNoallocDecodeArgs layout changed");
 
 namespace {
 
 constexpr int kD = 512;
 constexpr int kHG = 64;
-constexpr int kTile = 128;
 constexpr int kPage = 64;
 constexpr int kNativePageBytes = kPage * 584;
 
@@ -81,49 +73,36 @@ int scratch_for_current_device(float** part_o, float** part_ml) {
 
 extern "C" {
 
-// Arguments of one decode call; pointer fields are device pointers except `err` may be null.
-struct PackmlaNoallocDecodeArgs {
-  const void* q;              // bf16 [B, H, 512]; tail rotated by the query position
-  int64_t q_stride_b;         // elements
-  int64_t q_stride_h;         // elements
-  int32_t B;
-  int32_t H;
-  const void* swa_pool;       // Native pages (uint8), SWA rows
-  int64_t swa_pool_bytes;
-  const int32_t* swa_slots;   // [B, swa_cap]
-  int32_t swa_cap;
-  const int32_t* swa_len;     // [B]
-  int32_t csa_packed;         // 1 = Packed planes, 0 = Native pages
-  const void* csa_pool;       // Native pages (uint8) when csa_packed == 0
-  int64_t csa_pool_bytes;
-  const void* csa_values;     // Packed: uint8 [rows, 256]
-  const void* csa_bitmap;     // Packed: uint64 [rows, 8]
-  const void* csa_scales;     // Packed: uint8 [rows, 8]
-  int64_t csa_rows;           // Packed rows
-  const int32_t* csa_slots;   // [B, csa_cap]
-  const int32_t* csa_pos;     // [B, csa_cap]
-  int32_t csa_cap;
-  const int32_t* csa_len;     // [B]
-  const float* freqs;         // [freq_rows, 32, 2]
-  int64_t freq_rows;
-  const float* sink;          // [H]
-  float scale;                // softmax scale
-  const int32_t* q_pos;       // [B]
-  int32_t num_splits;
-  void* out;                  // bf16 [B, H, 512]
-  float* lse;                 // [B, H]
-  int* err;                   // int32[4] device error word, or null
-};
-
 // Returns 0 on success; otherwise 1 and packmla_noalloc_last_error() describes the problem.
 int packmla_sparse_mla_decode_noalloc(const PackmlaNoallocDecodeArgs* a, cudaStream_t stream) {
   if (a == nullptr) return fail("null argument block");
   if (a->B < 0 || a->H <= 0 || a->num_splits < 1) return fail("B >= 0, H > 0 and num_splits >= 1 required");
   if ((int64_t)a->B * a->num_splits * a->H > PACKMLA_NOALLOC_MAX_PARTS)
     return fail("B * num_splits * H exceeds the 4096 partial rows of the built-in scratch");
-  if (a->swa_pool_bytes % kNativePageBytes != 0) return fail("swa_pool_bytes must be whole pages");
-  if (!a->csa_packed && a->csa_pool_bytes % kNativePageBytes != 0) return fail("csa_pool_bytes must be whole pages");
   if (a->B == 0) return 0;
+  // the kernel reads q with 16-byte vector loads: the rows must start on 16-byte boundaries
+  if (a->q == nullptr || (reinterpret_cast<uintptr_t>(a->q) & 15) != 0)
+    return fail("q must be a non-null 16-byte aligned pointer");
+  if (a->q_stride_b % 8 != 0 || a->q_stride_h % 8 != 0 || a->q_stride_b < 0 || a->q_stride_h < 0)
+    return fail("q strides must be non-negative multiples of 8 elements");
+  if (a->swa_cap < 0 || a->csa_cap < 0) return fail("swa_cap and csa_cap must be >= 0");
+  if (a->freq_rows <= 0) return fail("freq_rows must be > 0");
+  if (a->swa_pool == nullptr || a->swa_slots == nullptr || a->swa_len == nullptr || a->csa_slots == nullptr ||
+      a->csa_pos == nullptr || a->csa_len == nullptr || a->freqs == nullptr || a->sink == nullptr ||
+      a->q_pos == nullptr || a->out == nullptr || a->lse == nullptr)
+    return fail("null input or output pointer");
+  if (a->swa_pool_bytes <= 0 || a->swa_pool_bytes % kNativePageBytes != 0)
+    return fail("swa_pool_bytes must be a positive number of whole pages");
+  if (a->csa_packed) {
+    if (a->csa_values == nullptr || a->csa_bitmap == nullptr || a->csa_scales == nullptr || a->csa_rows <= 0)
+      return fail("Packed rows need values, bitmap and scales planes and csa_rows > 0");
+  } else if (a->csa_pool == nullptr || a->csa_pool_bytes <= 0 || a->csa_pool_bytes % kNativePageBytes != 0) {
+    return fail("Native rows need csa_pool with a positive number of whole pages");
+  }
+  if (((reinterpret_cast<uintptr_t>(a->swa_pool) | reinterpret_cast<uintptr_t>(a->csa_pool) |
+        reinterpret_cast<uintptr_t>(a->csa_values) | reinterpret_cast<uintptr_t>(a->csa_bitmap) |
+        reinterpret_cast<uintptr_t>(a->freqs) | reinterpret_cast<uintptr_t>(a->out)) & 15) != 0)
+    return fail("pools, planes, freqs and out must be 16-byte aligned");
   float* part_o = nullptr;
   float* part_ml = nullptr;
   if (scratch_for_current_device(&part_o, &part_ml) != 0) return 1;
@@ -135,8 +114,6 @@ int packmla_sparse_mla_decode_noalloc(const PackmlaNoallocDecodeArgs* a, cudaStr
   p.H = a->H;
   p.num_groups = (a->H + kHG - 1) / kHG;
   p.num_splits = a->num_splits;
-  const int cap = a->swa_cap + a->csa_cap;
-  p.rows_per_split = ((cap + a->num_splits - 1) / a->num_splits + kTile - 1) / kTile * kTile;
   p.swa_pool = static_cast<const uint8_t*>(a->swa_pool);
   p.swa_pool_slots = a->swa_pool_bytes / kNativePageBytes * kPage;
   p.swa_slots = a->swa_slots;
@@ -171,5 +148,7 @@ int packmla_sparse_mla_decode_noalloc(const PackmlaNoallocDecodeArgs* a, cudaStr
 const char* packmla_noalloc_last_error(void) { return g_last_error; }
 
 int packmla_noalloc_max_parts(void) { return PACKMLA_NOALLOC_MAX_PARTS; }
+
+size_t packmla_noalloc_args_size(void) { return sizeof(PackmlaNoallocDecodeArgs); }
 
 }  // extern "C"
