@@ -183,6 +183,9 @@ class Engine:
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self._last_prefill = False
+        # optional device timing of steps: when set to a list, every step appends ("prefill" | "decode",
+        # start event, end event) recorded on the current stream around its device work
+        self.step_events: list | None = None
         # device prefix cache: processed tokens of a finished request -> its retained slot (LRU order)
         self.retained: OrderedDict[tuple, int] = OrderedDict()
         # prompt forks: leader rid -> requests with the same prompt that copy its KV once it is prefilled
@@ -415,14 +418,28 @@ class Engine:
                 return self._decode()
         return []
 
+    def _events(self, kind: str):
+        """(start, end) CUDA events of this step when step timing is on, else None."""
+        if self.step_events is None or self.device.type != "cuda":
+            return None
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        self.step_events.append((kind, ev[0], ev[1]))
+        return ev
+
     def _prefill_chunk(self, req: Request) -> list[tuple[int, int]]:
         chunk = self.ecfg.chunked_prefill_size
         start = req.prefilled
         toks = req.prompt[start:start + chunk]
         t = torch.tensor(toks, dtype=torch.int64)
+        ev = self._events("prefill")
+        if ev is not None:
+            ev[0].record()
         if self.device.type == "cuda":
             t = t.pin_memory().to(self.device, non_blocking=True)
+        self.h2d_bytes_last = t.numel() * t.element_size()
         logits = self.model.prefill(t, start, req.slot)
+        if ev is not None:
+            ev[1].record()
         req.prefilled += len(toks)
         self.metrics.inc("prefill_tokens", len(toks))
         if req.prefilled < len(req.prompt):
@@ -445,8 +462,13 @@ class Engine:
             self._h_slots[i] = r.slot
             self._h_temps[i] = r.params.temperature
         self.h2d_bytes_last = b * (8 + 8 + 8 + 4)
+        ev = self._events("decode")
+        if ev is not None:
+            ev[0].record()
         out = self.runner.run(self._h_tokens[:b], self._h_pos[:b], self._h_slots[:b], self._h_temps[:b])
         self._h_out[:b].copy_(out, non_blocking=True)
+        if ev is not None:
+            ev[1].record()
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
         self.d2h_bytes_last = b * 8

@@ -171,3 +171,43 @@ def test_clients_send_the_api_key_from_the_environment(monkeypatch):
     assert auth_headers() == {"Authorization": "Bearer k1"}
     monkeypatch.setenv("PACKMLA_API_KEY", "k2")
     assert auth_headers() == {"Authorization": "Bearer k2"}
+
+
+def test_bench_phase_runs_every_request_to_its_length():
+    """bench.py's serving phase on the tiny CPU model: all requests finish with their full output, the
+    engine never runs more than C of them, and prompt chunks are counted as host -> device bytes."""
+    import importlib.util
+    import os
+
+    import torch
+
+    from packmla.config import EngineConfig, ModelConfig
+    from packmla.engine.engine import Engine, SamplingParams
+    from packmla.parallel.comm import TPComm
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_main", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = ModelConfig.tiny()
+    C = 2
+    eng = Engine.build(cfg, EngineConfig(max_running_requests=C, chunked_prefill_size=16, prefix_cache=True,
+                                         disable_cuda_graph=True), "cpu", max_context=128, max_requests=C)
+    running_max = []
+    step = eng.step
+
+    def watched():
+        out = step()
+        running_max.append(len(eng.running))
+        return out
+
+    eng.step = watched
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist() for _ in range(3 * C)]
+    st = bench.run_phase(eng, prompts, SamplingParams(max_new_tokens=5), TPComm(), torch.device("cpu"), timed=True)
+    assert st["out_tokens"] == 3 * C * 5
+    assert max(running_max) <= C
+    assert st["h2d"] >= 3 * C * 40 * 8  # every prompt token crossed as an int64
+    assert st["wall_s"] > 0 and st["engine_steps"] >= 3 * C * 4
+    eng.flush_cache()
+    assert not eng.retained
