@@ -108,14 +108,26 @@ def _relative(output, target, denom):
     return (sq / denom).clamp_min(1e-30).sqrt()
 
 
+def _training_only(state: dict, what: str) -> None:
+    """Gradients, the continuous relaxation and codec anchors exist only for states of the training split."""
+    if state.get("role") != "train":
+        raise ValueError(f"{what}: state of role {state.get('role')!r}; only the training split may use it")
+
+
+def _relaxation_temperature(t: float) -> None:
+    if not 0 < t <= 0.15:
+        raise ValueError(f"relaxation temperature {t!r} outside (0, 0.15]")
+
+
 # ----------------------------------------------------------------------------- scalar (the deciding replay)
 def forward_error(math, ref, state: dict, model, temperature: float | None = None, *,
                   retained_features: int = KEEP, keep_mask: torch.Tensor | None = None) -> torch.Tensor:
     """Exact Packed attention error of one state; with `temperature`, straight-through gradients."""
     if temperature is not None and (retained_features != KEEP or keep_mask is not None):
-        raise ValueError("comparison masks and non-256 budgets are inference-only")
+        raise ValueError(f"gradients run at the serving budget of {KEEP} with the scorer's own mask; "
+                         "explicit masks and other budgets are for evaluation")
     if retained_features not in RETENTION_COUNTS:
-        raise ValueError("retained features must be 64 through 448 in multiples of 64")
+        raise ValueError(f"retained_features {retained_features!r} not in {RETENTION_COUNTS}")
     scores = None
     if keep_mask is not None:
         mask = keep_mask
@@ -127,8 +139,7 @@ def forward_error(math, ref, state: dict, model, temperature: float | None = Non
                             retained_features=retained_features)
     rows = exact
     if temperature is not None:
-        if state.get("role") != "train":
-            raise ValueError("only training issues may produce gradients")
+        _training_only(state, "straight-through gradient")
         soft = BudgetGate.apply(scores, temperature)
         gate = mask.float() + (soft - soft.detach())
         cont = _continuous_rows(math, state["raw"], gate, state["weight"], state["eps"], state["freq"])
@@ -145,10 +156,8 @@ def forward_error(math, ref, state: dict, model, temperature: float | None = Non
 
 def relaxed_forward_error(math, state: dict, model, temperature: float, anchor: dict | None = None):
     """Continuous gated path (training only); with `anchor`, plus the fixed codec residuals."""
-    if state.get("role") != "train":
-        raise ValueError("only training issues may use the continuous relaxation")
-    if not 0 < temperature <= 0.15:
-        raise ValueError("positive bounded relaxation temperature required")
+    _training_only(state, "continuous relaxation")
+    _relaxation_temperature(temperature)
     if anchor is not None:
         validate_codec_anchor(state, anchor)
     gate = BudgetGate.apply(model(state["raw"], state["eps"]), temperature)
@@ -168,8 +177,7 @@ def anchored_relaxed_forward_error(math, state, model, temperature, anchor):
 
 def codec_residual_anchor(math, ref, state: dict, model) -> dict:
     """Codec residuals at `model`'s hard mask, held fixed while training (not a serving input)."""
-    if state.get("role") != "train":
-        raise ValueError("only training states may construct codec anchors")
+    _training_only(state, "codec anchor")
     with torch.no_grad():
         scores = model(state["raw"], state["eps"])
         mask = torch.ones_like(scores, dtype=torch.bool)
@@ -183,13 +191,14 @@ def codec_residual_anchor(math, ref, state: dict, model) -> dict:
 
 
 def validate_codec_anchor(state: dict, anchor: dict) -> None:
-    if state.get("role") != "train" or anchor.get("state") is not state:
-        raise ValueError("same original training state required for codec anchor")
+    _training_only(state, "codec anchor")
+    if anchor.get("state") is not state:
+        raise ValueError("codec anchor was built for another state object")
     for key, like in (("rows", state["raw"]), ("output", state["target"])):
         v = anchor[key]
-        if (v.shape != like.shape or v.device != like.device or v.dtype != like.dtype or v.requires_grad
-                or not bool(torch.isfinite(v).all())):
-            raise ValueError("finite fixed codec residual geometry required")
+        fits = v.shape == like.shape and v.device == like.device and v.dtype == like.dtype
+        if not fits or v.requires_grad or not bool(torch.isfinite(v).all()):
+            raise ValueError(f"codec anchor {key!r} must be a finite constant shaped like the state's {key}")
 
 
 # ----------------------------------------------------------------------------- batched
@@ -198,20 +207,21 @@ _STACK = ("raw", "weight", "freq", "q", "swa", "sink", "target", "query_freq")
 
 def stack_states(states: list[dict], anchors: list[dict] | None = None) -> dict:
     if not states:
-        raise ValueError("nonempty batch required")
+        raise ValueError("stack_states: empty batch")
     first = states[0]
-    for s in states:
-        if s["eps"] != first["eps"] or s["scale"] != first["scale"]:
-            raise ValueError("same layer epsilon and scale required")
-        if any(s[k].shape != first[k].shape for k in _STACK):
-            raise ValueError("uniform fully-admitted shapes required")
+    for i, s in enumerate(states):
+        if (s["eps"], s["scale"]) != (first["eps"], first["scale"]):
+            raise ValueError(f"stack_states: state {i} is from another layer (epsilon or softmax scale differs)")
+        odd = [k for k in _STACK if s[k].shape != first[k].shape]
+        if odd:
+            raise ValueError(f"stack_states: state {i} differs in shape for {odd}")
     batch = {k: torch.stack([s[k] for s in states]) for k in _STACK}
     batch.update(eps=first["eps"], scale=first["scale"], roles=[s["role"] for s in states],
                  reference_squared_norm=torch.tensor([s["reference_squared_norm"] for s in states],
                                                      dtype=torch.float64, device=first["raw"].device))
     if anchors is not None:
         if len(anchors) != len(states):
-            raise ValueError("one fixed codec anchor per original training state required")
+            raise ValueError(f"stack_states: {len(anchors)} codec anchors for {len(states)} states")
         for s, a in zip(states, anchors):
             validate_codec_anchor(s, a)
         batch["codec_rows"] = torch.stack([a["rows"] for a in anchors])
@@ -240,8 +250,8 @@ def forward_errors(math, ref, batch: dict, model, temperature: float | None = No
                                        freqs[i * rows_per:(i + 1) * rows_per]) for i in range(n)])
     rows = exact
     if temperature is not None:
-        if any(r != "train" for r in batch["roles"]):
-            raise ValueError("only training issues may produce gradients")
+        for role in batch["roles"]:
+            _training_only({"role": role}, "straight-through gradient")
         soft = BudgetGate.apply(scores, temperature)
         gate = mask.float() + (soft - soft.detach())
         cont = _continuous_rows(math, raw, gate, weight, batch["eps"], freqs)
@@ -258,10 +268,9 @@ def forward_errors(math, ref, batch: dict, model, temperature: float | None = No
 
 
 def relaxed_forward_errors(math, batch: dict, model, temperature: float, *, anchored: bool = False):
-    if any(r != "train" for r in batch["roles"]):
-        raise ValueError("only training issues may use the continuous relaxation")
-    if not 0 < temperature <= 0.15:
-        raise ValueError("positive bounded relaxation temperature required")
+    for role in batch["roles"]:
+        _training_only({"role": role}, "continuous relaxation")
+    _relaxation_temperature(temperature)
     n, rows_per, width = batch["raw"].shape
     raw = batch["raw"].reshape(-1, width)
     gate = BudgetGate.apply(model(raw, batch["eps"]), temperature)
@@ -281,7 +290,7 @@ def _compare(vector, scalar, vgrad, sgrad, what: str) -> dict:
     torch.testing.assert_close(vector.detach(), scalar.detach(), atol=2e-6, rtol=2e-5)
     for a, b in zip(vgrad, sgrad):
         if not bool(torch.isfinite(a).all()):
-            raise ValueError(f"nonfinite {what} batch gradient")
+            raise ValueError(f"{what} preflight: the batched gradient has non-finite entries")
         torch.testing.assert_close(a, b, atol=2e-5, rtol=2e-4)
     return {"forward_max_abs": float((vector - scalar).detach().abs().max()),
             "gradient_max_abs": max(float((a - b).abs().max()) for a, b in zip(vgrad, sgrad)),
@@ -327,7 +336,7 @@ def validation_acceptable(metrics: dict, baseline: dict) -> bool:
 
 def measure(math, ref, states: list[dict], model) -> tuple[dict, list[dict]]:
     if not states:
-        raise ValueError("nonempty measurement states required")
+        raise ValueError("measure: no states to measure")
     dev = model.theta.device
     errs = []
     with torch.no_grad():
@@ -361,4 +370,4 @@ def select_objective(math, ref, model, gradient_mode: str) -> Objective:
                          lambda st, T, an=None: relaxed_forward_errors(math, stack_states(st, an), model, T,
                                                                        anchored=True),
                          lambda st, T, an=None: relaxed_preflight(math, st, model, T, an), True)
-    raise ValueError("explicit supported training gradient mode required")
+    raise ValueError(f"gradient mode {gradient_mode!r}: use straight_through, relaxed or anchored")

@@ -55,8 +55,10 @@ class StaticScore(torch.nn.Module):
         return raw.abs().clamp_min(1e-30).log() + self.theta
 
     def hard_mask(self, ref, raw: torch.Tensor, eps: float) -> torch.Tensor:
-        # the magnitude rule on |x| exp(theta): same order as the scores, same tie handling as TopMag
-        return ref.topmag_keep_mask(raw.abs() * self.theta.detach().exp(), 0.5)
+        """The kept coordinates: exp of the score, exp(theta) |x|, ranked by the codec's magnitude rule (the same
+        order as the scores, ties to the lower coordinate), so a learned static policy packs like TopMag."""
+        weighted = torch.exp(self.theta.detach()) * raw.abs()
+        return ref.topmag_keep_mask(weighted, 0.5)
 
 
 class ConditionalScore(torch.nn.Module):
@@ -118,17 +120,39 @@ class ExpandedConditionalScore(EvenConditionalScore):
 RANK16_NAMES = {"theta", "encoder", "decoder", "decoder_even"}
 
 
+class CheckpointError(ValueError):
+    """A policy or scorer checkpoint that packmla will not load (the message names the file and the field)."""
+
+
+def _as_tensor(name: str, value, device=None, dtype=None) -> torch.Tensor:
+    try:
+        t = torch.as_tensor(value, device=device, dtype=dtype)
+    except (TypeError, ValueError) as exc:
+        raise CheckpointError(f"parameter {name!r} is not a numeric array") from exc
+    if not bool(torch.isfinite(t).all()):
+        raise CheckpointError(f"parameter {name!r} holds non-finite values")
+    return t
+
+
+def _check_names(got, want: set, what: str) -> None:
+    missing, extra = sorted(want - set(got)), sorted(set(got) - want)
+    if missing or extra:
+        raise CheckpointError(f"{what}: missing parameters {missing}, unexpected parameters {extra}")
+
+
 def extend_parameters(parameters: dict, seed: int) -> dict:
-    """Rank-16 checkpoint -> rank-64 parameters (new encoder seeded, new decoders zero)."""
-    if set(parameters) != RANK16_NAMES:
-        raise ValueError("complete rank-16 quadratic warm scorer required")
-    model = ExpandedConditionalScore(torch.tensor(parameters["theta"]), seed=seed)
-    sd = model.state_dict()
-    for name, value in parameters.items():
-        if torch.tensor(value).shape != sd[name].shape:
-            raise ValueError("warm parameter geometry changed")
-    extra = {k: v.tolist() for k, v in sd.items() if k.startswith("extra_")}
-    return {**parameters, **extra}
+    """Rank-16 checkpoint -> rank-64 parameters: the 48 added encoder columns are drawn from `seed`, the added
+    decoders are zero, so the extended scorer scores exactly as the rank-16 one did."""
+    _check_names(parameters, RANK16_NAMES, "rank-16 warm start")
+    model = ExpandedConditionalScore(_as_tensor("theta", parameters["theta"]), seed=seed)
+    layout = model.state_dict()
+    for name in RANK16_NAMES:
+        if tuple(_as_tensor(name, parameters[name]).shape) != tuple(layout[name].shape):
+            raise CheckpointError(f"rank-16 warm start: {name!r} has shape "
+                                  f"{tuple(torch.as_tensor(parameters[name]).shape)}, expected "
+                                  f"{tuple(layout[name].shape)}")
+    added = {name: t.tolist() for name, t in layout.items() if name not in RANK16_NAMES}
+    return {**parameters, **added}
 
 
 def initial_rank16_parameters(seed: int) -> dict:
@@ -138,52 +162,72 @@ def initial_rank16_parameters(seed: int) -> dict:
 
 
 def restored_model(parameters: dict, device, seed: int) -> ExpandedConditionalScore:
-    """Rank-64 scorer from checkpoint parameters; only theta stays trainable (evaluation view)."""
-    theta = torch.tensor(parameters["theta"], device=device)
-    if theta.shape != (NORM_DIM,) or not bool(torch.isfinite(theta).all()) or float(theta.abs().max()) > BOUND + 1e-7:
-        raise ValueError("finite bounded 512 warm weights required")
-    model = ExpandedConditionalScore(theta, seed=seed).to(device)
-    expected = model.state_dict()
-    if set(parameters) != set(expected):
-        raise ValueError("complete rank-64 conditional warm model required")
-    tensors = {k: torch.as_tensor(v, device=device, dtype=expected[k].dtype) for k, v in parameters.items()}
-    for k in expected:
-        if tensors[k].shape != expected[k].shape or not bool(torch.isfinite(tensors[k]).all()):
-            raise ValueError("warm parameter shape or finiteness changed")
-    model.load_state_dict(tensors)
+    """Rank-64 scorer from checkpoint parameters; only theta stays trainable (the evaluation view).
+
+    Every parameter must be present with its shape and finite; theta must lie inside the trust region
+    [-BOUND, BOUND] that training keeps it in."""
+    template = ExpandedConditionalScore(torch.zeros(NORM_DIM), seed=seed).state_dict()
+    _check_names(parameters, set(template), "rank-64 scorer checkpoint")
+    loaded = {}
+    for name, ref in template.items():
+        t = _as_tensor(name, parameters[name], device=device, dtype=ref.dtype)
+        if t.shape != ref.shape:
+            raise CheckpointError(f"rank-64 scorer checkpoint: {name!r} has shape {tuple(t.shape)}, "
+                                  f"expected {tuple(ref.shape)}")
+        loaded[name] = t
+    if float(loaded["theta"].abs().max()) > BOUND + 1e-7:
+        raise CheckpointError(f"rank-64 scorer checkpoint: theta leaves the trust region |theta| <= {BOUND}")
+    model = ExpandedConditionalScore(loaded["theta"], seed=seed).to(device)
+    model.load_state_dict(loaded)
     for name, p in model.named_parameters():
         p.requires_grad_(name == "theta")
     return model
 
 
+def _policy_entries(doc, path: Path):
+    """The `selected` list of a policy document, or an error naming the file."""
+    entries = doc.get("selected") if isinstance(doc, dict) else None
+    if not isinstance(entries, list) or len(entries) == 0:
+        raise CheckpointError(f"policy {path}: 'selected' must be a non-empty list of {{layer, path}} entries")
+    return entries
+
+
 def read_policy(path: Path, layers: tuple[int, ...] = LAYERS) -> dict[int, dict]:
-    """Policy JSON -> {layer: {"layer", "path" (absolute)}}; relative paths resolve beside the policy."""
+    """Policy JSON -> {layer: {"layer", "path" (absolute)}}; relative checkpoint paths resolve beside the policy.
+
+    Each entry names one captured layer (a C4 layer index, at most once) and a non-empty checkpoint path."""
     path = Path(path)
-    policy = json.loads(path.read_text())
-    entries = policy.get("selected") if isinstance(policy, dict) else None
-    if not isinstance(entries, list) or not entries:
-        raise ValueError(f"nonempty selected-policy entries required: {path}")
-    out: dict[int, dict] = {}
-    for e in entries:
-        layer = e.get("layer") if isinstance(e, dict) else None
-        if type(layer) is not int or layer not in layers or layer in out:
-            raise ValueError(f"unique captured policy layers required: {path}: {layer}")
-        if not isinstance(e.get("path"), str) or not e["path"]:
-            raise ValueError(f"checkpoint path required: {path}: layer {layer}")
-        ck = Path(e["path"])
-        if not ck.is_absolute():
-            ck = path.parent / ck
-        out[layer] = {"layer": layer, "path": str(ck.resolve())}
-    return out
+    try:
+        doc = json.loads(path.read_text())
+    except (OSError, json.JSONDecodeError) as exc:
+        raise CheckpointError(f"policy {path}: not a readable JSON file") from exc
+    table: dict[int, dict] = {}
+    for position, entry in enumerate(_policy_entries(doc, path)):
+        if not isinstance(entry, dict):
+            raise CheckpointError(f"policy {path}: entry {position} is not an object")
+        layer, where = entry.get("layer"), entry.get("path")
+        if type(layer) is not int or layer not in layers:
+            raise CheckpointError(f"policy {path}: entry {position} names layer {layer!r}, not a captured layer")
+        if layer in table:
+            raise CheckpointError(f"policy {path}: layer {layer} appears twice")
+        if not isinstance(where, str) or where == "":
+            raise CheckpointError(f"policy {path}: layer {layer} has no checkpoint path")
+        target = Path(where) if Path(where).is_absolute() else path.parent / where
+        table[layer] = {"layer": layer, "path": str(target.resolve())}
+    return table
 
 
 def read_checkpoint(entry: dict) -> dict:
+    """One policy entry's checkpoint record; it must belong to the entry's layer and carry its parameters."""
     path, layer = Path(entry["path"]), entry["layer"]
     try:
         record = json.loads(path.read_text())
-    except OSError as exc:
-        raise ValueError(f"cannot read policy checkpoint: layer {layer}: {path}") from exc
-    if not isinstance(record, dict) or record.get("layer") != layer or not isinstance(
-            record.get("selected_parameters"), dict):
-        raise ValueError(f"complete selected checkpoint required: layer {layer}")
+    except (OSError, json.JSONDecodeError) as exc:
+        raise CheckpointError(f"checkpoint {path} (layer {layer}): not a readable JSON file") from exc
+    if not isinstance(record, dict):
+        raise CheckpointError(f"checkpoint {path} (layer {layer}): not a JSON object")
+    if record.get("layer") != layer:
+        raise CheckpointError(f"checkpoint {path}: records layer {record.get('layer')!r}, the policy says {layer}")
+    if not isinstance(record.get("selected_parameters"), dict):
+        raise CheckpointError(f"checkpoint {path} (layer {layer}): no 'selected_parameters' object")
     return record

@@ -52,15 +52,49 @@ def parameter_groups(model: ExpandedConditionalScore, scale: float) -> list[dict
 
 
 def _load_parameters(model, parameters: dict, device, theta0, bound) -> None:
-    expected = model.state_dict()
-    if set(parameters) != set(expected):
-        raise ValueError("warm model parameter names changed")
-    restored = {k: torch.as_tensor(v, device=device, dtype=expected[k].dtype) for k, v in parameters.items()}
-    if any(restored[k].shape != expected[k].shape or not bool(torch.isfinite(restored[k]).all()) for k in expected):
-        raise ValueError("warm model parameter shapes/values invalid")
-    if not torch.equal(restored["theta"], theta0) or float(restored["theta"].abs().max()) > bound + 1e-7:
-        raise ValueError("warm model theta disagrees with declared initialization/bound")
+    """Warm-start `model` from checkpoint parameters whose theta is the declared initial theta."""
+    layout = model.state_dict()
+    missing, extra = sorted(set(layout) - set(parameters)), sorted(set(parameters) - set(layout))
+    if missing or extra:
+        raise ValueError(f"warm start: missing parameters {missing}, unexpected parameters {extra}")
+    restored = {}
+    for name, ref in layout.items():
+        t = torch.as_tensor(parameters[name], device=device, dtype=ref.dtype)
+        if t.shape != ref.shape or not bool(torch.isfinite(t).all()):
+            raise ValueError(f"warm start: {name!r} must be finite with shape {tuple(ref.shape)}")
+        restored[name] = t
+    if float(restored["theta"].abs().max()) > bound + 1e-7:
+        raise ValueError(f"warm start: theta leaves the trust region |theta| <= {bound}")
+    if not torch.equal(restored["theta"], theta0):
+        raise ValueError("warm start: the checkpoint's theta is not the initial theta given to fit()")
     model.load_state_dict(restored)
+
+
+def _check_fit_arguments(train, development, mode, epochs, bound, train_batch_size, learning_rate_scale,
+                         temperature_start, temperature_end) -> None:
+    """Reject a fit whose settings leave the ranges the recipes use, or whose data splits overlap."""
+    problems = []
+    if mode != "conditional_expanded":
+        problems.append(f"mode {mode!r} (only conditional_expanded is trained)")
+    if not 1 <= epochs <= 100:
+        problems.append(f"epochs {epochs!r} outside 1..100")
+    if not 0 < bound <= 1:
+        problems.append(f"trust-region bound {bound!r} outside (0, 1]")
+    if not isinstance(train_batch_size, int) or not 1 <= train_batch_size <= 16:
+        problems.append(f"train_batch_size {train_batch_size!r} outside 1..16")
+    if not 0 < learning_rate_scale <= 1:
+        problems.append(f"learning_rate_scale {learning_rate_scale!r} outside (0, 1]")
+    if not 0 < temperature_end <= temperature_start <= 0.15:
+        problems.append(f"temperatures {temperature_start!r} -> {temperature_end!r} not a descending schedule "
+                        "inside (0, 0.15]")
+    if not train or not development:
+        problems.append("an empty training or development split")
+    elif any(st.get("role") != "train" for st in train):
+        problems.append("training states not marked role='train'")
+    elif {st["rid"] for st in train} & {st["rid"] for st in development}:
+        problems.append("issues shared by the training and development splits")
+    if problems:
+        raise ValueError("fit: " + "; ".join(problems))
 
 
 def fit(math, ref, train: list[dict], development: list[dict], initial_theta: torch.Tensor, *,
@@ -68,20 +102,12 @@ def fit(math, ref, train: list[dict], development: list[dict], initial_theta: to
         checkpoint=None, initial_parameters: dict | None = None, learning_rate_scale: float = 1.0,
         temperature_start: float = 0.03, temperature_end: float = 0.015, train_batch_size: int = 1,
         gradient_mode: str = "straight_through", device=None, scratch_root: Path | None = None) -> dict:
-    if mode != "conditional_expanded" or not 0 < bound <= 1 or not 1 <= epochs <= 100:
-        raise ValueError("explicit scoring mode and bounded trust region required")
-    if not isinstance(train_batch_size, int) or not 1 <= train_batch_size <= 16:
-        raise ValueError("explicit bounded training batch size required")
-    if not 0 < learning_rate_scale <= 1 or not 0 < temperature_end <= temperature_start <= 0.15:
-        raise ValueError("bounded learning-rate scale and descending positive temperatures required")
-    if not train or not development or any(s.get("role") != "train" for s in train):
-        raise ValueError("nonempty labeled training and development sets required")
-    if {s["rid"] for s in train} & {s["rid"] for s in development}:
-        raise ValueError("issue leakage")
+    _check_fit_arguments(train, development, mode, epochs, bound, train_batch_size, learning_rate_scale,
+                         temperature_start, temperature_end)
     device = torch.device(device) if device is not None else train[0]["raw"].device
     theta0 = initial_theta.detach().to(device)
     if theta0.shape != (512,) or not bool(torch.isfinite(theta0).all()) or float(theta0.abs().max()) > bound + 1e-7:
-        raise ValueError("invalid initial weights")
+        raise ValueError(f"fit: initial theta must be 512 finite values with |theta| <= {bound}")
     model = ExpandedConditionalScore(theta0, seed=seed).to(device)
     if initial_parameters is not None:
         _load_parameters(model, initial_parameters, device, theta0, bound)
@@ -91,7 +117,7 @@ def fit(math, ref, train: list[dict], development: list[dict], initial_theta: to
     base_metrics, _ = measure(math, ref, development, baseline)
     warm_metrics, _ = measure(math, ref, development, warm)
     if initial_parameters is not None and not validation_acceptable(warm_metrics, base_metrics):
-        raise ValueError("warm candidate violates the TopMag mean/p95 guard")
+        raise ValueError("fit: the warm start is worse than TopMag on the development split (mean or p95)")
     with StateBatches(train, device, train_batch_size, scratch_root) as batches:
         obj = select_objective(math, ref, model, gradient_mode)
         if obj.anchored:
@@ -104,7 +130,7 @@ def fit(math, ref, train: list[dict], development: list[dict], initial_theta: to
             if gradient_mode == "straight_through":
                 torch.testing.assert_close(sur.detach(), exact.detach(), atol=0, rtol=0)
             if not all(bool(torch.isfinite(g).all()) for g in torch.autograd.grad(sur, params)):
-                raise ValueError("candidate gradient preflight failed")
+                raise ValueError("fit: the first training state's gradient has non-finite entries")
         batch_check = None
         if train_batch_size > 1:
             with batches.stage(range(min(train_batch_size, len(train)))) as b:
@@ -185,6 +211,14 @@ def fit(math, ref, train: list[dict], development: list[dict], initial_theta: to
         return result
 
 
+def _exact_fp32_matmuls() -> None:
+    """Candidates are ranked by attention errors that differ in the fourth digit: fp32 products stay fp32
+    (no TF32 on either matmul path)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+
+
 def _cache_layers(cache: Path) -> tuple[int, ...]:
     return tuple(json.loads((Path(cache) / "config.json").read_text())["layers"])
 
@@ -193,7 +227,7 @@ def init_policy(cache: Path, output: Path, seed: int = 42) -> dict:
     """Write rank-16 starting checkpoints (theta 0, zero decoders) for every cached layer + a policy."""
     output = Path(output)
     if output.exists():
-        raise ValueError("new output directory required; historical runs are never overwritten")
+        raise ValueError(f"{output} exists: init_policy writes into a new directory only")
     output.mkdir(parents=True)
     entries = []
     for layer in _cache_layers(cache):
@@ -207,22 +241,23 @@ def init_policy(cache: Path, output: Path, seed: int = 42) -> dict:
 
 def run(cache: Path, policy: Path, output: Path, *, recipe: str, layers: tuple[int, ...], device: str = "cpu",
         threads: int = 4, epochs: int | None = None) -> dict:
-    if recipe not in RECIPES or threads < 1 or device not in ("cpu", "cuda"):
-        raise ValueError("known recipe, positive thread count and explicit cpu/cuda device required")
+    if recipe not in RECIPES:
+        raise ValueError(f"recipe {recipe!r} is not one of {sorted(RECIPES)}")
+    if threads < 1 or device not in ("cpu", "cuda"):
+        raise ValueError(f"threads {threads!r} / device {device!r}: need threads >= 1 and device cpu or cuda")
     output = Path(output)
     if output.exists():
-        raise ValueError("new output directory required; historical runs are never overwritten")
+        raise ValueError(f"{output} exists: a training run writes into a new directory only")
     if device == "cuda" and not torch.cuda.is_available():
-        raise ValueError("CUDA requested but unavailable; no silent CPU fallback")
+        raise ValueError("device cuda was asked for but no GPU is visible (training does not fall back to the CPU)")
     math, ref = Math(), reference()
     torch.set_num_threads(threads)
-    torch.backends.cuda.matmul.allow_tf32 = False
-    torch.set_float32_matmul_precision("highest")
+    _exact_fp32_matmuls()
     allowed = _cache_layers(cache)
     selected = read_policy(Path(policy), allowed)
     missing = sorted(set(layers) - selected.keys())
     if missing:
-        raise ValueError(f"policy missing requested layers: {missing}")
+        raise ValueError(f"the policy has no checkpoint for layers {missing}")
     records = {layer: read_checkpoint(e) for layer, e in selected.items() if layer in layers}
     settings = dict(RECIPES[recipe])
     if epochs is not None:
