@@ -412,6 +412,88 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       : "memory");
 }
 
+// Shared -> global bulk copy (16-byte aligned addresses, size a multiple of 16), tracked by the issuing
+// thread's bulk group: commit, then wait for the group before the source is overwritten or the CTA exits.
+__device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every committed bulk group of this thread complete (writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Programmatic dependent launch: wait until the grids this launch depends on have completed and their
+// memory is visible (a no-op for a launch without the attribute), and allow dependent grids to start.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------- thread-block clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// all threads of every CTA of the cluster: arrive (release) and wait (acquire); shared-memory writes made
+// before it are visible to the other CTAs' distributed-shared-memory reads after it
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the address of the same shared-memory location in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float dsmem_ld_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 dsmem_ld_u32x4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+// the two halves of cluster_sync, for work between them
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+// arrive without ordering this thread's memory operations (the barrier only orders execution)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+// Bulk copy from this CTA's shared memory to CTA-cluster shared memory (`dst_cluster`, `bar_cluster` from
+// dsmem_addr): the bytes complete_tx on that CTA's mbarrier.  16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                               uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
+// Asynchronous store of two floats to CTA-cluster shared memory, completing 8 bytes on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_f32x2(uint32_t dst_cluster, float a, float b, uint32_t bar_cluster) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   dst_cluster),
+               "f"(a), "f"(b), "r"(bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ float4 dsmem_ld_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // ----------------------------------------------------------------------------- conversions
 // Two fp32 -> packed e4m3x2 (round to nearest even, saturate to finite). lo -> byte 0.
 __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {

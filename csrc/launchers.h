@@ -40,7 +40,7 @@ struct DecodeParams {
   int64_t freq_rows;
   float scale_log2;          // softmax scale * log2(e)
   float* part_o;             // [B, splits, H, 512] (num_splits > 1)
-  float* part_ml;            // [B, splits, H, 2]   (num_splits > 1)
+  float* part_ml;            // [B, splits, H, 2]   (decode_uses_partials(num_splits))
   int* err;
   // set by launch_sparse_mla_decode from its arguments
   const float* sink;         // [H]
@@ -53,6 +53,18 @@ struct DecodeParams {
 
 void launch_sparse_mla_decode(const DecodeParams& p, const float* sink, const int32_t* q_pos,
                               __nv_bfloat16* out, float* lse, cudaStream_t stream);
+
+// Split-KV counts whose CTAs form one thread-block cluster and merge their partials in distributed shared
+// memory (no partial buffers, no combine launch); other counts above one write fp32 partials (part_o,
+// part_ml) that the combine kernel merges.
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline bool decode_splits_clustered(int splits) { return splits == 2 || splits == 4 || splits == 8; }
+inline bool decode_uses_partials(int splits) { return splits > 1 && !decode_splits_clustered(splits); }
+// How many clusters of `cluster` decode CTAs can be resident at once on the current device (0 if the
+// size cannot be launched).
+int decode_max_active_clusters(int cluster);
 
 void launch_umma_probe(const void* a, const void* b, int K, int N, int mode, float* d, int* err, cudaStream_t stream);
 

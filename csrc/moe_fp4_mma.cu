@@ -1,11 +1,10 @@
 // MXFP4 routed experts for decode-sized token counts (<= 16 tokens per expert per pass).
 //
 // Reference behaviour: FlashInfer `Mxfp4FlashinferCutlassMoEMethod`.  At decode batch sizes
-// an expert sees ~1-4 tokens, so the layer is a stream of the active experts' E2M1 weights.  The
-// tcgen05 kernel (moe_fp4_tc.cu) pays ~110 cycles per M=128/N=16/K=16 MMA with its weight operand
-// in tensor memory, i.e. ~1 us per 16 KB weight tile, 2.6x the HBM time of the tile.  This kernel
-// instead dequantizes the weights straight into register A fragments of m16n8k16 MMAs, so each
-// weight byte is touched once after landing in shared memory.
+// an expert sees ~1-4 tokens, so the layer is a stream of the active experts' E2M1 weights.  This
+// is the BF16-activation variant (expert_format "bf16"); the default MXFP8 x MXFP4 block-scaled
+// tcgen05 kernel is csrc/moe_mxf4.cu.  Here the weights are dequantized straight into register A
+// fragments of m16n8k16 MMAs, so each weight byte is touched once after landing in shared memory.
 //
 // Weight layout (packmla/ops/moe.py: tile_fp4_frag), per tile of 128 rows x 256 k (16 KB + 1 KB):
 //   warp (k-slice ks in 0..3 = 64 k, row half rh = 64 rows) owns 4 m16 tiles x 4 k16 steps;
@@ -13,7 +12,7 @@
 //     (row g, k 2q) (row g + 8, k 2q) (row g, k 2q + 8) (row g + 8, k 2q + 8)  (g = lane / 4,
 //     q = lane % 4, k relative to the step) -- exactly the A fragment a0..a7 after cvt.e2m1x2;
 //   scales  [ks][rh][g][mt][block][2 B]: UE8M0 of rows (g, g + 8) for the two 32-k blocks.
-// Token rows: the padded per-expert slot layout of moe_fp4_tc.cu (8 KB per 16-token, 256-k tile).
+// Token rows: padded per-expert slots gathered by moe_gather_slots_kernel (8 KB per 16-token, 256-k tile).
 //
 // CTA = 8 MMA warps + 1 loader warp (cp.async.bulk ring of 6 stages x 25 KB).  Per pass the
 // warps' K-slice partials (4 x [128 rows x 16 tokens]) are summed through shared memory; gate/up

@@ -14,6 +14,9 @@
 //   * Scratch is a file-scope device array of PACKMLA_NOALLOC_MAX_PARTS partial rows; one partial
 //     row is one (query, KV split, head) triple, so B * num_splits * H must not exceed the limit.
 //     Every GPU that loads the library holds the array (8 MiB + 32 KiB) until the process exits.
+//     Split counts 2, 4 and 8 merge their partials inside a thread-block cluster and leave the array
+//     untouched; the limit applies to every call all the same, so a caller's sizes do not depend on
+//     which merge a split count takes.
 //   * The first call on a device looks up the array's device address on that device (host code
 //     cannot use the array's name as a device pointer).  Make that first call before any stream
 //     capture on the device; the caller's current device must own the tensors.

@@ -69,7 +69,7 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
                        torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse,
                        torch::Tensor err, c10::optional<torch::Tensor> prof) {
   constexpr int kHG = 64;
-  if (prof) TORCH_CHECK(prof->is_cuda() && prof->scalar_type() == torch::kInt64 && prof->numel() >= 48);
+  if (prof) TORCH_CHECK(prof->is_cuda() && prof->scalar_type() == torch::kInt64 && prof->numel() >= 64);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
   TORCH_CHECK(q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
               "q rows must be 16-byte aligned");
@@ -85,13 +85,15 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   TORCH_CHECK(sink.scalar_type() == torch::kFloat32 && sink.numel() == H && sink.is_contiguous());
   TORCH_CHECK(q_pos.scalar_type() == torch::kInt32 && q_pos.numel() == B && q_pos.is_contiguous());
   TORCH_CHECK(num_splits >= 1);
-  if (num_splits > 1) {
+  if (decode_uses_partials((int)num_splits)) {
     TORCH_CHECK(part_o.is_cuda() && part_o.scalar_type() == torch::kFloat32 &&
                 part_o.numel() >= (int64_t)B * num_splits * H * kD, "part_o too small for the split partials");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(part_o.data_ptr()) % 16 == 0, "part_o must be 16-byte aligned");
     TORCH_CHECK(part_ml.is_cuda() && part_ml.scalar_type() == torch::kFloat32 &&
                 part_ml.numel() >= (int64_t)B * num_splits * H * 2, "part_ml too small for the split partials");
   }
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)B * H * kD);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out must be 16-byte aligned (bulk-copied rows)");
   TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.numel() == (int64_t)B * H);
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(q.device());
@@ -129,8 +131,8 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.freqs = freqs.data_ptr<float>();
   p.freq_rows = freqs.size(0);
   p.scale_log2 = (float)scale * 1.4426950408889634f;
-  p.part_o = num_splits > 1 ? part_o.data_ptr<float>() : nullptr;
-  p.part_ml = num_splits > 1 ? part_ml.data_ptr<float>() : nullptr;
+  p.part_o = decode_uses_partials((int)num_splits) ? part_o.data_ptr<float>() : nullptr;
+  p.part_ml = decode_uses_partials((int)num_splits) ? part_ml.data_ptr<float>() : nullptr;
   p.err = err.data_ptr<int>();
   p.prof = prof ? reinterpret_cast<unsigned long long*>(prof->data_ptr<int64_t>()) : nullptr;
   launch_sparse_mla_decode(p, sink.data_ptr<float>(), q_pos.data_ptr<int32_t>(),
@@ -653,6 +655,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act_s"), py::arg("out"), py::arg("err"), py::arg("prof") = py::none());
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
+  m.def("decode_max_active_clusters", [](int64_t cluster) {
+    TORCH_CHECK(decode_splits_clustered((int)cluster), "cluster size must be 2, 4 or 8");
+    return decode_max_active_clusters((int)cluster);
+  }, "co-resident decode clusters of the given size on the current device");
   m.def("sparse_mla_decode", &sparse_mla_decode, "Sparse MLA decode (tcgen05) + split combine", py::arg("q"),
         py::arg("swa_pool"), py::arg("swa_slots"), py::arg("swa_len"), py::arg("csa_packed"), py::arg("csa_pool"),
         py::arg("csa_values"), py::arg("csa_bitmap"), py::arg("csa_scales"), py::arg("csa_slots"), py::arg("csa_pos"),

@@ -212,7 +212,7 @@ def bench_decode(args, dev):
                   freqs=freqs, sink=torch.zeros(Hh, device=dev), scale=512 ** -0.5,
                   q_pos=torch.full((B,), args.context - 1, dtype=torch.int32, device=dev), csa_pool=pool,
                   csa_planes=planes)
-    splits = attn_ops.choose_splits(B, Hh, max(W, 1) + K)
+    splits = args.splits or attn_ops.choose_splits(B, Hh, max(W, 1) + K, max_clusters=attn_ops.max_active_clusters(dev))
     ws = attn_ops.DecodeWorkspace(B, Hh, splits, dev)
     out = torch.empty(B, Hh, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, Hh, dtype=torch.float32, device=dev)
@@ -240,7 +240,9 @@ def bench_decode(args, dev):
     check_errors(dev)
     stamps = None
     if args.prof and args.kv_format != "adapter":
-        prof = torch.zeros(48, dtype=torch.int64, device=dev)
+        prof = torch.zeros(64, dtype=torch.int64, device=dev)
+        prof[59] = 2 ** 63 - 1  # earliest CTA start (atomic min)
+        prof[46] = 2 ** 63 - 1  # earliest staged epilogue (atomic min)
         if args.protocol != "reference":  # the reference protocol's stamps come from a warm run
             L2Flush(dev)()
         attn_ops.sparse_mla_decode(q, swa_pool, workspace=ws, out=out, lse=lse, prof=prof, **args_d)
@@ -254,7 +256,16 @@ def bench_decode(args, dev):
         stamps.update({f"X0.{n}": round((pv[36 + i] - t0) / 1e3, 2) for i, n in
                        enumerate(["start", "scores", "maxima", "probs", "m_updated", "p_computed"]) if pv[36 + i]})
         stamps.update({"epilogue": round((pv[34] - t0) / 1e3, 2), "end": round((pv[35] - t0) / 1e3, 2),
-                       "unit": "us after CTA 0 start"})
+                       "unit": "us after the start of the last split of query 0, head group 0"})
+        extra = {44: "L1.fetched", 48: "ep.stats", 49: "ep.tmem_ld", 45: "cl.weights", 50: "ep.staged", 51: "ep.written", 52: "cl.ready", 53: "cl.received",
+                 54: "su.load0", 55: "su.idx1", 56: "su.q_converted"}
+        stamps.update({n: round((pv[i] - t0) / 1e3, 2) for i, n in extra.items() if pv[i]})
+        stamps.update({"cta_first_start": round((pv[59] - t0) / 1e3, 2),
+                       "cta_last_start": round((pv[58] - t0) / 1e3, 2),
+                       "cta_last_end": round((pv[57] - t0) / 1e3, 2)})
+        if pv[47]:
+            stamps.update({"cta_first_staged": round((pv[46] - t0) / 1e3, 2),
+                           "cta_last_staged": round((pv[47] - t0) / 1e3, 2)})
     flops = 4 * B * Hh * (K + W) * 512
     peak, tag = measured_hbm_gbs()
     gbs = nbytes / us / 1e3
@@ -411,6 +422,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--precision", default="default", choices=["default", "bf16"])
     ap.add_argument("--prof", action="store_true", help="report kernel phase / wait-time counters")
+    ap.add_argument("--splits", type=int, default=0, help="decode: KV splits (0 = the automatic choice)")
     ap.add_argument("--paired", action="store_true", help="decode-suite: native and direct in paired rounds")
     ap.add_argument("--protocol", default="cold", choices=["cold", "reference"],
                     help="decode: 'cold' times one graph replay per sample with L2 flushed before it; 'reference' "

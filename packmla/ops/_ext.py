@@ -11,8 +11,19 @@ _EXT = None
 _ERR: dict[int, torch.Tensor] = {}
 
 
-# kernels launched per extension entry point (for the bench's launch count)
-KERNELS_PER_CALL = {"native_store": 1, "packed_store": 1, "sparse_mla_decode": 2, "moe_fp4": 3, "moe_fp4_mma": 4, "add_rmsnorm": 1, "bs_probe": 1, "moe_mxf4": 4, "bs_probe2": 1, "rope_q": 1, "comp_pool": 1, "route_topk": 1, "silu_mul": 1, "index_key_store": 1, "index_select": 2, "umma_probe": 1, "gemm_allreduce": 1, "allreduce": 1}
+# split counts whose decode CTAs form one thread-block cluster and merge in distributed shared memory
+# (one launch); other counts above one write partials that a second (combine) kernel merges
+CLUSTER_SPLITS = (2, 4, 8)
+
+
+def decode_uses_partials(splits: int) -> bool:
+    return splits > 1 and splits not in CLUSTER_SPLITS
+
+
+# kernels launched per extension entry point (for the bench's launch count): a number, or a function of
+# the call's positional arguments
+KERNELS_PER_CALL = {"native_store": 1, "packed_store": 1,
+                    "sparse_mla_decode": lambda a: 2 if decode_uses_partials(int(a[16])) else 1, "moe_fp4": 3, "moe_fp4_mma": 4, "add_rmsnorm": 1, "bs_probe": 1, "moe_mxf4": 4, "bs_probe2": 1, "rope_q": 1, "comp_pool": 1, "route_topk": 1, "silu_mul": 1, "index_key_store": 1, "index_select": 2, "umma_probe": 1, "gemm_allreduce": 1, "allreduce": 1}
 
 
 class _Counting:
@@ -30,7 +41,7 @@ class _Counting:
         per = KERNELS_PER_CALL.get(name, 1)
 
         def wrapped(*a, **k):
-            self.launches += per
+            self.launches += per(a) if callable(per) else per
             return fn(*a, **k)
 
         return wrapped

@@ -12,7 +12,7 @@ import torch
 
 from ..formats import abi, codec
 from ..oracle import attention as oracle
-from ._ext import error_word, ext
+from ._ext import CLUSTER_SPLITS, decode_uses_partials, error_word, ext
 from .kv import native_pool_read
 
 NUM_SMS_B200 = 148
@@ -27,28 +27,62 @@ class PackedPlanes:
     scales: torch.Tensor  # uint8 [rows, 8]
 
 
-def choose_tiling(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> tuple[int, int]:
+_MAX_CLUSTERS: dict[int, dict[int, int]] = {}
+
+
+def max_active_clusters(device=None) -> dict[int, int]:
+    """Co-resident decode clusters of 2, 4 and 8 CTAs on `device` (queried once per device)."""
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    got = _MAX_CLUSTERS.get(idx)
+    if got is None:
+        with torch.cuda.device(idx):
+            got = {s: int(ext().decode_max_active_clusters(s)) for s in CLUSTER_SPLITS}
+        _MAX_CLUSTERS[idx] = got
+    return got
+
+
+def choose_tiling(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200,
+                  max_clusters: dict[int, int] | None = None) -> tuple[int, int]:
     """(KV splits per (query, head group), KV rows per tile).
 
-    As many splits as fill one wave of one CTA per SM, each at least one 128-row tile; with one split the
-    kernel writes the output itself (no partials, no combine launch)."""
+    One CTA per SM, one wave.  A split count of 2, 4 or 8 makes the splits of a (query, head group) one
+    thread-block cluster that merges its partials on chip; the smallest such size that gives every split at
+    most one 128-row tile is taken if its clusters are co-resident (`max_clusters`: size -> clusters), else
+    the largest that is.  More than 8 tiles with room for more than 8 splits: one tile per split through
+    the partial buffers and the combine kernel.  One split writes the output directly."""
     groups = (heads + HEAD_GROUP - 1) // HEAD_GROUP
     work = max(1, batch * groups)
     tiles = max(1, math.ceil(max_rows / TILE_ROWS))
-    return max(1, min(tiles, num_sms // work)), TILE_ROWS
+    if tiles == 1:
+        return 1, TILE_ROWS
+    fit = num_sms // work
+    mc = max_clusters or {s: num_sms // s for s in CLUSTER_SPLITS}
+    sizes = [s for s in CLUSTER_SPLITS if s <= fit and work <= mc.get(s, 0)]
+    if tiles > CLUSTER_SPLITS[-1] and fit > CLUSTER_SPLITS[-1]:
+        return min(tiles, fit), TILE_ROWS
+    if not sizes:
+        return 1, TILE_ROWS
+    for s in sizes:
+        if s >= tiles:
+            return s, TILE_ROWS
+    return sizes[-1], TILE_ROWS
 
 
-def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200) -> int:
-    return choose_tiling(batch, heads, max_rows, num_sms)[0]
+def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200,
+                  max_clusters: dict[int, int] | None = None) -> int:
+    return choose_tiling(batch, heads, max_rows, num_sms, max_clusters)[0]
 
 
 class DecodeWorkspace:
-    """Split-KV partials with stable pointers (safe to capture in CUDA graphs); empty with one split."""
+    """Split-KV partials with stable pointers (safe to capture in CUDA graphs); empty when the splits merge
+    inside a cluster or there is one split."""
 
     def __init__(self, batch: int, heads: int, splits: int, device, tile_rows: int = TILE_ROWS):
         self.splits = splits
         self.tile_rows = tile_rows
-        n = batch * splits * heads if splits > 1 else 0
+        n = batch * splits * heads if decode_uses_partials(splits) else 0
         self.part_o = torch.empty(n * abi.LATENT_DIM, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(n * 2, dtype=torch.float32, device=device)
 
@@ -78,7 +112,7 @@ def sparse_mla_decode(
     SWA rows: Native records at `swa_slots` [B, W] (first `swa_len[b]` used; -1 = masked).
     C4 rows: `csa_slots` [B, K] physical records, `csa_pos` [B, K] token positions (RoPE rows
     for Packed), first `csa_len[b]` used.  Exactly one of csa_pool (Native pages) /
-    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].  `prof` (optional int64 [48] on the
+    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].  `prof` (optional int64 [64] on the
     device) receives global-timer stamps of the first CTA's pipeline steps, for latency analysis.
     """
     if (csa_pool is None) == (csa_planes is None):
@@ -91,7 +125,8 @@ def sparse_mla_decode(
         if workspace is not None:
             num_splits = workspace.splits
         else:
-            num_splits = choose_splits(B, H, swa_slots.shape[1] + csa_slots.shape[1])
+            num_splits = choose_splits(B, H, swa_slots.shape[1] + csa_slots.shape[1],
+                                       max_clusters=max_active_clusters(q.device))
     if workspace is None or workspace.splits != num_splits:
         workspace = DecodeWorkspace(B, H, num_splits, q.device)
     if out is None:

@@ -106,11 +106,13 @@ def _build_cache(seed, n_swa_rows, n_csa_rows, packed):
                                                   (2, 128, 512, 3, 0.5), (1, 8, 40, None, 0.5),
                                                   (2, 64, 512, 1, 0.5), (3, 64, 317, 2, 0.5),
                                                   (1, 64, 1536, 1, 0.5), (2, 64, 1024, 1, 24.0),
-                                                  (2, 32, 700, 3, 24.0)])
+                                                  (2, 32, 700, 3, 24.0), (2, 32, 700, 4, 24.0),
+                                                  (1, 64, 1536, 8, 0.5), (2, 64, 512, 16, 0.5)])
 def test_sparse_decode_matches_oracle(cuda, packed, B, H, K, splits, qscale):
-    """GPU decode vs the fp32 oracle.  One split runs every 64-row stage of a query in one CTA (both
-    producer groups, direct output); several splits go through the partials and the combine kernel; a large
-    query scale makes the per-head maxima grow from stage to stage, so the O rescale in TMEM runs."""
+    """GPU decode vs the fp32 oracle.  One split runs every 128-row tile of a query in one CTA and writes the
+    output; 2, 4 or 8 splits are one thread-block cluster that merges in distributed shared memory (some
+    splits with no tile, a head group short of 64); other counts go through the partials and the combine
+    kernel; a large query scale makes the per-head maxima grow from tile to tile, so the O rescale runs."""
     seed = B * 1000 + H + K + int(packed)
     g = torch.Generator().manual_seed(seed)
     W = 128

@@ -152,9 +152,10 @@ def test_noalloc_accepts_exactly_the_scratch_limit(cuda):
 
     lib = _lib()
     assert lib.packmla_noalloc_max_parts() == 4096
-    c = _case(15, True, B=16, H=64, K=128, W=64)
-    ref_o, ref_lse = attn_ops.sparse_mla_decode(num_splits=4, **c)
-    out, lse = _call_noalloc(lib, c, 4)
+    # 16 splits (not a cluster size): every (query, split, head) row of the scratch is written and read
+    c = _case(15, True, B=4, H=64, K=128, W=64)
+    ref_o, ref_lse = attn_ops.sparse_mla_decode(num_splits=16, **c)
+    out, lse = _call_noalloc(lib, c, 16)
     assert torch.equal(out, ref_o) and torch.equal(lse, ref_lse)
 
 
