@@ -25,7 +25,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import sys
 import time
@@ -34,7 +33,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode output tok/s (32k in/256 out)"
-DEFAULT_CONCURRENCY = {1: 8, 2: 8, 4: 24, 8: 40}
 
 
 def build_identity() -> dict:
@@ -132,10 +130,11 @@ def main() -> None:
 
     import torch
 
+    from packmla.bench.engine_setup import DEFAULT_CONCURRENCY, build_engine
     from packmla.bench.timing import ClockSampler
     from packmla.config import EngineConfig, ModelConfig
-    from packmla.engine.engine import Engine, SamplingParams
-    from packmla.kv.pool import bytes_per_full_token, fixed_bytes, plan_capacity
+    from packmla.engine.engine import SamplingParams
+    from packmla.kv.pool import plan_capacity
     from packmla.ops import _ext, check_errors
     from packmla.parallel.comm import TPComm, init_from_env
 
@@ -154,17 +153,9 @@ def main() -> None:
         comm = FusedComm(device, cfg.hidden_size, gemm=args.oproj_gemm)
     else:
         comm = TPComm()
-    max_context = args.prompt_len + args.output_len + 256
-    buckets = [b for b in (1, 2, 4, 8, 16, 24, 32, 40, 48, 64) if b < C] + [C]
-    ecfg = EngineConfig(kv_cache_format=args.kv_format, tp=world, ep=world, max_running_requests=C,
-                        cuda_graph_bs=buckets, chunked_prefill_size=8192, prefix_cache=True)
-    pages_per_req = math.ceil(max_context / 256)
-    bpt = bytes_per_full_token(cfg, args.kv_format, ecfg.swa_full_tokens_ratio)
-    kv_bytes = int((C * pages_per_req + 8) * 256 * bpt) + fixed_bytes(cfg, C + 1) + (64 << 20)
-
     t0 = time.time()
-    eng = Engine.build(cfg, ecfg, device, rank, world, comm, max_context=max_context, max_requests=C,
-                       kv_bytes=kv_bytes, seed=args.seed)
+    eng, max_context = build_engine(cfg, device, rank, world, comm, C, args.prompt_len, args.output_len,
+                                    args.kv_format, args.seed)
     eng.runner.capture()
     torch.cuda.synchronize(device)
     # kernel launches of one decode step (an eager forward at the dummy slot, counted by the extension proxy)

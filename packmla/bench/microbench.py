@@ -398,15 +398,53 @@ def bench_store(args, dev):
     v = torch.zeros(4 * R, 256, dtype=torch.uint8, device=dev)
     bm = torch.zeros(4 * R, 8, dtype=torch.int64, device=dev)
     sc = torch.zeros(4 * R, 8, dtype=torch.uint8, device=dev)
-    native = time_op(lambda: kv_ops.native_store(raw, w, 1e-6, slots, pos, freqs, pool), args.rounds, args.warmup,
-                     dev, None)
-    packed = time_op(lambda: kv_ops.packed_store(raw, w, 1e-6, slots, v, bm, sc), args.rounds, args.warmup, dev, None)
-    return {"case": "kv_store", "rows": R, "native_us": round(native, 3), "packed_us": round(packed, 3)}
+    fn_n = lambda: kv_ops.native_store(raw, w, 1e-6, slots, pos, freqs, pool)  # noqa: E731
+    fn_p = lambda: kv_ops.packed_store(raw, w, 1e-6, slots, v, bm, sc)  # noqa: E731
+    if args.protocol == "reference":
+        native = time_op_replays(fn_n, args.rounds, args.warmup, dev)
+        packed = time_op_replays(fn_p, args.rounds, args.warmup, dev)
+    else:
+        native = time_op(fn_n, args.rounds, args.warmup, dev, None)
+        packed = time_op(fn_p, args.rounds, args.warmup, dev, None)
+    return {"case": "kv_store", "rows": R, "protocol": args.protocol, "native_us": round(native, 3),
+            "packed_us": round(packed, 3)}
+
+
+def bench_index(args, dev):
+    """Indexer of one C4 layer: B queries x 64 heads x 128 over the `context` / 4 records of each query's
+    request (FP8 keys), logits + top-k (csrc/indexer.cu), V4-Flash shapes."""
+    from packmla.config import ModelConfig
+    from packmla.ops import indexer as idx_ops
+
+    cfg = ModelConfig()
+    B, R = args.batch, args.context // 4
+    K = args.topk or cfg.index_topk
+    g = torch.Generator(device=dev).manual_seed(0)
+    keys = torch.zeros(B * R, 128, dtype=torch.uint8, device=dev)
+    scales = torch.zeros(B * R, dtype=torch.float32, device=dev)
+    idx_ops.index_key_store(torch.randn(B * R, 128, device=dev, generator=g), torch.arange(B * R, device=dev),
+                            keys, scales)
+    phys = (torch.arange(B, device=dev)[:, None] * R + torch.arange(R, device=dev)[None]).int().contiguous()
+    count = torch.full((B,), R, dtype=torch.int64, device=dev)
+    q = torch.randn(B, cfg.index_heads, cfg.index_dim, device=dev, generator=g).bfloat16()
+    w = torch.rand(B, cfg.index_heads, device=dev, generator=g)
+    fn = lambda: idx_ops.index_select(q, w, keys, scales, phys, count, R, K)  # noqa: E731
+    if args.protocol == "reference":
+        us = time_op_replays(fn, args.rounds, args.warmup, dev)
+    else:
+        us = time_op(fn, args.rounds, args.warmup, dev, L2Flush(dev), graph=True)
+    nbytes = B * R * (128 + 4 + 4) + B * cfg.index_heads * cfg.index_dim * 2 + B * K * 8
+    peak, tag = measured_hbm_gbs()
+    gbs = nbytes / us / 1e3
+    flops = 2 * B * R * cfg.index_heads * cfg.index_dim
+    return {"case": "index_select", "protocol": args.protocol, "batch": B, "context": args.context, "records": R,
+            "topk": K, "heads": cfg.index_heads, "us": round(us, 2), "bytes": nbytes, "GBps": round(gbs, 1),
+            "hbm_fraction": round(gbs / peak, 3), "fp8_TFLOPs": round(flops / us / 1e6, 1), "peak_note": tag}
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "decode", "store", "decode-suite", "decode-paired", "judge"],
+    ap.add_argument("case", choices=["moe", "decode", "store", "index", "decode-suite", "decode-paired", "judge"],
                     help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
                          "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
@@ -446,6 +484,8 @@ def main(argv=None):
     elif args.case == "decode":
         args.topk = args.topk or 2048
         out = bench_decode(args, dev)
+    elif args.case == "index":
+        out = bench_index(args, dev)
     elif args.case == "decode-paired":
         args.topk = args.topk or 2048
         modes = ("native", "direct", "adapter") if args.with_adapter else ("native", "direct")

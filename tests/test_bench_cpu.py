@@ -211,3 +211,24 @@ def test_bench_phase_runs_every_request_to_its_length():
     assert st["wall_s"] > 0 and st["engine_steps"] >= 3 * C * 4
     eng.flush_cache()
     assert not eng.retained
+
+
+def test_step_breakdown_groups_kernels_into_families():
+    from packmla.bench.step_breakdown import family
+
+    assert family("void (anonymous namespace)::mx_expert_kernel<0, 16>(CUtensorMap_st)") == "MoE experts (MXFP4)"
+    assert family("(anonymous namespace)::moe_gather_slots_kernel(int const*)") == "MoE experts (MXFP4)"
+    assert family("(anonymous namespace)::sparse_mla_decode_kernel(DecodeParams)") == "attention (sparse MLA decode)"
+    assert family("(anonymous namespace)::index_logits_kernel(LogitParams)") == "indexer"
+    assert family("nvjet_tst_32x64_64x16_4x1_v_bz_TNN") == "dense GEMM (cuBLAS)"
+    assert family("void at::native::vectorized_elementwise_kernel<4>") == "sampling / torch elementwise"
+    assert family("something_else") == "other"
+
+
+def test_engine_graph_buckets_end_at_the_concurrency():
+    from packmla.bench.engine_setup import DEFAULT_CONCURRENCY, graph_buckets
+
+    assert graph_buckets(8) == [1, 2, 4, 8]
+    assert graph_buckets(40) == [1, 2, 4, 8, 16, 24, 32, 40]
+    assert graph_buckets(5) == [1, 2, 4, 5]
+    assert DEFAULT_CONCURRENCY == {1: 8, 2: 8, 4: 24, 8: 40}
