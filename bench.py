@@ -115,6 +115,8 @@ def main() -> None:
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--dense-format", default="bf16", choices=["bf16", "fp8"],
+                    help="dense projections: BF16 (cuBLAS) or MXFP8 weights (packmla's tcgen05 GEMM)")
     ap.add_argument("--collectives", default="auto", choices=["auto", "fused", "nccl"],
                     help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL; auto = fused "
                          "at the world sizes the fused kernels were validated on (2), NCCL otherwise")
@@ -143,7 +145,7 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    cfg = ModelConfig()
+    cfg = ModelConfig(dense_format=args.dense_format)
     C = args.concurrency or DEFAULT_CONCURRENCY.get(world, 8 * world)
     if args.collectives == "auto":
         args.collectives = "fused" if world == 2 else "nccl"
@@ -230,6 +232,7 @@ def main() -> None:
             "collectives": (f"{args.collectives}/oproj-{args.oproj_gemm}" if args.collectives == "fused"
                             else args.collectives) if world > 1 else "none",
             "kv_cache_format": args.kv_format,
+            "dense_format": args.dense_format,
             "l2": ("inputs larger than L2: every decode step streams the routed experts its tokens select (up to "
                    "~108 GB / N of MXFP4 weights) and each request's selected KV rows of 43 layers"),
             "vs_baseline_note": ("the reference publishes no 32k/256 decode number (its README's 32k/256/C2 "

@@ -185,6 +185,34 @@ struct ArParams {
 
 int make_tmap_bf16_sw128(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
                          uint32_t box_rows);
+int make_tmap_u8_sw128(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
+                       uint32_t box_rows);
+
+// Dense projections with MXFP8 weights (csrc/dense_mx.cu): y[b] = x[b] W[b]^T for `batch` independent
+// (x, W) pairs, x [T, K] BF16 quantized per token to MXFP8 (E4M3 + UE8M0 per 32), W [N, K] E4M3 codes with
+// their UE8M0 scales pre-arranged per (256-row tile, 128-K group).  With K splits every split stores its fp32
+// partial and the split that finishes a tile last sums them in split order (deterministic) into BF16 y.
+struct DenseMxArgs {
+  const __nv_bfloat16* x;   // [batch][T][K] (x_stride_b elements between batches, rows of K contiguous)
+  int64_t x_stride_b;
+  int64_t x_stride_t;
+  int T, K, N, batch;
+  const uint8_t* w;         // [batch][N][K] E4M3 codes
+  const uint8_t* w_sf;      // [batch][N/256 tiles][K/128][256][4] UE8M0 (tile rows past N: any value)
+  __nv_bfloat16* y;         // [batch][T][N] (y_stride_t elements between rows)
+  int64_t y_stride_t;
+  int64_t y_stride_b;
+  uint8_t* a_img;           // workspace [batch][K/128][Tp][128] (Tp = T rounded up to 8); unused when the
+  uint32_t* a_sf;           //   GEMM quantizes x itself (dense_mx_fused_quant); [batch][K/128][Tp]
+  float* part;              // workspace [batch][splits][Tp][N_pad] fp32 (only with splits > 1)
+  int32_t* counters;        // workspace [batch][N/256 tiles], zero (left zero)
+  int splits;               // K splits per tile (1 = direct BF16 output)
+  int num_sms;
+  int* err;
+};
+int launch_dense_mx(const DenseMxArgs& a, cudaStream_t stream);
+// Whether the GEMM quantizes the activations itself for these sizes (one launch; x read in place).
+bool dense_mx_fused_quant(int T, int K, int splits);
 int gemm_ar_smem_bytes(int stages);
 int launch_gemm_allreduce(const GemmArParams& p, const void* w, const void* x, int num_sms, cudaStream_t stream);
 int launch_allreduce(const ArParams& p, int num_sms, cudaStream_t stream);

@@ -71,3 +71,19 @@ int make_tmap_bf16_sw128(void* out, const void* base, uint64_t k_elems, uint64_t
                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
+
+// 2-D map over a row-major matrix of bytes (E4M3 codes, K contiguous) with the 128-byte swizzle: a box of
+// 128 values x box_rows rows fills box_rows x 128 bytes in the K-major SW128 layout of the 8-bit tcgen05
+// kinds.  Rows past `rows` read as zero.
+int make_tmap_u8_sw128(void* out, const void* base, uint64_t k_elems, uint64_t rows, uint64_t row_bytes,
+                       uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  const cuuint64_t dims[2] = {k_elems, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return (int)fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}

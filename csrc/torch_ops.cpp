@@ -634,6 +634,60 @@ void packed_to_native(torch::Tensor values, torch::Tensor bitmap, torch::Tensor 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ----------------------------------------------------------------------------- dense MXFP8 projections
+void dense_mx(torch::Tensor x, torch::Tensor w, torch::Tensor w_sf, torch::Tensor y, torch::Tensor a_img,
+              torch::Tensor a_sf, torch::Tensor part, torch::Tensor counters, int64_t splits, torch::Tensor err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 3 && x.stride(2) == 1,
+              "x must be bf16 [batch, T, K] with K contiguous");
+  const int64_t batch = x.size(0), T = x.size(1), K = x.size(2);
+  TORCH_CHECK(w.scalar_type() == torch::kUInt8 && w.dim() == 3 && w.size(0) == batch && w.size(2) == K && w.is_contiguous(),
+              "w must be uint8 E4M3 codes [batch, N, K]");
+  const int64_t N = w.size(1), G = K / 128, tiles_n = (N + 255) / 256, Tp = (T + 7) & ~7;
+  TORCH_CHECK(K % 128 == 0, "K must be a multiple of 128");
+  TORCH_CHECK(splits >= 1 && splits <= G && (splits == 1 || T <= 128), "splits must be 1..K/128 (1 above 128 tokens)");
+  TORCH_CHECK(w_sf.scalar_type() == torch::kUInt8 && w_sf.is_contiguous() && w_sf.numel() == batch * tiles_n * G * 1024,
+              "w_sf must be uint8 [batch, N/256 tiles, K/128, 256, 4]");
+  TORCH_CHECK(y.scalar_type() == torch::kBFloat16 && y.dim() == 3 && y.size(0) == batch && y.size(1) == T &&
+              y.size(2) == N && y.stride(2) == 1, "y must be bf16 [batch, T, N] with N contiguous");
+  if (!dense_mx_fused_quant((int)T, (int)K, (int)splits)) {
+    TORCH_CHECK(a_img.scalar_type() == torch::kUInt8 && a_img.is_contiguous() && a_img.numel() >= batch * G * Tp * 128,
+                "a_img workspace too small");
+    TORCH_CHECK(a_sf.scalar_type() == torch::kInt32 && a_sf.is_contiguous() && a_sf.numel() >= batch * G * Tp,
+                "a_sf workspace too small");
+  }
+  if (splits > 1) {
+    TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.is_contiguous() &&
+                part.numel() >= batch * splits * Tp * tiles_n * 256, "part workspace too small");
+    TORCH_CHECK(counters.scalar_type() == torch::kInt32 && counters.is_contiguous() && counters.numel() >= batch * tiles_n,
+                "counters workspace too small");
+  }
+  if (T == 0 || N == 0 || batch == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  static int num_sms[64] = {0};
+  const int dev = x.get_device();
+  if (num_sms[dev] == 0) num_sms[dev] = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
+  DenseMxArgs a{};
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.x_stride_b = x.stride(0);
+  a.x_stride_t = x.stride(1);
+  a.T = (int)T; a.K = (int)K; a.N = (int)N; a.batch = (int)batch;
+  a.w = w.data_ptr<uint8_t>();
+  a.w_sf = w_sf.data_ptr<uint8_t>();
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.y_stride_t = y.stride(1);
+  a.y_stride_b = y.stride(0);
+  a.a_img = a_img.data_ptr<uint8_t>();
+  a.a_sf = reinterpret_cast<uint32_t*>(a_sf.data_ptr<int32_t>());
+  a.part = splits > 1 ? part.data_ptr<float>() : nullptr;
+  a.counters = splits > 1 ? counters.data_ptr<int32_t>() : nullptr;
+  a.splits = (int)splits;
+  a.num_sms = num_sms[dev];
+  a.err = err.data_ptr<int>();
+  const int rc = launch_dense_mx(a, stream());
+  TORCH_CHECK(rc == 0, "dense_mx launch rejected (", rc, "): sizes or alignment");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -655,6 +709,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act_s"), py::arg("out"), py::arg("err"), py::arg("prof") = py::none());
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
+  m.def("dense_mx", &dense_mx, "dense projections with MXFP8 weights: y[b] = x[b] W[b]^T (tcgen05 block-scaled)");
   m.def("decode_max_active_clusters", [](int64_t cluster) {
     TORCH_CHECK(decode_splits_clustered((int)cluster), "cluster size must be 2, 4 or 8");
     return decode_max_active_clusters((int)cluster);

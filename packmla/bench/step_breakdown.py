@@ -22,6 +22,7 @@ FAMILIES = [
     ("attention (sparse MLA decode)", r"sparse_mla_decode|mla_combine"),
     ("MoE experts (MXFP4)", r"mx_expert|moe_fp4|mx_quant|moe_route|moe_gather|moe_place|moe_count|moe_plan"),
     ("indexer", r"index_logits|index_topk|index_key"),
+    ("dense projections, MXFP8 (packmla)", r"dense_mx|dense_quant"),
     ("routing", r"route_topk"),
     ("dense GEMM (cuBLAS)", r"nvjet|gemm|cutlass|sm90|sm100|cublas|Kernel2"),
     ("norms / RoPE / SiLU (packmla)", r"add_rmsnorm|rope_q|silu_mul|rmsnorm"),
@@ -44,6 +45,7 @@ def main(argv=None) -> dict:
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
     ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--dense-format", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--top", type=int, default=25, help="kernels listed individually")
     args = ap.parse_args(argv)
 
@@ -58,7 +60,7 @@ def main(argv=None) -> dict:
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    cfg = ModelConfig()
+    cfg = ModelConfig(dense_format=args.dense_format)
     C = args.concurrency
     eng, _ = build_engine(cfg, device, 0, 1, TPComm(), C, args.prompt_len, args.output_len, args.kv_format)
     eng.runner.capture()
@@ -108,7 +110,7 @@ def main(argv=None) -> dict:
         fams[family(k)] = fams.get(family(k), 0.0) + v
     out = {
         "case": "decode_step_breakdown", "concurrency": C, "prompt_len": args.prompt_len,
-        "kv_format": args.kv_format, "steps": args.steps, "prefill_s": round(prefill_s, 1),
+        "kv_format": args.kv_format, "dense_format": args.dense_format, "steps": args.steps, "prefill_s": round(prefill_s, 1),
         "graph_step_ms": round(graph_ms, 3), "eager_kernel_ms_per_step": round(total / 1e3, 3),
         "families": {k: {"us_per_step": round(v, 1), "share": round(v / total, 4)}
                      for k, v in sorted(fams.items(), key=lambda kv: -kv[1])},

@@ -11,7 +11,8 @@ Model geometry of DeepSeek-V4-Flash-0731 as far as the reference records it:
   output 16 heads x 512 per TP4 rank, o_proj input 2048 per TP4 rank, shared
   expert intermediate 2048 (DeepGEMM JIT shapes N=1536/8192/4096/1024 at K=4096/1024/2048/512
   in the same log);
-* FP8 e4m3 dense weights, MXFP4 routed experts (`is_fp4_experts=True`, quant=fp8).
+* FP8 e4m3 dense weights, MXFP4 routed experts (`is_fp4_experts=True`, quant=fp8); packmla serves the
+  dense projections in BF16 by default and in MXFP8 with `dense_format="fp8"`.
 
 Values the reference does not contain (routed-expert count, top-k, vocab, indexer
 width, grouped-output split) are documented assumptions sized so the weights
@@ -63,7 +64,10 @@ class ModelConfig:
     rope_theta: float = 10000.0
     max_position: int = 1 << 20
     expert_format: str = "mxfp4"  # "mxfp4" | "bf16" (tiny CPU configs)
-    dense_format: str = "fp8"  # "fp8" | "bf16"
+    # dense projections: "bf16" (cuBLAS) or "fp8" (MXFP8 weights, csrc/dense_mx.cu; the router gate and the LM
+    # head stay BF16).  BF16 is the default: at decode token counts both paths are bound by per-call latency and
+    # the MXFP8 kernel's is longer (measured in profiles/dense_mxfp8_projections_decode.md)
+    dense_format: str = "bf16"
 
     def __post_init__(self):
         if len(self.compress_ratios) != self.num_layers:

@@ -32,7 +32,7 @@ _BF16 = torch.bfloat16
 # --------------------------------------------------------------------------- scalars
 def ue8m0_exponent(amax: torch.Tensor) -> torch.Tensor:
     """Exact smallest e with 448 * 2^e >= max(amax, 1e-4) (amax fp32, non-negative)."""
-    a = torch.clamp(amax.to(_F32), min=torch.tensor(abi.AMAX_FLOOR, dtype=_F32))
+    a = amax.to(_F32).clamp_min(abi.AMAX_FLOOR)  # the Python float becomes an fp32 scalar on amax's device
     mant, exp = torch.frexp(a)  # a = mant * 2^exp, mant in [0.5, 1)
     return (exp - 9 + (mant > 0.875).to(exp.dtype)).to(torch.int32)
 

@@ -31,6 +31,7 @@ from ..ops import attention as attn_ops
 from ..ops import kv as kv_ops
 from ..ops import indexer as idx_ops
 from ..ops import moe as moe_ops
+from ..ops import dense as dense_ops
 from ..ops import fused as fused_ops
 
 
@@ -63,7 +64,8 @@ class StepMeta:
 class V4FlashModel:
     def __init__(self, cfg: ModelConfig, weights: dict, pool: KVPool, comm=None):
         self.cfg = cfg
-        self.W = weights
+        # the model's own layer dicts: fusing and quantizing replace entries without touching the caller's
+        self.W = {**weights, "layers": [dict(lw) for lw in weights["layers"]]}
         self.pool = pool
         self.comm = comm
         self.device = pool.device
@@ -91,6 +93,15 @@ class V4FlashModel:
             self.adapter_ws = torch.zeros(-(-rows // abi.RECORDS_PER_PAGE) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8,
                                           device=self.device)
         self.fused = [self._fuse_layer(i) for i in range(cfg.num_layers)]
+        # MXFP8 dense projections (cfg.dense_format "fp8", csrc/dense_mx.cu); the router gate and the LM
+        # head stay BF16, as in DeepSeek's FP8 checkpoints
+        self.mx = None
+        self.dense_ws = None
+        if cfg.dense_format == "fp8":
+            self.mx = [self._quantize_dense(i) for i in range(cfg.num_layers)]
+            if self.device.type == "cuda":
+                self.dense_ws = self._dense_workspace()
+            self.ar_hook = None  # the fused GEMM + all-reduce takes BF16 weights
 
     def _fuse_layer(self, layer: int) -> dict:
         """Concatenate every projection of the normed residual into one weight per block.
@@ -118,6 +129,65 @@ class V4FlashModel:
                 off += rows
             out[key] = w
         return out
+
+    def _quantize_dense(self, layer: int) -> dict:
+        """MXFP8 weights of one layer's dense projections; their BF16 copies are dropped from the model.
+
+        w_h: the fused attention input projection; wqi: [wq_b ; wi_q] (the q up-projection and, in C4
+        layers, the indexer query share their input); wo_a: one [o_lora, heads_per_group x 512] matrix per
+        output group; wo_b; shared_w13; shared_w2."""
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
+        fz = self.fused[layer]
+        ratio = cfg.compress_ratios[layer]
+        wq = torch.cat([lw["wq_b"], lw["wi_q"]]) if ratio == abi.C4_RATIO else lw["wq_b"]
+        mx = {"w_h": dense_ops.quantize_weight(fz["w_h"]), "wqi": dense_ops.quantize_weight(wq),
+              "wo_a": dense_ops.quantize_weight(lw["wo_a"].transpose(1, 2)),
+              "wo_b": dense_ops.quantize_weight(lw["wo_b"]),
+              "shared_w13": dense_ops.quantize_weight(lw["shared_w13"]),
+              "shared_w2": dense_ops.quantize_weight(lw["shared_w2"])}
+        gate = lw["gate"].clone()  # a view of the fused FFN weight: keep only the gate rows
+        for n in ("wqkv_a", "wc_kv", "wc_gate", "wi_k", "wi_kgate", "wi_w", "wq_b", "wi_q", "wo_a", "wo_b",
+                  "shared_w13", "shared_w2"):
+            lw.pop(n, None)
+        lw["gate"] = gate
+        fz["w_h"] = fz["w_ffn"] = None
+        return mx
+
+    def _dense_workspace(self) -> "dense_ops.DenseWorkspace":
+        """One workspace for every dense call of a decode step (at most the pool's request count) and of a
+        prefill chunk."""
+        cfg, ecfg = self.cfg, self.pool.ecfg
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        calls = []
+        for T in {max(1, self.pool.max_requests + 1), max(1, ecfg.chunked_prefill_size)}:
+            for mx in self.mx:
+                for w in mx.values():
+                    calls.append((T, w.n, w.k, w.batch))
+        return dense_ops.DenseWorkspace.for_calls(calls, self.device, sms)
+
+    def _dense(self, layer: int, name: str, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        w = self.mx[layer][name]
+        ws = self.dense_ws
+        if ws is not None and not ws.fits(x.shape[-2], w.k, w.n, w.batch):
+            # larger than the engine's decode batch and prefill chunk (a direct model call): the growable
+            # per-device workspace (never reached inside a captured decode step)
+            ws = None
+        return dense_ops.mx_linear(x, w, out=out, workspace=ws)
+
+    def _proj_h(self, layer: int, h: torch.Tensor) -> torch.Tensor:
+        """The fused attention input projection (q LoRA | latent | compressor | indexer parts)."""
+        if self.mx is not None:
+            return self._dense(layer, "w_h", h)
+        return h @ self.fused[layer]["w_h"].T
+
+    def _proj_q(self, layer: int, q_lora: torch.Tensor):
+        """(q up-projection [T, heads x 512], indexer queries [T, index_heads x index_dim] or None)."""
+        if self.mx is None:
+            return q_lora @ self.W["layers"][layer]["wq_b"].T, None
+        qq = self._dense(layer, "wqi", q_lora)
+        hl = self.heads * self.cfg.latent_dim
+        return qq[:, :hl], (qq[:, hl:] if self.cfg.compress_ratios[layer] == abi.C4_RATIO else None)
 
     # ------------------------------------------------------------------ helpers
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
@@ -210,12 +280,14 @@ class V4FlashModel:
 
     # ------------------------------------------------------------------ indexer
     def _index_topk(self, layer: int, q_lora: torch.Tensor, y: torch.Tensor, phys: torch.Tensor,
-                    count: torch.Tensor, r_limit: int):
-        """Top-k C4 records per query: returns (slots int32 [B,K], rope positions int32 [B,K])."""
+                    count: torch.Tensor, r_limit: int, qi: torch.Tensor | None = None):
+        """Top-k C4 records per query: returns (slots int32 [B,K], rope positions int32 [B,K]).  `qi`: the
+        indexer queries [B, index_heads x index_dim] when the caller projected them already."""
         lw = self.W["layers"][layer]
         cfg = self.cfg
         B = q_lora.shape[0]
-        qi = (q_lora @ lw["wi_q"].T).view(B, cfg.index_heads, cfg.index_dim)
+        qi = (q_lora @ lw["wi_q"].T) if qi is None else qi
+        qi = qi.view(B, cfg.index_heads, cfg.index_dim)
         c = self.fused[layer]["wi_w"]
         wi = y[:, c:c + cfg.index_heads].float() * ((cfg.index_heads ** -0.5) * (cfg.index_dim ** -0.5))
         return idx_ops.index_select(qi.contiguous(), wi, self.pool.index_keys[layer], self.pool.index_scales[layer],
@@ -227,18 +299,19 @@ class V4FlashModel:
         cfg = self.cfg
         lw = self.W["layers"][layer]
         B = h.shape[0]
-        y = h @ self.fused[layer]["w_h"].T
+        y = self._proj_h(layer, h)
         Q = cfg.q_lora_rank
         q_lora = rmsnorm(y[:, :Q], lw["q_norm"], cfg.rms_eps)
         kv_raw = y[:, Q:Q + cfg.latent_dim].float()
         kv_ops.native_store(kv_raw, lw["kv_norm"], cfg.rms_eps, meta.swa_write, meta.positions, self.freqs,
                             self.pool.swa[layer])
-        q = fused_ops.rope_q((q_lora @ lw["wq_b"].T).view(B, self.heads, cfg.latent_dim), meta.positions, self.freqs)
+        q_lin, qi = self._proj_q(layer, q_lora)
+        q = fused_ops.rope_q(q_lin.view(B, self.heads, cfg.latent_dim), meta.positions, self.freqs)
         ratio = cfg.compress_ratios[layer]
         if ratio:
             self._compress_decode(layer, y, meta)
         if ratio == abi.C4_RATIO:
-            csa_slots, csa_pos = self._index_topk(layer, q_lora, y, meta.c4_phys, meta.c4_count, self.r4max)
+            csa_slots, csa_pos = self._index_topk(layer, q_lora, y, meta.c4_phys, meta.c4_count, self.r4max, qi)
             csa_len = meta.topk_len
             pool_native, planes = self.csa_planes(layer)
             if self.observer is not None:
@@ -270,6 +343,11 @@ class V4FlashModel:
     def _o_proj(self, layer: int, o: torch.Tensor, B: int) -> torch.Tensor:
         cfg = self.cfg
         lw = self.W["layers"][layer]
+        if self.mx is not None:  # grouped LoRA projection (one weight per group), then the output projection
+            o3 = o.view(B, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
+            o_lora = torch.empty(B, self.groups, cfg.o_lora_rank, dtype=torch.bfloat16, device=o.device)
+            self._dense(layer, "wo_a", o3, out=o_lora.transpose(0, 1))
+            return self._all_reduce(self._dense(layer, "wo_b", o_lora.view(B, self.groups * cfg.o_lora_rank)))
         o = o.view(B, self.groups, cfg.heads_per_group * cfg.latent_dim).transpose(0, 1)
         o_lora = torch.bmm(o, lw["wo_a"]).transpose(0, 1).reshape(B, self.groups * cfg.o_lora_rank)
         if self.ar_hook is not None:
@@ -286,12 +364,17 @@ class V4FlashModel:
         cfg = self.cfg
         lw = self.W["layers"][layer]
         fz = self.fused[layer]
-        g = h @ fz["w_ffn"].T
-        c = fz["gate"]
-        topk_ids, topk_w = fused_ops.route_topk(g[:, c:], lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
+        if self.mx is not None:  # MXFP8 shared expert, BF16 router gate
+            g = self._dense(layer, "shared_w13", h)
+            logits = h @ lw["gate"].T
+        else:
+            gf = h @ fz["w_ffn"].T
+            g, logits = gf[:, :fz["gate"]], gf[:, fz["gate"]:]
+        topk_ids, topk_w = fused_ops.route_topk(logits, lw["gate_bias"], cfg.moe_topk, cfg.routed_scaling)
         out = moe_ops.experts(h, topk_ids, topk_w, lw, self.expert_base, self.local_experts, cfg.expert_format,
                               precision=self.moe_precision)
-        shared = fused_ops.silu_mul(g[:, :c]) @ lw["shared_w2"].T
+        silu = fused_ops.silu_mul(g)
+        shared = self._dense(layer, "shared_w2", silu) if self.mx is not None else silu @ lw["shared_w2"].T
         if self.comm is None or self.world == 1:
             return shared, out
         if hasattr(self.comm, "all_reduce_sum"):
@@ -361,7 +444,7 @@ class V4FlashModel:
             lw = self.W["layers"][layer]
             n_attn, n_ffn = self._layer_norms(layer)
             x, h = fused_ops.add_rmsnorm(x, n_attn, eps, d, dfp, inplace=True)
-            y = h @ self.fused[layer]["w_h"].T
+            y = self._proj_h(layer, h)
             Q = cfg.q_lora_rank
             q_lora = rmsnorm(y[:, :Q], lw["q_norm"], eps)
             kv_raw = y[:, Q:Q + cfg.latent_dim].float().contiguous()
@@ -375,7 +458,8 @@ class V4FlashModel:
             last = slice(max(0, T - W), T)
             kv_ops.native_store(kv_raw[last].contiguous(), lw["kv_norm"], eps, req_slot * W + pos[last] % W,
                                 pos[last], self.freqs, self.pool.swa[layer])
-            q = fused_ops.rope_q((q_lora @ lw["wq_b"].T).view(T, self.heads, cfg.latent_dim), pos, self.freqs)
+            q_lin, qi = self._proj_q(layer, q_lora)
+            q = fused_ops.rope_q(q_lin.view(T, self.heads, cfg.latent_dim), pos, self.freqs)
             ratio = cfg.compress_ratios[layer]
             if ratio:
                 self._compress_prefill(layer, y, pos, req_slot, c4_phys_row, c128_phys_row)
@@ -383,7 +467,7 @@ class V4FlashModel:
                 count = (pos + 1) // abi.C4_RATIO
                 n_vis = int(min(self.r4max, (start + T) // abi.C4_RATIO))
                 lim = max(1, n_vis)
-                csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, y, c4_phys_row, count, lim)
+                csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, y, c4_phys_row, count, lim, qi=qi)
                 csa_len = torch.full((T,), csa_slots.shape[1], dtype=torch.int32, device=dev)
                 pool_native, planes = self.csa_planes(layer)
             elif ratio == abi.C128_RATIO:
@@ -410,13 +494,14 @@ class V4FlashModel:
                                      None if dfp is None else dfp[-1:])
         return (h @ self.W["lm_head"].T).float()[0]
 
-    def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int = 256):
+    def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int = 256, qi=None):
         T = q_lora.shape[0]
         outs_s, outs_p = [], []
         for t0 in range(0, T, block):
             t1 = min(T, t0 + block)
             ph = phys_row[:lim][None].expand(t1 - t0, -1).int().contiguous()
-            s, p = self._index_topk(layer, q_lora[t0:t1], y[t0:t1], ph, count[t0:t1], lim)
+            s, p = self._index_topk(layer, q_lora[t0:t1], y[t0:t1], ph, count[t0:t1], lim,
+                                    None if qi is None else qi[t0:t1])
             outs_s.append(s)
             outs_p.append(p)
         return torch.cat(outs_s).contiguous(), torch.cat(outs_p).contiguous()

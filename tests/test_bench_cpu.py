@@ -221,6 +221,8 @@ def test_step_breakdown_groups_kernels_into_families():
     assert family("(anonymous namespace)::sparse_mla_decode_kernel(DecodeParams)") == "attention (sparse MLA decode)"
     assert family("(anonymous namespace)::index_logits_kernel(LogitParams)") == "indexer"
     assert family("nvjet_tst_32x64_64x16_4x1_v_bz_TNN") == "dense GEMM (cuBLAS)"
+    assert family("void (anonymous namespace)::dense_mx_kernel<true>(CUtensorMap_st)") == \
+        "dense projections, MXFP8 (packmla)"
     assert family("void at::native::vectorized_elementwise_kernel<4>") == "sampling / torch elementwise"
     assert family("something_else") == "other"
 

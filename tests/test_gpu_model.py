@@ -12,6 +12,42 @@ from packmla.ops import moe as moe_ops
 pytestmark = pytest.mark.gpu
 
 
+class _Decisions:
+    """Records the GPU engine's discrete choices (routed experts with their weights, selected C4 records)
+    and replays them, in call order, into the CPU oracle engine: near-tied choices of the random model
+    flip under last-bit differences, and the end-to-end comparison should measure the arithmetic, not
+    which expert or record won a tie.  The router and the indexer have their own kernel tests."""
+
+    def __init__(self):
+        from packmla.ops import fused as fused_ops
+        from packmla.ops import indexer as idx_ops
+
+        self.mods = ((fused_ops, "route_topk"), (idx_ops, "index_select"))
+        self.orig = {name: getattr(mod, name) for mod, name in self.mods}
+        self.log = {name: [] for _, name in self.mods}
+
+    def record(self):
+        for mod, name in self.mods:
+            def rec(*a, _n=name, **k):
+                out = self.orig[_n](*a, **k)
+                self.log[_n].append(tuple(t.cpu() for t in out))
+                return out
+            setattr(mod, name, rec)
+
+    def replay(self):
+        pos = {name: 0 for _, name in self.mods}
+        for mod, name in self.mods:
+            def rep(*a, _n=name, **k):
+                out = self.log[_n][pos[_n]]
+                pos[_n] += 1
+                return tuple(t.clone() for t in out)
+            setattr(mod, name, rep)
+
+    def restore(self):
+        for mod, name in self.mods:
+            setattr(mod, name, self.orig[name])
+
+
 def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm()).item()
 
@@ -75,7 +111,8 @@ def test_engine_gpu_matches_cpu_oracle(cuda, fmt, precision):
     The random small model amplifies last-bit differences from layer to layer (in either precision);
     MXFP8 activations (precision "default") add a step of about 2 % at the first expert layer, because
     0.2 % input differences flip E4M3 roundings.  So the MXFP8 comparison covers the first prefill only;
-    the kernel's MXFP8 numerics on identical inputs are pinned by the MoE tests above."""
+    the kernel's MXFP8 numerics on identical inputs are pinned by the MoE tests above.  The CPU engine
+    replays the GPU engine's routed experts and selected C4 records (`_Decisions`)."""
     cfg = small_gpu_config()
     W = init_weights(cfg, device="cpu", seed=3)
     Wg = {"layers": [{k: v.cuda() for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
@@ -83,15 +120,20 @@ def test_engine_gpu_matches_cpu_oracle(cuda, fmt, precision):
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g)
     res = {}
-    for dev, weights in (("cpu", W), ("cuda", Wg)):
-        ecfg = EngineConfig(kv_cache_format=fmt, device=dev, max_running_requests=2, cuda_graph_bs=[1, 2],
-                            chunked_prefill_size=128, disable_cuda_graph=True, moe_precision=precision)
-        eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
-        slot = eng.pool.admit(400)
-        l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
-        l2 = eng.model.prefill(prompt[200:].to(dev), 200, slot)
-        l3 = eng.model.decode(prompt[:1].to(dev), torch.tensor([300], device=dev), torch.tensor([slot], device=dev))
-        res[dev] = (l1.cpu(), l2.cpu(), l3[0].cpu())
+    dec = _Decisions()
+    try:
+        for dev, weights in (("cuda", Wg), ("cpu", W)):
+            (dec.record if dev == "cuda" else dec.replay)()
+            ecfg = EngineConfig(kv_cache_format=fmt, device=dev, max_running_requests=2, cuda_graph_bs=[1, 2],
+                                chunked_prefill_size=128, disable_cuda_graph=True, moe_precision=precision)
+            eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
+            slot = eng.pool.admit(400)
+            l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
+            l2 = eng.model.prefill(prompt[200:].to(dev), 200, slot)
+            l3 = eng.model.decode(prompt[:1].to(dev), torch.tensor([300], device=dev), torch.tensor([slot], device=dev))
+            res[dev] = (l1.cpu(), l2.cpu(), l3[0].cpu())
+    finally:
+        dec.restore()
     check_errors(cuda)
     pairs = list(zip(res["cuda"], res["cpu"]))
     for a, b in (pairs if precision == "bf16" else pairs[:1]):
@@ -127,3 +169,51 @@ def test_moe_fp4_full_width_shapes(cuda):
     out = moe_ops.experts(h.cuda(), ids.cuda(), w.cuda(), {k: v.cuda() for k, v in lw.items()}, 0, 4, "mxfp4")
     check_errors(cuda)
     assert _rel(out.cpu(), ref) < 2e-2
+
+
+def test_engine_gpu_matches_cpu_oracle_fp8_dense(cuda):
+    """MXFP8 dense projections (csrc/dense_mx.cu) in the engine against the CPU oracle engine, whose dense
+    path computes the same MXFP8 arithmetic in fp32.  As with MXFP8 expert activations, last-bit input
+    differences flip E4M3 roundings from layer to layer, so the comparison covers the first prefill; the CPU
+    engine replays the GPU engine's routed experts and selected records (`_Decisions`)."""
+    cfg = small_gpu_config(dense_format="fp8")
+    W = init_weights(cfg, device="cpu", seed=4)
+    Wg = {"layers": [{k: v.cuda() for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
+          **{k: v.cuda() for k, v in W.items() if torch.is_tensor(v)}}
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g)
+    res = {}
+    dec = _Decisions()
+    try:
+        for dev, weights in (("cuda", Wg), ("cpu", W)):
+            (dec.record if dev == "cuda" else dec.replay)()
+            ecfg = EngineConfig(kv_cache_format="direct", device=dev, max_running_requests=2, cuda_graph_bs=[1, 2],
+                                chunked_prefill_size=128, disable_cuda_graph=True)
+            eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
+            assert eng.model.mx is not None and "wq_b" not in eng.model.W["layers"][1]
+            slot = eng.pool.admit(400)
+            l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
+            res[dev] = l1.cpu()
+    finally:
+        dec.restore()
+    check_errors(cuda)
+    assert _rel(res["cuda"], res["cpu"]) < 6e-2
+    assert "wq_b" in W["layers"][1]  # the caller's weights are left as they were
+
+
+def test_decode_graph_replay_matches_eager_fp8_dense(cuda):
+    cfg = small_gpu_config(dense_format="fp8")
+    W = init_weights(cfg, device=cuda, seed=6)
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (90, 33)]
+    outs = {}
+    for graphs in (False, True):
+        ecfg = EngineConfig(kv_cache_format="direct", max_running_requests=2, cuda_graph_bs=[1, 2],
+                            chunked_prefill_size=64, disable_cuda_graph=not graphs)
+        eng = Engine.build(cfg, ecfg, cuda, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=W)
+        if graphs:
+            eng.runner.capture()
+        outs[graphs] = eng.generate(prompts, SamplingParams(max_new_tokens=6))
+        eng.runner.release()
+    check_errors(cuda)
+    assert outs[True] == outs[False]
