@@ -119,13 +119,15 @@ class CaptureObserver:
 
 def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int = 2, train_queries: int = 2,
                   dev_queries: int = 3, prompt_len: int = 300, seed: int = 0, device: str = "cpu",
-                  layers: tuple[int, ...] | None = None, comm=None) -> dict:
+                  layers: tuple[int, ...] | None = None, comm=None, publish_root: Path | None = None) -> dict:
     """Run `issues` random requests through a Native-format engine and cache their C4-layer queries.
 
     Each issue contributes `train_queries` (train split) or `dev_queries` (development split) decode
     positions per layer; the split is frozen by `frozen_split`.  With a multi-rank `comm` (every rank
     calls this in lockstep with the same arguments), the engine runs tensor parallel, the observer
-    gathers the heads of every captured query, and rank 0 alone writes the cache.
+    gathers the heads of every captured query, and rank 0 alone writes the cache.  With `publish_root`,
+    rank 0 first publishes every issue's captured states there (packmla.training.data.publish) and builds
+    the cache from the verified publications.
     """
     from ...config import EngineConfig
     from ...engine.engine import Engine, SamplingParams
@@ -165,10 +167,21 @@ def capture_cache(output: Path, model_cfg, *, issues: int = 6, development: int 
             s["split"] = role
             roles[role].append(s)
         states_by_layer[layer] = roles
-    if rank == 0:
-        write_cache(Path(output), states_by_layer, split, per,
-                    {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native",
-                     "capture_tp": world})
+    model_info = {"name": model_cfg.name, "config": model_cfg.to_json(), "kv_cache_format": "native",
+                  "capture_tp": world}
+    if rank == 0 and publish_root is not None:
+        from . import publish
+
+        requests = {rid: {"split": role_of[rid]} for rid in ids}
+        publish.write_capture_config(Path(publish_root), {"layers": list(layers), "split": split,
+                                                          "requests": requests, "queries_captured": per,
+                                                          "model": model_info})
+        for rid in ids:
+            publish.publish_issue(Path(publish_root), rid,
+                                  {layer: [s for s in obs.states[layer] if s["rid"] == rid] for layer in layers})
+        publish.build_cache(Path(publish_root), Path(output), per)
+    elif rank == 0:
+        write_cache(Path(output), states_by_layer, split, per, model_info)
     return {"cache": str(output), "layers": list(layers), "split": split, "skipped": obs.skipped,
             "states": {layer: {r: len(v) for r, v in roles.items()} for layer, roles in states_by_layer.items()}}
 
@@ -185,6 +198,8 @@ def main(argv=None) -> dict:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--device", default="cpu", choices=["cpu", "cuda"])
     ap.add_argument("--layers", default=None, help="comma-separated C4 layers (default: all)")
+    ap.add_argument("--publish", type=Path, default=None,
+                    help="new publication root: publish every issue's raw captures there, build the cache from them")
     a = ap.parse_args(argv)
     if a.output.exists():
         raise SystemExit(f"{a.output} exists: captures are written to a new directory")
@@ -196,7 +211,7 @@ def main(argv=None) -> dict:
     layers = tuple(int(x) for x in a.layers.split(",")) if a.layers else None
     return capture_cache(a.output, cfg, issues=a.issues, development=a.development, train_queries=a.train_queries,
                          dev_queries=a.dev_queries, prompt_len=a.prompt_len, seed=a.seed, device=a.device,
-                         layers=layers)
+                         layers=layers, publish_root=a.publish)
 
 
 if __name__ == "__main__":

@@ -173,3 +173,21 @@ def test_capture_cli_writes_fresh_cache(tmp_path):
     assert out["skipped"] == 0 and all(v == {"train": 1, "development": 1} for v in out["states"].values())
     with pytest.raises(SystemExit):  # caches are never overwritten
         capture.main(["--output", str(tmp_path / "c")])
+
+
+def test_capture_cli_publishes_and_builds_from_publications(tmp_path):
+    from packmla.training.data import capture, publish
+    from packmla.training.data.cache import load_cached_layer
+
+    out = capture.main(["--output", str(tmp_path / "c"), "--publish", str(tmp_path / "pub"), "--issues", "2",
+                        "--development", "1", "--train-queries", "1", "--dev-queries", "2", "--prompt-len", "64"])
+    cfg = json.loads((tmp_path / "c" / "config.json").read_text())
+    assert cfg["model"]["capture_config_sha256"]  # the cache names the configuration it was built from
+    issues = sorted(json.loads((tmp_path / "pub" / "capture-config.json").read_text())["requests"])
+    reader = publish.PublishedCaptures(tmp_path / "pub", issues)
+    layer = out["layers"][0]
+    cached = load_cached_layer(tmp_path / "c", layer)
+    for role, rows in cached.items():
+        for s in rows:
+            pub = {p["ordinal"]: p for p in reader.load(s["rid"], layer)}
+            assert torch.equal(pub[s["ordinal"]]["target"], s["target"])
