@@ -36,22 +36,14 @@ METRIC = "decode output tok/s (32k in/256 out)"
 
 
 def build_identity() -> dict:
-    """git commit (when the checkout has one) and sha256 of the loaded extension."""
-    import glob
-    import hashlib
-    import subprocess
+    """The source identity of this run (packmla.utils.provenance): commit, modified paths, the compiled
+    sources' digest, the library's sha256 and whether it was built from those sources."""
+    from packmla.utils.provenance import source_identity
 
-    out = {}
-    try:
-        out["git_sha"] = subprocess.run(["git", "rev-parse", "HEAD"], cwd=ROOT, capture_output=True, text=True,
-                                        timeout=10).stdout.strip() or None
-    except (OSError, subprocess.SubprocessError):
-        out["git_sha"] = None
-    so = sorted(glob.glob(os.path.join(ROOT, "packmla", "_C*.so")))
-    if so:
-        with open(so[0], "rb") as f:
-            out["extension_sha256"] = hashlib.sha256(f.read()).hexdigest()[:16]
-    return out
+    ident = source_identity()
+    return {"git_sha": ident["git_commit"], "modified": ident["modified"], "csrc_sha256": ident["csrc_sha256"],
+            "extension_sha256": (ident["library"]["sha256"] or "")[:16] or None,
+            "library_matches_sources": ident["library_matches_sources"]}
 
 
 def reference_arm(args) -> None:
