@@ -211,6 +211,13 @@ struct DenseMxArgs {
   int* err;
 };
 int launch_dense_mx(const DenseMxArgs& a, cudaStream_t stream);
+
+// FP4 C4 records (csrc/kv_store_fp4.cu): rows -> normalized, tail-rotated, BF16-rounded, E2M1 with an E4M3
+// scale per 16; Native 288 B (packed = false) or Packed 224 B (the 256 largest magnitudes) in pages of 64
+// records (data rows, then scale rows).
+void launch_fp4_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
+                      const int64_t* positions, const float* freqs, int64_t freq_rows, uint8_t* pool,
+                      int64_t pool_slots, bool packed, int rows, int* err, cudaStream_t stream);
 // Whether the GEMM quantizes the activations itself for these sizes (one launch; x read in place).
 bool dense_mx_fused_quant(int T, int K, int splits);
 int gemm_ar_smem_bytes(int stages);

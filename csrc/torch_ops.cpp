@@ -688,6 +688,24 @@ void dense_mx(torch::Tensor x, torch::Tensor w, torch::Tensor w_sf, torch::Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void fp4_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, torch::Tensor positions,
+               torch::Tensor freqs, torch::Tensor pool, bool packed, torch::Tensor err) {
+  TORCH_CHECK(raw.is_cuda() && raw.scalar_type() == torch::kFloat32 && raw.dim() == 2 && raw.size(1) == 512 &&
+              raw.stride(1) == 1 && raw.stride(0) % 4 == 0, "raw must be fp32 [R, 512] with 16-byte rows");
+  TORCH_CHECK(weight.scalar_type() == torch::kFloat32 && weight.numel() == 512 && weight.is_contiguous());
+  TORCH_CHECK(slots.scalar_type() == torch::kInt64 && slots.numel() == raw.size(0) && slots.is_contiguous());
+  TORCH_CHECK(positions.scalar_type() == torch::kInt64 && positions.numel() == raw.size(0) && positions.is_contiguous());
+  TORCH_CHECK(freqs.scalar_type() == torch::kFloat32 && freqs.dim() == 3 && freqs.size(1) == 32 && freqs.is_contiguous());
+  const int64_t page_bytes = 64 * (packed ? 224 : 288);
+  TORCH_CHECK(pool.scalar_type() == torch::kUInt8 && pool.is_contiguous() && pool.numel() % page_bytes == 0,
+              "pool must be uint8 pages of 64 FP4 records");
+  const c10::cuda::CUDAGuard g(raw.device());
+  launch_fp4_store(raw.data_ptr<float>(), raw.stride(0), weight.data_ptr<float>(), (float)eps, slots.data_ptr<int64_t>(),
+                   positions.data_ptr<int64_t>(), freqs.data_ptr<float>(), freqs.size(0), pool.data_ptr<uint8_t>(),
+                   pool.numel() / page_bytes * 64, packed, (int)raw.size(0), err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "packmla sm_100a kernels";
   m.def("native_store", &native_store, "FP32 rows -> Native 584 B C4 records (paged)");
@@ -710,6 +728,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_fp4_mma", &moe_fp4_mma, "MXFP4 routed experts, register-fragment MMAs (decode-sized batches)");
   m.def("moe_fp4", &moe_fp4, "MXFP4 routed experts (route, gate/up+SiLU, down+scatter)");
   m.def("dense_mx", &dense_mx, "dense projections with MXFP8 weights: y[b] = x[b] W[b]^T (tcgen05 block-scaled)");
+  m.def("fp4_store", &fp4_store, "FP4 C4 records (E2M1 + E4M3 per 16; Native 288 B / Packed 224 B) into paged pools");
   m.def("decode_max_active_clusters", [](int64_t cluster) {
     TORCH_CHECK(decode_splits_clustered((int)cluster), "cluster size must be 2, 4 or 8");
     return decode_max_active_clusters((int)cluster);

@@ -104,3 +104,35 @@ def packed_to_native(values: torch.Tensor, bitmap: torch.Tensor, scales: torch.T
         base_s = abi.RECORDS_PER_PAGE * abi.NATIVE_DATA_BYTES + int(rr[i]) * abi.NATIVE_SCALE_BYTES
         pages[page[i], base_d:base_d + abi.NATIVE_DATA_BYTES] = recs[i, :abi.NATIVE_DATA_BYTES]
         pages[page[i], base_s:base_s + abi.NATIVE_SCALE_BYTES] = recs[i, abi.NATIVE_DATA_BYTES:]
+
+
+def fp4_store(raw: torch.Tensor, weight: torch.Tensor, eps: float, slots: torch.Tensor, positions: torch.Tensor,
+              freqs: torch.Tensor, pool: torch.Tensor, packed: bool) -> None:
+    """Write FP4 C4 records (the V4.1 cache, packmla/formats/fp4.py) for rows `raw` [R, 512] at physical
+    `slots` (-1 = skip): Native 288 B or, with `packed`, Packed 224 B, in pages of 64 records (data rows, then
+    scale rows).  `positions` are the RoPE rows; the records hold the normalized, tail-rotated values."""
+    from ..formats import fp4
+
+    if raw.is_cuda:
+        ext().fp4_store(raw.float().contiguous(), weight.float().contiguous(), float(eps), slots.to(torch.int64),
+                        positions.to(torch.int64), freqs, pool, bool(packed), error_word(raw.device))
+        return
+    keep = slots >= 0
+    if not bool(keep.any()):
+        return
+    fr = torch.view_as_complex(freqs[positions[keep].long()].contiguous())
+    rows = fp4.rotated_rows(codec.rms_normalize(raw[keep].float(), weight.float(), eps), fr)
+    fmt = "direct" if packed else "native"
+    data_row = fp4.record_bytes(fmt) - fp4.GROUPS
+    if packed:
+        codes, words, scales = fp4.packed_encode(rows)
+        data = torch.cat((codes, words.contiguous().view(torch.uint8).view(rows.shape[0], fp4.BITMAP_BYTES)), -1)
+    else:
+        data, scales = fp4.native_encode(rows)
+    pages = pool.view(-1, fp4.page_bytes(fmt))
+    for s, d, sc in zip(slots[keep].tolist(), data, scales):
+        page, r = divmod(s, abi.RECORDS_PER_PAGE)
+        pages[page, r * data_row:(r + 1) * data_row] = d
+        off = abi.RECORDS_PER_PAGE * data_row + r * fp4.GROUPS
+        pages[page, off:off + fp4.GROUPS] = sc
+

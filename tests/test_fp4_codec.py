@@ -167,3 +167,22 @@ def test_fp4_capacity_gain_is_below_the_record_shrink():
     direct = fp4.capacity_tokens(cfg, "direct", 1 << 30)
     gain = direct / native
     assert 1.0 < gain < 288 / 224  # indexer keys, C128 records and the SWA share do not shrink
+
+
+def test_fp4_store_cpu_path_writes_the_page_layout():
+    """The op's CPU path, filling one page through a slot permutation, writes write_page's bytes."""
+    from packmla.formats import codec, fp4
+    from packmla.ops import kv as kv_ops
+
+    g = torch.Generator().manual_seed(5)
+    raw = torch.randn(64, 512, generator=g)
+    w = torch.rand(512, generator=g) + 0.5
+    freqs = kv_ops.freq_table_f32(codec.rope_table(128))
+    pos = torch.randint(0, 128, (64,), generator=g)
+    slots = torch.randperm(64, generator=g)
+    rows = fp4.rotated_rows(codec.rms_normalize(raw, w, 1e-6), torch.view_as_complex(freqs[pos].contiguous()))
+    order = torch.argsort(slots)
+    for packed, fmt in ((False, "native"), (True, "direct")):
+        pool = torch.zeros(fp4.page_bytes(fmt), dtype=torch.uint8)
+        kv_ops.fp4_store(raw, w, 1e-6, slots, pos, freqs, pool, packed)
+        assert torch.equal(pool, fp4.write_page(fmt, rows[order]))

@@ -141,3 +141,30 @@ def test_sparse_decode_matches_oracle(cuda, packed, B, H, K, splits, qscale):
     check_errors(cuda)
     torch.testing.assert_close(o.float().cpu(), ref_o.float(), atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(lse.cpu(), ref_lse, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("rows", [1, 24, 130])
+def test_fp4_store_byte_exact(cuda, packed, rows):
+    """FP4 C4 records (V4.1 cache) from the device store equal the CPU codec's bytes, ties included."""
+    from packmla.formats import fp4
+
+    g = torch.Generator().manual_seed(300 + rows + int(packed))
+    raw = torch.randn(rows, 512, generator=g) * 2
+    raw[0] = torch.round(raw[0] * 4) / 4  # many equal magnitudes after quantization
+    if rows > 1:
+        raw[1] = 1.0
+    weight = torch.rand(512, generator=g) + 0.25
+    freqs = _freqs()
+    pos = torch.randint(0, 4000, (rows,), generator=g)
+    pages = (rows + 63) // 64 + 1
+    slots = torch.randperm(pages * 64, generator=g)[:rows]
+    if rows > 2:
+        slots[2] = -1
+    fmt = "direct" if packed else "native"
+    pool = torch.full((pages * fp4.page_bytes(fmt),), 0x5A, dtype=torch.uint8)
+    gpool = pool.cuda()
+    kv_ops.fp4_store(raw.cuda(), weight.cuda(), 1e-6, slots.cuda(), pos.cuda(), freqs.cuda(), gpool, packed)
+    check_errors(cuda)
+    kv_ops.fp4_store(raw, weight, 1e-6, slots, pos, freqs, pool, packed)
+    assert torch.equal(gpool.cpu(), pool)
