@@ -105,7 +105,7 @@ def main() -> None:
                     help="concurrent requests C (default 8 / 8 / 24 / 40 at 1 / 2 / 4 / 8 GPUs)")
     ap.add_argument("--prompt-len", type=int, default=32768)
     ap.add_argument("--output-len", type=int, default=256)
-    ap.add_argument("--kv-format", default="direct", choices=["direct", "native"])
+    ap.add_argument("--kv-format", default="direct", choices=["direct", "native", "fp4-native", "fp4-direct"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--dense-format", default="bf16", choices=["bf16", "fp8"],
                     help="dense projections: BF16 (cuBLAS) or MXFP8 weights (packmla's tcgen05 GEMM)")

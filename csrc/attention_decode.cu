@@ -37,6 +37,8 @@
 // Set-up: TMEM, barriers and the expansion table are prepared before griddepcontrol.wait (programmatic
 // dependent launch); Q arrives by bulk copies into the K buffer and is converted to FP16 from there, so
 // the first tile's index and row loads own the load path while Q streams in.
+#include <cuda_fp4.h>
+
 #include "launchers.h"
 #include "common/sm100.cuh"
 
@@ -50,6 +52,10 @@ constexpr int kThreads = 512;      // 16 warps: all expand, all run the softmax,
 constexpr int kPage = 64;
 constexpr int kNativeData = 576;
 constexpr int kNativePageBytes = kPage * 584;
+constexpr int kFp4NativeData = 256;                       // FP4 Native data row: 512 E2M1 codes
+constexpr int kFp4PackedData = 192;                       // FP4 Packed data row: 256 codes + 8 bitmap words
+constexpr int kFp4NativePage = kPage * (kFp4NativeData + 32);
+constexpr int kFp4PackedPage = kPage * (kFp4PackedData + 32);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -145,7 +151,7 @@ __device__ __forceinline__ uint4 bf16x8_to_f16(uint4 v) {
 }
 
 struct RowRef {
-  int kind;  // 0 = masked, 1 = native (swa pool), 2 = native (csa pool), 3 = packed
+  int kind;  // 0 = masked, 1 = native (swa pool), 2 = native (csa pool), 3 = packed, 4/5 = FP4 native/packed
   int slot;
   int pos;
 };
@@ -183,7 +189,7 @@ __device__ __forceinline__ RowRef idx_resolve(const DecodeParams& p, const RowId
     pm::report_error(p.err, pm::kIndexOutOfRange, i);
     return r;
   }
-  r.kind = p.csa_packed ? 3 : 2;
+  r.kind = p.csa_fp4 ? 3 + p.csa_fp4 : (p.csa_packed ? 3 : 2);
   r.slot = s;
   r.pos = x.pos;
   return r;
@@ -193,7 +199,11 @@ __device__ __forceinline__ RowRef idx_resolve(const DecodeParams& p, const RowId
 //   Native: u[i] = 16-byte unit v + 8 i of the record (units 0..27 E4M3, 28..35 BF16 tail; i = 4 only v < 4).
 //   Packed: u[0], u[1] = value units v, v + 8; u[2] = bitmap unit v (v < 4); u[3], u[4] = 16-byte units
 //           2 v, 2 v + 1 of the record's RoPE row (the cos/sin of pairs 4 v .. 4 v + 3).
-//   sc: the row's 8 UE8M0 scale bytes.
+//   FP4 Native: u[0], u[1] = code units v, v + 8 (32 coordinates each); sc = E4M3 scale bytes 2 v, 2 v + 1
+//           (sc.x) and 2 v + 16, 2 v + 17 (sc.y).
+//   FP4 Packed: u[0] = code unit v (v < 8: the 128 survivor code bytes); u[2] = bitmap words 2 v, 2 v + 1
+//           (v < 4); u[3], u[4] = the 32 E4M3 scale bytes.
+//   sc: the row's 8 UE8M0 scale bytes (FP8 rows).
 struct Raw {
   uint4 u[5];
   uint2 sc;
@@ -223,7 +233,31 @@ __device__ __forceinline__ void fetch(const DecodeParams& p, const RowRef& rr, i
     R.u[3] = fq[2 * v];
     R.u[4] = fq[2 * v + 1];
     R.sc = *reinterpret_cast<const uint2*>(p.csa_scales + (int64_t)rr.slot * 8);
+  } else if (rr.kind == 4) {
+    const int64_t page = rr.slot / kPage, rip = rr.slot % kPage;
+    const uint8_t* pg = p.csa_pool + page * kFp4NativePage;
+    const uint4* data = reinterpret_cast<const uint4*>(pg + rip * kFp4NativeData);
+    R.u[0] = data[v];
+    R.u[1] = data[v + 8];
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(pg + kPage * kFp4NativeData + rip * 32);
+    R.sc = make_uint2(sc[v], sc[v + 8]);
+  } else if (rr.kind == 5) {
+    const int64_t page = rr.slot / kPage, rip = rr.slot % kPage;
+    const uint8_t* pg = p.csa_pool + page * kFp4PackedPage;
+    const uint4* data = reinterpret_cast<const uint4*>(pg + rip * kFp4PackedData);
+    R.u[0] = data[v];
+    if (v < 4) R.u[2] = data[8 + v];
+    const uint4* sc = reinterpret_cast<const uint4*>(pg + kPage * kFp4PackedData + rip * 32);
+    R.u[3] = sc[0];
+    R.u[4] = sc[1];
   }
+}
+
+// Two E2M1 codes (low nibble = the lower coordinate) -> FP16x2 bits, times an FP16x2 scale.  E2M1 x E4M3
+// products have at most 6 significant bits and lie in [2^-10, 2688]: exact in FP16.
+__device__ __forceinline__ uint32_t fp4x2_scaled(uint32_t byte, __half2 s2) {
+  const __half2_raw r = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)byte, __NV_E2M1);
+  return h2_bits(__hmul2(__half2(r), s2));
 }
 
 __device__ __forceinline__ int scale_exp(uint2 sc, int word) {
@@ -316,6 +350,62 @@ __device__ __noinline__ void expand_row(const Raw R, int brow, int v, uint8_t* _
       *reinterpret_cast<uint4*>(col_v + i * kKChunk) = o;
     }
     __syncwarp(0xFFu << (8 * ((threadIdx.x & 31) >> 3)));
+  } else if (R.kind == 4) {
+    // FP4 Native (values already rotated): code unit u = v + 8 h covers coordinates 32 u .. 32 u + 31, scale
+    // groups 2 u and 2 u + 1, output units 4 u .. 4 u + 3 (4 code bytes each)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 c = R.u[h];
+      const __half2 s2 = pm::e4m3x2_to_h2((uint16_t)(h ? R.sc.y : R.sc.x));
+      const __half2 sg[2] = {__low2half2(s2), __high2half2(s2)};
+      const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+      const int u = v + 8 * h;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = fp4x2_scaled((cw[m] >> (8 * k)) & 0xFFu, sg[m >> 1]);
+        *out(16 * (4 * u + m)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  } else if (R.kind == 5) {
+    // FP4 Packed: the 128 code bytes are staged; the 8 MSB-first bitmap words come from lanes 0..3 of the
+    // row's group and are bit-reversed (coordinate b at bit b); lane v expands unit v of every word
+    const uint32_t gmask = 0xFFu << (8 * ((threadIdx.x & 31) >> 3));
+    *reinterpret_cast<uint4*>(stg + 16 * v) = R.u[0];
+    uint64_t word[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t x = __shfl_sync(gmask, R.u[2].x, j, 8), y = __shfl_sync(gmask, R.u[2].y, j, 8);
+      const uint32_t z = __shfl_sync(gmask, R.u[2].z, j, 8), w = __shfl_sync(gmask, R.u[2].w, j, 8);
+      word[2 * j] = __brevll(((uint64_t)y << 32) | x);
+      word[2 * j + 1] = __brevll(((uint64_t)w << 32) | z);
+    }
+    __syncwarp(gmask);
+    const uint32_t sw[8] = {R.u[3].x, R.u[3].y, R.u[3].z, R.u[3].w, R.u[4].x, R.u[4].y, R.u[4].z, R.u[4].w};
+    const uint64_t below = (1ull << (8 * v)) - 1ull;
+    int prefix = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t bits = (uint32_t)(word[i] >> (8 * v)) & 0xFFu;
+      const int rank = prefix + __popcll(word[i] & below);
+      prefix += __popcll(word[i]);
+      // 8 codes from nibble `rank` (nibbles past the survivors are masked off), one per byte, then the
+      // kept ones moved to their coordinates with the byte-permute table
+      const uint32_t* vw = reinterpret_cast<const uint32_t*>(stg + 4 * (rank >> 3));
+      const uint32_t nib = __funnelshift_r(vw[0], vw[1], 4u * (uint32_t)(rank & 7));
+      const uint32_t ev = nib & 0x0F0F0F0Fu, od = (nib >> 4) & 0x0F0F0F0Fu;
+      const uint32_t lo = __byte_perm(ev, od, 0x5140), hi = __byte_perm(ev, od, 0x7362);
+      const uint4 e = lut[bits];
+      const uint32_t b0 = __byte_perm(lo, hi, e.x) & e.z, b1 = __byte_perm(lo, hi, e.y) & e.w;
+      const uint32_t p0 = b0 | (b0 >> 4), p1 = b1 | (b1 >> 4);  // bytes 0 and 2: code pairs
+      const uint32_t sb = (sw[i] >> (8 * (v >> 1))) & 0xFFu;    // scale group 4 i + v / 2
+      const __half2 s2 = pm::e4m3x2_to_h2((uint16_t)(sb | (sb << 8)));
+      *reinterpret_cast<uint4*>(col_v + i * kKChunk) =
+          make_uint4(fp4x2_scaled(p0 & 0xFFu, s2), fp4x2_scaled((p0 >> 16) & 0xFFu, s2),
+                     fp4x2_scaled(p1 & 0xFFu, s2), fp4x2_scaled((p1 >> 16) & 0xFFu, s2));
+    }
+    __syncwarp(gmask);
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(col_v + i * kKChunk) = zero4();

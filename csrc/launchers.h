@@ -27,7 +27,8 @@ struct DecodeParams {
   const int32_t* swa_len;    // [B]
   // CSA rows
   int csa_packed;
-  const uint8_t* csa_pool;   // native pages (csa_packed == 0)
+  int csa_fp4;               // 0 = FP8 records; 1 = FP4 Native pages (288 B records), 2 = FP4 Packed (224 B)
+  const uint8_t* csa_pool;   // native pages (csa_packed == 0; FP8 or, with csa_fp4, FP4)
   const uint8_t* csa_values; // packed planes
   const uint64_t* csa_bitmap;
   const uint8_t* csa_scales;

@@ -67,7 +67,7 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
                        torch::Tensor csa_scales, torch::Tensor csa_slots, torch::Tensor csa_pos, torch::Tensor csa_len,
                        torch::Tensor freqs, torch::Tensor sink, double scale, torch::Tensor q_pos, int64_t num_splits,
                        torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse,
-                       torch::Tensor err, c10::optional<torch::Tensor> prof) {
+                       torch::Tensor err, c10::optional<torch::Tensor> prof, int64_t csa_fp4) {
   constexpr int kHG = 64;
   if (prof) TORCH_CHECK(prof->is_cuda() && prof->scalar_type() == torch::kInt64 && prof->numel() >= 64);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
@@ -111,7 +111,15 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   p.swa_cap = swa_slots.size(1);
   p.swa_len = swa_len.data_ptr<int32_t>();
   p.csa_packed = csa_packed ? 1 : 0;
-  if (csa_packed) {
+  TORCH_CHECK(csa_fp4 >= 0 && csa_fp4 <= 2 && !(csa_fp4 && csa_packed), "csa_fp4: 0 (FP8), 1 (FP4 Native), 2 (FP4 Packed)");
+  p.csa_fp4 = (int)csa_fp4;
+  if (csa_fp4) {
+    const int64_t page = kPage * (csa_fp4 == 1 ? 288 : 224);
+    TORCH_CHECK(csa_pool.scalar_type() == torch::kUInt8 && csa_pool.numel() % page == 0 && csa_pool.is_contiguous() &&
+                reinterpret_cast<uintptr_t>(csa_pool.data_ptr()) % 16 == 0, "csa_pool must hold FP4 pages of 64 records");
+    p.csa_pool = csa_pool.data_ptr<uint8_t>();
+    p.csa_pool_rows = csa_pool.numel() / page * kPage;
+  } else if (csa_packed) {
     TORCH_CHECK(csa_values.scalar_type() == torch::kUInt8 && csa_values.dim() == 2 && csa_values.size(1) == 256 && csa_values.is_contiguous());
     TORCH_CHECK(csa_bitmap.scalar_type() == torch::kInt64 && csa_bitmap.size(0) == csa_values.size(0) && csa_bitmap.is_contiguous());
     TORCH_CHECK(csa_scales.scalar_type() == torch::kUInt8 && csa_scales.size(0) == csa_values.size(0) && csa_scales.is_contiguous());
@@ -738,7 +746,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_values"), py::arg("csa_bitmap"), py::arg("csa_scales"), py::arg("csa_slots"), py::arg("csa_pos"),
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
-        py::arg("prof") = py::none());
+        py::arg("prof") = py::none(), py::arg("csa_fp4") = 0);
   m.def("packed_to_native", &packed_to_native, "Adapter: Packed planes rows -> Native records (paged workspace)");
   m.def("segment_copy", &segment_copy, "batched 16-byte-aligned copies between device and mapped host memory");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");

@@ -193,6 +193,17 @@ def bench_decode(args, dev):
             kv_ops.packed_store(torch.randn(b - a, 512, device=dev, generator=g), w, 1e-6,
                                 torch.arange(a, b, device=dev), planes.values, planes.bitmap, planes.scales)
         rec_bytes = abi.PACKED_RECORD_BYTES
+    elif args.kv_format.startswith("fp4-"):
+        from packmla.formats import fp4
+
+        fmt4 = args.kv_format[4:]
+        pool = torch.zeros(((rows + 63) // 64) * fp4.page_bytes(fmt4), dtype=torch.uint8, device=dev)
+        for a in range(0, rows, chunk):
+            b = min(rows, a + chunk)
+            kv_ops.fp4_store(torch.randn(b - a, 512, device=dev, generator=g), w, 1e-6,
+                             torch.arange(a, b, device=dev), (torch.arange(a, b, device=dev) % records) * 4,
+                             freqs, pool, fmt4 == "direct")
+        rec_bytes = fp4.record_bytes(fmt4)
     else:
         pool = torch.zeros(((rows + 63) // 64) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
         for a in range(0, rows, chunk):
@@ -212,6 +223,8 @@ def bench_decode(args, dev):
                   freqs=freqs, sink=torch.zeros(Hh, device=dev), scale=512 ** -0.5,
                   q_pos=torch.full((B,), args.context - 1, dtype=torch.int32, device=dev), csa_pool=pool,
                   csa_planes=planes)
+    if args.kv_format.startswith("fp4-"):
+        args_d["csa_fp4"] = args.kv_format[4:]
     splits = args.splits or attn_ops.choose_splits(B, Hh, max(W, 1) + K, max_clusters=attn_ops.max_active_clusters(dev))
     ws = attn_ops.DecodeWorkspace(B, Hh, splits, dev)
     out = torch.empty(B, Hh, 512, dtype=torch.bfloat16, device=dev)
@@ -344,6 +357,7 @@ def bench_decode_paired(args, dev, modes=("native", "direct")) -> dict:
 
 
 SUITE_CONTEXTS, SUITE_BATCHES, SUITE_FORMATS = (32768, 131072), (1, 16, 64), ("native", "direct")
+FP4_SUITE_BATCHES = (8, 16, 24, 28, 32)
 BAD_CLOCK_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown")
 
 
@@ -487,7 +501,7 @@ def bench_dense(args, dev):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["moe", "decode", "store", "index", "dense", "decode-suite", "decode-paired",
-                                     "judge"],
+                                     "fp4-suite", "judge"],
                     help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
                          "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
@@ -497,7 +511,8 @@ def main(argv=None):
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--swa", type=int, default=128, help="decode: SWA rows per query (0 = selected records only)")
-    ap.add_argument("--kv-format", default="direct", choices=["direct", "native", "adapter"])
+    ap.add_argument("--kv-format", default="direct", choices=["direct", "native", "adapter", "fp4-native",
+                                                              "fp4-direct"])
     ap.add_argument("--rows", type=int, default=24)
     ap.add_argument("--rounds", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=10)
@@ -535,6 +550,17 @@ def main(argv=None):
         args.topk = args.topk or 2048
         modes = ("native", "direct", "adapter") if args.with_adapter else ("native", "direct")
         print(json.dumps(bench_decode_paired(args, dev, modes)), flush=True)
+        return
+    elif args.case == "fp4-suite":
+        # the V4.1 FP4 decode table: H64, one query token, K512, SWA128, batches 8-32, FP4 Native and Packed
+        args.topk, args.heads, args.swa = args.topk or 512, 64, 128
+        for batch in FP4_SUITE_BATCHES:
+            for fmt in ("fp4-native", "fp4-direct"):
+                args.batch, args.kv_format = batch, fmt
+                row = bench_decode(args, dev)
+                row["clocks"] = dict(LAST_CLOCKS)
+                print(json.dumps(row), flush=True)
+                torch.cuda.empty_cache()
         return
     elif args.case == "decode-suite":
         args.topk = args.topk or 2048

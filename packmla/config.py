@@ -126,14 +126,16 @@ class ModelConfig:
         return cls(**base)
 
 
-KV_FORMATS = ("native", "direct")
+# C4 cache formats: FP8 Native (584 B) and Packed (328 B) records; FP4 Native (288 B) and Packed (224 B)
+# records, the V4.1 cache (E2M1 + E4M3 per 16, RoPE applied at store)
+KV_FORMATS = ("native", "direct", "fp4-native", "fp4-direct")
 
 
 @dataclass
 class EngineConfig:
     """Serving options; flag names mirror the reference server (scripts/local/run-server.sh:55-139)."""
 
-    kv_cache_format: str = "direct"  # native | direct
+    kv_cache_format: str = "direct"  # native | direct | fp4-native | fp4-direct
     tp: int = 1
     ep: int = 1
     mem_fraction_static: float = 0.88
@@ -172,8 +174,10 @@ class EngineConfig:
         """
         if self.kv_cache_format not in KV_FORMATS:
             raise ValueError(f"--kv-cache-format must be one of {KV_FORMATS}")
-        if self.kv_cache_format == "direct" and self.keep_count != abi.PACKED_KEEP:
+        if self.kv_cache_format in ("direct", "fp4-direct") and self.keep_count != abi.PACKED_KEEP:
             raise ValueError("direct serving supports keep_count 256 only")
+        if self.kv_cache_format.startswith("fp4-") and self.enable_hierarchical_cache:
+            raise ValueError("the FP4 cache formats do not support HiCache")
         if self.enable_hierarchical_cache and self.keep_count != abi.PACKED_KEEP:
             raise ValueError("HiCache requires the 256-survivor layout")
         if not 0.0 < self.mem_fraction_static <= 0.98:

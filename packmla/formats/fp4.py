@@ -171,11 +171,24 @@ def read_page(kv_format: str, page: torch.Tensor, records: int = abi.RECORDS_PER
 def gather_rows(pool: torch.Tensor, kv_format: str, indices: torch.Tensor,
                 records: int = abi.RECORDS_PER_PAGE) -> torch.Tensor:
     """Paged FP4 pool uint8 [num_pages, page bytes] and record ids [N] -> rotated rows fp32 [N, 512]
-    (record id = page * records + row; ids < 0 give zero rows)."""
-    out = torch.zeros(indices.numel(), abi.LATENT_DIM)
-    for i, rid in enumerate(indices.reshape(-1).tolist()):
-        if rid >= 0:
-            out[i] = read_page(kv_format, pool[rid // records], records)[rid % records]
+    (record id = page * records + row; ids < 0 give zero rows).  Only the named records are decoded."""
+    ids = indices.reshape(-1).long()
+    out = torch.zeros(ids.numel(), abi.LATENT_DIM)
+    valid = ids >= 0
+    if not bool(valid.any()):
+        return out
+    pool = pool.reshape(-1, page_bytes(kv_format, records))
+    data_row = record_bytes(kv_format) - GROUPS
+    page, row = ids[valid] // records, ids[valid] % records
+    data_off = row[:, None] * data_row + torch.arange(data_row)
+    scale_off = records * data_row + row[:, None] * GROUPS + torch.arange(GROUPS)
+    data = pool[page[:, None], data_off]
+    scales = pool[page[:, None], scale_off]
+    if kv_format == "direct":
+        words = data[:, PACKED_CODE_BYTES:].contiguous().view(torch.int64)
+        out[valid] = packed_decode(data[:, :PACKED_CODE_BYTES].contiguous(), words, scales)
+    else:
+        out[valid] = native_decode(data.contiguous(), scales)
     return out
 
 

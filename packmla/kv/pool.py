@@ -5,7 +5,8 @@ Layout (per rank; the latent KV is shared by all heads, so TP ranks hold full co
 * page = 256 tokens = 64 C4 records.  A request owns a row of the page table; the same
   page id addresses every C4 layer's pool (one allocation serves all layers).
 * C4 layers:   Native pages (584 B/record) in `native` mode, or Packed planes
-               (256 + 64 + 8 B/record) in `direct` mode; plus FP8 indexer keys
+               (256 + 64 + 8 B/record) in `direct` mode, or FP4 pages (288 B / 224 B per record, data
+               rows then scale rows) in `fp4-native` / `fp4-direct` mode; plus FP8 indexer keys
                (index_dim B + 4 B fp32 scale per record).
 * C128 layers: Native pages; one C128 record per 128 tokens, 64 records per C128 page.
 * SWA:         per layer a ring of 128 Native records per request slot.
@@ -25,7 +26,7 @@ from dataclasses import dataclass
 import torch
 
 from ..config import EngineConfig, ModelConfig
-from ..formats import abi
+from ..formats import abi, fp4
 
 
 @dataclass
@@ -42,6 +43,8 @@ class CapacityReport:
 
 
 def c4_record_bytes(kv_format: str) -> int:
+    if kv_format.startswith("fp4-"):
+        return fp4.record_bytes(kv_format[4:])
     return abi.PACKED_RECORD_BYTES if kv_format == "direct" else abi.NATIVE_RECORD_BYTES
 
 
@@ -119,10 +122,16 @@ class KVPool:
         self.c4_values: dict[int, torch.Tensor] = {}
         self.c4_bitmap: dict[int, torch.Tensor] = {}
         self.c4_scales: dict[int, torch.Tensor] = {}
+        self.c4_fp4: dict[int, torch.Tensor] = {}
+        # FP4 formats: "native" / "direct" (pages of packmla.formats.fp4), None for the FP8 formats
+        self.fp4_format = self.kv_format[4:] if self.kv_format.startswith("fp4-") else None
         self.index_keys: dict[int, torch.Tensor] = {}
         self.index_scales: dict[int, torch.Tensor] = {}
         for layer in cfg.c4_layers:
-            if self.kv_format == "direct":
+            if self.fp4_format is not None:
+                self.c4_fp4[layer] = torch.zeros(num_pages * fp4.page_bytes(self.fp4_format), dtype=torch.uint8,
+                                                 device=dev)
+            elif self.kv_format == "direct":
                 self.c4_values[layer] = torch.zeros(rows, abi.PACKED_KEEP, dtype=torch.uint8, device=dev)
                 self.c4_bitmap[layer] = torch.zeros(rows, abi.BITMAP_WORDS, dtype=torch.int64, device=dev)
                 self.c4_scales[layer] = torch.zeros(rows, abi.NUM_TILES, dtype=torch.uint8, device=dev)
@@ -162,7 +171,7 @@ class KVPool:
     # ------------------------------------------------------------------ bytes
     def device_bytes(self) -> int:
         total = 0
-        for d in (self.c4_native, self.c4_values, self.c4_bitmap, self.c4_scales, self.index_keys,
+        for d in (self.c4_native, self.c4_values, self.c4_bitmap, self.c4_scales, self.c4_fp4, self.index_keys,
                   self.index_scales, self.c128_native, self.comp_state, self.index_state):
             total += sum(t.numel() * t.element_size() for t in d.values())
         total += sum(t.numel() * t.element_size() for t in self.swa)
@@ -221,7 +230,10 @@ class KVPool:
         j = torch.arange(R, device=dev)
         srow, drow = (sp[:, None] * R + j).reshape(-1), (dp[:, None] * R + j).reshape(-1)
         for layer in self.cfg.c4_layers:
-            if self.kv_format == "direct":
+            if self.fp4_format is not None:
+                pages = self.c4_fp4[layer].view(-1, fp4.page_bytes(self.fp4_format))
+                pages[dp] = pages[sp]
+            elif self.kv_format == "direct":
                 for t in (self.c4_values[layer], self.c4_bitmap[layer], self.c4_scales[layer]):
                     t[drow] = t[srow]
             else:

@@ -197,6 +197,8 @@ class V4FlashModel:
 
     def csa_planes(self, layer: int):
         p = self.pool
+        if p.fp4_format is not None:
+            return p.c4_fp4[layer], None
         if self.kv_format == "direct":
             return None, attn_ops.PackedPlanes(p.c4_values[layer], p.c4_bitmap[layer], p.c4_scales[layer])
         return p.c4_native[layer], None
@@ -268,7 +270,10 @@ class V4FlashModel:
         p = self.pool
         if self.observer is not None:
             self.observer.observe_raw(layer, raw, slots)
-        if self.kv_format == "direct":
+        if p.fp4_format is not None:
+            kv_ops.fp4_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, rope_pos, self.freqs, p.c4_fp4[layer],
+                             p.fp4_format == "direct")
+        elif self.kv_format == "direct":
             kv_ops.packed_store(raw, lw["c_norm"], self.cfg.rms_eps, slots, p.c4_values[layer], p.c4_bitmap[layer],
                                 p.c4_scales[layer])
         else:
@@ -326,7 +331,8 @@ class V4FlashModel:
             pool_native, planes = self.pool.swa[layer], None
         o, _ = attn_ops.sparse_mla_decode(
             q, self.pool.swa[layer], meta.swa_slots, meta.swa_len, csa_slots, csa_pos, csa_len, self.freqs,
-            lw["sink"], self.scale, meta.positions_i32, csa_pool=pool_native, csa_planes=planes)
+            lw["sink"], self.scale, meta.positions_i32, csa_pool=pool_native, csa_planes=planes,
+            csa_fp4=self.pool.fp4_format if ratio == abi.C4_RATIO else None)
         return self._o_proj(layer, o, B)
 
     def _adapter_rows(self, planes, csa_slots: torch.Tensor, csa_pos: torch.Tensor):
@@ -486,7 +492,8 @@ class V4FlashModel:
                 pool_native, planes = self.pool.swa[layer], None
             o, _ = attn_ops.sparse_mla_decode(
                 q.contiguous(), scratch, swa_slots, swa_len, csa_slots, csa_pos, csa_len, self.freqs, lw["sink"],
-                self.scale, meta_pos.int(), csa_pool=pool_native, csa_planes=planes)
+                self.scale, meta_pos.int(), csa_pool=pool_native, csa_planes=planes,
+                csa_fp4=self.pool.fp4_format if ratio == abi.C4_RATIO else None)
             a = self._o_proj(layer, o, T)
             x, h = fused_ops.add_rmsnorm(x, n_ffn, eps, a, inplace=True)
             d, dfp = self._moe_block(layer, h)

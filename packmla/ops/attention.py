@@ -106,21 +106,26 @@ def sparse_mla_decode(
     out: torch.Tensor | None = None,
     lse: torch.Tensor | None = None,
     prof: torch.Tensor | None = None,
+    csa_fp4: str | None = None,
 ):
     """q [B,H,512] bf16 (tail rotated by the query position) -> (out bf16 [B,H,512], lse fp32 [B,H]).
 
     SWA rows: Native records at `swa_slots` [B, W] (first `swa_len[b]` used; -1 = masked).
     C4 rows: `csa_slots` [B, K] physical records, `csa_pos` [B, K] token positions (RoPE rows
     for Packed), first `csa_len[b]` used.  Exactly one of csa_pool (Native pages) /
-    csa_planes (Packed) is given.  `freqs` is float32 [P, 32, 2].  `prof` (optional int64 [64] on the
+    csa_planes (Packed) is given.  With `csa_fp4` ("native" or "direct") csa_pool holds FP4 pages of the V4.1
+    cache (packmla.formats.fp4: Native 288 B or Packed 224 B records, RoPE applied at store, so `csa_pos` is
+    not read).  `freqs` is float32 [P, 32, 2].  `prof` (optional int64 [64] on the
     device) receives global-timer stamps of the first CTA's pipeline steps, for latency analysis.
     """
     if (csa_pool is None) == (csa_planes is None):
         raise ValueError("give exactly one of csa_pool (native) or csa_planes (packed)")
+    if csa_fp4 not in (None, "native", "direct") or (csa_fp4 and csa_pool is None):
+        raise ValueError("csa_fp4 is 'native' or 'direct' and reads csa_pool")
     B, H, _ = q.shape
     if not q.is_cuda:
         return _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos,
-                           csa_pool, csa_planes)
+                           csa_pool, csa_planes, csa_fp4)
     if num_splits is None:
         if workspace is not None:
             num_splits = workspace.splits
@@ -143,11 +148,13 @@ def sparse_mla_decode(
         q, swa_pool, swa_slots, swa_len, packed, native_pool, values, bitmap, scales,
         csa_slots, csa_pos, csa_len, freqs, sink, float(scale), q_pos, int(num_splits),
         workspace.part_o, workspace.part_ml, out, lse, error_word(dev), prof,
+        {None: 0, "native": 1, "direct": 2}[csa_fp4],
     )
     return out, lse
 
 
-def gather_rows_cpu(swa_pool, swa_slots_b, n_swa, csa_slots_b, csa_pos_b, n_csa, freqs, csa_pool, csa_planes):
+def gather_rows_cpu(swa_pool, swa_slots_b, n_swa, csa_slots_b, csa_pos_b, n_csa, freqs, csa_pool, csa_planes,
+                    csa_fp4=None):
     """Decoded fp32 rows [N, 512] of one query (masked -1 entries dropped)."""
     rows = []
     s = swa_slots_b[:n_swa].long()
@@ -159,7 +166,12 @@ def gather_rows_cpu(swa_pool, swa_slots_b, n_swa, csa_slots_b, csa_pos_b, n_csa,
     valid = c >= 0
     c, p = c[valid], p[valid]
     if c.numel():
-        if csa_planes is None:
+        if csa_fp4 is not None:
+            from ..formats import fp4
+
+            pages = csa_pool.cpu().view(-1, fp4.page_bytes(csa_fp4))
+            rows.append(fp4.gather_rows(pages, csa_fp4, c))
+        elif csa_planes is None:
             rows.append(codec.native_decode(native_pool_read(csa_pool, c).cpu()))
         else:
             fr = torch.view_as_complex(freqs[p].float().contiguous()).cpu()
@@ -171,11 +183,11 @@ def gather_rows_cpu(swa_pool, swa_slots_b, n_swa, csa_slots_b, csa_pos_b, n_csa,
 
 
 def _decode_cpu(q, swa_pool, swa_slots, swa_len, csa_slots, csa_pos, csa_len, freqs, sink, scale, q_pos, csa_pool,
-                csa_planes):
+                csa_planes, csa_fp4=None):
     B = q.shape[0]
     kv = []
     for b in range(B):
         kv.append(gather_rows_cpu(swa_pool, swa_slots[b], int(swa_len[b]), csa_slots[b], csa_pos[b], int(csa_len[b]),
-                                  freqs, csa_pool, csa_planes))
+                                  freqs, csa_pool, csa_planes, csa_fp4))
     qf = torch.view_as_complex(freqs[q_pos.long()].float().contiguous())
     return oracle.sparse_mla_decode(q.float(), kv, sink.float(), scale, qf)

@@ -30,7 +30,8 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=30000)
     ap.add_argument("--device", default="cuda")
-    ap.add_argument("--kv-cache-format", default="direct", choices=["native", "direct"])
+    ap.add_argument("--kv-cache-format", default="direct", choices=["native", "direct", "fp4-native", "fp4-direct"],
+                    help="C4 cache: FP8 Native / Packed records, or the FP4 (V4.1) Native / Packed records")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--mem-fraction-static", type=float, default=0.88)
     ap.add_argument("--max-running-requests", type=int, default=64)

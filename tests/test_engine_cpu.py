@@ -16,7 +16,7 @@ def _rel(a, b):
 def test_prefill_chunking_and_decode_agree():
     cfg = ModelConfig.tiny(num_layers=4)
     W = init_weights(cfg)
-    for fmt in ("direct", "native"):
+    for fmt in ("direct", "native", "fp4-native", "fp4-direct"):
         pool = KVPool(cfg, EngineConfig(kv_cache_format=fmt, device="cpu"), 16, 4, 1024, "cpu")
         m = V4FlashModel(cfg, W, pool)
         toks = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(0))
@@ -60,6 +60,10 @@ def test_engine_config_rejects_unsupported():
         EngineConfig(kv_cache_format="direct", keep_count=192).validate()
     with pytest.raises(ValueError):
         EngineConfig(kv_cache_format="packed").validate()
+    with pytest.raises(ValueError, match="HiCache"):
+        EngineConfig(kv_cache_format="fp4-direct", enable_hierarchical_cache=True).validate()
+    with pytest.raises(ValueError, match="adapter"):
+        EngineConfig(kv_cache_format="fp4-direct", decode_impl="adapter").validate()
     with pytest.raises(ValueError):
         EngineConfig(kv_cache_format="native", enable_hierarchical_cache=True, keep_count=128).validate()
 

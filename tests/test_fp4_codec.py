@@ -186,3 +186,38 @@ def test_fp4_store_cpu_path_writes_the_page_layout():
         pool = torch.zeros(fp4.page_bytes(fmt), dtype=torch.uint8)
         kv_ops.fp4_store(raw, w, 1e-6, slots, pos, freqs, pool, packed)
         assert torch.equal(pool, fp4.write_page(fmt, rows[order]))
+
+
+def test_decode_op_cpu_path_matches_the_fp4_reference():
+    """The attention op's CPU path over an FP4 pool equals fp4.sparse_decode_reference (SWA rows decoded
+    from their Native pool)."""
+    from packmla.formats import abi, codec, fp4
+    from packmla.ops import attention as attn_ops
+    from packmla.ops import kv as kv_ops
+
+    g = torch.Generator().manual_seed(11)
+    freqs = kv_ops.freq_table_f32(codec.rope_table(256))
+    w = torch.rand(512, generator=g) + 0.5
+    swa_pool = torch.zeros(abi.NATIVE_PAGE_BYTES, dtype=torch.uint8)
+    kv_ops.native_store(torch.randn(64, 512, generator=g), w, 1e-6, torch.arange(64), torch.arange(64), freqs, swa_pool)
+    for fmt in ("native", "direct"):
+        pool = torch.zeros(2 * fp4.page_bytes(fmt), dtype=torch.uint8)
+        kv_ops.fp4_store(torch.randn(100, 512, generator=g), w, 1e-6, torch.arange(100), torch.arange(100), freqs,
+                         pool, fmt == "direct")
+        B, H = 2, 4
+        q = torch.randn(B, H, 512, generator=g).bfloat16()
+        swa_slots = torch.randint(0, 64, (B, 8), generator=g, dtype=torch.int32)
+        swa_len = torch.tensor([8, 5], dtype=torch.int32)
+        csa_slots = torch.randint(0, 100, (B, 16), generator=g, dtype=torch.int32)
+        csa_slots[1, 2] = -1
+        csa_len = torch.tensor([16, 11], dtype=torch.int32)
+        sink, q_pos = torch.randn(H, generator=g), torch.tensor([3, 200], dtype=torch.int32)
+        o, lse = attn_ops.sparse_mla_decode(q, swa_pool, swa_slots, swa_len, csa_slots, torch.zeros_like(csa_slots),
+                                            csa_len, freqs, sink, 0.05, q_pos, csa_pool=pool, csa_fp4=fmt)
+        swa_rows = [codec.native_decode(attn_ops.native_pool_read(swa_pool, swa_slots[b, : swa_len[b]].long()))
+                    for b in range(B)]
+        qf = torch.view_as_complex(freqs[q_pos.long()].contiguous())
+        ro, rl = fp4.sparse_decode_reference(q.float(), pool.view(2, -1), fmt, csa_slots, csa_len, swa_rows, sink,
+                                             0.05, qf)
+        torch.testing.assert_close(o.float(), ro.float(), atol=0, rtol=0)
+        torch.testing.assert_close(lse, rl, atol=0, rtol=0)

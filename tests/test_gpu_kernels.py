@@ -168,3 +168,44 @@ def test_fp4_store_byte_exact(cuda, packed, rows):
     check_errors(cuda)
     kv_ops.fp4_store(raw, weight, 1e-6, slots, pos, freqs, pool, packed)
     assert torch.equal(gpool.cpu(), pool)
+
+
+@pytest.mark.parametrize("fmt", ["native", "direct"])
+@pytest.mark.parametrize("B,H,K,splits,qscale", [(2, 64, 512, None, 0.5), (3, 16, 317, 1, 0.5),
+                                                  (2, 128, 512, 3, 0.5), (2, 64, 1024, 2, 24.0),
+                                                  (1, 64, 1536, 8, 0.5)])
+def test_fp4_decode_matches_oracle(cuda, fmt, B, H, K, splits, qscale):
+    """GPU decode over FP4 C4 records (V4.1 cache: Native 288 B / Packed 224 B) beside Native SWA rows vs the
+    fp32 oracle, which decodes the same pages on the CPU."""
+    from packmla.formats import fp4
+
+    seed = 7000 + B * 100 + H + K
+    g = torch.Generator().manual_seed(seed)
+    W = 128
+    n_swa, n_csa = 2 * W * B, 4 * K * B
+    freqs, swa_pool, _, _, posrow = _build_cache(seed, n_swa, 0, False)
+    w = torch.rand(512, generator=g) + 0.5
+    pages = (n_csa + 63) // 64
+    pool = torch.zeros(pages * fp4.page_bytes(fmt), dtype=torch.uint8)
+    posrow = torch.randint(0, 8000, (n_csa,), generator=g)
+    kv_ops.fp4_store(torch.randn(n_csa, 512, generator=g), w, 1e-6, torch.arange(n_csa), posrow, freqs, pool,
+                     fmt == "direct")
+    swa_slots = torch.randint(0, n_swa, (B, W), generator=g, dtype=torch.int32)
+    swa_len = torch.randint(W // 2, W + 1, (B,), generator=g, dtype=torch.int32)
+    csa_slots = torch.randint(0, n_csa, (B, K), generator=g, dtype=torch.int32)
+    csa_slots[0, 3] = -1
+    csa_len = torch.randint(K // 2, K + 1, (B,), generator=g, dtype=torch.int32)
+    csa_len[0] = K
+    csa_pos = posrow[csa_slots.clamp(min=0).long()].int()
+    q = (torch.randn(B, H, 512, generator=g) * qscale).bfloat16()
+    sink = torch.randn(H, generator=g)
+    q_pos = torch.randint(0, 8000, (B,), generator=g, dtype=torch.int32)
+    args = dict(swa_slots=swa_slots, swa_len=swa_len, csa_slots=csa_slots, csa_pos=csa_pos, csa_len=csa_len,
+                sink=sink, scale=1 / 512 ** 0.5, q_pos=q_pos)
+    ref_o, ref_lse = attn_ops.sparse_mla_decode(q, swa_pool, freqs=freqs, csa_pool=pool, csa_fp4=fmt, **args)
+    dev = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in args.items()}
+    o, lse = attn_ops.sparse_mla_decode(q.cuda(), swa_pool.cuda(), freqs=freqs.cuda(), csa_pool=pool.cuda(),
+                                        csa_fp4=fmt, num_splits=splits, **dev)
+    check_errors(cuda)
+    torch.testing.assert_close(o.float().cpu(), ref_o.float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(lse.cpu(), ref_lse, atol=2e-2, rtol=2e-2)

@@ -104,7 +104,7 @@ def test_moe_fp4_expert_parallel_partials_sum(cuda):
 
 
 @pytest.mark.parametrize("precision", ["bf16", "default"])
-@pytest.mark.parametrize("fmt", ["direct", "native"])
+@pytest.mark.parametrize("fmt", ["direct", "native", "fp4-native", "fp4-direct"])
 def test_engine_gpu_matches_cpu_oracle(cuda, fmt, precision):
     """GPU engine vs the CPU oracle engine.
 
