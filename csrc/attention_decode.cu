@@ -815,7 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
         else
           pm::bulk_s2g(p.part_o + (part * p.H + h0) * kD, sPart, (uint32_t)nh * kD * 4u);
         pm::bulk_commit();
-        pm::bulk_wait_all();  // written before the CTA exits (and before dependents read it)
+        pm::bulk_wait_read_all();  // the staging is read before the CTA exits; the writes complete with the grid
         stamp(51);
       }
     } else {

@@ -422,6 +422,9 @@ __device__ __forceinline__ void bulk_s2g(void* gmem_dst, const void* smem_src, u
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // every committed bulk group of this thread complete (writes performed)
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// every committed bulk group of this thread has read its shared-memory source (the buffer may be reused or
+// the CTA may exit; the writes complete with the grid)
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // Programmatic dependent launch: wait until the grids this launch depends on have completed and their
 // memory is visible (a no-op for a launch without the attribute), and allow dependent grids to start.

@@ -55,7 +55,7 @@ class StepMeta:
     c128_pos: torch.Tensor  # [B, R128] int32
     c128_len: torch.Tensor  # [B] int32
     c128_write: torch.Tensor  # [B] int64
-    no_rows: torch.Tensor  # [B, 1] int32 filled with -1 (layers without compressed records)
+    no_rows: torch.Tensor  # [B, 0] int32 (layers without compressed records: an empty C4 list)
     zero_len: torch.Tensor  # [B] int32 zeros
     topk_len: torch.Tensor  # [B] int32 = index top-k
     positions_i32: torch.Tensor  # [B] int32
@@ -239,7 +239,7 @@ class V4FlashModel:
         c128_len = torch.full((B,), self.r128max, dtype=torch.int32, device=dev)
         return StepMeta(pos, req, swa_slots, swa_len, swa_write, c4_phys.int(), c4_count, c4_write,
                         c128_slots, c128_pos, c128_len, c128_write,
-                        torch.full((B, 1), -1, dtype=torch.int32, device=dev),
+                        torch.empty((B, 0), dtype=torch.int32, device=dev),
                         torch.zeros(B, dtype=torch.int32, device=dev),
                         torch.full((B,), self.topk, dtype=torch.int32, device=dev), pos.int())
 
@@ -486,8 +486,8 @@ class V4FlashModel:
                 csa_len = torch.full((T,), lim, dtype=torch.int32, device=dev)
                 pool_native, planes = self.pool.c128_native[layer], None
             else:
-                csa_slots = torch.full((T, 1), -1, dtype=torch.int32, device=dev)
-                csa_pos = torch.zeros((T, 1), dtype=torch.int32, device=dev)
+                csa_slots = torch.empty((T, 0), dtype=torch.int32, device=dev)
+                csa_pos = torch.empty((T, 0), dtype=torch.int32, device=dev)
                 csa_len = torch.zeros(T, dtype=torch.int32, device=dev)
                 pool_native, planes = self.pool.swa[layer], None
             o, _ = attn_ops.sparse_mla_decode(
