@@ -78,7 +78,7 @@ def run_phase(eng, prompts: list[list[int]], params, comm, device, timed: bool) 
         torch.cuda.synchronize(device)
     wall = time.perf_counter() - t0
     comm.barrier()
-    out_tokens = sum(len(eng.result(r).output_ids) for r in rids)
+    out_tokens = sum(len(eng.result(r).output_ids) for r in rids if eng.owns(r))  # this rank's requests
     stats = {"wall_s": wall, "engine_steps": n_steps, "out_tokens": out_tokens, "h2d": h2d, "d2h": d2h}
     if timed:
         dec_ms = pre_ms = 0.0
@@ -112,6 +112,9 @@ def main() -> None:
     ap.add_argument("--collectives", default="auto", choices=["auto", "fused", "nccl"],
                     help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL; auto = fused "
                          "at the world sizes the fused kernels were validated on (2), NCCL otherwise")
+    ap.add_argument("--dp-attention", default="auto", choices=["auto", "on", "off"],
+                    help="DP attention (each rank serves C/N requests with every head, MoE tokens exchanged by "
+                         "all-gather / reduce-scatter) or TP attention; auto = TP")
     ap.add_argument("--oproj-gemm", default="auto", choices=["auto", "fused", "library"],
                     help="with fused collectives: projection inside the all-reduce kernel, cuBLAS first, or "
                          "by token count")
@@ -139,8 +142,13 @@ def main() -> None:
     torch.cuda.set_device(device)
     cfg = ModelConfig(dense_format=args.dense_format)
     C = args.concurrency or DEFAULT_CONCURRENCY.get(world, 8 * world)
+    dp = world > 1 and args.dp_attention == "on"
+    if dp and C % world:
+        raise SystemExit(f"--dp-attention: concurrency {C} must be a multiple of {world}")
     if args.collectives == "auto":
-        args.collectives = "fused" if world == 2 else "nccl"
+        args.collectives = "fused" if world == 2 and not dp else "nccl"
+    if dp and args.collectives == "fused":
+        raise SystemExit("--dp-attention exchanges MoE tokens over NCCL: use --collectives nccl")
     if world > 1 and args.collectives == "fused":
         from packmla.parallel.fused import FusedComm
 
@@ -149,13 +157,13 @@ def main() -> None:
         comm = TPComm()
     t0 = time.time()
     eng, max_context = build_engine(cfg, device, rank, world, comm, C, args.prompt_len, args.output_len,
-                                    args.kv_format, args.seed)
+                                    args.kv_format, args.seed, dp_attention=dp)
     eng.runner.capture()
     torch.cuda.synchronize(device)
     # kernel launches of one decode step (an eager forward at the dummy slot, counted by the extension proxy)
     ext = _ext.ext()
     ext.launches, ext.enabled = 0, True
-    eng.runner._forward(C)
+    eng.runner._forward(eng.runner.max_b)
     ext.enabled = False
     launches_per_decode = ext.launches
     eng.pool.comp_state_reset(eng.dummy_slot)
@@ -186,7 +194,7 @@ def main() -> None:
     wall_s = comm.max_over_ranks(st["wall_s"], device)
     pre_ms = comm.max_over_ranks(st["prefill_ms"], device)
     n_req = 3 * C
-    out_tokens = st["out_tokens"]
+    out_tokens = int(comm.sum_over_ranks(st["out_tokens"], device)) if dp else st["out_tokens"]
     dec_tokens = out_tokens - n_req  # each request's first token comes from its prefill
     value = dec_tokens / (dec_ms / 1000.0)
     e2e = out_tokens / wall_s
@@ -220,7 +228,7 @@ def main() -> None:
             "requests_measured": n_req,
             "prefix_cache": "on, flushed between the warm-up and measured phases",
             "chunked_prefill": 8192,
-            "parallelism": f"tp{world}ep{world}",
+            "parallelism": (f"dp{world}-attention ep{world}" if dp else f"tp{world}ep{world}"),
             "collectives": (f"{args.collectives}/oproj-{args.oproj_gemm}" if args.collectives == "fused"
                             else args.collectives) if world > 1 else "none",
             "kv_cache_format": args.kv_format,

@@ -1,7 +1,7 @@
 // Adapter: Packed C4 records (values / bitmap / scales planes) -> Native 584 B records in a paged
 // workspace, so a Native reader can consume Packed KV (reference: `packed_to_native.cu`, the CUDA
-// Adapter mode that reconstructs the selected rows before stock FlashMLA; 256 survivors only,
-// 64-bit addressing).
+// Adapter mode that reconstructs the selected rows before stock FlashMLA, 64-bit addressing).  Any
+// survivor count: the values plane holds `keep` bytes per row (64 .. 448; the default layout 256).
 //
 // One warp per record.  Lane l owns the 16 consecutive coordinates [16 l, 16 l + 16): bits
 // 16 (l % 4) .. + 15 of bitmap word l / 4.  A warp prefix sum of the lanes' popcounts gives each lane
@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(256) packed_to_native_kernel(
     const uint8_t* __restrict__ values, const uint64_t* __restrict__ bitmap, const uint8_t* __restrict__ scales,
     int64_t src_rows_total, const int32_t* __restrict__ rows, const int32_t* __restrict__ positions,
     const float* __restrict__ freqs, int64_t freq_rows, uint8_t* __restrict__ out, const int64_t* __restrict__ dst,
-    int64_t out_slots, int n, int* err) {
+    int64_t out_slots, int keep, int n, int* err) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
@@ -44,13 +44,13 @@ __global__ void __launch_bounds__(256) packed_to_native_kernel(
   }
   int k = incl - cnt;  // index of this lane's first kept value
   const float scale = pm::exp2i((int)scales[row * 8 + (lane >> 2)] - 127);
-  const uint8_t* vrow = values + row * 256;
+  const uint8_t* vrow = values + row * keep;
   float x[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     x[i] = 0.f;
     if (bits & (1u << i)) {
-      const uint16_t code = k < 256 ? vrow[k] : 0;  // a corrupt bitmap (> 256 bits) reads no further
+      const uint16_t code = k < keep ? vrow[k] : 0;  // a corrupt bitmap (> keep bits) reads no further
       ++k;
       x[i] = __low2float(pm::e4m3x2_to_h2(code)) * scale;  // exact: E4M3 x power of two
     }
@@ -101,9 +101,9 @@ __global__ void __launch_bounds__(256) packed_to_native_kernel(
 
 void launch_packed_to_native(const uint8_t* values, const uint64_t* bitmap, const uint8_t* scales, int64_t src_rows,
                              const int32_t* rows, const int32_t* positions, const float* freqs, int64_t freq_rows,
-                             uint8_t* out, const int64_t* dst, int64_t out_slots, int n, int* err,
+                             uint8_t* out, const int64_t* dst, int64_t out_slots, int keep, int n, int* err,
                              cudaStream_t stream) {
   if (n <= 0) return;
   packed_to_native_kernel<<<(n + 7) / 8, 256, 0, stream>>>(values, bitmap, scales, src_rows, rows, positions, freqs,
-                                                           freq_rows, out, dst, out_slots, n, err);
+                                                           freq_rows, out, dst, out_slots, keep, n, err);
 }

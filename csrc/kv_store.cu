@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256) native_store_kernel(
 __global__ void __launch_bounds__(256) packed_store_kernel(
     const float* __restrict__ raw, int64_t raw_stride, const float* __restrict__ weight, float eps,
     const int64_t* __restrict__ slots, uint8_t* __restrict__ values, uint64_t* __restrict__ bitmap,
-    uint8_t* __restrict__ scales, int64_t pool_rows, int rows, int* err) {
+    uint8_t* __restrict__ scales, int64_t pool_rows, int keep_n, int rows, int* err) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
 #pragma unroll
   for (int k = 0; k < 16; ++k) key[k] = __float_as_uint(x[k]) & 0x7FFFFFFFu;
 
-  // T = largest value with count(key >= T) >= 256  (the 256th largest magnitude)
+  // T = largest value with count(key >= T) >= keep_n  (the keep_n-th largest magnitude)
   uint32_t T = 0;
 #pragma unroll 1
   for (int bit = 30; bit >= 0; --bit) {
@@ -143,13 +143,13 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
 #pragma unroll
     for (int k = 0; k < 16; ++k) c += key[k] >= cand;
     c = __reduce_add_sync(0xffffffffu, c);
-    if (c >= 256) T = cand;
+    if (c >= keep_n) T = cand;
   }
   int gt = 0;
 #pragma unroll
   for (int k = 0; k < 16; ++k) gt += key[k] > T;
   gt = __reduce_add_sync(0xffffffffu, gt);
-  const int need = 256 - gt;  // equal-to-T elements to keep, lowest coordinates first
+  const int need = keep_n - gt;  // equal-to-T elements to keep, lowest coordinates first
 
   bool keep[16];
   int eq_before = 0;  // equal elements in earlier chunks (warp-uniform)
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
       y[4 * j + i] = bf16_round(__fmul_rn(__fmul_rn(xm[4 * j + i], r), w));
     }
 
-  uint8_t* vrow = values + slot * 256;
+  uint8_t* vrow = values + slot * keep_n;
   int out_before = 0;
   int codes[4];
   uint64_t words[4];
@@ -252,9 +252,9 @@ void launch_native_store(const float* raw, int64_t raw_stride, const float* weig
 }
 
 void launch_packed_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
-                         uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int rows, int* err,
-                         cudaStream_t stream) {
+                         uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int keep, int rows,
+                         int* err, cudaStream_t stream) {
   if (rows == 0) return;
   packed_store_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(raw, raw_stride, weight, eps, slots, values, bitmap, scales,
-                                                          pool_rows, rows, err);
+                                                          pool_rows, keep, rows, err);
 }

@@ -10,8 +10,8 @@ void launch_native_store(const float* raw, int64_t raw_stride, const float* weig
                          const int64_t* positions, const float* freqs, int64_t freq_rows, uint8_t* pool,
                          int64_t pool_slots, int rows, int* err, cudaStream_t stream);
 void launch_packed_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
-                         uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int rows, int* err,
-                         cudaStream_t stream);
+                         uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int keep, int rows,
+                         int* err, cudaStream_t stream);
 
 // Sparse MLA decode (csrc/attention_decode.cu).  A query's rows [SWA ; C4] are split into 64-row
 // stages; split s of num_splits takes an even share of whole stages.
@@ -231,5 +231,5 @@ int launch_segment_copy(const int64_t* segs_dev, int nseg, int num_sms, cudaStre
 // Adapter: Packed planes rows -> Native records at dst slots of a paged workspace.
 void launch_packed_to_native(const uint8_t* values, const uint64_t* bitmap, const uint8_t* scales, int64_t src_rows,
                              const int32_t* rows, const int32_t* positions, const float* freqs, int64_t freq_rows,
-                             uint8_t* out, const int64_t* dst, int64_t out_slots, int n, int* err,
+                             uint8_t* out, const int64_t* dst, int64_t out_slots, int keep, int n, int* err,
                              cudaStream_t stream);

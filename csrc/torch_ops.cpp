@@ -50,7 +50,9 @@ void packed_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Te
   check_err(err);
   TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == torch::kFloat32 && weight.numel() == kD && weight.is_contiguous());
   TORCH_CHECK(slots.scalar_type() == torch::kInt64 && slots.numel() == raw.size(0) && slots.is_contiguous());
-  TORCH_CHECK(values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.size(1) == 256 && values.is_contiguous());
+  TORCH_CHECK(values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.is_contiguous());
+  TORCH_CHECK(values.size(1) >= 64 && values.size(1) <= 448 && values.size(1) % 64 == 0,
+              "values rows hold the survivor count: 64 .. 448 in steps of 64");
   TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.dim() == 2 && bitmap.size(1) == 8 && bitmap.is_contiguous());
   TORCH_CHECK(scales.scalar_type() == torch::kUInt8 && scales.dim() == 2 && scales.size(1) == 8 && scales.is_contiguous());
   TORCH_CHECK(bitmap.size(0) == values.size(0) && scales.size(0) == values.size(0));
@@ -58,7 +60,7 @@ void packed_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Te
   launch_packed_store(raw.data_ptr<float>(), raw.stride(0), weight.data_ptr<float>(), (float)eps,
                       slots.data_ptr<int64_t>(), values.data_ptr<uint8_t>(),
                       reinterpret_cast<uint64_t*>(bitmap.data_ptr<int64_t>()), scales.data_ptr<uint8_t>(),
-                      values.size(0), raw.size(0), err.data_ptr<int>(), stream());
+                      values.size(0), (int)values.size(1), raw.size(0), err.data_ptr<int>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -621,8 +623,9 @@ void packed_to_native(torch::Tensor values, torch::Tensor bitmap, torch::Tensor 
                       torch::Tensor positions, torch::Tensor freqs, torch::Tensor out, torch::Tensor dst,
                       torch::Tensor err) {
   check_err(err);
-  TORCH_CHECK(values.is_cuda() && values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.size(1) == 256 &&
-              values.is_contiguous(), "values must be CUDA uint8 [rows, 256]");
+  TORCH_CHECK(values.is_cuda() && values.scalar_type() == torch::kUInt8 && values.dim() == 2 && values.size(1) >= 64 &&
+              values.size(1) <= 448 && values.size(1) % 64 == 0 && values.is_contiguous(),
+              "values must be CUDA uint8 [rows, keep], keep 64 .. 448 in steps of 64");
   TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.is_contiguous() && bitmap.size(0) == values.size(0) &&
               bitmap.size(1) == 8, "bitmap must be int64 [rows, 8]");
   TORCH_CHECK(scales.scalar_type() == torch::kUInt8 && scales.is_contiguous() && scales.size(0) == values.size(0) &&
@@ -637,8 +640,8 @@ void packed_to_native(torch::Tensor values, torch::Tensor bitmap, torch::Tensor 
   launch_packed_to_native(values.data_ptr<uint8_t>(), reinterpret_cast<const uint64_t*>(bitmap.data_ptr<int64_t>()),
                           scales.data_ptr<uint8_t>(), values.size(0), rows.data_ptr<int32_t>(),
                           positions.data_ptr<int32_t>(), freqs.data_ptr<float>(), freqs.size(0), out.data_ptr<uint8_t>(),
-                          dst.data_ptr<int64_t>(), out.numel() / kNativePageBytes * kPage, (int)rows.numel(),
-                          err.data_ptr<int>(), stream());
+                          dst.data_ptr<int64_t>(), out.numel() / kNativePageBytes * kPage, (int)values.size(1),
+                          (int)rows.numel(), err.data_ptr<int>(), stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

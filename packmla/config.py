@@ -155,6 +155,10 @@ class EngineConfig:
     # SGLang's radix prefix cache on; the server turns this on unless --disable-radix-cache)
     prefix_cache: bool = False
     keep_count: int = abi.PACKED_KEEP
+    # per-layer survivor counts of the Packed C4 layout (model layer index -> count, 64 .. 448 in steps of
+    # 64; the reference's --dsv4-c4-cache-layer-keep-counts).  Fixed at start-up; a layer's values plane is
+    # count bytes per record.  Counts other than 256 are read by reconstruction (decode_impl "adapter").
+    layer_keep_counts: dict[int, int] | None = None
     swa_full_tokens_ratio: float = 0.1
     random_seed: int = 0
     device: str = "cuda"
@@ -165,6 +169,15 @@ class EngineConfig:
     # C4 attention over Packed KV: "direct" reads the planes inside the attention kernel; "adapter"
     # first reconstructs the selected rows as Native records (the reference's Adapter mode)
     decode_impl: str = "direct"
+    # DP attention (the reference server's --enable-dp-attention): each rank serves its own requests with
+    # every attention head; only the routed experts are split, and every MoE block exchanges tokens
+    # between the ranks (all-gather in, reduce-scatter out).  Per-rank attention work does not grow with
+    # the number of ranks.
+    dp_attention: bool = False
+
+    def keep_for(self, layer: int) -> int:
+        """Survivor count of a C4 layer's Packed records."""
+        return (self.layer_keep_counts or {}).get(layer, self.keep_count)
 
     def validate(self) -> None:
         """Reject unsupported combinations before any pool allocation.
@@ -174,11 +187,19 @@ class EngineConfig:
         """
         if self.kv_cache_format not in KV_FORMATS:
             raise ValueError(f"--kv-cache-format must be one of {KV_FORMATS}")
-        if self.kv_cache_format in ("direct", "fp4-direct") and self.keep_count != abi.PACKED_KEEP:
-            raise ValueError("direct serving supports keep_count 256 only")
+        counts = {self.keep_count, *(self.layer_keep_counts or {}).values()}
+        for c in counts:
+            if not (64 <= c <= 448 and c % 64 == 0):
+                raise ValueError(f"survivor count {c}: 64 .. 448 in steps of 64")
+        if counts != {abi.PACKED_KEEP}:
+            if self.kv_cache_format != "direct":
+                raise ValueError("per-layer survivor counts are a Packed (direct) layout")
+            if self.decode_impl != "adapter":
+                raise ValueError("direct serving supports keep_count 256 only: survivor counts other than 256 are "
+                                 "read by reconstruction (decode_impl adapter)")
         if self.kv_cache_format.startswith("fp4-") and self.enable_hierarchical_cache:
             raise ValueError("the FP4 cache formats do not support HiCache")
-        if self.enable_hierarchical_cache and self.keep_count != abi.PACKED_KEEP:
+        if self.enable_hierarchical_cache and counts != {abi.PACKED_KEEP}:
             raise ValueError("HiCache requires the 256-survivor layout")
         if not 0.0 < self.mem_fraction_static <= 0.98:
             raise ValueError("mem_fraction_static must be in (0, 0.98]")

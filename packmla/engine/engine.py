@@ -10,7 +10,10 @@ Public API (what the HTTP server and bench.py call):
 Reference behaviour: SGLang scheduler + `decode_cuda_graph_runner.py` (third_party/README.md:294-298):
 chunked prefill (8192), full decode CUDA graphs for padded batch sizes, FCFS admission bounded by
 the KV pool.  Multi-rank: every rank runs the same deterministic schedule in lockstep; logits are
-identical on all ranks after the all-reduces, so sampling needs no broadcast.
+identical on all ranks after the all-reduces, so sampling needs no broadcast.  With DP attention
+(`EngineConfig.dp_attention`) request rid belongs to rank rid % world, which alone schedules and serves it;
+the ranks agree on each step's kind (prefill chunks or one decode step) and token counts through one
+small exchange per step, because every MoE block exchanges tokens between them.
 """
 from __future__ import annotations
 
@@ -89,6 +92,8 @@ class DecodeGraphRunner:
         self.pool_handle = None
 
     def _forward(self, b: int) -> None:
+        if self.model.dp:  # every rank runs the same padded batch in a DP decode step
+            self.model.dp_counts = [b] * self.model.world
         logits = self.model.decode(self.tokens[:b], self.positions[:b], self.slots[:b])
         self.out_tokens[:b] = sample(logits, self.temps[:b])
 
@@ -118,10 +123,12 @@ class DecodeGraphRunner:
         torch.cuda.current_stream(self.device).wait_stream(stream)
         self.model.pool.comp_state_reset(self.dummy_slot)
 
-    def run(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, temps: torch.Tensor) -> torch.Tensor:
-        """Inputs are (pinned) host or device tensors of length b; returns device token ids [b]."""
+    def run(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, temps: torch.Tensor,
+            pad_to: int = 0) -> torch.Tensor:
+        """Inputs are (pinned) host or device tensors of length b; returns device token ids [b].  The batch
+        runs padded to at least `pad_to` rows (DP attention: the batch every rank runs)."""
         b = tokens.shape[0]
-        bp = self.bucket(b) if self.enabled else b
+        bp = self.bucket(max(b, pad_to)) if self.enabled else max(b, pad_to)
         self.tokens[:b].copy_(tokens, non_blocking=True)
         self.positions[:b].copy_(positions, non_blocking=True)
         self.slots[:b].copy_(slots, non_blocking=True)
@@ -165,6 +172,10 @@ class Engine:
         self.comm = comm
         self.device = pool.device
         self.metrics = Metrics()
+        self.dp = bool(engine_cfg.dp_attention) and getattr(comm, "world", 1) > 1
+        self.rank = getattr(comm, "rank", 0)
+        self.world = getattr(comm, "world", 1)
+        self._owner: dict[int, int] = {}  # DP attention: owners other than rid % world (forked choices)
         self.dummy_slot = pool.max_requests - 1
         pool._free_slots.remove(self.dummy_slot)
         self.waiting: deque[Request] = deque()
@@ -203,7 +214,8 @@ class Engine:
               seed: int = 0, weights: dict | None = None) -> "Engine":
         engine_cfg.validate()
         dev = torch.device(device)
-        W = weights if weights is not None else init_weights(model_cfg, rank, world, dev, seed)
+        W = weights if weights is not None else init_weights(model_cfg, rank, world, dev, seed,
+                                                             dp_attention=engine_cfg.dp_attention)
         if dev.type == "cuda" and model_cfg.expert_format == "mxfp4":
             from ..ops.moe import prepare_experts, prepare_experts_mx
 
@@ -232,6 +244,8 @@ class Engine:
         if not prompt:
             raise ValueError("empty prompt")
         req = Request(next(self._ids), list(prompt), params or SamplingParams(), t_arrival=time.perf_counter())
+        if not self.owns(req.rid):  # DP attention: another rank serves it
+            return req.rid
         self.waiting.append(req)
         self.metrics.inc("requests_received")
         return req.rid
@@ -245,6 +259,11 @@ class Engine:
             return [lead]
         followers = [Request(next(self._ids), list(prompt), params or SamplingParams(), t_arrival=time.perf_counter())
                      for _ in range(n - 1)]
+        if self.dp:  # the copies live where the leader's KV is
+            for f in followers:
+                self._owner[f.rid] = lead % self.world
+            if not self.owns(lead):
+                return [lead] + [f.rid for f in followers]
         self.forks[lead] = followers
         self.metrics.inc("requests_received", n - 1)
         return [lead] + [f.rid for f in followers]
@@ -276,10 +295,19 @@ class Engine:
             produced.append((f.rid, tok))
         return produced
 
+    def owns(self, rid: int) -> bool:
+        """Whether this rank serves request rid (always, unless DP attention spreads the requests)."""
+        return not self.dp or self._owner.get(rid, rid % self.world) == self.rank
+
     def has_work(self) -> bool:
+        if self.dp:  # any rank's work keeps every rank stepping (the MoE exchanges need all of them)
+            local = int(bool(self.waiting or self.running))
+            return any(v[0] for v in self.comm.exchange_ints([local], self.device))
         return bool(self.waiting or self.running or self.forks)
 
     def result(self, rid: int) -> Request:
+        if not self.owns(rid):
+            raise KeyError(f"request {rid} is served by rank {self._owner.get(rid, rid % self.world)}")
         return self.done[rid]
 
     def abort(self, rid: int) -> bool:
@@ -401,6 +429,8 @@ class Engine:
         Returns the (rid, token) pairs produced by this step.
         """
         rank = getattr(self.comm, "rank", 0)
+        if self.dp:
+            return self._step_dp()
         # with both kinds of work pending, prefill chunks and decode steps alternate: a queue of long
         # prompts must not stall the running requests' token streams for many steps
         if self.running and self._last_prefill and self.ecfg.prefill_decode_interleave:
@@ -416,6 +446,35 @@ class Engine:
             self._last_prefill = False
             with nvtx_range(f"scheduler.batch rank={rank} decode b={len(self.running)}"):
                 return self._decode()
+        return []
+
+    def _step_dp(self) -> list[tuple[int, int]]:
+        """One DP-attention step.  Every rank proposes (tokens of its next prefill chunk, running requests);
+        the step is a decode step when any rank has running requests and either the last step was a
+        prefill (interleaving) or no rank can prefill; otherwise a prefill step, in which ranks without a
+        chunk run a token-less forward.  Decode steps pad every rank to the same batch bucket."""
+        req = self._admit()
+        p_tok = min(self.ecfg.chunked_prefill_size, len(req.prompt) - req.prefilled) if req is not None else 0
+        plans = self.comm.exchange_ints([p_tok, len(self.running)], self.device)
+        any_prefill = any(p[0] for p in plans)
+        max_run = max(p[1] for p in plans)
+        if max_run and (not any_prefill or (self._last_prefill and self.ecfg.prefill_decode_interleave)):
+            self._last_prefill = False
+            with nvtx_range(f"scheduler.batch rank={self.rank} dp-decode b={len(self.running)} pad={max_run}"):
+                return self._decode(pad_to=max_run)
+        if not any_prefill:
+            return []
+        self._last_prefill = True
+        self.model.dp_counts = [p[0] for p in plans]
+        if req is not None:
+            with nvtx_range(f"scheduler.batch rank={self.rank} dp-prefill rid={req.rid} start={req.prefilled}"):
+                return self._prefill_chunk(req)
+        ev = self._events("prefill")
+        if ev is not None:
+            ev[0].record()
+        self.model.dp_idle_forward()
+        if ev is not None:
+            ev[1].record()
         return []
 
     def _events(self, kind: str):
@@ -453,7 +512,7 @@ class Engine:
             self.running.append(req)
         return [(req.rid, tok)] + forked
 
-    def _decode(self) -> list[tuple[int, int]]:
+    def _decode(self, pad_to: int = 0) -> list[tuple[int, int]]:
         reqs = self.running
         b = len(reqs)
         for i, r in enumerate(reqs):
@@ -465,7 +524,7 @@ class Engine:
         ev = self._events("decode")
         if ev is not None:
             ev[0].record()
-        out = self.runner.run(self._h_tokens[:b], self._h_pos[:b], self._h_slots[:b], self._h_temps[:b])
+        out = self.runner.run(self._h_tokens[:b], self._h_pos[:b], self._h_slots[:b], self._h_temps[:b], pad_to)
         self._h_out[:b].copy_(out, non_blocking=True)
         if ev is not None:
             ev[1].record()
@@ -478,8 +537,9 @@ class Engine:
             self._emit(r, tok)
             produced.append((r.rid, tok))
         self.running = [r for r in reqs if not r.finished]
-        self.metrics.inc("decode_steps")
-        self.metrics.inc("decode_tokens", b)
+        if b:
+            self.metrics.inc("decode_steps")
+            self.metrics.inc("decode_tokens", b)
         return produced
 
     def _emit(self, req: Request, tok: int) -> None:

@@ -42,14 +42,19 @@ class CapacityReport:
         return dict(self.__dict__)
 
 
-def c4_record_bytes(kv_format: str) -> int:
+def c4_record_bytes(kv_format: str, keep: int = abi.PACKED_KEEP) -> int:
+    """Logical bytes of one C4 record; a Packed record with K survivors is K + 72 bytes."""
     if kv_format.startswith("fp4-"):
         return fp4.record_bytes(kv_format[4:])
-    return abi.PACKED_RECORD_BYTES if kv_format == "direct" else abi.NATIVE_RECORD_BYTES
+    return keep + abi.BITMAP_WORDS * 8 + abi.NUM_TILES if kv_format == "direct" else abi.NATIVE_RECORD_BYTES
 
 
-def bytes_per_full_token(cfg: ModelConfig, kv_format: str, swa_ratio: float) -> float:
-    c4 = len(cfg.c4_layers) * (c4_record_bytes(kv_format) + cfg.index_dim + 4) / abi.C4_RATIO
+def bytes_per_full_token(cfg: ModelConfig, kv_format: str, swa_ratio: float,
+                         keep_for=None) -> float:
+    """`keep_for(layer)`: a C4 layer's Packed survivor count (default 256 everywhere); the layers' actual
+    record sizes are summed, smaller layouts are not padded."""
+    c4 = sum(c4_record_bytes(kv_format, keep_for(layer) if keep_for else abi.PACKED_KEEP) + cfg.index_dim + 4
+             for layer in cfg.c4_layers) / abi.C4_RATIO
     c128 = len(cfg.c128_layers) * abi.NATIVE_RECORD_BYTES / abi.C128_RATIO
     swa = swa_ratio * cfg.num_layers * abi.NATIVE_RECORD_BYTES
     return c4 + c128 + swa
@@ -68,7 +73,7 @@ def fixed_bytes(cfg: ModelConfig, max_requests: int) -> int:
 
 def plan_capacity(cfg: ModelConfig, ecfg: EngineConfig, available_bytes: int) -> CapacityReport:
     """Token capacity for a KV budget; pages of 256 tokens."""
-    bpt = bytes_per_full_token(cfg, ecfg.kv_cache_format, ecfg.swa_full_tokens_ratio)
+    bpt = bytes_per_full_token(cfg, ecfg.kv_cache_format, ecfg.swa_full_tokens_ratio, ecfg.keep_for)
     fixed = fixed_bytes(cfg, ecfg.max_running_requests)
     usable = max(0, available_bytes - fixed)
     tokens = int(usable // bpt)
@@ -127,12 +132,16 @@ class KVPool:
         self.fp4_format = self.kv_format[4:] if self.kv_format.startswith("fp4-") else None
         self.index_keys: dict[int, torch.Tensor] = {}
         self.index_scales: dict[int, torch.Tensor] = {}
+        unknown = set(ecfg.layer_keep_counts or {}) - set(cfg.c4_layers)
+        if unknown:
+            raise ValueError(f"survivor counts for layers without C4 records: {sorted(unknown)}")
+        self.keep = {layer: ecfg.keep_for(layer) for layer in cfg.c4_layers}
         for layer in cfg.c4_layers:
             if self.fp4_format is not None:
                 self.c4_fp4[layer] = torch.zeros(num_pages * fp4.page_bytes(self.fp4_format), dtype=torch.uint8,
                                                  device=dev)
             elif self.kv_format == "direct":
-                self.c4_values[layer] = torch.zeros(rows, abi.PACKED_KEEP, dtype=torch.uint8, device=dev)
+                self.c4_values[layer] = torch.zeros(rows, self.keep[layer], dtype=torch.uint8, device=dev)
                 self.c4_bitmap[layer] = torch.zeros(rows, abi.BITMAP_WORDS, dtype=torch.int64, device=dev)
                 self.c4_scales[layer] = torch.zeros(rows, abi.NUM_TILES, dtype=torch.uint8, device=dev)
             else:

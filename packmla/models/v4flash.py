@@ -74,15 +74,21 @@ class V4FlashModel:
         self.world = meta["world"]
         self.expert_base = meta["expert_base"]
         self.local_experts = meta["local_experts"]
-        self.heads = cfg.num_heads // self.world
-        self.groups = cfg.o_groups // self.world
+        # DP attention: this rank serves its own requests with every head; only the routed experts are
+        # split, and each MoE block exchanges tokens with the other ranks (all-gather in, reduce-scatter
+        # out).  `dp_counts` (tokens of every rank in the current forward, set by the caller) sizes it.
+        self.dp = bool(meta.get("dp_attention", False)) and self.world > 1
+        self.dp_counts: list[int] | None = None
+        attn_world = meta.get("attn_world", self.world)
+        self.heads = cfg.num_heads // attn_world
+        self.groups = cfg.o_groups // attn_world
         self.scale = 1.0 / math.sqrt(cfg.latent_dim)
         self.freqs = kv_ops.freq_table_f32(codec.rope_table(cfg.max_position, cfg.rope_theta)).to(self.device)
         self.r4max = pool.max_context // abi.C4_RATIO
         self.r128max = max(1, pool.max_context // abi.C128_RATIO)
         self.topk = min(cfg.index_topk, self.r4max)
         # fused output projection + all-reduce over peer memory (parallel.fused.FusedComm) when available
-        self.ar_hook = getattr(comm, "gemm_all_reduce", None) if self.world > 1 else None
+        self.ar_hook = getattr(comm, "gemm_all_reduce", None) if self.world > 1 and not self.dp else None
         self.moe_precision = "default"  # MXFP8 expert activations ("bf16": BF16 activations)
         # optional capture observer (packmla.training.data.capture): sees every C4 store and every decode
         # query of a C4 layer; None on the serving path
@@ -191,7 +197,7 @@ class V4FlashModel:
 
     # ------------------------------------------------------------------ helpers
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
-        if self.comm is None or self.world == 1:
+        if self.comm is None or self.world == 1 or self.dp:  # DP attention: the rank has every head
             return t
         return self.comm.all_reduce(t)
 
@@ -346,6 +352,20 @@ class V4FlashModel:
                                 self.freqs, self.adapter_ws, dst)
         return dst.view(B, K).int().contiguous(), self.adapter_ws, None
 
+    def _reconstruct_visible(self, planes, phys_row: torch.Tensor, n: int, csa_slots: torch.Tensor,
+                             csa_pos: torch.Tensor):
+        """Prefill over a Packed layout read by reconstruction (survivor counts other than 256): the
+        request's first n records -> Native records in a workspace (record r at slot r, RoPE at 4 r), and
+        the selected slots remapped to it (a C4 record's RoPE position is 4 x its index)."""
+        dev = self.device
+        r = torch.arange(n, device=dev, dtype=torch.int64)
+        src = phys_row[:n].long()
+        ws = torch.zeros(-(-n // abi.RECORDS_PER_PAGE) * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
+        kv_ops.packed_to_native(planes.values, planes.bitmap, planes.scales, src.clamp_min(0), r * abi.C4_RATIO,
+                                self.freqs, ws, torch.where(src >= 0, r, torch.full_like(r, -1)))
+        slots = torch.where(csa_slots >= 0, csa_pos // abi.C4_RATIO, torch.full_like(csa_slots, -1))
+        return slots.int().contiguous(), ws, None
+
     def _o_proj(self, layer: int, o: torch.Tensor, B: int) -> torch.Tensor:
         cfg = self.cfg
         lw = self.W["layers"][layer]
@@ -367,6 +387,8 @@ class V4FlashModel:
         and the routed experts' fp32 sum, added to the residual by the next fused norm; over TP/EP their
         all-reduced bf16 sum.
         """
+        if self.dp:
+            return self._moe_block_dp(layer, h)
         cfg = self.cfg
         lw = self.W["layers"][layer]
         fz = self.fused[layer]
@@ -386,6 +408,64 @@ class V4FlashModel:
         if hasattr(self.comm, "all_reduce_sum"):
             return self.comm.all_reduce_sum(out, shared), None
         return self._all_reduce((out + shared.float()).to(torch.bfloat16)), None
+
+    def _moe_block_dp(self, layer: int, h: torch.Tensor):
+        """MoE under DP attention: the shared expert and the router run on this rank's tokens; the tokens
+        and their routing go to every rank (one all-gather, rows padded to the largest count), each rank's
+        experts take every real row, and a reduce-scatter returns each rank the sum for its own rows."""
+        cfg = self.cfg
+        lw = self.W["layers"][layer]
+        fz = self.fused[layer]
+        counts = self.dp_counts or [h.shape[0]] * self.world
+        T, Tm, H = h.shape[0], max(counts), cfg.hidden_size
+        k = cfg.moe_topk
+        if T:
+            if self.mx is not None:
+                g = self._dense(layer, "shared_w13", h)
+                logits = h @ lw["gate"].T
+            else:
+                gf = h @ fz["w_ffn"].T
+                g, logits = gf[:, :fz["gate"]], gf[:, fz["gate"]:]
+            ids, w = fused_ops.route_topk(logits, lw["gate_bias"], k, cfg.routed_scaling)
+            route = torch.cat((ids.int(), w.float().view(torch.int32)), 1).view(torch.bfloat16)
+        send = torch.zeros(Tm, H + 4 * k, dtype=torch.bfloat16, device=h.device)
+        if T:
+            send[:T, :H] = h
+            send[:T, H:] = route
+        allr = self.comm.all_gather_rows(send)  # [world * Tm, H + 4k]
+        if all(c == Tm for c in counts):
+            rows = None
+            real = allr
+        else:
+            rows = torch.cat([torch.arange(c, device=h.device) + i * Tm for i, c in enumerate(counts)])
+            real = allr.index_select(0, rows)
+        if real.shape[0]:
+            rt = real[:, H:].contiguous().view(torch.int32)
+            out = moe_ops.experts(real[:, :H].contiguous(), rt[:, :k].contiguous(),
+                                  rt[:, k:].contiguous().view(torch.float32),
+                                  lw, self.expert_base, self.local_experts, cfg.expert_format,
+                                  precision=self.moe_precision).float()
+        else:
+            out = torch.zeros(0, H, dtype=torch.float32, device=h.device)
+        # the partial sums are reduced in fp32, as one rank sums its experts' outputs
+        if rows is None:
+            full = out
+        else:
+            full = torch.zeros(self.world * Tm, H, dtype=torch.float32, device=h.device)
+            full.index_copy_(0, rows, out)
+        mine = self.comm.reduce_scatter_rows(full)[:T]
+        if not T:
+            return None, None
+        silu = fused_ops.silu_mul(g)
+        shared = self._dense(layer, "shared_w2", silu) if self.mx is not None else silu @ lw["shared_w2"].T
+        return shared, mine
+
+    def dp_idle_forward(self) -> None:
+        """A forward without tokens of this rank (DP attention, another rank's prefill step): every MoE
+        block's exchange, so this rank's experts serve the other ranks' tokens."""
+        h = torch.zeros(0, self.cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
+        for layer in range(self.cfg.num_layers):
+            self._moe_block_dp(layer, h)
 
     def _layer_norms(self, layer: int):
         lw = self.W["layers"][layer]
@@ -476,6 +556,9 @@ class V4FlashModel:
                 csa_slots, csa_pos = self._index_topk_chunked(layer, q_lora, y, c4_phys_row, count, lim, qi=qi)
                 csa_len = torch.full((T,), csa_slots.shape[1], dtype=torch.int32, device=dev)
                 pool_native, planes = self.csa_planes(layer)
+                if planes is not None and planes.values.shape[1] != abi.PACKED_KEEP:
+                    csa_slots, pool_native, planes = self._reconstruct_visible(planes, c4_phys_row, lim, csa_slots,
+                                                                               csa_pos)
             elif ratio == abi.C128_RATIO:
                 n128 = (pos + 1) // abi.C128_RATIO
                 lim = max(1, int(min(self.r128max, (start + T) // abi.C128_RATIO)))

@@ -5,6 +5,8 @@ Sharding for `world` ranks (tensor parallel attention, expert parallel MoE):
   * wo_a groups and wo_b input rows: output groups split (o_groups / world per rank)
   * shared expert intermediate: split; routed experts: n_routed / world per rank
   * everything else replicated (latent KV projections, compressors, indexer, norms, router)
+With `dp_attention` every rank holds the whole attention block and the whole shared expert (it serves
+its own requests with all heads) and only the routed experts are split.
 Routed experts are MXFP4 (E2M1 nibbles, low nibble = even k, UE8M0 scale per 32 k) on GPU
 configs, BF16 on tiny CPU configs.  Dense projections are BF16.
 
@@ -43,15 +45,19 @@ def _fp4_expert(n_exp, out_f, in_f, gen, device):
     return w, (s + e + 127).to(torch.uint8)
 
 
-def init_weights(cfg: ModelConfig, rank: int = 0, world: int = 1, device="cpu", seed: int = 0) -> dict:
-    """Per-rank weight dict.  Replicated tensors are identical on every rank (same seed)."""
+def init_weights(cfg: ModelConfig, rank: int = 0, world: int = 1, device="cpu", seed: int = 0,
+                 dp_attention: bool = False) -> dict:
+    """Per-rank weight dict.  Replicated tensors are identical on every rank (same seed).  With
+    `dp_attention` the attention block and the shared expert are whole on every rank and the routed
+    experts are split over the `world` ranks."""
     if cfg.num_heads % world or cfg.o_groups % world or cfg.n_routed_experts % world or cfg.moe_intermediate % world:
         raise ValueError(f"world size {world} does not divide heads/groups/experts/intermediate")
     dev = torch.device(device)
     g = torch.Generator(device=dev)
     H, L, Q = cfg.hidden_size, cfg.latent_dim, cfg.q_lora_rank
-    hl, gl, el = cfg.num_heads // world, cfg.o_groups // world, cfg.n_routed_experts // world
-    il = cfg.moe_intermediate // world
+    a_rank, a_world = (0, 1) if dp_attention else (rank, world)  # the attention / shared-expert split
+    hl, gl, el = cfg.num_heads // a_world, cfg.o_groups // a_world, cfg.n_routed_experts // world
+    il = cfg.moe_intermediate // a_world
     hpg = cfg.heads_per_group
     W: dict = {}
 
@@ -73,7 +79,7 @@ def init_weights(cfg: ModelConfig, rank: int = 0, world: int = 1, device="cpu", 
         lw["kv_norm"] = (1.0 + 0.1 * torch.randn(L, generator=g, device=dev)).float()
         # sharded tensors are generated per unit (head / group / 256-row block / expert) with a
         # seed of the unit's global index, so every TP/EP split slices the same full model
-        h_lo, g_lo = rank * hl, rank * gl
+        h_lo, g_lo = a_rank * hl, a_rank * gl
         lw["wq_b"] = torch.cat([_unit(g, seed, base + 2, h, (L, Q), Q ** -0.5, dev) for h in range(h_lo, h_lo + hl)])
         rep(base + 6)
         lw["sink"] = torch.randn(cfg.num_heads, generator=g, device=dev).float()[h_lo:h_lo + hl].contiguous()
@@ -101,7 +107,7 @@ def init_weights(cfg: ModelConfig, rank: int = 0, world: int = 1, device="cpu", 
         lw["gate_bias"] = torch.zeros(cfg.n_routed_experts, dtype=torch.float32, device=dev)
         I = cfg.moe_intermediate
         blk = min(256, I // 8)  # world sizes up to 8 split the intermediate on block boundaries
-        u_lo, u_n = rank * il // blk, il // blk
+        u_lo, u_n = a_rank * il // blk, il // blk
         lw["shared_w13"] = torch.cat(
             [_unit(g, seed, base + 9, u, (blk, H), H ** -0.5, dev) for u in range(u_lo, u_lo + u_n)]
             + [_unit(g, seed, base + 10, u, (blk, H), H ** -0.5, dev) for u in range(u_lo, u_lo + u_n)])
@@ -123,7 +129,8 @@ def init_weights(cfg: ModelConfig, rank: int = 0, world: int = 1, device="cpu", 
                                     for e in range(e_lo, e_lo + el)])
         layers.append(lw)
     W["layers"] = layers
-    W["meta"] = {"rank": rank, "world": world, "expert_base": rank * el, "local_experts": el}
+    W["meta"] = {"rank": rank, "world": world, "expert_base": rank * el, "local_experts": el,
+                 "dp_attention": bool(dp_attention), "attn_world": a_world}
     return W
 
 

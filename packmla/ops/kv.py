@@ -56,7 +56,8 @@ def packed_store(
     bitmap: torch.Tensor,
     scales: torch.Tensor,
 ) -> None:
-    """Select top-256 |raw|, masked RMSNorm, quantize and write the three planes at `slots`."""
+    """Select the top-K |raw| (K = values.shape[1]: 256 by default, 64 .. 448 in steps of 64 for per-layer
+    layouts), masked RMSNorm, quantize and write the three planes at `slots`."""
     if raw.is_cuda:
         ext().packed_store(raw, weight, float(eps), slots.to(torch.int64), values, bitmap, scales,
                            error_word(raw.device))
@@ -64,7 +65,7 @@ def packed_store(
     keep = slots >= 0
     if not bool(keep.any()):
         return
-    v, b, s = codec.packed_encode(raw[keep].float(), weight.float(), eps)
+    v, b, s = codec.packed_encode(raw[keep].float(), weight.float(), eps, keep=values.shape[1])
     idx = slots[keep].long()
     values[idx] = v
     bitmap[idx] = b

@@ -83,6 +83,9 @@ def build_parser() -> argparse.ArgumentParser:
     ref.add_argument("--export-metrics-to-file", action="store_true",
                      help="append per-request metrics as JSON lines under --export-metrics-to-file-dir")
     ref.add_argument("--export-metrics-to-file-dir", default=None)
+    ref.add_argument("--enable-dp-attention", action="store_true",
+                     help="each rank serves its own requests with every attention head; routed experts stay "
+                          "split, MoE tokens are exchanged between the ranks (NCCL)")
     ref.add_argument("--disable-radix-cache", action="store_true",
                      help="release a finished request's KV at once instead of keeping it on the device for a "
                           "later prompt that extends it")
@@ -106,14 +109,18 @@ def resolve_args(args) -> dict:
         impl = "adapter" if args.dsv4_c4_cache_implementation == "adapter" else "direct"
     if args.ep is not None and args.ep != args.tp:
         raise SystemExit(f"--ep {args.ep}: packmla shards the routed experts over the TP ranks (EP = TP = {args.tp})")
-    if args.dsv4_c4_cache_layer_keep_counts:
-        counts = {int(x.split(":")[-1]) for x in args.dsv4_c4_cache_layer_keep_counts.replace(" ", "").split(",") if x}
-        if counts != {256}:
-            raise SystemExit("per-layer keep counts other than 256 are evaluation-only "
-                             "(python -m packmla.training.evaluate --retention-sweep)")
+    layer_counts = None
+    if args.dsv4_c4_cache_layer_keep_counts:  # "layer:count,layer:count" (model layer indices of C4 layers)
+        layer_counts = {}
+        for item in args.dsv4_c4_cache_layer_keep_counts.replace(" ", "").split(","):
+            if item:
+                layer, count = item.split(":")
+                layer_counts[int(layer)] = int(count)
     kw = dict(kv_cache_format=fmt, decode_impl=impl, keep_count=args.dsv4_c4_cache_keep_count,
+              layer_keep_counts=layer_counts,
               prefill_decode_interleave=not args.no_prefill_decode_interleave,
-              prefix_cache=not args.disable_radix_cache, hicache_mem_layout=args.hicache_mem_layout)
+              prefix_cache=not args.disable_radix_cache, hicache_mem_layout=args.hicache_mem_layout,
+              dp_attention=bool(getattr(args, "enable_dp_attention", False)) and args.tp > 1)
     disable_graphs = args.disable_cuda_graph or args.device == "cpu"
     bs = args.cuda_graph_bs
     if args.cuda_graph_config:
@@ -189,7 +196,7 @@ def build_engine(args, rank: int, local: int, world: int, comm):
         from ..kv.pool import bytes_per_full_token, fixed_bytes
 
         kv_bytes = int(args.max_total_tokens * bytes_per_full_token(cfg, ecfg.kv_cache_format,
-                                                                    ecfg.swa_full_tokens_ratio)
+                                                                    ecfg.swa_full_tokens_ratio, ecfg.keep_for)
                        + fixed_bytes(cfg, args.max_running_requests + 1))
     eng = Engine.build(cfg, ecfg, dev, rank, world, comm, max_context=args.context_length,
                        max_requests=args.max_running_requests, kv_bytes=kv_bytes, seed=args.seed, weights=W)
@@ -214,7 +221,7 @@ def main(argv=None) -> None:
     cpu_group = dist.new_group(backend="gloo") if world > 1 else None
     comm = None
     if world > 1:
-        if args.device == "cuda" and args.collectives == "fused":
+        if args.device == "cuda" and args.collectives == "fused" and not args.enable_dp_attention:
             from ..parallel.fused import FusedComm
 
             comm = FusedComm(torch.device("cuda", local), model_config(args.model)[0].hidden_size)

@@ -9,6 +9,8 @@ Tensor parallelism: rank 0 serves HTTP and, once per loop iteration, broadcasts 
 applies (add / abort / flush / stop) to the other ranks over a CPU (gloo) group; every rank applies
 the same operations in the same order and then takes the same `Engine.step()`, so the schedules
 and the KV pools stay identical in lockstep (reference: Gloo CPU broadcast of the batch each step).
+With DP attention each request is served by one rank, so after every step the ranks' produced tokens
+(with their finish state) are gathered to rank 0 over the same CPU group.
 """
 from __future__ import annotations
 
@@ -57,6 +59,7 @@ class EngineDriver:
         self.steps = 0
         self._step_started: float | None = None
         self.rank = rank
+        self._last_work = False
         self.world = world
         self.cpu_group = cpu_group
         self._inbox: queue.Queue = queue.Queue()
@@ -146,7 +149,9 @@ class EngineDriver:
     # ------------------------------------------------------------------ engine thread
     def _collect_ops(self) -> list[tuple]:
         ops = []
-        block = not self.engine.has_work()
+        # the work state of the loop's last has_work(): under DP attention that call is a collective, which
+        # only the loop may make (every rank makes it once per iteration)
+        block = not self._last_work
         try:
             ops.append(self._inbox.get(timeout=self.IDLE_WAIT_S) if block else self._inbox.get_nowait())
             while True:
@@ -221,7 +226,8 @@ class EngineDriver:
                 ops = self._sync_ops(ops)
                 if not self._apply(ops):
                     break
-                if not eng.has_work():
+                self._last_work = eng.has_work()
+                if not self._last_work:
                     continue
                 self._step_started = time.perf_counter()
                 if self.fault_hook is not None:
@@ -233,7 +239,21 @@ class EngineDriver:
 
                     check_errors(eng.device)  # a kernel's bounded wait or bounds check failed: stop serving
                 self._step_started = None
+                events = []
                 for rid, tok in produced:
+                    req = eng.done.pop(rid, None)  # the driver keeps no history of finished requests
+                    fin = req is not None and req.finished
+                    p = req.params if fin else None
+                    hit_eos = bool(fin and not p.ignore_eos and p.eos_token_id is not None and req.output_ids
+                                   and req.output_ids[-1] == p.eos_token_id)
+                    events.append((rid, tok, fin, hit_eos, req.cached_tokens if fin else 0))
+                if getattr(eng, "dp", False):  # every rank's tokens reach the HTTP streams on rank 0
+                    import torch.distributed as dist
+
+                    gathered = [None] * self.world
+                    dist.all_gather_object(gathered, events, group=self.cpu_group)
+                    events = [e for evs in gathered for e in evs]
+                for rid, tok, fin, hit_eos, cached in events:
                     ext = self._rid_to_ext.get(rid)
                     st = self._streams.get(ext) if ext is not None else None
                     if st is not None:
@@ -243,13 +263,9 @@ class EngineDriver:
                             eng.metrics.observe("time_to_first_token_seconds", st.t_first - st.t_submit)
                         st.tokens.append(tok)
                         self._deliver_to(st, tok)
-                    req = eng.done.pop(rid, None)  # the driver keeps no history of finished requests
-                    if req is not None and req.finished:
-                        p = req.params
-                        hit_eos = (not p.ignore_eos and p.eos_token_id is not None and req.output_ids
-                                   and req.output_ids[-1] == p.eos_token_id)
+                    if fin:
                         if st is not None:
-                            st.cached_tokens = req.cached_tokens
+                            st.cached_tokens = cached
                             now = time.perf_counter()
                             eng.metrics.inc("e2e_seconds_sum", now - st.t_submit)
                             eng.metrics.observe("e2e_request_latency_seconds", now - st.t_submit)

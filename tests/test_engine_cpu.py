@@ -150,3 +150,41 @@ def test_prefill_chunks_and_decode_steps_alternate():
     assert outs[True][:2] == outs[False][:2]
     assert outs[True][2].startswith("dpdpdp")  # alternating while the long prompt is prefilled
     assert outs[False][2].startswith("ppppppp")  # prefill first: the short request waits
+
+
+def test_per_layer_survivor_counts():
+    """Per-layer Packed layouts: validation (adapter reads only, 64 .. 448 by 64, C4 layers only, no HiCache),
+    capacity summing each layer's record size, and prefill chunking / decode agreement through
+    reconstruction."""
+    cfg = ModelConfig.tiny(num_layers=4)
+    c4 = cfg.c4_layers
+    counts = {layer: (128 if i % 2 == 0 else 448) for i, layer in enumerate(c4)}
+    with pytest.raises(ValueError, match="256 only"):
+        EngineConfig(layer_keep_counts=counts).validate()
+    with pytest.raises(ValueError, match="steps of 64"):
+        EngineConfig(decode_impl="adapter", layer_keep_counts={c4[0]: 100}).validate()
+    with pytest.raises(ValueError, match="HiCache"):
+        EngineConfig(decode_impl="adapter", layer_keep_counts=counts, enable_hierarchical_cache=True).validate()
+    ecfg = EngineConfig(kv_cache_format="direct", decode_impl="adapter", layer_keep_counts=counts, device="cpu")
+    ecfg.validate()
+    non_c4 = next(i for i in range(cfg.num_layers) if i not in c4)
+    with pytest.raises(ValueError, match="without C4"):
+        KVPool(cfg, EngineConfig(decode_impl="adapter", layer_keep_counts={non_c4: 128}, device="cpu"), 4, 2, 512,
+               "cpu")
+    from packmla.kv.pool import bytes_per_full_token
+
+    base = bytes_per_full_token(cfg, "direct", 0.1)
+    mixed = bytes_per_full_token(cfg, "direct", 0.1, ecfg.keep_for)
+    assert mixed - base == pytest.approx(sum(c - 256 for c in counts.values()) / 4)
+    W = init_weights(cfg)
+    pool = KVPool(cfg, ecfg, 16, 4, 1024, "cpu")
+    assert {l: pool.c4_values[l].shape[1] for l in c4} == counts
+    m = V4FlashModel(cfg, W, pool)
+    toks = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(1))
+    s1 = pool.admit(300)
+    full = m.prefill(toks, 0, s1)
+    s2 = pool.admit(300)
+    m.prefill(toks[:200], 0, s2)
+    m.prefill(toks[200:299], 200, s2)
+    step = m.decode(toks[299:300], torch.tensor([299]), torch.tensor([s2]))[0]
+    assert _rel(step, full) < 2e-2

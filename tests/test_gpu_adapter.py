@@ -43,3 +43,36 @@ def test_packed_to_native_matches_oracle(cuda):
                             out_gpu, dst.to(cuda))
     check_errors(cuda)
     assert torch.equal(out_gpu.cpu(), out_cpu)
+
+
+@pytest.mark.parametrize("keep", [64, 192, 320, 448])
+def test_packed_layouts_of_other_survivor_counts(cuda, keep):
+    """Per-layer Packed layouts (K survivors, values planes of K bytes): the device store writes the CPU
+    codec's planes byte for byte, ties included, and the reconstruction reads them back into the CPU
+    oracle's Native records."""
+    g = torch.Generator().manual_seed(keep)
+    n = 150
+    raw = torch.randn(n, 512, generator=g) * 2
+    raw[0] = torch.round(raw[0] * 2) / 2  # magnitude ties at the selection boundary
+    raw[1] = 1.0
+    w = torch.rand(512, generator=g) + 0.25
+    slots = torch.randperm(n + 7, generator=g)[:n]
+    planes = [torch.full((n + 7, keep), 3, dtype=torch.uint8), torch.zeros(n + 7, 8, dtype=torch.int64),
+              torch.zeros(n + 7, 8, dtype=torch.uint8)]
+    gplanes = [t.to(cuda) for t in planes]
+    kv_ops.packed_store(raw.to(cuda), w.to(cuda), 1e-6, slots.to(cuda), *gplanes)
+    check_errors(cuda)
+    kv_ops.packed_store(raw, w, 1e-6, slots, *planes)
+    for a, b in zip(gplanes, planes):
+        assert torch.equal(a.cpu(), b)
+    table = codec.rope_table(4096)
+    freqs = torch.stack((table.real, table.imag), -1).float().contiguous()
+    src = slots[:100].int()
+    pos = torch.randint(0, 4096, (100,), generator=g, dtype=torch.int32)
+    dst = torch.arange(100, dtype=torch.int64)
+    out_cpu = torch.zeros(2 * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8)
+    kv_ops.packed_to_native(*planes, src, pos, freqs, out_cpu, dst)
+    out_gpu = torch.zeros_like(out_cpu, device=cuda)
+    kv_ops.packed_to_native(*gplanes, src.to(cuda), pos.to(cuda), freqs.to(cuda), out_gpu, dst.to(cuda))
+    check_errors(cuda)
+    assert torch.equal(out_gpu.cpu(), out_cpu)

@@ -217,3 +217,35 @@ def test_decode_graph_replay_matches_eager_fp8_dense(cuda):
         eng.runner.release()
     check_errors(cuda)
     assert outs[True] == outs[False]
+
+
+def test_engine_per_layer_survivor_counts_match_cpu_oracle(cuda):
+    """Per-layer Packed layouts (C4 layers alternating 128 and 384 survivors), read by reconstruction in
+    prefill and decode: the GPU engine matches the CPU oracle engine (decisions replayed)."""
+    cfg = small_gpu_config()
+    counts = {layer: (128 if i % 2 == 0 else 384) for i, layer in enumerate(cfg.c4_layers)}
+    W = init_weights(cfg, device="cpu", seed=3)
+    Wg = {"layers": [{k: v.cuda() for k, v in l.items()} for l in W["layers"]], "meta": W["meta"],
+          **{k: v.cuda() for k, v in W.items() if torch.is_tensor(v)}}
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g)
+    res = {}
+    dec = _Decisions()
+    try:
+        for dev, weights in (("cuda", Wg), ("cpu", W)):
+            (dec.record if dev == "cuda" else dec.replay)()
+            ecfg = EngineConfig(kv_cache_format="direct", decode_impl="adapter", layer_keep_counts=counts, device=dev,
+                                max_running_requests=2, cuda_graph_bs=[1, 2], chunked_prefill_size=128,
+                                disable_cuda_graph=True, moe_precision="bf16")
+            eng = Engine.build(cfg, ecfg, dev, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=weights)
+            assert {l: eng.pool.c4_values[l].shape[1] for l in cfg.c4_layers} == counts
+            slot = eng.pool.admit(400)
+            l1 = eng.model.prefill(prompt[:200].to(dev), 0, slot)
+            l2 = eng.model.prefill(prompt[200:].to(dev), 200, slot)
+            l3 = eng.model.decode(prompt[:1].to(dev), torch.tensor([300], device=dev), torch.tensor([slot], device=dev))
+            res[dev] = (l1.cpu(), l2.cpu(), l3[0].cpu())
+    finally:
+        dec.restore()
+    check_errors(cuda)
+    for a, b in zip(res["cuda"], res["cpu"]):
+        assert _rel(a, b) < 3e-2

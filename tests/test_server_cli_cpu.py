@@ -39,8 +39,12 @@ def test_selectors_and_rejections():
     assert kw["decode_impl"] == "adapter" and not kw["disable_cuda_graph"]
     with pytest.raises(SystemExit):
         _resolve("--tp", "2", "--ep", "4")
-    with pytest.raises(SystemExit):
-        _resolve("--dsv4-c4-cache-layer-keep-counts", "2:256,4:192")
+    _, kw = _resolve("--dsv4-c4-cache-layer-keep-counts", "2:256,4:192")
+    assert kw["layer_keep_counts"] == {2: 256, 4: 192}
+    with pytest.raises(ValueError):  # a non-256 layout is read by reconstruction only
+        EngineConfig(**kw).validate()
+    _, kw = _resolve("--dsv4-c4-cache-layer-keep-counts", "2:256,4:192", "--dsv4-c4-cache-implementation", "adapter")
+    EngineConfig(**kw).validate()
     with pytest.raises(SystemExit):  # unsupported choice
         _resolve("--moe-runner-backend", "deep_gemm")
     _, kw = _resolve("--dsv4-c4-cache-keep-count", "192")
