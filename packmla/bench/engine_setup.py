@@ -13,7 +13,7 @@ def graph_buckets(concurrency: int) -> list[int]:
 
 
 def build_engine(cfg, device, rank: int, world: int, comm, concurrency: int, prompt_len: int, output_len: int,
-                 kv_format: str = "direct", seed: int = 0, dp_attention: bool = False):
+                 kv_format: str = "direct", seed: int = 0, dp_attention: bool = False, prefix_cache: bool = True):
     """-> (engine, max_context).  The pool holds every request's pages plus a few spare pages; with DP
     attention each rank serves concurrency / world requests, so its pool and graph buckets are sized for
     those."""
@@ -24,7 +24,7 @@ def build_engine(cfg, device, rank: int, world: int, comm, concurrency: int, pro
     C = concurrency // world if dp_attention else concurrency
     max_context = prompt_len + output_len + 256
     ecfg = EngineConfig(kv_cache_format=kv_format, tp=world, ep=world, max_running_requests=C,
-                        cuda_graph_bs=graph_buckets(C), chunked_prefill_size=8192, prefix_cache=True,
+                        cuda_graph_bs=graph_buckets(C), chunked_prefill_size=8192, prefix_cache=prefix_cache,
                         dp_attention=dp_attention)
     pages_per_req = math.ceil(max_context / 256)
     bpt = bytes_per_full_token(cfg, kv_format, ecfg.swa_full_tokens_ratio)

@@ -154,6 +154,10 @@ class EngineConfig:
     # prompt that extends it adopts the slot and prefills only the new tokens (the reference serves with
     # SGLang's radix prefix cache on; the server turns this on unless --disable-radix-cache)
     prefix_cache: bool = False
+    # with the prefix cache: requests that share a prompt prefix share its KV pages, in blocks of this many
+    # tokens (packmla.kv.prefix_blocks; a multiple of 256, 0 = off).  Blocks are cached where a prefill
+    # chunk ends, so they are used when the block is a multiple of chunked_prefill_size.
+    prefix_block_tokens: int = 8192
     keep_count: int = abi.PACKED_KEEP
     # per-layer survivor counts of the Packed C4 layout (model layer index -> count, 64 .. 448 in steps of
     # 64; the reference's --dsv4-c4-cache-layer-keep-counts).  Fixed at start-up; a layer's values plane is
@@ -207,6 +211,8 @@ class EngineConfig:
             raise ValueError("tp and ep must be >= 1")
         if self.hicache_mem_layout not in ("page_first", "layer_first"):
             raise ValueError("--hicache-mem-layout must be page_first or layer_first")
+        if self.prefix_block_tokens % 256:
+            raise ValueError("prefix_block_tokens must be a multiple of 256")
         if self.hicache_ratio <= 0:
             raise ValueError("hicache_ratio must be positive")
         if self.moe_precision not in ("default", "bf16"):

@@ -66,6 +66,7 @@ class Request:
     t_first_token: float | None = None
     t_finish: float | None = None
     cached_tokens: int = 0  # prompt tokens whose KV came from the device prefix cache or the host tier
+    block_tail: object = None  # the prefix-block node its prefill has reached (chains the next block)
 
     @property
     def context_len(self) -> int:
@@ -201,6 +202,12 @@ class Engine:
         self.retained: OrderedDict[tuple, int] = OrderedDict()
         # prompt forks: leader rid -> requests with the same prompt that copy its KV once it is prefilled
         self.forks: dict[int, list[Request]] = {}
+        self.blocks = None
+        if (engine_cfg.prefix_cache and engine_cfg.prefix_block_tokens
+                and engine_cfg.prefix_block_tokens % engine_cfg.chunked_prefill_size == 0):
+            from ..kv.prefix_blocks import PrefixBlockCache
+
+            self.blocks = PrefixBlockCache(pool, engine_cfg.prefix_block_tokens)
         self.hicache = None
         if engine_cfg.enable_hierarchical_cache:
             from ..kv.hicache import HostKVCache
@@ -277,7 +284,7 @@ class Engine:
             pages = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
             c128 = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
             while ((not self.pool._free_slots or pages > self.pool.pages.free or c128 > self.pool.c128_pages.free)
-                   and self._evict_retained()):
+                   and self._evict_cached()):
                 pass
             if (len(self.running) + 1 >= self.runner.max_b or not self.pool._free_slots
                     or pages > self.pool.pages.free or c128 > self.pool.c128_pages.free):
@@ -353,6 +360,15 @@ class Engine:
         self.metrics.inc("prefix_cache_evictions")
         return True
 
+    def _evict_cached(self) -> bool:
+        """Free cached KV for admission: a retained slot first, else the least recently used prefix block."""
+        if self._evict_retained():
+            return True
+        if self.blocks is not None and self.blocks.evict_one():
+            self.metrics.inc("prefix_block_evictions")
+            return True
+        return False
+
     def _match_retained(self, prompt: list[int]) -> tuple | None:
         """Longest retained context that is a strict prefix of `prompt` (at least one token to prefill)."""
         best = None
@@ -364,6 +380,8 @@ class Engine:
     def flush_prefix_cache(self) -> None:
         while self._evict_retained():
             pass
+        if self.blocks is not None:
+            self.blocks.flush()
 
     def _adopt(self, req: Request, need: int) -> bool | None:
         """Continue `req` in the retained slot of its longest cached prefix, growing its pages.
@@ -377,7 +395,7 @@ class Engine:
                 - len(self.pool._req_pages[slot]))
         grow128 = ((need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
                    - len(self.pool._req_c128[slot]))
-        while (grow > self.pool.pages.free or grow128 > self.pool.c128_pages.free) and self._evict_retained():
+        while (grow > self.pool.pages.free or grow128 > self.pool.c128_pages.free) and self._evict_cached():
             pass
         if grow > self.pool.pages.free or grow128 > self.pool.c128_pages.free:
             self.retained[key] = slot  # keep it for later; admission waits for running requests to finish
@@ -405,16 +423,30 @@ class Engine:
                     return None
                 if adopted:
                     return req
-            pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE
-            c128_needed = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
+            # shared prompt blocks: their pages are mapped, not allocated (pinned against eviction meanwhile)
+            chain = self.blocks.match(req.prompt) if self.blocks is not None else []
+            shared, shared128 = self.blocks.shared_pages(chain) if chain else ([], [])
+            for n in chain:
+                n.pins += 1
+            pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE - len(shared)
+            c128_needed = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE - len(shared128)
             while ((not self.pool._free_slots or pages_needed > self.pool.pages.free
-                    or c128_needed > self.pool.c128_pages.free) and self._evict_retained()):
+                    or c128_needed > self.pool.c128_pages.free) and self._evict_cached()):
                 pass
-            if (not self.pool._free_slots or pages_needed > self.pool.pages.free
-                    or c128_needed > self.pool.c128_pages.free):
+            fits = not (not self.pool._free_slots or pages_needed > self.pool.pages.free
+                        or c128_needed > self.pool.c128_pages.free)
+            if fits:
+                req.slot = self.pool.admit(need, shared, shared128)  # the request's own page references
+            for n in chain:
+                n.pins -= 1
+            if not fits:
                 return None
-            req.slot = self.pool.admit(need)
-            if self.hicache is not None:
+            if chain:  # resume at the end of the last shared block
+                self.blocks.attach(chain, req.slot)
+                req.prefilled = req.cached_tokens = (chain[-1].index + 1) * self.blocks.block
+                req.block_tail = chain[-1]
+                self.metrics.inc("prefix_block_hit_tokens", req.prefilled)
+            elif self.hicache is not None:
                 entry = self.hicache.match(req.prompt)
                 if entry is not None:  # earlier turn of this context: restore its KV, prefill the rest
                     req.prefilled = self.hicache.restore(entry, req.slot)
@@ -501,6 +533,11 @@ class Engine:
             ev[1].record()
         req.prefilled += len(toks)
         self.metrics.inc("prefill_tokens", len(toks))
+        if self.blocks is not None and req.prefilled % self.blocks.block == 0:
+            # the chunk ended on a block boundary: cache the block if it extends the request's cached chain
+            idx, tail = req.prefilled // self.blocks.block - 1, req.block_tail
+            if (tail is None and idx == 0) or (tail is not None and tail.index == idx - 1):
+                req.block_tail = self.blocks.insert(req.prompt, req.slot, idx, tail)
         if req.prefilled < len(req.prompt):
             return []
         self.waiting.popleft()
@@ -597,6 +634,7 @@ class Engine:
             "tp": self.ecfg.tp,
             "prefix_cache": self.ecfg.prefix_cache,
             "prefix_cache_retained": len(self.retained),
+            "prefix_blocks": len(self.blocks.nodes) if self.blocks is not None else 0,
             "enable_hierarchical_cache": self.hicache is not None,
             "hicache_host_bytes": self.hicache.host_bytes() if self.hicache is not None else 0,
         }

@@ -83,11 +83,13 @@ def plan_capacity(cfg: ModelConfig, ecfg: EngineConfig, available_bytes: int) ->
 
 
 class PageAllocator:
-    """Free-list page allocator (host side)."""
+    """Free-list page allocator with reference counts (host side): a page shared by several requests
+    (and the prefix-block cache) returns to the free list when its last holder releases it."""
 
     def __init__(self, num_pages: int):
         self.num_pages = num_pages
         self._free = list(range(num_pages - 1, -1, -1))
+        self._ref = [0] * num_pages
 
     @property
     def free(self) -> int:
@@ -96,10 +98,28 @@ class PageAllocator:
     def alloc(self, n: int) -> list[int]:
         if n > len(self._free):
             raise MemoryError(f"KV pool exhausted: need {n} pages, {len(self._free)} free")
-        return [self._free.pop() for _ in range(n)]
+        pages = [self._free.pop() for _ in range(n)]
+        for p in pages:
+            self._ref[p] = 1
+        return pages
+
+    def share(self, pages: list[int]) -> None:
+        """One more holder of each (allocated) page."""
+        for p in pages:
+            if self._ref[p] <= 0:
+                raise ValueError(f"page {p} is not allocated")
+            self._ref[p] += 1
+
+    def refs(self, page: int) -> int:
+        return self._ref[page]
 
     def release(self, pages: list[int]) -> None:
-        self._free.extend(pages)
+        for p in pages:
+            if self._ref[p] <= 0:
+                raise ValueError(f"page {p} released more often than held")
+            self._ref[p] -= 1
+            if self._ref[p] == 0:
+                self._free.append(p)
 
 
 class KVPool:
@@ -187,13 +207,22 @@ class KVPool:
         return total
 
     # ------------------------------------------------------------------ requests
-    def admit(self, tokens: int) -> int:
-        """Reserve a request slot with pages for `tokens` tokens; returns the slot."""
+    def admit(self, tokens: int, shared_pages: list[int] | None = None,
+              shared_c128: list[int] | None = None) -> int:
+        """Reserve a request slot with pages for `tokens` tokens; returns the slot.  `shared_pages` /
+        `shared_c128`: the request's first pages, held by the prefix-block cache and shared read-only
+        (the request takes one more reference on each)."""
         if not self._free_slots:
             raise MemoryError("no free request slot")
         slot = self._free_slots.pop()
         self._req_pages[slot] = []
         self._req_c128[slot] = []
+        for alloc, pages, table, owned in ((self.pages, shared_pages, self.page_table, self._req_pages),
+                                           (self.c128_pages, shared_c128, self.c128_table, self._req_c128)):
+            if pages:
+                alloc.share(pages)
+                owned[slot].extend(pages)
+                table[slot, :len(pages)] = torch.tensor(pages, dtype=torch.int32, device=self.device)
         try:
             self.ensure(slot, tokens)
         except MemoryError:

@@ -249,3 +249,26 @@ def test_engine_per_layer_survivor_counts_match_cpu_oracle(cuda):
     check_errors(cuda)
     for a, b in zip(res["cuda"], res["cpu"]):
         assert _rel(a, b) < 3e-2
+
+
+def test_prefix_blocks_reproduce_recomputation_exactly(cuda):
+    """Shared prompt blocks on the GPU: a request that maps the cached blocks of an earlier prompt (pages by
+    reference, SWA and pooling states restored, the partly filled C128 page copied) produces exactly the
+    tokens of an engine that recomputes the whole prompt with the same chunk boundaries."""
+    cfg = small_gpu_config()
+    W = init_weights(cfg, device=cuda, seed=9)
+    g = torch.Generator().manual_seed(4)
+    prefix = torch.randint(0, cfg.vocab_size, (512,), generator=g).tolist()
+    prompts = [prefix + torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 77, 140)]
+    outs = {}
+    for cache in (True, False):
+        ecfg = EngineConfig(kv_cache_format="direct", max_running_requests=2, cuda_graph_bs=[1, 2],
+                            chunked_prefill_size=128, prefix_cache=cache, prefix_block_tokens=256)
+        eng = Engine.build(cfg, ecfg, cuda, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=W)
+        eng.runner.capture()
+        outs[cache] = [eng.generate([p], SamplingParams(max_new_tokens=4))[0] for p in prompts]
+        if cache:
+            assert eng.metrics.snapshot()["prefix_block_hit_tokens"] == 2 * 512
+        eng.runner.release()
+    check_errors(cuda)
+    assert outs[True] == outs[False]

@@ -99,3 +99,70 @@ def test_group_without_room_falls_back_to_prefill_and_sampling_is_independent():
     while eng3.has_work():
         eng3.step()
     assert len(eng3.result(rids[1]).output_ids) == 2
+
+
+def _block_engine(max_running=3, fmt="direct", prefix=True):
+    cfg = ModelConfig.tiny(num_layers=3)
+    ecfg = EngineConfig(kv_cache_format=fmt, device="cpu", chunked_prefill_size=64, max_running_requests=max_running,
+                        cuda_graph_bs=[1, 2, 4], prefix_cache=prefix, prefix_block_tokens=256)
+    return Engine.build(cfg, ecfg, "cpu", max_context=1024)
+
+
+def test_concurrent_requests_share_prefix_blocks_exactly():
+    """Requests submitted together with a shared 512-token prefix: the first prefill caches two 256-token
+    blocks (pages by reference, SWA window and pooling states at each block end, the partly filled C128
+    page copied); the others map those pages, restore the snapshot and prefill only their own suffix.
+    Outputs equal an engine without any prefix cache; every page returns to the pool after a flush."""
+    for fmt in ("direct", "native"):
+        prefix = _toks(512, 11)
+        prompts = [prefix + _toks(40 + 13 * i, 20 + i) for i in range(3)]
+        eng = _block_engine(fmt=fmt)
+        rids = [eng.add_request(p, SamplingParams(max_new_tokens=5)) for p in prompts]
+        while eng.has_work():
+            eng.step()
+        outs = [eng.result(r).output_ids for r in rids]
+        m = eng.metrics.snapshot()
+        assert m["prefix_block_hit_tokens"] == 2 * 512, m
+        assert m["prefill_tokens"] == sum(len(p) for p in prompts) - 2 * 512
+        assert [eng.result(r).cached_tokens for r in rids] == [0, 512, 512]
+        assert len(eng.blocks.nodes) == 2
+        ref = _block_engine(fmt=fmt, prefix=False)
+        assert outs == [ref.generate([p], SamplingParams(max_new_tokens=5))[0] for p in prompts], fmt
+        eng.flush_cache()
+        assert not eng.blocks.nodes and eng.pool.pages.free == eng.pool.num_pages
+        assert eng.pool.c128_pages.free == eng.pool.num_c128_pages
+
+
+def test_prefix_blocks_chain_and_evict_leaves_first():
+    """A longer prompt extends the cached chain (its parent pointer is the last shared block); flushing
+    drops retained slots, then the blocks leaves first, and every page returns to the pool."""
+    eng = _block_engine(max_running=2)
+    base = _toks(512, 31)
+    eng.generate([base + _toks(10, 32)], SamplingParams(max_new_tokens=2))
+    eng.generate([base + _toks(300, 33)], SamplingParams(max_new_tokens=2))
+    assert eng.metrics.snapshot()["prefix_block_hit_tokens"] == 512
+    nodes = list(eng.blocks.nodes.values())
+    assert sorted(n.index for n in nodes) == [0, 1, 2]
+    by_index = {n.index: n for n in nodes}
+    assert by_index[2].parent is by_index[1] and by_index[1].parent is by_index[0]
+    assert not eng.blocks.evict_one() or len(eng.blocks.nodes) == 2  # a leaf went first
+    eng.flush_prefix_cache()
+    assert not eng.blocks.nodes and eng.pool.pages.free == eng.pool.num_pages
+
+
+def test_page_allocator_reference_counts():
+    from packmla.kv.pool import PageAllocator
+
+    a = PageAllocator(4)
+    p = a.alloc(2)
+    a.share(p)
+    a.release(p)
+    assert a.free == 2  # still held once
+    a.release(p)
+    assert a.free == 4
+    import pytest
+
+    with pytest.raises(ValueError):
+        a.release(p)
+    with pytest.raises(ValueError):
+        a.share(p)
