@@ -51,6 +51,15 @@ class SamplingParams:
     temperature: float = 0.0  # 0 = greedy
     ignore_eos: bool = True
     eos_token_id: int | None = None
+    # log-probabilities (the OpenAI completions `echo` / `logprobs`): `prompt_logprobs` = k >= 0 scores
+    # every prompt token after the first (and keeps the top k at each position); `logprobs` records the
+    # log-probability of each generated token.  A request scoring its prompt prefills all of it (no prefix
+    # reuse); max_new_tokens = 0 then generates nothing.
+    prompt_logprobs: int | None = None
+    logprobs: bool = False
+    # score prompt tokens from this index on (SGLang's logprob_start_len): the tokens before it may come
+    # from a prefix cache, so requests sharing a long context re-prefill only their own tail
+    prompt_logprobs_from: int = 0
 
 
 @dataclass
@@ -67,6 +76,9 @@ class Request:
     t_finish: float | None = None
     cached_tokens: int = 0  # prompt tokens whose KV came from the device prefix cache or the host tier
     block_tail: object = None  # the prefix-block node its prefill has reached (chains the next block)
+    prompt_lp: list = field(default_factory=list)  # per prompt token: log-probability (None for the first)
+    prompt_top: list = field(default_factory=list)  # per prompt token: [(token, log-probability)] top-k
+    output_lp: list = field(default_factory=list)  # per generated token (SamplingParams.logprobs)
 
     @property
     def context_len(self) -> int:
@@ -89,6 +101,7 @@ class DecodeGraphRunner:
         self.slots = torch.full((self.max_b,), dummy_slot, dtype=torch.int64, device=dev)
         self.temps = torch.zeros(self.max_b, dtype=torch.float32, device=dev)
         self.out_tokens = torch.zeros(self.max_b, dtype=torch.int64, device=dev)
+        self.out_lp = torch.zeros(self.max_b, dtype=torch.float32, device=dev)
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.pool_handle = None
 
@@ -97,6 +110,7 @@ class DecodeGraphRunner:
             self.model.dp_counts = [b] * self.model.world
         logits = self.model.decode(self.tokens[:b], self.positions[:b], self.slots[:b])
         self.out_tokens[:b] = sample(logits, self.temps[:b])
+        self.out_lp[:b] = logits.gather(1, self.out_tokens[:b, None])[:, 0] - torch.logsumexp(logits, -1)
 
     def bucket(self, b: int) -> int:
         for s in self.buckets:
@@ -192,6 +206,7 @@ class Engine:
         self._h_slots = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
         self._h_temps = torch.zeros(mb, dtype=torch.float32, pin_memory=pin)
         self._h_out = torch.zeros(mb, dtype=torch.int64, pin_memory=pin)
+        self._h_lp = torch.zeros(mb, dtype=torch.float32, pin_memory=pin)
         self.h2d_bytes_last = 0
         self.d2h_bytes_last = 0
         self._last_prefill = False
@@ -369,11 +384,13 @@ class Engine:
             return True
         return False
 
-    def _match_retained(self, prompt: list[int]) -> tuple | None:
-        """Longest retained context that is a strict prefix of `prompt` (at least one token to prefill)."""
+    def _match_retained(self, prompt: list[int], limit: int | None = None) -> tuple | None:
+        """Longest retained context that is a strict prefix of `prompt` (at least one token to prefill),
+        at most `limit` tokens long."""
         best = None
+        limit = len(prompt) - 1 if limit is None else min(limit, len(prompt) - 1)
         for key in self.retained:
-            if len(key) < len(prompt) and (best is None or len(key) > len(best)) and tuple(prompt[:len(key)]) == key:
+            if len(key) <= limit and (best is None or len(key) > len(best)) and tuple(prompt[:len(key)]) == key:
                 best = key
         return best
 
@@ -383,11 +400,11 @@ class Engine:
         if self.blocks is not None:
             self.blocks.flush()
 
-    def _adopt(self, req: Request, need: int) -> bool | None:
+    def _adopt(self, req: Request, need: int, limit: int | None = None) -> bool | None:
         """Continue `req` in the retained slot of its longest cached prefix, growing its pages.
         True: adopted; False: no cached prefix; None: cached, but the pages do not fit yet (a full
         admission would need more, so the request waits for running requests to finish)."""
-        key = self._match_retained(req.prompt)
+        key = self._match_retained(req.prompt, limit)
         if key is None:
             return False
         slot = self.retained.pop(key)
@@ -417,14 +434,20 @@ class Engine:
                 raise ValueError(f"request {req.rid} needs {need} tokens > max_context {self.pool.max_context}")
             if len(self.running) >= self.runner.max_b:
                 return None
-            if self.retained:
-                adopted = self._adopt(req, need)
+            # a scored prompt reuses cached KV only before its first scored token's predecessor
+            reuse_limit = (len(req.prompt) if req.params.prompt_logprobs is None
+                           else max(0, req.params.prompt_logprobs_from - 1))
+            reuse = reuse_limit > 0
+            if self.retained and reuse:
+                adopted = self._adopt(req, need, reuse_limit)
                 if adopted is None:
                     return None
                 if adopted:
                     return req
             # shared prompt blocks: their pages are mapped, not allocated (pinned against eviction meanwhile)
-            chain = self.blocks.match(req.prompt) if self.blocks is not None else []
+            chain = self.blocks.match(req.prompt) if self.blocks is not None and reuse else []
+            while chain and (chain[-1].index + 1) * self.blocks.block > reuse_limit:
+                chain.pop()
             shared, shared128 = self.blocks.shared_pages(chain) if chain else ([], [])
             for n in chain:
                 n.pins += 1
@@ -446,7 +469,7 @@ class Engine:
                 req.prefilled = req.cached_tokens = (chain[-1].index + 1) * self.blocks.block
                 req.block_tail = chain[-1]
                 self.metrics.inc("prefix_block_hit_tokens", req.prefilled)
-            elif self.hicache is not None:
+            elif self.hicache is not None and req.params.prompt_logprobs is None:
                 entry = self.hicache.match(req.prompt)
                 if entry is not None:  # earlier turn of this context: restore its KV, prefill the rest
                     req.prefilled = self.hicache.restore(entry, req.slot)
@@ -528,7 +551,23 @@ class Engine:
         if self.device.type == "cuda":
             t = t.pin_memory().to(self.device, non_blocking=True)
         self.h2d_bytes_last = t.numel() * t.element_size()
-        logits = self.model.prefill(t, start, req.slot)
+        k = req.params.prompt_logprobs
+        if k is None:
+            logits = self.model.prefill(t, start, req.slot)
+        else:  # score the next prompt token after the chunk's positions from the scoring start on
+            if not req.prompt_lp:  # tokens before the first scored one (a reused prefix included): None
+                n0 = max(1, req.params.prompt_logprobs_from, start + 1)
+                req.prompt_lp.extend([None] * n0)
+                req.prompt_top.extend([None] * n0)
+            first = len(req.prompt_lp) - 1 - start  # chunk row predicting the next unscored token
+            targets = torch.tensor(req.prompt[start + first + 1:start + len(toks) + 1], dtype=torch.int64,
+                                   device=self.device)
+            if first >= 0 and targets.numel():
+                logits, (lp, tv, ti) = self.model.prefill(t, start, req.slot, score=(targets, k, first))
+                req.prompt_lp.extend(lp.tolist())
+                req.prompt_top.extend([list(zip(i, v)) for i, v in zip(ti.tolist(), tv.tolist())])
+            else:
+                logits = self.model.prefill(t, start, req.slot)
         if ev is not None:
             ev[1].record()
         req.prefilled += len(toks)
@@ -541,8 +580,14 @@ class Engine:
         if req.prefilled < len(req.prompt):
             return []
         self.waiting.popleft()
+        if req.params.max_new_tokens == 0:  # prompt scoring only
+            req.t_first_token = time.perf_counter()
+            self._finish(req)
+            return [(req.rid, None)]
         temp = torch.tensor([req.params.temperature], device=self.device)
         tok = int(sample(logits[None], temp)[0])
+        if req.params.logprobs:
+            req.output_lp.append(float(logits[tok] - torch.logsumexp(logits, -1)))
         forked = self._fork(req, logits) if req.rid in self.forks else []  # before the leader can finish
         self._emit(req, tok)
         if not req.finished:
@@ -563,14 +608,20 @@ class Engine:
             ev[0].record()
         out = self.runner.run(self._h_tokens[:b], self._h_pos[:b], self._h_slots[:b], self._h_temps[:b], pad_to)
         self._h_out[:b].copy_(out, non_blocking=True)
+        want_lp = any(r.params.logprobs for r in reqs)
+        if want_lp:
+            self._h_lp[:b].copy_(self.runner.out_lp[:b], non_blocking=True)
         if ev is not None:
             ev[1].record()
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
         self.d2h_bytes_last = b * 8
         toks = self._h_out[:b].tolist()
+        lps = self._h_lp[:b].tolist() if want_lp else [None] * b
         produced = []
-        for r, tok in zip(list(reqs), toks):
+        for r, tok, lp in zip(list(reqs), toks, lps):
+            if r.params.logprobs:
+                r.output_lp.append(lp)
             self._emit(r, tok)
             produced.append((r.rid, tok))
         self.running = [r for r in reqs if not r.finished]
@@ -586,16 +637,19 @@ class Engine:
         eos = req.params.eos_token_id
         if len(req.output_ids) >= req.params.max_new_tokens or (not req.params.ignore_eos and eos is not None
                                                                  and tok == eos):
-            req.finished = True
-            req.t_finish = time.perf_counter()
-            if self.hicache is not None:  # write through: every token but the last has its KV stored
-                self.hicache.save(req.slot, req.prompt + req.output_ids[:-1])
-            if self.ecfg.prefix_cache:
-                self._retain(req)
-            else:
-                self.pool.release(req.slot)
-            self.done[req.rid] = req
-            self.metrics.inc("requests_finished")
+            self._finish(req)
+
+    def _finish(self, req: Request) -> None:
+        req.finished = True
+        req.t_finish = time.perf_counter()
+        if self.hicache is not None:  # write through: every token but the last has its KV stored
+            self.hicache.save(req.slot, req.prompt + req.output_ids[:-1])
+        if self.ecfg.prefix_cache:
+            self._retain(req)
+        else:
+            self.pool.release(req.slot)
+        self.done[req.rid] = req
+        self.metrics.inc("requests_finished")
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | None = None) -> list[list[int]]:
         rids = [self.add_request(p, params) for p in prompts]

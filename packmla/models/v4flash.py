@@ -492,11 +492,14 @@ class V4FlashModel:
         return (h @ self.W["lm_head"].T).float()
 
     # ------------------------------------------------------------------ prefill
-    def prefill(self, tokens: torch.Tensor, start: int, req_slot: int) -> torch.Tensor:
+    def prefill(self, tokens: torch.Tensor, start: int, req_slot: int, score: tuple | None = None):
         """Process prompt tokens [T] of one request at positions start..start+T-1 (pages ensured).
 
         Returns logits of the last token.  Attention of each prompt token uses the same kernel
         as decode with per-token row lists; SWA rows of the chunk live in a scratch Native pool.
+        With `score` = (targets [n] int64, top, first): also the log-probability of targets[i] after chunk
+        position first + i (the next prompt token) and, with top > 0, the top log-probabilities there:
+        returns (logits, (token_logprobs [n] fp32, top_values [n, top], top_ids [n, top])).
         """
         cfg = self.cfg
         dev = self.device
@@ -582,7 +585,31 @@ class V4FlashModel:
             d, dfp = self._moe_block(layer, h)
         _, h = fused_ops.add_rmsnorm(x[-1:], self.W["final_norm"], eps, d[-1:],
                                      None if dfp is None else dfp[-1:])
-        return (h @ self.W["lm_head"].T).float()[0]
+        logits = (h @ self.W["lm_head"].T).float()[0]
+        if score is None:
+            return logits
+        a = score[2]
+        return logits, self._score_rows(x[a:], d[a:], None if dfp is None else dfp[a:], score[0], score[1])
+
+    def _score_rows(self, x, d, dfp, targets: torch.Tensor, top: int, rows: int = 1024):
+        """Log-probabilities of `targets` after the first len(targets) positions of a prefill chunk (final
+        norm and LM head in blocks of `rows`, so full-vocabulary logits exist for one block at a time)."""
+        n = targets.shape[0]
+        lp = torch.empty(n, dtype=torch.float32, device=x.device)
+        tv = torch.empty(n, max(top, 0), dtype=torch.float32, device=x.device)
+        ti = torch.empty(n, max(top, 0), dtype=torch.int64, device=x.device)
+        for a in range(0, n, rows):
+            b = min(n, a + rows)
+            _, h = fused_ops.add_rmsnorm(x[a:b], self.W["final_norm"], self.cfg.rms_eps, d[a:b],
+                                         None if dfp is None else dfp[a:b])
+            logits = (h @ self.W["lm_head"].T).float()
+            lse = torch.logsumexp(logits, -1)
+            lp[a:b] = logits.gather(1, targets[a:b, None].long())[:, 0] - lse
+            if top > 0:
+                v, i = logits.topk(top, -1)
+                tv[a:b] = v - lse[:, None]
+                ti[a:b] = i
+        return lp, tv, ti
 
     def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int = 256, qi=None):
         T = q_lora.shape[0]

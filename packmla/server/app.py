@@ -33,10 +33,33 @@ from .driver import EngineDriver
 from .tokenizer import ByteTokenizer
 
 
-def _params(body: dict, tok: ByteTokenizer, default_max: int = 16) -> SamplingParams:
+def _logprobs_args(body: dict) -> tuple[bool, int | None]:
+    """(echo, logprobs) of a completions request: `logprobs` k in [0, 20] returns each token's
+    log-probability and, for prompt positions (with echo), the top k there."""
+    echo = bool(body.get("echo", False))
+    k = body.get("logprobs")
+    if k is not None and (isinstance(k, bool) or not isinstance(k, int) or not 0 <= k <= 20):
+        raise HTTPException(400, "logprobs must be an integer in [0, 20]")
+    if (echo or k is not None) and body.get("stream"):
+        raise HTTPException(400, "echo and logprobs are returned by non-streaming requests only")
+    return echo, k
+
+
+def _start_len(body: dict) -> int:
+    """SGLang's `logprob_start_len`: prompt tokens before it are not scored (and may come from a cache)."""
+    v = body.get("logprob_start_len", 0)
+    if v is None:
+        return 0
+    if isinstance(v, bool) or not isinstance(v, int) or v < 0:
+        raise HTTPException(400, "logprob_start_len must be an integer >= 0")
+    return v
+
+
+def _params(body: dict, tok: ByteTokenizer, default_max: int = 16, scoring: tuple | None = None) -> SamplingParams:
     max_tokens = body.get("max_completion_tokens", body.get("max_tokens", body.get("max_new_tokens", default_max)))
-    if max_tokens is None or int(max_tokens) < 1:
-        raise HTTPException(400, "max_tokens must be >= 1")
+    echo, k = scoring if scoring is not None else (False, None)
+    if max_tokens is None or int(max_tokens) < (0 if echo else 1):
+        raise HTTPException(400, "max_tokens must be >= 1 (>= 0 with echo)")
     temp = float(body.get("temperature", 0.0) or 0.0)
     if temp < 0:
         raise HTTPException(400, "temperature must be >= 0")
@@ -49,7 +72,9 @@ def _params(body: dict, tok: ByteTokenizer, default_max: int = 16) -> SamplingPa
         if v is not None and not (v == neutral or (name == "top_k" and v == 0)):
             raise HTTPException(400, f"{name}={v} is not supported (greedy or temperature sampling only)")
     return SamplingParams(max_new_tokens=int(max_tokens), temperature=temp,
-                          ignore_eos=bool(body.get("ignore_eos", False)), eos_token_id=tok.eos_token_id)
+                          ignore_eos=bool(body.get("ignore_eos", False)), eos_token_id=tok.eos_token_id,
+                          prompt_logprobs=(k or 0) if echo and k is not None else None, logprobs=k is not None,
+                          prompt_logprobs_from=_start_len(body))
 
 
 def _prompts(prompt, tok: ByteTokenizer) -> list[list[int]]:
@@ -260,10 +285,28 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "packmla",
                                             "max_model_len": eng.pool.max_context}]}
 
+    def _logprobs_obj(prompt: list[int], toks: list[int], st, echo: bool, k: int) -> dict:
+        """The OpenAI completions `logprobs` object of one choice (prompt tokens first with echo)."""
+        lp = st.logprobs or {}
+        ids = (list(prompt) if echo else []) + list(toks)
+        values = (list(lp.get("prompt_lp", [])) if echo else []) + list(lp.get("output_lp", []))[:len(toks)]
+        top = None
+        if k:
+            top = [None if t is None else {tokenizer.decode([i]): v for i, v in t}
+                   for t in (lp.get("prompt_top", []) if echo else [])]
+            top += [{tokenizer.decode([t]): v} for t, v in zip(toks, lp.get("output_lp", []))]
+        strs = [tokenizer.decode([t]) for t in ids]
+        offsets, pos = [], 0
+        for x in strs:
+            offsets.append(pos)
+            pos += len(x)
+        return {"tokens": strs, "token_logprobs": values, "top_logprobs": top, "text_offset": offsets}
+
     @app.post("/v1/completions")
     async def completions(req: Request):
         body = await req.json()
-        params = _params(body, tokenizer)
+        echo, k = _logprobs_args(body)
+        params = _params(body, tokenizer, scoring=(echo, k))
         prompts = _prompts(body.get("prompt"), tokenizer)
         n_choices = _n(body)
         _StopRule(body, tokenizer)  # validate before submitting anything
@@ -293,13 +336,18 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
 
             return StreamingResponse(gen(), media_type="text/event-stream")
         streams = [st for p in prompts for st in await _submit_group(p, params, n_choices)]
+        owners = [p for p in prompts for _ in range(n_choices)]
         choices = []
         ntok = 0
         for i, st in enumerate(streams):
             rule = _StopRule(body, tokenizer)
             toks = await _collect(st, rule)
             ntok += len(toks)
-            choices.append({"index": i, "text": _text(toks, rule), "token_ids": toks, "logprobs": None,
+            text = _text(toks, rule)
+            if echo:
+                text = tokenizer.decode(owners[i]) + text
+            choices.append({"index": i, "text": text, "token_ids": toks,
+                            "logprobs": _logprobs_obj(owners[i], toks, st, echo, k) if k is not None else None,
                             "finish_reason": st.finish_reason})
         return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": choices,

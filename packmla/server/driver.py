@@ -40,6 +40,7 @@ class Stream:
     params: SamplingParams | None = None
     prompt: list[int] | None = None  # kept only when the request log records prompt ids
     cached_tokens: int = 0  # prompt tokens served from a KV cache tier (known when the request ends)
+    logprobs: dict | None = None  # prompt / output log-probabilities, when requested (set when it ends)
 
 
 class EngineDriver:
@@ -246,14 +247,17 @@ class EngineDriver:
                     p = req.params if fin else None
                     hit_eos = bool(fin and not p.ignore_eos and p.eos_token_id is not None and req.output_ids
                                    and req.output_ids[-1] == p.eos_token_id)
-                    events.append((rid, tok, fin, hit_eos, req.cached_tokens if fin else 0))
+                    scored = fin and (p.prompt_logprobs is not None or p.logprobs)
+                    extra = {"prompt_lp": req.prompt_lp, "prompt_top": req.prompt_top,
+                             "output_lp": req.output_lp} if scored else None
+                    events.append((rid, tok, fin, hit_eos, req.cached_tokens if fin else 0, extra))
                 if getattr(eng, "dp", False):  # every rank's tokens reach the HTTP streams on rank 0
                     import torch.distributed as dist
 
                     gathered = [None] * self.world
                     dist.all_gather_object(gathered, events, group=self.cpu_group)
                     events = [e for evs in gathered for e in evs]
-                for rid, tok, fin, hit_eos, cached in events:
+                for rid, tok, fin, hit_eos, cached, extra in events:
                     ext = self._rid_to_ext.get(rid)
                     st = self._streams.get(ext) if ext is not None else None
                     if st is not None:
@@ -261,8 +265,11 @@ class EngineDriver:
                             st.t_first = time.perf_counter()
                             eng.metrics.inc("ttft_seconds_sum", st.t_first - st.t_submit)
                             eng.metrics.observe("time_to_first_token_seconds", st.t_first - st.t_submit)
-                        st.tokens.append(tok)
-                        self._deliver_to(st, tok)
+                        if tok is not None:  # None: a prompt-scoring request that generates nothing
+                            st.tokens.append(tok)
+                            self._deliver_to(st, tok)
+                        if extra is not None:
+                            st.logprobs = extra
                     if fin:
                         if st is not None:
                             st.cached_tokens = cached

@@ -188,3 +188,61 @@ def test_per_layer_survivor_counts():
     m.prefill(toks[200:299], 200, s2)
     step = m.decode(toks[299:300], torch.tensor([299]), torch.tensor([s2]))[0]
     assert _rel(step, full) < 2e-2
+
+
+def test_prompt_logprobs_match_direct_forward_and_chunking():
+    """Prompt scoring (the completions `echo` + `logprobs`): the log-probability of prompt token i equals
+    log-softmax of a direct prefill ending at token i - 1, whatever the chunk size; the top-k holds the
+    most likely tokens; max_new_tokens = 0 generates nothing."""
+    cfg = ModelConfig.tiny(num_layers=3)
+    W = init_weights(cfg)
+    prompt = torch.randint(3, cfg.vocab_size, (150,), generator=torch.Generator().manual_seed(5)).tolist()
+    got = {}
+    for chunk in (64, 256):
+        ecfg = EngineConfig(device="cpu", chunked_prefill_size=chunk, max_running_requests=2, cuda_graph_bs=[1, 2],
+                            prefix_cache=True)
+        eng = Engine.build(cfg, ecfg, "cpu", max_context=512, weights=W)
+        rid = eng.add_request(prompt, SamplingParams(max_new_tokens=0, prompt_logprobs=3))
+        while eng.has_work():
+            eng.step()
+        r = eng.result(rid)
+        assert r.output_ids == [] and len(r.prompt_lp) == len(prompt) and r.prompt_lp[0] is None
+        got[chunk] = r
+    a, b = got[64], got[256]
+    assert max(abs(x - y) for x, y in zip(a.prompt_lp[1:], b.prompt_lp[1:])) < 2e-3
+    for i in (1, 64, 65, 149):  # a chunk start, the first token of the second chunk, the last token
+        pool = KVPool(cfg, EngineConfig(device="cpu"), 16, 2, 1024, "cpu")
+        m = V4FlashModel(cfg, W, pool)
+        logits = m.prefill(torch.tensor(prompt[:i]), 0, pool.admit(300))
+        ref = (logits.log_softmax(-1)[prompt[i]]).item()
+        assert abs(a.prompt_lp[i] - ref) < 2e-3, (i, a.prompt_lp[i], ref)
+        top = a.prompt_top[i]
+        assert len(top) == 3 and top[0][1] >= top[1][1] >= top[2][1] and a.prompt_lp[i] <= top[0][1] + 1e-5
+        assert top[0][0] == int(logits.argmax())
+
+
+def test_prompt_scoring_from_a_start_reuses_the_shared_prefix():
+    """logprob_start_len: requests that share a long context and differ in their last tokens (the
+    multiple-choice scoring of LongBench) reuse the context's prefix blocks and score only their tails,
+    with the log-probabilities of a request scored in full."""
+    cfg = ModelConfig.tiny(num_layers=3)
+    W = init_weights(cfg)
+    g = torch.Generator().manual_seed(8)
+    ctx = torch.randint(3, cfg.vocab_size, (600,), generator=g).tolist()
+    ecfg = EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=2, cuda_graph_bs=[1, 2],
+                        prefix_cache=True, prefix_block_tokens=256)
+    eng = Engine.build(cfg, ecfg, "cpu", max_context=1024, weights=W)
+    full = Engine.build(cfg, EngineConfig(device="cpu", chunked_prefill_size=64, max_running_requests=2,
+                                          cuda_graph_bs=[1, 2]), "cpu", max_context=1024, weights=W)
+    for choice in (7, 8, 9):
+        p = ctx + [choice, 5]
+        rid = eng.add_request(p, SamplingParams(max_new_tokens=0, prompt_logprobs=0, prompt_logprobs_from=len(ctx)))
+        ref = full.add_request(p, SamplingParams(max_new_tokens=0, prompt_logprobs=0))
+        for e in (eng, full):
+            while e.has_work():
+                e.step()
+        a, b = eng.result(rid), full.result(ref)
+        assert all(v is None for v in a.prompt_lp[:len(ctx)]) and len(a.prompt_lp) == len(p)
+        for i in (len(ctx), len(ctx) + 1):
+            assert abs(a.prompt_lp[i] - b.prompt_lp[i]) < 2e-3
+    assert eng.metrics.snapshot()["prefix_block_hit_tokens"] == 2 * 512  # the second and third requests

@@ -260,3 +260,59 @@ def test_api_key_guards_every_route_but_health():
             assert ok.status_code == 200
     finally:
         driver.stop()
+
+
+def test_completions_echo_and_logprobs(served):
+    """echo + logprobs + max_tokens 0 scores the prompt (the request lm-eval's log-likelihood tasks send);
+    logprobs alone returns each generated token's log-probability."""
+    client, eng, tok, cfg = served
+    prompt = "the quick brown fox"
+    ids = tok.encode(prompt)
+    r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 0, "echo": True, "logprobs": 2})
+    assert r.status_code == 200, r.text
+    ch = r.json()["choices"][0]
+    lp = ch["logprobs"]
+    assert ch["token_ids"] == [] and ch["text"] == tok.decode(ids)
+    assert len(lp["token_logprobs"]) == len(ids) and lp["token_logprobs"][0] is None
+    assert all(v <= 0 for v in lp["token_logprobs"][1:])
+    assert lp["top_logprobs"][0] is None and all(len(t) <= 2 for t in lp["top_logprobs"][1:])
+    assert lp["text_offset"][0] == 0 and len(lp["tokens"]) == len(ids)
+    r2 = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 3, "logprobs": 0})
+    lp2 = r2.json()["choices"][0]["logprobs"]
+    assert len(lp2["token_logprobs"]) == 3 and all(v <= 0 for v in lp2["token_logprobs"])
+    assert client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 0}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": prompt, "logprobs": 99}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": prompt, "echo": True, "logprobs": 1,
+                                                "stream": True}).status_code == 400
+
+
+def test_longbench_evaluator_scores_choices_and_resumes(served, tmp_path):
+    """The LongBench v2 evaluator over the HTTP API: each choice letter scored as a continuation (echo +
+    logprobs + logprob_start_len), the best one predicted; results appended per item, a rerun skips the
+    finished items; contexts beyond the limit are middle-truncated."""
+    from packmla.bench import longbench
+
+    client, eng, tok, cfg = served
+    items = [{"_id": f"q{i}", "domain": "d", "sub_domain": "s", "difficulty": ("easy", "hard")[i % 2],
+              "length": "short", "question": f"question {i}?", "choice_A": "a", "choice_B": "b", "choice_C": "c",
+              "choice_D": "d", "answer": "ABCD"[i], "context": "lorem ipsum " * (10 + 5 * i)} for i in range(3)]
+    data = tmp_path / "data.jsonl"
+    data.write_text("\n".join(json.dumps(x) for x in items))
+
+    def post(body):
+        r = client.post("/v1/completions", json=body)
+        assert r.status_code == 200, r.text
+        return r.json()
+
+    loaded = longbench.load_items(data)
+    out = tmp_path / "run"
+    s1 = longbench.evaluate(loaded, post, tok, out, max_prompt_tokens=300)
+    rows = [json.loads(x) for x in (out / "items.jsonl").read_text().splitlines()]
+    assert s1["overall"]["n"] == 3 and set(s1["difficulty"]) == {"easy", "hard"}
+    assert all(set(r["scores"]) == set("ABCD") and r["pred"] == max(r["scores"], key=r["scores"].get) for r in rows)
+    assert all(r["prompt_tokens"] <= 300 for r in rows)
+    s2 = longbench.evaluate(loaded, post, tok, out, max_prompt_tokens=300)  # resumed: nothing new to score
+    assert s2 == s1 and len((out / "items.jsonl").read_text().splitlines()) == 3
+    g = longbench.evaluate(loaded[:1], post, tok, tmp_path / "gen", mode="generate")
+    assert g["overall"]["n"] == 1
+    assert longbench.parse_answer("The correct answer is (C).") == "C"
