@@ -122,7 +122,7 @@ def test_peer_wait_times_out_with_error_status():
         comm.close()
 
 
-# ----------------------------------------------------------------------------- two GPUs
+# ----------------------------------------------------------------------------- 2, 4 and 8 GPUs
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -167,15 +167,15 @@ def _mp_worker(rank: int, world: int, port: int, out_dir: str):
 
 
 @pytest.mark.multigpu
-def test_fused_collectives_two_gpus(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp.spawn(_mp_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    r0 = torch.load(tmp_path / "r0.pt")
-    r1 = torch.load(tmp_path / "r1.pt")
-    for key, (y0, ref) in r0.items():
-        y1 = r1[key][0]
-        assert torch.equal(y0, y1), key  # every rank receives the same bits
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_collectives_multi_gpu(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_mp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    res = [torch.load(tmp_path / f"r{r}.pt") for r in range(world)]
+    for key, (y0, ref) in res[0].items():
+        for r in range(1, world):
+            assert torch.equal(y0, res[r][key][0]), (key, r)  # every rank receives the same bits
         rel = ((y0.float() - ref).norm() / ref.norm()).item()
         assert rel < 1e-2, (key, rel)
 
@@ -196,7 +196,7 @@ def _engine(rank, world, comm, dev):
     from packmla.config import EngineConfig
     from packmla.engine.engine import Engine
 
-    cfg = small_gpu_config()
+    cfg = small_gpu_config(o_groups=8)  # output groups split over up to 8 ranks
     ecfg = EngineConfig(kv_cache_format="direct", tp=world, ep=world, max_running_requests=2, cuda_graph_bs=[1],
                         disable_cuda_graph=True, moe_precision="bf16")
     return Engine.build(cfg, ecfg, dev, rank, world, comm, max_context=1024, max_requests=2, kv_bytes=64 << 20)
@@ -219,7 +219,7 @@ def _model_worker(rank: int, world: int, port: int, out_dir: str):
                             device_id=dev)
     from helpers import small_gpu_config
 
-    comm = FusedComm(dev, small_gpu_config().hidden_size, timeout_s=5.0)
+    comm = FusedComm(dev, small_gpu_config(o_groups=8).hidden_size, timeout_s=5.0)
     try:
         eng = _engine(rank, world, comm, dev)
         fused = _run_model(eng, dev)
@@ -235,20 +235,21 @@ def _model_worker(rank: int, world: int, port: int, out_dir: str):
 
 
 @pytest.mark.multigpu
-def test_model_tp2_fused_matches_single_rank(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_model_tp_fused_matches_single_rank(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     dev = torch.device("cuda", 0)
     eng = _engine(0, 1, None, dev)
     ref = _run_model(eng, dev)
     del eng
     torch.cuda.empty_cache()
-    mp.spawn(_model_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_model_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     got = torch.load(tmp_path / "m.pt")
     assert got["fallbacks"] == 0
     rel = {}
     for name in ("fused", "nccl"):
         rel[name] = [((a - b).norm() / b.norm()).item() for a, b in zip(got[name], ref)]
-    print("TP2 vs single-rank relative error (prefill, decode):", rel)
+    print(f"TP{world} vs single-rank relative error (prefill, decode):", rel)
     # partial sums are rounded to bf16 before either all-reduce; the random model amplifies it per layer
     assert max(rel["fused"]) < 6e-2 and max(rel["nccl"]) < 6e-2, rel
