@@ -10,11 +10,14 @@
 // scale per row (amax / 448).
 //
 //   index_key_store:  warp per row: amax, scale, E4M3 codes, swizzled write (slot -1: no write).
-//   index_logits:     CTA = (query, chunk of 128-record tiles).  The query's heads are quantized
-//                     to E4M3 per head (scale folded into w, since relu is positively homogeneous)
-//                     into the B operand; each tile's two key pages arrive by cp.async.bulk (two
-//                     stages); one tcgen05.mma kind::f8f6f4 chain S^T[128 records x 64 heads]
-//                     (K = 128); the epilogue thread of record r reduces its TMEM row to the score.
+//   index_logits:     CTA = (up to 4 queries, chunk of 128-record tiles).  The queries' heads are
+//                     quantized to E4M3 per head (scale folded into w, since relu is positively
+//                     homogeneous) into the B operand; each tile's two key pages arrive by
+//                     cp.async.bulk (two stages); one tcgen05.mma kind::f8f6f4 chain
+//                     S^T[128 records x 64 heads per query] (K = 128); the epilogue thread of record r
+//                     reduces its TMEM row to one score per query.  Several queries share a CTA only
+//                     when they share one physical-row list (a prefill chunk's queries of one request,
+//                     passed with row stride 0): each key tile then serves all of them.
 //   index_topk:       CTA per query: 4-pass 8-bit radix select of the k-th largest score, then a
 //                     deterministic (index-ordered) compaction; writes physical slots and RoPE rows.
 #include "launchers.h"
@@ -63,6 +66,7 @@ struct LogitParams {
   const int64_t* count;    // [B] visible records
   int R;                   // records scored (multiple of 128 not required)
   int tiles_per_cta;
+  int nq;                  // queries per CTA (1, 2 or 4; above 1 only with phys_stride == 0)
   float* scores;           // [B, score_stride]
   int64_t score_stride;
   int* err;
@@ -72,9 +76,10 @@ constexpr int kLogitThreads = 128;
 constexpr int kKeyStage = kRows * kD + kRows * 4;  // 16 KB keys + 512 B scales
 constexpr int kOffQ = 2 * kKeyStage;               // 2 stages (each 1024-aligned: 16896 = 16.5 KB -> pad)
 constexpr int kStageStride = 17408;                // 17 KB, multiple of 1024
+constexpr int kQmax = 4;                           // queries per CTA sharing one physical-row list
 constexpr int kOffQ2 = 2 * kStageStride;
-constexpr int kOffW = kOffQ2 + kHmax * kD;
-constexpr int kOffBar = kOffW + kHmax * 4;
+constexpr int kOffW = kOffQ2 + kQmax * kHmax * kD;  // B operand: 64 rows per query
+constexpr int kOffBar = kOffW + kQmax * kHmax * 4;
 constexpr int kLogitSmem = kOffBar + 64 + 1024;
 
 __global__ void __launch_bounds__(kLogitThreads) index_logits_kernel(const LogitParams p) {
@@ -86,15 +91,18 @@ __global__ void __launch_bounds__(kLogitThreads) index_logits_kernel(const Logit
   uint64_t* mdone = full + 2;                                    // [1]
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.y;
+  const int b0 = blockIdx.y * p.nq;
+  const int nqb = min(p.nq, p.B - b0);  // this CTA's queries
+  const int ncols = kHmax * p.nq;        // MMA N and TMEM columns (64, 128 or 256)
   const int tile0 = blockIdx.x * p.tiles_per_cta;
   const int ntile_total = (p.R + kRows - 1) / kRows;
   const int tile1 = min(ntile_total, tile0 + p.tiles_per_cta);
   if (tile0 >= tile1) return;
-  const int64_t cnt = min((int64_t)p.R, p.count[b]);
+  int64_t cnt = 0;  // records to load: the largest visible count of the CTA's queries
+  for (int qi = 0; qi < nqb; ++qi) cnt = max(cnt, min((int64_t)p.R, p.count[b0 + qi]));
 
   if (warp == 0) {
-    pm::tmem_alloc(tslot, 64);
+    pm::tmem_alloc(tslot, ncols);
     pm::tmem_relinquish();
   }
   if (tid == 0) {
@@ -103,13 +111,14 @@ __global__ void __launch_bounds__(kLogitThreads) index_logits_kernel(const Logit
     pm::mbar_init(mdone, 1);
     pm::fence_mbar_init();
   }
-  // query heads -> E4M3 (per-head scale folded into w), B operand rows (swizzled by head % 8)
-  if (tid < kHmax) {
-    const int h = tid;
+  // query heads -> E4M3 (per-head scale folded into w), B operand row 64 qi + h (swizzled by row % 8)
+  for (int row = tid; row < ncols; row += kLogitThreads) {
+    const int qi = row / kHmax, h = row % kHmax;
+    const bool valid = qi < nqb && h < p.H;
     float vals[kD];
     float amax = 0.f;
-    if (h < p.H) {
-      const __nv_bfloat16* qr = p.q + ((int64_t)b * p.H + h) * kD;
+    if (valid) {
+      const __nv_bfloat16* qr = p.q + ((int64_t)(b0 + qi) * p.H + h) * kD;
 #pragma unroll
       for (int i = 0; i < kD; i += 8) {
         const uint4 u = *reinterpret_cast<const uint4*>(qr + i);
@@ -137,17 +146,17 @@ __global__ void __launch_bounds__(kLogitThreads) index_logits_kernel(const Logit
         wds[j] = (uint32_t)pm::f32x2_to_e4m3x2(vals[i] * inv, vals[i + 1] * inv) |
                  ((uint32_t)pm::f32x2_to_e4m3x2(vals[i + 2] * inv, vals[i + 3] * inv) << 16);
       }
-      *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(h, 16 * u, 0)) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+      *reinterpret_cast<uint4*>(sQ + pm::sw128_offset(row, 16 * u, 0)) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
     }
-    sW[h] = h < p.H ? p.w[(int64_t)b * p.H + h] * qs : 0.f;
+    sW[row] = valid ? p.w[(int64_t)(b0 + qi) * p.H + h] * qs : 0.f;
   }
   pm::fence_proxy_async_smem();
   pm::tc_fence_before();
   __syncthreads();
   pm::tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t idesc = pm::make_idesc_f8(128, kHmax, 0, 0);
-  const int32_t* phys_b = p.phys + (int64_t)b * p.phys_stride;
+  const uint32_t idesc = pm::make_idesc_f8(128, ncols, 0, 0);
+  const int32_t* phys_b = p.phys + (int64_t)b0 * p.phys_stride;  // shared by the CTA's queries
 
   // issue the copies of tile `j` (two pages) into stage `st`; returns false if the tile is masked
   auto issue = [&](int j, int st) {
@@ -187,34 +196,31 @@ __global__ void __launch_bounds__(kLogitThreads) index_logits_kernel(const Logit
     }
     ok = ok && pm::mbar_wait(mdone, it & 1, p.err, 41);
     pm::tc_fence_after();
-    // epilogue: thread = record row
+    // epilogue: thread = record row, one score per query of the CTA
     const int r = j * kRows + tid;
-    float d[64];
-    if (ok) {
+    const int ph = r < cnt ? phys_b[r] : -1;
+    const float ks = *reinterpret_cast<const float*>(smem + st * kStageStride + kRows * kD + tid * 4);
+#pragma unroll 1
+    for (int qi = 0; qi < nqb; ++qi) {
+      float acc = 0.f;
+      if (ok) {
 #pragma unroll
-      for (int c = 0; c < 64; c += 16) {
-        float t[16];
-        pm::tmem_ld16(tmem + c + ((uint32_t)(32 * warp) << 16), t);
+        for (int c = 0; c < 64; c += 16) {
+          float t[16];
+          pm::tmem_ld16(tmem + qi * kHmax + c + ((uint32_t)(32 * warp) << 16), t);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) d[c + i] = t[i];
+          for (int i = 0; i < 16; ++i) acc += sW[qi * kHmax + c + i] * fmaxf(t[i], 0.f);
+        }
       }
-    }
-    if (r < p.R) {
-      float score = -INFINITY;
-      const int ph = r < cnt ? phys_b[r] : -1;
-      if (ok && ph >= 0) {
-        float acc = 0.f;
-#pragma unroll
-        for (int h = 0; h < 64; ++h) acc += sW[h] * fmaxf(d[h], 0.f);
-        const float ks = *reinterpret_cast<const float*>(smem + st * kStageStride + kRows * kD + tid * 4);
-        score = acc * ks;
+      if (r < p.R) {
+        const int64_t cq = min((int64_t)p.R, p.count[b0 + qi]);
+        p.scores[(int64_t)(b0 + qi) * p.score_stride + r] = (ok && ph >= 0 && r < cq) ? acc * ks : -INFINITY;
       }
-      p.scores[(int64_t)b * p.score_stride + r] = score;
     }
     pm::tc_fence_before();
     __syncthreads();  // TMEM row read and stage st consumed before it is refilled / overwritten
   }
-  if (warp == 0) pm::tmem_dealloc(tmem, 64);
+  if (warp == 0) pm::tmem_dealloc(tmem, ncols);
 }
 
 // ----------------------------------------------------------------------------- top-k
@@ -353,13 +359,16 @@ void launch_index_logits(const __nv_bfloat16* q, const float* w, int B, int H, c
                          const int64_t* count, int R, float* scores, int64_t score_stride, int num_sms, int* err,
                          cudaStream_t stream) {
   if (B == 0 || R == 0) return;
+  // queries that share one physical-row list (row stride 0) share CTAs: each key tile serves up to 4
+  const int nq = phys_stride == 0 ? (B >= 4 ? 4 : (B >= 2 ? 2 : 1)) : 1;
+  const int qblocks = (B + nq - 1) / nq;
   const int ntiles = (R + kRows - 1) / kRows;
   const int want_ctas = 2 * num_sms;
-  const int chunks = max(1, min(ntiles, (want_ctas + B - 1) / B));
+  const int chunks = max(1, min(ntiles, (want_ctas + qblocks - 1) / qblocks));
   const int per = (ntiles + chunks - 1) / chunks;
-  LogitParams p{q, w, B, H, keys, kscales, nrows, phys, phys_stride, count, R, per, scores, score_stride, err};
+  LogitParams p{q, w, B, H, keys, kscales, nrows, phys, phys_stride, count, R, per, nq, scores, score_stride, err};
   cudaFuncSetAttribute(index_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLogitSmem);
-  index_logits_kernel<<<dim3((ntiles + per - 1) / per, B), kLogitThreads, kLogitSmem, stream>>>(p);
+  index_logits_kernel<<<dim3((ntiles + per - 1) / per, qblocks), kLogitThreads, kLogitSmem, stream>>>(p);
 }
 
 void launch_index_topk(const float* scores, int64_t stride, int B, int R, int k, const int32_t* phys,

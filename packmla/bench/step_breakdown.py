@@ -38,6 +38,57 @@ def family(name: str) -> str:
     return "other"
 
 
+def _families(prof, per: int, top: int) -> tuple[float, dict, list]:
+    per_kernel: dict[str, float] = {}
+    for ev in prof.key_averages():
+        t = getattr(ev, "self_device_time_total", None)
+        if t is None:
+            t = ev.self_cuda_time_total
+        if t > 0:
+            per_kernel[ev.key] = per_kernel.get(ev.key, 0.0) + t / per
+    total = sum(per_kernel.values())
+    fams: dict[str, float] = {}
+    for k, v in per_kernel.items():
+        fams[family(k)] = fams.get(family(k), 0.0) + v
+    return total, ({k: {"us": round(v, 1), "share": round(v / total, 4)}
+                    for k, v in sorted(fams.items(), key=lambda kv: -kv[1])}), (
+        [{"name": k[:90], "us": round(v, 1), "share": round(v / total, 4)}
+         for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1])[:top]])
+
+
+def prefill_breakdown(args, cfg, device) -> dict:
+    """Kernel time of one 8192-token prefill chunk (the third of one request, eager, under the profiler)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from ..engine.engine import SamplingParams
+    from ..ops import check_errors
+    from ..parallel.comm import TPComm
+    from .engine_setup import build_engine
+
+    eng, _ = build_engine(cfg, device, 0, 1, TPComm(), 1, args.prompt_len, args.output_len, args.kv_format,
+                          prefix_cache=False)
+    gen = torch.Generator().manual_seed(0)
+    eng.add_request(torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=gen).tolist(),
+                    SamplingParams(max_new_tokens=1))
+    for _ in range(2):
+        eng.step()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        s.record()
+        eng.step()
+        e.record()
+        torch.cuda.synchronize(device)
+    check_errors(device)
+    total, fams, kernels = _families(prof, 1, args.top)
+    out = {"case": "prefill_chunk_breakdown", "chunk_tokens": 8192, "positions": [16384, 24576],
+           "kv_format": args.kv_format, "chunk_ms_profiled": round(s.elapsed_time(e), 2),
+           "kernel_ms": round(total / 1e3, 2), "families": fams, "kernels": kernels}
+    print(json.dumps(out), flush=True)
+    return out
+
+
 def main(argv=None) -> dict:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--concurrency", type=int, default=8)
@@ -47,6 +98,8 @@ def main(argv=None) -> dict:
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--dense-format", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--top", type=int, default=25, help="kernels listed individually")
+    ap.add_argument("--phase", default="decode", choices=["decode", "prefill"],
+                    help="prefill: one request alone, its third 8192-token chunk profiled (positions 16k-24k)")
     args = ap.parse_args(argv)
 
     import torch
@@ -62,6 +115,8 @@ def main(argv=None) -> dict:
     torch.cuda.set_device(device)
     cfg = ModelConfig(dense_format=args.dense_format)
     C = args.concurrency
+    if args.phase == "prefill":
+        return prefill_breakdown(args, cfg, device)
     eng, _ = build_engine(cfg, device, 0, 1, TPComm(), C, args.prompt_len, args.output_len, args.kv_format)
     eng.runner.capture()
     gen = torch.Generator().manual_seed(0)

@@ -611,12 +611,16 @@ class V4FlashModel:
                 ti[a:b] = i
         return lp, tv, ti
 
-    def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int = 256, qi=None):
+    def _index_topk_chunked(self, layer, q_lora, y, phys_row, count, lim, block: int | None = None, qi=None):
+        """Top-k of a prefill chunk's queries, `block` queries per indexer call (default: as many as keep the
+        fp32 score buffer within 32M entries, 256 .. 2048)."""
         T = q_lora.shape[0]
+        if block is None:
+            block = max(256, min(2048, ((32 << 20) // max(1, lim)) // 4 * 4))
         outs_s, outs_p = [], []
         for t0 in range(0, T, block):
             t1 = min(T, t0 + block)
-            ph = phys_row[:lim][None].expand(t1 - t0, -1).int().contiguous()
+            ph = phys_row[:lim].int()[None].expand(t1 - t0, -1)  # one row for all (the indexer shares key tiles)
             s, p = self._index_topk(layer, q_lora[t0:t1], y[t0:t1], ph, count[t0:t1], lim,
                                     None if qi is None else qi[t0:t1])
             outs_s.append(s)
