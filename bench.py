@@ -111,7 +111,7 @@ def main() -> None:
                     help="dense projections: BF16 (cuBLAS) or MXFP8 weights (packmla's tcgen05 GEMM)")
     ap.add_argument("--collectives", default="auto", choices=["auto", "fused", "nccl"],
                     help="TP all-reduces: packmla's fused GEMM+all-reduce kernels over NVLink, or NCCL; auto = fused "
-                         "at the world sizes the fused kernels were validated on (2), NCCL otherwise")
+                         "at the world sizes the fused kernels were validated on (2 and 4), NCCL otherwise")
     ap.add_argument("--dp-attention", default="auto", choices=["auto", "on", "off"],
                     help="DP attention (each rank serves C/N requests with every head, MoE tokens exchanged by "
                          "all-gather / reduce-scatter) or TP attention; auto = TP")
@@ -146,7 +146,7 @@ def main() -> None:
     if dp and C % world:
         raise SystemExit(f"--dp-attention: concurrency {C} must be a multiple of {world}")
     if args.collectives == "auto":
-        args.collectives = "fused" if world == 2 and not dp else "nccl"
+        args.collectives = "fused" if world in (2, 4) and not dp else "nccl"
     if dp and args.collectives == "fused":
         raise SystemExit("--dp-attention exchanges MoE tokens over NCCL: use --collectives nccl")
     if world > 1 and args.collectives == "fused":
