@@ -515,8 +515,10 @@ class V4FlashModel:
         tok_of = start - (W - 1) + swa_slots.long()
         swa_slots = torch.where(tok_of >= 0, swa_slots, torch.full_like(swa_slots, -1)).contiguous()
         swa_len = torch.full((T,), W, dtype=torch.int32, device=dev)
-        prev = torch.arange(start - (W - 1), start, device=dev)
-        prev_ok = prev >= 0
+        # the window's tokens before the chunk (host-known: no device round trip per layer)
+        n_prev = min(W - 1, start)
+        prev_ring = req_slot * W + torch.arange(start - n_prev, start, device=dev) % W
+        prev_dst = torch.arange(W - 1 - n_prev, W - 1, device=dev)
         meta_pos = pos
         x = self.W["embed"][tokens]
         pt = self.pool.page_table[req_slot].long()
@@ -538,10 +540,9 @@ class V4FlashModel:
             q_lora = rmsnorm(y[:, :Q], lw["q_norm"], eps)
             kv_raw = y[:, Q:Q + cfg.latent_dim].float().contiguous()
             scratch = torch.zeros(scr_pages * abi.NATIVE_PAGE_BYTES, dtype=torch.uint8, device=dev)
-            if bool(prev_ok.any()):
-                ring = req_slot * W + prev[prev_ok] % W
-                recs = kv_ops.native_pool_read(self.pool.swa[layer], ring)
-                _native_pool_write(scratch, torch.nonzero(prev_ok)[:, 0], recs)
+            if n_prev:
+                recs = kv_ops.native_pool_read(self.pool.swa[layer], prev_ring)
+                _native_pool_write(scratch, prev_dst, recs)
             kv_ops.native_store(kv_raw, lw["kv_norm"], eps, torch.arange(W - 1, W - 1 + T, device=dev),
                                 pos, self.freqs, scratch)
             last = slice(max(0, T - W), T)
@@ -551,7 +552,7 @@ class V4FlashModel:
             q = fused_ops.rope_q(q_lin.view(T, self.heads, cfg.latent_dim), pos, self.freqs)
             ratio = cfg.compress_ratios[layer]
             if ratio:
-                self._compress_prefill(layer, y, pos, req_slot, c4_phys_row, c128_phys_row)
+                self._compress_prefill(layer, y, pos, req_slot, c4_phys_row, c128_phys_row, start)
             if ratio == abi.C4_RATIO:
                 count = (pos + 1) // abi.C4_RATIO
                 n_vis = int(min(self.r4max, (start + T) // abi.C4_RATIO))
@@ -627,7 +628,7 @@ class V4FlashModel:
             outs_p.append(p)
         return torch.cat(outs_s).contiguous(), torch.cat(outs_p).contiguous()
 
-    def _compress_prefill(self, layer, y, pos, req_slot, c4_phys_row, c128_phys_row):
+    def _compress_prefill(self, layer, y, pos, req_slot, c4_phys_row, c128_phys_row, start: int):
         """Sequential-equivalent pooling over the chunk; stores every record completed in it."""
         lw = self.W["layers"][layer]
         fz = self.fused[layer]
@@ -637,12 +638,12 @@ class V4FlashModel:
         c = fz["wc_kv"]
         kv = y[:, c:c + L].float()
         gate = y[:, c + L:c + 2 * L].float() + lw["c_ape"][slot_in]
-        raw, rec = _pool_chunk(self.pool.comp_state[layer], req_slot, gate, kv, pos, ratio)
+        raw, rec = _pool_chunk(self.pool.comp_state[layer], req_slot, gate, kv, pos, ratio, start)
         if ratio == abi.C4_RATIO:
             c = fz["wi_k"]
             k = y[:, c:c + D].float()
             kg = y[:, c + D:c + 2 * D].float() + lw["i_ape"][slot_in]
-            kraw, _ = _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio)
+            kraw, _ = _pool_chunk(self.pool.index_state[layer], req_slot, kg, k, pos, ratio, start)
         if not rec.numel():
             return
         if ratio == abi.C4_RATIO:
@@ -658,17 +659,17 @@ class V4FlashModel:
 
 
 def _pool_chunk(state: torch.Tensor, req_slot: int, gate: torch.Tensor, val: torch.Tensor, pos: torch.Tensor,
-                ratio: int):
-    """Online-softmax pooling of consecutive tokens into groups of `ratio`.
+                ratio: int, p0: int):
+    """Online-softmax pooling of consecutive tokens (positions p0 .. p0 + T - 1, `pos`) into groups of
+    `ratio`.
 
     Returns (raw rows of groups completed in the chunk [G, D], their record indices [G]);
     the trailing partial group is left in `state[req_slot]`.
     """
     T, D = gate.shape
-    p0 = int(pos[0])
     first_group = p0 // ratio
     grp = (pos // ratio) - first_group  # [T] 0-based group ids in the chunk
-    ng = int(grp[-1]) + 1
+    ng = (p0 + T - 1) // ratio - first_group + 1
     st = state[req_slot]
     # per-group max over tokens (and the carried state for group 0)
     gmax = torch.full((ng, D), float("-inf"), device=gate.device)
