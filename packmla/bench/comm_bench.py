@@ -1,6 +1,7 @@
 """Per-call device time of the TP collectives: packmla's fused kernels vs cuBLAS + NCCL.
 
     torchrun --nproc-per-node N -m packmla.bench.comm_bench [--tokens B ...]
+    python -m packmla.bench.comm_bench [--tokens B ...]          (one GPU: the kernels at world 1)
 
 Cases per token count B (decode batch of all ranks' requests):
   o_proj   Y = sum_r X_r W_r^T, X_r [B, 8192/N], W_r [4096, 8192/N] bf16 (attention output projection)
@@ -64,6 +65,15 @@ def main() -> None:
     from ..ops._ext import check_errors
 
     rank, world, local = init_from_env("nccl")
+    if not dist.is_initialized():  # one process without torchrun: a one-rank group (the kernels run at world 1)
+        import socket
+
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{port}",
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     hidden, o_in = 4096, 8192
     K = o_in // world
