@@ -101,10 +101,10 @@ def test_group_without_room_falls_back_to_prefill_and_sampling_is_independent():
     assert len(eng3.result(rids[1]).output_ids) == 2
 
 
-def _block_engine(max_running=3, fmt="direct", prefix=True):
+def _block_engine(max_running=3, fmt="direct", prefix=True, **kw):
     cfg = ModelConfig.tiny(num_layers=3)
     ecfg = EngineConfig(kv_cache_format=fmt, device="cpu", chunked_prefill_size=64, max_running_requests=max_running,
-                        cuda_graph_bs=[1, 2, 4], prefix_cache=prefix, prefix_block_tokens=256)
+                        cuda_graph_bs=[1, 2, 4], prefix_cache=prefix, prefix_block_tokens=256, **kw)
     return Engine.build(cfg, ecfg, "cpu", max_context=1024)
 
 
@@ -166,3 +166,21 @@ def test_page_allocator_reference_counts():
         a.release(p)
     with pytest.raises(ValueError):
         a.share(p)
+
+
+def test_prefix_blocks_with_fp4_and_per_layer_layouts():
+    """Shared prefix blocks over FP4 Packed pages and over per-layer Packed survivor counts (read by
+    reconstruction) give the tokens of an engine without the cache."""
+    cfg = ModelConfig.tiny(num_layers=3)
+    counts = {layer: 128 for layer in cfg.c4_layers}
+    prefix = _toks(512, 41)
+    prompts = [prefix + _toks(30 + 7 * i, 50 + i) for i in range(2)]
+    for fmt, kw in (("fp4-direct", {}), ("direct", {"decode_impl": "adapter", "layer_keep_counts": counts})):
+        eng = _block_engine(fmt=fmt, **kw)
+        rids = [eng.add_request(p, SamplingParams(max_new_tokens=3)) for p in prompts]
+        while eng.has_work():
+            eng.step()
+        assert eng.metrics.snapshot()["prefix_block_hit_tokens"] == 512, fmt
+        ref = _block_engine(fmt=fmt, prefix=False, **kw)
+        assert [eng.result(r).output_ids for r in rids] == \
+            [ref.generate([p], SamplingParams(max_new_tokens=3))[0] for p in prompts], fmt
