@@ -228,6 +228,8 @@ class Engine:
             from ..kv.hicache import HostKVCache
 
             self.hicache = HostKVCache(pool, engine_cfg.hicache_ratio, engine_cfg.hicache_mem_layout)
+            if self.blocks is not None:
+                self.blocks.host = self.hicache  # evicted prompt blocks move to the host tier
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -444,21 +446,27 @@ class Engine:
                     return None
                 if adopted:
                     return req
-            # shared prompt blocks: their pages are mapped, not allocated (pinned against eviction meanwhile)
+            # shared prompt blocks: their pages are mapped, not allocated (pinned against eviction meanwhile);
+            # host-resident ones are copied back into new pages first
             chain = self.blocks.match(req.prompt) if self.blocks is not None and reuse else []
             while chain and (chain[-1].index + 1) * self.blocks.block > reuse_limit:
                 chain.pop()
-            shared, shared128 = self.blocks.shared_pages(chain) if chain else ([], [])
+            n_shared, n_shared128 = self.blocks.shared_counts(chain) if chain else (0, 0)
+            r_pages, r_c128 = self.blocks.restore_need(chain) if chain else (0, 0)
             for n in chain:
                 n.pins += 1
-            pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE - len(shared)
-            c128_needed = (need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE - len(shared128)
+            pages_needed = (need + KVPool.TOKENS_PER_PAGE - 1) // KVPool.TOKENS_PER_PAGE - n_shared + r_pages
+            c128_needed = ((need + KVPool.TOKENS_PER_C128_PAGE - 1) // KVPool.TOKENS_PER_C128_PAGE
+                           - n_shared128 + r_c128)
             while ((not self.pool._free_slots or pages_needed > self.pool.pages.free
                     or c128_needed > self.pool.c128_pages.free) and self._evict_cached()):
                 pass
             fits = not (not self.pool._free_slots or pages_needed > self.pool.pages.free
                         or c128_needed > self.pool.c128_pages.free)
             if fits:
+                if r_pages:
+                    self.metrics.inc("prefix_block_host_hits", self.blocks.promote(chain))
+                shared, shared128 = self.blocks.shared_pages(chain) if chain else ([], [])
                 req.slot = self.pool.admit(need, shared, shared128)  # the request's own page references
             for n in chain:
                 n.pins -= 1
@@ -689,6 +697,7 @@ class Engine:
             "prefix_cache": self.ecfg.prefix_cache,
             "prefix_cache_retained": len(self.retained),
             "prefix_blocks": len(self.blocks.nodes) if self.blocks is not None else 0,
+            "prefix_blocks_on_host": self.blocks.host_nodes if self.blocks is not None else 0,
             "enable_hierarchical_cache": self.hicache is not None,
             "hicache_host_bytes": self.hicache.host_bytes() if self.hicache is not None else 0,
         }

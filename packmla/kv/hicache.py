@@ -226,5 +226,34 @@ class HostKVCache:
             self._free_c128.extend(e.host_c128)
         self.entries.clear()
 
+    # ------------------------------------------------------------------ page lists (prefix blocks)
+    def alloc_host(self, n_pages: int, n_c128: int, evict_entries: bool = True) -> tuple | None:
+        """Host pages for a prefix block's pages (request entries are evicted first when `evict_entries`)."""
+        if evict_entries:
+            self._evict_until(n_pages, n_c128)
+        if len(self._free) < n_pages or len(self._free_c128) < n_c128:
+            return None
+        return [self._free.pop() for _ in range(n_pages)], [self._free_c128.pop() for _ in range(n_c128)]
+
+    def free_host(self, host_pages: list[int], host_c128: list[int]) -> None:
+        self._free.extend(host_pages)
+        self._free_c128.extend(host_c128)
+
+    def copy_pages(self, dev_pages: list[int], host_pages: list[int], dev_c128: list[int], host_c128: list[int],
+                   to_host: bool) -> int:
+        """Every plane of the given device pages <-> the given host pages, in one segment-copy launch."""
+        pairs = []
+        for d, h in zip(dev_pages, host_pages):
+            for p in self.planes:
+                o = self._host_start(p, h, self.page_bytes)
+                pairs.append((p.dev[d * p.page_bytes:(d + 1) * p.page_bytes], self.host[o:o + p.page_bytes]))
+        for d, h in zip(dev_c128, host_c128):
+            for p in self.c128_planes:
+                o = self._host_start(p, h, self.c128_page_bytes)
+                pairs.append((p.dev[d * p.page_bytes:(d + 1) * p.page_bytes], self.host_c128[o:o + p.page_bytes]))
+        n = self._run(pairs, to_host) if pairs else 0
+        self.stats["bytes_d2h" if to_host else "bytes_h2d"] += n
+        return n
+
     def host_bytes(self) -> int:
         return self.host.numel() + self.host_c128.numel()

@@ -272,3 +272,32 @@ def test_prefix_blocks_reproduce_recomputation_exactly(cuda):
         eng.runner.release()
     check_errors(cuda)
     assert outs[True] == outs[False]
+
+
+def test_prefix_blocks_through_the_host_tier_reproduce_recomputation(cuda):
+    """Shared prompt blocks demoted to pinned host pages (segment-copy kernel, snapshots to pinned memory)
+    and promoted back into new device pages on the next match produce exactly the tokens of recomputation."""
+    cfg = small_gpu_config()
+    W = init_weights(cfg, device=cuda, seed=9)
+    g = torch.Generator().manual_seed(5)
+    prefix = torch.randint(0, cfg.vocab_size, (512,), generator=g).tolist()
+    prompts = [prefix + torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 77)]
+    outs = {}
+    for cache in (True, False):
+        ecfg = EngineConfig(kv_cache_format="direct", max_running_requests=2, cuda_graph_bs=[1, 2],
+                            chunked_prefill_size=128, prefix_cache=cache, prefix_block_tokens=256,
+                            enable_hierarchical_cache=cache, disable_cuda_graph=True)
+        eng = Engine.build(cfg, ecfg, cuda, max_context=1024, max_requests=2, kv_bytes=64 << 20, weights=W)
+        outs[cache] = [eng.generate([prompts[0]], SamplingParams(max_new_tokens=4))[0]]
+        if cache:
+            while eng._evict_retained():
+                pass
+            eng.hicache.flush()
+            while eng.blocks.evict_one():
+                pass
+            assert eng.blocks.host_nodes == 2 and eng.pool.pages.free == eng.pool.num_pages
+        outs[cache].append(eng.generate([prompts[1]], SamplingParams(max_new_tokens=4))[0])
+        if cache:
+            assert eng.metrics.snapshot()["prefix_block_host_hits"] == 2
+    check_errors(cuda)
+    assert outs[True] == outs[False]

@@ -184,3 +184,35 @@ def test_prefix_blocks_with_fp4_and_per_layer_layouts():
         ref = _block_engine(fmt=fmt, prefix=False, **kw)
         assert [eng.result(r).output_ids for r in rids] == \
             [ref.generate([p], SamplingParams(max_new_tokens=3))[0] for p in prompts], fmt
+
+
+def test_prefix_blocks_move_to_the_host_tier_and_back():
+    """With HiCache on, evicted blocks move to pinned host pages (their KV pages, the C128 pages their
+    tokens write, their snapshots) instead of being dropped; a later prompt on the same prefix copies them
+    back into new pages, root first, and gives the tokens of an engine without any cache.  With host room
+    for one block only, demoting the root drops the host-resident leaf first."""
+    prefix = _toks(512, 61)
+    first, later = prefix + _toks(33, 62), prefix + _toks(47, 63)
+    ref = _block_engine(prefix=False).generate([later], SamplingParams(max_new_tokens=4))[0]
+    for ratio, kept in ((2.0, 2), (1e-6, 1)):
+        eng = _block_engine(enable_hierarchical_cache=True, hicache_ratio=ratio)
+        eng.generate([first], SamplingParams(max_new_tokens=2))
+        while eng._evict_retained():
+            pass
+        eng.hicache.flush()  # only the blocks may serve the later prompt
+        while eng.blocks.evict_one():
+            pass
+        assert eng.blocks.host_nodes == kept and eng.blocks.held_pages == 0
+        assert eng.pool.pages.free == eng.pool.num_pages and eng.pool.c128_pages.free == eng.pool.num_c128_pages
+        assert eng.blocks.stats["demoted"] == 2 and eng.blocks.stats["dropped"] == 2 - kept
+        rid = eng.add_request(later, SamplingParams(max_new_tokens=4))
+        while eng.has_work():
+            eng.step()
+        m = eng.metrics.snapshot()
+        assert m["prefix_block_host_hits"] == kept and eng.blocks.host_nodes == 0
+        assert eng.result(rid).cached_tokens == 256 * kept
+        assert eng.result(rid).output_ids == ref, ratio
+        assert eng.server_info()["prefix_blocks_on_host"] == 0
+        eng.flush_cache()
+        assert not eng.blocks.nodes and eng.pool.pages.free == eng.pool.num_pages
+        assert sorted(eng.hicache._free) == list(range(eng.hicache.num_host_pages))
