@@ -151,7 +151,8 @@ __device__ __forceinline__ uint4 bf16x8_to_f16(uint4 v) {
 }
 
 struct RowRef {
-  int kind;  // 0 = masked, 1 = native (swa pool), 2 = native (csa pool), 3 = packed, 4/5 = FP4 native/packed
+  int kind;  // 0 = masked, 1 = native (swa pool), 2 = native (csa pool), 3 = packed, 4/5 = FP4 native/packed,
+             // 6/7 = GLM-5.3 native/packed
   int slot;
   int pos;
 };
@@ -189,7 +190,7 @@ __device__ __forceinline__ RowRef idx_resolve(const DecodeParams& p, const RowId
     pm::report_error(p.err, pm::kIndexOutOfRange, i);
     return r;
   }
-  r.kind = p.csa_fp4 ? 3 + p.csa_fp4 : (p.csa_packed ? 3 : 2);
+  r.kind = p.csa_glm ? 5 + p.csa_glm : (p.csa_fp4 ? 3 + p.csa_fp4 : (p.csa_packed ? 3 : 2));
   r.slot = s;
   r.pos = x.pos;
   return r;
@@ -203,6 +204,8 @@ __device__ __forceinline__ RowRef idx_resolve(const DecodeParams& p, const RowId
 //           (sc.x) and 2 v + 16, 2 v + 17 (sc.y).
 //   FP4 Packed: u[0] = code unit v (v < 8: the 128 survivor code bytes); u[2] = bitmap words 2 v, 2 v + 1
 //           (v < 4); u[3], u[4] = the 32 E4M3 scale bytes.
+//   GLM Native: u[i] = 16-byte unit v + 8 i of the 512-code row.
+//   GLM Packed: u[0], u[1] = value units v, v + 8; u[2] = bitmap unit v (v < 4).
 //   sc: the row's 8 UE8M0 scale bytes (FP8 rows).
 struct Raw {
   uint4 u[5];
@@ -250,6 +253,16 @@ __device__ __forceinline__ void fetch(const DecodeParams& p, const RowRef& rr, i
     const uint4* sc = reinterpret_cast<const uint4*>(pg + kPage * kFp4PackedData + rip * 32);
     R.u[3] = sc[0];
     R.u[4] = sc[1];
+  } else if (rr.kind == 6) {
+    const uint4* data = reinterpret_cast<const uint4*>(p.csa_pool + (int64_t)rr.slot * kD);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) R.u[i] = data[v + 8 * i];
+  } else if (rr.kind == 7) {
+    const uint4* vals = reinterpret_cast<const uint4*>(p.csa_values + (int64_t)rr.slot * 256);
+    const uint4* bits = reinterpret_cast<const uint4*>(p.csa_bitmap + (int64_t)rr.slot * 8);
+    R.u[0] = vals[v];
+    R.u[1] = vals[v + 8];
+    if (v < 4) R.u[2] = bits[v];
   }
 }
 
@@ -294,8 +307,18 @@ __device__ __noinline__ void expand_row(const Raw R, int brow, int v, uint8_t* _
     // the lane's tail unit (8 BF16 coordinates, already rotated)
     const int ut = v >= 4 ? v + 24 : v + 32;
     *out(896 + 16 * (ut - 28)) = bf16x8_to_f16(v >= 4 ? R.u[3] : R.u[4]);
-  } else if (R.kind == 3) {
+  } else if (R.kind == 6) {
+    // GLM Native: raw E4M3 units v + 8 i (coordinates 16 u .. 16 u + 15), exact in FP16
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int u = v + 8 * i;
+      *out(32 * u) = dq8(make_uint2(R.u[i].x, R.u[i].y), 0, err);
+      *out(32 * u + 16) = dq8(make_uint2(R.u[i].z, R.u[i].w), 0, err);
+    }
+  } else if (R.kind == 3 || R.kind == 7) {
     // the values are staged (256 bytes); the 8 bitmap words come from lanes 0..3 of the row's group
+    // (GLM Packed rows: raw E4M3 survivors, no scales and no RoPE word)
+    const bool glm = R.kind == 7;
     const uint32_t gmask = 0xFFu << (8 * ((threadIdx.x & 31) >> 3));
     *reinterpret_cast<uint4*>(stg + 16 * v) = R.u[0];
     *reinterpret_cast<uint4*>(stg + 16 * (v + 8)) = R.u[1];
@@ -323,9 +346,9 @@ __device__ __noinline__ void expand_row(const Raw R, int brow, int v, uint8_t* _
       const uint32_t lo = __funnelshift_r(vw[0], vw[1], sh), hi = __funnelshift_r(vw[1], vw[2], sh);
       const uint4 e = lut[bits];
       const uint2 codes = make_uint2(__byte_perm(lo, hi, e.x) & e.z, __byte_perm(lo, hi, e.y) & e.w);
-      const int ex = scale_exp(R.sc, i);
+      const int ex = glm ? 0 : scale_exp(R.sc, i);
       uint4 o;
-      if (i < 7) {
+      if (i < 7 || glm) {
         o = dq8(codes, ex, err);
       } else {
         // dequantize (exact in fp32), round to BF16, rotate with the record's pair (cos, sin), round again
@@ -512,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
   // inputs the epilogue needs, loaded now so no late global load sits before a cluster barrier
   if (tid < kHG) sink2v[tid] = (p.sink && h0 + tid < p.H) ? p.sink[h0 + tid] * kLog2e : -INFINITY;
   const int qpos_raw = p.q_pos ? p.q_pos[b] : 0;
-  const int nswa = min(p.swa_len[b], p.swa_cap);
+  const int nswa = p.swa_cap > 0 ? min(p.swa_len[b], p.swa_cap) : 0;
   const int ntot = nswa + min(p.csa_len[b], p.csa_cap);
   const int tiles_q = (ntot + kTileRows - 1) / kTileRows;
   const int t0 = (split * tiles_q) / p.num_splits;  // 32-bit: tiles_q is at most a few thousand
@@ -745,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     __nv_bfloat16* sOut = reinterpret_cast<__nv_bfloat16*>(sK);  // [64 heads][512] BF16
     __half* sPartH = reinterpret_cast<__half*>(sK);              // [64 heads][512] FP16 O / l (cluster merge)
     int qp = 0;
-    if (direct || clustered) {
+    if ((direct || clustered) && !p.no_rope) {
       qp = qpos_raw;
       if (qp < 0 || qp >= p.freq_rows) { pm::report_error(p.err, pm::kIndexOutOfRange, b); qp = 0; }
     }
@@ -753,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
     // for the tail, their inverse-RoPE pairs, loaded now so they have arrived by the cluster barrier
     const int d0 = 8 * (tid % (kD / 8));
     float rc[4] = {1.f, 1.f, 1.f, 1.f}, rs[4] = {0.f, 0.f, 0.f, 0.f};
-    if (clustered && d0 >= 448) {
+    if (clustered && d0 >= 448 && !p.no_rope) {
       const float4* f = reinterpret_cast<const float4*>(p.freqs + (int64_t)qp * 64 + (d0 - 448));
       const float4 f0 = f[0], f1 = f[1];  // (cos, sin) of pairs (d0 - 448) / 2 .. + 3
       rc[0] = f0.x; rs[0] = -f0.y; rc[1] = f0.z; rs[1] = -f0.w;
@@ -784,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = __bfloat162float(__float2bfloat16_rn(o[i] * fac[32 * hf + i]));
-        if (d >= 448) {  // inverse RoPE of the tail: pair (d, d + 1) = lanes (2 k, 2 k + 1)
+        if (d >= 448 && !p.no_rope) {  // inverse RoPE of the tail: pair (d, d + 1) = lanes (2 k, 2 k + 1)
           const int pair = (d - 448) >> 1;
           const float c = p.freqs[(int64_t)qp * 64 + 2 * pair], sn = -p.freqs[(int64_t)qp * 64 + 2 * pair + 1];
           const bool odd = d & 1;
@@ -896,7 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_decode_kernel(const De
         for (int k = 0; k < 4; ++k) {  // BF16 output; the tail inverse-rotated (pairs (d, d + 1)) and rounded again
           float re = __bfloat162float(__float2bfloat16_rn(acc[2 * k]));
           float im = __bfloat162float(__float2bfloat16_rn(acc[2 * k + 1]));
-          if (d0 >= 448) {
+          if (d0 >= 448 && !p.no_rope) {
             const float r2 = __fsub_rn(__fmul_rn(re, rc[k]), __fmul_rn(im, rs[k]));
             const float i2 = __fadd_rn(__fmul_rn(re, rs[k]), __fmul_rn(im, rc[k]));
             re = r2;
@@ -929,7 +952,7 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restric
                                                           const int32_t* __restrict__ q_pos,
                                                           const float* __restrict__ freqs, int64_t freq_rows, int B,
                                                           int H, int splits, __nv_bfloat16* __restrict__ out,
-                                                          float* __restrict__ lse, int* err) {
+                                                          float* __restrict__ lse, int* err, int no_rope) {
   pm::griddep_wait();  // the decode kernel's partials are complete
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (wid >= B * H) return;
@@ -959,7 +982,7 @@ __global__ void __launch_bounds__(256) mla_combine_kernel(const float* __restric
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i] = __bfloat162float(__float2bfloat16_rn(acc[i] * inv));
   // inverse-rotate the tail (coords 448..511 live in chunk j = 3, lanes 16..31)
-  if (lane >= 16) {
+  if (lane >= 16 && !no_rope) {
     int pos = q_pos ? q_pos[b] : 0;
     if (pos < 0 || pos >= freq_rows) { pm::report_error(err, pm::kIndexOutOfRange, b); pos = 0; }
     const float* f = freqs + (int64_t)pos * 64;
@@ -1028,7 +1051,7 @@ void launch_sparse_mla_decode(const DecodeParams& params, const float* sink, con
   if (p.num_splits > 1 && !clustered) {
     const int warps = p.B * p.H;
     launch_pdl(mla_combine_kernel, (warps + 7) / 8, 256, 0, 1, stream, p.part_o, p.part_ml, sink, q_pos, p.freqs,
-               p.freq_rows, p.B, p.H, p.num_splits, out, lse, p.err);
+               p.freq_rows, p.B, p.H, p.num_splits, out, lse, p.err, p.no_rope);
   }
 }
 

@@ -117,6 +117,9 @@ __global__ void __launch_bounds__(256) native_store_kernel(
 }
 
 // ----------------------------------------------------------------------------- packed
+// kRaw: GLM-5.3 Packed rows (raw E4M3 survivors, no scale plane): the same selection and masked norm, codes
+// of y itself.
+template <bool kRaw>
 __global__ void __launch_bounds__(256) packed_store_kernel(
     const float* __restrict__ raw, int64_t raw_stride, const float* __restrict__ weight, float eps,
     const int64_t* __restrict__ slots, uint8_t* __restrict__ values, uint64_t* __restrict__ bitmap,
@@ -195,11 +198,14 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
   uint64_t words[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float amax = 0.f;
+    int e = 0;
+    if (!kRaw) {
+      float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fabsf(y[4 * j + i]));
-    amax = half_max(amax);
-    const int e = ue8m0_exp(amax);
+      for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fabsf(y[4 * j + i]));
+      amax = half_max(amax);
+      e = ue8m0_exp(amax);
+    }
     codes[j] = e + 127;
     const float inv = pm::exp2i(-e);
     uint16_t lo = pm::f32x2_to_e4m3x2(y[4 * j + 0] * inv, y[4 * j + 1] * inv);
@@ -231,6 +237,7 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
 #pragma unroll
     for (int j = 0; j < 4; ++j) bitmap[slot * 8 + 2 * j + half] = words[j];
   }
+  if (kRaw) return;
   int c_hi[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) c_hi[j] = __shfl_sync(0xffffffffu, codes[j], 16);
@@ -239,6 +246,66 @@ __global__ void __launch_bounds__(256) packed_store_kernel(
     uint32_t hi_word = (uint32_t)codes[2] | ((uint32_t)c_hi[2] << 8) | ((uint32_t)codes[3] << 16) | ((uint32_t)c_hi[3] << 24);
     *reinterpret_cast<uint2*>(scales + slot * 8) = make_uint2(lo_word, hi_word);
   }
+}
+
+// ----------------------------------------------------------------------------- GLM-5.3 Native
+// 512 raw E4M3 codes of y = bf16((x r) w) per row, rows contiguous ([rows, 512] bytes).
+__global__ void __launch_bounds__(256) glm_native_store_kernel(
+    const float* __restrict__ raw, int64_t raw_stride, const float* __restrict__ weight, float eps,
+    const int64_t* __restrict__ slots, uint8_t* __restrict__ pool, int64_t pool_rows, int rows, int* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int64_t slot = slots[warp];
+  if (slot < 0) return;
+  if (slot >= pool_rows) { if (lane == 0) pm::report_error(err, pm::kIndexOutOfRange, warp); return; }
+  float x[16];
+  load_row(raw + (int64_t)warp * raw_stride, lane, x);
+  const float ss = lane_sumsq(x);
+  const float r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.f / 512.f), eps)));
+  uint8_t* row = pool + slot * kD;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      y[i] = bf16_round(__fmul_rn(__fmul_rn(x[4 * j + i], r), weight[128 * j + 4 * lane + i]));
+    const uint16_t lo = pm::f32x2_to_e4m3x2(y[0], y[1]), hi = pm::f32x2_to_e4m3x2(y[2], y[3]);
+    *reinterpret_cast<uint32_t*>(row + 128 * j + 4 * lane) = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+}
+
+// GLM-5.3 Adapter: Packed rows (256 survivors + LSB-first bitmap) -> Native rows (dropped coordinates 0).
+// One warp per row; lane l writes coordinates 16 l .. 16 l + 15 (bits 16 (l % 4) .. of word l / 4).
+__global__ void __launch_bounds__(256) glm_packed_to_native_kernel(
+    const uint8_t* __restrict__ values, const uint64_t* __restrict__ bitmap, int64_t pool_rows,
+    const int64_t* __restrict__ rows_in, uint8_t* __restrict__ out, int rows, int* err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int64_t r = rows_in[warp];
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)warp * kD) + lane;
+  if (r < 0 || r >= pool_rows) {
+    if (r >= pool_rows && lane == 0) pm::report_error(err, pm::kIndexOutOfRange, warp);
+    *dst = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint64_t* bw = bitmap + r * 8;
+  const int w = lane >> 2, sh = 16 * (lane & 3);
+  int rank = 0;
+  for (int k = 0; k < w; ++k) rank += __popcll(bw[k]);
+  const uint64_t word = bw[w];
+  rank += __popcll(word & ((1ull << sh) - 1ull));
+  const uint32_t bits = (uint32_t)(word >> sh) & 0xFFFFu;
+  const uint8_t* v = values + r * 256;
+  alignas(16) uint8_t c[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const bool kept = ((bits >> k) & 1u) && rank < 256;  // a row with more than 256 bits set reads no further
+    c[k] = kept ? v[rank] : (uint8_t)0;
+    rank += kept;
+  }
+  *dst = *reinterpret_cast<const uint4*>(c);
 }
 
 }  // namespace
@@ -255,6 +322,24 @@ void launch_packed_store(const float* raw, int64_t raw_stride, const float* weig
                          uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int keep, int rows,
                          int* err, cudaStream_t stream) {
   if (rows == 0) return;
-  packed_store_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(raw, raw_stride, weight, eps, slots, values, bitmap, scales,
-                                                          pool_rows, keep, rows, err);
+  packed_store_kernel<false><<<(rows + 7) / 8, 256, 0, stream>>>(raw, raw_stride, weight, eps, slots, values, bitmap,
+                                                                 scales, pool_rows, keep, rows, err);
+}
+
+void launch_glm_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
+                      bool packed, uint8_t* pool, uint8_t* values, uint64_t* bitmap, int64_t pool_rows, int rows,
+                      int* err, cudaStream_t stream) {
+  if (rows == 0) return;
+  if (packed)
+    packed_store_kernel<true><<<(rows + 7) / 8, 256, 0, stream>>>(raw, raw_stride, weight, eps, slots, values, bitmap,
+                                                                  nullptr, pool_rows, 256, rows, err);
+  else
+    glm_native_store_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(raw, raw_stride, weight, eps, slots, pool, pool_rows,
+                                                                rows, err);
+}
+
+void launch_glm_packed_to_native(const uint8_t* values, const uint64_t* bitmap, int64_t pool_rows,
+                                 const int64_t* rows_in, uint8_t* out, int rows, int* err, cudaStream_t stream) {
+  if (rows == 0) return;
+  glm_packed_to_native_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(values, bitmap, pool_rows, rows_in, out, rows, err);
 }

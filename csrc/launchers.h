@@ -12,6 +12,13 @@ void launch_native_store(const float* raw, int64_t raw_stride, const float* weig
 void launch_packed_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
                          uint8_t* values, uint64_t* bitmap, uint8_t* scales, int64_t pool_rows, int keep, int rows,
                          int* err, cudaStream_t stream);
+// GLM-5.3 MLA rows: Native = 512 raw E4M3 codes per row ([rows, 512]); Packed = the 256 largest-|raw|
+// coordinates' codes ([rows, 256]) + an LSB-first 512-bit bitmap ([rows, 8] words).
+void launch_glm_store(const float* raw, int64_t raw_stride, const float* weight, float eps, const int64_t* slots,
+                      bool packed, uint8_t* pool, uint8_t* values, uint64_t* bitmap, int64_t pool_rows, int rows,
+                      int* err, cudaStream_t stream);
+void launch_glm_packed_to_native(const uint8_t* values, const uint64_t* bitmap, int64_t pool_rows,
+                                 const int64_t* rows_in, uint8_t* out, int rows, int* err, cudaStream_t stream);
 
 // Sparse MLA decode (csrc/attention_decode.cu).  A query's rows [SWA ; C4] are split into 64-row
 // stages; split s of num_splits takes an even share of whole stages.
@@ -28,6 +35,8 @@ struct DecodeParams {
   // CSA rows
   int csa_packed;
   int csa_fp4;               // 0 = FP8 records; 1 = FP4 Native pages (288 B records), 2 = FP4 Packed (224 B)
+  int csa_glm;               // 0, or GLM-5.3 rows: 1 = Native (csa_pool [rows, 512] E4M3), 2 = Packed (values, bitmap)
+  int no_rope;               // 1: no RoPE tail (the output is not inverse-rotated; freqs and q_pos are not read)
   const uint8_t* csa_pool;   // native pages (csa_packed == 0; FP8 or, with csa_fp4, FP4)
   const uint8_t* csa_values; // packed planes
   const uint64_t* csa_bitmap;

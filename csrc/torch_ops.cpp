@@ -150,6 +150,122 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor swa_pool, torch::Tensor sw
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+namespace {
+void check_glm_rows(const torch::Tensor& t, int64_t width, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.size(1) == width && t.is_contiguous() &&
+              reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, what);
+}
+}  // namespace
+
+void glm_store(torch::Tensor raw, torch::Tensor weight, double eps, torch::Tensor slots, bool packed,
+               torch::Tensor pool, torch::Tensor values, torch::Tensor bitmap, torch::Tensor err) {
+  check_rows(raw);
+  check_err(err);
+  TORCH_CHECK(weight.is_cuda() && weight.scalar_type() == torch::kFloat32 && weight.numel() == kD && weight.is_contiguous());
+  TORCH_CHECK(slots.scalar_type() == torch::kInt64 && slots.numel() == raw.size(0) && slots.is_contiguous());
+  int64_t rows;
+  if (packed) {
+    TORCH_CHECK(values.scalar_type() == torch::kUInt8, "values must be uint8");
+    check_glm_rows(values, 256, "values must be [rows, 256] contiguous, 16-byte aligned");
+    TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.size(0) == values.size(0), "bitmap must be int64 [rows, 8]");
+    check_glm_rows(bitmap, 8, "bitmap must be [rows, 8] contiguous, 16-byte aligned");
+    rows = values.size(0);
+  } else {
+    TORCH_CHECK(pool.scalar_type() == torch::kUInt8, "pool must be uint8");
+    check_glm_rows(pool, kD, "pool must be [rows, 512] contiguous, 16-byte aligned");
+    rows = pool.size(0);
+  }
+  const c10::cuda::CUDAGuard g(raw.device());
+  launch_glm_store(raw.data_ptr<float>(), raw.stride(0), weight.data_ptr<float>(), (float)eps, slots.data_ptr<int64_t>(),
+                   packed, packed ? nullptr : pool.data_ptr<uint8_t>(), packed ? values.data_ptr<uint8_t>() : nullptr,
+                   packed ? reinterpret_cast<uint64_t*>(bitmap.data_ptr<int64_t>()) : nullptr, rows, raw.size(0),
+                   err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void glm_packed_to_native(torch::Tensor values, torch::Tensor bitmap, torch::Tensor rows, torch::Tensor out,
+                          torch::Tensor err) {
+  check_err(err);
+  TORCH_CHECK(values.scalar_type() == torch::kUInt8, "values must be uint8");
+  check_glm_rows(values, 256, "values must be [rows, 256] contiguous, 16-byte aligned");
+  TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.size(0) == values.size(0), "bitmap must be int64 [rows, 8]");
+  check_glm_rows(bitmap, 8, "bitmap must be [rows, 8] contiguous, 16-byte aligned");
+  TORCH_CHECK(rows.is_cuda() && rows.scalar_type() == torch::kInt64 && rows.dim() == 1 && rows.is_contiguous());
+  TORCH_CHECK(out.scalar_type() == torch::kUInt8 && out.size(0) == rows.size(0), "out must be uint8 [R, 512]");
+  check_glm_rows(out, kD, "out must be [R, 512] contiguous, 16-byte aligned");
+  const c10::cuda::CUDAGuard g(values.device());
+  launch_glm_packed_to_native(values.data_ptr<uint8_t>(), reinterpret_cast<const uint64_t*>(bitmap.data_ptr<int64_t>()),
+                              values.size(0), rows.data_ptr<int64_t>(), out.data_ptr<uint8_t>(), (int)rows.size(0),
+                              err.data_ptr<int>(), stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void glm_sparse_decode(torch::Tensor q, int64_t csa_glm, torch::Tensor pool, torch::Tensor values, torch::Tensor bitmap,
+                       torch::Tensor slots, torch::Tensor lens, double scale, int64_t num_splits, torch::Tensor part_o,
+                       torch::Tensor part_ml, torch::Tensor out, torch::Tensor lse, torch::Tensor err) {
+  constexpr int kHG = 64;
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == kD && q.stride(2) == 1);
+  TORCH_CHECK(q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "q rows must be 16-byte aligned");
+  check_err(err);
+  const int B = q.size(0), H = q.size(1);
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == torch::kInt32 && slots.dim() == 2 && slots.size(0) == B &&
+              slots.is_contiguous(), "slots must be int32 [B, K]");
+  TORCH_CHECK(lens.is_cuda() && lens.scalar_type() == torch::kInt32 && lens.numel() == B && lens.is_contiguous());
+  TORCH_CHECK(csa_glm == 1 || csa_glm == 2, "csa_glm: 1 (GLM Native) or 2 (GLM Packed)");
+  TORCH_CHECK(num_splits >= 1);
+  if (decode_uses_partials((int)num_splits)) {
+    TORCH_CHECK(part_o.is_cuda() && part_o.scalar_type() == torch::kFloat32 &&
+                part_o.numel() >= (int64_t)B * num_splits * H * kD, "part_o too small for the split partials");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(part_o.data_ptr()) % 16 == 0, "part_o must be 16-byte aligned");
+    TORCH_CHECK(part_ml.is_cuda() && part_ml.scalar_type() == torch::kFloat32 &&
+                part_ml.numel() >= (int64_t)B * num_splits * H * 2, "part_ml too small for the split partials");
+  }
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)B * H * kD);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out must be 16-byte aligned (bulk-copied rows)");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.numel() == (int64_t)B * H);
+  DecodeParams p{};
+  if (csa_glm == 1) {
+    TORCH_CHECK(pool.scalar_type() == torch::kUInt8, "pool must be uint8");
+    check_glm_rows(pool, kD, "pool must be [rows, 512] contiguous, 16-byte aligned");
+    p.csa_pool = pool.data_ptr<uint8_t>();
+    p.csa_pool_rows = pool.size(0);
+  } else {
+    TORCH_CHECK(values.scalar_type() == torch::kUInt8, "values must be uint8");
+    check_glm_rows(values, 256, "values must be [rows, 256] contiguous, 16-byte aligned");
+    TORCH_CHECK(bitmap.scalar_type() == torch::kInt64 && bitmap.size(0) == values.size(0), "bitmap must be int64 [rows, 8]");
+    check_glm_rows(bitmap, 8, "bitmap must be [rows, 8] contiguous, 16-byte aligned");
+    p.csa_values = values.data_ptr<uint8_t>();
+    p.csa_bitmap = reinterpret_cast<const uint64_t*>(bitmap.data_ptr<int64_t>());
+    p.csa_pool_rows = values.size(0);
+  }
+  if (B == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.q_stride_b = q.stride(0);
+  p.q_stride_h = q.stride(1);
+  p.B = B;
+  p.H = H;
+  p.num_groups = (H + kHG - 1) / kHG;
+  p.num_splits = (int)num_splits;
+  // no SWA rows: swa_cap 0 (the length and slot pointers are never read)
+  p.swa_slots = slots.data_ptr<int32_t>();
+  p.swa_len = lens.data_ptr<int32_t>();
+  p.csa_glm = (int)csa_glm;
+  p.no_rope = 1;
+  p.csa_slots = slots.data_ptr<int32_t>();
+  p.csa_pos = slots.data_ptr<int32_t>();  // not read (no Packed FP8 rows)
+  p.csa_cap = slots.size(1);
+  p.csa_len = lens.data_ptr<int32_t>();
+  p.scale_log2 = (float)scale * 1.4426950408889634f;
+  p.part_o = decode_uses_partials((int)num_splits) ? part_o.data_ptr<float>() : nullptr;
+  p.part_ml = decode_uses_partials((int)num_splits) ? part_ml.data_ptr<float>() : nullptr;
+  p.err = err.data_ptr<int>();
+  launch_sparse_mla_decode(p, nullptr, nullptr, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(),
+                           stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 torch::Tensor umma_probe(torch::Tensor a, torch::Tensor b, int64_t mode, torch::Tensor err) {
   const auto want = mode == 3 ? torch::kUInt8 : torch::kBFloat16;
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == want && a.is_contiguous());
@@ -750,6 +866,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("csa_len"), py::arg("freqs"), py::arg("sink"), py::arg("scale"), py::arg("q_pos"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_ml"), py::arg("out"), py::arg("lse"), py::arg("err"),
         py::arg("prof") = py::none(), py::arg("csa_fp4") = 0);
+  m.def("glm_store", &glm_store, "GLM-5.3 MLA rows (Native 512 B raw E4M3, or Packed 256 survivors + bitmap)");
+  m.def("glm_packed_to_native", &glm_packed_to_native, "GLM-5.3 Adapter: Packed rows -> Native rows");
+  m.def("glm_sparse_decode", &glm_sparse_decode, "Sparse MLA decode over GLM-5.3 Native or Packed rows (tcgen05)");
   m.def("packed_to_native", &packed_to_native, "Adapter: Packed planes rows -> Native records (paged workspace)");
   m.def("segment_copy", &segment_copy, "batched 16-byte-aligned copies between device and mapped host memory");
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle of a symmetric buffer");

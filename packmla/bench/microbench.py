@@ -6,6 +6,7 @@
     python -m packmla.bench.microbench decode-paired [--batch 16] [--context 32768] [--with-adapter]
     python -m packmla.bench.microbench decode-suite [--paired] > suite.jsonl
     python -m packmla.bench.microbench judge --results suite.jsonl [--paired] [--rounds 30]
+    python -m packmla.bench.microbench glm-suite [--rounds 30] [--glm-batches 1,8,16,24,32,64]
 
 Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
 measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
@@ -356,6 +357,88 @@ def bench_decode_paired(args, dev, modes=("native", "direct")) -> dict:
             "swa": args.swa, "context": args.context, "modes": meta, **res, "clocks": clk.summary()}
 
 
+GLM_SUITE_BATCHES, GLM_SUITE_TAILS, GLM_SUITE_CACHES = (1, 8, 16, 24, 32, 64), (0, 3), ("warm", "rotating")
+
+
+def bench_glm(args, dev) -> list[dict]:
+    """GLM-5.3 decode, Native (512 B rows) vs Direct (320 B Packed rows): the reference's upstream-decode
+    protocol shape (benchmarks/microbench/glm53-flash-packed/README.md:1-40): 16 local heads (TP4), one
+    query per sequence selecting top-k 2048 rows plus 0 or 3 tail rows of a 131076-token context, batches
+    1 .. 64; "warm" reuses one input bank (L2-resident), "rotating" flushes L2 before every sample.  Both
+    modes are CUDA graphs timed in paired rounds; one JSON row per case."""
+    from packmla.formats import glm
+    from packmla.ops import check_errors
+    from packmla.ops.attention import DecodeWorkspace, choose_splits
+    from packmla.ops.glm import GLMPlanes, glm_sparse_decode, glm_store
+
+    from .timing import ClockSampler
+
+    ctx, H = args.context, args.heads
+    g = torch.Generator(device=dev).manual_seed(20261024)
+    pool = torch.empty(ctx, 512, dtype=torch.uint8, device=dev)
+    planes = GLMPlanes(torch.empty(ctx, 256, dtype=torch.uint8, device=dev),
+                       torch.empty(ctx, 8, dtype=torch.int64, device=dev))
+    w = torch.rand(512, device=dev, generator=g) + 0.5
+    for s0 in range(0, ctx, 1 << 16):
+        n = min(1 << 16, ctx - s0)
+        raw = torch.randn(n, 512, device=dev, generator=g)
+        slots = torch.arange(s0, s0 + n, device=dev)
+        glm_store(raw, w, 1e-6, slots, pool=pool)
+        glm_store(raw, w, 1e-6, slots, planes=planes)
+    check_errors(dev)
+    flush = L2Flush(dev)
+    rows_out = []
+    for batch in args.glm_batches:
+        for tails in GLM_SUITE_TAILS:
+            K = glm.GLM53.index_topk + tails
+            q = torch.randn(batch, H, 512, device=dev, generator=g).bfloat16()
+            sel = torch.stack([torch.randperm(ctx - tails, device=dev, generator=g)[:glm.GLM53.index_topk]
+                               for _ in range(batch)]).int()
+            if tails:
+                tail = torch.arange(ctx - tails, ctx, device=dev, dtype=torch.int32).expand(batch, tails)
+                sel = torch.cat((sel, tail), 1)
+            sel = sel.contiguous()
+            lens = torch.full((batch,), K, dtype=torch.int32, device=dev)
+            ws = DecodeWorkspace(batch, H, choose_splits(batch, H, K), dev)
+            graphs = {}
+            for mode, kw in (("native", {"pool": pool}), ("direct", {"planes": planes})):
+                out = torch.empty(batch, H, 512, dtype=torch.bfloat16, device=dev)
+                lse = torch.empty(batch, H, dtype=torch.float32, device=dev)
+                fn = (lambda kw=kw, out=out, lse=lse:
+                      glm_sparse_decode(q, sel, lens, workspace=ws, out=out, lse=lse, **kw))
+                for _ in range(args.warmup):
+                    fn()
+                torch.cuda.synchronize(dev)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    fn()
+                graphs[mode] = gr
+            check_errors(dev)
+            for cache in GLM_SUITE_CACHES:
+                def timer(gr, cold=cache == "rotating"):
+                    def run() -> float:
+                        if cold:
+                            flush()
+                        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        s.record()
+                        gr.replay()
+                        e.record()
+                        torch.cuda.synchronize(dev)
+                        return s.elapsed_time(e) * 1e3
+                    return run
+
+                with ClockSampler(torch.device(dev).index or 0) as clk:
+                    res = paired_rounds({m: timer(gr) for m, gr in graphs.items()}, args.rounds)
+                row = {"case": f"glm_decode_h{H}_q1_t{tails}_b{batch}_{cache}", "batch": batch, "heads": H,
+                       "rows_per_query": K, "context": ctx, "splits": ws.splits, **res, "clocks": clk.summary()}
+                print(json.dumps(row), flush=True)
+                rows_out.append(row)
+            for gr in graphs.values():
+                gr.reset()
+    check_errors(dev)
+    return rows_out
+
+
 SUITE_CONTEXTS, SUITE_BATCHES, SUITE_FORMATS = (32768, 131072), (1, 16, 64), ("native", "direct")
 FP4_SUITE_BATCHES = (8, 16, 24, 28, 32)
 BAD_CLOCK_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown")
@@ -501,7 +584,7 @@ def bench_dense(args, dev):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["moe", "decode", "store", "index", "dense", "decode-suite", "decode-paired",
-                                     "fp4-suite", "judge"],
+                                     "fp4-suite", "glm-suite", "judge"],
                     help="decode-suite: native vs direct at batch 1/16/64, 128 heads, 32k and 128k contexts, "
                          "top-k 2048 (one JSON line per case)")
     ap.add_argument("--tokens", type=int, default=40)
@@ -526,6 +609,8 @@ def main(argv=None):
                          "microbenchmark does")
     ap.add_argument("--with-adapter", action="store_true", help="decode-paired: add the adapter mode")
     ap.add_argument("--results", default=None, help="judge: the JSON lines of a decode-suite run")
+    ap.add_argument("--glm-batches", default=",".join(map(str, GLM_SUITE_BATCHES)),
+                    help="glm-suite: comma-separated batches")
     args = ap.parse_args(argv)
     if args.case == "judge":
         with open(args.results) as f:
@@ -561,6 +646,12 @@ def main(argv=None):
                 row["clocks"] = dict(LAST_CLOCKS)
                 print(json.dumps(row), flush=True)
                 torch.cuda.empty_cache()
+        return
+    elif args.case == "glm-suite":
+        args.heads = 16 if args.heads == 128 else args.heads
+        args.context = 131076 if args.context == 32768 else args.context
+        args.glm_batches = [int(x) for x in str(args.glm_batches).split(",") if x]
+        bench_glm(args, dev)
         return
     elif args.case == "decode-suite":
         args.topk = args.topk or 2048
