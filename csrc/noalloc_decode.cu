@@ -103,6 +103,21 @@ int packmla_sparse_mla_decode_noalloc(const PackmlaNoallocDecodeArgs* a, cudaStr
         reinterpret_cast<uintptr_t>(a->csa_values) | reinterpret_cast<uintptr_t>(a->csa_bitmap) |
         reinterpret_cast<uintptr_t>(a->freqs) | reinterpret_cast<uintptr_t>(a->out)) & 15) != 0)
     return fail("pools, planes, freqs and out must be 16-byte aligned");
+  if (decode_splits_clustered(a->num_splits)) {
+    // every (query, head group) cluster must be co-resident, as in every validated launch
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= PACKMLA_NOALLOC_MAX_DEVICES)
+      return fail("no current CUDA device");
+    static int fit_cache[PACKMLA_NOALLOC_MAX_DEVICES][9] = {};
+    int fit;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (fit_cache[dev][a->num_splits] == 0) fit_cache[dev][a->num_splits] = decode_max_active_clusters(a->num_splits);
+      fit = fit_cache[dev][a->num_splits];
+    }
+    if ((int64_t)a->B * ((a->H + kHG - 1) / kHG) > fit)
+      return fail("more split clusters than are co-resident on this device: use fewer splits");
+  }
   float* part_o = nullptr;
   float* part_ml = nullptr;
   if (scratch_for_current_device(&part_o, &part_ml) != 0) return 1;

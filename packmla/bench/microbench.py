@@ -6,7 +6,7 @@
     python -m packmla.bench.microbench decode-paired [--batch 16] [--context 32768] [--with-adapter]
     python -m packmla.bench.microbench decode-suite [--paired] > suite.jsonl
     python -m packmla.bench.microbench judge --results suite.jsonl [--paired] [--rounds 30]
-    python -m packmla.bench.microbench glm-suite [--rounds 30] [--glm-batches 1,8,16,24,32,64]
+    python -m packmla.bench.microbench glm-suite [--rounds 30] [--glm-batches 1,8,16,24]
 
 Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
 measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
@@ -357,19 +357,24 @@ def bench_decode_paired(args, dev, modes=("native", "direct")) -> dict:
             "swa": args.swa, "context": args.context, "modes": meta, **res, "clocks": clk.summary()}
 
 
-GLM_SUITE_BATCHES, GLM_SUITE_TAILS, GLM_SUITE_CACHES = (1, 8, 16, 24, 32, 64), (0, 3), ("warm", "rotating")
+# the reference's table also has batches 32 and 64; the device GLM decode is limited to batch 24
+# (packmla.ops.glm.MAX_DEVICE_BATCH)
+GLM_SUITE_BATCHES, GLM_SUITE_TAILS, GLM_SUITE_CACHES = (1, 8, 16, 24), (0, 3), ("warm", "rotating")
 
 
 def bench_glm(args, dev) -> list[dict]:
     """GLM-5.3 decode, Native (512 B rows) vs Direct (320 B Packed rows): the reference's upstream-decode
     protocol shape (benchmarks/microbench/glm53-flash-packed/README.md:1-40): 16 local heads (TP4), one
     query per sequence selecting top-k 2048 rows plus 0 or 3 tail rows of a 131076-token context, batches
-    1 .. 64; "warm" reuses one input bank (L2-resident), "rotating" flushes L2 before every sample.  Both
+    1 .. 24 (the reference's 32 and 64 exceed the device limit of `packmla.ops.glm`); "warm" reuses one input bank (L2-resident), "rotating" flushes L2 before every sample.  Both
     modes are CUDA graphs timed in paired rounds; one JSON row per case."""
     from packmla.formats import glm
     from packmla.ops import check_errors
-    from packmla.ops.attention import DecodeWorkspace, choose_splits
-    from packmla.ops.glm import GLMPlanes, glm_sparse_decode, glm_store
+    from packmla.ops.attention import DecodeWorkspace, choose_splits, max_active_clusters
+    from packmla.ops.glm import MAX_DEVICE_BATCH, GLMPlanes, glm_sparse_decode, glm_store
+
+    if max(args.glm_batches) > MAX_DEVICE_BATCH:
+        raise SystemExit(f"glm-suite: batches above {MAX_DEVICE_BATCH} stay off the device")
 
     from .timing import ClockSampler
 
@@ -399,7 +404,7 @@ def bench_glm(args, dev) -> list[dict]:
                 sel = torch.cat((sel, tail), 1)
             sel = sel.contiguous()
             lens = torch.full((batch,), K, dtype=torch.int32, device=dev)
-            ws = DecodeWorkspace(batch, H, choose_splits(batch, H, K), dev)
+            ws = DecodeWorkspace(batch, H, choose_splits(batch, H, K, max_clusters=max_active_clusters(dev)), dev)
             graphs = {}
             for mode, kw in (("native", {"pool": pool}), ("direct", {"planes": planes})):
                 out = torch.empty(batch, H, 512, dtype=torch.bfloat16, device=dev)
@@ -428,7 +433,12 @@ def bench_glm(args, dev) -> list[dict]:
                     return run
 
                 with ClockSampler(torch.device(dev).index or 0) as clk:
+                    t_end = time.perf_counter() + 0.8
                     res = paired_rounds({m: timer(gr) for m, gr in graphs.items()}, args.rounds)
+                    while time.perf_counter() < t_end:  # untimed replays until the sampler has seen the work
+                        for gr in graphs.values():
+                            gr.replay()
+                        torch.cuda.synchronize(dev)
                 row = {"case": f"glm_decode_h{H}_q1_t{tails}_b{batch}_{cache}", "batch": batch, "heads": H,
                        "rows_per_query": K, "context": ctx, "splits": ws.splits, **res, "clocks": clk.summary()}
                 print(json.dumps(row), flush=True)

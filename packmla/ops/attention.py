@@ -70,6 +70,17 @@ def choose_tiling(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_
     return sizes[-1], TILE_ROWS
 
 
+def check_cluster_fit(batch: int, heads: int, splits: int, device) -> None:
+    """A split count of 2, 4 or 8 launches one thread-block cluster per (query, head group); every launch
+    the kernel has been validated with keeps all of them co-resident, so a count whose clusters would not
+    all fit at once is refused (`choose_tiling` never picks one)."""
+    if splits in CLUSTER_SPLITS:
+        work = batch * ((heads + HEAD_GROUP - 1) // HEAD_GROUP)
+        fit = max_active_clusters(device).get(splits, 0)
+        if work > fit:
+            raise ValueError(f"{work} clusters of {splits} CTAs exceed the {fit} co-resident on this device")
+
+
 def choose_splits(batch: int, heads: int, max_rows: int, num_sms: int = NUM_SMS_B200,
                   max_clusters: dict[int, int] | None = None) -> int:
     return choose_tiling(batch, heads, max_rows, num_sms, max_clusters)[0]
@@ -132,6 +143,7 @@ def sparse_mla_decode(
         else:
             num_splits = choose_splits(B, H, swa_slots.shape[1] + csa_slots.shape[1],
                                        max_clusters=max_active_clusters(q.device))
+    check_cluster_fit(B, H, num_splits, q.device)
     if workspace is None or workspace.splits != num_splits:
         workspace = DecodeWorkspace(B, H, num_splits, q.device)
     if out is None:

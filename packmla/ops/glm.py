@@ -20,6 +20,13 @@ from ..formats import glm
 from ._ext import error_word, ext
 
 
+# Batches above this stay off the device: the GLM decode suite's first batch-32 case raised an illegal address
+# on its first CUDA-graph replay (the same graph's eager launches had passed).  That launch used 32 clusters
+# of 4 CTAs chosen without the device's co-resident cluster count (which `check_cluster_fit` now enforces);
+# reading the code has not yet shown the mechanism.
+MAX_DEVICE_BATCH = 24
+
+
 @dataclass
 class GLMPlanes:
     values: torch.Tensor  # uint8 [rows, 256]
@@ -74,12 +81,15 @@ def glm_sparse_decode(q: torch.Tensor, slots: torch.Tensor, lens: torch.Tensor, 
                       lse: torch.Tensor | None = None):
     """q bf16 [B, H, 512] (absorbed queries) over the rows `slots` int32 [B, K] (first `lens[b]` used,
     -1 masked) of a Native pool or Packed planes -> (out bf16 [B, H, 512], lse fp32 [B, H])."""
-    from .attention import DecodeWorkspace, choose_splits, max_active_clusters
+    from .attention import DecodeWorkspace, check_cluster_fit, choose_splits, max_active_clusters
 
     if (pool is None) == (planes is None):
         raise ValueError("give exactly one of pool (native) or planes (packed)")
     scale = glm.GLM53.softmax_scale if scale is None else scale
     B, H, _ = q.shape
+    if q.is_cuda and B > MAX_DEVICE_BATCH:
+        raise ValueError(f"GLM decode on the device is limited to batch {MAX_DEVICE_BATCH}: a batch-32 case raised "
+                         "an illegal address under CUDA-graph replay and stays off the GPU until its cause is found")
     if not q.is_cuda:
         rows = []
         for b in range(B):
@@ -91,6 +101,7 @@ def glm_sparse_decode(q: torch.Tensor, slots: torch.Tensor, lens: torch.Tensor, 
     if num_splits is None:
         num_splits = workspace.splits if workspace is not None else choose_splits(
             B, H, slots.shape[1], max_clusters=max_active_clusters(q.device))
+    check_cluster_fit(B, H, num_splits, q.device)
     if workspace is None or workspace.splits != num_splits:
         workspace = DecodeWorkspace(B, H, num_splits, q.device)
     if out is None:

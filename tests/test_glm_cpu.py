@@ -86,3 +86,10 @@ def test_bad_arguments():
         glm_store(raw, w, 1e-6, torch.arange(2))
     with pytest.raises(ValueError):
         glm.packed_encode(raw, w, 1e-6, mask=torch.ones(2, 512, dtype=torch.bool))
+
+
+def test_device_batch_limit_is_enforced_before_any_launch():
+    from packmla.bench import microbench
+    from packmla.ops import glm as glm_ops
+
+    assert glm_ops.MAX_DEVICE_BATCH == 24 and max(microbench.GLM_SUITE_BATCHES) <= glm_ops.MAX_DEVICE_BATCH
