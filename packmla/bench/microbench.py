@@ -6,7 +6,7 @@
     python -m packmla.bench.microbench decode-paired [--batch 16] [--context 32768] [--with-adapter]
     python -m packmla.bench.microbench decode-suite [--paired] > suite.jsonl
     python -m packmla.bench.microbench judge --results suite.jsonl [--paired] [--rounds 30]
-    python -m packmla.bench.microbench glm-suite [--rounds 30] [--glm-batches 1,8,16,24]
+    python -m packmla.bench.microbench glm-suite [--rounds 30] [--glm-batches 1,8,16,24] [--out F [--resume]]
 
 Each case prints one JSON line: mean microseconds, achieved bytes/s and the fraction of the
 measured HBM copy bandwidth (MEASURED_PEAKS.json, "of measured").
@@ -379,6 +379,12 @@ def bench_glm(args, dev) -> list[dict]:
     from .timing import ClockSampler
 
     ctx, H = args.context, args.heads
+    rec = None
+    if getattr(args, "out", None):
+        from .suite_record import SuiteRecord
+
+        rec = SuiteRecord(args.out, {"suite": "glm", "seed": 20261024, "context": ctx, "heads": H,
+                                     "rounds": args.rounds, "warmup": args.warmup}, resume=args.resume)
     g = torch.Generator(device=dev).manual_seed(20261024)
     pool = torch.empty(ctx, 512, dtype=torch.uint8, device=dev)
     planes = GLMPlanes(torch.empty(ctx, 256, dtype=torch.uint8, device=dev),
@@ -395,6 +401,9 @@ def bench_glm(args, dev) -> list[dict]:
     rows_out = []
     for batch in args.glm_batches:
         for tails in GLM_SUITE_TAILS:
+            names = {c: f"glm_decode_h{H}_q1_t{tails}_b{batch}_{c}" for c in GLM_SUITE_CACHES}
+            if rec is not None and all(n in rec.done for n in names.values()):
+                continue  # measured by the run being resumed
             K = glm.GLM53.index_topk + tails
             q = torch.randn(batch, H, 512, device=dev, generator=g).bfloat16()
             sel = torch.stack([torch.randperm(ctx - tails, device=dev, generator=g)[:glm.GLM53.index_topk]
@@ -420,6 +429,9 @@ def bench_glm(args, dev) -> list[dict]:
                 graphs[mode] = gr
             check_errors(dev)
             for cache in GLM_SUITE_CACHES:
+                if rec is not None and names[cache] in rec.done:
+                    continue
+
                 def timer(gr, cold=cache == "rotating"):
                     def run() -> float:
                         if cold:
@@ -439,9 +451,11 @@ def bench_glm(args, dev) -> list[dict]:
                         for gr in graphs.values():
                             gr.replay()
                         torch.cuda.synchronize(dev)
-                row = {"case": f"glm_decode_h{H}_q1_t{tails}_b{batch}_{cache}", "batch": batch, "heads": H,
+                row = {"case": names[cache], "batch": batch, "heads": H,
                        "rows_per_query": K, "context": ctx, "splits": ws.splits, **res, "clocks": clk.summary()}
                 print(json.dumps(row), flush=True)
+                if rec is not None:
+                    rec.write(row)
                 rows_out.append(row)
             for gr in graphs.values():
                 gr.reset()
@@ -619,6 +633,10 @@ def main(argv=None):
                          "microbenchmark does")
     ap.add_argument("--with-adapter", action="store_true", help="decode-paired: add the adapter mode")
     ap.add_argument("--results", default=None, help="judge: the JSON lines of a decode-suite run")
+    ap.add_argument("--out", default=None, help="glm-suite: append the rows to this JSON-lines file (with a "
+                                                 "manifest of the sources, library and fixture)")
+    ap.add_argument("--resume", action="store_true", help="glm-suite: continue --out, skipping recorded cases; "
+                                                          "the manifest must match the current identity")
     ap.add_argument("--glm-batches", default=",".join(map(str, GLM_SUITE_BATCHES)),
                     help="glm-suite: comma-separated batches")
     args = ap.parse_args(argv)

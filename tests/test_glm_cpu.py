@@ -1,4 +1,6 @@
 """CPU: GLM-5.3 MLA rows (Native 512 B, Packed 320 B), the Adapter and the decode oracle path."""
+import json
+
 import pytest
 import torch
 
@@ -93,3 +95,29 @@ def test_device_batch_limit_is_enforced_before_any_launch():
     from packmla.ops import glm as glm_ops
 
     assert glm_ops.MAX_DEVICE_BATCH == 24 and max(microbench.GLM_SUITE_BATCHES) <= glm_ops.MAX_DEVICE_BATCH
+
+
+def test_suite_record_resumes_only_with_a_matching_manifest(tmp_path):
+    from packmla.bench.suite_record import SuiteRecord
+
+    ident = {"csrc_sha256": "a", "library_sha256": "b", "library_built_from": "a"}
+    fix = {"suite": "glm", "seed": 1, "rounds": 30}
+    out = tmp_path / "glm.jsonl"
+    rec = SuiteRecord(out, fix, identity=ident)
+    rec.write({"case": "c1", "us": 1.0})
+    with pytest.raises(ValueError):
+        rec.write({"case": "c1", "us": 2.0})
+    with pytest.raises(ValueError, match="exists"):
+        SuiteRecord(out, fix, identity=ident)
+    with open(out, "a") as f:
+        f.write('{"case": "c2", "us"')  # an interrupted write
+    again = SuiteRecord(out, fix, resume=True, identity=ident)
+    assert again.done == {"c1"}
+    again.write({"case": "c2", "us": 3.0})
+    assert [json.loads(x)["case"] for x in out.read_text().splitlines()] == ["c1", "c2"]
+    with pytest.raises(ValueError, match="library_sha256"):
+        SuiteRecord(out, fix, resume=True, identity={**ident, "library_sha256": "other"})
+    with pytest.raises(ValueError, match="rounds"):
+        SuiteRecord(out, {**fix, "rounds": 10}, resume=True, identity=ident)
+    with pytest.raises(ValueError, match="nothing to resume"):
+        SuiteRecord(tmp_path / "none.jsonl", fix, resume=True, identity=ident)
