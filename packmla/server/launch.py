@@ -5,7 +5,8 @@ run-server.sh (settings as named environment values, scripts/local/launch-config
     MODEL=tiny DEVICE=cpu python -m packmla.server.launch native --smoke     # start, wait, read out, stop
     TP=8 python -m packmla.server.launch direct --dry-run                   # print the command only
 
-Environment (all optional): MODE (native | direct; the positional mode wins), MODEL (default v4-flash),
+Environment (all optional): MODE (native | direct; the positional mode wins), MODEL_FAMILY (dsv4 | dsv41 |
+glm53; dsv41 serves the V4.1 FP4 cache formats), MODEL (default v4-flash),
 DEVICE (cuda | cpu), TP, EP, PORT (30000), MASTER_PORT (29500), MEM_FRAC, CTX_LEN, MAX_RUN, CHUNK,
 DECODE_CFG (the --cuda-graph-config JSON), SERVER_SEED, HICACHE_RATIO (turns HiCache on),
 C4_KEEP_COUNT, C4_LAYER_KEEP_COUNTS, STORE_IMPLEMENTATION, REQUEST_METRICS_DIR (request log and
@@ -38,16 +39,57 @@ ENV_FLAGS = (  # environment name -> server flag
 )
 
 
+FAMILIES = ("dsv4", "dsv41", "glm53")
+CODEC_OVERRIDES = ("HICACHE_RATIO", "C4_KEEP_COUNT", "C4_LAYER_KEEP_COUNTS", "STORE_IMPLEMENTATION")
+
+
+def _family_checks(family: str, env: dict) -> tuple[int, int | None]:
+    """(TP, EP) of a V4.1 or GLM-5.3 launch, validated as the reference's launch configuration does
+    (scripts/local/launch-config.sh:10-38, run-server.sh:82-97): TP 1, 2, 4 or 8; EP (default TP) a
+    divisor of TP; no HiCache or C4 codec overrides; an explicit GPU list names exactly TP devices."""
+    label = "V4.1" if family == "dsv41" else "GLM"
+    tp = int(env.get("TP", "4" if family == "dsv41" else "8"))
+    if tp not in (1, 2, 4, 8):
+        raise SystemExit(f"{label} requires TP1/2/4/8")
+    ep = int(env.get("EP", str(tp)))
+    if ep < 1 or ep > tp or tp % ep:
+        raise SystemExit(f"{label} EP must be a positive divisor of TP (TP={tp} EP={ep})")
+    if any(env.get(k) for k in CODEC_OVERRIDES):
+        raise SystemExit("V4.1 does not support HiCache or C4 codec overrides" if family == "dsv41"
+                         else "GLM Packed does not support HiCache or DeepSeek codec overrides")
+    gpus = env.get("GPUS") or env.get("CUDA_VISIBLE_DEVICES")
+    if gpus:
+        devices = gpus.split(",")
+        if len(devices) != tp or any(not d.strip() for d in devices):
+            raise SystemExit(f"{label} needs TP={tp} visible GPUs; got GPUS={gpus}")
+    return tp, ep
+
+
 def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
-    """(command, extra environment) of the server launch described by `env`."""
+    """(command, extra environment) of the server launch described by `env`.  MODEL_FAMILY selects dsv4
+    (default), dsv41 (the V4.1 FP4 cache: native -> fp4-native, direct -> fp4-direct, EP ranks) or glm53."""
     mode = mode or env.get("MODE", "direct")
     if mode not in ("native", "direct"):
         raise SystemExit(f"mode must be native or direct, not {mode!r}")
+    family = env.get("MODEL_FAMILY", "dsv4")
+    if family not in FAMILIES:
+        raise SystemExit("MODEL_FAMILY must be dsv4, dsv41 or glm53")
+    fmt = mode
+    if family != "dsv4":
+        tp, ep = _family_checks(family, env)
+        if family == "glm53":
+            raise SystemExit("GLM-5.3 serving is not built: packmla provides the GLM MLA row formats, stores, "
+                             "Adapter and decode (packmla.ops.glm, packmla.kv.glm_pool), not the GLM model "
+                             "(KDA layers, hyper-connections)")
+        if ep != tp:
+            raise SystemExit(f"EP={ep}: packmla shards the routed experts over the TP ranks (EP = TP = {tp})")
+        env = {**env, "TP": str(tp), "EP": str(ep)}
+        fmt = "fp4-" + mode
     tp = int(env.get("TP", "1"))
     if tp < 1:
         raise SystemExit("TP must be >= 1")
     port = env.get("PORT", "30000")
-    flags = ["--model", env.get("MODEL", "v4-flash"), "--kv-cache-format", mode, "--port", port,
+    flags = ["--model", env.get("MODEL", "v4-flash"), "--kv-cache-format", fmt, "--port", port,
              "--device", env.get("DEVICE", "cuda")]
     for name, flag in ENV_FLAGS:
         if env.get(name):

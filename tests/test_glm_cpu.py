@@ -121,3 +121,36 @@ def test_suite_record_resumes_only_with_a_matching_manifest(tmp_path):
         SuiteRecord(out, {**fix, "rounds": 10}, resume=True, identity=ident)
     with pytest.raises(ValueError, match="nothing to resume"):
         SuiteRecord(tmp_path / "none.jsonl", fix, resume=True, identity=ident)
+
+
+def test_glm_pool_lifecycle_capacity_and_decode_on_cpu():
+    from packmla.kv.glm_pool import GLMCacheConfig, GLMKVPool, bytes_per_token, capacity_tokens
+
+    for bad in (GLMCacheConfig(kv_cache_format="fp4"), GLMCacheConfig(kv_cache_dtype="bf16"),
+                GLMCacheConfig(model_dtype="float16"), GLMCacheConfig(kv_cache_format="direct",
+                                                                      enable_hierarchical_cache=True),
+                GLMCacheConfig(keep_count=128)):
+        with pytest.raises(ValueError):
+            GLMKVPool(bad, 4, 2, 256, "cpu")
+    native, direct = GLMCacheConfig(), GLMCacheConfig(kv_cache_format="direct")
+    assert bytes_per_token(native) == 11 * 644 and bytes_per_token(direct) == 11 * 452
+    budget = 64 << 30
+    assert capacity_tokens(direct, budget) / capacity_tokens(native, budget) > 1.42
+    raw, w = _rows(100, 9)
+    g = torch.Generator().manual_seed(10)
+    q = torch.randn(1, 16, 512, generator=g).bfloat16()
+    outs = {}
+    for cfg in (native, direct):
+        pool = GLMKVPool(cfg, num_pages=6, max_requests=2, max_context=256, device="cpu")
+        slot = pool.admit(100)
+        assert pool.pages.free == 4
+        pos = torch.arange(100)
+        for layer in (3, 43):
+            pool.store(layer, raw, w, 1e-6, slot, pos)
+        rows = pool.rows_of(slot, pos).int()[None]
+        assert int(pool.rows_of(slot, torch.tensor([200]))[0]) == -1  # past the request's pages
+        outs[cfg.kv_cache_format] = pool.decode(43, q, rows, torch.tensor([100], dtype=torch.int32))
+        pool.release(slot)
+        assert pool.pages.free == 6
+    # Direct keeps half the coordinates: close to, not equal to, Native
+    assert float((outs["native"][0].float() - outs["direct"][0].float()).abs().max()) < 0.5

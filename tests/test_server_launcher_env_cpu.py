@@ -107,3 +107,26 @@ def test_capacity_stress_compares_reuse_tiers(monkeypatch, tmp_path):
     # reuse means less prefill work for the same conversation
     assert r["prefix"]["prefill_tokens"] < r["none"]["prefill_tokens"]
     assert r["hicache"]["prefill_tokens"] < r["none"]["prefill_tokens"]
+
+
+def test_model_families_are_validated_like_the_reference_launcher():
+    import pytest
+
+    from packmla.server.launch import resolve
+
+    cmd, _ = resolve("direct", {"MODEL_FAMILY": "dsv41", "TP": "4"})
+    assert cmd[cmd.index("--kv-cache-format") + 1] == "fp4-direct" and cmd[cmd.index("--ep") + 1] == "4"
+    cmd, _ = resolve("native", {"MODEL_FAMILY": "dsv41", "TP": "2", "GPUS": "0,1"})
+    assert cmd[cmd.index("--kv-cache-format") + 1] == "fp4-native" and cmd[cmd.index("--tp") + 1] == "2"
+    for env, msg in (({"MODEL_FAMILY": "dsv41", "TP": "3"}, "TP1/2/4/8"),
+                     ({"MODEL_FAMILY": "dsv41", "TP": "4", "EP": "3"}, "divisor"),
+                     ({"MODEL_FAMILY": "dsv41", "TP": "2", "EP": "1"}, "EP = TP"),
+                     ({"MODEL_FAMILY": "dsv41", "HICACHE_RATIO": "2"}, "HiCache"),
+                     ({"MODEL_FAMILY": "dsv41", "TP": "2", "GPUS": "0,"}, "visible GPUs"),
+                     ({"MODEL_FAMILY": "glm53", "C4_KEEP_COUNT": "128"}, "GLM Packed"),
+                     ({"MODEL_FAMILY": "glm53"}, "not built"),
+                     ({"MODEL_FAMILY": "glm99"}, "MODEL_FAMILY")):
+        with pytest.raises(SystemExit, match=msg):
+            resolve("direct", env)
+    cmd, _ = resolve("direct", {})
+    assert cmd[cmd.index("--kv-cache-format") + 1] == "direct"
