@@ -1,0 +1,134 @@
+"""Executable model of a fused expert-parallel exchange over symmetric peer buffers (dispatch, local
+experts, combine), for checking its buffer reuse and progress on the host before a kernel implements it.
+
+Reference behaviour: DeepEP dispatch / combine under `--ep` (scripts/local/run-server.sh:89-100): each
+(token, expert) pair goes to the expert's owner and comes back weighted.  `packmla.parallel.ep.EPMoE`
+does it with two NCCL all-to-alls; the fused form replaces them with stores into peers' buffers:
+
+* every rank r owns, in its symmetric memory, one receive region per source s (`rows[r][s][i]`, capacity
+  T k pairs, so a sender needs no offsets from other senders) and one return region per destination d
+  (`back[r][d][i]`);
+* dispatch (rank s, call c): pair j of s's routing, owned by d, is the i-th pair s sends to d; s stores
+  the row into rows[d][s][i], then its count and `flag_rows[d][s] = c` (release);
+* each owner d acquires `flag_rows[d][s] >= c` for every s, runs its experts on the received rows and
+  stores output i into back[s][d][i], then releases `flag_back[s][d] = c`;
+* source s acquires `flag_back[s][d] >= c` for every d and sums its pairs in routing order.
+
+One buffer per region suffices: s writes call c + 1 rows into d's region only after it has received all
+of d's call-c outputs, and d sends those only after it has read s's call-c rows.  The same argument covers
+the return regions.  `wait_all_back=False` lets a source start the next dispatch after one owner's return
+(a bug the checker must catch as a stale read).  Memory is modelled sequentially consistent at step
+granularity, with flags compared `>= c`, as in `packmla.parallel.protocol`.
+"""
+from __future__ import annotations
+
+import random
+
+from .protocol import ProtocolError
+
+
+class EPExchangeModel:
+    def __init__(self, world: int, tokens: int, topk: int, experts: int, calls: int, seed: int = 0,
+                 wait_all_back: bool = True):
+        if experts % world:
+            raise ValueError("experts must divide evenly over the ranks")
+        rng = random.Random(seed)
+        self.world, self.T, self.k, self.E, self.calls = world, tokens, topk, experts, calls
+        self.local = experts // world
+        self.wait_all_back = wait_all_back
+        # routing[c][r] = list of (token, expert) pairs of rank r in routing order
+        self.routing = [[[(t, rng.randrange(experts)) for t in range(tokens) for _ in range(topk)]
+                         for _ in range(world)] for _ in range(calls)]
+        W = range(world)
+        self.rows = {(d, s): {} for d in W for s in W}     # rows[d][s][i] = tag
+        self.back = {(s, d): {} for s in W for d in W}     # back[s][d][i] = tag
+        self.flag_rows = {(d, s): 0 for d in W for s in W}
+        self.flag_back = {(s, d): 0 for s in W for d in W}
+        self.count = {(d, s): 0 for d in W for s in W}
+        self.results: dict = {}
+        self.progs = [self._program(r) for r in W]
+        self.pcs = [0] * world
+
+    # tags: a dispatched row = ("row", call, src, pair); a returned output = ("out", call, src, pair)
+    def _program(self, r: int) -> list:
+        steps = []
+        for c in range(1, self.calls + 1):
+            pairs = self.routing[c - 1][r]
+            per_dest: dict[int, list[int]] = {}
+            for j, (_, e) in enumerate(pairs):
+                per_dest.setdefault(e // self.local, []).append(j)
+            for d in range(self.world):  # dispatch: rows, then count and flag
+                for i, j in enumerate(per_dest.get(d, [])):
+                    steps.append(("store_row", c, d, i, j))
+                steps.append(("release_rows", c, d, len(per_dest.get(d, []))))
+            for s in range(self.world):  # owner side: wait for every source, compute, return
+                steps.append(("acquire_rows", c, s))
+                steps.append(("compute_return", c, s))
+            waits = range(self.world) if self.wait_all_back else [r]
+            for d in waits:
+                steps.append(("acquire_back", c, d))
+            steps.append(("combine", c, dict(per_dest)))
+        return steps
+
+    def _enabled(self, r: int) -> bool:
+        if self.pcs[r] >= len(self.progs[r]):
+            return False
+        op = self.progs[r][self.pcs[r]]
+        if op[0] == "acquire_rows":
+            return self.flag_rows[(r, op[2])] >= op[1]
+        if op[0] == "acquire_back":
+            return self.flag_back[(r, op[2])] >= op[1]
+        return True
+
+    def _step(self, r: int) -> None:
+        op = self.progs[r][self.pcs[r]]
+        kind, c = op[0], op[1]
+        if kind == "store_row":
+            _, _, d, i, j = op
+            self.rows[(d, r)][i] = ("row", c, r, j)
+        elif kind == "release_rows":
+            _, _, d, n = op
+            self.count[(d, r)] = n
+            self.flag_rows[(d, r)] = c
+        elif kind == "compute_return":
+            s = op[2]
+            n = self.count[(r, s)]
+            for i in range(n):
+                tag = self.rows[(r, s)].get(i)
+                if tag is None or tag[0] != "row" or tag[1] != c or tag[2] != s:
+                    raise ProtocolError(f"rank {r} read {tag} for call {c} row {i} from rank {s}")
+                self.back[(s, r)][i] = ("out", c, s, tag[3])
+            self.flag_back[(s, r)] = c
+        elif kind == "combine":
+            per_dest = op[2]
+            got = {}
+            for d, js in per_dest.items():
+                for i, j in enumerate(js):
+                    tag = self.back[(r, d)].get(i)
+                    if tag != ("out", c, r, j):
+                        raise ProtocolError(f"rank {r} combined {tag} for call {c} pair {j} from rank {d}")
+                    got[j] = tag
+            self.results[(r, c)] = sorted(got)
+        self.pcs[r] += 1
+
+    def run(self, rng: random.Random) -> None:
+        while True:
+            ready = [r for r in range(self.world) if self._enabled(r)]
+            if not ready:
+                if any(self.pcs[r] < len(self.progs[r]) for r in range(self.world)):
+                    raise ProtocolError("deadlock: unfinished ranks and no enabled step")
+                break
+            self._step(rng.choice(ready))
+        for r in range(self.world):
+            for c in range(1, self.calls + 1):
+                if self.results.get((r, c)) != list(range(self.T * self.k)):
+                    raise ProtocolError(f"rank {r} call {c} combined {self.results.get((r, c))}")
+
+
+def explore(world: int, tokens: int, topk: int, experts: int, calls: int, schedules: int, seed: int = 0,
+            wait_all_back: bool = True) -> int:
+    """Run `schedules` random interleavings; returns how many completed (raises on the first race)."""
+    rng = random.Random(seed)
+    for n in range(schedules):
+        EPExchangeModel(world, tokens, topk, experts, calls, seed=seed + n, wait_all_back=wait_all_back).run(rng)
+    return schedules

@@ -30,3 +30,15 @@ def test_model_detects_a_missing_flag_wait():
             for cta in m.active[0]:  # rank 0 reads before acquiring the peer's flag
                 cta.steps = [s for s in cta.steps if s[0] != "acquire_rs"]
             m.run(random.Random(seed))
+
+
+def test_fused_ep_exchange_protocol_has_no_race_and_the_early_dispatch_bug_is_caught():
+    import pytest
+
+    from packmla.parallel.ep_protocol import explore
+    from packmla.parallel.protocol import ProtocolError
+
+    for world in (2, 4, 8):
+        assert explore(world, tokens=3, topk=2, experts=2 * world, calls=3, schedules=60, seed=world) == 60
+    with pytest.raises(ProtocolError):
+        explore(4, tokens=3, topk=2, experts=8, calls=3, schedules=200, seed=1, wait_all_back=False)
