@@ -11,7 +11,7 @@ Non-256 budgets replay through the dense codec simulation, admitted only after t
 each query reproduce the real codec bit for bit.  Statistics: per issue/layer query means, then
 layers and issues equally (mean); pooled query-layer p95 (linear); 10,000 whole-issue bootstrap draws
 (seed 42) for 95 % intervals of the mean and of the paired difference to magnitude at the same budget.
-Outputs: JSON (complete results) + CSV + Markdown summary (+ PNG curves when matplotlib is installed),
+Outputs: JSON (complete results) + CSV + Markdown summary (+ PNG curves of a retention sweep),
 published only to fresh paths, JSON last.
 """
 from __future__ import annotations
@@ -123,7 +123,8 @@ def _fresh(paths: list[Path]) -> None:
 
 
 def _write_reports(output: Path, result: dict, created: list[Path]) -> list[str]:
-    """CSV, Markdown and (retention sweep, with matplotlib) PNG reports; every file is appended to
+    """CSV, Markdown and (retention sweep) PNG reports, drawn by matplotlib when it is installed and by
+    `packmla.utils.png_plot` otherwise; every file is appended to
     `created` as soon as it exists so that a failure can remove the partial report."""
     fields = ("method", "retained_features", "mean", "p95")
     with output.with_suffix(".csv").open("x", newline="") as f:
@@ -147,15 +148,27 @@ def _write_reports(output: Path, result: dict, created: list[Path]) -> list[str]
         f.write("\n".join(lines))
     files = [str(output.with_suffix(".csv")), str(output.with_suffix(".md"))]
     if result.get("retention_sweep"):
+        rows = {r["method"]: r for r in result["summary"]}
         try:
             import matplotlib
 
             matplotlib.use("Agg")
             import matplotlib.pyplot as plt
-        except ImportError:
-            result["figures"] = {"skipped": "matplotlib is not installed"}
+        except ImportError:  # the built-in PNG writer: same curves, legend in the report and the PNG's text
+            from ..utils.png_plot import line_chart
+
+            result["figures"] = {"renderer": "packmla.utils.png_plot"}
+            for metric in ("mean", "p95"):
+                path = output.parent / f"{output.stem}-{metric}.png"
+                created.append(path)
+                info = line_chart(path, list(RETENTION_COUNTS),
+                                  {fam: [100 * rows[f"{fam}_{k}"][metric] for k in RETENTION_COUNTS]
+                                   for fam in ("topmag", "structured", "learned")},
+                                  title=f"{title}: {metric}", xlabel="retained latent coordinates (of 512)",
+                                  ylabel=f"{metric} relative output error (%)")
+                result["figures"][metric] = info["legend"]
+                files.append(str(path))
             return files
-        rows = {r["method"]: r for r in result["summary"]}
         for metric in ("mean", "p95"):
             fig, ax = plt.subplots(figsize=(8, 5))
             for fam in ("topmag", "structured", "learned"):

@@ -156,6 +156,17 @@ def test_capture_train_evaluate_end_to_end(tmp_path, monkeypatch):
                        str(tmp_path / "cmp.json"), "--compare-masks"])
     diag = evaluate.main(["--cache", str(tmp_path / "cache"), "--policy", out["policy"], "--output",
                           str(tmp_path / "diag.json")])
+    sweep = evaluate.main(["--cache", str(tmp_path / "cache"), "--policy", out["policy"], "--output",
+                           str(tmp_path / "sweep.json"), "--retention-sweep"])
+    from packmla.utils.png_plot import read_png
+
+    for metric in ("mean", "p95"):  # curves drawn without matplotlib
+        img, text = read_png(tmp_path / f"sweep-{metric}.png")
+        assert img.shape == (500, 800, 3) and "topmag=blue" in text["Legend"]
+        drawn = [bool((img == c).all(-1).any()) for c in ((31, 119, 180), (255, 127, 14), (44, 160, 44))]
+        assert any(drawn)  # curves were drawn (a later series may cover an equal earlier one)
+    saved = json.loads((tmp_path / "sweep.json").read_text())
+    assert saved["figures"]["renderer"] == "packmla.utils.png_plot" and len(sweep["summary"]) == 21
     from packmla.training.data import storage
 
     aud = storage.main(["--cache", str(tmp_path / "cache"), "--repeat", "1"])
@@ -191,3 +202,18 @@ def test_capture_cli_publishes_and_builds_from_publications(tmp_path):
         for s in rows:
             pub = {p["ordinal"]: p for p in reader.load(s["rid"], layer)}
             assert torch.equal(pub[s["ordinal"]]["target"], s["target"])
+
+
+def test_png_line_chart_round_trip(tmp_path):
+    from packmla.utils.png_plot import line_chart, read_png
+
+    info = line_chart(tmp_path / "c.png", [64, 128, 256], {"a": [1.0, 2.0, 3.5], "b": [0.5, 0.7, 0.9]},
+                      title="t", xlabel="x", ylabel="y (%)")
+    img, text = read_png(tmp_path / "c.png")
+    assert img.shape == (500, 800, 3) and text["Y-Axis"] == "y (%)" and info["legend"] == {"a": "blue", "b": "orange"}
+    assert bool((img == (31, 119, 180)).all(-1).any()) and bool((img == (255, 127, 14)).all(-1).any())
+    assert info["y_range"][0] <= 0.5 and info["y_range"][1] >= 3.5
+    import pytest
+
+    with pytest.raises(FileExistsError):  # never overwrites
+        line_chart(tmp_path / "c.png", [1, 2], {"a": [1, 2]})
