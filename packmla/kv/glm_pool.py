@@ -118,8 +118,10 @@ class GLMKVPool:
     def rows_of(self, slot: int, positions: torch.Tensor) -> torch.Tensor:
         """Physical rows of token positions of request `slot` (int64, -1 for positions past its pages)."""
         pos = positions.to(self.device, torch.int64)
-        page = self.page_table[slot].to(torch.int64)[(pos // TOKENS_PER_PAGE).clamp(0, self.max_pages_per_req - 1)]
-        return torch.where((page >= 0) & (pos >= 0), page * TOKENS_PER_PAGE + pos % TOKENS_PER_PAGE,
+        idx = pos // TOKENS_PER_PAGE
+        inside = (pos >= 0) & (idx < self.max_pages_per_req)
+        page = self.page_table[slot].to(torch.int64)[idx.clamp(0, self.max_pages_per_req - 1)]
+        return torch.where(inside & (page >= 0), page * TOKENS_PER_PAGE + pos % TOKENS_PER_PAGE,
                            torch.full_like(pos, -1))
 
     # ------------------------------------------------------------------ data path

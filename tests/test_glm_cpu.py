@@ -148,7 +148,7 @@ def test_glm_pool_lifecycle_capacity_and_decode_on_cpu():
         for layer in (3, 43):
             pool.store(layer, raw, w, 1e-6, slot, pos)
         rows = pool.rows_of(slot, pos).int()[None]
-        assert int(pool.rows_of(slot, torch.tensor([200]))[0]) == -1  # past the request's pages
+        assert pool.rows_of(slot, torch.tensor([200, 256, 1000, -1])).tolist() == [-1] * 4  # no row of its own
         outs[cfg.kv_cache_format] = pool.decode(43, q, rows, torch.tensor([100], dtype=torch.int32))
         pool.release(slot)
         assert pool.pages.free == 6
