@@ -154,3 +154,18 @@ def test_glm_pool_lifecycle_capacity_and_decode_on_cpu():
         assert pool.pages.free == 6
     # Direct keeps half the coordinates: close to, not equal to, Native
     assert float((outs["native"][0].float() - outs["direct"][0].float()).abs().max()) < 0.5
+
+
+def test_split_clusters_must_all_be_co_resident(monkeypatch):
+    from packmla.ops import attention
+
+    monkeypatch.setitem(attention._MAX_CLUSTERS, 0, {2: 40, 4: 30, 8: 12})
+    dev = torch.device("cuda", 0)
+    attention.check_cluster_fit(30, 64, 4, dev)  # 30 clusters of 4: co-resident
+    attention.check_cluster_fit(500, 128, 9, dev)  # not a cluster count: partials, no limit
+    with pytest.raises(ValueError, match="co-resident"):
+        attention.check_cluster_fit(32, 16, 4, dev)  # the faulted launch's shape
+    with pytest.raises(ValueError, match="co-resident"):
+        attention.check_cluster_fit(7, 128, 8, dev)  # 14 clusters of 8 > 12
+    # the automatic choice never picks such a count
+    assert attention.choose_tiling(32, 16, 2048, max_clusters={2: 40, 4: 30, 8: 12})[0] == 2
