@@ -94,3 +94,41 @@ def test_decode_graph_replay(cuda):
     torch.cuda.synchronize()
     check_errors(cuda)
     assert torch.equal(out, eager)
+
+
+def test_decode_graph_replay_with_changed_inputs_and_canary_rows(cuda):
+    """Capture once, then change the planes' rows, the indices and the lengths in place; the replay equals an
+    eager call on the new inputs, and rows past the output (canaries) are never written."""
+    from packmla.ops.attention import DecodeWorkspace, choose_splits
+
+    rows, B, H, K = 2048, 4, 16, 2048
+    _, _, _, _, planes = _cache(7, rows, cuda)
+    g = torch.Generator().manual_seed(8)
+    q = torch.randn(B, H, 512, generator=g).bfloat16().to(cuda)
+    sl = torch.randint(0, rows, (B, K), generator=g, dtype=torch.int32).to(cuda)
+    lens = torch.full((B,), K, dtype=torch.int32, device=cuda)
+    canary = torch.full((B + 1, H, 512), -91.0, dtype=torch.bfloat16, device=cuda)
+    lse_buf = torch.full((B + 1, H), -91.0, dtype=torch.float32, device=cuda)
+    out, lse = canary[:B], lse_buf[:B]
+    ws = DecodeWorkspace(B, H, choose_splits(B, H, K), cuda)
+    glm_sparse_decode(q, sl, lens, planes=planes, out=out, lse=lse, workspace=ws)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        glm_sparse_decode(q, sl, lens, planes=planes, out=out, lse=lse, workspace=ws)
+    _, _, _, _, other = _cache(9, rows, cuda)
+    planes.values.copy_(other.values)
+    planes.bitmap.copy_(other.bitmap)
+    sl.copy_(torch.randint(0, rows, (B, K), generator=g, dtype=torch.int32).to(cuda))
+    sl[1, 7] = -1
+    lens.copy_(torch.tensor([K, 1000, 1, 0], dtype=torch.int32))
+    q.copy_(torch.randn(B, H, 512, generator=g).bfloat16())
+    graph.replay()
+    torch.cuda.synchronize()
+    check_errors(cuda)
+    ref_o, ref_lse = glm_sparse_decode(q, sl, lens, planes=planes, workspace=ws)
+    check_errors(cuda)
+    assert torch.equal(out, ref_o) and torch.equal(lse, ref_lse)
+    assert bool((canary[B] == -91.0).all()) and bool((lse_buf[B] == -91.0).all())
+    cpu_o, _ = glm_sparse_decode(q.cpu(), sl.cpu(), lens.cpu(),
+                                 planes=GLMPlanes(planes.values.cpu(), planes.bitmap.cpu()))
+    torch.testing.assert_close(out.float().cpu(), cpu_o.float(), atol=2e-2, rtol=2e-2)
