@@ -25,6 +25,12 @@ def build_parser() -> argparse.ArgumentParser:
                     help="tiny | small | v4-flash | path to a packmla checkpoint")
     ap.add_argument("--served-model-name", default=None)
     ap.add_argument("--api-key", default=None, help="require `Authorization: Bearer KEY` on every route but /health")
+    ap.add_argument("--chat-preparation-workers", type=int, default=0, choices=[0, 1, 2, 4],
+                    help="chat-template conversion on 1, 2 or 4 worker threads, admission bounded by the pool "
+                         "(0: inline on the API loop; the reference's DSV4_ASYNC_PREPARATION / "
+                         "DSV4_PREPARATION_WORKERS)")
+    ap.add_argument("--frontend-diagnostics", action="store_true",
+                    help="chat responses carry preparation and first-output stamps (FRONTEND_DIAGNOSTICS=1)")
     ap.add_argument("--tokenizer", "--tokenizer-path", dest="tokenizer", default=None,
                     help="directory with Hugging Face tokenizer files (local only); default: byte-level tokenizer")
     ap.add_argument("--host", default="127.0.0.1")
@@ -239,7 +245,9 @@ def main(argv=None) -> None:
     from .app import create_app
 
     app = create_app(driver, load_tokenizer(args.tokenizer, eng.cfg.vocab_size), name,
-                     {"server_args": {k: v for k, v in vars(args).items() if k != "api_key"}}, api_key=args.api_key)
+                     {"server_args": {k: v for k, v in vars(args).items() if k != "api_key"}}, api_key=args.api_key,
+                     preparation_workers=args.chat_preparation_workers,
+                     frontend_diagnostics=args.frontend_diagnostics)
     driver.start()
     print(json.dumps({"event": "server_ready", "host": args.host, "port": args.port,
                       "max_total_num_tokens": eng.capacity.max_total_tokens}), flush=True)

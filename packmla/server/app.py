@@ -133,12 +133,76 @@ def _sse(obj) -> bytes:
     return f"data: {json.dumps(obj)}\n\n".encode()
 
 
+class ChatPreparation:
+    """Chat-template conversion of a request's messages, inline (no worker, the default) or on a pool of
+    1, 2 or 4 worker threads with admission bounded by the pool size.
+
+    Reference behaviour: SGLang's opt-in `SGLANG_DSV4_ASYNC_PREPARATION` text-chat worker with
+    `DSV4_PREPARATION_WORKERS=1|2|4` (third_party/README.md:310-323): conversion leaves the API event loop;
+    a cancelled request keeps its admission until its conversion completes; shutdown drains owned work;
+    off creates no worker.  `prepare` returns the token ids and, in perf_counter seconds, the stamps
+    queued / started / finished / resumed (the last when the API coroutine runs again)."""
+
+    def __init__(self, convert, workers: int = 0):
+        if workers not in (0, 1, 2, 4):
+            raise ValueError("chat preparation workers must be 0 (inline), 1, 2 or 4")
+        self.convert = convert
+        self.workers = workers
+        self._pool = None
+        self._admission: asyncio.Semaphore | None = None
+        if workers:
+            from concurrent.futures import ThreadPoolExecutor
+
+            self._pool = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="chat-prep")
+
+    def _run(self, msgs, stamps: dict):
+        stamps["started"] = time.perf_counter()
+        try:
+            return self.convert(msgs)
+        finally:
+            stamps["finished"] = time.perf_counter()
+
+    async def prepare(self, msgs) -> tuple[list[int], dict]:
+        stamps = {"queued": time.perf_counter()}
+        if self._pool is None:
+            return self._run(msgs, stamps), stamps
+        if self._admission is None:
+            self._admission = asyncio.Semaphore(self.workers)
+        await self._admission.acquire()
+        fut = asyncio.get_running_loop().run_in_executor(self._pool, self._run, msgs, stamps)
+        # the admission is released when the conversion ends, not when a cancelled caller stops waiting
+        fut.add_done_callback(lambda _f: self._admission.release())
+        ids = await asyncio.shield(fut)
+        stamps["resumed"] = time.perf_counter()
+        return ids, stamps
+
+    def close(self) -> None:
+        if self._pool is not None:
+            self._pool.shutdown(wait=True)  # drain conversions still running
+
+
+def _diagnostics(t0: float, prep: dict, st, api_first: float | None) -> dict:
+    """First-output diagnostics in ms after the API handler started (fields that never happened stay absent)."""
+    out = {f"preparation_{k}_ms": round((v - t0) * 1e3, 3) for k, v in prep.items()}
+    if st is not None and st.t_submit:
+        out["submitted_ms"] = round((st.t_submit - t0) * 1e3, 3)
+    if st is not None and st.t_first is not None:
+        out["first_output_engine_ms"] = round((st.t_first - t0) * 1e3, 3)
+    if api_first is not None:
+        out["first_output_api_ms"] = round((api_first - t0) * 1e3, 3)
+    return out
+
+
 def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, server_args: dict | None = None,
-               api_key: str | None = None) -> FastAPI:
+               api_key: str | None = None, preparation_workers: int = 0,
+               frontend_diagnostics: bool = False) -> FastAPI:
     """`api_key`: when set, every route but /health answers 401 unless the request carries
-    `Authorization: Bearer <api_key>` (SGLang's --api-key)."""
+    `Authorization: Bearer <api_key>` (SGLang's --api-key).  `preparation_workers`: chat-template
+    conversion on 1, 2 or 4 worker threads (0: inline).  `frontend_diagnostics`: chat responses carry a
+    `diagnostics` object with preparation and first-output stamps."""
     eng = driver.engine
     vocab = eng.cfg.vocab_size
+    prep = ChatPreparation(tokenizer.apply_chat_template, preparation_workers)
 
     @contextlib.asynccontextmanager
     async def lifespan(_app):
@@ -160,6 +224,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             yield
         finally:
             task.cancel()
+            prep.close()
 
     app = FastAPI(title="packmla", lifespan=lifespan)
 
@@ -355,6 +420,7 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
+        t0 = time.perf_counter()
         body = await req.json()
         msgs = body.get("messages")
         if not isinstance(msgs, list) or not msgs:
@@ -362,7 +428,9 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         params = _params(body, tokenizer)
         n_choices = _n(body)
         _StopRule(body, tokenizer)
-        ids = tokenizer.apply_chat_template(msgs)
+        ids, stamps = await prep.prepare(msgs)
+        eng.metrics.observe("chat_preparation_seconds", stamps["finished"] - stamps["started"])
+        api_first = [None]
         rid = f"chatcmpl-{uuid.uuid4().hex}"
         created = int(time.time())
         if body.get("stream"):
@@ -376,6 +444,8 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                 async for kind, i, item in _merge(streams, body):
                     if kind == "tok":
                         n += 1
+                        if api_first[0] is None:
+                            api_first[0] = time.perf_counter()
                         yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
                                     "model": model_name,
                                     "choices": [{"index": i, "delta": {"content": tokenizer.decode([item])},
@@ -384,6 +454,8 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                     ended += 1
                     last = {"usage": _usage(len(ids), n, _cached(streams, n_choices))} \
                         if ended == len(streams) else {}
+                    if last and frontend_diagnostics:
+                        last["diagnostics"] = _diagnostics(t0, stamps, streams[0], api_first[0])
                     yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                                 "choices": [{"index": i, "delta": {}, "finish_reason": streams[i].finish_reason}],
                                 **last})
@@ -394,12 +466,21 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         choices, ntok = [], 0
         for i, st in enumerate(streams):
             rule = _StopRule(body, tokenizer)
-            toks = await _collect(st, rule)
+            toks = []
+            async for t in _tokens(st, rule):
+                if api_first[0] is None:
+                    api_first[0] = time.perf_counter()
+                toks.append(t)
+            if st.finish_reason == "error":
+                raise HTTPException(500, f"engine failed: {driver.error!r}")
             ntok += len(toks)
             choices.append({"index": i, "message": {"role": "assistant", "content": _text(toks, rule)},
                             "finish_reason": st.finish_reason})
-        return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": choices, "usage": _usage(len(ids), ntok, _cached(streams, n_choices))}
+        out = {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
+               "choices": choices, "usage": _usage(len(ids), ntok, _cached(streams, n_choices))}
+        if frontend_diagnostics:
+            out["diagnostics"] = _diagnostics(t0, stamps, streams[0], api_first[0])
+        return out
 
     @app.post("/generate")
     async def generate(req: Request):

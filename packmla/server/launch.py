@@ -10,7 +10,8 @@ glm53; dsv41 serves the V4.1 FP4 cache formats), MODEL (default v4-flash),
 DEVICE (cuda | cpu), TP, EP, PORT (30000), MASTER_PORT (29500), MEM_FRAC, CTX_LEN, MAX_RUN, CHUNK,
 DECODE_CFG (the --cuda-graph-config JSON), SERVER_SEED, HICACHE_RATIO (turns HiCache on),
 C4_KEEP_COUNT, C4_LAYER_KEEP_COUNTS, STORE_IMPLEMENTATION, REQUEST_METRICS_DIR (request log and
-per-request metric files; the directory must exist), NSYS_OUTPUT (run under Nsight Systems, which
+per-request metric files; the directory must exist), DSV4_ASYNC_PREPARATION (0 | 1) and
+DSV4_PREPARATION_WORKERS (1 | 2 | 4): chat conversion off the API loop, FRONTEND_DIAGNOSTICS (0 | 1), NSYS_OUTPUT (run under Nsight Systems, which
 records only between POST /start_profile and /stop_profile).  TP > 1 runs one process per GPU under torchrun
 on 127.0.0.1.
 
@@ -94,6 +95,19 @@ def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
     for name, flag in ENV_FLAGS:
         if env.get(name):
             flags += [flag, env[name]]
+    diag = env.get("FRONTEND_DIAGNOSTICS", "0")
+    if diag not in ("0", "1"):
+        raise SystemExit("FRONTEND_DIAGNOSTICS must be 0 or 1")
+    prep = env.get("DSV4_ASYNC_PREPARATION", "0")
+    if prep not in ("0", "1"):
+        raise SystemExit("DSV4_ASYNC_PREPARATION must be 0 or 1")
+    workers = env.get("DSV4_PREPARATION_WORKERS", "1")
+    if workers not in ("1", "2", "4"):
+        raise SystemExit("DSV4_PREPARATION_WORKERS must be 1, 2 or 4")
+    if prep == "1":
+        flags += ["--chat-preparation-workers", workers]
+    if diag == "1":
+        flags += ["--frontend-diagnostics"]
     if env.get("HICACHE_RATIO"):
         flags += ["--enable-hierarchical-cache", "--hicache-ratio", env["HICACHE_RATIO"]]
     metrics_dir = env.get("REQUEST_METRICS_DIR")

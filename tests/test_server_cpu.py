@@ -316,3 +316,69 @@ def test_longbench_evaluator_scores_choices_and_resumes(served, tmp_path):
     g = longbench.evaluate(loaded[:1], post, tok, tmp_path / "gen", mode="generate")
     assert g["overall"]["n"] == 1
     assert longbench.parse_answer("The correct answer is (C).") == "C"
+
+
+def test_chat_preparation_workers_and_frontend_diagnostics():
+    """Chat conversion on a 2-worker pool gives the same tokens as inline conversion; diagnostics carry the
+    preparation and first-output stamps in order; a conversion outlives a cancelled caller and keeps its
+    admission until it ends."""
+    import asyncio
+    import time as _time
+
+    from packmla.server.app import ChatPreparation
+
+    cfg = ModelConfig.tiny(num_layers=2)
+    eng = Engine.build(cfg, EngineConfig(device="cpu", max_running_requests=2, cuda_graph_bs=[1, 2]), "cpu",
+                       max_context=256)
+    driver = EngineDriver(eng).start()
+    msgs = [{"role": "user", "content": "hello there"}]
+    body = {"model": "tiny", "messages": msgs, "max_tokens": 3, "temperature": 0}
+    outs = {}
+    try:
+        for workers, diag in ((0, False), (2, True)):
+            app = create_app(driver, ByteTokenizer(cfg.vocab_size), "tiny", preparation_workers=workers,
+                             frontend_diagnostics=diag)
+            with TestClient(app) as client:
+                r = client.post("/v1/chat/completions", json=body).json()
+                outs[workers] = r["choices"][0]["message"]["content"]
+                if diag:
+                    d = r["diagnostics"]
+                    order = ["preparation_queued_ms", "preparation_started_ms", "preparation_finished_ms",
+                             "preparation_resumed_ms", "submitted_ms", "first_output_engine_ms",
+                             "first_output_api_ms"]
+                    assert [d[k] for k in order] == sorted(d[k] for k in order)
+                    lines = [x for x in client.post("/v1/chat/completions", json={**body, "stream": True}).text
+                             .splitlines() if x.startswith("data: {")]
+                    assert "first_output_api_ms" in json.loads(lines[-1][6:])["diagnostics"]
+                else:
+                    assert "diagnostics" not in r
+    finally:
+        driver.stop()
+    assert outs[0] == outs[2]
+
+    release = threading.Event()
+
+    def slow(m):
+        release.wait(5)
+        return [1, 2, 3]
+
+    prep = ChatPreparation(slow, 1)
+
+    async def scenario():
+        first = asyncio.create_task(prep.prepare(["a"]))
+        await asyncio.sleep(0.05)
+        first.cancel()  # the caller goes away; the conversion keeps the single admission
+        await asyncio.sleep(0.05)
+        second = asyncio.create_task(prep.prepare(["b"]))
+        await asyncio.sleep(0.1)
+        assert not second.done()  # still waiting for the admission held by the running conversion
+        release.set()
+        ids, stamps = await asyncio.wait_for(second, 5)
+        return ids, stamps
+
+    t = _time.perf_counter()
+    ids, stamps = asyncio.run(scenario())
+    assert ids == [1, 2, 3] and stamps["queued"] >= t and stamps["resumed"] >= stamps["finished"]
+    prep.close()
+    with pytest.raises(ValueError):
+        ChatPreparation(slow, 3)

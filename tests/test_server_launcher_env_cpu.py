@@ -130,3 +130,23 @@ def test_model_families_are_validated_like_the_reference_launcher():
             resolve("direct", env)
     cmd, _ = resolve("direct", {})
     assert cmd[cmd.index("--kv-cache-format") + 1] == "direct"
+
+
+def test_frontend_preparation_and_diagnostics_environment():
+    import pytest
+
+    from packmla.server.launch import resolve
+
+    cmd, _ = resolve("direct", {"DSV4_ASYNC_PREPARATION": "1", "DSV4_PREPARATION_WORKERS": "4",
+                                "FRONTEND_DIAGNOSTICS": "1"})
+    assert cmd[cmd.index("--chat-preparation-workers") + 1] == "4" and "--frontend-diagnostics" in cmd
+    cmd, _ = resolve("direct", {})
+    assert "--chat-preparation-workers" not in cmd and "--frontend-diagnostics" not in cmd
+    for env, msg in (({"DSV4_PREPARATION_WORKERS": "3"}, "1, 2 or 4"), ({"FRONTEND_DIAGNOSTICS": "yes"}, "0 or 1"),
+                     ({"DSV4_ASYNC_PREPARATION": "2"}, "0 or 1")):
+        with pytest.raises(SystemExit, match=msg):
+            resolve("native", env)
+    from packmla.server.__main__ import build_parser
+
+    a = build_parser().parse_args(["--chat-preparation-workers", "2", "--frontend-diagnostics"])
+    assert a.chat_preparation_workers == 2 and a.frontend_diagnostics
