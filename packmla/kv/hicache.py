@@ -8,7 +8,10 @@ tier works at request granularity: when a request finishes, its KV (every C4 pag
 with all planes and indexer keys, its C128 pages, and the request slot's SWA ring and compressor
 state) is written through to host memory, keyed by the processed tokens.  A new request whose prompt
 starts with such a key gets the KV copied back into its freshly allocated pages and prefills only the
-remaining tokens (a multi-turn conversation re-sends its history every turn).
+remaining tokens (a multi-turn conversation re-sends its history every turn).  The same host pages also
+hold prefix blocks evicted from the device block tree (`packmla.kv.prefix_blocks`): `alloc_host` /
+`copy_pages` / `free_host` move a block's own KV and C128 pages, and a block may take the pages of
+least recently used request entries, never the reverse.
 
 Layout: `page_first` (default: one host page holds the page's planes of all layers contiguously, so a
 request's pages are few large segments) or `layer_first` (each plane of each layer has its own host
