@@ -216,6 +216,8 @@ class PrefixBlockCache:
         block's end): add it, or find the same block already cached.  Returns the node (None: not cached)."""
         if (parent is None) != (index == 0):
             return None
+        if parent is not None and self.nodes.get(parent.key) is not parent:
+            return None  # the parent was dropped since: a block under it could never be matched
         key = _chain_key(parent.key if parent else b"", prompt[index * self.block:(index + 1) * self.block])
         node = self.nodes.get(key)
         if node is not None:

@@ -216,3 +216,17 @@ def test_prefix_blocks_move_to_the_host_tier_and_back():
         eng.flush_cache()
         assert not eng.blocks.nodes and eng.pool.pages.free == eng.pool.num_pages
         assert sorted(eng.hicache._free) == list(range(eng.hicache.num_host_pages))
+
+
+def test_block_under_a_dropped_parent_is_not_cached():
+    eng = _block_engine()
+    base = _toks(300, 71)
+    eng.generate([base], SamplingParams(max_new_tokens=1))
+    (node,) = list(eng.blocks.nodes.values())
+    while eng._evict_retained():
+        pass
+    eng.blocks.flush()
+    slot = eng.pool.admit(600)
+    assert eng.blocks.insert(base + _toks(300, 72), slot, 1, node) is None and not eng.blocks.nodes
+    eng.pool.release(slot)
+    assert eng.pool.pages.free == eng.pool.num_pages
