@@ -110,6 +110,8 @@ class PrefixBlockCache:
 
     def shared_pages(self, chain: list[BlockNode]) -> tuple[list[int], list[int]]:
         """(KV pages, whole C128 pages) a request admitted on `chain` maps read-only (all on the device)."""
+        if not chain:
+            return [], []
         if any(n.host is not None for n in chain):
             raise ValueError("host-resident blocks must be promoted before they are mapped")
         pages = [p for n in chain for p in n.pages]
