@@ -1,7 +1,8 @@
 """CPU: randomized bookkeeping of the prefix-block tree with the HiCache host tier (no model).
 
 Random admissions on matched chains (promoting host-resident blocks), block insertions, request
-releases, evictions (demotion to the host or drop) and flushes, with the invariants checked after
+releases (some written through to the host tier as request entries, which compete with demoted blocks
+for host pages), evictions (demotion to the host or drop) and flushes, with the invariants checked after
 every operation: each device page's reference count equals its holders (device blocks and requests),
 child counters match the tree, host-resident blocks hold no device pages, host pages are never lost or
 doubly owned, and a flush returns every page.
@@ -92,9 +93,12 @@ def test_random_block_operations_keep_the_books(seed):
                 r["done"] += 1
                 if r["tail"] is None:  # not cached: later blocks of this request are not either
                     r["done"] = len(r["prompt"])
-        elif op < 0.85 and requests:
+        elif op < 0.85 and requests:  # a request ends; the host tier may keep its processed tokens
             slot = rng.choice(list(requests))
-            del requests[slot]
+            r = requests.pop(slot)
+            done = min(r["done"] * BLOCK, len(r["prompt"]))
+            if done and rng.random() < 0.5:
+                host.save(slot, r["prompt"][:done])
             pool.release(slot)
         else:
             blocks.evict_one()
