@@ -73,6 +73,12 @@ FAMILIES: dict[str, dict] = {
                     MB + ["decode", "--batch", "8", "--heads", "64", "--topk", "512", "--swa", "128", "--context",
                           "32768", "--kv-format", "fp4-direct", "--rounds", "1", "--warmup", "1"]),
     },
+    "glm": {  # GLM-5.3 rows: stores, Adapter and the decode row kinds (the reference's --model-family glm53)
+        "tests": ["tests/test_gpu_glm.py"],
+        "bench": [MB + ["glm-suite", "--rounds", "30"]],
+        "profile": ("sparse_mla_decode_kernel",
+                    MB + ["glm-suite", "--rounds", "1", "--warmup", "1", "--glm-batches", "8"]),
+    },
 }
 STAGES = ("build", "validate", "bench", "profile")
 NCU_METRICS = ("gpu__time_duration.sum", "dram__bytes_read.sum", "dram__bytes_write.sum",
