@@ -29,13 +29,18 @@ from .protocol import ProtocolError
 
 class EPExchangeModel:
     def __init__(self, world: int, tokens: int, topk: int, experts: int, calls: int, seed: int = 0,
-                 wait_all_back: bool = True):
+                 wait_all_back: bool = True, arrival_order: bool = False):
+        """`arrival_order`: an owner serves the sources in the order their flags arrive (any released source
+        next), as a kernel that overlaps the exchange with the expert GEMMs would, instead of 0, 1, ..."""
         if experts % world:
             raise ValueError("experts must divide evenly over the ranks")
         rng = random.Random(seed)
         self.world, self.T, self.k, self.E, self.calls = world, tokens, topk, experts, calls
         self.local = experts // world
         self.wait_all_back = wait_all_back
+        self.arrival_order = arrival_order
+        self.served: dict = {}
+        self._rng = random.Random(seed)
         # routing[c][r] = list of (token, expert) pairs of rank r in routing order
         self.routing = [[[(t, rng.randrange(experts)) for t in range(tokens) for _ in range(topk)]
                          for _ in range(world)] for _ in range(calls)]
@@ -62,8 +67,11 @@ class EPExchangeModel:
                     steps.append(("store_row", c, d, i, j))
                 steps.append(("release_rows", c, d, len(per_dest.get(d, []))))
             for s in range(self.world):  # owner side: wait for every source, compute, return
-                steps.append(("acquire_rows", c, s))
-                steps.append(("compute_return", c, s))
+                if self.arrival_order:
+                    steps.append(("serve_any", c))
+                else:
+                    steps.append(("acquire_rows", c, s))
+                    steps.append(("compute_return", c, s))
             waits = range(self.world) if self.wait_all_back else [r]
             for d in waits:
                 steps.append(("acquire_back", c, d))
@@ -78,7 +86,22 @@ class EPExchangeModel:
             return self.flag_rows[(r, op[2])] >= op[1]
         if op[0] == "acquire_back":
             return self.flag_back[(r, op[2])] >= op[1]
+        if op[0] == "serve_any":
+            return bool(self._ready_sources(r, op[1]))
         return True
+
+    def _ready_sources(self, r: int, c: int) -> list[int]:
+        done = self.served.setdefault((r, c), set())
+        return [s for s in range(self.world) if s not in done and self.flag_rows[(r, s)] >= c]
+
+    def _serve(self, r: int, c: int, s: int) -> None:
+        n = self.count[(r, s)]
+        for i in range(n):
+            tag = self.rows[(r, s)].get(i)
+            if tag is None or tag[0] != "row" or tag[1] != c or tag[2] != s:
+                raise ProtocolError(f"rank {r} read {tag} for call {c} row {i} from rank {s}")
+            self.back[(s, r)][i] = ("out", c, s, tag[3])
+        self.flag_back[(s, r)] = c
 
     def _step(self, r: int) -> None:
         op = self.progs[r][self.pcs[r]]
@@ -91,14 +114,11 @@ class EPExchangeModel:
             self.count[(d, r)] = n
             self.flag_rows[(d, r)] = c
         elif kind == "compute_return":
-            s = op[2]
-            n = self.count[(r, s)]
-            for i in range(n):
-                tag = self.rows[(r, s)].get(i)
-                if tag is None or tag[0] != "row" or tag[1] != c or tag[2] != s:
-                    raise ProtocolError(f"rank {r} read {tag} for call {c} row {i} from rank {s}")
-                self.back[(s, r)][i] = ("out", c, s, tag[3])
-            self.flag_back[(s, r)] = c
+            self._serve(r, c, op[2])
+        elif kind == "serve_any":
+            s = self._rng.choice(self._ready_sources(r, c))
+            self.served[(r, c)].add(s)
+            self._serve(r, c, s)
         elif kind == "combine":
             per_dest = op[2]
             got = {}
@@ -126,9 +146,10 @@ class EPExchangeModel:
 
 
 def explore(world: int, tokens: int, topk: int, experts: int, calls: int, schedules: int, seed: int = 0,
-            wait_all_back: bool = True) -> int:
+            wait_all_back: bool = True, arrival_order: bool = False) -> int:
     """Run `schedules` random interleavings; returns how many completed (raises on the first race)."""
     rng = random.Random(seed)
     for n in range(schedules):
-        EPExchangeModel(world, tokens, topk, experts, calls, seed=seed + n, wait_all_back=wait_all_back).run(rng)
+        EPExchangeModel(world, tokens, topk, experts, calls, seed=seed + n, wait_all_back=wait_all_back,
+                        arrival_order=arrival_order).run(rng)
     return schedules

@@ -40,5 +40,9 @@ def test_fused_ep_exchange_protocol_has_no_race_and_the_early_dispatch_bug_is_ca
 
     for world in (2, 4, 8):
         assert explore(world, tokens=3, topk=2, experts=2 * world, calls=3, schedules=60, seed=world) == 60
-    with pytest.raises(ProtocolError):
-        explore(4, tokens=3, topk=2, experts=8, calls=3, schedules=200, seed=1, wait_all_back=False)
+        assert explore(world, tokens=3, topk=2, experts=2 * world, calls=3, schedules=60, seed=world,
+                       arrival_order=True) == 60  # owners serve sources as their flags arrive
+    for arrival in (False, True):
+        with pytest.raises(ProtocolError):
+            explore(4, tokens=3, topk=2, experts=8, calls=3, schedules=200, seed=1, wait_all_back=False,
+                    arrival_order=arrival)
