@@ -153,3 +153,44 @@ def explore(world: int, tokens: int, topk: int, experts: int, calls: int, schedu
         EPExchangeModel(world, tokens, topk, experts, calls, seed=seed + n, wait_all_back=wait_all_back,
                         arrival_order=arrival_order).run(rng)
     return schedules
+
+
+def emulate_exchange(h: list, ids: list, w: list, experts: int, expert_fn) -> list:
+    """The data path of the protocol above on tensors, all ranks in one process: the oracle a fused kernel
+    is checked against.  h[r] [T, H], ids[r] / w[r] [T, k] of rank r; `expert_fn(rows, global_expert_ids)`
+    returns the unweighted outputs.  Each rank's symmetric memory holds rows[r] [world, T k, H] (one
+    region per source) and back[r] [world, T k, H] (one region per owner); pair j of source s that owner d
+    receives as its i-th lands at rows[d][s, i] and returns to back[s][d, i].  Returns the per-rank fp32
+    sums over k in routing order."""
+    import torch
+
+    world = len(h)
+    T, k = ids[0].shape
+    H = h[0].shape[1]
+    local = experts // world
+    rows = [torch.zeros(world, T * k, H, dtype=h[0].dtype) for _ in range(world)]
+    rows_ids = [torch.full((world, T * k), -1, dtype=torch.int64) for _ in range(world)]
+    back = [torch.zeros(world, T * k, H, dtype=torch.float32) for _ in range(world)]
+    count = [[0] * world for _ in range(world)]
+    index = []  # index[s][j] = (owner, slot) of pair j of source s
+    for s in range(world):  # dispatch
+        flat = ids[s].reshape(-1)
+        slots = []
+        for j in range(T * k):
+            d = int(flat[j]) // local
+            i = count[d][s]
+            rows[d][s, i] = h[s][j // k]
+            rows_ids[d][s, i] = int(flat[j])
+            count[d][s] = i + 1
+            slots.append((d, i))
+        index.append(slots)
+    for d in range(world):  # owners: experts on each source region, outputs back to the source
+        for s in range(world):
+            n = count[d][s]
+            if n:
+                back[s][d, :n] = expert_fn(rows[d][s, :n], rows_ids[d][s, :n]).float()
+    out = []
+    for s in range(world):  # combine in routing order
+        pairs = torch.stack([back[s][d, i] for d, i in index[s]]).view(T, k, H)
+        out.append((pairs * w[s].float()[..., None]).sum(1))
+    return out

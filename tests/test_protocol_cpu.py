@@ -46,3 +46,24 @@ def test_fused_ep_exchange_protocol_has_no_race_and_the_early_dispatch_bug_is_ca
         with pytest.raises(ProtocolError):
             explore(4, tokens=3, topk=2, experts=8, calls=3, schedules=200, seed=1, wait_all_back=False,
                     arrival_order=arrival)
+
+
+def test_fused_ep_exchange_data_path_matches_dense_moe():
+    import torch
+
+    from packmla.parallel.ep_protocol import emulate_exchange
+
+    g = torch.Generator().manual_seed(3)
+    world, T, k, H, E = 4, 5, 3, 16, 8
+    W = torch.randn(E, H, H, generator=g)
+
+    def expert_fn(rows, e):
+        return torch.einsum("nh,nhg->ng", rows.float(), W[e])
+
+    h = [torch.randn(T, H, generator=g) for _ in range(world)]
+    ids = [torch.randint(0, E, (T, k), generator=g) for _ in range(world)]
+    w = [torch.rand(T, k, generator=g) for _ in range(world)]
+    out = emulate_exchange(h, ids, w, E, expert_fn)
+    for r in range(world):
+        dense = sum(w[r][:, j, None] * expert_fn(h[r], ids[r][:, j]) for j in range(k))
+        torch.testing.assert_close(out[r], dense, atol=1e-4, rtol=1e-4)
