@@ -43,7 +43,7 @@ class GLMCacheConfig:
         if self.model_dtype != "bfloat16":
             raise ValueError("GLM MLA rows require a BF16 model dtype")
         if self.enable_hierarchical_cache or self.keep_count is not None:
-            raise ValueError("GLM Packed does not support HiCache or DeepSeek codec overrides")
+            raise ValueError("the GLM MLA pool takes neither the host tier nor a C4 survivor-count setting")
         g = self.geometry
         if (g.kv_lora_rank, g.qk_head_dim, len(g.mla_layers)) != (glm.LATENT_DIM, 256, 11):
             raise ValueError("GLM MLA rows require the pinned GLM-5.3 text geometry")

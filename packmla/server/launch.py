@@ -11,8 +11,8 @@ DEVICE (cuda | cpu), TP, EP, PORT (30000), MASTER_PORT (29500), MEM_FRAC, CTX_LE
 DECODE_CFG (the --cuda-graph-config JSON), SERVER_SEED, HICACHE_RATIO (turns HiCache on),
 C4_KEEP_COUNT, C4_LAYER_KEEP_COUNTS, STORE_IMPLEMENTATION, REQUEST_METRICS_DIR (request log and
 per-request metric files; the directory must exist), DSV4_ASYNC_PREPARATION (0 | 1) and
-DSV4_PREPARATION_WORKERS (1 | 2 | 4): chat conversion off the API loop, FRONTEND_DIAGNOSTICS (0 | 1), NSYS_OUTPUT (run under Nsight Systems, which
-records only between POST /start_profile and /stop_profile).  TP > 1 runs one process per GPU under torchrun
+DSV4_PREPARATION_WORKERS (1 | 2 | 4): chat conversion off the API loop, FRONTEND_DIAGNOSTICS (0 | 1),
+NSYS_OUTPUT (run under Nsight Systems, which records only between POST /start_profile and /stop_profile).  TP > 1 runs one process per GPU under torchrun
 on 127.0.0.1.
 
 The launcher owns the server's process group: it starts the server in a new session, waits for
@@ -51,18 +51,18 @@ def _family_checks(family: str, env: dict) -> tuple[int, int | None]:
     label = "V4.1" if family == "dsv41" else "GLM"
     tp = int(env.get("TP", "4" if family == "dsv41" else "8"))
     if tp not in (1, 2, 4, 8):
-        raise SystemExit(f"{label} requires TP1/2/4/8")
+        raise SystemExit(f"{label} launches take a TP size of 1, 2, 4 or 8 (got {tp})")
     ep = int(env.get("EP", str(tp)))
     if ep < 1 or ep > tp or tp % ep:
-        raise SystemExit(f"{label} EP must be a positive divisor of TP (TP={tp} EP={ep})")
+        raise SystemExit(f"{label}: EP={ep} does not divide TP={tp}")
     if any(env.get(k) for k in CODEC_OVERRIDES):
-        raise SystemExit("V4.1 does not support HiCache or C4 codec overrides" if family == "dsv41"
-                         else "GLM Packed does not support HiCache or DeepSeek codec overrides")
+        raise SystemExit(f"{label}: HiCache and the C4 codec settings ({', '.join(CODEC_OVERRIDES)}) apply to dsv4 "
+                         "only")
     gpus = env.get("GPUS") or env.get("CUDA_VISIBLE_DEVICES")
     if gpus:
         devices = gpus.split(",")
         if len(devices) != tp or any(not d.strip() for d in devices):
-            raise SystemExit(f"{label} needs TP={tp} visible GPUs; got GPUS={gpus}")
+            raise SystemExit(f"{label}: the GPU list {gpus!r} must name exactly {tp} devices")
     return tp, ep
 
 
@@ -74,7 +74,7 @@ def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
         raise SystemExit(f"mode must be native or direct, not {mode!r}")
     family = env.get("MODEL_FAMILY", "dsv4")
     if family not in FAMILIES:
-        raise SystemExit("MODEL_FAMILY must be dsv4, dsv41 or glm53")
+        raise SystemExit(f"unknown MODEL_FAMILY {family!r} (one of {', '.join(FAMILIES)})")
     fmt = mode
     if family != "dsv4":
         tp, ep = _family_checks(family, env)
@@ -97,13 +97,13 @@ def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
             flags += [flag, env[name]]
     diag = env.get("FRONTEND_DIAGNOSTICS", "0")
     if diag not in ("0", "1"):
-        raise SystemExit("FRONTEND_DIAGNOSTICS must be 0 or 1")
+        raise SystemExit(f"FRONTEND_DIAGNOSTICS takes 0 or 1, not {diag!r}")
     prep = env.get("DSV4_ASYNC_PREPARATION", "0")
     if prep not in ("0", "1"):
-        raise SystemExit("DSV4_ASYNC_PREPARATION must be 0 or 1")
+        raise SystemExit(f"DSV4_ASYNC_PREPARATION takes 0 or 1, not {prep!r}")
     workers = env.get("DSV4_PREPARATION_WORKERS", "1")
     if workers not in ("1", "2", "4"):
-        raise SystemExit("DSV4_PREPARATION_WORKERS must be 1, 2 or 4")
+        raise SystemExit(f"DSV4_PREPARATION_WORKERS takes 1, 2 or 4, not {workers!r}")
     if prep == "1":
         flags += ["--chat-preparation-workers", workers]
     if diag == "1":

@@ -118,14 +118,14 @@ def test_model_families_are_validated_like_the_reference_launcher():
     assert cmd[cmd.index("--kv-cache-format") + 1] == "fp4-direct" and cmd[cmd.index("--ep") + 1] == "4"
     cmd, _ = resolve("native", {"MODEL_FAMILY": "dsv41", "TP": "2", "GPUS": "0,1"})
     assert cmd[cmd.index("--kv-cache-format") + 1] == "fp4-native" and cmd[cmd.index("--tp") + 1] == "2"
-    for env, msg in (({"MODEL_FAMILY": "dsv41", "TP": "3"}, "TP1/2/4/8"),
-                     ({"MODEL_FAMILY": "dsv41", "TP": "4", "EP": "3"}, "divisor"),
+    for env, msg in (({"MODEL_FAMILY": "dsv41", "TP": "3"}, "1, 2, 4 or 8"),
+                     ({"MODEL_FAMILY": "dsv41", "TP": "4", "EP": "3"}, "does not divide"),
                      ({"MODEL_FAMILY": "dsv41", "TP": "2", "EP": "1"}, "EP = TP"),
                      ({"MODEL_FAMILY": "dsv41", "HICACHE_RATIO": "2"}, "HiCache"),
-                     ({"MODEL_FAMILY": "dsv41", "TP": "2", "GPUS": "0,"}, "visible GPUs"),
-                     ({"MODEL_FAMILY": "glm53", "C4_KEEP_COUNT": "128"}, "GLM Packed"),
+                     ({"MODEL_FAMILY": "dsv41", "TP": "2", "GPUS": "0,"}, "exactly 2 devices"),
+                     ({"MODEL_FAMILY": "glm53", "C4_KEEP_COUNT": "128"}, "dsv4 only"),
                      ({"MODEL_FAMILY": "glm53"}, "not built"),
-                     ({"MODEL_FAMILY": "glm99"}, "MODEL_FAMILY")):
+                     ({"MODEL_FAMILY": "glm99"}, "unknown MODEL_FAMILY")):
         with pytest.raises(SystemExit, match=msg):
             resolve("direct", env)
     cmd, _ = resolve("direct", {})
@@ -142,8 +142,8 @@ def test_frontend_preparation_and_diagnostics_environment():
     assert cmd[cmd.index("--chat-preparation-workers") + 1] == "4" and "--frontend-diagnostics" in cmd
     cmd, _ = resolve("direct", {})
     assert "--chat-preparation-workers" not in cmd and "--frontend-diagnostics" not in cmd
-    for env, msg in (({"DSV4_PREPARATION_WORKERS": "3"}, "1, 2 or 4"), ({"FRONTEND_DIAGNOSTICS": "yes"}, "0 or 1"),
-                     ({"DSV4_ASYNC_PREPARATION": "2"}, "0 or 1")):
+    for env, msg in (({"DSV4_PREPARATION_WORKERS": "3"}, "takes 1, 2 or 4"), ({"FRONTEND_DIAGNOSTICS": "yes"}, "takes 0 or 1"),
+                     ({"DSV4_ASYNC_PREPARATION": "2"}, "takes 0 or 1")):
         with pytest.raises(SystemExit, match=msg):
             resolve("native", env)
     from packmla.server.__main__ import build_parser
