@@ -18,6 +18,8 @@ import argparse
 import json
 import os
 
+from .reasoning import PARSERS as REASONING_PARSERS
+
 
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m packmla.server")
@@ -98,7 +100,9 @@ def build_parser() -> argparse.ArgumentParser:
     for flag in ("--skip-server-warmup", "--trust-remote-code", "--disable-overlap-schedule",
                  "--disable-flashinfer-autotune", "--language-model-only"):
         ref.add_argument(flag, action="store_true", help="accepted; no effect in packmla")
-    for flag in ("--reasoning-parser", "--tool-call-parser", "--model-type", "--dsa-decode-backend",
+    ref.add_argument("--reasoning-parser", default=None, choices=sorted(REASONING_PARSERS),
+                     help="chat messages carry the output's think block as reasoning_content")
+    for flag in ("--tool-call-parser", "--model-type", "--dsa-decode-backend",
                  "--dsa-prefill-backend", "--dsv4-attn-backend"):
         ref.add_argument(flag, default=None, help="accepted; no effect in packmla")
     return ap
@@ -247,7 +251,7 @@ def main(argv=None) -> None:
     app = create_app(driver, load_tokenizer(args.tokenizer, eng.cfg.vocab_size), name,
                      {"server_args": {k: v for k, v in vars(args).items() if k != "api_key"}}, api_key=args.api_key,
                      preparation_workers=args.chat_preparation_workers,
-                     frontend_diagnostics=args.frontend_diagnostics)
+                     frontend_diagnostics=args.frontend_diagnostics, reasoning_parser=args.reasoning_parser)
     driver.start()
     print(json.dumps({"event": "server_ready", "host": args.host, "port": args.port,
                       "max_total_num_tokens": eng.capacity.max_total_tokens}), flush=True)

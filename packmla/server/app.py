@@ -195,14 +195,20 @@ def _diagnostics(t0: float, prep: dict, st, api_first: float | None) -> dict:
 
 def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, server_args: dict | None = None,
                api_key: str | None = None, preparation_workers: int = 0,
-               frontend_diagnostics: bool = False) -> FastAPI:
+               frontend_diagnostics: bool = False, reasoning_parser: str | None = None) -> FastAPI:
     """`api_key`: when set, every route but /health answers 401 unless the request carries
     `Authorization: Bearer <api_key>` (SGLang's --api-key).  `preparation_workers`: chat-template
     conversion on 1, 2 or 4 worker threads (0: inline).  `frontend_diagnostics`: chat responses carry a
-    `diagnostics` object with preparation and first-output stamps."""
+    `diagnostics` object with preparation and first-output stamps.  `reasoning_parser`: chat messages
+    carry the output's think block as `reasoning_content` (a request may send `separate_reasoning` false)."""
     eng = driver.engine
     vocab = eng.cfg.vocab_size
     prep = ChatPreparation(tokenizer.apply_chat_template, preparation_workers)
+    if reasoning_parser is not None:
+        from .reasoning import PARSERS
+
+        if reasoning_parser not in PARSERS:
+            raise ValueError(f"unknown reasoning parser {reasoning_parser!r}")
 
     @contextlib.asynccontextmanager
     async def lifespan(_app):
@@ -431,12 +437,25 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
         ids, stamps = await prep.prepare(msgs)
         eng.metrics.observe("chat_preparation_seconds", stamps["finished"] - stamps["started"])
         api_first = [None]
+        parser = reasoning_parser if body.get("separate_reasoning", True) else None
         rid = f"chatcmpl-{uuid.uuid4().hex}"
         created = int(time.time())
         if body.get("stream"):
             streams = await _submit_group(ids, params, n_choices)
 
             async def gen():
+                from .reasoning import ReasoningSplitter, opened_by_request
+
+                splitters = [ReasoningSplitter(parser, opened_by_request(body)) if parser else None
+                             for _ in streams]
+
+                def delta_chunk(i, reasoning: str, content: str) -> bytes | None:
+                    delta = {k: v for k, v in (("reasoning_content", reasoning), ("content", content)) if v}
+                    if not delta:
+                        return None
+                    return _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
+                                 "model": model_name, "choices": [{"index": i, "delta": delta, "finish_reason": None}]})
+
                 for i in range(len(streams)):
                     yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                                 "choices": [{"index": i, "delta": {"role": "assistant"}, "finish_reason": None}]})
@@ -446,11 +465,16 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
                         n += 1
                         if api_first[0] is None:
                             api_first[0] = time.perf_counter()
-                        yield _sse({"id": rid, "object": "chat.completion.chunk", "created": created,
-                                    "model": model_name,
-                                    "choices": [{"index": i, "delta": {"content": tokenizer.decode([item])},
-                                                 "finish_reason": None}]})
+                        text = tokenizer.decode([item])
+                        chunk = (delta_chunk(i, *splitters[i].feed(text)) if splitters[i] is not None
+                                 else delta_chunk(i, "", text))
+                        if chunk is not None:
+                            yield chunk
                         continue
+                    if splitters[i] is not None:
+                        chunk = delta_chunk(i, *splitters[i].finish())
+                        if chunk is not None:
+                            yield chunk
                     ended += 1
                     last = {"usage": _usage(len(ids), n, _cached(streams, n_choices))} \
                         if ended == len(streams) else {}
@@ -474,8 +498,13 @@ def create_app(driver: EngineDriver, tokenizer: ByteTokenizer, model_name: str, 
             if st.finish_reason == "error":
                 raise HTTPException(500, f"engine failed: {driver.error!r}")
             ntok += len(toks)
-            choices.append({"index": i, "message": {"role": "assistant", "content": _text(toks, rule)},
-                            "finish_reason": st.finish_reason})
+            text = _text(toks, rule)
+            message = {"role": "assistant", "content": text}
+            if parser:
+                from .reasoning import opened_by_request, split
+
+                message["reasoning_content"], message["content"] = split(parser, text, opened_by_request(body))
+            choices.append({"index": i, "message": message, "finish_reason": st.finish_reason})
         out = {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
                "choices": choices, "usage": _usage(len(ids), ntok, _cached(streams, n_choices))}
         if frontend_diagnostics:

@@ -104,6 +104,8 @@ def resolve(mode: str | None, env: dict) -> tuple[list[str], dict]:
     workers = env.get("DSV4_PREPARATION_WORKERS", "1")
     if workers not in ("1", "2", "4"):
         raise SystemExit(f"DSV4_PREPARATION_WORKERS takes 1, 2 or 4, not {workers!r}")
+    # the reference launches serve the DeepSeek families with their reasoning parser
+    flags += ["--reasoning-parser", "deepseek-v41" if family == "dsv41" else "deepseek-v4"]
     if prep == "1":
         flags += ["--chat-preparation-workers", workers]
     if diag == "1":

@@ -382,3 +382,32 @@ def test_chat_preparation_workers_and_frontend_diagnostics():
     prep.close()
     with pytest.raises(ValueError):
         ChatPreparation(slow, 3)
+
+
+def test_reasoning_parser_moves_the_think_block_to_reasoning_content():
+    cfg = ModelConfig.tiny(num_layers=2)
+    eng = Engine.build(cfg, EngineConfig(device="cpu", max_running_requests=2, cuda_graph_bs=[1, 2]), "cpu",
+                       max_context=256)
+    driver = EngineDriver(eng).start()
+    body = {"model": "tiny", "messages": [{"role": "user", "content": "think"}], "max_tokens": 6, "temperature": 0}
+    try:
+        with TestClient(create_app(driver, ByteTokenizer(cfg.vocab_size), "tiny")) as plain_client:
+            plain = plain_client.post("/v1/chat/completions", json=body).json()["choices"][0]["message"]
+        assert "reasoning_content" not in plain
+        app = create_app(driver, ByteTokenizer(cfg.vocab_size), "tiny", reasoning_parser="deepseek-v4")
+        with TestClient(app) as client:
+            think = {**body, "chat_template_kwargs": {"thinking": True}}
+            msg = client.post("/v1/chat/completions", json=think).json()["choices"][0]["message"]
+            # greedy output without an end tag: all of it is the open think block
+            assert msg["reasoning_content"] == plain["content"] and msg["content"] == ""
+            lines = [json.loads(x[6:]) for x in client.post("/v1/chat/completions", json={**think, "stream": True})
+                     .text.splitlines() if x.startswith("data: {")]
+            deltas = [c["choices"][0]["delta"] for c in lines]
+            assert "".join(d.get("reasoning_content", "") for d in deltas) == plain["content"]
+            assert not any(d.get("content") for d in deltas)
+            off = client.post("/v1/chat/completions", json={**think, "separate_reasoning": False}).json()
+            assert off["choices"][0]["message"]["content"] == plain["content"]
+            no_think = client.post("/v1/chat/completions", json=body).json()["choices"][0]["message"]
+            assert no_think["content"] == plain["content"] and no_think["reasoning_content"] == ""
+    finally:
+        driver.stop()

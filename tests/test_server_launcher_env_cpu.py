@@ -130,6 +130,7 @@ def test_model_families_are_validated_like_the_reference_launcher():
             resolve("direct", env)
     cmd, _ = resolve("direct", {})
     assert cmd[cmd.index("--kv-cache-format") + 1] == "direct"
+    assert cmd[cmd.index("--reasoning-parser") + 1] == "deepseek-v4"
 
 
 def test_frontend_preparation_and_diagnostics_environment():
